@@ -1,0 +1,185 @@
+"""Seeded synthetic knowledge graphs with the shapes of the benchmark configs.
+
+The reference's datasets (FB15k-237, YAGO3-10, Wikidata5M, Freebase, ...) are not
+available, so every workload here is a seeded synthetic stand-in with the entity,
+relation and triple counts of the five benchmark configurations:
+
+* relation ids follow a finite Zipf law over a seeded permutation of the base
+  relations;
+* heads are uniform (or Zipf for config 2), tails follow a Zipf law over a seeded
+  entity permutation, which produces the hub entities that drive the c2 budget;
+* duplicate (h, r, t) triples are dropped and resampled until the stated count
+  is reached.
+
+Queries follow the reference's ``batch_iter`` (src/dataloader.py:99-123): every
+sampled training triple yields the two queries (h, r, t) and (t, r + R, h), so a
+``--batch_size b`` step has ``2 b`` queries, and the batch's own triples are
+hidden through the edge-visibility mask (src/main.py:888).
+"""
+from __future__ import annotations
+
+import dataclasses
+import os
+
+import numpy as np
+
+SEED = 1234
+
+
+@dataclasses.dataclass(frozen=True)
+class KGConfig:
+    """One benchmark configuration (entities, relations, triples, model sizes)."""
+
+    index: int
+    entities: int
+    relations: int          # base relations R; the model sees n = 2R + 1 operators
+    train_triples: int      # triples in the training graph (the CSR)
+    s_rel: float            # Zipf exponent of relation frequency
+    s_tail: float           # Zipf exponent of tail frequency
+    head_zipf: float        # 0.0 means uniform heads
+    emb: int
+    batch_size: int         # --batch_size; a training step has 2 * batch_size queries
+    c1: int                 # entity budget per (query, channel); 0 disables top-k
+    c2: int                 # fact budget per source (c2 // 2 per direction)
+    T: int = 3              # hops (--L in the reference CLI)
+    N: int = 3              # channels (--N; the operator's L)
+    split_all: int = 0      # config 1 states the total triple count and splits 80/10/10
+
+    @property
+    def n(self) -> int:
+        return 2 * self.relations + 1
+
+    @property
+    def queries(self) -> int:
+        return 2 * self.batch_size
+
+    @property
+    def use_topk(self) -> bool:
+        return self.c1 > 0 or self.c2 > 0
+
+
+CONFIGS = {
+    1: KGConfig(1, 3_000, 12, 22_400, 1.2, 1.0, 0.0, 128, 32, 0, 0, split_all=28_000),
+    2: KGConfig(2, 14_500, 237, 272_000, 1.1, 1.0, 1.0, 128, 64, 1000, 400),
+    3: KGConfig(3, 123_000, 37, 1_080_000, 1.3, 1.2, 0.0, 256, 128, 1000, 400),
+    4: KGConfig(4, 4_600_000, 822, 20_600_000, 1.1, 1.0, 0.0, 1024, 256, 1000, 400),
+    5: KGConfig(5, 86_000_000, 14_824, 338_000_000, 1.2, 1.0, 0.0, 1024, 256, 1000, 400),
+}
+
+
+def scaled_config(base: KGConfig, entities: int, relations: int, train_triples: int,
+                  batch_size: int | None = None) -> KGConfig:
+    """A smaller graph with the same distributions, for tests and CPU baselines."""
+    return dataclasses.replace(base, entities=entities, relations=relations,
+                               train_triples=train_triples, split_all=0,
+                               batch_size=batch_size or base.batch_size)
+
+
+class _ZipfSampler:
+    """Finite Zipf law P(k) ∝ k^-s over k = 1..K, by inverse CDF (float64)."""
+
+    def __init__(self, K: int, s: float):
+        ranks = np.arange(1, K + 1, dtype=np.float64)
+        cdf = np.cumsum(ranks ** (-s))
+        self.cdf = cdf / cdf[-1]
+
+    def __call__(self, u: np.ndarray) -> np.ndarray:
+        idx = np.searchsorted(self.cdf, u, side="right")
+        return np.minimum(idx, self.cdf.size - 1)
+
+
+def generate_triples(cfg: KGConfig, seed: int = SEED):
+    """Return (train, valid, test) int64 arrays of shape [m, 3] (head, rel, tail)."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    E, R = cfg.entities, cfg.relations
+    rel_perm = rng.permutation(R)
+    tail_perm = rng.permutation(E)
+    head_perm = rng.permutation(E)
+    rel_zipf = _ZipfSampler(R, cfg.s_rel)
+    tail_zipf = _ZipfSampler(E, cfg.s_tail)
+    head_zipf = _ZipfSampler(E, cfg.head_zipf) if cfg.head_zipf > 0 else None
+
+    if cfg.split_all:
+        total = cfg.split_all
+    else:
+        total = cfg.train_triples + 2 * (cfg.train_triples // 10)
+    # Pack (h, r, t) into one int64 key for duplicate removal when it fits.
+    packable = float(E) * R * E < 2.0 ** 62
+    keys_seen = np.empty(0, dtype=np.int64)
+    chunks = []
+    have = 0
+    while have < total:
+        need = total - have
+        draw = int(need * 1.05) + 1024
+        r = rel_perm[rel_zipf(rng.random(draw))]
+        t = tail_perm[tail_zipf(rng.random(draw))]
+        if head_zipf is None:
+            h = rng.integers(0, E, size=draw)
+        else:
+            h = head_perm[head_zipf(rng.random(draw))]
+        tri = np.stack([h, r, t], axis=1).astype(np.int64)
+        if packable:
+            key = (tri[:, 0] * R + tri[:, 1]) * E + tri[:, 2]
+            _, first = np.unique(key, return_index=True)
+            first.sort()
+            tri, key = tri[first], key[first]
+            fresh = ~np.isin(key, keys_seen, assume_unique=True)
+            tri, key = tri[fresh], key[fresh]
+            tri, key = tri[:need], key[:need]
+            keys_seen = np.concatenate([keys_seen, key])
+        else:
+            raise NotImplementedError("graphs whose (h, r, t) key exceeds 62 bits")
+        chunks.append(tri)
+        have += tri.shape[0]
+    triples = np.concatenate(chunks, axis=0)
+    if cfg.split_all:
+        n_train = int(round(total * 0.8))
+        n_valid = int(round(total * 0.1))
+    else:
+        n_train = cfg.train_triples
+        n_valid = cfg.train_triples // 10
+    train = triples[:n_train]
+    valid = triples[n_train:n_train + n_valid]
+    test = triples[n_train + n_valid:]
+    return train, valid, test
+
+
+def load_or_generate(cfg: KGConfig, seed: int = SEED, cache_dir: str | None = None):
+    """Generate the graph once and cache it as .npy under ``cache_dir``."""
+    cache_dir = cache_dir or os.environ.get(
+        "FLASHLOG_B200_CACHE", os.path.join(os.path.dirname(os.path.dirname(__file__)), ".cache"))
+    tag = f"kg_e{cfg.entities}_r{cfg.relations}_m{cfg.train_triples}_s{seed}_{cfg.s_rel}_{cfg.s_tail}_{cfg.head_zipf}_{cfg.split_all}"
+    path = os.path.join(cache_dir, tag + ".npz")
+    if os.path.exists(path):
+        data = np.load(path)
+        return data["train"], data["valid"], data["test"]
+    train, valid, test = generate_triples(cfg, seed)
+    os.makedirs(cache_dir, exist_ok=True)
+    tmp = path + f".tmp{os.getpid()}.npz"
+    np.savez(tmp, train=train, valid=valid, test=test)
+    os.replace(tmp, path)
+    return train, valid, test
+
+
+def training_queries(train: np.ndarray, cfg: KGConfig, step: int = 0, seed: int = SEED):
+    """One training batch as in ``batch_iter``: B/2 triples give 2 queries each.
+
+    Returns (triple_ids, heads, relations, tails) with 2 * batch_size queries
+    ordered (h, r, t), (t, r + R, h) per sampled triple.
+    """
+    rng = np.random.Generator(np.random.PCG64([seed, step]))
+    ids = rng.choice(train.shape[0], size=cfg.batch_size, replace=False)
+    h, r, t = train[ids, 0], train[ids, 1], train[ids, 2]
+    heads = np.stack([h, t], axis=1).reshape(-1)
+    rels = np.stack([r, r + cfg.relations], axis=1).reshape(-1)
+    tails = np.stack([t, h], axis=1).reshape(-1)
+    return ids.astype(np.int64), heads.astype(np.int64), rels.astype(np.int64), tails.astype(np.int64)
+
+
+def random_attention(queries: int, T: int, N: int, n: int, seed: int = SEED, std: float = 1.0):
+    """Kernel-level stand-in for the LSTM attention: w_t = softmax(N(0, std^2))."""
+    rng = np.random.Generator(np.random.PCG64([seed, 7]))
+    logits = rng.standard_normal((queries, T, N, n)).astype(np.float32) * np.float32(std)
+    logits -= logits.max(axis=-1, keepdims=True)
+    e = np.exp(logits)
+    return (e / e.sum(axis=-1, keepdims=True)).astype(np.float32)

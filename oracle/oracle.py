@@ -1,0 +1,238 @@
+"""numpy front end of the C oracle (flashlog_oracle.c).
+
+TEST INFRASTRUCTURE ONLY: tests/, __graft_entry__.smoke() and bench.py's CPU
+baseline / reference legs use it as the checker.  The product package never
+imports this module.
+
+Conventions follow the reference operator API (flashlog_kernel/flashlog_kernel.py):
+a state is a coalesced COO over [B, L, E] given as row = b * L + l (int64),
+entity (int64) and value (float32), sorted by (row, entity); w is [B, L, n].
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+from . import build as _build
+
+_lib = None
+
+SKIP_NONPOS_W = 1
+DROP_MASKED = 2
+MASK_BY_TRIPLE = 4
+WOT_I = 8
+SAMPLED = 16
+EDGE_SCORE = 32
+
+# Flag sets of the three reference expansion paths.
+MODE_TOPK = SKIP_NONPOS_W | DROP_MASKED | MASK_BY_TRIPLE   # flashlog.cu:1402-1559 + flashlog_kernel.py:1217-1228
+MODE_CPU = SKIP_NONPOS_W | DROP_MASKED                     # flashlog.cpp:506-578
+MODE_ALL_EDGES = 0                                         # flashlog.cu:1743-1829
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        path = _build.ORACLE_SO
+        if not os.path.exists(path):
+            _build.build_oracle()
+        _lib = ctypes.CDLL(path)
+        _lib.flo_group_threshold.restype = ctypes.c_float
+        _lib.flo_sampling_phase.restype = ctypes.c_double
+        for name in ("flo_build_side", "flo_topc", "flo_hop_forward", "flo_fact_bound",
+                     "flo_fixed_relation", "flo_coalesce_sum"):
+            getattr(_lib, name).restype = ctypes.c_int64
+    return _lib
+
+
+def _p(a):
+    return ctypes.c_void_p(a.ctypes.data) if a is not None else ctypes.c_void_p(0)
+
+
+def _c(a, dtype):
+    return np.ascontiguousarray(a, dtype=dtype)
+
+
+def build_side(src, dst, rel, nodes):
+    """One CSR side: (row_ptr, columns, edge_rel, order, group_ptr, group_rel, group_start, group_count)."""
+    src, dst, rel = _c(src, np.int64), _c(dst, np.int64), _c(rel, np.int64)
+    m = src.size
+    row_ptr = np.empty(nodes + 1, np.int32)
+    cols = np.empty(m, np.int32)
+    erel = np.empty(m, np.int16)
+    order = np.empty(m, np.int32)
+    gptr = np.empty(nodes + 1, np.int32)
+    grel = np.empty(max(m, 1), np.int16)
+    gstart = np.empty(max(m, 1), np.int32)
+    gcount = np.empty(max(m, 1), np.int32)
+    g = lib().flo_build_side(ctypes.c_int64(m), _p(src), _p(dst), _p(rel), ctypes.c_int64(nodes),
+                             _p(row_ptr), _p(cols), _p(erel), _p(order), _p(gptr), _p(grel),
+                             _p(gstart), _p(gcount))
+    if g < 0:
+        raise ValueError("CSR requires equal 1D arrays and int32-sized graph")
+    return row_ptr, cols, erel, order, gptr, grel[:g].copy(), gstart[:g].copy(), gcount[:g].copy()
+
+
+def build_csr(head, tail, rel, nodes):
+    """The reference's 16-tuple layout (flashlog_kernel.py:678-697)."""
+    ori = build_side(head, tail, rel, nodes)
+    inv = build_side(tail, head, rel, nodes)
+    return (*ori[:4], *inv[:4], *ori[4:], *inv[4:])
+
+
+def topc(row, val, c1):
+    """c1 kept-entry indices, or None when no row exceeds c1 nonzeros."""
+    row, val = _c(row, np.int64), _c(val, np.float32)
+    keep = np.zeros(row.size, np.uint8)
+    k = lib().flo_topc(ctypes.c_int64(row.size), _p(row), _p(val), ctypes.c_int64(c1), _p(keep))
+    if k < 0:
+        return None
+    return np.flatnonzero(keep).astype(np.int64)
+
+
+def csr_masks(csr, mask, edge_weight=None):
+    """CSR-ordered float masks per side (prepare_csr_masks, flashlog_kernel.py:232-255)."""
+    m = _c(mask, np.float32).reshape(-1)
+    if edge_weight is not None:
+        m = (m * (1.0 / (1.0 + np.exp(-_c(edge_weight, np.float32).reshape(-1))))).astype(np.float32)
+    return m[csr[3].astype(np.int64)], m[csr[7].astype(np.int64)]
+
+
+def hop_forward(row, ent, val, w, csr, r_size, E, topk_edges=1 << 60, mode=MODE_TOPK,
+                mask=None, edge_weight=None, wot_i=False, sampling_seed=-1, record=True):
+    """One propagation hop with coalesce-sum; returns a dict of numpy arrays.
+
+    out_key = row * E + e (sorted), out_val = pre-normalization sums, and the
+    per-fact provenance (entry, relation column, m, output position).
+    """
+    row, ent, val = _c(row, np.int64), _c(ent, np.int64), _c(val, np.float32)
+    w = _c(w, np.float32)
+    B, L, n = w.shape
+    nnz = row.size
+    ori_rp, ori_col, _, ori_order, inv_rp, inv_col, _, inv_order = csr[:8]
+    ori_gptr, ori_grel, ori_gstart, ori_gcount, inv_gptr, inv_grel, inv_gstart, inv_gcount = csr[8:]
+    flags = mode | (WOT_I if wot_i else 0)
+    if sampling_seed >= 0:
+        flags |= SAMPLED
+    if edge_weight is not None and not (flags & MASK_BY_TRIPLE):
+        raise ValueError("edge weights are applied through the triple-indexed mask")
+    if mask is None:
+        mask = np.ones(ori_col.size, np.uint8)
+    if flags & MASK_BY_TRIPLE:
+        mask_triple = _c(np.asarray(mask).reshape(-1) != 0, np.uint8)
+        mo = mi = None
+    else:
+        mask_triple = None
+        mo, mi = csr_masks(csr, mask, None)
+    ew = _c(edge_weight, np.float32).reshape(-1) if edge_weight is not None else None
+    cap = lib().flo_fact_bound(ctypes.c_int64(nnz), _p(ent), _p(_c(ori_rp, np.int32)), _p(_c(inv_rp, np.int32)))
+    cap = max(int(cap), 1)
+    out_key = np.empty(cap, np.int64)
+    out_val = np.empty(cap, np.float32)
+    if record:
+        f_entry = np.empty(cap, np.int64)
+        f_rel = np.empty(cap, np.int32)
+        f_m = np.empty(cap, np.float32)
+        f_out = np.empty(cap, np.int64)
+    else:
+        f_entry = f_rel = f_m = f_out = None
+    nf = ctypes.c_int64(0)
+    arrs = [_c(a, t) for a, t in ((ori_col, np.int32), (ori_order, np.int32), (ori_gptr, np.int32),
+                                   (ori_grel, np.int16), (ori_gstart, np.int32), (ori_gcount, np.int32),
+                                   (inv_col, np.int32), (inv_order, np.int32), (inv_gptr, np.int32),
+                                   (inv_grel, np.int16), (inv_gstart, np.int32), (inv_gcount, np.int32))]
+    u = lib().flo_hop_forward(
+        ctypes.c_int64(nnz), _p(row), _p(ent), _p(val), _p(w), ctypes.c_int64(L), ctypes.c_int64(n),
+        ctypes.c_int64(E), ctypes.c_int64(r_size), *[_p(a) for a in arrs],
+        _p(mo), _p(mi), _p(mask_triple), _p(ew), ctypes.c_int64(int(min(topk_edges, 1 << 62))),
+        ctypes.c_int64(flags), ctypes.c_int64(sampling_seed),
+        _p(out_key), _p(out_val), _p(f_entry), _p(f_rel), _p(f_m), _p(f_out), ctypes.byref(nf))
+    nf = nf.value
+    res = dict(out_key=out_key[:u].copy(), out_val=out_val[:u].copy(), n_facts=nf)
+    if record:
+        res.update(fact_entry=f_entry[:nf].copy(), fact_rel=f_rel[:nf].copy(),
+                   fact_m=f_m[:nf].copy(), fact_out=f_out[:nf].copy())
+    return res
+
+
+def hop_backward(fw, g_out, row, val, w, r_size):
+    """grad of the entry values and of w from a recorded forward (flashlog.cpp:991-1134)."""
+    row, val, w = _c(row, np.int64), _c(val, np.float32), _c(w, np.float32)
+    g_out = _c(g_out, np.float32)
+    grad_v = np.empty(row.size, np.float32)
+    grad_w = np.zeros(w.shape, np.float32)
+    lib().flo_hop_backward(ctypes.c_int64(fw["n_facts"]), _p(fw["fact_entry"]), _p(fw["fact_rel"]),
+                           _p(fw["fact_m"]), _p(fw["fact_out"]), _p(g_out), ctypes.c_int64(row.size),
+                           _p(row), _p(val), _p(w), ctypes.c_int64(w.shape[-1]), ctypes.c_int64(r_size),
+                           _p(grad_v), _p(grad_w))
+    return grad_v, grad_w
+
+
+def normalize_forward(out_row, x, rows, eps=1e-7):
+    out_row, x = _c(out_row, np.int64), _c(x, np.float32)
+    denom = np.empty(rows, np.float32)
+    y = np.empty(x.size, np.float32)
+    lib().flo_normalize_forward(ctypes.c_int64(x.size), _p(out_row), _p(x), ctypes.c_int64(rows),
+                                ctypes.c_float(eps), _p(denom), _p(y))
+    return y, denom
+
+
+def normalize_backward(out_row, x, denom, g, eps=1e-7):
+    out_row, x, denom, g = _c(out_row, np.int64), _c(x, np.float32), _c(denom, np.float32), _c(g, np.float32)
+    gx = np.empty(x.size, np.float32)
+    lib().flo_normalize_backward(ctypes.c_int64(x.size), _p(out_row), _p(x), _p(denom), _p(g),
+                                 ctypes.c_int64(denom.size), ctypes.c_float(eps), _p(gx))
+    return gx
+
+
+def fixed_relation(b, l, e, v, ops, csr, r_size, E):
+    """Rule step + coalesce-sum (flashlog.cu:1561-1741, flashlog_kernel.py:182-210)."""
+    b, l, e, v = _c(b, np.int64), _c(l, np.int64), _c(e, np.int64), _c(v, np.float32)
+    ops = _c(ops, np.int64)
+    Bq, L = ops.shape
+    arrs = [_c(csr[1], np.int32), _c(csr[8], np.int32), _c(csr[9], np.int16), _c(csr[10], np.int32),
+            _c(csr[11], np.int32), _c(csr[5], np.int32), _c(csr[12], np.int32), _c(csr[13], np.int16),
+            _c(csr[14], np.int32), _c(csr[15], np.int32)]
+    args = [ctypes.c_int64(v.size), _p(b), _p(l), _p(e), _p(v), _p(ops), ctypes.c_int64(L),
+            ctypes.c_int64(r_size), *[_p(a) for a in arrs]]
+    nf = lib().flo_fixed_relation(*args, ctypes.c_int64(0), None, None, None, None)
+    nf = int(nf)
+    ob, ol, oe, ov = (np.empty(max(nf, 1), np.int64) for _ in range(3)), None, None, None
+    ob = np.empty(max(nf, 1), np.int64)
+    ol = np.empty(max(nf, 1), np.int64)
+    oe = np.empty(max(nf, 1), np.int64)
+    ov = np.empty(max(nf, 1), np.float32)
+    lib().flo_fixed_relation(*args, ctypes.c_int64(nf), _p(ob), _p(ol), _p(oe), _p(ov))
+    keys = (ob[:nf] * L + ol[:nf]) * E + oe[:nf]
+    return coalesce_sum(keys, ov[:nf])
+
+
+def coalesce_sum(keys, vals):
+    keys, vals = _c(keys, np.int64), _c(vals, np.float32)
+    ok = np.empty(max(keys.size, 1), np.int64)
+    ov = np.empty(max(keys.size, 1), np.float32)
+    u = lib().flo_coalesce_sum(ctypes.c_int64(keys.size), _p(keys), _p(vals), _p(ok), _p(ov))
+    return ok[:u].copy(), ov[:u].copy()
+
+
+def filtered_ranks(idx_b, idx_e, values, targets, filter_keys, B, E, use_eql=False):
+    idx_b, idx_e = _c(idx_b, np.int64), _c(idx_e, np.int64)
+    values, targets = _c(values, np.float32), _c(targets, np.int64)
+    fk = _c(np.sort(np.asarray(filter_keys, np.int64)), np.int64)
+    ranks = np.empty(B, np.float32)
+    lib().flo_filtered_ranks(ctypes.c_int64(values.size), _p(idx_b), _p(idx_e), _p(values), _p(targets),
+                             ctypes.c_int64(fk.size), _p(fk), ctypes.c_int64(B), ctypes.c_int64(E),
+                             ctypes.c_int(int(bool(use_eql))), _p(ranks))
+    return ranks
+
+
+def sampled_takes(w_dir, grel, gcount, budget, seed, b, l, src, is_inv):
+    """Per-group quotas of the sampled c2 path for one (entry, direction)."""
+    w_dir, grel, gcount = _c(w_dir, np.float32), _c(grel, np.int16), _c(gcount, np.int32)
+    take = np.empty(max(grel.size, 1), np.int32)
+    lib().flo_sampled_takes(_p(w_dir), _p(grel), _p(gcount), ctypes.c_int64(0), ctypes.c_int64(grel.size),
+                            ctypes.c_int64(budget), ctypes.c_int64(seed), ctypes.c_int64(b), ctypes.c_int64(l),
+                            ctypes.c_int64(src), ctypes.c_int(int(bool(is_inv))), _p(take))
+    return take[:grel.size]

@@ -1,0 +1,225 @@
+"""Generate golden vectors by running the reference's own code (build container only).
+
+The reference's Python operator glue (flashlog_kernel/flashlog_kernel.py) and
+the evaluation helper of src/main.py are imported read-only from the reference
+checkout; their native module is the reference's CPU extension compiled from
+its own sources by oracle/build.py (oracle/_ref), so no JIT build runs.  The
+fixtures are small .npz files committed beside this script; the GPU box and the
+CPU test suite read only the fixtures.
+
+Usage:  python tests/golden/make_golden.py [--reference /path/to/reference]
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, REPO)
+
+
+def _import_reference(ref_root):
+    import torch  # noqa: F401
+    from oracle import reference as R
+    sys.path.insert(0, ref_root)
+    sys.path.insert(0, os.path.join(ref_root, "src"))
+    import flashlog_kernel.flashlog_kernel as fk
+    fk._module = R.module("flashlog_ref_cpu")
+    fk._csr_builder = R.module("flashlog_ref_csr")
+    return fk
+
+
+def _graph(E, R, m, seed):
+    rng = np.random.default_rng(seed)
+    h = rng.integers(0, E, m)
+    t = np.minimum((rng.pareto(1.2, m) * E / 20).astype(np.int64), E - 1)
+    r = rng.integers(0, R, m)
+    tri = np.unique(np.stack([h, r, t], 1), axis=0)
+    tri = tri[rng.permutation(tri.shape[0])]
+    return tri
+
+
+def _state(rng, B, L, E, per_row, zero_frac=0.1, ties=False, neg=False):
+    rows, ents = [], []
+    for r in range(B * L):
+        k = int(rng.integers(1, per_row + 1))
+        rows.append(np.full(k, r))
+        ents.append(np.sort(rng.choice(E, k, replace=False)))
+    row = np.concatenate(rows)
+    ent = np.concatenate(ents)
+    if ties:
+        val = (rng.integers(0, 5, row.size) / 4.0).astype(np.float32)
+    else:
+        val = rng.random(row.size).astype(np.float32)
+    if neg:
+        val = np.where(rng.random(row.size) < 0.3, -val, val).astype(np.float32)
+    val[rng.random(row.size) < zero_frac] = 0
+    return row.astype(np.int64), ent.astype(np.int64), val
+
+
+def _w(rng, B, L, n, ties):
+    if ties:
+        return (rng.integers(0, 4, size=(B, L, n)) / 4.0).astype(np.float32)
+    x = rng.standard_normal((B, L, n)).astype(np.float32)
+    e = np.exp(x - x.max(-1, keepdims=True))
+    return (e / e.sum(-1, keepdims=True)).astype(np.float32)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=os.path.join(os.sep, "root", "reference"))
+    args = ap.parse_args()
+    import torch
+    torch.set_num_threads(1)
+    fk = _import_reference(args.reference)
+    out = {}
+
+    # --- CSR: a tiny graph in full, the config-1 graph by digest -------------
+    tri = _graph(60, 4, 400, 11)
+    csr = fk.build_csr_structure(torch.from_numpy(tri[:, 0]), torch.from_numpy(tri[:, 2]),
+                                 torch.from_numpy(tri[:, 1]), 60)
+    np.savez_compressed(os.path.join(HERE, "csr_tiny.npz"), triples=tri, E=60,
+                        **{f"f{i}": c.numpy() for i, c in enumerate(csr)})
+    from flashlog_b200.synthetic import CONFIGS, load_or_generate
+    cfg = CONFIGS[1]
+    train, valid, test = load_or_generate(cfg)
+    csr1 = fk.build_csr_structure(torch.from_numpy(train[:, 0]), torch.from_numpy(train[:, 2]),
+                                  torch.from_numpy(train[:, 1]), cfg.entities)
+    digests = np.array([hashlib.sha256(c.numpy().tobytes()).hexdigest() for c in csr1])
+    train_digest = hashlib.sha256(np.ascontiguousarray(train).tobytes()).hexdigest()
+    np.savez_compressed(os.path.join(HERE, "csr_config1.npz"), digests=digests,
+                        train_digest=np.array(train_digest))
+
+    # --- c1 selection (flashlog_kernel.py:1092-1137) ------------------------
+    rng = np.random.default_rng(21)
+    cases = {}
+    for ci, (c1, ties, neg, per_row) in enumerate([(5, False, False, 12), (5, True, False, 12),
+                                                   (3, True, True, 9), (0, False, False, 6),
+                                                   (20, False, False, 12), (1, True, False, 4)]):
+        row, ent, val = _state(rng, 4, 3, 500, per_row, ties=ties, neg=neg)
+        t = lambda a: torch.from_numpy(a)
+        kept = fk._sparse_topc_entries(t(row // 3), t(row % 3), t(ent), t(val), c1, 3)
+        cases[f"c{ci}_row"] = row
+        cases[f"c{ci}_ent"] = ent
+        cases[f"c{ci}_val"] = val
+        cases[f"c{ci}_c1"] = np.array(c1)
+        cases[f"c{ci}_kept"] = np.array([-1]) if kept is None else kept.numpy()
+    np.savez_compressed(os.path.join(HERE, "topc.npz"), n=np.array(6), **cases)
+
+    # --- one hop forward + backward through the reference CPU operators -----
+    E, Rr = cfg.entities, cfg.relations
+    n = 2 * Rr + 1
+    ctuple = tuple(c for c in csr1)
+    rng = np.random.default_rng(31)
+    hop = {}
+    specs = [("topk3_ties", 3, True, 4, True, False), ("topk200", 200, False, 30, True, False),
+             ("notopk", 0, False, 25, False, False), ("topk5_c1", 5, False, 40, True, True),
+             ("wot_i", 4, True, 10, True, False)]
+    for name, topk, ties, per_row, use_topk, with_c1 in specs:
+        B, L = 4, 3
+        row, ent, val = _state(rng, B, L, E, per_row, zero_frac=0.05)
+        w = _w(rng, B, L, n, ties)
+        mask = rng.random(train.shape[0]) > 0.15
+        idx = torch.from_numpy(np.stack([row // L, row % L, ent]))
+        v = torch.from_numpy(val).requires_grad_(True)
+        wt = torch.from_numpy(w).requires_grad_(True)
+        sp = torch.sparse_coo_tensor(idx, v, (B, L, E)).coalesce()
+        c1 = 6 if with_c1 else None
+        wot_i = name == "wot_i"
+        y = fk.vectorized_operation_sparse3d_csr_sum_norm(
+            sp, wt, ctuple, torch.from_numpy(mask), Rr, wot_i=wot_i, use_topk=use_topk,
+            topk_edges=topk, topk_nodes=c1)
+        yc = y.coalesce()
+        g = torch.from_numpy(rng.standard_normal(yc.values().shape[0]).astype(np.float32))
+        (yc.values() * g).sum().backward()
+        x = fk.vectorized_operation_sparse3d_csr_sum(
+            torch.sparse_coo_tensor(idx, torch.from_numpy(val), (B, L, E)).coalesce(),
+            torch.from_numpy(w), ctuple, torch.from_numpy(mask), Rr, wot_i=wot_i,
+            use_topk=use_topk, topk_edges=topk, topk_nodes=c1).coalesce()
+        yi = yc.indices().numpy()
+        hop.update({f"{name}_row": row, f"{name}_ent": ent, f"{name}_val": val, f"{name}_w": w,
+                    f"{name}_mask": mask.astype(np.uint8), f"{name}_topk": np.array(topk),
+                    f"{name}_use_topk": np.array(use_topk), f"{name}_c1": np.array(-1 if c1 is None else c1),
+                    f"{name}_wot_i": np.array(wot_i),
+                    f"{name}_out_key": (yi[0] * L + yi[1]) * E + yi[2],
+                    f"{name}_out_y": yc.values().detach().numpy(),
+                    f"{name}_out_x": x.values().numpy(),
+                    f"{name}_g": g.numpy(), f"{name}_grad_v": v.grad.numpy(),
+                    f"{name}_grad_w": wt.grad.numpy()})
+    np.savez_compressed(os.path.join(HERE, "hop_config1.npz"), names=np.array([s[0] for s in specs]), **hop)
+
+    # --- three-hop DRUM propagation + readout + loss (src/model_DRUM_kernel_sp.py:92-204)
+    rng = np.random.default_rng(41)
+    from flashlog_b200.synthetic import training_queries
+    ids, qh, qr, qt = training_queries(train, cfg)
+    qh, qr, qt = qh[:8], qr[:8], qt[:8]
+    B, L, T = 8, 3, 3
+    logits = rng.standard_normal((B, T, L, n)).astype(np.float32)
+    mask = np.ones(train.shape[0], bool)
+    mask[ids[:4]] = False
+    lg = torch.from_numpy(logits).requires_grad_(True)
+    sb = torch.arange(B).repeat_interleave(L)
+    sl = torch.arange(L).repeat(B)
+    se = torch.from_numpy(qh).repeat_interleave(L)
+    state = torch.sparse_coo_tensor(torch.stack([sb, sl, se]), torch.ones(B * L), (B, L, E)).coalesce()
+    c1, c2 = 30, 16
+    for t in range(T):
+        w_t = torch.softmax(lg[:, t], dim=-1)
+        state = fk.vectorized_operation_sparse3d_csr_sum_norm(
+            state, w_t, ctuple, torch.from_numpy(mask), Rr, use_topk=True, topk_edges=c2 // 2,
+            topk_nodes=c1).coalesce()
+    sidx = state.indices()
+    final = torch.sparse_coo_tensor(torch.stack([sidx[0], sidx[2]]), state.values(), (B, E)).coalesce()
+    from utils import log_loss_common_sp
+    loss = log_loss_common_sp(final, torch.from_numpy(qt), E, 1.0)
+    loss.backward()
+    fi = final.indices().numpy()
+    np.savez_compressed(os.path.join(HERE, "drum3_config1.npz"), heads=qh, rels=qr, tails=qt,
+                        logits=logits, mask=mask.astype(np.uint8), c1=np.array(c1), c2=np.array(c2),
+                        final_key=fi[0] * E + fi[1], final_val=final.values().detach().numpy(),
+                        loss=np.array(loss.item(), np.float32), grad_logits=lg.grad.numpy())
+
+    # --- normalize forward/backward (flashlog_kernel.py:536-607) ------------
+    rng = np.random.default_rng(51)
+    row, ent, val = _state(rng, 5, 3, 400, 30, zero_frac=0.0)
+    val[:3] = 0.0
+    idx = torch.from_numpy(np.stack([row // 3, row % 3, ent]))
+    v = torch.from_numpy(val).requires_grad_(True)
+    y = fk.normalize_sparse3d(torch.sparse_coo_tensor(idx, v, (5, 3, 400)).coalesce())
+    g = torch.from_numpy(rng.standard_normal(val.size).astype(np.float32))
+    (y.coalesce().values() * g).sum().backward()
+    np.savez_compressed(os.path.join(HERE, "normalize.npz"), row=row, ent=ent, val=val,
+                        y=y.coalesce().values().detach().numpy(), g=g.numpy(), grad=v.grad.numpy())
+
+    # --- filtered ranks: MRR / hits of the CPU twin (src/main.py:391-466) ---
+    import main as ref_main
+    rng = np.random.default_rng(61)
+    rk = {}
+    for ci, use_eql in enumerate([False, True, True]):
+        Bq, Eq = 16, 300
+        keys = np.unique(rng.integers(0, Bq * Eq, 1200))
+        vals = (rng.integers(0, 6, keys.size) / 5.0).astype(np.float32) if ci else rng.random(keys.size).astype(np.float32)
+        targets = rng.integers(0, Eq, Bq)
+        fb = rng.integers(0, Bq, 200)
+        fe = rng.integers(0, Eq, 200)
+        state = torch.sparse_coo_tensor(torch.from_numpy(np.stack([keys // Eq, keys % Eq])),
+                                        torch.from_numpy(vals), (Bq, Eq)).coalesce()
+        hits = np.zeros(10)
+        mrr = ref_main.calculate_hits_full_sparse(state, [{"t": int(x)} for x in targets],
+                                                  (torch.from_numpy(fb), torch.from_numpy(fe)), hits,
+                                                  use_eql=use_eql)
+        rk.update({f"r{ci}_keys": keys, f"r{ci}_vals": vals, f"r{ci}_targets": targets,
+                   f"r{ci}_fb": fb, f"r{ci}_fe": fe, f"r{ci}_eql": np.array(use_eql),
+                   f"r{ci}_mrr": np.array(mrr), f"r{ci}_hits": hits, f"r{ci}_B": np.array(Bq),
+                   f"r{ci}_E": np.array(Eq)})
+    np.savez_compressed(os.path.join(HERE, "ranks.npz"), n=np.array(3), **rk)
+    print("golden fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

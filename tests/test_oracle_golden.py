@@ -1,0 +1,132 @@
+"""The C oracle against golden vectors produced by the reference's own code.
+
+These run on CPU.  They pin the checker that the GPU parity tests rely on.
+"""
+import hashlib
+
+import numpy as np
+import pytest
+
+from helpers import O, config1_graph, oracle_hop_norm, oracle_hop_norm_backward
+
+
+def test_csr_tiny_matches_reference(golden):
+    d = golden("csr_tiny.npz")
+    tri = d["triples"]
+    csr = O.build_csr(tri[:, 0], tri[:, 2], tri[:, 1], int(d["E"]))
+    for i, c in enumerate(csr):
+        ref = d[f"f{i}"]
+        assert c.dtype == ref.dtype, i
+        assert np.array_equal(c, ref), i
+
+
+def test_csr_config1_digests(golden):
+    d = golden("csr_config1.npz")
+    cfg, train, csr = config1_graph()
+    assert hashlib.sha256(np.ascontiguousarray(train).tobytes()).hexdigest() == str(d["train_digest"])
+    for i, c in enumerate(csr):
+        assert hashlib.sha256(c.tobytes()).hexdigest() == str(d["digests"][i]), i
+
+
+def test_csr_rejects_out_of_range():
+    with pytest.raises(ValueError):
+        O.build_side(np.array([0, 5]), np.array([1, 2]), np.array([0, 0]), 3)
+
+
+def test_topc_matches_reference(golden):
+    d = golden("topc.npz")
+    for ci in range(int(d["n"])):
+        kept = O.topc(d[f"c{ci}_row"], d[f"c{ci}_val"], int(d[f"c{ci}_c1"]))
+        ref = d[f"c{ci}_kept"]
+        if ref.size == 1 and ref[0] == -1:
+            assert kept is None, ci
+        else:
+            assert kept is not None and np.array_equal(kept, ref), ci
+
+
+@pytest.mark.parametrize("name", ["topk3_ties", "topk200", "notopk", "topk5_c1", "wot_i"])
+def test_hop_forward_backward_matches_reference(golden, name):
+    d = golden("hop_config1.npz")
+    cfg, train, csr = config1_graph()
+    E, R = cfg.entities, cfg.relations
+    row, ent, val, w = d[f"{name}_row"], d[f"{name}_ent"], d[f"{name}_val"], d[f"{name}_w"]
+    c1 = int(d[f"{name}_c1"])
+    h = oracle_hop_norm(row, ent, val, w, csr, R, E, int(d[f"{name}_topk"]), bool(d[f"{name}_use_topk"]),
+                        None if c1 < 0 else c1, d[f"{name}_mask"], bool(d[f"{name}_wot_i"]))
+    assert np.array_equal(h["fw"]["out_key"], d[f"{name}_out_key"])
+    # Expansion sums follow the reference's order exactly.
+    assert np.array_equal(h["fw"]["out_val"], d[f"{name}_out_x"])
+    np.testing.assert_allclose(h["y"], d[f"{name}_out_y"], rtol=1e-6, atol=0)
+    gv, gw = oracle_hop_norm_backward(h, d[f"{name}_g"], row, val, w, R)
+    np.testing.assert_allclose(gv, d[f"{name}_grad_v"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(gw, d[f"{name}_grad_w"], rtol=1e-5, atol=1e-6)
+
+
+def test_normalize_matches_reference(golden):
+    d = golden("normalize.npz")
+    row = d["row"]
+    y, denom = O.normalize_forward(row, d["val"], 15)
+    np.testing.assert_array_equal(y, d["y"])
+    gx = O.normalize_backward(row, d["val"], denom, d["g"])
+    np.testing.assert_allclose(gx, d["grad"], rtol=1e-5, atol=1e-6)
+
+
+def test_filtered_ranks_match_reference(golden):
+    d = golden("ranks.npz")
+    for ci in range(int(d["n"])):
+        keys, B, E = d[f"r{ci}_keys"], int(d[f"r{ci}_B"]), int(d[f"r{ci}_E"])
+        targets = d[f"r{ci}_targets"]
+        filt = np.unique(np.concatenate([d[f"r{ci}_fb"] * E + d[f"r{ci}_fe"], np.arange(B) * E + targets]))
+        ranks = O.filtered_ranks(keys // E, keys % E, d[f"r{ci}_vals"], targets, filt, B, E,
+                                 bool(d[f"r{ci}_eql"]))
+        hits = np.zeros(10)
+        for r in ranks:
+            hits += (float(r) <= np.arange(1, 11))
+        np.testing.assert_allclose((1.0 / ranks.astype(np.float64)).sum(), float(d[f"r{ci}_mrr"]), rtol=1e-6)
+        np.testing.assert_array_equal(hits, d[f"r{ci}_hits"])
+
+
+def test_drum3_matches_reference(golden):
+    """Three hops of the DRUM sparse model with deterministic c1/c2, readout and loss."""
+    import torch
+    d = golden("drum3_config1.npz")
+    cfg, train, csr = config1_graph()
+    E, R = cfg.entities, cfg.relations
+    heads, tails = d["heads"], d["tails"]
+    B, T, L, n = d["logits"].shape
+    logits = torch.from_numpy(d["logits"]).requires_grad_(True)
+    ws = [torch.softmax(logits[:, t], dim=-1) for t in range(T)]
+    row = np.repeat(np.arange(B) * L, L) + np.tile(np.arange(L), B)
+    ent = np.repeat(heads, L).astype(np.int64)
+    val = np.ones(row.size, np.float32)
+    states, hops = [], []
+    c1, c2 = int(d["c1"]), int(d["c2"])
+    for t in range(T):
+        w = ws[t].detach().numpy()
+        h = oracle_hop_norm(row, ent, val, w, csr, R, E, c2 // 2, True, c1, d["mask"], False)
+        hops.append((h, row, val, w))
+        row, ent, val = h["out_row"], h["fw"]["out_key"] % E, h["y"]
+    b = row // L
+    key = b * E + ent
+    fk, fv = O.coalesce_sum(key, val)
+    np.testing.assert_array_equal(fk, d["final_key"])
+    np.testing.assert_allclose(fv, d["final_val"], rtol=1e-5, atol=1e-9)
+    # loss = -mean(log(max(score(b, tail_b), 1e-7)))
+    score = np.zeros(B, np.float32)
+    for k, v in zip(fk, fv):
+        if k % E == tails[k // E]:
+            score[k // E] = v
+    loss = -np.mean(np.log(np.maximum(score, 1e-7)))
+    np.testing.assert_allclose(loss, float(d["loss"]), rtol=1e-5)
+    # backward: dloss/dscore, through the three hops
+    gscore = np.where(score > 1e-7, -1.0 / (B * np.maximum(score, 1e-7)), 0.0).astype(np.float32)
+    g = np.array([gscore[r // L] if e == tails[r // L] else 0.0 for r, e in zip(row, ent)], np.float32)
+    gws = []
+    for h, hrow, hval, w in reversed(hops):
+        gv, gw = oracle_hop_norm_backward(h, g, hrow, hval, w, R)
+        gws.append(gw)
+        g = gv
+    gws = gws[::-1]
+    total = sum((ws[t] * torch.from_numpy(gws[t])).sum() for t in range(T))
+    total.backward()
+    np.testing.assert_allclose(logits.grad.numpy(), d["grad_logits"], rtol=1e-4, atol=1e-6)
