@@ -1,0 +1,484 @@
+"""Benchmark: propagated facts/s of one L=3 sparse DRUM fwd+bwd step.
+
+Workload (default): config 4 of the benchmark configs -- 4.6M entities, 822
+base relations (+ inverses), 20.6M training triples; DRUM with T=3 hops,
+N=3 channels, batch 256 (512 queries: every sampled triple gives (h, r, t) and
+(t, r + R, h)), c1 = 1000 entity budget, c2 = 400 fact budget, deterministic
+top-k.  Seeded synthetic data (the reference's datasets are unavailable).
+
+A fact is one emitted (query, channel, src -> dst) contribution through a
+kept, visible graph edge in a hop's forward; identity terms are not counted.
+value = sum of facts over the timed steps / device time of those steps (hop
+forward + backward, readout, loss, gradient all-reduce and the parameter
+update), inputs resident in HBM.  e2e = the same metric through the
+reference-facing operator API (COO states,
+vectorized_operation_sparse3d_csr_sum_norm per hop) with the step's query
+batch copied from pinned host memory and the loss read back every step.
+
+The per-query attention w_t = softmax(table[r_q, t] / tau_1) is a learnable
+table indexed by the query relation; it stands in for the reference's LSTM
+over the relation embedding (outside the propagation hot path).
+
+Multi-GPU (torchrun): every rank runs its own 512 queries on a replica of the
+CSR (weak scaling); per step one NCCL all_gather of the batch triple ids (so
+every replica hides the union, src/main.py:888) and one all_reduce of the
+attention gradients.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+from flashlog_b200.synthetic import CONFIGS, load_or_generate, training_queries  # noqa: E402
+
+PROFILE_TRAFFIC = os.path.join(REPO, "profiles", "hop_forward_traffic.json")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", type=int, default=4)
+    ap.add_argument("--batch-size", type=int, default=0, help="override --batch_size (queries = 2x)")
+    ap.add_argument("--e2e-steps", type=int, default=0, help="timed e2e steps (default: --steps)")
+    ap.add_argument("--cpu-queries", type=int, default=16)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi samples (clocks, throttle reasons) during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.gpu), "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for nm, flag in zip(names, parts[5:9]):
+                if flag.lower() in ("active", "1", "yes"):
+                    reasons.add(nm)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+class HopTimer:
+    """CUDA events around each hop forward (expand + row reduction) on the launching stream."""
+
+    def __init__(self):
+        self.pairs = []
+        self.enabled = False
+
+    def record_start(self):
+        if self.enabled:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self.pairs.append([e, None])
+
+    def record_end(self):
+        if self.enabled:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self.pairs[-1][1] = e
+
+    def total_ms(self):
+        return sum(a.elapsed_time(b) for a, b in self.pairs)
+
+
+class Stats:
+    """Per-hop counts (device tensors, reduced after the timed region)."""
+
+    def __init__(self, graph):
+        self.graph = graph
+        self.records = []
+        self.timer = HopTimer()
+
+    def append(self, rec):
+        self.records.append(rec)
+
+    def reduce(self):
+        g = self.graph.csr
+        S = G = F = U = 0
+        for ent, entry_count, u in self.records:
+            e = ent.to(torch.int64)
+            S += e.numel()
+            G += int(((g[8][e + 1] - g[8][e]).sum() + (g[12][e + 1] - g[12][e]).sum()).item())
+            F += int(entry_count.to(torch.int64).sum().item()) - e.numel()  # identity terms excluded
+            U += int(u)
+        return S, G, F, U
+
+
+# ---------------------------------------------------------------------------
+def setup(args, rank, world, device):
+    cfg = CONFIGS[args.config]
+    if args.batch_size:
+        import dataclasses
+        cfg = dataclasses.replace(cfg, batch_size=args.batch_size)
+    train, _, _ = load_or_generate(cfg)
+    from flashlog_b200.flashlog_kernel import build_csr_structure
+    tt = torch.from_numpy(train).to(device)
+    csr = build_csr_structure(tt[:, 0], tt[:, 2], tt[:, 1], cfg.entities)
+    del tt
+    return cfg, train, csr
+
+
+def batches_for(cfg, train, n, rank, seed_base=1234):
+    out = []
+    for s in range(n):
+        ids, h, r, t = training_queries(train, cfg, step=s, seed=seed_base + 7919 * rank)
+        out.append((ids, h, r, t))
+    return out
+
+
+def run_value_arm(args, cfg, train, csr, rank, world, device):
+    from flashlog_b200 import _lib, engine
+    from flashlog_b200.ops import Graph
+    import torch.distributed as dist
+
+    graph = Graph.of(csr)
+    R, T, N = cfg.relations, cfg.T, cfg.N
+    n = 2 * R + 1
+    gen = torch.Generator(device="cpu").manual_seed(1234)
+    table = (torch.randn(2 * R, T, N, n, generator=gen) * 1.0).to(device).requires_grad_(True)
+    mask = torch.ones(train.shape[0], dtype=torch.uint8, device=device)
+    nb = args.warmup + args.steps
+    data = batches_for(cfg, train, nb, rank)
+    dev_data = [tuple(torch.from_numpy(x).to(device) for x in b) for b in data]
+    stats = Stats(graph)
+    lr = 0.01
+
+    def step(ids, h, r, t, collect):
+        if world > 1:
+            gathered = [torch.empty_like(ids) for _ in range(world)]
+            dist.all_gather(gathered, ids)
+            hide = torch.cat(gathered)
+        else:
+            hide = ids
+        mask[hide] = 0
+        w_all = table[r]
+        rp, ent, val = engine.drum_propagate(h, w_all, graph, R, c1=cfg.c1 or None, c2=cfg.c2, mask_triple=mask,
+                                             stats=stats if collect else None)
+        loss = engine.readout_loss(rp, ent, val, t, N)
+        table.grad = None
+        loss.backward()
+        if world > 1:
+            dist.all_reduce(table.grad)
+            table.grad.div_(world)
+        with torch.no_grad():
+            table.sub_(lr * table.grad)
+        mask[hide] = 1
+        return loss
+
+    for b in dev_data[:args.warmup]:
+        step(*b, collect=False)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    launches0 = _lib.lib().fl_launch_count()
+    stats.timer.enabled = True
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for b in dev_data[args.warmup:]:
+        step(*b, collect=True)
+    t1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = t0.elapsed_time(t1)
+    launches = _lib.lib().fl_launch_count() - launches0
+    clk = clocks.stop()
+    S, G, F, U = stats.reduce()
+    hop_ms = stats.timer.total_ms()
+    n_hops = len(stats.timer.pairs)
+    return dict(ms=ms, facts=F, S=S, G=G, U=U, hop_ms=hop_ms, n_hops=n_hops, launches=launches, clocks=clk,
+                data=data, table=table)
+
+
+def run_e2e_arm(args, cfg, train, csr, data, table, rank, world, device, steps):
+    """Same metric through the reference-facing operator API with host buffers."""
+    import flashlog_b200.flashlog_kernel as fk
+    import torch.distributed as dist
+
+    R, T, N, E = cfg.relations, cfg.T, cfg.N, cfg.entities
+    mask = torch.ones(train.shape[0], dtype=torch.bool, device=device)
+    pinned = [tuple(torch.from_numpy(x).pin_memory() for x in b) for b in data]
+    h2d = sum(x.numel() * x.element_size() for x in pinned[0])
+    tab = table.detach().clone().requires_grad_(True)
+
+    def step(ids_h, h_h, r_h, t_h):
+        ids = ids_h.to(device, non_blocking=True)
+        h = h_h.to(device, non_blocking=True)
+        r = r_h.to(device, non_blocking=True)
+        t = t_h.to(device, non_blocking=True)
+        if world > 1:
+            gathered = [torch.empty_like(ids) for _ in range(world)]
+            dist.all_gather(gathered, ids)
+            hide = torch.cat(gathered)
+        else:
+            hide = ids
+        mask[hide] = False
+        Q = h.numel()
+        w_all = tab[r]
+        sb = torch.arange(Q, device=device).repeat_interleave(N)
+        sl = torch.arange(N, device=device).repeat(Q)
+        se = h.repeat_interleave(N)
+        state = torch.sparse_coo_tensor(torch.stack([sb, sl, se]), torch.ones(Q * N, device=device),
+                                        (Q, N, E), is_coalesced=True)
+        for hop in range(T):
+            w_t = torch.softmax(w_all[:, hop], dim=-1)
+            state = fk.vectorized_operation_sparse3d_csr_sum_norm(state, w_t, csr, mask, R, use_topk=True,
+                                                                 topk_edges=cfg.c2 // 2, topk_nodes=cfg.c1)
+        idx = state.indices()
+        hit = idx[2] == t[idx[0]]
+        score = torch.zeros(Q, device=device).index_add(0, idx[0][hit], state.values()[hit])
+        loss = -torch.mean(torch.log(torch.clamp(score, min=1e-7)))
+        tab.grad = None
+        loss.backward()
+        if world > 1:
+            dist.all_reduce(tab.grad)
+            tab.grad.div_(world)
+        with torch.no_grad():
+            tab.sub_(0.01 * tab.grad)
+        mask[hide] = True
+        return loss.item()  # device -> host read of the step's result
+
+    for b in pinned[:args.warmup]:
+        step(*b)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for b in pinned[args.warmup:args.warmup + steps]:
+        step(*b)
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    return e0.elapsed_time(e1), h2d, 4
+
+
+def cpu_baseline(args, cfg, train, csr):
+    """The reference's OpenMP path on a bounded sample of the same workload."""
+    from oracle import cpu_baseline as CB
+    torch.set_num_threads(os.cpu_count() or 1)
+    csr_np = tuple(c.cpu().numpy() for c in csr)
+    R, T, N = cfg.relations, cfg.T, cfg.N
+    n = 2 * R + 1
+    rng = np.random.default_rng(99)
+    batches = []
+    for s in range(4):
+        ids, h, r, t = training_queries(train, cfg, step=1000 + s)
+        q = args.cpu_queries
+        h, r, t, ids = h[:q], r[:q], t[:q], ids[:q // 2]
+        w_all = rng.standard_normal((q, T, N, n)).astype(np.float32)
+        mask = np.ones(train.shape[0], np.uint8)
+        mask[ids] = 0
+        batches.append((h, t, w_all, mask))
+    rate, facts, secs, steps, kind = CB.time_sample(csr_np, batches, R, cfg.entities, cfg.c1, cfg.c2,
+                                                    min_seconds=args.cpu_seconds, max_seconds=3 * args.cpu_seconds)
+    return dict(value=rate, unit="facts/s", cores=torch.get_num_threads(), kind=kind,
+                sample=f"{steps} steps x {args.cpu_queries} queries of config {cfg.index} "
+                       f"({facts} facts in {secs:.1f} s); c1 via the oracle port, expansion/reduction/"
+                       f"normalization fwd+bwd in the reference's compiled OpenMP extension")
+
+
+def workload_desc(cfg, world):
+    return (f"config {cfg.index}: {cfg.entities} entities, {cfg.relations} relations (+inverses), "
+            f"{cfg.train_triples} triples; DRUM T={cfg.T} N={cfg.N}, batch {cfg.batch_size} "
+            f"({cfg.queries} queries) per GPU, c1={cfg.c1} c2={cfg.c2}, deterministic top-k")
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    cfg0 = CONFIGS[args.config]
+    metric = "propagated facts/sec (L=3 DRUM fwd+bwd)"
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        import dataclasses
+        cfg = dataclasses.replace(cfg0, batch_size=args.batch_size) if args.batch_size else cfg0
+        train, _, _ = load_or_generate(cfg)
+        from oracle import oracle as O
+        csr_np = O.build_csr(train[:, 0], train[:, 2], train[:, 1], cfg.entities)
+        from oracle import cpu_baseline as CB
+        torch.set_num_threads(os.cpu_count() or 1)
+        rng = np.random.default_rng(99)
+        R, T, N = cfg.relations, cfg.T, cfg.N
+        vals = []
+        steps_done = 0
+        t_all = time.perf_counter()
+        for s in range(args.warmup + args.steps):
+            ids, h, r, t = training_queries(train, cfg, step=2000 + s)
+            q = args.cpu_queries
+            w_all = rng.standard_normal((q, T, N, 2 * R + 1)).astype(np.float32)
+            mask = np.ones(train.shape[0], np.uint8)
+            mask[ids[:q // 2]] = 0
+            t0 = time.perf_counter()
+            f, _, kind = CB.drum_step(csr_np, h[:q], t[:q], w_all, mask, R, cfg.entities, cfg.c1, cfg.c2)
+            el = time.perf_counter() - t0
+            if s >= args.warmup:
+                vals.append((f, el))
+                steps_done += 1
+        facts = sum(f for f, _ in vals)
+        secs = sum(e for _, e in vals)
+        value = facts / secs if secs > 0 else 0.0
+        line = {"impl": "reference", "metric": metric, "value": value, "unit": "facts/s", "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * secs / max(steps_done, 1),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic",
+                "config": {"workload": workload_desc(cfg, 1) + f"; CPU sample of {args.cpu_queries} queries per step",
+                           "global_batch": args.cpu_queries, "parallelism": "OpenMP host threads"},
+                "cpu_baseline": {"value": value, "unit": "facts/s", "cores": torch.get_num_threads(), "kind": kind,
+                                 "sample": f"{steps_done} steps x {args.cpu_queries} queries"},
+                "e2e": {"value": value, "unit": "facts/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+
+    import torch.distributed as dist
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=300))
+    cfg, train, csr = setup(args, rank, world, device)
+    res = run_value_arm(args, cfg, train, csr, rank, world, device)
+    ms = res["ms"]
+    facts = res["facts"]
+    hop_ms = res["hop_ms"]
+    if world > 1:
+        t = torch.tensor([ms, float(facts)], dtype=torch.float64, device=device)
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = t.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        ms, facts = float(mx[0].item()), int(sm[1].item())
+    value = facts / (ms / 1000.0)
+    e2e = None
+    if not args.no_e2e:
+        steps_e2e = args.e2e_steps or args.steps
+        e2e_ms, h2d, d2h = run_e2e_arm(args, cfg, train, csr, res["data"], res["table"], rank, world, device,
+                                       steps_e2e)
+        local_facts = res["facts"] * steps_e2e / args.steps
+        if world > 1:
+            t = torch.tensor([e2e_ms, local_facts], dtype=torch.float64, device=device)
+            mx = t.clone()
+            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+            sm = t.clone()
+            dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+            e2e_ms, local_facts = float(mx[0].item()), float(sm[1].item())
+        e2e = {"value": local_facts / (e2e_ms / 1000.0), "unit": "facts/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / steps_e2e,
+               "api": "vectorized_operation_sparse3d_csr_sum_norm per hop (COO in/out)"}
+    peaks_path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    peak, peak_src = 6650.0, "fallback"
+    if os.path.exists(peaks_path):
+        try:
+            peak = float(json.load(open(peaks_path))["hbm_gbs"])
+            peak_src = "measured"
+        except Exception:
+            pass
+    S, G, U = res["S"], res["G"], res["U"]
+    alg_bytes = 24 * S + 14 * G + 5 * res["facts"] + 8 * U
+    achieved = alg_bytes / (hop_ms / 1000.0) / 1e9 if hop_ms > 0 else 0.0
+    traffic = None
+    if os.path.exists(PROFILE_TRAFFIC):
+        try:
+            prof = json.load(open(PROFILE_TRAFFIC))
+            if prof.get("config") == cfg.index:
+                traffic = prof.get("dram_bytes_per_hop_forward")
+        except Exception:
+            traffic = None
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            cpu = cpu_baseline(args, cfg, train, csr)
+        except Exception as exc:  # the baseline never decides the GPU result
+            cpu = {"value": None, "unit": "facts/s", "cores": os.cpu_count(), "kind": "reference",
+                   "sample": f"failed: {exc}"}
+    if rank == 0:
+        line = {"metric": metric, "value": value, "unit": "facts/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": workload_desc(cfg, world), "global_batch": cfg.queries * world,
+                           "per_gpu_queries": cfg.queries, "parallelism": f"query-sharded dp{world}",
+                           "l2": "inputs larger than L2 (CSR ~0.7 GB; fresh query batch every step)",
+                           "facts_per_step": facts / args.steps},
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                             "frac": achieved / peak, "traffic": traffic, "peak_source": peak_src,
+                             "kernel": "hop forward (expand + row reduction), rank 0",
+                             "algorithmic_bytes": "24*S + 14*G + 5*F + 8*U per hop",
+                             "units": {"S": S, "G": G, "F": res["facts"], "U": U, "hops": res["n_hops"],
+                                       "hop_forward_ms": hop_ms}},
+                "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": res["launches"], "clocks": res["clocks"]}
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

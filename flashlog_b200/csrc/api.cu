@@ -1,0 +1,244 @@
+// api.cu -- the extern "C" boundary of libflashlog_b200.so.
+//
+// Each entry point validates its arguments, runs stream-ordered kernels on the
+// caller's stream and returns an int status; fl_last_error() holds a
+// thread-local message for the last failure.
+#include <stdarg.h>
+#include <string.h>
+
+#include <atomic>
+
+#include "common.cuh"
+#include "hop.cuh"
+
+namespace fl {
+
+static thread_local char g_err[512] = "";
+static std::atomic<unsigned long long> g_launches{0};
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+void set_error(const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+}
+
+int check_launch(const char *what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        set_error("%s: %s", what, cudaGetErrorString(e));
+        return FL_ECUDA;
+    }
+    return FL_OK;
+}
+
+// Declarations of the kernels' host wrappers defined in other units.
+size_t csr_build_workspace(int64_t m, int64_t nodes);
+int csr_build_side(const int64_t *src, const int64_t *dst, const int64_t *rel, int64_t m, int64_t nodes,
+                   int64_t relations, int32_t *row_ptr, int32_t *col, int16_t *edge_rel, int32_t *order,
+                   int32_t *group_ptr, int16_t *group_rel, int32_t *group_start, int32_t *group_count,
+                   int64_t *n_groups, void *ws, size_t ws_bytes, cudaStream_t st);
+size_t fixed_relation_workspace(int64_t nnz);
+int fixed_relation_plan(const int64_t *b, const int64_t *l, const int32_t *ent, int64_t nnz, const int64_t *ops,
+                        int64_t Lr, int64_t R, const fl_csr_side &ori, const fl_csr_side &inv, int64_t *slot_base,
+                        int64_t *total, void *ws, size_t ws_bytes, cudaStream_t st);
+int fixed_relation_fill(const int64_t *b, const int64_t *l, const int32_t *ent, const float *val, int64_t nnz,
+                        const int64_t *ops, int64_t Lr, int64_t R, const fl_csr_side &ori, const fl_csr_side &inv,
+                        const int64_t *slot_base, int32_t *fact_dst, float *fact_val, int32_t *entry_count,
+                        cudaStream_t st);
+size_t filtered_ranks_workspace(int64_t B);
+int filtered_ranks(const int64_t *ib, const int64_t *ie, const float *v, int64_t nnz, const int64_t *targets,
+                   const int64_t *fk, int64_t nf, int64_t B, int64_t E, int use_eql, float *ranks, void *ws,
+                   size_t ws_bytes, cudaStream_t st);
+
+namespace {
+
+// COO (b, l, e) sorted by key -> row_ptr by binary search per row; entity ids
+// narrowed to int32.  Out-of-range or unsorted input sets *bad.
+__global__ void coo_rows_kernel(const int64_t *b, const int64_t *l, int64_t nnz, int64_t L, int64_t rows,
+                                int64_t *row_ptr) {
+    int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (r > rows) return;
+    int64_t lo = 0, hi = nnz;  // first i with key(i) >= r
+    while (lo < hi) {
+        int64_t mid = lo + ((hi - lo) >> 1);
+        if (b[mid] * L + l[mid] < r) lo = mid + 1; else hi = mid;
+    }
+    row_ptr[r] = lo;
+}
+
+__global__ void coo_ent_kernel(const int64_t *b, const int64_t *l, const int64_t *e, int64_t nnz, int64_t L,
+                               int64_t rows, int64_t E, int32_t *ent, int *bad) {
+    int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (i >= nnz) return;
+    const int64_t key = b[i] * L + l[i];
+    bool ok = e[i] >= 0 && e[i] < E && l[i] >= 0 && l[i] < L && key >= 0 && key < rows;
+    if (ok && i > 0) {
+        const int64_t pk = b[i - 1] * L + l[i - 1];
+        ok = pk < key || (pk == key && e[i - 1] < e[i]);
+    }
+    if (!ok) atomicExch(bad, 1);
+    ent[i] = static_cast<int32_t>(e[i]);
+}
+
+__global__ void rows_coo_kernel(const int64_t *row_ptr, const int32_t *ent, int64_t rows, int64_t L, int64_t U,
+                                int64_t *idx) {
+    const int64_t r = blockIdx.x;
+    if (r >= rows) return;
+    const int64_t a = row_ptr[r], z = row_ptr[r + 1];
+    for (int64_t k = a + threadIdx.x; k < z; k += blockDim.x) {
+        idx[k] = r / L;
+        idx[U + k] = r % L;
+        idx[2 * U + k] = ent[k];
+    }
+}
+
+}  // namespace
+}  // namespace fl
+
+using namespace fl;
+
+extern "C" {
+
+const char *fl_last_error(void) { return g_err; }
+
+int fl_version(void) { return 1; }
+
+unsigned long long fl_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int fl_device_sm_count(void) {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    return n;
+}
+
+size_t fl_csr_build_workspace(int64_t m, int64_t nodes) { return csr_build_workspace(m, nodes); }
+
+int fl_csr_build_side(const int64_t *src, const int64_t *dst, const int64_t *rel, int64_t m, int64_t nodes,
+                      int64_t relations, int32_t *row_ptr, int32_t *col, int16_t *edge_rel, int32_t *order,
+                      int32_t *group_ptr, int16_t *group_rel, int32_t *group_start, int32_t *group_count,
+                      int64_t *n_groups, void *ws, size_t ws_bytes, fl_stream_t stream) {
+    return csr_build_side(src, dst, rel, m, nodes, relations, row_ptr, col, edge_rel, order, group_ptr, group_rel,
+                          group_start, group_count, n_groups, ws, ws_bytes, as_stream(stream));
+}
+
+int fl_coo_to_rows(const int64_t *b, const int64_t *l, const int64_t *e, int64_t nnz, int64_t L, int64_t rows,
+                   int64_t E, int64_t *row_ptr, int32_t *ent, int *bad, fl_stream_t stream) {
+    FL_REQUIRE(L > 0 && rows >= 0 && nnz >= 0, "invalid state shape");
+    cudaStream_t st = as_stream(stream);
+    launch(coo_rows_kernel, static_cast<unsigned>((rows + 1 + 255) / 256), 256, 0, st, b, l, nnz, L, rows, row_ptr);
+    if (nnz > 0)
+        launch(coo_ent_kernel, static_cast<unsigned>((nnz + 255) / 256), 256, 0, st, b, l, e, nnz, L, rows, E, ent, bad);
+    return check_launch("coo_to_rows");
+}
+
+int fl_rows_to_coo(const int64_t *row_ptr, const int32_t *ent, int64_t rows, int64_t L, int64_t U, int64_t *indices,
+                   fl_stream_t stream) {
+    FL_REQUIRE(L > 0, "invalid L");
+    if (rows > 0 && U > 0)
+        launch(rows_coo_kernel, static_cast<unsigned>(rows), 256, 0, as_stream(stream), row_ptr, ent, rows, L, U, indices);
+    return check_launch("rows_to_coo");
+}
+
+size_t fl_topc_workspace(int64_t rows, int64_t S) { return topc_workspace(rows, S); }
+
+int fl_topc_select(const int64_t *row_ptr, const int32_t *ent, const float *val, int64_t rows, int64_t S, int64_t c1,
+                   const double *noise, int64_t *out_row_ptr, int32_t *out_ent, float *out_val, int64_t *out_src,
+                   void *ws, size_t ws_bytes, fl_stream_t stream) {
+    return topc_select(row_ptr, ent, val, rows, S, c1, noise, out_row_ptr, out_ent, out_val, out_src, ws, ws_bytes,
+                       as_stream(stream));
+}
+
+int fl_topc_candidates(const int64_t *row_ptr, const float *val, int64_t rows, int64_t S, int64_t c1,
+                       int64_t *n_candidates, void *ws, size_t ws_bytes, fl_stream_t stream) {
+    return topc_candidates(row_ptr, val, rows, S, c1, n_candidates, ws, ws_bytes, as_stream(stream));
+}
+
+size_t fl_hop_workspace(int64_t rows, int64_t S) { return hop_workspace(rows, S); }
+
+int fl_hop_plan(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *ent, int64_t S, fl_csr_side ori,
+                fl_csr_side inv, int64_t *slot_base, int64_t *total_slots, void *ws, size_t ws_bytes,
+                fl_stream_t stream) {
+    FL_REQUIRE(p != nullptr && p->n == 2 * p->r_size + 1, "w must have n = 2 * r_size + 1 columns");
+    return hop_plan(p, row_ptr, ent, S, ori, inv, slot_base, total_slots, ws, ws_bytes, as_stream(stream));
+}
+
+int fl_hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *ent, const float *val, int64_t S,
+                  const float *w, fl_csr_side ori, fl_csr_side inv, const float *mask_csr_ori,
+                  const float *mask_csr_inv, const uint8_t *mask_triple, const float *edge_weight,
+                  const int64_t *slot_base, int32_t *fact_dst, float *fact_val, int16_t *fact_rel, float *fact_m,
+                  int32_t *entry_count, fl_stream_t stream) {
+    FL_REQUIRE(p != nullptr && p->n == 2 * p->r_size + 1, "w must have n = 2 * r_size + 1 columns");
+    FL_REQUIRE(p->n - 1 <= 32767, "relation columns exceed int16");
+    FL_REQUIRE(!((p->flags & FL_SAMPLED) && p->sampling_seed < 0), "sampled mode needs a seed");
+    return hop_expand(p, row_ptr, ent, val, S, w, ori, inv, mask_csr_ori, mask_csr_inv, mask_triple, edge_weight,
+                      slot_base, fact_dst, fact_val, fact_rel, fact_m, entry_count, as_stream(stream));
+}
+
+size_t fl_reduce_workspace(int64_t rows, int64_t total_slots) { return row_reduce_workspace(rows, total_slots); }
+
+int fl_row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *slot_base, const int32_t *entry_count,
+                  const int32_t *fact_dst, const float *fact_val, int64_t total_slots, int32_t *fact_pos, float eps,
+                  int64_t *out_row_ptr, int32_t *out_ent, float *out_x, float *out_y, float *out_denom,
+                  void *ws, size_t ws_bytes, fl_stream_t stream) {
+    return row_reduce(row_ptr, rows, E, slot_base, entry_count, fact_dst, fact_val, total_slots, fact_pos, eps,
+                      out_row_ptr, out_ent, out_x, out_y, out_denom, ws, ws_bytes, as_stream(stream));
+}
+
+size_t fl_hop_backward_workspace(int64_t rows, int64_t n) { return hop_backward_workspace(rows, n); }
+
+int fl_hop_backward(const fl_hop_params *p, const int64_t *row_ptr, const float *val, int64_t S, const float *w,
+                    const int64_t *slot_base, const int32_t *entry_count, const int32_t *fact_pos,
+                    const int16_t *fact_rel, const float *fact_m, const int64_t *out_row_ptr, const float *out_x,
+                    const float *out_denom, const float *g_y, float *grad_val, float *grad_w, void *ws,
+                    size_t ws_bytes, fl_stream_t stream) {
+    FL_REQUIRE(p != nullptr, "null params");
+    return hop_backward(p, row_ptr, val, S, w, slot_base, entry_count, fact_pos, fact_rel, fact_m, out_row_ptr, out_x,
+                        out_denom, g_y, grad_val, grad_w, ws, ws_bytes, as_stream(stream));
+}
+
+int fl_normalize_forward(const int64_t *row_ptr, const float *x, int64_t rows, float eps, float *y, float *denom,
+                         fl_stream_t stream) {
+    return normalize_forward(row_ptr, x, rows, eps, y, denom, as_stream(stream));
+}
+
+int fl_normalize_backward(const int64_t *row_ptr, const float *x, const float *denom, const float *g, int64_t rows,
+                          float eps, float *gx, fl_stream_t stream) {
+    return normalize_backward(row_ptr, x, denom, g, rows, eps, gx, as_stream(stream));
+}
+
+int fl_scatter_grad(const float *grad_sel, const int64_t *src_index, int64_t n_sel, float *grad_full, int64_t n_full,
+                    fl_stream_t stream) {
+    return scatter_grad(grad_sel, src_index, n_sel, grad_full, n_full, as_stream(stream));
+}
+
+size_t fl_fixed_relation_workspace(int64_t nnz) { return fixed_relation_workspace(nnz); }
+
+int fl_fixed_relation_plan(const int64_t *b, const int64_t *l, const int32_t *ent, int64_t nnz, const int64_t *ops,
+                           int64_t Lr, int64_t r_size, fl_csr_side ori, fl_csr_side inv, int64_t *slot_base,
+                           int64_t *total, void *ws, size_t ws_bytes, fl_stream_t stream) {
+    return fixed_relation_plan(b, l, ent, nnz, ops, Lr, r_size, ori, inv, slot_base, total, ws, ws_bytes,
+                               as_stream(stream));
+}
+
+int fl_fixed_relation_fill(const int64_t *b, const int64_t *l, const int32_t *ent, const float *val, int64_t nnz,
+                           const int64_t *ops, int64_t Lr, int64_t r_size, fl_csr_side ori, fl_csr_side inv,
+                           const int64_t *slot_base, int32_t *fact_dst, float *fact_val, int32_t *entry_count,
+                           fl_stream_t stream) {
+    return fixed_relation_fill(b, l, ent, val, nnz, ops, Lr, r_size, ori, inv, slot_base, fact_dst, fact_val,
+                               entry_count, as_stream(stream));
+}
+
+size_t fl_filtered_ranks_workspace(int64_t B) { return filtered_ranks_workspace(B); }
+
+int fl_filtered_ranks(const int64_t *idx_b, const int64_t *idx_e, const float *values, int64_t nnz,
+                      const int64_t *targets, const int64_t *filter_keys, int64_t n_filter, int64_t B, int64_t E,
+                      int use_eql, float *ranks, void *ws, size_t ws_bytes, fl_stream_t stream) {
+    return filtered_ranks(idx_b, idx_e, values, nnz, targets, filter_keys, n_filter, B, E, use_eql, ranks, ws, ws_bytes,
+                          as_stream(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,1086 @@
+// hop.cu -- one soft-grounding propagation hop on B200 (sm_100a).
+//
+// Reference semantics (paths relative to the reference project):
+//   expansion   flashlog_kernel/source/flashlog.cu:1368-1559 (top-k fill,
+//               c2 threshold 26-63 / 1342-1366, sampled quotas 1458-1528),
+//               1743-1854 (all-edges fill, identity)
+//   coalesce    flashlog_kernel/flashlog_kernel.py:258-357 (sum per key)
+//   normalize   flashlog.cu:2480-2691, flashlog_kernel.py:536-607
+//   backward    flashlog.cu:1856-1959, flashlog.cpp:991-1134
+//
+// B200 design.  The state is a row layout over r = b * L + l.  A warp expands
+// one source entry: it finds the c2 threshold by a weighted radix select over
+// the entry's relation groups, then streams the taken CSR edges with
+// coalesced int32 loads and writes facts (dst, value, relation) into slots
+// reserved by a prefix sum of per-entry capacities, in the reference's
+// canonical order (ori groups, inv groups, identity).  One CTA then reduces
+// each row: facts of a destination range are gathered into shared memory in
+// canonical order, stably radix-sorted by destination and summed
+// sequentially per destination, which reproduces the CPU reference's
+// summation order exactly and needs no atomics.  Rows larger than one tile
+// are split by a destination histogram; a range too dense to split is
+// accumulated into a dense shared-memory window tile by tile, still in
+// canonical order.  The backward accumulates grad_w with exact 128-bit
+// fixed-point adds, so its result does not depend on thread order.
+#include <math.h>
+
+#include "common.cuh"
+#include "hop.cuh"
+#include "scan.cuh"
+
+namespace fl {
+namespace {
+
+constexpr int64_t kNoBudget = int64_t(1) << 62;
+
+struct Side {
+    const int32_t *row_ptr, *col, *order, *gptr, *gstart, *gcount;
+    const int16_t *grel;
+    const float *mask_csr;
+};
+
+__device__ __forceinline__ int64_t find_row(const int64_t *row_ptr, int64_t rows, int64_t i) {
+    int64_t lo = 0, hi = rows;  // largest r with row_ptr[r] <= i
+    while (lo < hi) {
+        int64_t mid = (lo + hi + 1) >> 1;
+        if (row_ptr[mid] <= i) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+// ---------------------------------------------------------------------------
+// Plan: per-entry fact capacity (budget-capped degree per side + identity).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int64_t side_degree(const Side &s, int64_t src) {
+    // Groups of a source are contiguous in CSR order, so its degree follows
+    // from the first group's start and the last group's end.
+    const int64_t g0 = s.gptr[src], g1 = s.gptr[src + 1];
+    return g0 == g1 ? 0 : static_cast<int64_t>(s.gstart[g1 - 1]) + s.gcount[g1 - 1] - s.gstart[g0];
+}
+
+__global__ void hop_capacity_kernel(const int32_t *ent, int64_t S, Side ori, Side inv, int64_t topk,
+                                    int wot_i, int64_t *cap) {
+    int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (i >= S) return;
+    int64_t src = ent[i];
+    int64_t d0 = side_degree(ori, src);
+    int64_t d1 = side_degree(inv, src);
+    if (topk < kNoBudget) { d0 = d0 < topk ? d0 : topk; d1 = d1 < topk ? d1 : topk; }
+    cap[i] = d0 + d1 + (wot_i ? 0 : 1);
+}
+
+// ---------------------------------------------------------------------------
+// Expansion: one warp per source entry.
+// ---------------------------------------------------------------------------
+constexpr int kExpandWarps = 8;
+
+struct WarpScratch {
+    unsigned int hist[256];
+    int32_t incl[32];
+    int32_t start[32];
+    float prod[32];
+    int32_t rel[32];
+    int32_t quota[32];
+};
+
+// Weighted order statistic over the groups' weights (flashlog.cu:26-63): the
+// key T with sum(count | key > T) < budget <= sum(count | key >= T).  Returns
+// T and the number of edges to keep at T.  Only groups with w > 0 count.
+__device__ void group_threshold(const float *wdir, const Side &sd, int64_t g0, int64_t g1, int64_t budget,
+                                WarpScratch &ws, uint32_t *thr, int64_t *keep) {
+    const int lane = threadIdx.x & 31;
+    uint32_t prefix = 0, pmask = 0;
+    int64_t krem = budget;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int d = lane; d < 256; d += 32) ws.hist[d] = 0;
+        __syncwarp();
+        for (int64_t g = g0 + lane; g < g1; g += 32) {
+            float wg = wdir[sd.grel[g]];
+            if (!(wg > 0.0f)) continue;
+            uint32_t key = __float_as_uint(wg);
+            if ((key & pmask) == prefix) atomicAdd(&ws.hist[(key >> shift) & 255u], static_cast<unsigned>(sd.gcount[g]));
+        }
+        __syncwarp();
+        // lane j owns digits 255 - 8j .. 248 - 8j (descending)
+        int64_t part = 0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) part += ws.hist[255 - (lane * 8 + k)];
+        int64_t incl = warp_inclusive_scan(part);
+        int64_t excl = incl - part;
+        unsigned ball = __ballot_sync(kFull, incl >= krem && excl < krem);
+        int src_lane = __ffs(ball) - 1;  // exactly one lane crosses krem
+        int digit = 0;
+        int64_t above = 0;
+        if (lane == src_lane) {
+            int64_t acc = excl;
+            for (int k = 0; k < 8; ++k) {
+                int d = 255 - (lane * 8 + k);
+                int64_t h = ws.hist[d];
+                if (acc + h >= krem) { digit = d; above = acc; break; }
+                acc += h;
+            }
+        }
+        digit = __shfl_sync(kFull, digit, src_lane);
+        above = __shfl_sync(kFull, above, src_lane);
+        krem -= above;
+        prefix |= static_cast<uint32_t>(digit) << shift;
+        pmask |= 255u << shift;
+        __syncwarp();
+    }
+    *thr = prefix;
+    *keep = krem;
+}
+
+struct ExpandArgs {
+    const int64_t *row_ptr;
+    const int32_t *ent;
+    const float *val;
+    int64_t S, rows, n, r_size, topk, flags, seed, L;
+    const float *w;
+    Side ori, inv;
+    const uint8_t *mask_triple;
+    const float *edge_weight;
+    const int64_t *slot_base;
+    int32_t *fact_dst;
+    float *fact_val;
+    int16_t *fact_rel;
+    float *fact_m;
+    int32_t *entry_count;
+};
+
+__device__ __forceinline__ double splitmix_phase(int64_t seed, int64_t b, int64_t l, int64_t src, bool inv) {
+    uint64_t z = static_cast<uint64_t>(seed) ^ (static_cast<uint64_t>(b) * 0x9e3779b97f4a7c15ULL) ^
+                 (static_cast<uint64_t>(l) * 0xbf58476d1ce4e5b9ULL) ^ (static_cast<uint64_t>(src) * 0x94d049bb133111ebULL) ^
+                 (inv ? 0xd1b54a32d192ed03ULL : 0x8cb92baa3f3d8dd7ULL);
+    z += 0x9e3779b97f4a7c15ULL;
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ULL;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebULL;
+    z ^= z >> 31;
+    return static_cast<double>(z >> 11) * 0x1.0p-53;
+}
+
+__global__ void __launch_bounds__(kExpandWarps * 32) hop_expand_kernel(ExpandArgs a) {
+    __shared__ WarpScratch scratch[kExpandWarps];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    WarpScratch &ws = scratch[wib];
+    const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kExpandWarps;
+    const bool skip_nonpos = (a.flags & FL_SKIP_NONPOS_W) != 0;
+    const bool drop_masked = (a.flags & FL_DROP_MASKED) != 0;
+    const bool sampled = (a.flags & FL_SAMPLED) != 0;
+    const bool edge_w = (a.flags & FL_EDGE_WEIGHT) != 0 && a.edge_weight != nullptr;
+    const bool edge_score = (a.flags & FL_EDGE_SCORE) != 0;
+    const bool wot_i = (a.flags & FL_WOT_I) != 0;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * kExpandWarps + wib; i < a.S; i += nwarps) {
+        const int64_t row = find_row(a.row_ptr, a.rows, i);
+        const int64_t src = a.ent[i];
+        const float v = a.val[i];
+        const float *wrow = a.w + row * a.n;
+        const int64_t out = a.slot_base[i];
+        int64_t written = 0;
+        for (int dir = 0; dir < 2; ++dir) {
+            const Side &sd = dir ? a.inv : a.ori;
+            const int64_t off = dir ? a.r_size : 0;
+            const float *wdir = wrow + off;
+            const int64_t g0 = sd.gptr[src], g1 = sd.gptr[src + 1];
+            if (g0 == g1) continue;
+            bool use_thr = false;
+            uint32_t thr = 0;
+            int64_t keep_thr = 0;
+            // sampled-mode state (lane 0 only)
+            int64_t q_target = 0, q_residual = 0, q_spare = 0, q_left = 0, q_capleft = 0, q_prefix = 0;
+            double q_wsum = 0.0, q_phase = 0.0;
+            if (sampled) {
+                if (lane == 0) {
+                    int64_t capacity = 0;
+                    double wsum = 0.0;
+                    for (int64_t g = g0; g < g1; ++g) {
+                        double wt = wdir[sd.grel[g]];
+                        if (wt > 0 && sd.gcount[g] > 0) { capacity += sd.gcount[g]; wsum += wt; }
+                    }
+                    q_target = a.topk < capacity ? a.topk : capacity;
+                    q_wsum = wsum;
+                    int64_t allocated = capacity;
+                    if (q_target < capacity) {
+                        allocated = 0;
+                        for (int64_t g = g0; g < g1; ++g) {
+                            double wt = wdir[sd.grel[g]];
+                            int64_t c = sd.gcount[g];
+                            if (wt > 0 && c > 0)
+                                allocated += static_cast<int64_t>(fmin(static_cast<double>(c),
+                                                                       floor(static_cast<double>(q_target) * wt / wsum)));
+                        }
+                    }
+                    q_residual = q_target - allocated;
+                    q_spare = capacity - allocated;
+                    q_left = q_residual;
+                    q_capleft = q_spare;
+                    q_phase = splitmix_phase(a.seed, row / a.L, row % a.L, src, dir == 1);
+                    q_prefix = 0;
+                }
+            } else if (skip_nonpos && a.topk < kNoBudget) {
+                int64_t total = 0;
+                for (int64_t g = g0 + lane; g < g1; g += 32)
+                    if (wdir[sd.grel[g]] > 0.0f) total += sd.gcount[g];
+                total = warp_sum(total);
+                if (total > a.topk) {
+                    use_thr = true;
+                    group_threshold(wdir, sd, g0, g1, a.topk, ws, &thr, &keep_thr);
+                }
+            }
+            int64_t tie_seen = 0;
+            for (int64_t cb = g0; cb < g1; cb += 32) {
+                const int64_t g = cb + lane;
+                const bool valid = g < g1;
+                int32_t rel = valid ? sd.grel[g] : 0;
+                int32_t cnt = valid ? sd.gcount[g] : 0;
+                float wg = valid ? wdir[rel] : 0.0f;
+                int32_t take;
+                if (sampled) {
+                    // Sequential quota arithmetic of flashlog.cu:1505-1531, lane 0.
+                    ws.rel[lane] = rel;
+                    __syncwarp();
+                    if (lane == 0) {
+                        int64_t nvalid = (g1 - cb) < 32 ? (g1 - cb) : 32;
+                        for (int k = 0; k < nvalid; ++k) {
+                            int32_t c = sd.gcount[cb + k];
+                            float sc = wdir[ws.rel[k]];
+                            int64_t cur = sc > 0.0f ? c : 0;
+                            if (cur > 0 && q_spare > 0) {
+                                int64_t base = static_cast<int64_t>(fmin(static_cast<double>(c),
+                                    floor(static_cast<double>(q_target) * static_cast<double>(sc) / q_wsum)));
+                                int64_t spare = static_cast<int64_t>(c) - base;
+                                q_prefix += spare;
+                                q_capleft -= spare;
+                                int64_t cumulative = q_prefix == q_spare ? q_residual
+                                    : static_cast<int64_t>(floor(static_cast<double>(q_residual) * static_cast<double>(q_prefix) /
+                                                                 static_cast<double>(q_spare) + q_phase));
+                                int64_t extra = cumulative - (q_residual - q_left);
+                                int64_t lim = spare < q_left ? spare : q_left;
+                                extra = extra < lim ? extra : lim;
+                                extra = extra > 0 ? extra : 0;
+                                extra = extra > (q_left - q_capleft) ? extra : (q_left - q_capleft);
+                                q_left -= extra;
+                                cur = base + extra;
+                            }
+                            ws.quota[k] = static_cast<int32_t>(cur);
+                        }
+                    }
+                    __syncwarp();
+                    take = valid ? ws.quota[lane] : 0;
+                } else if (!skip_nonpos) {
+                    take = cnt;
+                } else if (!use_thr) {
+                    take = wg > 0.0f ? cnt : 0;
+                } else {
+                    uint32_t key = __float_as_uint(wg);
+                    bool pos = wg > 0.0f;
+                    bool tie = valid && pos && key == thr;
+                    int64_t tcnt = tie ? cnt : 0;
+                    int64_t tincl = warp_inclusive_scan(tcnt);
+                    int64_t texcl = tincl - tcnt + tie_seen;
+                    tie_seen += __shfl_sync(kFull, tincl, 31);
+                    if (!pos || key < thr) take = 0;
+                    else if (key > thr) take = cnt;
+                    else {
+                        int64_t left = keep_thr - texcl;
+                        take = left > 0 ? static_cast<int32_t>(left < cnt ? left : cnt) : 0;
+                    }
+                }
+                if (!valid) take = 0;
+                int32_t incl = warp_inclusive_scan(take);
+                int32_t tot = __shfl_sync(kFull, incl, 31);
+                ws.incl[lane] = incl;
+                ws.start[lane] = valid ? sd.gstart[g] : 0;
+                ws.prod[lane] = v * wg;
+                ws.rel[lane] = rel + static_cast<int32_t>(off);
+                __syncwarp();
+                for (int32_t f0 = 0; f0 < tot; f0 += 32) {
+                    const int32_t f = f0 + lane;
+                    const bool act = f < tot;
+                    bool visible = false;
+                    int32_t dst = 0, frel = 0;
+                    float value = 0.0f, m = 1.0f;
+                    if (act) {
+                        int lo = 0, hi = 31;  // first lane with incl > f
+                        while (lo < hi) { int mid = (lo + hi) >> 1; if (ws.incl[mid] > f) hi = mid; else lo = mid + 1; }
+                        const int32_t eoff = f - (lo ? ws.incl[lo - 1] : 0);
+                        const int64_t p = static_cast<int64_t>(ws.start[lo]) + eoff;
+                        visible = true;
+                        if (a.mask_triple) {
+                            const int64_t edge = sd.order[p];
+                            const bool mv = a.mask_triple[edge] != 0;
+                            m = mv ? 1.0f : 0.0f;
+                            if (edge_w) {
+                                float ew = a.edge_weight[edge];
+                                m *= edge_score ? ew : 1.0f / (1.0f + expf(-ew));
+                            }
+                            if (drop_masked && !mv) visible = false;
+                        } else if (sd.mask_csr) {
+                            m = sd.mask_csr[p];
+                            if (drop_masked && m == 0.0f) visible = false;
+                        }
+                        dst = sd.col[p];
+                        value = ws.prod[lo] * m;
+                        frel = ws.rel[lo];
+                    }
+                    const unsigned ball = __ballot_sync(kFull, act && visible);
+                    if (act && visible) {
+                        const int64_t pos = out + written + __popc(ball & lanemask_lt());
+                        a.fact_dst[pos] = dst;
+                        a.fact_val[pos] = value;
+                        a.fact_rel[pos] = static_cast<int16_t>(frel);
+                        if (a.fact_m) a.fact_m[pos] = m;
+                    }
+                    written += __popc(ball);
+                }
+                __syncwarp();
+            }
+        }
+        if (!wot_i) {
+            if (lane == 0) {
+                const int64_t pos = out + written;
+                a.fact_dst[pos] = static_cast<int32_t>(src);
+                a.fact_val[pos] = v * wrow[a.n - 1];
+                a.fact_rel[pos] = static_cast<int16_t>(a.n - 1);
+                if (a.fact_m) a.fact_m[pos] = 1.0f;
+            }
+            written += 1;
+        }
+        if (lane == 0) a.entry_count[i] = static_cast<int32_t>(written);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Row reduction: stable radix sort by destination in shared memory.
+// ---------------------------------------------------------------------------
+constexpr int kRThreads = 512;
+constexpr int kRWarps = kRThreads / 32;
+constexpr int kTile = 8192;             // facts sorted at once
+constexpr int kWarpItems = kTile / kRWarps;  // 512 per warp region
+constexpr int kLoadK = 4;               // flat facts per thread per load step
+constexpr int kLoadStep = kRThreads * kLoadK;
+constexpr int kEChunk = 1024;           // entries per prefix chunk
+constexpr int kBins = 1024;             // histogram bins per refinement level
+constexpr int kDenseW = 4096;           // widest destination window summed densely
+
+struct ReduceSmem {
+    uint32_t key[2][kTile];
+    uint16_t idx[2][kTile];
+    float val[kTile];
+    uint32_t slot[kTile];
+    uint32_t shist[kRWarps][256];
+    uint32_t lvl1[kBins];
+    uint32_t lvl2[kBins];
+    uint32_t epre[kEChunk + 1];
+    uint32_t eslot[kEChunk];
+    float acc[kDenseW];
+    uint32_t touched[kDenseW / 32];
+    uint16_t items1[kBins + 1];
+    uint16_t items2[kBins + 1];
+    int64_t scan_scratch[kRWarps + 1];
+    float fscratch[kRWarps + 1];
+    int n_items1, n_items2;
+};
+
+struct ReduceArgs {
+    const int64_t *row_ptr;      // rows of the (selected) state
+    int64_t rows;
+    const int64_t *slot_base;    // per entry
+    const int32_t *entry_count;  // per entry
+    const int32_t *fact_dst;
+    const float *fact_val;
+    int64_t E;
+    int32_t *fact_pos;           // may be null
+    int32_t *tmp_ent;            // outputs at the row's slot base
+    float *tmp_x;
+    int64_t *out_count;
+    float *out_sum;
+};
+
+__device__ __forceinline__ int bits_for(int64_t width) {  // bits to represent width - 1
+    int b = 0;
+    while ((int64_t(1) << b) < width) ++b;
+    return b;
+}
+
+// Stream the row's facts in canonical order; for each fact whose destination
+// lies in [lo, hi) call visit(slot, dst, pos) where pos is the ordinal among
+// visited facts.  Returns the number visited.  All threads must call it.
+template <typename Visit>
+__device__ int64_t stream_row(const ReduceArgs &a, ReduceSmem &sm, int64_t ea, int64_t eb, int64_t lo, int64_t hi,
+                              Visit visit) {
+    int64_t visited = 0;
+    for (int64_t ec = ea; ec < eb; ec += kEChunk) {
+        const int64_t ne = (eb - ec) < kEChunk ? (eb - ec) : kEChunk;
+        // prefix of entry fact counts within the chunk (2 entries per thread)
+        int64_t c0 = 0, c1 = 0;
+        const int64_t j0 = ec + 2 * threadIdx.x, j1 = j0 + 1;
+        if (2 * threadIdx.x < ne) { c0 = a.entry_count[j0]; sm.eslot[2 * threadIdx.x] = static_cast<uint32_t>(a.slot_base[j0]); }
+        if (2 * threadIdx.x + 1 < ne) { c1 = a.entry_count[j1]; sm.eslot[2 * threadIdx.x + 1] = static_cast<uint32_t>(a.slot_base[j1]); }
+        int64_t tot;
+        int64_t ex = block_exclusive_scan<int64_t>(c0 + c1, sm.scan_scratch, &tot);
+        if (2 * threadIdx.x < ne) sm.epre[2 * threadIdx.x] = static_cast<uint32_t>(ex);
+        if (2 * threadIdx.x + 1 < ne) sm.epre[2 * threadIdx.x + 1] = static_cast<uint32_t>(ex + c0);
+        if (threadIdx.x == 0) sm.epre[ne] = static_cast<uint32_t>(tot);
+        __syncthreads();
+        const uint32_t nf = static_cast<uint32_t>(tot);
+        for (uint32_t fb = 0; fb < nf; fb += kLoadStep) {
+            uint32_t slot[kLoadK];
+            int32_t dst[kLoadK];
+            int cnt = 0;
+#pragma unroll
+            for (int k = 0; k < kLoadK; ++k) {
+                const uint32_t f = fb + threadIdx.x * kLoadK + k;
+                dst[k] = -1;
+                if (f < nf) {
+                    int l2 = 0, h2 = static_cast<int>(ne) - 1;  // last entry with epre <= f
+                    while (l2 < h2) { int mid = (l2 + h2 + 1) >> 1; if (sm.epre[mid] <= f) l2 = mid; else h2 = mid - 1; }
+                    slot[k] = sm.eslot[l2] + (f - sm.epre[l2]);
+                    int32_t d = a.fact_dst[slot[k]];
+                    if (d >= lo && d < hi) { dst[k] = d; ++cnt; }
+                }
+            }
+            int64_t btot;
+            int64_t bex = block_exclusive_scan<int64_t>(cnt, sm.scan_scratch, &btot);
+            int64_t pos = visited + bex;
+#pragma unroll
+            for (int k = 0; k < kLoadK; ++k)
+                if (dst[k] >= 0) visit(slot[k], dst[k], pos++);
+            visited += btot;
+            __syncthreads();
+        }
+    }
+    return visited;
+}
+
+// Stable LSD radix sort of sm.key[0][0..n) with payload sm.idx[0] over `bits`
+// key bits.  Returns the buffer index (0/1) holding the result.
+__device__ int tile_sort(ReduceSmem &sm, int n, int bits) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int cur = 0;
+    for (int shift = 0; shift < bits; shift += 8) {
+        const int nb = (bits - shift) < 8 ? (bits - shift) : 8;
+        const uint32_t dmask = (1u << nb) - 1u;
+        const int ndig = 1 << nb;
+        for (int d = lane; d < 256; d += 32) sm.shist[warp][d] = 0;
+        __syncwarp();
+        const int wbase = warp * kWarpItems;
+        for (int k = 0; k < kWarpItems / 32; ++k) {
+            int j = wbase + k * 32 + lane;
+            if (j < n) atomicAdd(&sm.shist[warp][(sm.key[cur][j] >> shift) & dmask], 1u);
+        }
+        __syncthreads();
+        // digit-major exclusive offsets: thread t < ndig owns digit t
+        uint32_t dsum = 0;
+        if (static_cast<int>(threadIdx.x) < ndig)
+            for (int w2 = 0; w2 < kRWarps; ++w2) dsum += sm.shist[w2][threadIdx.x];
+        int64_t tot;
+        int64_t dex = block_exclusive_scan<int64_t>(static_cast<int64_t>(threadIdx.x < static_cast<unsigned>(ndig) ? dsum : 0),
+                                                    sm.scan_scratch, &tot);
+        if (static_cast<int>(threadIdx.x) < ndig) {
+            uint32_t run = static_cast<uint32_t>(dex);
+            for (int w2 = 0; w2 < kRWarps; ++w2) {
+                uint32_t h = sm.shist[w2][threadIdx.x];
+                sm.shist[w2][threadIdx.x] = run;
+                run += h;
+            }
+        }
+        __syncthreads();
+        for (int k = 0; k < kWarpItems / 32; ++k) {
+            int j = wbase + k * 32 + lane;
+            bool valid = j < n;
+            uint32_t key = valid ? sm.key[cur][j] : 0u;
+            uint32_t d = (key >> shift) & dmask;
+            unsigned act = __ballot_sync(kFull, valid);
+            if (valid) {
+                unsigned peers = __match_any_sync(act, d);
+                int rank = __popc(peers & lanemask_lt());
+                uint32_t base = sm.shist[warp][d];
+                int leader = __ffs(peers) - 1;
+                sm.key[cur ^ 1][base + rank] = key;
+                sm.idx[cur ^ 1][base + rank] = sm.idx[cur][j];
+                __syncwarp(act);
+                if (lane == leader) sm.shist[warp][d] = base + __popc(peers);
+            }
+            __syncwarp();
+        }
+        __syncthreads();
+        cur ^= 1;
+    }
+    return cur;
+}
+
+// Sort the loaded tile [0, n) (keys are dst - lo) and emit one output per
+// destination, summing in canonical order.  Returns the block-sum of outputs.
+__device__ float emit_sorted(const ReduceArgs &a, ReduceSmem &sm, int n, int bits, int64_t lo, int64_t obase,
+                             int64_t *written) {
+    const int cur = tile_sort(sm, n, bits);
+    uint32_t *seg = sm.key[cur ^ 1];  // free buffer: segment starts
+    int64_t nseg_total = 0;
+    for (int base = 0; base < n; base += kRThreads) {
+        int j = base + threadIdx.x;
+        bool head = j < n && (j == 0 || sm.key[cur][j] != sm.key[cur][j - 1]);
+        int64_t tot;
+        int64_t ex = block_exclusive_scan<int64_t>(head ? 1 : 0, sm.scan_scratch, &tot);
+        if (head) seg[nseg_total + ex] = static_cast<uint32_t>(j);
+        nseg_total += tot;
+    }
+    __syncthreads();
+    const int nseg = static_cast<int>(nseg_total);
+    float local = 0.0f;
+    for (int s = threadIdx.x; s < nseg; s += kRThreads) {
+        const int st = static_cast<int>(seg[s]);
+        const int en = s + 1 < nseg ? static_cast<int>(seg[s + 1]) : n;
+        float x = 0.0f;
+        for (int q = st; q < en; ++q) x += sm.val[sm.idx[cur][q]];
+        const int64_t oi = *written + s;
+        a.tmp_ent[obase + oi] = static_cast<int32_t>(lo + sm.key[cur][st]);
+        a.tmp_x[obase + oi] = x;
+        if (a.fact_pos)
+            for (int q = st; q < en; ++q) a.fact_pos[sm.slot[sm.idx[cur][q]]] = static_cast<int32_t>(oi);
+        local += x;
+    }
+    *written += nseg;
+    float total = block_sum(local, sm.fscratch);
+    return total;
+}
+
+// Process the destination range [lo, hi) holding `count` <= kTile facts.
+__device__ float process_sorted_range(const ReduceArgs &a, ReduceSmem &sm, int64_t ea, int64_t eb, int64_t lo,
+                                      int64_t hi, int64_t obase, int64_t *written) {
+    int64_t n = stream_row(a, sm, ea, eb, lo, hi, [&](uint32_t slot, int32_t dst, int64_t pos) {
+        sm.key[0][pos] = static_cast<uint32_t>(dst - lo);
+        sm.idx[0][pos] = static_cast<uint16_t>(pos);
+        sm.val[pos] = a.fact_val[slot];
+        sm.slot[pos] = slot;
+    });
+    __syncthreads();
+    if (n == 0) return 0.0f;
+    return emit_sorted(a, sm, static_cast<int>(n), bits_for(hi - lo), lo, obase, written);
+}
+
+// Dense window [lo, hi), hi - lo <= kDenseW, any number of facts: tiles of
+// canonical order are stably sorted and added into acc[] one fact at a time.
+__device__ float process_dense_range(const ReduceArgs &a, ReduceSmem &sm, int64_t ea, int64_t eb, int64_t lo,
+                                     int64_t hi, int64_t obase, int64_t *written) {
+    const int W = static_cast<int>(hi - lo);
+    const int bits = bits_for(W);
+    for (int d = threadIdx.x; d < kDenseW; d += kRThreads) sm.acc[d] = 0.0f;
+    for (int d = threadIdx.x; d < kDenseW / 32; d += kRThreads) sm.touched[d] = 0u;
+    __syncthreads();
+    int64_t in_tile = 0;
+    auto flush = [&](int n) {
+        if (n == 0) return;
+        const int cur = tile_sort(sm, n, bits);
+        for (int j = threadIdx.x; j < n; j += kRThreads) {
+            bool head = (j == 0 || sm.key[cur][j] != sm.key[cur][j - 1]);
+            if (!head) continue;
+            const uint32_t d = sm.key[cur][j];
+            float accv = sm.acc[d];
+            for (int q = j; q < n && sm.key[cur][q] == d; ++q) accv += sm.val[sm.idx[cur][q]];
+            sm.acc[d] = accv;
+            atomicOr(&sm.touched[d >> 5], 1u << (d & 31));
+        }
+        __syncthreads();
+    };
+    // Stream in canonical order; flush whenever the next load step might overflow the tile.
+    for (int64_t ec = ea; ec < eb; ec += kEChunk) {
+        const int64_t ne = (eb - ec) < kEChunk ? (eb - ec) : kEChunk;
+        int64_t c0 = 0, c1 = 0;
+        const int64_t j0 = ec + 2 * threadIdx.x, j1 = j0 + 1;
+        if (2 * threadIdx.x < ne) { c0 = a.entry_count[j0]; sm.eslot[2 * threadIdx.x] = static_cast<uint32_t>(a.slot_base[j0]); }
+        if (2 * threadIdx.x + 1 < ne) { c1 = a.entry_count[j1]; sm.eslot[2 * threadIdx.x + 1] = static_cast<uint32_t>(a.slot_base[j1]); }
+        int64_t tot;
+        int64_t ex = block_exclusive_scan<int64_t>(c0 + c1, sm.scan_scratch, &tot);
+        if (2 * threadIdx.x < ne) sm.epre[2 * threadIdx.x] = static_cast<uint32_t>(ex);
+        if (2 * threadIdx.x + 1 < ne) sm.epre[2 * threadIdx.x + 1] = static_cast<uint32_t>(ex + c0);
+        if (threadIdx.x == 0) sm.epre[ne] = static_cast<uint32_t>(tot);
+        __syncthreads();
+        const uint32_t nf = static_cast<uint32_t>(tot);
+        for (uint32_t fb = 0; fb < nf; fb += kLoadStep) {
+            if (in_tile + kLoadStep > kTile) { flush(static_cast<int>(in_tile)); in_tile = 0; }
+            uint32_t slot[kLoadK];
+            int32_t dst[kLoadK];
+            int cnt = 0;
+#pragma unroll
+            for (int k = 0; k < kLoadK; ++k) {
+                const uint32_t f = fb + threadIdx.x * kLoadK + k;
+                dst[k] = -1;
+                if (f < nf) {
+                    int l2 = 0, h2 = static_cast<int>(ne) - 1;
+                    while (l2 < h2) { int mid = (l2 + h2 + 1) >> 1; if (sm.epre[mid] <= f) l2 = mid; else h2 = mid - 1; }
+                    slot[k] = sm.eslot[l2] + (f - sm.epre[l2]);
+                    int32_t d = a.fact_dst[slot[k]];
+                    if (d >= lo && d < hi) { dst[k] = d; ++cnt; }
+                }
+            }
+            int64_t btot;
+            int64_t bex = block_exclusive_scan<int64_t>(cnt, sm.scan_scratch, &btot);
+            int64_t pos = in_tile + bex;
+#pragma unroll
+            for (int k = 0; k < kLoadK; ++k)
+                if (dst[k] >= 0) {
+                    sm.key[0][pos] = static_cast<uint32_t>(dst[k] - lo);
+                    sm.idx[0][pos] = static_cast<uint16_t>(pos);
+                    sm.val[pos] = a.fact_val[slot[k]];
+                    ++pos;
+                }
+            in_tile += btot;
+            __syncthreads();
+        }
+    }
+    flush(static_cast<int>(in_tile));
+    // Output index of every touched destination (ordered compaction).
+    uint32_t *oidx = sm.key[1];
+    int64_t nout = 0;
+    float local = 0.0f;
+    for (int base = 0; base < W; base += kRThreads) {
+        int d = base + threadIdx.x;
+        bool t = d < W && ((sm.touched[d >> 5] >> (d & 31)) & 1u);
+        int64_t tot;
+        int64_t ex = block_exclusive_scan<int64_t>(t ? 1 : 0, sm.scan_scratch, &tot);
+        if (t) {
+            const int64_t oi = *written + nout + ex;
+            oidx[d] = static_cast<uint32_t>(oi);
+            a.tmp_ent[obase + oi] = static_cast<int32_t>(lo + d);
+            a.tmp_x[obase + oi] = sm.acc[d];
+            local += sm.acc[d];
+        }
+        nout += tot;
+    }
+    __syncthreads();
+    if (a.fact_pos) {
+        stream_row(a, sm, ea, eb, lo, hi, [&](uint32_t slot, int32_t dst, int64_t) {
+            a.fact_pos[slot] = static_cast<int32_t>(oidx[dst - lo]);
+        });
+    }
+    *written += nout;
+    return block_sum(local, sm.fscratch);
+}
+
+// Greedy split of consecutive histogram bins into items of <= kTile facts; a
+// bin above kTile always forms an item of its own.  Writes item start bins
+// followed by the kBins sentinel and returns the number of items.
+__device__ int split_bins(const uint32_t *hist, uint16_t *items) {
+    int n = 0, start = 0;
+    uint32_t accum = 0;
+    for (int b = 0; b < kBins; ++b) {
+        const uint32_t h = hist[b];
+        if (h > static_cast<uint32_t>(kTile)) {
+            if (b > start) items[n++] = static_cast<uint16_t>(start);
+            items[n++] = static_cast<uint16_t>(b);
+            start = b + 1;
+            accum = 0;
+            continue;
+        }
+        if (accum + h > static_cast<uint32_t>(kTile)) {
+            items[n++] = static_cast<uint16_t>(start);
+            start = b;
+            accum = 0;
+        }
+        accum += h;
+    }
+    if (start < kBins) items[n++] = static_cast<uint16_t>(start);
+    items[n] = kBins;
+    return n;
+}
+
+__global__ void __launch_bounds__(kRThreads, 1) row_reduce_kernel(ReduceArgs a) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    ReduceSmem &sm = *reinterpret_cast<ReduceSmem *>(smem_raw);
+    const int64_t r = blockIdx.x;
+    if (r >= a.rows) return;
+    const int64_t ea = a.row_ptr[r], eb = a.row_ptr[r + 1];
+    if (ea == eb) {
+        if (threadIdx.x == 0) { a.out_count[r] = 0; a.out_sum[r] = 0.0f; }
+        return;
+    }
+    const int64_t obase = a.slot_base[ea];
+    int64_t F = 0;
+    for (int64_t e = ea + threadIdx.x; e < eb; e += kRThreads) F += a.entry_count[e];
+    F = block_sum(F, sm.scan_scratch);
+    int64_t written = 0;
+    float rsum = 0.0f;
+    if (F <= kTile) {
+        rsum = process_sorted_range(a, sm, ea, eb, 0, a.E, obase, &written);
+    } else {
+        const int b1 = bits_for(a.E);
+        const int sh1 = b1 > 10 ? b1 - 10 : 0;
+        for (int b = threadIdx.x; b < kBins; b += kRThreads) sm.lvl1[b] = 0;
+        __syncthreads();
+        stream_row(a, sm, ea, eb, 0, a.E, [&](uint32_t, int32_t dst, int64_t) { atomicAdd(&sm.lvl1[dst >> sh1], 1u); });
+        __syncthreads();
+        if (threadIdx.x == 0) sm.n_items1 = split_bins(sm.lvl1, sm.items1);
+        __syncthreads();
+        const int n1 = sm.n_items1;
+        for (int it = 0; it < n1; ++it) {
+            const int bl = sm.items1[it], bh = sm.items1[it + 1];
+            uint32_t cnt = 0;
+            for (int b = bl; b < bh; ++b) cnt += sm.lvl1[b];
+            const int64_t lo = static_cast<int64_t>(bl) << sh1;
+            int64_t hi = static_cast<int64_t>(bh) << sh1;
+            if (hi > a.E) hi = a.E;
+            if (cnt == 0 || lo >= hi) continue;
+            if (cnt <= static_cast<uint32_t>(kTile)) {
+                rsum += process_sorted_range(a, sm, ea, eb, lo, hi, obase, &written);
+            } else if (hi - lo <= kDenseW) {
+                rsum += process_dense_range(a, sm, ea, eb, lo, hi, obase, &written);
+            } else {
+                const int b2 = bits_for(hi - lo);
+                const int sh2 = b2 > 10 ? b2 - 10 : 0;
+                for (int b = threadIdx.x; b < kBins; b += kRThreads) sm.lvl2[b] = 0;
+                __syncthreads();
+                stream_row(a, sm, ea, eb, lo, hi,
+                           [&](uint32_t, int32_t dst, int64_t) { atomicAdd(&sm.lvl2[(dst - lo) >> sh2], 1u); });
+                __syncthreads();
+                if (threadIdx.x == 0) sm.n_items2 = split_bins(sm.lvl2, sm.items2);
+                __syncthreads();
+                const int n2 = sm.n_items2;
+                for (int it2 = 0; it2 < n2; ++it2) {
+                    const int cl = sm.items2[it2], ch = sm.items2[it2 + 1];
+                    uint32_t c2 = 0;
+                    for (int b = cl; b < ch; ++b) c2 += sm.lvl2[b];
+                    const int64_t lo2 = lo + (static_cast<int64_t>(cl) << sh2);
+                    int64_t hi2 = lo + (static_cast<int64_t>(ch) << sh2);
+                    if (hi2 > hi) hi2 = hi;
+                    if (c2 == 0 || lo2 >= hi2) continue;
+                    if (c2 <= static_cast<uint32_t>(kTile))
+                        rsum += process_sorted_range(a, sm, ea, eb, lo2, hi2, obase, &written);
+                    else
+                        rsum += process_dense_range(a, sm, ea, eb, lo2, hi2, obase, &written);
+                }
+            }
+        }
+    }
+    if (threadIdx.x == 0) { a.out_count[r] = written; a.out_sum[r] = rsum; }
+}
+
+// Compact per-row outputs (at the row's slot base) into a row layout and
+// write normalized values.
+__global__ void compact_kernel(const int64_t *row_ptr, const int64_t *slot_base, const int64_t *out_row_ptr,
+                               int64_t rows, const int32_t *tmp_ent, const float *tmp_x, const float *out_sum,
+                               float eps, int32_t *out_ent, float *out_x, float *out_y, float *out_denom) {
+    const int64_t r = blockIdx.x;
+    if (r >= rows) return;
+    const int64_t o0 = out_row_ptr[r], n = out_row_ptr[r + 1] - o0;
+    const float d = out_sum[r];
+    if (threadIdx.x == 0 && out_denom) out_denom[r] = d;
+    if (n == 0) return;
+    const int64_t src0 = slot_base[row_ptr[r]];
+    const float dd = d > eps ? d : eps;
+    for (int64_t k = threadIdx.x; k < n; k += blockDim.x) {
+        float x = tmp_x[src0 + k];
+        out_ent[o0 + k] = tmp_ent[src0 + k];
+        if (out_x) out_x[o0 + k] = x;
+        if (out_y) out_y[o0 + k] = x / dd;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Backward of one hop (+ normalization).
+// ---------------------------------------------------------------------------
+constexpr int kBThreads = 256;
+constexpr int kSmemRel = 4096;  // relations whose exact grad_w accumulators fit in shared memory
+
+struct BackwardArgs {
+    const int64_t *row_ptr;
+    const float *val;
+    const float *w;
+    int64_t rows, n;
+    float eps;
+    int normalize;
+    const int64_t *slot_base;
+    const int32_t *entry_count;
+    const int32_t *fact_pos;
+    const int16_t *fact_rel;
+    const float *fact_m;
+    const int64_t *out_row_ptr;
+    const float *out_x;
+    const float *out_denom;
+    const float *g_y;
+    float *grad_val;
+    float *grad_w;
+    unsigned long long *gacc;  // rows * n * 2 exact accumulators when n > kSmemRel
+};
+
+__global__ void __launch_bounds__(kBThreads) hop_backward_kernel(BackwardArgs a) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    unsigned long long *sacc = reinterpret_cast<unsigned long long *>(smem_raw);
+    __shared__ float fscratch[kBThreads / 32 + 1];
+    __shared__ int64_t iscratch[kBThreads / 32 + 1];
+    const int64_t r = blockIdx.x;
+    if (r >= a.rows) return;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t oa = a.out_row_ptr[r], ob = a.out_row_ptr[r + 1];
+    const int64_t ea = a.row_ptr[r], eb = a.row_ptr[r + 1];
+    const bool in_smem = a.n <= kSmemRel;
+    unsigned long long *acc = in_smem ? sacc : a.gacc + static_cast<size_t>(r) * a.n * 2;
+    for (int64_t c = threadIdx.x; c < 2 * a.n; c += kBThreads) acc[c] = 0ull;
+    float d = a.out_denom ? a.out_denom[r] : 1.0f;
+    float dd = d > a.eps ? d : a.eps;
+    float corr = 0.0f;
+    if (a.normalize) {
+        float s = 0.0f;
+        for (int64_t u = oa + threadIdx.x; u < ob; u += kBThreads) s += a.g_y[u] * a.out_x[u];
+        s = block_sum(s, fscratch);
+        corr = (d >= a.eps) ? s / (dd * dd) : 0.0f;
+    }
+    // Bound of |g * v * m| for the fixed-point scale.
+    float gmax = 0.0f, vmax = 0.0f, mmax = 1.0f;
+    for (int64_t u = oa + threadIdx.x; u < ob; u += kBThreads) {
+        float g = a.normalize ? (a.g_y[u] / dd - corr) : a.g_y[u];
+        gmax = fmaxf(gmax, fabsf(g));
+    }
+    int64_t F = 0;
+    for (int64_t e = ea + threadIdx.x; e < eb; e += kBThreads) {
+        vmax = fmaxf(vmax, fabsf(a.val[e]));
+        F += a.entry_count[e];
+    }
+    if (a.fact_m) {
+        float mm = 0.0f;
+        for (int64_t e = ea + warp; e < eb; e += kBThreads / 32) {
+            const int64_t s0 = a.slot_base[e], cnt = a.entry_count[e];
+            for (int64_t f = lane; f < cnt; f += 32) mm = fmaxf(mm, fabsf(a.fact_m[s0 + f]));
+        }
+        mmax = block_max(mm, fscratch);
+    }
+    gmax = block_max(gmax, fscratch);
+    vmax = block_max(vmax, fscratch);
+    F = block_sum(F, iscratch);
+    float bound = gmax * vmax * mmax * 1.0001f;
+    const int scale = fixed_scale_for(bound, F + 1);
+    __syncthreads();
+    const float *wrow = a.w + r * a.n;
+    for (int64_t e = ea + warp; e < eb; e += kBThreads / 32) {
+        const float v = a.val[e];
+        const int64_t s0 = a.slot_base[e], cnt = a.entry_count[e];
+        float gv = 0.0f;
+        for (int64_t f = lane; f < cnt; f += 32) {
+            const int64_t slot = s0 + f;
+            const int64_t u = oa + a.fact_pos[slot];
+            const float g = a.normalize ? (a.g_y[u] / dd - corr) : a.g_y[u];
+            const int c = a.fact_rel[slot];
+            const float m = a.fact_m ? a.fact_m[slot] : 1.0f;
+            gv += g * wrow[c] * m;
+            fixed_atomic_add(acc + 2 * c, to_fixed(g * v * m, scale));
+        }
+        gv = warp_sum(gv);
+        if (lane == 0) a.grad_val[e] = gv;
+    }
+    __syncthreads();
+    for (int64_t c = threadIdx.x; c < a.n; c += kBThreads)
+        a.grad_w[r * a.n + c] = fixed_to_float(acc[2 * c], acc[2 * c + 1], scale);
+}
+
+__global__ void scatter_grad_kernel(const float *grad_sel, const int64_t *src, int64_t n, float *grad_full) {
+    int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (i < n) grad_full[src[i]] = grad_sel[i];
+}
+
+// ---------------------------------------------------------------------------
+// Normalization alone (flashlog.cu:2508-2591): one CTA per row.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) normalize_forward_kernel(const int64_t *row_ptr, const float *x, int64_t rows,
+                                                                float eps, float *y, float *denom) {
+    __shared__ float part[256];
+    const int64_t r = blockIdx.x;
+    if (r >= rows) return;
+    const int64_t a0 = row_ptr[r], a1 = row_ptr[r + 1];
+    // 256 strided partials then a halving tree, as the reference kernel.
+    float s = 0.0f;
+    for (int64_t i = a0 + threadIdx.x; i < a1; i += 256) s += x[i];
+    part[threadIdx.x] = s;
+    __syncthreads();
+    for (int stride = 128; stride > 0; stride >>= 1) {
+        if (threadIdx.x < stride) part[threadIdx.x] += part[threadIdx.x + stride];
+        __syncthreads();
+    }
+    const float raw = part[0];
+    if (threadIdx.x == 0) denom[r] = raw;
+    const float d = raw >= eps ? raw : eps;
+    for (int64_t i = a0 + threadIdx.x; i < a1; i += 256) y[i] = x[i] / d;
+}
+
+__global__ void __launch_bounds__(256) normalize_backward_kernel(const int64_t *row_ptr, const float *x,
+                                                                 const float *denom, const float *g, int64_t rows,
+                                                                 float eps, float *gx) {
+    __shared__ float part[256];
+    const int64_t r = blockIdx.x;
+    if (r >= rows) return;
+    const int64_t a0 = row_ptr[r], a1 = row_ptr[r + 1];
+    float s = 0.0f;
+    for (int64_t i = a0 + threadIdx.x; i < a1; i += 256) s += g[i] * x[i];
+    part[threadIdx.x] = s;
+    __syncthreads();
+    for (int stride = 128; stride > 0; stride >>= 1) {
+        if (threadIdx.x < stride) part[threadIdx.x] += part[threadIdx.x + stride];
+        __syncthreads();
+    }
+    const float raw = denom[r];
+    const bool active = raw >= eps;
+    const float d = active ? raw : eps;
+    const float corr = active ? part[0] / (d * d) : 0.0f;
+    for (int64_t i = a0 + threadIdx.x; i < a1; i += 256) gx[i] = g[i] / d - corr;
+}
+
+}  // namespace
+
+// ===========================================================================
+// Host side
+// ===========================================================================
+static Side make_side(const fl_csr_side &s, const float *mask_csr) {
+    Side d;
+    d.row_ptr = s.row_ptr; d.col = s.col; d.order = s.order; d.gptr = s.group_ptr;
+    d.gstart = s.group_start; d.gcount = s.group_count; d.grel = s.group_rel; d.mask_csr = mask_csr;
+    return d;
+}
+
+size_t hop_workspace(int64_t rows, int64_t S) {
+    size_t s = carve_bytes<int64_t>(S + 1) + scan_workspace(S > rows ? S : rows) + carve_bytes<int64_t>(rows + 1) * 3 +
+               carve_bytes<float>(rows + 1);
+    return s + 4096;
+}
+
+size_t hop_output_tmp_bytes(int64_t total_slots) {
+    return carve_bytes<int32_t>(total_slots) + carve_bytes<float>(total_slots);
+}
+
+int hop_plan(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *ent, int64_t S, const fl_csr_side &ori,
+             const fl_csr_side &inv, int64_t *slot_base, int64_t *total_slots, void *ws, size_t ws_bytes,
+             cudaStream_t st) {
+    Carve c(ws, ws_bytes);
+    int64_t *cap = c.take<int64_t>(S + 1);
+    size_t sws = scan_workspace(S);
+    void *scan_ws = c.take<char>(sws);
+    FL_REQUIRE(cap && scan_ws, "hop workspace too small");
+    (void)row_ptr;
+    if (S > 0) {
+        launch(hop_capacity_kernel, static_cast<unsigned>((S + 255) / 256), 256, 0, st, 
+            ent, S, make_side(ori, nullptr), make_side(inv, nullptr), p->topk_edges, (p->flags & FL_WOT_I) ? 1 : 0, cap);
+    }
+    int rc = exclusive_scan<int64_t>(cap, S, slot_base, scan_ws, sws, st);
+    if (rc) return rc;
+    FL_CUDA(cudaMemcpyAsync(total_slots, slot_base + S, sizeof(int64_t), cudaMemcpyDeviceToHost, st));
+    FL_CUDA(cudaStreamSynchronize(st));
+    return check_launch("hop_plan");
+}
+
+int hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *ent, const float *val, int64_t S,
+               const float *w, const fl_csr_side &ori, const fl_csr_side &inv, const float *mask_csr_ori,
+               const float *mask_csr_inv, const uint8_t *mask_triple, const float *edge_weight,
+               const int64_t *slot_base, int32_t *fact_dst, float *fact_val, int16_t *fact_rel, float *fact_m,
+               int32_t *entry_count, cudaStream_t st) {
+    if (S == 0) return FL_OK;
+    ExpandArgs a;
+    a.row_ptr = row_ptr; a.ent = ent; a.val = val; a.S = S; a.rows = p->rows; a.n = p->n; a.r_size = p->r_size;
+    a.topk = p->topk_edges; a.flags = p->flags; a.seed = p->sampling_seed; a.L = p->L; a.w = w;
+    a.ori = make_side(ori, mask_csr_ori); a.inv = make_side(inv, mask_csr_inv);
+    a.mask_triple = mask_triple; a.edge_weight = edge_weight; a.slot_base = slot_base;
+    a.fact_dst = fact_dst; a.fact_val = fact_val; a.fact_rel = fact_rel; a.fact_m = fact_m; a.entry_count = entry_count;
+    int64_t blocks = (S + kExpandWarps - 1) / kExpandWarps;
+    int sms = fl_device_sm_count();
+    int64_t cap_blocks = static_cast<int64_t>(sms > 0 ? sms : 148) * 32;
+    if (blocks > cap_blocks) blocks = cap_blocks;
+    launch(hop_expand_kernel, static_cast<unsigned>(blocks), kExpandWarps * 32, 0, st, a);
+    return check_launch("hop_expand");
+}
+
+int row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *slot_base, const int32_t *entry_count,
+               const int32_t *fact_dst, const float *fact_val, int64_t total_slots, int32_t *fact_pos, float eps,
+               int64_t *out_row_ptr, int32_t *out_ent, float *out_x, float *out_y, float *out_denom,
+               void *ws, size_t ws_bytes, cudaStream_t st) {
+    FL_REQUIRE(total_slots < (int64_t(1) << 32), "too many facts in one hop (%lld)", static_cast<long long>(total_slots));
+    FL_REQUIRE(E < (int64_t(1) << 31), "entity count exceeds int32");
+    Carve c(ws, ws_bytes);
+    int64_t *out_count = c.take<int64_t>(rows + 1);
+    float *out_sum = c.take<float>(rows + 1);
+    size_t sws = scan_workspace(rows);
+    void *scan_ws = c.take<char>(sws);
+    int32_t *tmp_ent = c.take<int32_t>(total_slots > 0 ? total_slots : 1);
+    float *tmp_x = c.take<float>(total_slots > 0 ? total_slots : 1);
+    FL_REQUIRE(out_count && out_sum && scan_ws && tmp_ent && tmp_x, "row_reduce workspace too small");
+    if (rows > 0) {
+        ReduceArgs a;
+        a.row_ptr = row_ptr; a.rows = rows; a.slot_base = slot_base; a.entry_count = entry_count;
+        a.fact_dst = fact_dst; a.fact_val = fact_val; a.E = E; a.fact_pos = fact_pos;
+        a.tmp_ent = tmp_ent; a.tmp_x = tmp_x; a.out_count = out_count; a.out_sum = out_sum;
+        const size_t smem = sizeof(ReduceSmem);
+        static bool attr_set = false;
+        if (!attr_set) {
+            FL_CUDA(cudaFuncSetAttribute(row_reduce_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem)));
+            attr_set = true;
+        }
+        launch(row_reduce_kernel, static_cast<unsigned>(rows), kRThreads, smem, st, a);
+        int rc = check_launch("row_reduce");
+        if (rc) return rc;
+    }
+    int rc = exclusive_scan<int64_t>(out_count, rows, out_row_ptr, scan_ws, sws, st);
+    if (rc) return rc;
+    if (rows > 0)
+        launch(compact_kernel, static_cast<unsigned>(rows), 256, 0, st, row_ptr, slot_base, out_row_ptr, rows, tmp_ent, tmp_x,
+                                                                     out_sum, eps, out_ent, out_x, out_y, out_denom);
+    return check_launch("row_compact");
+}
+
+size_t row_reduce_workspace(int64_t rows, int64_t total_slots) {
+    return carve_bytes<int64_t>(rows + 1) + carve_bytes<float>(rows + 1) + scan_workspace(rows) +
+           hop_output_tmp_bytes(total_slots) + 4096;
+}
+
+size_t hop_backward_workspace(int64_t rows, int64_t n) {
+    return n > kSmemRel ? carve_bytes<unsigned long long>(static_cast<size_t>(rows) * n * 2) : 256;
+}
+
+int hop_backward(const fl_hop_params *p, const int64_t *row_ptr, const float *val, int64_t S, const float *w,
+                 const int64_t *slot_base, const int32_t *entry_count, const int32_t *fact_pos, const int16_t *fact_rel,
+                 const float *fact_m, const int64_t *out_row_ptr, const float *out_x, const float *out_denom,
+                 const float *g_y, float *grad_val, float *grad_w, void *ws, size_t ws_bytes, cudaStream_t st) {
+    (void)S;
+    BackwardArgs a;
+    a.row_ptr = row_ptr; a.val = val; a.w = w; a.rows = p->rows; a.n = p->n; a.eps = p->eps;
+    a.normalize = (p->flags & FL_NO_NORMALIZE) ? 0 : 1;
+    a.slot_base = slot_base; a.entry_count = entry_count; a.fact_pos = fact_pos; a.fact_rel = fact_rel;
+    a.fact_m = fact_m; a.out_row_ptr = out_row_ptr; a.out_x = out_x; a.out_denom = out_denom; a.g_y = g_y;
+    a.grad_val = grad_val; a.grad_w = grad_w; a.gacc = nullptr;
+    size_t smem = 0;
+    if (p->n > kSmemRel) {
+        Carve c(ws, ws_bytes);
+        a.gacc = c.take<unsigned long long>(static_cast<size_t>(p->rows) * p->n * 2);
+        FL_REQUIRE(a.gacc != nullptr, "hop backward workspace too small");
+    } else {
+        smem = static_cast<size_t>(p->n) * 2 * sizeof(unsigned long long);
+        static bool attr_set = false;
+        if (!attr_set) {
+            FL_CUDA(cudaFuncSetAttribute(hop_backward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kSmemRel * 2 * sizeof(unsigned long long))));
+            attr_set = true;
+        }
+    }
+    if (p->rows > 0)
+        launch(hop_backward_kernel, static_cast<unsigned>(p->rows), kBThreads, smem, st, a);
+    return check_launch("hop_backward");
+}
+
+int normalize_forward(const int64_t *row_ptr, const float *x, int64_t rows, float eps, float *y, float *denom,
+                      cudaStream_t st) {
+    if (rows > 0) launch(normalize_forward_kernel, static_cast<unsigned>(rows), 256, 0, st, row_ptr, x, rows, eps, y, denom);
+    return check_launch("normalize_forward");
+}
+
+int normalize_backward(const int64_t *row_ptr, const float *x, const float *denom, const float *g, int64_t rows,
+                       float eps, float *gx, cudaStream_t st) {
+    if (rows > 0)
+        launch(normalize_backward_kernel, static_cast<unsigned>(rows), 256, 0, st, row_ptr, x, denom, g, rows, eps, gx);
+    return check_launch("normalize_backward");
+}
+
+int scatter_grad(const float *grad_sel, const int64_t *src, int64_t n_sel, float *grad_full, int64_t n_full,
+                 cudaStream_t st) {
+    FL_CUDA(cudaMemsetAsync(grad_full, 0, static_cast<size_t>(n_full) * sizeof(float), st));
+    if (n_sel > 0)
+        launch(scatter_grad_kernel, static_cast<unsigned>((n_sel + 255) / 256), 256, 0, st, grad_sel, src, n_sel, grad_full);
+    return check_launch("scatter_grad");
+}
+
+}  // namespace fl

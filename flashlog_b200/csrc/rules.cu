@@ -1,0 +1,189 @@
+// rules.cu -- rule-bank evaluator kernels.
+//
+//   fixed-operator step   flashlog_kernel/source/flashlog.cu:1561-1741 (one
+//                         operator per (query, rule) row: forward relation,
+//                         inverse relation + R, or identity 2R; the value is
+//                         copied) followed by the coalesce-sum of
+//                         flashlog_kernel.py:206-210.  The facts go through
+//                         the same per-row stable-sort reduction as a hop.
+//   filtered ranks        flashlog.cu:2754-2910 (tie-averaged rank that also
+//                         counts the implicit zeros when the truth is 0).
+#include "common.cuh"
+#include "scan.cuh"
+
+namespace fl {
+namespace {
+
+struct SideR {
+    const int32_t *col, *gptr, *gstart, *gcount;
+    const int16_t *grel;
+};
+
+__device__ __forceinline__ int64_t find_group(const SideR &s, int64_t src, int rel) {
+    int64_t lo = s.gptr[src], hi = s.gptr[src + 1];
+    const int64_t end = hi;
+    while (lo < hi) {
+        int64_t mid = lo + (hi - lo) / 2;
+        if (static_cast<int>(s.grel[mid]) < rel) lo = mid + 1; else hi = mid;
+    }
+    return (lo < end && static_cast<int>(s.grel[lo]) == rel) ? lo : -1;
+}
+
+__global__ void fixed_count_kernel(const int64_t *b, const int64_t *l, const int32_t *ent, int64_t nnz,
+                                   const int64_t *ops, int64_t Lr, int64_t R, SideR ori, SideR inv, int64_t *cnt) {
+    int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (i >= nnz) return;
+    const int64_t op = ops[b[i] * Lr + l[i]];
+    if (op == 2 * R) { cnt[i] = 1; return; }
+    const bool inv_dir = op >= R;
+    const int rel = static_cast<int>(inv_dir ? op - R : op);
+    const SideR &s = inv_dir ? inv : ori;
+    const int64_t g = find_group(s, ent[i], rel);
+    cnt[i] = g < 0 ? 0 : s.gcount[g];
+}
+
+// One warp per entry: copy the group's destinations (coalesced int32 loads).
+__global__ void fixed_fill_kernel(const int64_t *b, const int64_t *l, const int32_t *ent, const float *val,
+                                  int64_t nnz, const int64_t *ops, int64_t Lr, int64_t R, SideR ori, SideR inv,
+                                  const int64_t *slot_base, int32_t *fact_dst, float *fact_val, int32_t *entry_count) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); i < nnz; i += nw) {
+        const int64_t op = ops[b[i] * Lr + l[i]];
+        const int64_t out = slot_base[i];
+        const float v = val[i];
+        if (op == 2 * R) {
+            if (lane == 0) { fact_dst[out] = ent[i]; fact_val[out] = v; entry_count[i] = 1; }
+            continue;
+        }
+        const bool inv_dir = op >= R;
+        const int rel = static_cast<int>(inv_dir ? op - R : op);
+        const SideR &s = inv_dir ? inv : ori;
+        const int64_t g = find_group(s, ent[i], rel);
+        const int64_t c = g < 0 ? 0 : s.gcount[g];
+        const int64_t p0 = g < 0 ? 0 : s.gstart[g];
+        for (int64_t k = lane; k < c; k += 32) {
+            fact_dst[out + k] = s.col[p0 + k];
+            fact_val[out + k] = v;
+        }
+        if (lane == 0) entry_count[i] = static_cast<int32_t>(c);
+    }
+}
+
+__device__ __forceinline__ bool bsearch64(const int64_t *keys, int64_t n, int64_t key) {
+    int64_t lo = 0, hi = n;
+    while (lo < hi) {
+        int64_t mid = lo + ((hi - lo) >> 1);
+        if (keys[mid] < key) lo = mid + 1; else hi = mid;
+    }
+    return lo < n && keys[lo] == key;
+}
+
+__global__ void ranks_truth_kernel(const int64_t *ib, const int64_t *ie, const float *v, int64_t nnz,
+                                   const int64_t *targets, float *truth) {
+    int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (i < nnz && ie[i] == targets[ib[i]]) truth[ib[i]] = v[i];
+}
+
+__global__ void ranks_filter_kernel(const int64_t *fk, int64_t nf, int64_t E, int32_t *fcount) {
+    int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (i < nf) atomicAdd(&fcount[fk[i] / E], 1);
+}
+
+__global__ void ranks_count_kernel(const int64_t *ib, const int64_t *ie, const float *v, int64_t nnz,
+                                   const float *truth, const int64_t *fk, int64_t nf, int64_t E, int32_t *greater,
+                                   int32_t *equal, int32_t *expl) {
+    int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (i >= nnz) return;
+    const int64_t b = ib[i];
+    if (bsearch64(fk, nf, b * E + ie[i])) return;
+    const float t = truth[b];
+    atomicAdd(&expl[b], 1);
+    if (v[i] > t) atomicAdd(&greater[b], 1);
+    else if (v[i] == t) atomicAdd(&equal[b], 1);
+}
+
+__global__ void ranks_finalize_kernel(const float *truth, const int32_t *greater, const int32_t *equal,
+                                      const int32_t *expl, const int32_t *fcount, int64_t B, int64_t E, int use_eql,
+                                      float *ranks) {
+    int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (b >= B) return;
+    if (use_eql) {
+        // fp32 count arithmetic of flashlog.cu:2829-2834 (counts exact below 2^24)
+        float missing = static_cast<float>(E) - static_cast<float>(fcount[b]) - static_cast<float>(expl[b]);
+        float eq = static_cast<float>(equal[b]) + (truth[b] == 0.0f ? missing : 0.0f);
+        eq += 1.0f;
+        ranks[b] = static_cast<float>(greater[b]) + (eq + 1.0f) * 0.5f;
+    } else {
+        ranks[b] = static_cast<float>(greater[b]) + 1.0f;
+    }
+}
+
+SideR make_side_r(const fl_csr_side &s) {
+    SideR r;
+    r.col = s.col; r.gptr = s.group_ptr; r.gstart = s.group_start; r.gcount = s.group_count; r.grel = s.group_rel;
+    return r;
+}
+
+}  // namespace
+
+size_t fixed_relation_workspace(int64_t nnz) { return carve_bytes<int64_t>(nnz + 1) + scan_workspace(nnz) + 1024; }
+
+int fixed_relation_plan(const int64_t *b, const int64_t *l, const int32_t *ent, int64_t nnz, const int64_t *ops,
+                        int64_t Lr, int64_t R, const fl_csr_side &ori, const fl_csr_side &inv, int64_t *slot_base,
+                        int64_t *total, void *ws, size_t ws_bytes, cudaStream_t st) {
+    Carve c(ws, ws_bytes);
+    int64_t *cnt = c.take<int64_t>(nnz + 1);
+    size_t sws = scan_workspace(nnz);
+    void *scan_ws = c.take<char>(sws);
+    FL_REQUIRE(cnt && scan_ws, "fixed_relation workspace too small");
+    if (nnz > 0)
+        launch(fixed_count_kernel, static_cast<unsigned>((nnz + 255) / 256), 256, 0, st, 
+            b, l, ent, nnz, ops, Lr, R, make_side_r(ori), make_side_r(inv), cnt);
+    int rc = exclusive_scan<int64_t>(cnt, nnz, slot_base, scan_ws, sws, st);
+    if (rc) return rc;
+    FL_CUDA(cudaMemcpyAsync(total, slot_base + nnz, sizeof(int64_t), cudaMemcpyDeviceToHost, st));
+    FL_CUDA(cudaStreamSynchronize(st));
+    return check_launch("fixed_relation_plan");
+}
+
+int fixed_relation_fill(const int64_t *b, const int64_t *l, const int32_t *ent, const float *val, int64_t nnz,
+                        const int64_t *ops, int64_t Lr, int64_t R, const fl_csr_side &ori, const fl_csr_side &inv,
+                        const int64_t *slot_base, int32_t *fact_dst, float *fact_val, int32_t *entry_count,
+                        cudaStream_t st) {
+    if (nnz == 0) return FL_OK;
+    int64_t blocks = (nnz + 7) / 8;
+    if (blocks > 148 * 32) blocks = 148 * 32;
+    launch(fixed_fill_kernel, static_cast<unsigned>(blocks), 256, 0, st, b, l, ent, val, nnz, ops, Lr, R, make_side_r(ori),
+                                                                    make_side_r(inv), slot_base, fact_dst, fact_val,
+                                                                    entry_count);
+    return check_launch("fixed_relation_fill");
+}
+
+size_t filtered_ranks_workspace(int64_t B) { return carve_bytes<float>(B) + 4 * carve_bytes<int32_t>(B) + 1024; }
+
+int filtered_ranks(const int64_t *ib, const int64_t *ie, const float *v, int64_t nnz, const int64_t *targets,
+                   const int64_t *fk, int64_t nf, int64_t B, int64_t E, int use_eql, float *ranks, void *ws,
+                   size_t ws_bytes, cudaStream_t st) {
+    Carve c(ws, ws_bytes);
+    float *truth = c.take<float>(B);
+    int32_t *greater = c.take<int32_t>(B), *equal = c.take<int32_t>(B), *expl = c.take<int32_t>(B),
+            *fcount = c.take<int32_t>(B);
+    FL_REQUIRE(truth && greater && equal && expl && fcount, "filtered_ranks workspace too small");
+    if (B == 0) return FL_OK;
+    FL_CUDA(cudaMemsetAsync(truth, 0, B * sizeof(float), st));
+    FL_CUDA(cudaMemsetAsync(greater, 0, B * sizeof(int32_t), st));
+    FL_CUDA(cudaMemsetAsync(equal, 0, B * sizeof(int32_t), st));
+    FL_CUDA(cudaMemsetAsync(expl, 0, B * sizeof(int32_t), st));
+    FL_CUDA(cudaMemsetAsync(fcount, 0, B * sizeof(int32_t), st));
+    if (nnz > 0) launch(ranks_truth_kernel, static_cast<unsigned>((nnz + 255) / 256), 256, 0, st, ib, ie, v, nnz, targets, truth);
+    if (nf > 0) launch(ranks_filter_kernel, static_cast<unsigned>((nf + 255) / 256), 256, 0, st, fk, nf, E, fcount);
+    if (nnz > 0)
+        launch(ranks_count_kernel, static_cast<unsigned>((nnz + 255) / 256), 256, 0, st, ib, ie, v, nnz, truth, fk, nf, E,
+                                                                                   greater, equal, expl);
+    launch(ranks_finalize_kernel, static_cast<unsigned>((B + 255) / 256), 256, 0, st, truth, greater, equal, expl, fcount, B,
+                                                                                E, use_eql, ranks);
+    return check_launch("filtered_ranks");
+}
+
+}  // namespace fl

@@ -1,0 +1,87 @@
+"""Multi-hop DRUM propagation that keeps the state in the row layout between hops.
+
+This is the hot path of one sparse DRUM training step
+(src/model_DRUM_kernel_sp.py:92-204 with the deterministic c1/c2 budgets):
+for t in range(T): w_t = softmax(w_all[:, t] / tau_1); state = normalize(hop(state, w_t));
+then the channel readout and log loss of src/utils.py:36-47.  Each hop is
+one autograd node whose forward and backward run in the library's kernels;
+the state never goes through the COO round trip of the operator API.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib as L
+from . import ops
+from .ops import Graph
+
+
+class HopNorm(torch.autograd.Function):
+    """c1 selection + expansion + coalesce-sum + normalization of one hop.
+
+    `stats` (optional) collects per-hop counts and gets a `timer` with
+    record_start / record_end around the hop's expansion and reduction.
+    """
+
+    @staticmethod
+    def forward(ctx, val, w, row_ptr, ent, graph, r_size, topk_edges, c1, flags, mask_triple, eps, stats):
+        v = val.detach().contiguous()
+        ctx.pruned = None
+        ctx.n_in = v.numel()
+        if c1 is not None and c1 >= 0 and v.numel() > c1:
+            rp, en, vv, src = ops.topc_select(row_ptr, ent, v, int(c1))
+            if src.numel() != v.numel():
+                row_ptr, ent, v, ctx.pruned = rp, en, vv, src
+        wf = w.detach().contiguous()
+        fw = ops.hop_forward(row_ptr, ent, v, wf, graph, r_size, topk_edges, flags, mask_triple=mask_triple, eps=eps,
+                             timing=None if stats is None else stats.timer)
+        if stats is not None:
+            stats.append((ent, fw.entry_count[:ent.numel()], fw.out_ent.numel()))
+        ctx.fw = fw
+        ctx.save_for_backward(row_ptr, v, wf)
+        ctx.mark_non_differentiable(fw.out_row_ptr, fw.out_ent)
+        return fw.out_y, fw.out_row_ptr, fw.out_ent
+
+    @staticmethod
+    def backward(ctx, g_y, _g_rp, _g_ent):
+        row_ptr, v, wf = ctx.saved_tensors
+        grad_v, grad_w = ops.hop_backward(ctx.fw, row_ptr, v, wf, g_y, normalize=True)
+        if ctx.pruned is not None:
+            grad_v = ops.scatter_grad(grad_v, ctx.pruned, ctx.n_in)
+        return grad_v, grad_w, None, None, None, None, None, None, None, None, None, None
+
+
+def initial_state(heads: torch.Tensor, N: int):
+    """One entry (h, value 1) per (query, channel) row."""
+    Q = heads.numel()
+    dev = heads.device
+    row_ptr = torch.arange(Q * N + 1, dtype=torch.int64, device=dev)
+    ent = heads.to(torch.int32).repeat_interleave(N)
+    val = torch.ones(Q * N, dtype=torch.float32, device=dev)
+    return row_ptr, ent, val
+
+
+def readout_loss(row_ptr, ent, val, tails, N: int, tau_2: float = 1.0, thr: float = 1e-7):
+    """log_loss_common_sp of the channel-summed scores (src/utils.py:36-47)."""
+    Q = tails.numel()
+    rows = row_ptr.numel() - 1
+    counts = row_ptr[1:] - row_ptr[:-1]
+    row_of = torch.repeat_interleave(torch.arange(rows, device=val.device), counts, output_size=ent.numel())
+    q = row_of // N
+    hit = ent.to(torch.int64) == tails[q]
+    score = torch.zeros(Q, dtype=val.dtype, device=val.device).index_add(0, q[hit], val[hit])
+    return -torch.mean(torch.log(torch.maximum(score / tau_2, torch.full_like(score, thr))))
+
+
+def drum_propagate(heads, w_all, graph: Graph, r_size: int, *, c1=None, c2=0, mask_triple=None, tau_1=1.0,
+                   eps=1e-7, stats=None):
+    """T hops of the sparse DRUM operator; w_all is [Q, T, N, n] logits."""
+    Q, T, N, n = w_all.shape
+    row_ptr, ent, val = initial_state(heads, N)
+    topk = c2 // 2 if c2 and c2 > 0 else L.NO_BUDGET
+    flags = L.FL_SKIP_NONPOS_W | L.FL_DROP_MASKED
+    for t in range(T):
+        w_t = torch.softmax(w_all[:, t] / tau_1, dim=-1)
+        val, row_ptr, ent = HopNorm.apply(val, w_t, row_ptr, ent, graph, r_size, topk, c1, flags, mask_triple, eps,
+                                          stats)
+    return row_ptr, ent, val

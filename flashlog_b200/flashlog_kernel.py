@@ -1,0 +1,578 @@
+"""Drop-in replacement of the reference operator module flashlog_kernel.flashlog_kernel.
+
+Same public names, argument orders, return types and error behaviour as the
+reference's flashlog_kernel/flashlog_kernel.py; the work runs in the sm_100a
+kernels of libflashlog_b200.so.  There is no CPU path: CPU tensors raise
+ValueError (the reference's OpenMP path is this build's timed CPU baseline,
+not a fallback).
+"""
+from __future__ import annotations
+
+import os
+import time
+
+import torch
+from torch import autograd
+
+from . import _lib as L
+from . import ops
+from .ops import Graph
+
+_FLASHLOG_CPU_THREADS_CONFIGURED = False
+
+
+# ---------------------------------------------------------------------------
+# Host configuration (flashlog_kernel.py:13-102)
+# ---------------------------------------------------------------------------
+def _flashlog_available_logical_cpus():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def configure_flashlog_cpu_threads(force=False):
+    """Apply FLASHLOG_CPU_THREADS / FLASHLOG_CPU_INTEROP_THREADS to torch's host threads.
+
+    Semantics of flashlog_kernel.py:60-102: unset/off/none/false/0 leaves torch
+    alone, "auto" picks a bandwidth-friendly count, an integer forces it.
+    """
+    global _FLASHLOG_CPU_THREADS_CONFIGURED
+    if _FLASHLOG_CPU_THREADS_CONFIGURED and not force:
+        return torch.get_num_threads()
+    setting = os.environ.get("FLASHLOG_CPU_THREADS", "off").strip().lower()
+    logical = max(1, _flashlog_available_logical_cpus())
+    if setting in ("off", "none", "false", "0"):
+        _FLASHLOG_CPU_THREADS_CONFIGURED = True
+        return torch.get_num_threads()
+    if setting in ("", "auto"):
+        target = logical if logical < 24 else min(16, max(8, logical // 2))
+    else:
+        try:
+            target = int(setting)
+        except ValueError:
+            target = logical
+    target = max(1, min(target, logical))
+    if torch.get_num_threads() != target:
+        torch.set_num_threads(target)
+    interop = os.environ.get("FLASHLOG_CPU_INTEROP_THREADS")
+    if interop is not None:
+        try:
+            n = max(1, int(interop))
+            if torch.get_num_interop_threads() != n:
+                torch.set_num_interop_threads(n)
+        except (ValueError, RuntimeError):
+            pass
+    _FLASHLOG_CPU_THREADS_CONFIGURED = True
+    return torch.get_num_threads()
+
+
+def _kernel_stage_timing_enabled():
+    return os.environ.get("FLASHLOG_STAGE_TIMING", "") == "1"
+
+
+def _kernel_log(stage, start_time):
+    """StageTiming lines of flashlog_kernel.py:158-165 (FLASHLOG_STAGE_TIMING=1)."""
+    if not _kernel_stage_timing_enabled():
+        return
+    if torch.cuda.is_available():
+        torch.cuda.synchronize()
+    print("StageTiming flashlog_kernel stage:{} seconds:{:.4f}".format(stage, time.perf_counter() - float(start_time)))
+
+
+def get_module():
+    """The native library (the reference JIT-builds a torch extension here)."""
+    return L.lib()
+
+
+def score_function(x):
+    return torch.sigmoid(x)
+
+
+def _cuda_or_raise(t, what="operator"):
+    if not t.is_cuda:
+        raise ValueError(f"flashlog_b200 {what} requires CUDA tensors (no CPU path)")
+
+
+# ---------------------------------------------------------------------------
+# CSR construction (flashlog_kernel.py:626-697)
+# ---------------------------------------------------------------------------
+def _group_starts_and_counts(sorted_values, sorted_relations=None):
+    """Group boundaries of sorted keys (flashlog_kernel.py:637-660); returns int32 (starts, counts)."""
+    n = sorted_values.numel()
+    if not n:
+        return torch.empty(0, dtype=torch.int32), torch.empty(0, dtype=torch.int32)
+    flags = torch.ones(n, dtype=torch.bool, device=sorted_values.device)
+    flags[1:] = sorted_values[1:] != sorted_values[:-1]
+    if sorted_relations is not None:
+        flags[1:] |= sorted_relations[1:] != sorted_relations[:-1]
+    starts = flags.nonzero().flatten().to(torch.int32)
+    counts = torch.empty_like(starts)
+    counts[:-1] = starts[1:] - starts[:-1]
+    counts[-1] = n - starts[-1]
+    return starts, counts
+
+
+def build_csr_structure(row_indices, col_indices, r_indices, num_nodes):
+    """16-tuple CSR of both directions, built on the GPU (replaces csr.cpp:12-69).
+
+    Output layout and ordering are those of the reference (edges by source,
+    relation, triple id); tensors are returned on the input's device.
+    """
+    device = row_indices.device
+    cdev = device if device.type == "cuda" else torch.device("cuda", torch.cuda.current_device())
+    row, col, rel = (x.detach().to(device=cdev, dtype=torch.int64).contiguous()
+                     for x in (row_indices, col_indices, r_indices))
+    relations = int(rel.max().item()) + 1 if rel.numel() else 0
+    if rel.numel() and (int(rel.min().item()) < 0 or relations - 1 > 32767):
+        raise ValueError("CSR entity or relation ID outside supported range")
+    nodes = int(num_nodes)
+    ori = ops.build_csr_side(row, col, rel, nodes, relations)
+    inv = ops.build_csr_side(col, row, rel, nodes, relations)
+    out = (*ori[:4], *inv[:4], *ori[4:], *inv[4:])
+    if device != cdev:
+        out = tuple(t.to(device) for t in out)
+    return out
+
+
+def _apply_mask_order(mask_values, order, weight=None):
+    mask_f = (mask_values if mask_values.dtype == torch.bool else mask_values.float()).contiguous().view(-1)
+    _cuda_or_raise(mask_f, "mask preparation")
+    m = mask_f[order.to(device=mask_f.device, dtype=torch.long)].float()
+    if weight is not None:
+        m = m * score_function(weight.to(device=mask_f.device, dtype=torch.float).squeeze(-1).view(-1)[order.long()])
+    return m.contiguous()
+
+
+def _prepared_mask_pair(mask_values):
+    if (isinstance(mask_values, (tuple, list)) and len(mask_values) == 2 and
+            torch.is_tensor(mask_values[0]) and torch.is_tensor(mask_values[1])):
+        return mask_values[0].contiguous().float(), mask_values[1].contiguous().float()
+    return None
+
+
+def prepare_csr_masks(csr_struct, mask_values, weight=None):
+    """CSR-ordered ORI/INV masks for one model forward (flashlog_kernel.py:250-255)."""
+    return (_apply_mask_order(mask_values, csr_struct[3], weight),
+            _apply_mask_order(mask_values, csr_struct[7], weight))
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+def _coo(row_ptr, ent, values, B, Lch, E):
+    idx = ops.rows_to_coo(row_ptr, ent, Lch)
+    return torch.sparse_coo_tensor(idx, values, [B, Lch, E], is_coalesced=True)
+
+
+def _align_sparse_grad_to_output(grad, out_indices, Lch, E):
+    """Gradient values at the forward's output coordinates (flashlog_kernel.py:360-376)."""
+    if not grad.is_sparse:
+        return grad[tuple(out_indices)].contiguous()
+    grad = grad.coalesce()
+    if grad.indices().shape == out_indices.shape and torch.equal(grad.indices(), out_indices):
+        return grad.values().contiguous()
+    keys = out_indices[0] * (Lch * E) + out_indices[1] * E + out_indices[2]
+    gidx = grad.indices()
+    gkeys = gidx[0] * (Lch * E) + gidx[1] * E + gidx[2]
+    values = torch.zeros(keys.numel(), device=grad.device, dtype=grad.dtype)
+    if gkeys.numel() and keys.numel():
+        pos = torch.searchsorted(gkeys, keys)
+        safe = pos.clamp(max=gkeys.numel() - 1)
+        valid = (pos < gkeys.numel()) & (gkeys[safe] == keys)
+        values[valid] = grad.values()[safe[valid]]
+    return values
+
+
+def _rows(sp_batch, sp_level, sp_entity, B, Lch, E, graph=None):
+    if graph is not None and graph.E < E:
+        raise ValueError(f"the CSR covers {graph.E} entities but the state has {E}")
+    row_ptr, ent, bad = ops.coo_to_rows(sp_batch, sp_level, sp_entity, B, Lch, E)
+    return row_ptr, ent, bad
+
+
+def _check_bad(bad):
+    if int(bad.item()):
+        raise ValueError("sparse state indices are out of range or not coalesced")
+
+
+def _select_sources(ctx, row_ptr, ent, val, topk_nodes, sampling):
+    """c1 selection; records the kept indices for the backward (flashlog_kernel.py:1140-1155)."""
+    ctx.pruned = None
+    ctx.original_input_size = val.numel()
+    if topk_nodes is None:
+        return row_ptr, ent, val
+    if topk_nodes < 0:
+        raise ValueError("topk_nodes/c must be nonnegative")
+    if val.numel() <= topk_nodes:
+        return row_ptr, ent, val
+    noise = None
+    if sampling:
+        ncand = ops.topc_candidates(row_ptr, val, int(topk_nodes))
+        if ncand:
+            nz = val[val != 0]
+            if not bool(torch.isfinite(nz).all()) or bool((nz <= 0).any()):
+                raise ValueError("Entity sampling requires finite nonnegative state scores")
+            # Exponential race noise from torch's generator, one draw per candidate in state order.
+            noise = torch.empty(ncand, device=val.device, dtype=torch.float64).exponential_()
+    sel_row_ptr, sel_ent, sel_val, src = ops.topc_select(row_ptr, ent, val, int(topk_nodes), noise)
+    if src.numel() == val.numel():
+        return row_ptr, ent, val
+    ctx.pruned = src
+    return sel_row_ptr, sel_ent, sel_val
+
+
+def _restore(ctx, grad):
+    if ctx.pruned is None:
+        return grad
+    return ops.scatter_grad(grad, ctx.pruned, ctx.original_input_size)
+
+
+def _graph_topk(csr_args):
+    (ori_row_ptr, ori_col_ind, ori_r_ind, ori_order, inv_row_ptr, inv_col_ind, inv_r_ind, inv_order,
+     ori_gp, ori_gr, ori_gs, ori_gc, inv_gp, inv_gr, inv_gs, inv_gc) = csr_args
+    return Graph.of((ori_row_ptr, ori_col_ind, ori_r_ind, ori_order, inv_row_ptr, inv_col_ind, inv_r_ind,
+                     inv_order, ori_gp, ori_gr, ori_gs, ori_gc, inv_gp, inv_gr, inv_gs, inv_gc))
+
+
+def _graph_groups(ori_col, ori_gp, ori_gr, ori_gs, ori_gc, inv_col, inv_gp, inv_gr, inv_gs, inv_gc):
+    """Graph view from group arrays only (the all-edges operator passes no row_ptr/order)."""
+    dev = ori_col.device
+    z = torch.empty(0, dtype=torch.int32, device=dev)
+    return Graph.of((ori_gp, ori_col, z.to(torch.int16), z, inv_gp, inv_col, z.to(torch.int16), z,
+                     ori_gp, ori_gr, ori_gs, ori_gc, inv_gp, inv_gr, inv_gs, inv_gc))
+
+
+def _topk_flags(weight, edge_weight_is_score, sampling, wot_i):
+    flags = L.FL_SKIP_NONPOS_W | L.FL_DROP_MASKED
+    if weight is not None:
+        flags |= L.FL_EDGE_WEIGHT
+        if edge_weight_is_score:
+            flags |= L.FL_EDGE_SCORE
+    if sampling:
+        flags |= L.FL_SAMPLED
+    if wot_i:
+        flags |= L.FL_WOT_I
+    return flags
+
+
+def _check_w(w):
+    if not bool(torch.isfinite(w).all()):
+        raise RuntimeError("FlashLog sparse top-k received non-finite attention weights; "
+                           "aborting before edge count/fill to prevent uninitialized indices")
+
+
+# ---------------------------------------------------------------------------
+# Sparse SUM operators
+# ---------------------------------------------------------------------------
+class FlashLogFunctionSparse3DTopKSum(autograd.Function):
+    """Sparse sum with c1/c2 budgets (flashlog_kernel.py:1158-1348), 33 positional arguments."""
+
+    @staticmethod
+    def forward(ctx, sp_batch, sp_level, sp_entity, sp_value, w,
+                ori_row_ptr, ori_col_ind, ori_r_ind, ori_order,
+                inv_row_ptr, inv_col_ind, inv_r_ind, inv_order,
+                ori_row_group_ptr, ori_group_rel, ori_group_edge_start, ori_group_edge_count,
+                inv_row_group_ptr, inv_group_rel, inv_group_edge_start, inv_group_edge_count,
+                mask_values, weight, B, L_, E, r_size, wot_i, topk_edges,
+                edge_weight_is_score=False, topk_nodes=None, cache_backward=True, sampling=False):
+        _cuda_or_raise(sp_value)
+        t0 = time.perf_counter()
+        graph = _graph_topk((ori_row_ptr, ori_col_ind, ori_r_ind, ori_order, inv_row_ptr, inv_col_ind, inv_r_ind,
+                             inv_order, ori_row_group_ptr, ori_group_rel, ori_group_edge_start,
+                             ori_group_edge_count, inv_row_group_ptr, inv_group_rel, inv_group_edge_start,
+                             inv_group_edge_count))
+        val = sp_value.detach().to(torch.float32).contiguous()
+        row_ptr, ent, bad = _rows(sp_batch, sp_level, sp_entity, B, L_, E, graph)
+        _check_bad(bad)
+        row_ptr, ent, val = _select_sources(ctx, row_ptr, ent, val, topk_nodes, sampling)
+        _kernel_log("sparse3d_topk_sum.select", t0)
+        t0 = time.perf_counter()
+        wf = w.detach().to(torch.float32).contiguous()
+        _check_w(wf)
+        seed = int(torch.randint(0, 2 ** 63 - 1, ()).item()) if sampling else -1
+        fw = ops.hop_forward(row_ptr, ent, val, wf, graph, r_size, int(topk_edges),
+                             _topk_flags(weight, edge_weight_is_score, sampling, wot_i),
+                             mask_triple=mask_values, edge_weight=None if weight is None else weight.detach(),
+                             seed=seed)
+        _kernel_log("sparse3d_topk_sum.cuda_forward", t0)
+        ctx.fw = fw
+        ctx.save_for_backward(row_ptr, val, wf)
+        ctx.B, ctx.L, ctx.E = B, L_, E
+        if weight is not None and bool(getattr(weight, "requires_grad", False)):
+            raise NotImplementedError("learnable edge weights (--use_soft) are not supported by flashlog_b200 yet")
+        out = _coo(fw.out_row_ptr, fw.out_ent, fw.out_x, B, L_, E)
+        ctx.out_indices = out.indices()
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        row_ptr, val, wf = ctx.saved_tensors
+        g = _align_sparse_grad_to_output(grad_out, ctx.out_indices, ctx.L, ctx.E).to(torch.float32)
+        grad_val, grad_w = ops.hop_backward(ctx.fw, row_ptr, val, wf, g, normalize=False)
+        grad_val = _restore(ctx, grad_val)
+        grads = (None, None, None, grad_val, grad_w) + (None,) * 28
+        return grads[:len(ctx.needs_input_grad)]
+
+
+class FlashLogFunctionSparse3DAllEdgesSum(autograd.Function):
+    """Sparse sum over every edge (flashlog_kernel.py:1351-1447), 22 positional arguments."""
+
+    @staticmethod
+    def forward(ctx, sp_batch, sp_level, sp_entity, sp_value, w,
+                ori_col_ind, ori_mask,
+                ori_row_group_ptr, ori_group_rel, ori_group_edge_start, ori_group_edge_count,
+                inv_col_ind, inv_mask,
+                inv_row_group_ptr, inv_group_rel, inv_group_edge_start, inv_group_edge_count,
+                B, L_, E, r_size, wot_i, cache_backward=True):
+        _cuda_or_raise(sp_value)
+        graph = _graph_groups(ori_col_ind, ori_row_group_ptr, ori_group_rel, ori_group_edge_start,
+                              ori_group_edge_count, inv_col_ind, inv_row_group_ptr, inv_group_rel,
+                              inv_group_edge_start, inv_group_edge_count)
+        val = sp_value.detach().to(torch.float32).contiguous()
+        row_ptr, ent, bad = _rows(sp_batch, sp_level, sp_entity, B, L_, E, graph)
+        _check_bad(bad)
+        ctx.pruned = None
+        wf = w.detach().to(torch.float32).contiguous()
+        flags = L.FL_WOT_I if wot_i else 0
+        fw = ops.hop_forward(row_ptr, ent, val, wf, graph, r_size, L.NO_BUDGET, flags,
+                             mask_csr=(ori_mask, inv_mask))
+        ctx.fw = fw
+        ctx.save_for_backward(row_ptr, val, wf)
+        ctx.B, ctx.L, ctx.E = B, L_, E
+        out = _coo(fw.out_row_ptr, fw.out_ent, fw.out_x, B, L_, E)
+        ctx.out_indices = out.indices()
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        row_ptr, val, wf = ctx.saved_tensors
+        g = _align_sparse_grad_to_output(grad_out, ctx.out_indices, ctx.L, ctx.E).to(torch.float32)
+        grad_val, grad_w = ops.hop_backward(ctx.fw, row_ptr, val, wf, g, normalize=False)
+        grads = (None, None, None, grad_val, grad_w) + (None,) * 18
+        return grads[:len(ctx.needs_input_grad)]
+
+
+class _Sparse3DSumNormFused(autograd.Function):
+    """c1 + expansion + coalesce-sum + row normalization as one node.
+
+    Equal to normalize_sparse3d(FlashLogFunctionSparse3DTopKSum(...)) of the
+    reference's CUDA path (flashlog_kernel.py:1908-1916); the normalization is
+    computed in the same kernel that reduces the rows.
+    """
+
+    @staticmethod
+    def forward(ctx, sp_value, w, sp_batch, sp_level, sp_entity, csr, mask_values, weight, B, L_, E, r_size, wot_i,
+                topk_edges, topk_nodes, sampling, all_edges, masks_csr, eps):
+        _cuda_or_raise(sp_value)
+        val = sp_value.detach().to(torch.float32).contiguous()
+        graph = Graph.of(csr)
+        row_ptr, ent, bad = _rows(sp_batch, sp_level, sp_entity, B, L_, E, graph)
+        _check_bad(bad)
+        wf = w.detach().to(torch.float32).contiguous()
+        if all_edges:
+            ctx.pruned = None
+            fw = ops.hop_forward(row_ptr, ent, val, wf, graph, r_size, L.NO_BUDGET, L.FL_WOT_I if wot_i else 0,
+                                 mask_csr=masks_csr, eps=eps)
+        else:
+            row_ptr, ent, val = _select_sources(ctx, row_ptr, ent, val, topk_nodes, sampling)
+            _check_w(wf)
+            seed = int(torch.randint(0, 2 ** 63 - 1, ()).item()) if sampling else -1
+            fw = ops.hop_forward(row_ptr, ent, val, wf, graph, r_size, int(topk_edges),
+                                 _topk_flags(weight, False, sampling, wot_i), mask_triple=mask_values,
+                                 edge_weight=None if weight is None else weight.detach(), seed=seed, eps=eps)
+        ctx.fw = fw
+        ctx.save_for_backward(row_ptr, val, wf)
+        ctx.B, ctx.L, ctx.E = B, L_, E
+        out = _coo(fw.out_row_ptr, fw.out_ent, fw.out_y, B, L_, E)
+        ctx.out_indices = out.indices()
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        row_ptr, val, wf = ctx.saved_tensors
+        g = _align_sparse_grad_to_output(grad_out, ctx.out_indices, ctx.L, ctx.E).to(torch.float32)
+        grad_val, grad_w = ops.hop_backward(ctx.fw, row_ptr, val, wf, g, normalize=True)
+        grad_val = _restore(ctx, grad_val)
+        return (grad_val, grad_w) + (None,) * 17
+
+
+class Sparse3DNormalizeFunction(autograd.Function):
+    """Row normalization of a coalesced sparse state (flashlog_kernel.py:536-607)."""
+
+    @staticmethod
+    def forward(ctx, sp_batch, sp_level, sp_entity, sp_value, B, L_, E, eps):
+        _cuda_or_raise(sp_value)
+        x = sp_value.detach().to(torch.float32).contiguous()
+        row_ptr, ent, bad = _rows(sp_batch, sp_level, sp_entity, B, L_, E)
+        _check_bad(bad)
+        y, denom = ops.normalize_forward(row_ptr, x, float(eps))
+        ctx.save_for_backward(row_ptr, x, denom)
+        ctx.eps = float(eps)
+        idx = torch.stack([sp_batch.long(), sp_level.long(), sp_entity.long()], dim=0)
+        ctx.idx = idx
+        ctx.L, ctx.E = L_, E
+        return torch.sparse_coo_tensor(idx, y, [B, L_, E], is_coalesced=True)
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        row_ptr, x, denom = ctx.saved_tensors
+        g = _align_sparse_grad_to_output(grad_out, ctx.idx, ctx.L, ctx.E).to(torch.float32)
+        gx = ops.normalize_backward(row_ptr, x, denom, g, ctx.eps)
+        return None, None, None, gx, None, None, None, None
+
+
+def normalize_sparse3d(s, eps=1e-7):
+    s = s if s.is_coalesced() else s.coalesce()
+    idx = s.indices()
+    B, L_, E = s.shape
+    return Sparse3DNormalizeFunction.apply(idx[0], idx[1], idx[2], s.values(), B, L_, E, eps)
+
+
+def _csr_parts(csr_struct):
+    return tuple(csr_struct)
+
+
+def vectorized_operation_sparse3d_csr_sum(sp_state, w, csr_struct, mask_values, r_size, weight=None, wot_i=False,
+                                          use_topk=False, topk_edges=0, prepared_masks=None, topk_nodes=None,
+                                          sampling=False):
+    """One hop, coalesced sum (flashlog_kernel.py:1814-1888, CUDA dispatch)."""
+    if sampling and use_topk:
+        return sampled_sparse_propagation(sp_state, w, csr_struct, mask_values, r_size, weight, wot_i, topk_nodes,
+                                          topk_edges, "sum")
+    sp_state = sp_state.coalesce()
+    _cuda_or_raise(sp_state)
+    idx = sp_state.indices()
+    val = sp_state.values()
+    B, L_, E = sp_state.shape
+    c = _csr_parts(csr_struct)
+    effective_topk = topk_edges if (use_topk and topk_edges > 0) else (1 << 60)
+    can_use_all_edges = not (use_topk and (topk_edges > 0 or topk_nodes is not None))
+    can_use_all_edges = can_use_all_edges and not (weight is not None and bool(getattr(weight, "requires_grad", False)))
+    if can_use_all_edges:
+        prepared = _prepared_mask_pair(prepared_masks) if prepared_masks is not None else _prepared_mask_pair(mask_values)
+        if prepared is not None:
+            ori_mask, inv_mask = prepared
+        else:
+            ori_mask, inv_mask = prepare_csr_masks(csr_struct, mask_values, weight)
+        return FlashLogFunctionSparse3DAllEdgesSum.apply(
+            idx[0], idx[1], idx[2], val, w, c[1], ori_mask, c[8], c[9], c[10], c[11], c[5], inv_mask,
+            c[12], c[13], c[14], c[15], B, L_, E, r_size, wot_i, torch.is_grad_enabled())
+    return FlashLogFunctionSparse3DTopKSum.apply(
+        idx[0], idx[1], idx[2], val, w, c[0], c[1], c[2], c[3], c[4], c[5], c[6], c[7],
+        c[8], c[9], c[10], c[11], c[12], c[13], c[14], c[15],
+        mask_values, weight, B, L_, E, r_size, wot_i, effective_topk,
+        False, topk_nodes if use_topk else None, torch.is_grad_enabled())
+
+
+def vectorized_operation_sparse3d_csr_sum_norm(sp_state, w, csr_struct, mask_values, r_size, weight=None,
+                                               wot_i=False, use_topk=False, topk_edges=0, prepared_masks=None,
+                                               eps=1e-7, topk_nodes=None, sampling=False):
+    """One hop followed by row normalization (flashlog_kernel.py:1901-1954), fused in one kernel pass."""
+    sp_state = sp_state.coalesce()
+    _cuda_or_raise(sp_state)
+    if weight is not None and bool(getattr(weight, "requires_grad", False)):
+        return normalize_sparse3d(vectorized_operation_sparse3d_csr_sum(
+            sp_state, w, csr_struct, mask_values, r_size, weight=weight, wot_i=wot_i, use_topk=use_topk,
+            topk_edges=topk_edges, prepared_masks=prepared_masks, topk_nodes=topk_nodes, sampling=sampling), eps=eps)
+    idx = sp_state.indices()
+    B, L_, E = sp_state.shape
+    sampled = bool(sampling and use_topk)
+    if sampled:
+        all_edges = False
+        eff = topk_edges if topk_edges > 0 else (1 << 60)
+        nodes = topk_nodes
+    else:
+        eff = topk_edges if (use_topk and topk_edges > 0) else (1 << 60)
+        all_edges = not (use_topk and (topk_edges > 0 or topk_nodes is not None))
+        nodes = topk_nodes if use_topk else None
+    masks_csr = None
+    if all_edges:
+        prepared = _prepared_mask_pair(prepared_masks) if prepared_masks is not None else _prepared_mask_pair(mask_values)
+        masks_csr = prepared if prepared is not None else prepare_csr_masks(csr_struct, mask_values, weight)
+    return _Sparse3DSumNormFused.apply(sp_state.values(), w, idx[0], idx[1], idx[2], _csr_parts(csr_struct),
+                                       mask_values, weight, B, L_, E, r_size, wot_i, eff, nodes, sampled,
+                                       all_edges, masks_csr, eps)
+
+
+def sampled_sparse_propagation(state, w, csr_struct, mask_values, r_size, weight=None, wot_i=False,
+                               topk_nodes=None, topk_edges=0, mode="sum"):
+    """Training-only c1/c2 sampling (flashlog_kernel.py:1957-1971)."""
+    state = state.coalesce()
+    _cuda_or_raise(state)
+    idx, val = state.indices(), state.values()
+    B, L_, E = state.shape
+    function = FlashLogFunctionSparse3DTopKMax if mode == "max" else FlashLogFunctionSparse3DTopKSum
+    return function.apply(idx[0], idx[1], idx[2], val, w, *csr_struct, mask_values, weight, B, L_, E, r_size, wot_i,
+                          topk_edges if topk_edges > 0 else (1 << 60), False, topk_nodes, torch.is_grad_enabled(),
+                          True)
+
+
+class FlashLogFunctionSparse3DTopKMax(autograd.Function):
+    """Sparse MAX propagation (flashlog_kernel.py:1450-1626)."""
+
+    @staticmethod
+    def forward(ctx, *args):
+        raise NotImplementedError("sparse MAX propagation (smDRUM/mmDRUM) is not implemented in flashlog_b200 yet")
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        raise NotImplementedError
+
+
+# ---------------------------------------------------------------------------
+# Rule evaluator (flashlog_kernel.py:168-210)
+# ---------------------------------------------------------------------------
+def sparse2d_filtered_ranks_cuda(idx_b, idx_e, values, targets, filter_keys, B, E, use_eql=False):
+    """Filtered tie-averaged ranks (flashlog.cu:2839-2910); filter_keys sorted ascending."""
+    return ops.filtered_ranks(idx_b, idx_e, values, targets, filter_keys, int(B), int(E), bool(use_eql))
+
+
+def vectorized_operation_sparse3d_fixed_relation(sp_state, operators, csr_struct, r_size):
+    """Advance rule states through one fixed operator per (query, rule) (flashlog_kernel.py:182-210)."""
+    if not sp_state.is_cuda:
+        raise ValueError("fixed-relation rule inference currently requires CUDA")
+    sp_state = sp_state.coalesce()
+    indices = sp_state.indices()
+    values = sp_state.values()
+    B, L_, E = sp_state.shape
+    if tuple(operators.shape) != (B, L_):
+        raise ValueError("operators must have shape [{}, {}], got {}".format(B, L_, tuple(operators.shape)))
+    c = tuple(csr_struct)
+    graph = _graph_groups(c[1], c[8], c[9], c[10], c[11], c[5], c[12], c[13], c[14], c[15])
+    row_ptr, ent, val = ops.fixed_relation(indices[0], indices[1], indices[2], values, operators, graph, int(r_size),
+                                           B, L_)
+    return _coo(row_ptr, ent, val.to(values.dtype), B, L_, E)
+
+
+# ---------------------------------------------------------------------------
+# Dense path (flashlog_kernel.py:700-1089)
+# ---------------------------------------------------------------------------
+def _compute_active_nodes(A):
+    """Sorted unique active node indices of A [batch, L, E] (flashlog_kernel.py:617-623)."""
+    non_zero = torch.nonzero(A.sum(1))
+    if non_zero.numel() == 0:
+        return torch.empty(0, dtype=torch.long, device=A.device)
+    return torch.unique(non_zero[:, 1])
+
+
+class FlashLogFunction(autograd.Function):
+    @staticmethod
+    def forward(ctx, *args):
+        raise NotImplementedError("the dense [B, L, E] propagation path is not implemented in flashlog_b200 yet")
+
+    @staticmethod
+    def backward(ctx, *grads):
+        raise NotImplementedError
+
+
+def vectorized_operation_csr(*args, **kwargs):
+    raise NotImplementedError("the dense [B, L, E] propagation path is not implemented in flashlog_b200 yet")
+
+
+def dense_csr_sum_cuda(*args, **kwargs):
+    raise NotImplementedError("the dense [B, L, E] propagation path is not implemented in flashlog_b200 yet")
+
+
+def dense_csr_max(*args, **kwargs):
+    raise NotImplementedError("the dense [B, L, E] propagation path is not implemented in flashlog_b200 yet")

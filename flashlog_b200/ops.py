@@ -1,0 +1,352 @@
+"""Tensor-level wrappers over the C ABI (one function per stage of the hot path).
+
+Every function takes CUDA tensors, allocates its outputs and workspace with
+torch on the tensors' device and runs the library's kernels on the current
+stream.  CPU tensors are rejected: there is no CPU path.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib as L
+from ._lib import check, lib
+
+EPS = 1e-7
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _ws(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("flashlog_b200 runs on CUDA tensors only (no CPU fallback)")
+
+
+_CSR_DTYPES = (torch.int32, torch.int32, torch.int16, torch.int32) * 2 + \
+              (torch.int32, torch.int16, torch.int32, torch.int32) * 2
+
+
+class Graph:
+    """Device CSR of both directions in the reference's 16-tuple layout.
+
+    csr[0:4]  ori row_ptr, col, edge_rel, order
+    csr[4:8]  inv row_ptr, col, edge_rel, order
+    csr[8:12] ori group_ptr, group_rel, group_start, group_count
+    csr[12:16] inv group_ptr, group_rel, group_start, group_count
+    """
+
+    _cache: dict = {}
+
+    def __init__(self, csr):
+        csr = tuple(csr)
+        if len(csr) != 16:
+            raise ValueError("csr_struct must be the 16-tuple of build_csr_structure")
+        _require_cuda(*[c for c in csr if c.numel()])
+        self.csr = tuple(c if c.dtype == d else c.to(d) for c, d in zip(csr, _CSR_DTYPES))
+        self.csr = tuple(c.contiguous() for c in self.csr)
+        self.E = self.csr[0].numel() - 1
+        c = self.csr
+        self.ori = L.fl_csr_side(_p(c[0]), _p(c[1]), _p(c[3]), _p(c[8]), _p(c[10]), _p(c[11]), _p(c[9]))
+        self.inv = L.fl_csr_side(_p(c[4]), _p(c[5]), _p(c[7]), _p(c[12]), _p(c[14]), _p(c[15]), _p(c[13]))
+        self.device = c[0].device
+
+    @classmethod
+    def of(cls, csr):
+        """Cached view of a csr tuple (keyed by its tensors' storage)."""
+        key = tuple((t.data_ptr(), t.numel(), t.dtype) for t in csr)
+        g = cls._cache.get(key)
+        if g is None:
+            if len(cls._cache) > 8:
+                cls._cache.clear()
+            g = cls(csr)
+            cls._cache[key] = g
+        return g
+
+
+# --------------------------------------------------------------------------
+# CSR build
+# --------------------------------------------------------------------------
+def build_csr_side(src, dst, rel, nodes: int, relations: int):
+    _require_cuda(src, dst, rel)
+    src, dst, rel = (x.to(torch.int64).contiguous() for x in (src, dst, rel))
+    m = src.numel()
+    dev = src.device
+    row_ptr = torch.empty(nodes + 1, dtype=torch.int32, device=dev)
+    col = torch.empty(m, dtype=torch.int32, device=dev)
+    erel = torch.empty(m, dtype=torch.int16, device=dev)
+    order = torch.empty(m, dtype=torch.int32, device=dev)
+    gptr = torch.empty(nodes + 1, dtype=torch.int32, device=dev)
+    grel = torch.empty(max(m, 1), dtype=torch.int16, device=dev)
+    gstart = torch.empty(max(m, 1), dtype=torch.int32, device=dev)
+    gcount = torch.empty(max(m, 1), dtype=torch.int32, device=dev)
+    ws = _ws(lib().fl_csr_build_workspace(m, nodes), dev)
+    ng = ctypes.c_int64(0)
+    check(lib().fl_csr_build_side(_p(src), _p(dst), _p(rel), m, nodes, relations, _p(row_ptr), _p(col), _p(erel),
+                                  _p(order), _p(gptr), _p(grel), _p(gstart), _p(gcount), ctypes.byref(ng), _p(ws),
+                                  ws.numel(), _stream()), "build_csr_side")
+    g = ng.value
+    return row_ptr, col, erel, order, gptr, grel[:g].clone(), gstart[:g].clone(), gcount[:g].clone()
+
+
+# --------------------------------------------------------------------------
+# layouts
+# --------------------------------------------------------------------------
+def coo_to_rows(b, l, e, B: int, Lch: int, E: int):
+    """Coalesced COO -> (row_ptr i64[B*L+1], ent i32); raises on invalid input."""
+    _require_cuda(b, l, e)
+    b, l, e = (x.to(torch.int64).contiguous() for x in (b, l, e))
+    rows = B * Lch
+    row_ptr = torch.empty(rows + 1, dtype=torch.int64, device=b.device)
+    ent = torch.empty(e.numel(), dtype=torch.int32, device=b.device)
+    bad = torch.zeros(1, dtype=torch.int32, device=b.device)
+    check(lib().fl_coo_to_rows(_p(b), _p(l), _p(e), e.numel(), Lch, rows, E, _p(row_ptr), _p(ent), _p(bad),
+                               _stream()), "coo_to_rows")
+    return row_ptr, ent, bad
+
+
+def rows_to_coo(row_ptr, ent, Lch: int):
+    U = ent.numel()
+    rows = row_ptr.numel() - 1
+    idx = torch.empty((3, U), dtype=torch.int64, device=ent.device)
+    check(lib().fl_rows_to_coo(_p(row_ptr), _p(ent), rows, Lch, U, _p(idx), _stream()), "rows_to_coo")
+    return idx
+
+
+# --------------------------------------------------------------------------
+# c1
+# --------------------------------------------------------------------------
+def topc_candidates(row_ptr, val, c1: int) -> int:
+    rows = row_ptr.numel() - 1
+    S = val.numel()
+    ws = _ws(lib().fl_topc_workspace(rows, S), val.device)
+    n = ctypes.c_int64(0)
+    check(lib().fl_topc_candidates(_p(row_ptr), _p(val), rows, S, c1, ctypes.byref(n), _p(ws), ws.numel(), _stream()),
+          "topc_candidates")
+    return n.value
+
+
+def topc_select(row_ptr, ent, val, c1: int, noise=None):
+    """c1 selection; returns (row_ptr, ent, val, src_index) of the kept entries."""
+    _require_cuda(row_ptr, ent, val)
+    rows = row_ptr.numel() - 1
+    S = val.numel()
+    dev = val.device
+    out_row_ptr = torch.empty(rows + 1, dtype=torch.int64, device=dev)
+    out_ent = torch.empty(S, dtype=torch.int32, device=dev)
+    out_val = torch.empty(S, dtype=torch.float32, device=dev)
+    out_src = torch.empty(S, dtype=torch.int64, device=dev)
+    ws = _ws(lib().fl_topc_workspace(rows, S), dev)
+    if noise is not None:
+        noise = noise.to(torch.float64).contiguous()
+    check(lib().fl_topc_select(_p(row_ptr), _p(ent), _p(val), rows, S, int(c1), _p(noise), _p(out_row_ptr),
+                               _p(out_ent), _p(out_val), _p(out_src), _p(ws), ws.numel(), _stream()), "topc_select")
+    k = int(out_row_ptr[-1].item())
+    return out_row_ptr, out_ent[:k], out_val[:k], out_src[:k]
+
+
+# --------------------------------------------------------------------------
+# one hop
+# --------------------------------------------------------------------------
+@dataclass
+class HopForward:
+    params: L.fl_hop_params
+    slot_base: torch.Tensor
+    entry_count: torch.Tensor
+    fact_rel: torch.Tensor
+    fact_m: torch.Tensor | None
+    fact_pos: torch.Tensor | None
+    out_row_ptr: torch.Tensor
+    out_ent: torch.Tensor
+    out_x: torch.Tensor
+    out_y: torch.Tensor
+    out_denom: torch.Tensor
+    n_facts_slots: int
+    fact_dst: torch.Tensor | None = None
+    fact_val: torch.Tensor | None = None
+
+
+def hop_params(rows, Lch, n, r_size, E, topk_edges, flags, seed=-1, eps=EPS):
+    return L.fl_hop_params(rows, Lch, n, r_size, E, int(min(topk_edges, L.NO_BUDGET)), int(flags), int(seed),
+                           float(eps))
+
+
+def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int, flags: int, *,
+                mask_triple=None, mask_csr=None, edge_weight=None, seed: int = -1, eps: float = EPS,
+                keep_facts: bool = False, record: bool = True, timing=None) -> HopForward:
+    """Expansion + per-row coalesce-sum + normalization of one hop."""
+    _require_cuda(row_ptr, ent, val, w)
+    B, Lch, n = w.shape
+    rows = B * Lch
+    S = ent.numel()
+    dev = val.device
+    if row_ptr.numel() != rows + 1:
+        raise ValueError(f"w has {rows} (item, channel) rows but the state has {row_ptr.numel() - 1}")
+    if n != 2 * r_size + 1:
+        raise ValueError(f"w must have 2 * r_size + 1 = {2 * r_size + 1} columns, got {n}")
+    w = w.contiguous()
+    params = hop_params(rows, Lch, n, r_size, graph.E, topk_edges, flags, seed, eps)
+    slot_base = torch.empty(S + 1, dtype=torch.int64, device=dev)
+    ws = _ws(lib().fl_hop_workspace(rows, S), dev)
+    total = ctypes.c_int64(0)
+    check(lib().fl_hop_plan(ctypes.byref(params), _p(row_ptr), _p(ent), S, graph.ori, graph.inv, _p(slot_base),
+                            ctypes.byref(total), _p(ws), ws.numel(), _stream()), "hop_plan")
+    T = max(total.value, 1)
+    fact_dst = torch.empty(T, dtype=torch.int32, device=dev)
+    fact_val = torch.empty(T, dtype=torch.float32, device=dev)
+    fact_rel = torch.empty(T, dtype=torch.int16, device=dev)
+    fact_m = torch.empty(T, dtype=torch.float32, device=dev) if (flags & L.FL_EDGE_WEIGHT) else None
+    entry_count = torch.empty(max(S, 1), dtype=torch.int32, device=dev)
+    mo = mi = None
+    M = graph.csr[1].numel()
+    if mask_csr is not None:
+        mo, mi = (m.reshape(-1).to(torch.float32).contiguous() for m in mask_csr)
+        if mo.numel() != M or mi.numel() != graph.csr[5].numel():
+            raise ValueError("CSR-ordered masks must have one value per edge")
+    if mask_triple is not None:
+        mask_triple = mask_triple.reshape(-1)
+        mask_triple = (mask_triple if mask_triple.dtype == torch.uint8 else (mask_triple != 0).to(torch.uint8)).contiguous()
+        if mask_triple.numel() < M:
+            raise ValueError("edge visibility mask must have one entry per triple")
+    if edge_weight is not None:
+        edge_weight = edge_weight.reshape(-1).to(torch.float32).contiguous()
+        if edge_weight.numel() < M:
+            raise ValueError("edge weights must have one entry per triple")
+    if timing is not None:
+        timing.record_start()
+    check(lib().fl_hop_expand(ctypes.byref(params), _p(row_ptr), _p(ent), _p(val), S, _p(w), graph.ori, graph.inv,
+                              _p(mo), _p(mi), _p(mask_triple), _p(edge_weight), _p(slot_base), _p(fact_dst),
+                              _p(fact_val), _p(fact_rel), _p(fact_m), _p(entry_count), _stream()), "hop_expand")
+    fact_pos = torch.empty(T, dtype=torch.int32, device=dev) if record else None
+    out_row_ptr = torch.empty(rows + 1, dtype=torch.int64, device=dev)
+    out_ent = torch.empty(T, dtype=torch.int32, device=dev)
+    out_x = torch.empty(T, dtype=torch.float32, device=dev)
+    out_y = torch.empty(T, dtype=torch.float32, device=dev)
+    out_denom = torch.empty(max(rows, 1), dtype=torch.float32, device=dev)
+    ws2 = _ws(lib().fl_reduce_workspace(rows, T), dev)
+    check(lib().fl_row_reduce(_p(row_ptr), rows, graph.E, _p(slot_base), _p(entry_count), _p(fact_dst), _p(fact_val),
+                              T, _p(fact_pos), ctypes.c_float(eps), _p(out_row_ptr), _p(out_ent), _p(out_x), _p(out_y),
+                              _p(out_denom), _p(ws2), ws2.numel(), _stream()), "row_reduce")
+    if timing is not None:
+        timing.record_end()
+    u = int(out_row_ptr[rows].item())
+    return HopForward(params, slot_base, entry_count, fact_rel, fact_m, fact_pos, out_row_ptr, out_ent[:u],
+                      out_x[:u], out_y[:u], out_denom[:rows], total.value,
+                      fact_dst if keep_facts else None, fact_val if keep_facts else None)
+
+
+def hop_backward(fw: HopForward, row_ptr, val, w, g_y, normalize: bool = True):
+    """Gradients of one hop w.r.t. the entry values and w."""
+    B, Lch, n = w.shape
+    rows = B * Lch
+    S = val.numel()
+    dev = val.device
+    params = L.fl_hop_params(fw.params.rows, fw.params.L, fw.params.n, fw.params.r_size, fw.params.E,
+                             fw.params.topk_edges, fw.params.flags | (0 if normalize else L.FL_NO_NORMALIZE),
+                             fw.params.sampling_seed, fw.params.eps)
+    grad_val = torch.empty(max(S, 1), dtype=torch.float32, device=dev)
+    grad_w = torch.empty((rows, n), dtype=torch.float32, device=dev)
+    ws = _ws(lib().fl_hop_backward_workspace(rows, n), dev)
+    g_y = g_y.to(torch.float32).contiguous()
+    check(lib().fl_hop_backward(ctypes.byref(params), _p(row_ptr), _p(val), S, _p(w.contiguous()), _p(fw.slot_base),
+                                _p(fw.entry_count), _p(fw.fact_pos), _p(fw.fact_rel), _p(fw.fact_m),
+                                _p(fw.out_row_ptr), _p(fw.out_x), _p(fw.out_denom), _p(g_y), _p(grad_val),
+                                _p(grad_w), _p(ws), ws.numel(), _stream()), "hop_backward")
+    return grad_val[:S], grad_w.view(B, Lch, n)
+
+
+def scatter_grad(grad_sel, src_index, n_full: int):
+    out = torch.empty(max(n_full, 1), dtype=torch.float32, device=grad_sel.device)
+    check(lib().fl_scatter_grad(_p(grad_sel.contiguous()), _p(src_index), src_index.numel(), _p(out), n_full,
+                                _stream()), "scatter_grad")
+    return out[:n_full]
+
+
+def normalize_forward(row_ptr, x, eps=EPS):
+    rows = row_ptr.numel() - 1
+    y = torch.empty_like(x)
+    denom = torch.empty(max(rows, 1), dtype=torch.float32, device=x.device)
+    check(lib().fl_normalize_forward(_p(row_ptr), _p(x.contiguous()), rows, ctypes.c_float(eps), _p(y), _p(denom),
+                                     _stream()), "normalize_forward")
+    return y, denom[:rows]
+
+
+def normalize_backward(row_ptr, x, denom, g, eps=EPS):
+    rows = row_ptr.numel() - 1
+    gx = torch.empty_like(x)
+    check(lib().fl_normalize_backward(_p(row_ptr), _p(x.contiguous()), _p(denom.contiguous()),
+                                      _p(g.to(torch.float32).contiguous()), rows, ctypes.c_float(eps), _p(gx),
+                                      _stream()), "normalize_backward")
+    return gx
+
+
+# --------------------------------------------------------------------------
+# rule evaluator
+# --------------------------------------------------------------------------
+def fixed_relation(b, l, e, v, ops_, graph: Graph, r_size: int, B: int, Lr: int):
+    """One fixed-operator rule step + coalesce-sum; returns (row_ptr, ent, val)."""
+    _require_cuda(b, l, e, v, ops_)
+    row_ptr, ent, bad = coo_to_rows(b, l, e, B, Lr, graph.E)
+    if int(bad.item()):
+        raise ValueError("sparse state indices are out of range or not coalesced")
+    b, l = b.to(torch.int64).contiguous(), l.to(torch.int64).contiguous()
+    v = v.to(torch.float32).contiguous()
+    ops_ = ops_.to(torch.int64).contiguous()
+    if tuple(ops_.shape) != (B, Lr):
+        raise ValueError(f"operators must have shape [{B}, {Lr}]")
+    nnz = v.numel()
+    dev = v.device
+    slot_base = torch.empty(nnz + 1, dtype=torch.int64, device=dev)
+    ws = _ws(lib().fl_fixed_relation_workspace(nnz), dev)
+    total = ctypes.c_int64(0)
+    check(lib().fl_fixed_relation_plan(_p(b), _p(l), _p(ent), nnz, _p(ops_), Lr, r_size, graph.ori, graph.inv,
+                                       _p(slot_base), ctypes.byref(total), _p(ws), ws.numel(), _stream()),
+          "fixed_relation_plan")
+    T = max(total.value, 1)
+    fact_dst = torch.empty(T, dtype=torch.int32, device=dev)
+    fact_val = torch.empty(T, dtype=torch.float32, device=dev)
+    entry_count = torch.empty(max(nnz, 1), dtype=torch.int32, device=dev)
+    check(lib().fl_fixed_relation_fill(_p(b), _p(l), _p(ent), _p(v), nnz, _p(ops_), Lr, r_size, graph.ori, graph.inv,
+                                       _p(slot_base), _p(fact_dst), _p(fact_val), _p(entry_count), _stream()),
+          "fixed_relation_fill")
+    rows = B * Lr
+    out_row_ptr = torch.empty(rows + 1, dtype=torch.int64, device=dev)
+    out_ent = torch.empty(T, dtype=torch.int32, device=dev)
+    out_x = torch.empty(T, dtype=torch.float32, device=dev)
+    out_denom = torch.empty(max(rows, 1), dtype=torch.float32, device=dev)
+    ws2 = _ws(lib().fl_reduce_workspace(rows, T), dev)
+    check(lib().fl_row_reduce(_p(row_ptr), rows, graph.E, _p(slot_base), _p(entry_count), _p(fact_dst), _p(fact_val),
+                              T, None, ctypes.c_float(EPS), _p(out_row_ptr), _p(out_ent), _p(out_x), None,
+                              _p(out_denom), _p(ws2), ws2.numel(), _stream()), "row_reduce")
+    u = int(out_row_ptr[rows].item())
+    return out_row_ptr, out_ent[:u], out_x[:u]
+
+
+def filtered_ranks(idx_b, idx_e, values, targets, filter_keys, B: int, E: int, use_eql: bool = False):
+    _require_cuda(idx_b, idx_e, values, targets, filter_keys)
+    idx_b, idx_e, targets, filter_keys = (x.to(torch.int64).contiguous() for x in (idx_b, idx_e, targets, filter_keys))
+    values = values.to(torch.float32).contiguous()
+    if idx_b.numel() and (int(idx_b.min()) < 0 or int(idx_b.max()) >= B or int(idx_e.min()) < 0 or int(idx_e.max()) >= E):
+        raise ValueError("score indices out of range")
+    if targets.numel() != B:
+        raise ValueError("targets must have one entity per query")
+    if filter_keys.numel() and (int(filter_keys.min()) < 0 or int(filter_keys.max()) >= B * E):
+        raise ValueError("filter keys out of range")
+    ranks = torch.empty(max(B, 1), dtype=torch.float32, device=values.device)
+    ws = _ws(lib().fl_filtered_ranks_workspace(B), values.device)
+    check(lib().fl_filtered_ranks(_p(idx_b), _p(idx_e), _p(values), values.numel(), _p(targets), _p(filter_keys),
+                                  filter_keys.numel(), B, E, int(bool(use_eql)), _p(ranks), _p(ws), ws.numel(),
+                                  _stream()), "filtered_ranks")
+    return ranks[:B]

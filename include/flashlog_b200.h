@@ -1,0 +1,191 @@
+/*
+ * flashlog_b200.h -- C ABI of the B200 (sm_100a) FlashLog propagation library
+ * (libflashlog_b200.so).
+ *
+ * Plain device pointers, sizes, a CUDA stream and an int status; no torch
+ * types.  Every call is ordered on the stream it is given and never allocates
+ * device memory: callers pass a workspace sized by the matching *_workspace
+ * query.  Calls documented as "syncs" copy a size to a host pointer and
+ * synchronize the stream.
+ *
+ * Status codes: FL_OK, FL_EINVAL (bad argument), FL_ECUDA (a CUDA call or
+ * launch failed).  fl_last_error() returns a thread-local message for the last
+ * failure.
+ *
+ * Layouts (the reference's formats, flashlog_kernel/flashlog_kernel.py:678-697
+ * and flashlog_kernel/source/csr.cpp:12-69):
+ *   CSR side  row_ptr i32[E+1], col i32[M], order i32[M] (CSR position ->
+ *             triple id), group_ptr i32[E+1], group_rel i16[G],
+ *             group_start i32[G], group_count i32[G]; edges sorted by
+ *             (source, relation, triple id).
+ *   state     a coalesced [B, L, E] COO held as rows r = b * L + l:
+ *             row_ptr i64[rows+1], ent i32[S] ascending per row, val f32[S].
+ *   weights   w f32[B, L, n], n = 2R + 1: columns [0, R) forward relations,
+ *             [R, 2R) inverse relations, n - 1 identity.
+ *   facts     per source entry i a slot range [slot_base[i], slot_base[i] +
+ *             entry_count[i]) holding (dst i32, value f32, relation column
+ *             i16 [, m f32]) in the reference's canonical order: forward
+ *             groups, inverse groups, identity.
+ */
+#ifndef FLASHLOG_B200_H
+#define FLASHLOG_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *fl_stream_t;
+
+enum { FL_OK = 0, FL_EINVAL = 1, FL_ECUDA = 2 };
+
+/* Expansion flags: which reference path a hop follows. */
+enum {
+    FL_SKIP_NONPOS_W = 1,  /* groups with w <= 0 take no edge (top-k fill, flashlog.cu:1511) */
+    FL_DROP_MASKED = 2,    /* hidden edges emit no fact (flashlog_kernel.py:1217-1228)      */
+    FL_WOT_I = 8,          /* no identity term                                             */
+    FL_SAMPLED = 16,       /* c2 by weighted quotas, SplitMix64 phase (flashlog.cu:1458-1528) */
+    FL_EDGE_SCORE = 32,    /* edge_weight holds scores, not logits                         */
+    FL_EDGE_WEIGHT = 64,   /* multiply facts by sigmoid(edge_weight[triple])               */
+    FL_NO_NORMALIZE = 1 << 20  /* backward: g_y is the gradient of the sums, not of the normalized rows */
+};
+
+typedef struct {
+    const int32_t *row_ptr, *col, *order, *group_ptr, *group_start, *group_count;
+    const int16_t *group_rel;
+} fl_csr_side;
+
+typedef struct {
+    int64_t rows, L, n, r_size, E; /* rows = B * L                              */
+    int64_t topk_edges;             /* c2 // 2 per direction; >= 2^62: no budget */
+    int64_t flags;                  /* FL_* flags                                */
+    int64_t sampling_seed;          /* FL_SAMPLED only                           */
+    float eps;                      /* row normalization epsilon                 */
+} fl_hop_params;
+
+const char *fl_last_error(void);
+int fl_version(void);
+int fl_device_sm_count(void);
+/* Number of kernels this library has launched in the process so far. */
+unsigned long long fl_launch_count(void);
+
+/* CSR build on the device.  Replaces build_side (csr.cpp:12-69).  src, dst,
+ * rel are i64[m]; ids outside [0, nodes) / [0, relations) are rejected before
+ * any write.  Group arrays need room for m entries; *n_groups (host) receives
+ * the number of groups (syncs). */
+size_t fl_csr_build_workspace(int64_t m, int64_t nodes);
+int fl_csr_build_side(const int64_t *src, const int64_t *dst, const int64_t *rel, int64_t m, int64_t nodes,
+                      int64_t relations, int32_t *row_ptr, int32_t *col, int16_t *edge_rel, int32_t *order,
+                      int32_t *group_ptr, int16_t *group_rel, int32_t *group_start, int32_t *group_count,
+                      int64_t *n_groups, void *ws, size_t ws_bytes, fl_stream_t stream);
+
+/* COO (b, l, e i64, coalesced order) -> row layout; *bad (device int, caller
+ * zeroed) is set when ids are out of range or unsorted.  Replaces the index
+ * handling of flashlog_kernel.py:1821-1824 / 1167-1178. */
+int fl_coo_to_rows(const int64_t *b, const int64_t *l, const int64_t *e, int64_t nnz, int64_t L, int64_t rows,
+                   int64_t E, int64_t *row_ptr, int32_t *ent, int *bad, fl_stream_t stream);
+/* Row layout -> COO indices i64[3, U] (b, l, e). */
+int fl_rows_to_coo(const int64_t *row_ptr, const int32_t *ent, int64_t rows, int64_t L, int64_t U, int64_t *indices,
+                   fl_stream_t stream);
+
+/* c1 entity budget.  Replaces _sparse_topc_entries (flashlog_kernel.py:1092-1137).
+ * Rows with at most c1 nonzeros are kept whole; larger rows keep their c1
+ * largest nonzero values, ties to the lower entity.  noise (f64, or NULL)
+ * selects the sampled mode: candidate k (nonzero entries of over-budget rows
+ * in state order) scores log(v) - log(noise[k]).  out_src[j] is the input
+ * index of kept entry j; outputs have capacity S. */
+size_t fl_topc_workspace(int64_t rows, int64_t S);
+int fl_topc_select(const int64_t *row_ptr, const int32_t *ent, const float *val, int64_t rows, int64_t S, int64_t c1,
+                   const double *noise, int64_t *out_row_ptr, int32_t *out_ent, float *out_val, int64_t *out_src,
+                   void *ws, size_t ws_bytes, fl_stream_t stream);
+/* Number of sampled-mode candidates (syncs). */
+int fl_topc_candidates(const int64_t *row_ptr, const float *val, int64_t rows, int64_t S, int64_t c1,
+                       int64_t *n_candidates, void *ws, size_t ws_bytes, fl_stream_t stream);
+
+/* Hop planning: per-entry fact capacity (degree capped by topk_edges per
+ * direction, + identity) and its scan into slot_base i64[S+1]; *total_slots
+ * (host) receives slot_base[S] (syncs).  Replaces the count kernels and the
+ * two .item() calls of flashlog.cu:2040-2062 / 2160-2182. */
+size_t fl_hop_workspace(int64_t rows, int64_t S);
+int fl_hop_plan(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *ent, int64_t S, fl_csr_side ori,
+                fl_csr_side inv, int64_t *slot_base, int64_t *total_slots, void *ws, size_t ws_bytes,
+                fl_stream_t stream);
+
+/* Hop expansion (one warp per source entry).  Replaces
+ * fill_sparse3d_topk_kernel / fill_sparse3d_all_edges_kernel /
+ * fill_sparse3d_identity_kernel (flashlog.cu:1402-1559, 1759-1854).  The edge
+ * visibility comes from mask_triple (u8 per triple, read through order, the
+ * top-k path) or mask_csr_ori / mask_csr_inv (f32 per CSR position, the
+ * all-edges path), or is 1 when all are NULL.  fact_m may be NULL unless
+ * FL_EDGE_WEIGHT is set. */
+int fl_hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *ent, const float *val, int64_t S,
+                  const float *w, fl_csr_side ori, fl_csr_side inv, const float *mask_csr_ori,
+                  const float *mask_csr_inv, const uint8_t *mask_triple, const float *edge_weight,
+                  const int64_t *slot_base, int32_t *fact_dst, float *fact_val, int16_t *fact_rel, float *fact_m,
+                  int32_t *entry_count, fl_stream_t stream);
+
+/* Per-row coalesce-sum (+ normalization) of expanded facts.  Replaces the
+ * coalesce of flashlog_kernel.py:258-357 (argsort + unique + scatter_add) and
+ * sparse3d_normalize_forward_cuda (flashlog.cu:2593-2649).  Sums follow the
+ * canonical fact order.  fact_pos (i32 per slot, may be NULL) receives each
+ * fact's output index within its row.  Outputs out_ent / out_x / out_y have
+ * capacity total_slots, out_row_ptr i64[rows+1] (its last entry is the
+ * output count), out_denom f32[rows] (raw row sums).  Stream-ordered; no
+ * host synchronization. */
+size_t fl_reduce_workspace(int64_t rows, int64_t total_slots);
+int fl_row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *slot_base, const int32_t *entry_count,
+                  const int32_t *fact_dst, const float *fact_val, int64_t total_slots, int32_t *fact_pos, float eps,
+                  int64_t *out_row_ptr, int32_t *out_ent, float *out_x, float *out_y, float *out_denom,
+                  void *ws, size_t ws_bytes, fl_stream_t stream);
+
+/* Hop backward (+ normalization backward unless FL_NO_NORMALIZE).  Replaces
+ * flashlog_backward_sparse3d_cached_cuda (flashlog.cu:2317-2361) and
+ * sparse3d_normalize_backward_cuda (flashlog.cu:2651-2691).  g_y f32[U]
+ * (gradient of out_y, or of out_x with FL_NO_NORMALIZE) -> grad_val f32[S]
+ * and grad_w f32[rows, n] (every column written). */
+size_t fl_hop_backward_workspace(int64_t rows, int64_t n);
+int fl_hop_backward(const fl_hop_params *p, const int64_t *row_ptr, const float *val, int64_t S, const float *w,
+                    const int64_t *slot_base, const int32_t *entry_count, const int32_t *fact_pos,
+                    const int16_t *fact_rel, const float *fact_m, const int64_t *out_row_ptr, const float *out_x,
+                    const float *out_denom, const float *g_y, float *grad_val, float *grad_w, void *ws,
+                    size_t ws_bytes, fl_stream_t stream);
+
+/* Row normalization alone.  Replaces sparse3d_normalize_{forward,backward}_cuda
+ * (flashlog.cu:2593-2691). */
+int fl_normalize_forward(const int64_t *row_ptr, const float *x, int64_t rows, float eps, float *y, float *denom,
+                         fl_stream_t stream);
+int fl_normalize_backward(const int64_t *row_ptr, const float *x, const float *denom, const float *g, int64_t rows,
+                          float eps, float *gx, fl_stream_t stream);
+
+/* grad_full[src_index[j]] = grad_sel[j], zeros elsewhere.  Replaces
+ * _restore_pruned_gradient (flashlog_kernel.py:1150-1155). */
+int fl_scatter_grad(const float *grad_sel, const int64_t *src_index, int64_t n_sel, float *grad_full, int64_t n_full,
+                    fl_stream_t stream);
+
+/* Rule step with one fixed operator per (query, rule) row: ops i64[B, Lr]
+ * holds a forward relation, inverse relation + R, or identity 2R.  Replaces
+ * flashlog_forward_sparse3d_fixed_relation_cuda (flashlog.cu:1677-1741); the
+ * facts are then reduced by fl_row_reduce.  plan: *total (host) receives the
+ * number of facts (syncs). */
+size_t fl_fixed_relation_workspace(int64_t nnz);
+int fl_fixed_relation_plan(const int64_t *b, const int64_t *l, const int32_t *ent, int64_t nnz, const int64_t *ops,
+                           int64_t Lr, int64_t r_size, fl_csr_side ori, fl_csr_side inv, int64_t *slot_base,
+                           int64_t *total, void *ws, size_t ws_bytes, fl_stream_t stream);
+int fl_fixed_relation_fill(const int64_t *b, const int64_t *l, const int32_t *ent, const float *val, int64_t nnz,
+                           const int64_t *ops, int64_t Lr, int64_t r_size, fl_csr_side ori, fl_csr_side inv,
+                           const int64_t *slot_base, int32_t *fact_dst, float *fact_val, int32_t *entry_count,
+                           fl_stream_t stream);
+
+/* Filtered tie-averaged ranks; filter_keys (b * E + e) sorted ascending.
+ * Replaces sparse2d_filtered_ranks_cuda (flashlog.cu:2839-2910). */
+size_t fl_filtered_ranks_workspace(int64_t B);
+int fl_filtered_ranks(const int64_t *idx_b, const int64_t *idx_e, const float *values, int64_t nnz,
+                      const int64_t *targets, const int64_t *filter_keys, int64_t n_filter, int64_t B, int64_t E,
+                      int use_eql, float *ranks, void *ws, size_t ws_bytes, fl_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FLASHLOG_B200_H */

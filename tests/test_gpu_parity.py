@@ -1,0 +1,370 @@
+"""Parity of the CUDA path (through the C ABI) with the oracle and the golden vectors.
+
+Integer and index results (CSR, c1/c2 selections, output coordinates, ranks)
+are compared bit for bit.  Expansion sums follow the reference CPU order and
+are compared bit for bit as well; normalized values and gradients use the
+north-star tolerance rel 1e-5.
+"""
+import numpy as np
+import pytest
+
+from helpers import O, config1_graph, oracle_hop_norm, oracle_hop_norm_backward
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-5
+
+
+@pytest.fixture(scope="module")
+def fk():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    import flashlog_b200.flashlog_kernel as fk
+    from flashlog_b200 import _lib
+    _lib.lib()
+    return fk
+
+
+@pytest.fixture(scope="module")
+def g1(fk):
+    cfg, train, csr_np = config1_graph()
+    t = torch.from_numpy(train).cuda()
+    csr = fk.build_csr_structure(t[:, 0], t[:, 2], t[:, 1], cfg.entities)
+    return cfg, train, csr_np, csr
+
+
+def _cuda(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    return t if dtype is None else t.to(dtype)
+
+
+def _state(rng, B, L, E, per_row, zero_frac=0.05, ties=False, neg=False):
+    rows, ents = [], []
+    for r in range(B * L):
+        k = int(rng.integers(1, per_row + 1))
+        rows.append(np.full(k, r))
+        ents.append(np.sort(rng.choice(E, k, replace=False)))
+    row = np.concatenate(rows).astype(np.int64)
+    ent = np.concatenate(ents).astype(np.int64)
+    val = ((rng.integers(0, 5, row.size) / 4.0) if ties else rng.random(row.size)).astype(np.float32)
+    if neg:
+        val = np.where(rng.random(row.size) < 0.3, -val, val).astype(np.float32)
+    val[rng.random(row.size) < zero_frac] = 0
+    return row, ent, val
+
+
+def _w(rng, B, L, n, ties):
+    if ties:
+        return (rng.integers(0, 4, size=(B, L, n)) / 4.0).astype(np.float32)
+    x = rng.standard_normal((B, L, n)).astype(np.float32)
+    e = np.exp(x - x.max(-1, keepdims=True))
+    return (e / e.sum(-1, keepdims=True)).astype(np.float32)
+
+
+def _sp(row, ent, val, B, L, E, requires_grad=False):
+    idx = _cuda(np.stack([row // L, row % L, ent]))
+    v = _cuda(val).requires_grad_(requires_grad)
+    return torch.sparse_coo_tensor(idx, v, (B, L, E), is_coalesced=True), v
+
+
+def _keys(sp, L, E):
+    i = sp.indices().cpu().numpy()
+    return (i[0] * L + i[1]) * E + i[2]
+
+
+# ---------------------------------------------------------------------------
+def test_csr_build_matches_oracle(fk, g1):
+    cfg, train, csr_np, csr = g1
+    for i, (a, b) in enumerate(zip(csr, csr_np)):
+        assert a.dtype == torch.from_numpy(b).dtype, i
+        assert np.array_equal(a.cpu().numpy(), b), i
+
+
+def test_csr_build_tiny_golden(fk, golden):
+    d = golden("csr_tiny.npz")
+    tri = _cuda(d["triples"])
+    csr = fk.build_csr_structure(tri[:, 0], tri[:, 2], tri[:, 1], int(d["E"]))
+    for i, c in enumerate(csr):
+        assert np.array_equal(c.cpu().numpy(), d[f"f{i}"]), i
+
+
+def test_csr_build_rejects_bad_ids(fk):
+    with pytest.raises(ValueError):
+        fk.build_csr_structure(_cuda(np.array([0, 7])), _cuda(np.array([1, 2])), _cuda(np.array([0, 0])), 4)
+
+
+def test_topc_matches_oracle(fk):
+    from flashlog_b200 import ops
+    rng = np.random.default_rng(3)
+    for c1, ties, neg in [(5, False, False), (5, True, False), (3, True, True), (0, False, False), (1, True, False),
+                          (20, False, False)]:
+        row, ent, val = _state(rng, 6, 3, 800, 40, ties=ties, neg=neg)
+        rp, en, bad = ops.coo_to_rows(_cuda(row // 3), _cuda(row % 3), _cuda(ent), 6, 3, 800)
+        assert int(bad.item()) == 0
+        _, _, sel_val, src = ops.topc_select(rp, en, _cuda(val), c1)
+        ref = O.topc(row, val, c1)
+        ref = np.arange(row.size) if ref is None else ref
+        assert np.array_equal(src.cpu().numpy(), ref), (c1, ties, neg)
+        assert np.array_equal(sel_val.cpu().numpy(), val[ref])
+
+
+def test_topc_golden(fk, golden):
+    from flashlog_b200 import ops
+    d = golden("topc.npz")
+    for ci in range(int(d["n"])):
+        row, ent, val, c1 = d[f"c{ci}_row"], d[f"c{ci}_ent"], d[f"c{ci}_val"], int(d[f"c{ci}_c1"])
+        rp, en, _ = ops.coo_to_rows(_cuda(row // 3), _cuda(row % 3), _cuda(ent), 4, 3, 500)
+        _, _, _, src = ops.topc_select(rp, en, _cuda(val), c1)
+        ref = d[f"c{ci}_kept"]
+        ref = np.arange(row.size) if (ref.size == 1 and ref[0] == -1) else ref
+        assert np.array_equal(src.cpu().numpy(), ref), ci
+
+
+def test_topc_sampled_scores(fk):
+    """Sampled c1 keeps the c1 largest log(v) - log(noise) per row (flashlog_kernel.py:1125-1136)."""
+    from flashlog_b200 import ops
+    rng = np.random.default_rng(4)
+    row, ent, val = _state(rng, 4, 3, 600, 50, zero_frac=0.1)
+    rp, en, _ = ops.coo_to_rows(_cuda(row // 3), _cuda(row % 3), _cuda(ent), 4, 3, 600)
+    c1 = 7
+    ncand = ops.topc_candidates(rp, _cuda(val), c1)
+    noise = rng.exponential(size=ncand)
+    _, _, _, src = ops.topc_select(rp, en, _cuda(val), c1, noise=_cuda(noise))
+    # numpy restatement of the exponential race
+    keep = []
+    k = 0
+    for r in range(12):
+        idx = np.flatnonzero(row == r)
+        nz = idx[val[idx] != 0]
+        if nz.size <= c1:
+            keep.extend(idx.tolist())
+            continue
+        sc = np.log(val[nz].astype(np.float64)) - np.log(noise[k:k + nz.size])
+        k += nz.size
+        order = np.argsort(-sc, kind="stable")[:c1]
+        keep.extend(sorted(nz[order].tolist()))
+    assert np.array_equal(src.cpu().numpy(), np.array(sorted(keep)))
+
+
+@pytest.mark.parametrize("topk,ties,wot_i", [(3, True, False), (7, False, False), (200, False, False),
+                                             (1 << 60, True, False), (4, True, True)])
+def test_hop_topk_forward_backward(fk, g1, topk, ties, wot_i):
+    cfg, train, csr_np, csr = g1
+    E, R = cfg.entities, cfg.relations
+    n = 2 * R + 1
+    rng = np.random.default_rng(topk % 97 + (5 if ties else 0) + (11 if wot_i else 0))
+    B, L = 5, 3
+    row, ent, val = _state(rng, B, L, E, 40)
+    w = _w(rng, B, L, n, ties)
+    mask = rng.random(train.shape[0]) > 0.15
+    sp, v = _sp(row, ent, val, B, L, E, requires_grad=True)
+    wt = _cuda(w).requires_grad_(True)
+    out = fk.vectorized_operation_sparse3d_csr_sum(sp, wt, csr, _cuda(mask), R, wot_i=wot_i, use_topk=True,
+                                                   topk_edges=topk)
+    fw = O.hop_forward(row, ent, val, w, csr_np, R, E, topk_edges=topk, mode=O.MODE_TOPK, mask=mask, wot_i=wot_i)
+    assert np.array_equal(_keys(out, L, E), fw["out_key"])
+    assert np.array_equal(out.values().detach().cpu().numpy(), fw["out_val"])
+    g = rng.standard_normal(fw["out_key"].size).astype(np.float32)
+    (out.values() * _cuda(g)).sum().backward()
+    gv, gw = O.hop_backward(fw, g, row, val, w, R)
+    np.testing.assert_allclose(v.grad.cpu().numpy(), gv, rtol=RTOL, atol=1e-6)
+    np.testing.assert_allclose(wt.grad.cpu().numpy(), gw, rtol=RTOL, atol=1e-6)
+
+
+def test_hop_all_edges_forward_backward(fk, g1):
+    cfg, train, csr_np, csr = g1
+    E, R = cfg.entities, cfg.relations
+    n = 2 * R + 1
+    rng = np.random.default_rng(8)
+    B, L = 4, 3
+    row, ent, val = _state(rng, B, L, E, 30)
+    w = _w(rng, B, L, n, False)
+    w[0, 0, :3] = 0.0  # zero-weight groups still emit (zero-valued) facts on this path
+    mask = (rng.random(train.shape[0]) > 0.2).astype(np.float32)
+    sp, v = _sp(row, ent, val, B, L, E, requires_grad=True)
+    wt = _cuda(w).requires_grad_(True)
+    out = fk.vectorized_operation_sparse3d_csr_sum(sp, wt, csr, _cuda(mask), R, use_topk=False)
+    fw = O.hop_forward(row, ent, val, w, csr_np, R, E, mode=O.MODE_ALL_EDGES, mask=mask)
+    assert np.array_equal(_keys(out, L, E), fw["out_key"])
+    assert np.array_equal(out.values().detach().cpu().numpy(), fw["out_val"])
+    g = rng.standard_normal(fw["out_key"].size).astype(np.float32)
+    (out.values() * _cuda(g)).sum().backward()
+    gv, gw = O.hop_backward(fw, g, row, val, w, R)
+    np.testing.assert_allclose(v.grad.cpu().numpy(), gv, rtol=RTOL, atol=1e-6)
+    np.testing.assert_allclose(wt.grad.cpu().numpy(), gw, rtol=RTOL, atol=1e-6)
+
+
+@pytest.mark.parametrize("name", ["topk3_ties", "topk200", "notopk", "topk5_c1", "wot_i"])
+def test_sum_norm_matches_reference_golden(fk, g1, golden, name):
+    """The fused sum+normalize operator against the reference CPU operator's own outputs."""
+    d = golden("hop_config1.npz")
+    cfg, train, csr_np, csr = g1
+    E, R = cfg.entities, cfg.relations
+    row, ent, val, w = d[f"{name}_row"], d[f"{name}_ent"], d[f"{name}_val"], d[f"{name}_w"]
+    B, L = w.shape[0], w.shape[1]
+    c1 = int(d[f"{name}_c1"])
+    sp, v = _sp(row, ent, val, B, L, E, requires_grad=True)
+    wt = _cuda(w).requires_grad_(True)
+    y = fk.vectorized_operation_sparse3d_csr_sum_norm(
+        sp, wt, csr, _cuda(d[f"{name}_mask"].astype(bool)), R, wot_i=bool(d[f"{name}_wot_i"]),
+        use_topk=bool(d[f"{name}_use_topk"]), topk_edges=int(d[f"{name}_topk"]), topk_nodes=None if c1 < 0 else c1)
+    assert np.array_equal(_keys(y, L, E), d[f"{name}_out_key"])
+    np.testing.assert_allclose(y.values().detach().cpu().numpy(), d[f"{name}_out_y"], rtol=RTOL, atol=0)
+    (y.values() * _cuda(d[f"{name}_g"])).sum().backward()
+    np.testing.assert_allclose(v.grad.cpu().numpy(), d[f"{name}_grad_v"], rtol=RTOL, atol=1e-6)
+    np.testing.assert_allclose(wt.grad.cpu().numpy(), d[f"{name}_grad_w"], rtol=RTOL, atol=1e-6)
+
+
+def test_drum3_engine_matches_reference_golden(fk, g1, golden):
+    from flashlog_b200 import engine
+    from flashlog_b200.ops import Graph
+    d = golden("drum3_config1.npz")
+    cfg, train, csr_np, csr = g1
+    E, R = cfg.entities, cfg.relations
+    logits = _cuda(d["logits"]).requires_grad_(True)
+    heads, tails = _cuda(d["heads"]), _cuda(d["tails"])
+    N = logits.shape[2]
+    rp, ent, val = engine.drum_propagate(heads, logits, Graph.of(csr), R, c1=int(d["c1"]), c2=int(d["c2"]),
+                                         mask_triple=_cuda(d["mask"]))
+    loss = engine.readout_loss(rp, ent, val, tails, N)
+    np.testing.assert_allclose(loss.item(), float(d["loss"]), rtol=RTOL)
+    loss.backward()
+    np.testing.assert_allclose(logits.grad.cpu().numpy(), d["grad_logits"], rtol=1e-4, atol=1e-6)
+    # channel readout of the final state
+    counts = (rp[1:] - rp[:-1]).cpu().numpy()
+    row = np.repeat(np.arange(counts.size), counts)
+    keys = (row // N) * E + ent.cpu().numpy()
+    fk_, fv_ = O.coalesce_sum(keys, val.detach().cpu().numpy())
+    assert np.array_equal(fk_, d["final_key"])
+    np.testing.assert_allclose(fv_, d["final_val"], rtol=RTOL, atol=1e-9)
+
+
+def test_large_rows_histogram_and_dense_paths(fk):
+    """Rows above one shared-memory tile, a hub destination (dense window) and a wide entity range."""
+    from flashlog_b200 import ops
+    from flashlog_b200.ops import Graph
+    rng = np.random.default_rng(12)
+    for E in (60_000, 5_000_000):
+        R = 6
+        m_rand = 120_000
+        h = rng.integers(0, 30_000, m_rand)
+        t = rng.integers(0, E, m_rand)
+        r = rng.integers(0, R, m_rand)
+        hub = E - 17
+        hs = np.repeat(np.arange(2500), R)
+        hr = np.tile(np.arange(R), 2500)
+        tri = np.unique(np.concatenate([np.stack([h, r, t], 1), np.stack([hs, hr, np.full(hs.size, hub)], 1)]), axis=0)
+        csr_np = O.build_csr(tri[:, 0], tri[:, 2], tri[:, 1], E)
+        tt = _cuda(tri)
+        csr = fk.build_csr_structure(tt[:, 0], tt[:, 2], tt[:, 1], E)
+        B, L = 2, 1
+        ent = np.concatenate([np.arange(0, 2500), np.sort(rng.choice(np.arange(2500, 30_000), 1500, replace=False))])
+        row = np.zeros(ent.size, np.int64)
+        ent2 = np.sort(rng.choice(30_000, 300, replace=False))
+        row = np.concatenate([row, np.ones(ent2.size, np.int64)])
+        ent = np.concatenate([ent, ent2]).astype(np.int64)
+        val = rng.random(ent.size).astype(np.float32)
+        w = _w(rng, B, L, 2 * R + 1, False)
+        mask = np.ones(tri.shape[0], np.uint8)
+        rp, en, _ = ops.coo_to_rows(_cuda(row), _cuda(row * 0), _cuda(ent), B, L, E)
+        fw = ops.hop_forward(rp, en, _cuda(val), _cuda(w), Graph.of(csr), R, 1 << 62,
+                             1 | 2, mask_triple=_cuda(mask))
+        ref = O.hop_forward(row, ent, val, w, csr_np, R, E, mode=O.MODE_TOPK, mask=mask)
+        counts = (fw.out_row_ptr[1:] - fw.out_row_ptr[:-1]).cpu().numpy()
+        keys = np.repeat(np.arange(B * L), counts) * E + fw.out_ent.cpu().numpy()
+        assert ref["n_facts"] > 8192 * 2
+        assert np.array_equal(keys, ref["out_key"]), E
+        assert np.array_equal(fw.out_x.cpu().numpy(), ref["out_val"]), E
+        # backward through the dense window as well
+        g = rng.standard_normal(keys.size).astype(np.float32)
+        gv, gw = ops.hop_backward(fw, rp, _cuda(val), _cuda(w), _cuda(g), normalize=False)
+        rgv, rgw = O.hop_backward(ref, g, row, val, w, R)
+        np.testing.assert_allclose(gv.cpu().numpy(), rgv, rtol=RTOL, atol=1e-5)
+        np.testing.assert_allclose(gw.cpu().numpy(), rgw, rtol=RTOL, atol=1e-5)
+
+
+def test_sampled_c2_matches_oracle(fk, g1):
+    from flashlog_b200 import ops, _lib as Lb
+    from flashlog_b200.ops import Graph
+    cfg, train, csr_np, csr = g1
+    E, R = cfg.entities, cfg.relations
+    rng = np.random.default_rng(21)
+    B, L = 4, 3
+    row, ent, val = _state(rng, B, L, E, 30, zero_frac=0.0)
+    w = _w(rng, B, L, 2 * R + 1, False)
+    mask = (rng.random(train.shape[0]) > 0.1).astype(np.uint8)
+    seed = 987654321123
+    rp, en, _ = ops.coo_to_rows(_cuda(row // L), _cuda(row % L), _cuda(ent), B, L, E)
+    for topk in (2, 5, 40):
+        fw = ops.hop_forward(rp, en, _cuda(val), _cuda(w), Graph.of(csr), R, topk,
+                             Lb.FL_SKIP_NONPOS_W | Lb.FL_DROP_MASKED | Lb.FL_SAMPLED, mask_triple=_cuda(mask), seed=seed)
+        ref = O.hop_forward(row, ent, val, w, csr_np, R, E, topk_edges=topk, mode=O.MODE_TOPK, mask=mask,
+                            sampling_seed=seed)
+        counts = (fw.out_row_ptr[1:] - fw.out_row_ptr[:-1]).cpu().numpy()
+        keys = np.repeat(np.arange(B * L), counts) * E + fw.out_ent.cpu().numpy()
+        assert np.array_equal(keys, ref["out_key"]), topk
+        assert np.array_equal(fw.out_x.cpu().numpy(), ref["out_val"]), topk
+
+
+def test_normalize_matches_reference_golden(fk, golden):
+    d = golden("normalize.npz")
+    row, ent, val = d["row"], d["ent"], d["val"]
+    sp, v = _sp(row, ent, val, 5, 3, 400, requires_grad=True)
+    y = fk.normalize_sparse3d(sp)
+    np.testing.assert_allclose(y.values().detach().cpu().numpy(), d["y"], rtol=RTOL, atol=0)
+    (y.values() * _cuda(d["g"])).sum().backward()
+    np.testing.assert_allclose(v.grad.cpu().numpy(), d["grad"], rtol=RTOL, atol=1e-6)
+
+
+def test_fixed_relation_matches_oracle(fk, g1):
+    cfg, train, csr_np, csr = g1
+    E, R = cfg.entities, cfg.relations
+    rng = np.random.default_rng(31)
+    Bq, Lr = 5, 7
+    row, ent, val = _state(rng, Bq, Lr, E, 20, zero_frac=0.0)
+    val = np.round(val * 4).astype(np.float32)
+    ops_ = rng.integers(0, 2 * R + 1, size=(Bq, Lr))
+    ops_[0, 0] = 2 * R
+    sp, _ = _sp(row, ent, val, Bq, Lr, E)
+    out = fk.vectorized_operation_sparse3d_fixed_relation(sp, _cuda(ops_), csr, R)
+    rk, rv = O.fixed_relation(row // Lr, row % Lr, ent, val, ops_, csr_np, R, E)
+    assert np.array_equal(_keys(out, Lr, E), rk)
+    assert np.array_equal(out.values().cpu().numpy(), rv)
+
+
+def test_filtered_ranks_match_oracle_and_golden(fk, golden):
+    d = golden("ranks.npz")
+    for ci in range(int(d["n"])):
+        keys, B, E = d[f"r{ci}_keys"], int(d[f"r{ci}_B"]), int(d[f"r{ci}_E"])
+        targets = d[f"r{ci}_targets"]
+        filt = np.unique(np.concatenate([d[f"r{ci}_fb"] * E + d[f"r{ci}_fe"], np.arange(B) * E + targets]))
+        eql = bool(d[f"r{ci}_eql"])
+        ranks = fk.sparse2d_filtered_ranks_cuda(_cuda(keys // E), _cuda(keys % E), _cuda(d[f"r{ci}_vals"]),
+                                                _cuda(targets), _cuda(filt), B, E, eql).cpu().numpy()
+        ref = O.filtered_ranks(keys // E, keys % E, d[f"r{ci}_vals"], targets, filt, B, E, eql)
+        assert np.array_equal(ranks, ref)
+        hits = np.zeros(10)
+        for r in ranks:
+            hits += (float(r) <= np.arange(1, 11))
+        np.testing.assert_array_equal(hits, d[f"r{ci}_hits"])
+
+
+def test_hop_is_deterministic(fk, g1):
+    cfg, train, csr_np, csr = g1
+    E, R = cfg.entities, cfg.relations
+    rng = np.random.default_rng(41)
+    row, ent, val = _state(rng, 6, 3, E, 200)
+    w = _w(rng, 6, 3, 2 * R + 1, False)
+    outs = []
+    for _ in range(2):
+        sp, v = _sp(row, ent, val, 6, 3, E, requires_grad=True)
+        wt = _cuda(w).requires_grad_(True)
+        y = fk.vectorized_operation_sparse3d_csr_sum_norm(sp, wt, csr, torch.ones(train.shape[0], dtype=torch.bool,
+                                                                                  device="cuda"),
+                                                          R, use_topk=True, topk_edges=6, topk_nodes=50)
+        (y.values() * torch.arange(y.values().numel(), device="cuda").float().sin()).sum().backward()
+        outs.append((y.indices().cpu().numpy(), y.values().detach().cpu().numpy(), v.grad.cpu().numpy(),
+                     wt.grad.cpu().numpy()))
+    for a, b in zip(outs[0], outs[1]):
+        assert a.tobytes() == b.tobytes()

@@ -1,0 +1,107 @@
+"""Host-side checks that need no GPU: the C ABI library and the drop-in's host logic."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+import torch
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    text = open(os.path.join(REPO, "include", "flashlog_b200.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(fl_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_builds_and_exports_every_declared_symbol():
+    from flashlog_b200 import _lib
+    _lib.build()
+    handle = ctypes.CDLL(_lib.LIB_PATH)
+    syms = declared_symbols()
+    assert len(syms) >= 20
+    for s in syms:
+        assert hasattr(handle, s), s
+    # every declared symbol has a ctypes signature in the binding
+    assert set(syms) <= set(_lib.SIGNATURES), set(syms) - set(_lib.SIGNATURES)
+    assert _lib.lib().fl_version() == 1
+
+
+def test_library_is_built_for_sm100a():
+    from flashlog_b200 import _lib
+    assert "arch=compute_100a,code=sm_100a" in " ".join(_lib.NVCC_FLAGS)
+    assert "-fmad=false" in _lib.NVCC_FLAGS  # products are rounded separately, as in the reference
+
+
+def test_error_message_roundtrip():
+    from flashlog_b200 import _lib
+    lib = _lib.lib()
+    rc = lib.fl_coo_to_rows(None, None, None, 0, 0, 0, 0, None, None, None, None)
+    assert rc == 1
+    assert b"invalid" in lib.fl_last_error()
+    with pytest.raises(ValueError):
+        _lib.check(rc, "coo_to_rows")
+
+
+def test_cpu_tensors_are_rejected():
+    import flashlog_b200.flashlog_kernel as fk
+    idx = torch.tensor([[0], [0], [1]])
+    sp = torch.sparse_coo_tensor(idx, torch.ones(1), (1, 1, 4)).coalesce()
+    w = torch.softmax(torch.randn(1, 1, 3), -1)
+    csr = tuple(torch.zeros(2, dtype=torch.int32) for _ in range(16))
+    with pytest.raises(ValueError):
+        fk.vectorized_operation_sparse3d_csr_sum(sp, w, csr, torch.ones(1, dtype=torch.bool), 1, use_topk=True,
+                                                 topk_edges=2)
+    with pytest.raises(ValueError):
+        fk.vectorized_operation_sparse3d_csr_sum_norm(sp, w, csr, torch.ones(1, dtype=torch.bool), 1)
+    with pytest.raises(ValueError):
+        fk.vectorized_operation_sparse3d_fixed_relation(sp, torch.zeros(1, 1, dtype=torch.long), csr, 1)
+
+
+def test_exports_match_reference_names():
+    import flashlog_b200
+    for name in ("FlashLogFunction", "_compute_active_nodes", "build_csr_structure", "prepare_csr_masks",
+                 "vectorized_operation_csr", "vectorized_operation_sparse3d_csr_sum",
+                 "vectorized_operation_sparse3d_csr_sum_norm", "vectorized_operation_sparse3d_fixed_relation",
+                 "FlashLogFunctionSparse3DTopKSum", "FlashLogFunctionSparse3DAllEdgesSum",
+                 "FlashLogFunctionSparse3DTopKMax", "sampled_sparse_propagation", "normalize_sparse3d",
+                 "configure_flashlog_cpu_threads", "_group_starts_and_counts", "sparse2d_filtered_ranks_cuda"):
+        assert hasattr(flashlog_b200, name), name
+
+
+def test_configure_cpu_threads_env(monkeypatch):
+    import flashlog_b200.flashlog_kernel as fk
+    before = torch.get_num_threads()
+    try:
+        monkeypatch.setenv("FLASHLOG_CPU_THREADS", "off")
+        assert fk.configure_flashlog_cpu_threads(force=True) == before
+        monkeypatch.setenv("FLASHLOG_CPU_THREADS", "2")
+        assert fk.configure_flashlog_cpu_threads(force=True) == min(2, os.cpu_count())
+    finally:
+        torch.set_num_threads(before)
+
+
+def test_group_starts_and_counts():
+    import flashlog_b200.flashlog_kernel as fk
+    v = torch.tensor([0, 0, 1, 1, 1, 3])
+    r = torch.tensor([2, 2, 0, 1, 1, 0])
+    s, c = fk._group_starts_and_counts(v, r)
+    assert s.tolist() == [0, 2, 3, 5] and c.tolist() == [2, 1, 2, 1]
+    s, c = fk._group_starts_and_counts(v)
+    assert s.tolist() == [0, 2, 5] and c.tolist() == [2, 3, 1]
+
+
+def test_synthetic_graph_is_seeded_and_shaped():
+    from flashlog_b200.synthetic import CONFIGS, generate_triples, training_queries
+    cfg = CONFIGS[1]
+    a = generate_triples(cfg)
+    b = generate_triples(cfg)
+    assert all(np.array_equal(x, y) for x, y in zip(a, b))
+    train, valid, test = a
+    assert train.shape == (22_400, 3) and valid.shape[0] == 2_800 and test.shape[0] == 2_800
+    assert np.unique(np.concatenate([train, valid, test]), axis=0).shape[0] == 28_000
+    ids, h, r, t = training_queries(train, cfg)
+    assert h.size == 2 * cfg.batch_size
+    assert np.array_equal(r[1::2], r[0::2] + cfg.relations)
