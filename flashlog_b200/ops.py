@@ -207,7 +207,12 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
     fact_dst = torch.empty(T, dtype=torch.int32, device=dev)
     fact_val = torch.empty(T, dtype=torch.float32, device=dev)
     fact_rel = torch.empty(T, dtype=torch.int16, device=dev)
-    fact_m = torch.empty(T, dtype=torch.float32, device=dev) if (flags & L.FL_EDGE_WEIGHT) else None
+    # The mask value of each fact is needed by the backward whenever it can be
+    # anything but 1: soft edge weights, CSR-ordered float masks, or hidden
+    # edges kept as zero-valued facts.
+    need_m = bool(flags & L.FL_EDGE_WEIGHT) or mask_csr is not None or (
+        mask_triple is not None and not (flags & L.FL_DROP_MASKED))
+    fact_m = torch.empty(T, dtype=torch.float32, device=dev) if need_m else None
     entry_count = torch.empty(max(S, 1), dtype=torch.int32, device=dev)
     mo = mi = None
     M = graph.csr[1].numel()
