@@ -99,6 +99,7 @@ SIGNATURES = {
     "fl_filtered_ranks_workspace": (_SZ, [_I64]),
     "fl_filtered_ranks": (ctypes.c_int, [_P, _P, _P, _I64, _P, _P, _I64, _I64, _I64, ctypes.c_int, _P, _P, _SZ,
                                          _P]),
+    "fl_filtered_ranks_noalloc": (ctypes.c_int, [_P, _P, _P, _I64, _P, _P, _I64, _I64, _I64, ctypes.c_int, _P, _P]),
 }
 
 _lib = None

@@ -52,6 +52,9 @@ size_t filtered_ranks_workspace(int64_t B);
 int filtered_ranks(const int64_t *ib, const int64_t *ie, const float *v, int64_t nnz, const int64_t *targets,
                    const int64_t *fk, int64_t nf, int64_t B, int64_t E, int use_eql, float *ranks, void *ws,
                    size_t ws_bytes, cudaStream_t st);
+int filtered_ranks_noalloc(const int64_t *ib, const int64_t *ie, const float *v, int64_t nnz, const int64_t *targets,
+                           const int64_t *fk, int64_t nf, int64_t B, int64_t E, int use_eql, float *ranks,
+                           cudaStream_t st);
 
 namespace {
 
@@ -239,6 +242,13 @@ int fl_filtered_ranks(const int64_t *idx_b, const int64_t *idx_e, const float *v
                       int use_eql, float *ranks, void *ws, size_t ws_bytes, fl_stream_t stream) {
     return filtered_ranks(idx_b, idx_e, values, nnz, targets, filter_keys, n_filter, B, E, use_eql, ranks, ws, ws_bytes,
                           as_stream(stream));
+}
+
+int fl_filtered_ranks_noalloc(const int64_t *idx_b, const int64_t *idx_e, const float *values, int64_t nnz,
+                              const int64_t *targets, const int64_t *filter_keys, int64_t n_filter, int64_t B,
+                              int64_t E, int use_eql, float *ranks, fl_stream_t stream) {
+    return filtered_ranks_noalloc(idx_b, idx_e, values, nnz, targets, filter_keys, n_filter, B, E, use_eql, ranks,
+                                  as_stream(stream));
 }
 
 }  // extern "C"

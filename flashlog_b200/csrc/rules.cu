@@ -8,6 +8,8 @@
 //                         the same per-row stable-sort reduction as a hop.
 //   filtered ranks        flashlog.cu:2754-2910 (tie-averaged rank that also
 //                         counts the implicit zeros when the truth is 0).
+#include <mutex>
+
 #include "common.cuh"
 #include "scan.cuh"
 
@@ -184,6 +186,52 @@ int filtered_ranks(const int64_t *ib, const int64_t *ie, const float *v, int64_t
     launch(ranks_finalize_kernel, static_cast<unsigned>((B + 255) / 256), 256, 0, st, truth, greater, equal, expl, fcount, B,
                                                                                 E, use_eql, ranks);
     return check_launch("filtered_ranks");
+}
+
+// ---------------------------------------------------------------------------
+// Filtered ranks without any allocation.
+//
+// Some callers cannot allocate device memory at the moment they need ranks:
+// a plain C host program that has no device allocator of its own, or code
+// that must not call cudaMalloc because it synchronizes the whole device
+// (for example a latency-sensitive evaluation loop running beside training
+// on other streams).  This variant takes its per-query counters from a fixed
+// array in the library's device memory instead of a caller workspace.
+// ---------------------------------------------------------------------------
+constexpr int64_t kNoAllocMaxQueries = 65536;  // 5 arrays x 64 Ki x 4 B = 1.25 MiB per device
+static __device__ __align__(256) unsigned char g_rank_scratch[5 * kNoAllocMaxQueries * 4 + 5 * 256];
+
+constexpr int kMaxDevices = 64;
+static void *g_rank_scratch_addr[kMaxDevices];
+static std::mutex g_rank_scratch_mutex;
+
+static int rank_scratch_address(void **out) {
+    int dev = 0;
+    FL_CUDA(cudaGetDevice(&dev));
+    FL_REQUIRE(dev >= 0 && dev < kMaxDevices, "device index %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_rank_scratch_mutex);
+    if (g_rank_scratch_addr[dev] == nullptr) {
+        // The symbol's host-side name is not a device address; look the
+        // address up once per device, with that device current.
+        void *p = nullptr;
+        FL_CUDA(cudaGetSymbolAddress(&p, g_rank_scratch));
+        g_rank_scratch_addr[dev] = p;
+    }
+    *out = g_rank_scratch_addr[dev];
+    return FL_OK;
+}
+
+int filtered_ranks_noalloc(const int64_t *ib, const int64_t *ie, const float *v, int64_t nnz, const int64_t *targets,
+                           const int64_t *fk, int64_t nf, int64_t B, int64_t E, int use_eql, float *ranks,
+                           cudaStream_t st) {
+    FL_REQUIRE(B >= 0 && B <= kNoAllocMaxQueries,
+               "fl_filtered_ranks_noalloc handles at most %lld queries per call (got %lld); use fl_filtered_ranks",
+               static_cast<long long>(kNoAllocMaxQueries), static_cast<long long>(B));
+    void *scratch = nullptr;
+    int rc = rank_scratch_address(&scratch);
+    if (rc) return rc;
+    // filtered_ranks clears every counter it uses before counting.
+    return filtered_ranks(ib, ie, v, nnz, targets, fk, nf, B, E, use_eql, ranks, scratch, sizeof(g_rank_scratch), st);
 }
 
 }  // namespace fl

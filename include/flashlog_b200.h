@@ -185,6 +185,22 @@ int fl_filtered_ranks(const int64_t *idx_b, const int64_t *idx_e, const float *v
                       const int64_t *targets, const int64_t *filter_keys, int64_t n_filter, int64_t B, int64_t E,
                       int use_eql, float *ranks, void *ws, size_t ws_bytes, fl_stream_t stream);
 
+/* fl_filtered_ranks for callers that cannot allocate device memory (no
+ * reference counterpart: the reference allocates its counters with torch on
+ * every call).  Same inputs, outputs and results as fl_filtered_ranks, but the
+ * per-query counters live in a fixed 1.25 MiB array inside this library's
+ * device memory, which every GPU that loads the library keeps until the
+ * process exits; the call itself allocates nothing.  At most 65536 queries
+ * (B) per call -- larger B returns FL_EINVAL.  The first call on each device
+ * looks up that array's device address (cudaGetSymbolAddress) with the device
+ * current; make that first call before any stream capture.  All calls share
+ * the one array and each call clears it before counting, so calls that
+ * overlap on the GPU (concurrent streams, or host threads sharing a device)
+ * race and must be serialized by the caller. */
+int fl_filtered_ranks_noalloc(const int64_t *idx_b, const int64_t *idx_e, const float *values, int64_t nnz,
+                              const int64_t *targets, const int64_t *filter_keys, int64_t n_filter, int64_t B,
+                              int64_t E, int use_eql, float *ranks, fl_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
