@@ -151,12 +151,13 @@ class Stats:
     def reduce(self):
         g = self.graph.csr
         S = G = F = U = 0
-        for ent, entry_count, u in self.records:
-            e = ent.to(torch.int64)
-            S += e.numel()
+        for ent, s_live, entry_count, u_live in self.records:
+            n = int(s_live.item())
+            e = ent[:n].to(torch.int64)
+            S += n
             G += int(((g[8][e + 1] - g[8][e]).sum() + (g[12][e + 1] - g[12][e]).sum()).item())
-            F += int(entry_count.to(torch.int64).sum().item()) - e.numel()  # identity terms excluded
-            U += int(u)
+            F += int(entry_count[:n].to(torch.int64).sum().item()) - n  # identity terms excluded
+            U += int(u_live.item())
         return S, G, F, U
 
 
@@ -197,6 +198,7 @@ def run_value_arm(args, cfg, train, csr, rank, world, device):
     data = batches_for(cfg, train, nb, rank)
     dev_data = [tuple(torch.from_numpy(x).to(device) for x in b) for b in data]
     stats = Stats(graph)
+    status = engine.new_status(device)
     lr = 0.01
 
     def step(ids, h, r, t, collect):
@@ -209,7 +211,7 @@ def run_value_arm(args, cfg, train, csr, rank, world, device):
         mask[hide] = 0
         w_all = table[r]
         rp, ent, val = engine.drum_propagate(h, w_all, graph, R, c1=cfg.c1 or None, c2=cfg.c2, mask_triple=mask,
-                                             stats=stats if collect else None)
+                                             stats=stats if collect else None, status=status)
         loss = engine.readout_loss(rp, ent, val, t, N)
         table.grad = None
         loss.backward()
@@ -243,6 +245,7 @@ def run_value_arm(args, cfg, train, csr, rank, world, device):
     if world > 1:
         dist.barrier()
     ms = t0.elapsed_time(t1)
+    engine.check_status(status)  # no hop ran out of its buffers
     launches = _lib.lib().fl_launch_count() - launches0
     clk = clocks.stop()
     S, G, F, U = stats.reduce()

@@ -12,7 +12,7 @@ import subprocess
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libflashlog_b200.so")
 CSRC = os.path.join(HERE, "csrc")
-SOURCES = ["api.cu", "scan.cu", "topc.cu", "hop.cu", "rules.cu", "csr.cu"]
+SOURCES = ["api.cu", "scan.cu", "topc.cu", "hop.cu", "rules.cu", "csr.cu", "readout.cu"]
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
               "-fmad=false", "-Xcompiler", "-fPIC", "-shared"]
 
@@ -24,6 +24,7 @@ FL_EDGE_SCORE = 32
 FL_EDGE_WEIGHT = 64
 FL_NO_NORMALIZE = 1 << 20
 NO_BUDGET = 1 << 62
+FL_STATUS_SLOT_OVERFLOW = 1
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
@@ -54,7 +55,8 @@ class fl_csr_side(ctypes.Structure):
 class fl_hop_params(ctypes.Structure):
     _fields_ = [("rows", ctypes.c_int64), ("L", ctypes.c_int64), ("n", ctypes.c_int64),
                 ("r_size", ctypes.c_int64), ("E", ctypes.c_int64), ("topk_edges", ctypes.c_int64),
-                ("flags", ctypes.c_int64), ("sampling_seed", ctypes.c_int64), ("eps", ctypes.c_float)]
+                ("flags", ctypes.c_int64), ("sampling_seed", ctypes.c_int64), ("eps", ctypes.c_float),
+                ("slot_capacity", ctypes.c_int64), ("status", ctypes.c_void_p)]
 
 
 _P = ctypes.c_void_p
@@ -75,7 +77,7 @@ SIGNATURES = {
     "fl_coo_to_rows": (ctypes.c_int, [_P, _P, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P]),
     "fl_rows_to_coo": (ctypes.c_int, [_P, _P, _I64, _I64, _I64, _P, _P]),
     "fl_topc_workspace": (_SZ, [_I64, _I64]),
-    "fl_topc_select": (ctypes.c_int, [_P, _P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _SZ, _P]),
+    "fl_topc_select": (ctypes.c_int, [_P, _P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _I64, _P, _P, _SZ, _P]),
     "fl_topc_candidates": (ctypes.c_int, [_P, _P, _I64, _I64, _I64, ctypes.POINTER(ctypes.c_int64), _P, _SZ, _P]),
     "fl_hop_workspace": (_SZ, [_I64, _I64]),
     "fl_hop_plan": (ctypes.c_int, [_PARAMS, _P, _P, _I64, _SIDE, _SIDE, _P, ctypes.POINTER(ctypes.c_int64), _P,
@@ -84,13 +86,15 @@ SIGNATURES = {
                                      _P, _P, _P]),
     "fl_reduce_workspace": (_SZ, [_I64, _I64]),
     "fl_row_reduce": (ctypes.c_int, [_P, _I64, _I64, _P, _P, _P, _P, _I64, _P, ctypes.c_float, _P, _P, _P, _P, _P,
-                                     _P, _SZ, _P]),
+                                     _P, _P, _SZ, _P]),
     "fl_hop_backward_workspace": (_SZ, [_I64, _I64]),
     "fl_hop_backward": (ctypes.c_int, [_PARAMS, _P, _P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                        _SZ, _P]),
     "fl_normalize_forward": (ctypes.c_int, [_P, _P, _I64, ctypes.c_float, _P, _P, _P]),
     "fl_normalize_backward": (ctypes.c_int, [_P, _P, _P, _P, _I64, ctypes.c_float, _P, _P]),
-    "fl_scatter_grad": (ctypes.c_int, [_P, _P, _I64, _P, _I64, _P]),
+    "fl_scatter_grad": (ctypes.c_int, [_P, _P, _I64, _P, _P, _I64, _P]),
+    "fl_readout": (ctypes.c_int, [_P, _P, _P, _I64, _P, _I64, _P, _P]),
+    "fl_readout_backward": (ctypes.c_int, [_P, _P, _I64, _P, _I64, _P, _P, _I64, _P]),
     "fl_fixed_relation_workspace": (_SZ, [_I64]),
     "fl_fixed_relation_plan": (ctypes.c_int, [_P, _P, _P, _I64, _P, _I64, _I64, _SIDE, _SIDE, _P,
                                               ctypes.POINTER(ctypes.c_int64), _P, _SZ, _P]),

@@ -56,6 +56,11 @@ int filtered_ranks_noalloc(const int64_t *ib, const int64_t *ie, const float *v,
                            const int64_t *fk, int64_t nf, int64_t B, int64_t E, int use_eql, float *ranks,
                            cudaStream_t st);
 
+int readout(const int64_t *row_ptr, const int32_t *ent, const float *val, int64_t N, const int64_t *targets, int64_t Q,
+            float *scores, cudaStream_t st);
+int readout_backward(const int64_t *row_ptr, const int32_t *ent, int64_t N, const int64_t *targets, int64_t Q,
+                     const float *g, float *grad_val, int64_t n_val, cudaStream_t st);
+
 namespace {
 
 // COO (b, l, e) sorted by key -> row_ptr by binary search per row; entity ids
@@ -150,9 +155,9 @@ size_t fl_topc_workspace(int64_t rows, int64_t S) { return topc_workspace(rows, 
 
 int fl_topc_select(const int64_t *row_ptr, const int32_t *ent, const float *val, int64_t rows, int64_t S, int64_t c1,
                    const double *noise, int64_t *out_row_ptr, int32_t *out_ent, float *out_val, int64_t *out_src,
-                   void *ws, size_t ws_bytes, fl_stream_t stream) {
-    return topc_select(row_ptr, ent, val, rows, S, c1, noise, out_row_ptr, out_ent, out_val, out_src, ws, ws_bytes,
-                       as_stream(stream));
+                   int64_t out_capacity, int32_t *status, void *ws, size_t ws_bytes, fl_stream_t stream) {
+    return topc_select(row_ptr, ent, val, rows, S, c1, noise, out_row_ptr, out_ent, out_val, out_src, out_capacity,
+                       status, ws, ws_bytes, as_stream(stream));
 }
 
 int fl_topc_candidates(const int64_t *row_ptr, const float *val, int64_t rows, int64_t S, int64_t c1,
@@ -186,9 +191,9 @@ size_t fl_reduce_workspace(int64_t rows, int64_t total_slots) { return row_reduc
 int fl_row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *slot_base, const int32_t *entry_count,
                   const int32_t *fact_dst, const float *fact_val, int64_t total_slots, int32_t *fact_pos, float eps,
                   int64_t *out_row_ptr, int32_t *out_ent, float *out_x, float *out_y, float *out_denom,
-                  void *ws, size_t ws_bytes, fl_stream_t stream) {
+                  int32_t *status, void *ws, size_t ws_bytes, fl_stream_t stream) {
     return row_reduce(row_ptr, rows, E, slot_base, entry_count, fact_dst, fact_val, total_slots, fact_pos, eps,
-                      out_row_ptr, out_ent, out_x, out_y, out_denom, ws, ws_bytes, as_stream(stream));
+                      out_row_ptr, out_ent, out_x, out_y, out_denom, status, ws, ws_bytes, as_stream(stream));
 }
 
 size_t fl_hop_backward_workspace(int64_t rows, int64_t n) { return hop_backward_workspace(rows, n); }
@@ -213,9 +218,9 @@ int fl_normalize_backward(const int64_t *row_ptr, const float *x, const float *d
     return normalize_backward(row_ptr, x, denom, g, rows, eps, gx, as_stream(stream));
 }
 
-int fl_scatter_grad(const float *grad_sel, const int64_t *src_index, int64_t n_sel, float *grad_full, int64_t n_full,
-                    fl_stream_t stream) {
-    return scatter_grad(grad_sel, src_index, n_sel, grad_full, n_full, as_stream(stream));
+int fl_scatter_grad(const float *grad_sel, const int64_t *src_index, int64_t n_sel, const int64_t *n_live,
+                    float *grad_full, int64_t n_full, fl_stream_t stream) {
+    return scatter_grad(grad_sel, src_index, n_sel, n_live, grad_full, n_full, as_stream(stream));
 }
 
 size_t fl_fixed_relation_workspace(int64_t nnz) { return fixed_relation_workspace(nnz); }
@@ -249,6 +254,16 @@ int fl_filtered_ranks_noalloc(const int64_t *idx_b, const int64_t *idx_e, const 
                               int64_t E, int use_eql, float *ranks, fl_stream_t stream) {
     return filtered_ranks_noalloc(idx_b, idx_e, values, nnz, targets, filter_keys, n_filter, B, E, use_eql, ranks,
                                   as_stream(stream));
+}
+
+int fl_readout(const int64_t *row_ptr, const int32_t *ent, const float *val, int64_t N, const int64_t *targets,
+               int64_t Q, float *scores, fl_stream_t stream) {
+    return readout(row_ptr, ent, val, N, targets, Q, scores, as_stream(stream));
+}
+
+int fl_readout_backward(const int64_t *row_ptr, const int32_t *ent, int64_t N, const int64_t *targets, int64_t Q,
+                        const float *g_scores, float *grad_val, int64_t n_val, fl_stream_t stream) {
+    return readout_backward(row_ptr, ent, N, targets, Q, g_scores, grad_val, n_val, as_stream(stream));
 }
 
 }  // extern "C"

@@ -58,10 +58,11 @@ __device__ __forceinline__ int64_t side_degree(const Side &s, int64_t src) {
     return g0 == g1 ? 0 : static_cast<int64_t>(s.gstart[g1 - 1]) + s.gcount[g1 - 1] - s.gstart[g0];
 }
 
-__global__ void hop_capacity_kernel(const int32_t *ent, int64_t S, Side ori, Side inv, int64_t topk,
-                                    int wot_i, int64_t *cap) {
+__global__ void hop_capacity_kernel(const int32_t *ent, const int64_t *row_ptr, int64_t rows, int64_t S, Side ori,
+                                    Side inv, int64_t topk, int wot_i, int64_t *cap) {
     int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
     if (i >= S) return;
+    if (i >= row_ptr[rows]) { cap[i] = 0; return; }  // beyond the live entries
     int64_t src = ent[i];
     int64_t d0 = side_degree(ori, src);
     int64_t d1 = side_degree(inv, src);
@@ -83,39 +84,82 @@ struct WarpScratch {
     int32_t quota[32];
 };
 
-// Weighted order statistic over the groups' weights (flashlog.cu:26-63): the
-// key T with sum(count | key > T) < budget <= sum(count | key >= T).  Returns
-// T and the number of edges to keep at T.  Only groups with w > 0 count.
-__device__ void group_threshold(const float *wdir, const Side &sd, int64_t g0, int64_t g1, int64_t budget,
+// Weighted order statistic over the groups' weights (flashlog.cu:26-63).
+// Groups with w > 0 count with multiplicity group_count.  When their total
+// exceeds the budget, returns true with *thr = the key T such that
+// sum(count | key > T) < budget <= sum(count | key >= T) and *keep = the
+// number of edges still to take at T; returns false when everything fits.
+// Keys are the fp32 bit patterns of the (positive) weights.
+__device__ __forceinline__ void group_key(const float *wdir, const Side &sd, int64_t g, int64_t g1, uint32_t *key,
+                                          uint32_t *cnt) {
+    *key = 0u;
+    *cnt = 0u;
+    if (g < g1) {
+        const float wg = wdir[sd.grel[g]];
+        if (wg > 0.0f) { *key = __float_as_uint(wg); *cnt = static_cast<uint32_t>(sd.gcount[g]); }
+    }
+}
+
+__device__ bool group_threshold(const float *wdir, const Side &sd, int64_t g0, int64_t g1, int64_t budget,
                                 WarpScratch &ws, uint32_t *thr, int64_t *keep) {
     const int lane = threadIdx.x & 31;
+    if (g1 - g0 <= 32) {
+        // One group per lane: every lane counts the groups at or above its own key.
+        uint32_t key, cnt;
+        group_key(wdir, sd, g0 + lane, g1, &key, &cnt);
+        const int64_t total = warp_sum(static_cast<int64_t>(cnt));
+        if (total <= budget) return false;
+        int64_t ge = 0, gt = 0;
+#pragma unroll 8
+        for (int j = 0; j < 32; ++j) {
+            const uint32_t kj = __shfl_sync(kFull, key, j);
+            const int64_t cj = __shfl_sync(kFull, cnt, j);
+            ge += kj >= key ? cj : 0;
+            gt += kj > key ? cj : 0;
+        }
+        const unsigned q = __ballot_sync(kFull, cnt > 0u && gt < budget && ge >= budget);
+        const int src = __ffs(q) - 1;
+        *thr = __shfl_sync(kFull, key, src);
+        *keep = budget - __shfl_sync(kFull, gt, src);
+        return true;
+    }
+    // MSB-first radix select over 8-bit digits.  Lanes with equal digits are
+    // merged with a warp match before the shared-memory add, so equal weights
+    // (common: groups of one relation share it) do not serialize.
     uint32_t prefix = 0, pmask = 0;
     int64_t krem = budget;
     for (int shift = 24; shift >= 0; shift -= 8) {
         for (int d = lane; d < 256; d += 32) ws.hist[d] = 0;
         __syncwarp();
-        for (int64_t g = g0 + lane; g < g1; g += 32) {
-            float wg = wdir[sd.grel[g]];
-            if (!(wg > 0.0f)) continue;
-            uint32_t key = __float_as_uint(wg);
-            if ((key & pmask) == prefix) atomicAdd(&ws.hist[(key >> shift) & 255u], static_cast<unsigned>(sd.gcount[g]));
+        for (int64_t cb = g0; cb < g1; cb += 32) {
+            uint32_t key, cnt;
+            group_key(wdir, sd, cb + lane, g1, &key, &cnt);
+            const bool part = cnt > 0u && (key & pmask) == prefix;
+            const unsigned act = __ballot_sync(kFull, part);
+            if (part) {
+                const uint32_t d = (key >> shift) & 255u;
+                const unsigned peers = __match_any_sync(act, d);
+                const unsigned sum = __reduce_add_sync(peers, cnt);
+                if (lane == __ffs(peers) - 1) atomicAdd(&ws.hist[d], sum);
+            }
         }
         __syncwarp();
         // lane j owns digits 255 - 8j .. 248 - 8j (descending)
         int64_t part = 0;
 #pragma unroll
         for (int k = 0; k < 8; ++k) part += ws.hist[255 - (lane * 8 + k)];
-        int64_t incl = warp_inclusive_scan(part);
-        int64_t excl = incl - part;
-        unsigned ball = __ballot_sync(kFull, incl >= krem && excl < krem);
-        int src_lane = __ffs(ball) - 1;  // exactly one lane crosses krem
+        const int64_t incl = warp_inclusive_scan(part);
+        if (shift == 24 && __shfl_sync(kFull, incl, 31) <= budget) return false;
+        const int64_t excl = incl - part;
+        const unsigned ball = __ballot_sync(kFull, incl >= krem && excl < krem);
+        const int src_lane = __ffs(ball) - 1;  // exactly one lane crosses krem
         int digit = 0;
         int64_t above = 0;
         if (lane == src_lane) {
             int64_t acc = excl;
             for (int k = 0; k < 8; ++k) {
-                int d = 255 - (lane * 8 + k);
-                int64_t h = ws.hist[d];
+                const int d = 255 - (lane * 8 + k);
+                const int64_t h = ws.hist[d];
                 if (acc + h >= krem) { digit = d; above = acc; break; }
                 acc += h;
             }
@@ -129,13 +173,15 @@ __device__ void group_threshold(const float *wdir, const Side &sd, int64_t g0, i
     }
     *thr = prefix;
     *keep = krem;
+    return true;
 }
 
 struct ExpandArgs {
     const int64_t *row_ptr;
     const int32_t *ent;
     const float *val;
-    int64_t S, rows, n, r_size, topk, flags, seed, L;
+    int64_t S, rows, n, r_size, topk, flags, seed, L, capacity;
+    int32_t *status;
     const float *w;
     Side ori, inv;
     const uint8_t *mask_triple;
@@ -159,18 +205,23 @@ __device__ __forceinline__ double splitmix_phase(int64_t seed, int64_t b, int64_
     return static_cast<double>(z >> 11) * 0x1.0p-53;
 }
 
-__global__ void __launch_bounds__(kExpandWarps * 32) hop_expand_kernel(ExpandArgs a) {
+template <bool kSampled>
+__global__ void __launch_bounds__(kExpandWarps * 32, kSampled ? 3 : 4) hop_expand_kernel(ExpandArgs a) {
     __shared__ WarpScratch scratch[kExpandWarps];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     WarpScratch &ws = scratch[wib];
     const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kExpandWarps;
     const bool skip_nonpos = (a.flags & FL_SKIP_NONPOS_W) != 0;
     const bool drop_masked = (a.flags & FL_DROP_MASKED) != 0;
-    const bool sampled = (a.flags & FL_SAMPLED) != 0;
     const bool edge_w = (a.flags & FL_EDGE_WEIGHT) != 0 && a.edge_weight != nullptr;
     const bool edge_score = (a.flags & FL_EDGE_SCORE) != 0;
     const bool wot_i = (a.flags & FL_WOT_I) != 0;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * kExpandWarps + wib; i < a.S; i += nwarps) {
+    const int64_t S_live = a.row_ptr[a.rows] < a.S ? a.row_ptr[a.rows] : a.S;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * kExpandWarps + wib; i < S_live; i += nwarps) {
+        if (a.capacity > 0 && a.slot_base[i + 1] > a.capacity) {  // would write past the fact buffers
+            if (lane == 0) { a.entry_count[i] = 0; if (a.status) atomicOr(a.status, FL_STATUS_SLOT_OVERFLOW); }
+            continue;
+        }
         const int64_t row = find_row(a.row_ptr, a.rows, i);
         const int64_t src = a.ent[i];
         const float v = a.val[i];
@@ -189,7 +240,7 @@ __global__ void __launch_bounds__(kExpandWarps * 32) hop_expand_kernel(ExpandArg
             // sampled-mode state (lane 0 only)
             int64_t q_target = 0, q_residual = 0, q_spare = 0, q_left = 0, q_capleft = 0, q_prefix = 0;
             double q_wsum = 0.0, q_phase = 0.0;
-            if (sampled) {
+            if constexpr (kSampled) {
                 if (lane == 0) {
                     int64_t capacity = 0;
                     double wsum = 0.0;
@@ -218,14 +269,7 @@ __global__ void __launch_bounds__(kExpandWarps * 32) hop_expand_kernel(ExpandArg
                     q_prefix = 0;
                 }
             } else if (skip_nonpos && a.topk < kNoBudget) {
-                int64_t total = 0;
-                for (int64_t g = g0 + lane; g < g1; g += 32)
-                    if (wdir[sd.grel[g]] > 0.0f) total += sd.gcount[g];
-                total = warp_sum(total);
-                if (total > a.topk) {
-                    use_thr = true;
-                    group_threshold(wdir, sd, g0, g1, a.topk, ws, &thr, &keep_thr);
-                }
+                use_thr = group_threshold(wdir, sd, g0, g1, a.topk, ws, &thr, &keep_thr);
             }
             int64_t tie_seen = 0;
             for (int64_t cb = g0; cb < g1; cb += 32) {
@@ -235,7 +279,7 @@ __global__ void __launch_bounds__(kExpandWarps * 32) hop_expand_kernel(ExpandArg
                 int32_t cnt = valid ? sd.gcount[g] : 0;
                 float wg = valid ? wdir[rel] : 0.0f;
                 int32_t take;
-                if (sampled) {
+                if constexpr (kSampled) {
                     // Sequential quota arithmetic of flashlog.cu:1505-1531, lane 0.
                     ws.rel[lane] = rel;
                     __syncwarp();
@@ -355,32 +399,33 @@ __global__ void __launch_bounds__(kExpandWarps * 32) hop_expand_kernel(ExpandArg
 // ---------------------------------------------------------------------------
 constexpr int kRThreads = 512;
 constexpr int kRWarps = kRThreads / 32;
-constexpr int kTile = 8192;             // facts sorted at once
+constexpr int kTile = 8192;                  // facts sorted at once in shared memory
 constexpr int kWarpItems = kTile / kRWarps;  // 512 per warp region
-constexpr int kLoadK = 4;               // flat facts per thread per load step
+constexpr int kLoadK = 4;                    // facts per thread per load step
 constexpr int kLoadStep = kRThreads * kLoadK;
-constexpr int kEChunk = 1024;           // entries per prefix chunk
-constexpr int kBins = 1024;             // histogram bins per refinement level
-constexpr int kDenseW = 4096;           // widest destination window summed densely
+constexpr int kEChunk = 1024;                // entries per prefix chunk
+constexpr int kBucketBits = 11;
+constexpr int kBuckets = 1 << kBucketBits;   // destination buckets per row
+constexpr int kDenseW = 4096;                // widest destination window summed densely
 
 struct ReduceSmem {
     uint32_t key[2][kTile];
     uint16_t idx[2][kTile];
-    float val[kTile];
+    uint32_t val[kTile];  // fact value bits (a destination id while partitioning)
     uint32_t slot[kTile];
-    uint32_t shist[kRWarps][256];
-    uint32_t lvl1[kBins];
-    uint32_t lvl2[kBins];
+    uint32_t shist[kRWarps][256];  // sort digit counters; run starts while partitioning
+    uint32_t bstart[kBuckets + 1];
+    uint32_t bcursor[kBuckets];
+    uint16_t items[kBuckets + 1];
     uint32_t epre[kEChunk + 1];
     uint32_t eslot[kEChunk];
     float acc[kDenseW];
     uint32_t touched[kDenseW / 32];
-    uint16_t items1[kBins + 1];
-    uint16_t items2[kBins + 1];
     int64_t scan_scratch[kRWarps + 1];
     float fscratch[kRWarps + 1];
-    int n_items1, n_items2;
+    int n_items;
 };
+static_assert(sizeof(ReduceSmem) <= 227 * 1024, "row reduction shared memory exceeds one CTA's budget");
 
 struct ReduceArgs {
     const int64_t *row_ptr;      // rows of the (selected) state
@@ -393,8 +438,11 @@ struct ReduceArgs {
     int32_t *fact_pos;           // may be null
     int32_t *tmp_ent;            // outputs at the row's slot base
     float *tmp_x;
+    uint2 *part;                 // (dst, slot) partition scratch at the row's slot base
     int64_t *out_count;
     float *out_sum;
+    int64_t capacity;            // length of the fact / output buffers
+    int32_t *status;             // device status bits (may be null)
 };
 
 __device__ __forceinline__ int bits_for(int64_t width) {  // bits to represent width - 1
@@ -403,28 +451,30 @@ __device__ __forceinline__ int bits_for(int64_t width) {  // bits to represent w
     return b;
 }
 
-// Stream the row's facts in canonical order; for each fact whose destination
-// lies in [lo, hi) call visit(slot, dst, pos) where pos is the ordinal among
-// visited facts.  Returns the number visited.  All threads must call it.
-template <typename Visit>
+// Stream the row's facts in canonical order (entries in row order, each
+// entry's facts in emission order).  For a fact whose destination lies in
+// [lo, hi), visit(slot, dst, pos) is called with pos its ordinal among the
+// visited facts.  Before each load step pre(visited) may flush and returns
+// the ordinal base to continue from.  All threads must call it.
+template <typename Visit, typename Pre>
 __device__ int64_t stream_row(const ReduceArgs &a, ReduceSmem &sm, int64_t ea, int64_t eb, int64_t lo, int64_t hi,
-                              Visit visit) {
+                              Visit visit, Pre pre) {
     int64_t visited = 0;
     for (int64_t ec = ea; ec < eb; ec += kEChunk) {
         const int64_t ne = (eb - ec) < kEChunk ? (eb - ec) : kEChunk;
-        // prefix of entry fact counts within the chunk (2 entries per thread)
         int64_t c0 = 0, c1 = 0;
         const int64_t j0 = ec + 2 * threadIdx.x, j1 = j0 + 1;
         if (2 * threadIdx.x < ne) { c0 = a.entry_count[j0]; sm.eslot[2 * threadIdx.x] = static_cast<uint32_t>(a.slot_base[j0]); }
         if (2 * threadIdx.x + 1 < ne) { c1 = a.entry_count[j1]; sm.eslot[2 * threadIdx.x + 1] = static_cast<uint32_t>(a.slot_base[j1]); }
         int64_t tot;
-        int64_t ex = block_exclusive_scan<int64_t>(c0 + c1, sm.scan_scratch, &tot);
+        const int64_t ex = block_exclusive_scan<int64_t>(c0 + c1, sm.scan_scratch, &tot);
         if (2 * threadIdx.x < ne) sm.epre[2 * threadIdx.x] = static_cast<uint32_t>(ex);
         if (2 * threadIdx.x + 1 < ne) sm.epre[2 * threadIdx.x + 1] = static_cast<uint32_t>(ex + c0);
         if (threadIdx.x == 0) sm.epre[ne] = static_cast<uint32_t>(tot);
         __syncthreads();
         const uint32_t nf = static_cast<uint32_t>(tot);
         for (uint32_t fb = 0; fb < nf; fb += kLoadStep) {
+            visited = pre(visited);
             uint32_t slot[kLoadK];
             int32_t dst[kLoadK];
             int cnt = 0;
@@ -436,12 +486,12 @@ __device__ int64_t stream_row(const ReduceArgs &a, ReduceSmem &sm, int64_t ea, i
                     int l2 = 0, h2 = static_cast<int>(ne) - 1;  // last entry with epre <= f
                     while (l2 < h2) { int mid = (l2 + h2 + 1) >> 1; if (sm.epre[mid] <= f) l2 = mid; else h2 = mid - 1; }
                     slot[k] = sm.eslot[l2] + (f - sm.epre[l2]);
-                    int32_t d = a.fact_dst[slot[k]];
+                    const int32_t d = a.fact_dst[slot[k]];
                     if (d >= lo && d < hi) { dst[k] = d; ++cnt; }
                 }
             }
             int64_t btot;
-            int64_t bex = block_exclusive_scan<int64_t>(cnt, sm.scan_scratch, &btot);
+            const int64_t bex = block_exclusive_scan<int64_t>(cnt, sm.scan_scratch, &btot);
             int64_t pos = visited + bex;
 #pragma unroll
             for (int k = 0; k < kLoadK; ++k)
@@ -451,6 +501,12 @@ __device__ int64_t stream_row(const ReduceArgs &a, ReduceSmem &sm, int64_t ea, i
         }
     }
     return visited;
+}
+
+template <typename Visit>
+__device__ int64_t stream_row(const ReduceArgs &a, ReduceSmem &sm, int64_t ea, int64_t eb, int64_t lo, int64_t hi,
+                              Visit visit) {
+    return stream_row(a, sm, ea, eb, lo, hi, visit, [](int64_t v) { return v; });
 }
 
 // Stable LSD radix sort of sm.key[0][0..n) with payload sm.idx[0] over `bits`
@@ -466,8 +522,15 @@ __device__ int tile_sort(ReduceSmem &sm, int n, int bits) {
         __syncwarp();
         const int wbase = warp * kWarpItems;
         for (int k = 0; k < kWarpItems / 32; ++k) {
-            int j = wbase + k * 32 + lane;
-            if (j < n) atomicAdd(&sm.shist[warp][(sm.key[cur][j] >> shift) & dmask], 1u);
+            const int j = wbase + k * 32 + lane;
+            const bool valid = j < n;
+            const uint32_t d = valid ? (sm.key[cur][j] >> shift) & dmask : 0u;
+            const unsigned act = __ballot_sync(kFull, valid);
+            if (valid) {
+                const unsigned peers = __match_any_sync(act, d);
+                if (lane == __ffs(peers) - 1) sm.shist[warp][d] += __popc(peers);
+            }
+            __syncwarp();
         }
         __syncthreads();
         // digit-major exclusive offsets: thread t < ndig owns digit t
@@ -475,32 +538,31 @@ __device__ int tile_sort(ReduceSmem &sm, int n, int bits) {
         if (static_cast<int>(threadIdx.x) < ndig)
             for (int w2 = 0; w2 < kRWarps; ++w2) dsum += sm.shist[w2][threadIdx.x];
         int64_t tot;
-        int64_t dex = block_exclusive_scan<int64_t>(static_cast<int64_t>(threadIdx.x < static_cast<unsigned>(ndig) ? dsum : 0),
-                                                    sm.scan_scratch, &tot);
+        const int64_t dex = block_exclusive_scan<int64_t>(
+            static_cast<int64_t>(threadIdx.x < static_cast<unsigned>(ndig) ? dsum : 0), sm.scan_scratch, &tot);
         if (static_cast<int>(threadIdx.x) < ndig) {
             uint32_t run = static_cast<uint32_t>(dex);
             for (int w2 = 0; w2 < kRWarps; ++w2) {
-                uint32_t h = sm.shist[w2][threadIdx.x];
+                const uint32_t h = sm.shist[w2][threadIdx.x];
                 sm.shist[w2][threadIdx.x] = run;
                 run += h;
             }
         }
         __syncthreads();
         for (int k = 0; k < kWarpItems / 32; ++k) {
-            int j = wbase + k * 32 + lane;
-            bool valid = j < n;
-            uint32_t key = valid ? sm.key[cur][j] : 0u;
-            uint32_t d = (key >> shift) & dmask;
-            unsigned act = __ballot_sync(kFull, valid);
+            const int j = wbase + k * 32 + lane;
+            const bool valid = j < n;
+            const uint32_t key = valid ? sm.key[cur][j] : 0u;
+            const uint32_t d = (key >> shift) & dmask;
+            const unsigned act = __ballot_sync(kFull, valid);
             if (valid) {
-                unsigned peers = __match_any_sync(act, d);
-                int rank = __popc(peers & lanemask_lt());
-                uint32_t base = sm.shist[warp][d];
-                int leader = __ffs(peers) - 1;
+                const unsigned peers = __match_any_sync(act, d);
+                const int rank = __popc(peers & lanemask_lt());
+                const uint32_t base = sm.shist[warp][d];
                 sm.key[cur ^ 1][base + rank] = key;
                 sm.idx[cur ^ 1][base + rank] = sm.idx[cur][j];
                 __syncwarp(act);
-                if (lane == leader) sm.shist[warp][d] = base + __popc(peers);
+                if (lane == __ffs(peers) - 1) sm.shist[warp][d] = base + __popc(peers);
             }
             __syncwarp();
         }
@@ -510,18 +572,19 @@ __device__ int tile_sort(ReduceSmem &sm, int n, int bits) {
     return cur;
 }
 
-// Sort the loaded tile [0, n) (keys are dst - lo) and emit one output per
-// destination, summing in canonical order.  Returns the block-sum of outputs.
+// Sort the loaded tile [0, n) (keys are dst - lo, values in sm.val) and emit
+// one output per destination, summing in canonical order.  Returns the
+// block-sum of the outputs.
 __device__ float emit_sorted(const ReduceArgs &a, ReduceSmem &sm, int n, int bits, int64_t lo, int64_t obase,
                              int64_t *written) {
     const int cur = tile_sort(sm, n, bits);
     uint32_t *seg = sm.key[cur ^ 1];  // free buffer: segment starts
     int64_t nseg_total = 0;
     for (int base = 0; base < n; base += kRThreads) {
-        int j = base + threadIdx.x;
-        bool head = j < n && (j == 0 || sm.key[cur][j] != sm.key[cur][j - 1]);
+        const int j = base + threadIdx.x;
+        const bool head = j < n && (j == 0 || sm.key[cur][j] != sm.key[cur][j - 1]);
         int64_t tot;
-        int64_t ex = block_exclusive_scan<int64_t>(head ? 1 : 0, sm.scan_scratch, &tot);
+        const int64_t ex = block_exclusive_scan<int64_t>(head ? 1 : 0, sm.scan_scratch, &tot);
         if (head) seg[nseg_total + ex] = static_cast<uint32_t>(j);
         nseg_total += tot;
     }
@@ -532,7 +595,7 @@ __device__ float emit_sorted(const ReduceArgs &a, ReduceSmem &sm, int n, int bit
         const int st = static_cast<int>(seg[s]);
         const int en = s + 1 < nseg ? static_cast<int>(seg[s + 1]) : n;
         float x = 0.0f;
-        for (int q = st; q < en; ++q) x += sm.val[sm.idx[cur][q]];
+        for (int q = st; q < en; ++q) x += __uint_as_float(sm.val[sm.idx[cur][q]]);
         const int64_t oi = *written + s;
         a.tmp_ent[obase + oi] = static_cast<int32_t>(lo + sm.key[cur][st]);
         a.tmp_x[obase + oi] = x;
@@ -541,104 +604,83 @@ __device__ float emit_sorted(const ReduceArgs &a, ReduceSmem &sm, int n, int bit
         local += x;
     }
     *written += nseg;
-    float total = block_sum(local, sm.fscratch);
-    return total;
+    return block_sum(local, sm.fscratch);
 }
 
-// Process the destination range [lo, hi) holding `count` <= kTile facts.
-__device__ float process_sorted_range(const ReduceArgs &a, ReduceSmem &sm, int64_t ea, int64_t eb, int64_t lo,
-                                      int64_t hi, int64_t obase, int64_t *written) {
-    int64_t n = stream_row(a, sm, ea, eb, lo, hi, [&](uint32_t slot, int32_t dst, int64_t pos) {
-        sm.key[0][pos] = static_cast<uint32_t>(dst - lo);
-        sm.idx[0][pos] = static_cast<uint16_t>(pos);
-        sm.val[pos] = a.fact_val[slot];
-        sm.slot[pos] = slot;
-    });
-    __syncthreads();
-    if (n == 0) return 0.0f;
-    return emit_sorted(a, sm, static_cast<int>(n), bits_for(hi - lo), lo, obase, written);
-}
-
-// Dense window [lo, hi), hi - lo <= kDenseW, any number of facts: tiles of
-// canonical order are stably sorted and added into acc[] one fact at a time.
-__device__ float process_dense_range(const ReduceArgs &a, ReduceSmem &sm, int64_t ea, int64_t eb, int64_t lo,
-                                     int64_t hi, int64_t obase, int64_t *written) {
+// Dense window [lo, hi), hi - lo <= kDenseW, over the contiguous (dst, slot)
+// pairs part[p0, p1) (canonical order; pairs outside the window are
+// skipped).  Tiles are stably sorted and added into acc[] one fact at a time,
+// so every destination is summed in canonical order.
+__device__ float dense_window(const ReduceArgs &a, ReduceSmem &sm, const uint2 *part, int64_t p0, int64_t p1,
+                              int64_t lo, int64_t hi, int64_t obase, int64_t *written) {
     const int W = static_cast<int>(hi - lo);
     const int bits = bits_for(W);
     for (int d = threadIdx.x; d < kDenseW; d += kRThreads) sm.acc[d] = 0.0f;
     for (int d = threadIdx.x; d < kDenseW / 32; d += kRThreads) sm.touched[d] = 0u;
     __syncthreads();
     int64_t in_tile = 0;
-    auto flush = [&](int n) {
-        if (n == 0) return;
+    for (int64_t fb = p0; fb < p1; fb += kLoadStep) {
+        if (in_tile + kLoadStep > kTile) {
+            const int n = static_cast<int>(in_tile);
+            const int cur = tile_sort(sm, n, bits);
+            for (int j = threadIdx.x; j < n; j += kRThreads) {
+                if (!(j == 0 || sm.key[cur][j] != sm.key[cur][j - 1])) continue;
+                const uint32_t d = sm.key[cur][j];
+                float accv = sm.acc[d];
+                for (int q = j; q < n && sm.key[cur][q] == d; ++q) accv += __uint_as_float(sm.val[sm.idx[cur][q]]);
+                sm.acc[d] = accv;
+                atomicOr(&sm.touched[d >> 5], 1u << (d & 31));
+            }
+            __syncthreads();
+            in_tile = 0;
+        }
+        uint2 pr[kLoadK];
+        int cnt = 0;
+#pragma unroll
+        for (int k = 0; k < kLoadK; ++k) {
+            const int64_t f = fb + static_cast<int64_t>(threadIdx.x) * kLoadK + k;
+            pr[k] = make_uint2(0xffffffffu, 0u);
+            if (f < p1) {
+                const uint2 v = part[f];
+                if (static_cast<int64_t>(v.x) >= lo && static_cast<int64_t>(v.x) < hi) { pr[k] = v; ++cnt; }
+            }
+        }
+        int64_t btot;
+        const int64_t bex = block_exclusive_scan<int64_t>(cnt, sm.scan_scratch, &btot);
+        int64_t pos = in_tile + bex;
+#pragma unroll
+        for (int k = 0; k < kLoadK; ++k)
+            if (pr[k].x != 0xffffffffu) {
+                sm.key[0][pos] = pr[k].x - static_cast<uint32_t>(lo);
+                sm.idx[0][pos] = static_cast<uint16_t>(pos);
+                sm.val[pos] = __float_as_uint(a.fact_val[pr[k].y]);
+                ++pos;
+            }
+        in_tile += btot;
+        __syncthreads();
+    }
+    if (in_tile > 0) {
+        const int n = static_cast<int>(in_tile);
         const int cur = tile_sort(sm, n, bits);
         for (int j = threadIdx.x; j < n; j += kRThreads) {
-            bool head = (j == 0 || sm.key[cur][j] != sm.key[cur][j - 1]);
-            if (!head) continue;
+            if (!(j == 0 || sm.key[cur][j] != sm.key[cur][j - 1])) continue;
             const uint32_t d = sm.key[cur][j];
             float accv = sm.acc[d];
-            for (int q = j; q < n && sm.key[cur][q] == d; ++q) accv += sm.val[sm.idx[cur][q]];
+            for (int q = j; q < n && sm.key[cur][q] == d; ++q) accv += __uint_as_float(sm.val[sm.idx[cur][q]]);
             sm.acc[d] = accv;
             atomicOr(&sm.touched[d >> 5], 1u << (d & 31));
         }
         __syncthreads();
-    };
-    // Stream in canonical order; flush whenever the next load step might overflow the tile.
-    for (int64_t ec = ea; ec < eb; ec += kEChunk) {
-        const int64_t ne = (eb - ec) < kEChunk ? (eb - ec) : kEChunk;
-        int64_t c0 = 0, c1 = 0;
-        const int64_t j0 = ec + 2 * threadIdx.x, j1 = j0 + 1;
-        if (2 * threadIdx.x < ne) { c0 = a.entry_count[j0]; sm.eslot[2 * threadIdx.x] = static_cast<uint32_t>(a.slot_base[j0]); }
-        if (2 * threadIdx.x + 1 < ne) { c1 = a.entry_count[j1]; sm.eslot[2 * threadIdx.x + 1] = static_cast<uint32_t>(a.slot_base[j1]); }
-        int64_t tot;
-        int64_t ex = block_exclusive_scan<int64_t>(c0 + c1, sm.scan_scratch, &tot);
-        if (2 * threadIdx.x < ne) sm.epre[2 * threadIdx.x] = static_cast<uint32_t>(ex);
-        if (2 * threadIdx.x + 1 < ne) sm.epre[2 * threadIdx.x + 1] = static_cast<uint32_t>(ex + c0);
-        if (threadIdx.x == 0) sm.epre[ne] = static_cast<uint32_t>(tot);
-        __syncthreads();
-        const uint32_t nf = static_cast<uint32_t>(tot);
-        for (uint32_t fb = 0; fb < nf; fb += kLoadStep) {
-            if (in_tile + kLoadStep > kTile) { flush(static_cast<int>(in_tile)); in_tile = 0; }
-            uint32_t slot[kLoadK];
-            int32_t dst[kLoadK];
-            int cnt = 0;
-#pragma unroll
-            for (int k = 0; k < kLoadK; ++k) {
-                const uint32_t f = fb + threadIdx.x * kLoadK + k;
-                dst[k] = -1;
-                if (f < nf) {
-                    int l2 = 0, h2 = static_cast<int>(ne) - 1;
-                    while (l2 < h2) { int mid = (l2 + h2 + 1) >> 1; if (sm.epre[mid] <= f) l2 = mid; else h2 = mid - 1; }
-                    slot[k] = sm.eslot[l2] + (f - sm.epre[l2]);
-                    int32_t d = a.fact_dst[slot[k]];
-                    if (d >= lo && d < hi) { dst[k] = d; ++cnt; }
-                }
-            }
-            int64_t btot;
-            int64_t bex = block_exclusive_scan<int64_t>(cnt, sm.scan_scratch, &btot);
-            int64_t pos = in_tile + bex;
-#pragma unroll
-            for (int k = 0; k < kLoadK; ++k)
-                if (dst[k] >= 0) {
-                    sm.key[0][pos] = static_cast<uint32_t>(dst[k] - lo);
-                    sm.idx[0][pos] = static_cast<uint16_t>(pos);
-                    sm.val[pos] = a.fact_val[slot[k]];
-                    ++pos;
-                }
-            in_tile += btot;
-            __syncthreads();
-        }
     }
-    flush(static_cast<int>(in_tile));
     // Output index of every touched destination (ordered compaction).
     uint32_t *oidx = sm.key[1];
     int64_t nout = 0;
     float local = 0.0f;
     for (int base = 0; base < W; base += kRThreads) {
-        int d = base + threadIdx.x;
-        bool t = d < W && ((sm.touched[d >> 5] >> (d & 31)) & 1u);
+        const int d = base + threadIdx.x;
+        const bool t = d < W && ((sm.touched[d >> 5] >> (d & 31)) & 1u);
         int64_t tot;
-        int64_t ex = block_exclusive_scan<int64_t>(t ? 1 : 0, sm.scan_scratch, &tot);
+        const int64_t ex = block_exclusive_scan<int64_t>(t ? 1 : 0, sm.scan_scratch, &tot);
         if (t) {
             const int64_t oi = *written + nout + ex;
             oidx[d] = static_cast<uint32_t>(oi);
@@ -649,23 +691,25 @@ __device__ float process_dense_range(const ReduceArgs &a, ReduceSmem &sm, int64_
         nout += tot;
     }
     __syncthreads();
-    if (a.fact_pos) {
-        stream_row(a, sm, ea, eb, lo, hi, [&](uint32_t slot, int32_t dst, int64_t) {
-            a.fact_pos[slot] = static_cast<int32_t>(oidx[dst - lo]);
-        });
-    }
+    if (a.fact_pos)
+        for (int64_t f = p0 + threadIdx.x; f < p1; f += kRThreads) {
+            const uint2 v = part[f];
+            if (static_cast<int64_t>(v.x) >= lo && static_cast<int64_t>(v.x) < hi)
+                a.fact_pos[v.y] = static_cast<int32_t>(oidx[v.x - lo]);
+        }
     *written += nout;
-    return block_sum(local, sm.fscratch);
+    const float total = block_sum(local, sm.fscratch);
+    return total;
 }
 
-// Greedy split of consecutive histogram bins into items of <= kTile facts; a
-// bin above kTile always forms an item of its own.  Writes item start bins
-// followed by the kBins sentinel and returns the number of items.
-__device__ int split_bins(const uint32_t *hist, uint16_t *items) {
+// Greedy split of consecutive buckets into items of <= kTile facts; a bucket
+// above kTile always forms an item of its own.  Reads counts from
+// bstart[b + 1] - bstart[b]; writes item start buckets and the sentinel.
+__device__ int split_buckets(const uint32_t *bstart, uint16_t *items) {
     int n = 0, start = 0;
     uint32_t accum = 0;
-    for (int b = 0; b < kBins; ++b) {
-        const uint32_t h = hist[b];
+    for (int b = 0; b < kBuckets; ++b) {
+        const uint32_t h = bstart[b + 1] - bstart[b];
         if (h > static_cast<uint32_t>(kTile)) {
             if (b > start) items[n++] = static_cast<uint16_t>(start);
             items[n++] = static_cast<uint16_t>(b);
@@ -680,8 +724,8 @@ __device__ int split_bins(const uint32_t *hist, uint16_t *items) {
         }
         accum += h;
     }
-    if (start < kBins) items[n++] = static_cast<uint16_t>(start);
-    items[n] = kBins;
+    if (start < kBuckets) items[n++] = static_cast<uint16_t>(start);
+    items[n] = static_cast<uint16_t>(kBuckets);
     return n;
 }
 
@@ -696,58 +740,113 @@ __global__ void __launch_bounds__(kRThreads, 1) row_reduce_kernel(ReduceArgs a) 
         return;
     }
     const int64_t obase = a.slot_base[ea];
+    if (a.slot_base[eb] > a.capacity) {  // the row's slots lie past the buffers: skip it
+        if (threadIdx.x == 0) {
+            a.out_count[r] = 0;
+            a.out_sum[r] = 0.0f;
+            if (a.status) atomicOr(a.status, FL_STATUS_SLOT_OVERFLOW);
+        }
+        return;
+    }
     int64_t F = 0;
     for (int64_t e = ea + threadIdx.x; e < eb; e += kRThreads) F += a.entry_count[e];
     F = block_sum(F, sm.scan_scratch);
     int64_t written = 0;
     float rsum = 0.0f;
     if (F <= kTile) {
-        rsum = process_sorted_range(a, sm, ea, eb, 0, a.E, obase, &written);
+        // The whole row fits one tile: load, sort by destination, emit.
+        const int64_t n = stream_row(a, sm, ea, eb, 0, a.E, [&](uint32_t slot, int32_t dst, int64_t pos) {
+            sm.key[0][pos] = static_cast<uint32_t>(dst);
+            sm.idx[0][pos] = static_cast<uint16_t>(pos);
+            sm.val[pos] = __float_as_uint(a.fact_val[slot]);
+            sm.slot[pos] = slot;
+        });
+        __syncthreads();
+        if (n > 0) rsum = emit_sorted(a, sm, static_cast<int>(n), bits_for(a.E), 0, obase, &written);
     } else {
+        // Pass A: destination histogram over kBuckets buckets.
         const int b1 = bits_for(a.E);
-        const int sh1 = b1 > 10 ? b1 - 10 : 0;
-        for (int b = threadIdx.x; b < kBins; b += kRThreads) sm.lvl1[b] = 0;
+        const int shift = b1 > kBucketBits ? b1 - kBucketBits : 0;
+        for (int b = threadIdx.x; b <= kBuckets; b += kRThreads) sm.bstart[b] = 0;
         __syncthreads();
-        stream_row(a, sm, ea, eb, 0, a.E, [&](uint32_t, int32_t dst, int64_t) { atomicAdd(&sm.lvl1[dst >> sh1], 1u); });
+        stream_row(a, sm, ea, eb, 0, a.E,
+                   [&](uint32_t, int32_t dst, int64_t) { atomicAdd(&sm.bstart[(dst >> shift) + 1], 1u); });
         __syncthreads();
-        if (threadIdx.x == 0) sm.n_items1 = split_bins(sm.lvl1, sm.items1);
+        {  // inclusive scan of bstart[1..kBuckets] -> bucket starts (4 per thread)
+            uint32_t v[4];
+            uint32_t sum = 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) { v[k] = sm.bstart[1 + threadIdx.x * 4 + k]; sum += v[k]; }
+            int64_t tot;
+            int64_t ex = block_exclusive_scan<int64_t>(sum, sm.scan_scratch, &tot);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) { ex += v[k]; sm.bstart[1 + threadIdx.x * 4 + k] = static_cast<uint32_t>(ex); }
+        }
         __syncthreads();
-        const int n1 = sm.n_items1;
-        for (int it = 0; it < n1; ++it) {
-            const int bl = sm.items1[it], bh = sm.items1[it + 1];
-            uint32_t cnt = 0;
-            for (int b = bl; b < bh; ++b) cnt += sm.lvl1[b];
-            const int64_t lo = static_cast<int64_t>(bl) << sh1;
-            int64_t hi = static_cast<int64_t>(bh) << sh1;
+        for (int b = threadIdx.x; b < kBuckets; b += kRThreads) sm.bcursor[b] = sm.bstart[b];
+        __syncthreads();
+        // Pass B: stable scatter of (dst, slot) into the buckets' runs.
+        uint32_t *runstart = &sm.shist[0][0];  // kBuckets entries while partitioning
+        auto flush = [&](int n) {
+            if (n == 0) return;
+            const int cur = tile_sort(sm, n, kBucketBits);
+            for (int j = threadIdx.x; j < n; j += kRThreads)
+                if (j == 0 || sm.key[cur][j] != sm.key[cur][j - 1]) runstart[sm.key[cur][j]] = static_cast<uint32_t>(j);
+            __syncthreads();
+            for (int j = threadIdx.x; j < n; j += kRThreads) {
+                const uint32_t b = sm.key[cur][j];
+                const uint16_t src = sm.idx[cur][j];
+                const uint32_t pos = sm.bcursor[b] + (static_cast<uint32_t>(j) - runstart[b]);
+                a.part[obase + pos] = make_uint2(sm.val[src], sm.slot[src]);
+            }
+            __syncthreads();
+            for (int j = threadIdx.x; j < n; j += kRThreads) {
+                const uint32_t b = sm.key[cur][j];
+                if (j + 1 == n || sm.key[cur][j + 1] != b) sm.bcursor[b] += static_cast<uint32_t>(j + 1) - runstart[b];
+            }
+            __syncthreads();
+        };
+        const int64_t residual = stream_row(
+            a, sm, ea, eb, 0, a.E,
+            [&](uint32_t slot, int32_t dst, int64_t pos) {
+                sm.key[0][pos] = static_cast<uint32_t>(dst) >> shift;
+                sm.idx[0][pos] = static_cast<uint16_t>(pos);
+                sm.val[pos] = static_cast<uint32_t>(dst);
+                sm.slot[pos] = slot;
+            },
+            [&](int64_t visited) -> int64_t {
+                if (visited + kLoadStep > kTile) { flush(static_cast<int>(visited)); return 0; }
+                return visited;
+            });
+        flush(static_cast<int>(residual));
+        // Pass C: items of consecutive buckets, each loaded contiguously.
+        if (threadIdx.x == 0) sm.n_items = split_buckets(sm.bstart, sm.items);
+        __syncthreads();
+        const int nit = sm.n_items;
+        const uint2 *part = a.part + obase;
+        for (int it = 0; it < nit; ++it) {
+            const int bl = sm.items[it], bh = sm.items[it + 1];
+            const int64_t p0 = sm.bstart[bl], p1 = sm.bstart[bh];
+            if (p1 == p0) continue;
+            const int64_t lo = static_cast<int64_t>(bl) << shift;
+            int64_t hi = static_cast<int64_t>(bh) << shift;
             if (hi > a.E) hi = a.E;
-            if (cnt == 0 || lo >= hi) continue;
-            if (cnt <= static_cast<uint32_t>(kTile)) {
-                rsum += process_sorted_range(a, sm, ea, eb, lo, hi, obase, &written);
-            } else if (hi - lo <= kDenseW) {
-                rsum += process_dense_range(a, sm, ea, eb, lo, hi, obase, &written);
+            if (p1 - p0 <= kTile) {
+                const int n = static_cast<int>(p1 - p0);
+                for (int k = threadIdx.x; k < n; k += kRThreads) {
+                    const uint2 v = part[p0 + k];
+                    sm.key[0][k] = v.x - static_cast<uint32_t>(lo);
+                    sm.idx[0][k] = static_cast<uint16_t>(k);
+                    sm.val[k] = __float_as_uint(a.fact_val[v.y]);
+                    sm.slot[k] = v.y;
+                }
+                __syncthreads();
+                rsum += emit_sorted(a, sm, n, bits_for(hi - lo), lo, obase, &written);
             } else {
-                const int b2 = bits_for(hi - lo);
-                const int sh2 = b2 > 10 ? b2 - 10 : 0;
-                for (int b = threadIdx.x; b < kBins; b += kRThreads) sm.lvl2[b] = 0;
-                __syncthreads();
-                stream_row(a, sm, ea, eb, lo, hi,
-                           [&](uint32_t, int32_t dst, int64_t) { atomicAdd(&sm.lvl2[(dst - lo) >> sh2], 1u); });
-                __syncthreads();
-                if (threadIdx.x == 0) sm.n_items2 = split_bins(sm.lvl2, sm.items2);
-                __syncthreads();
-                const int n2 = sm.n_items2;
-                for (int it2 = 0; it2 < n2; ++it2) {
-                    const int cl = sm.items2[it2], ch = sm.items2[it2 + 1];
-                    uint32_t c2 = 0;
-                    for (int b = cl; b < ch; ++b) c2 += sm.lvl2[b];
-                    const int64_t lo2 = lo + (static_cast<int64_t>(cl) << sh2);
-                    int64_t hi2 = lo + (static_cast<int64_t>(ch) << sh2);
-                    if (hi2 > hi) hi2 = hi;
-                    if (c2 == 0 || lo2 >= hi2) continue;
-                    if (c2 <= static_cast<uint32_t>(kTile))
-                        rsum += process_sorted_range(a, sm, ea, eb, lo2, hi2, obase, &written);
-                    else
-                        rsum += process_dense_range(a, sm, ea, eb, lo2, hi2, obase, &written);
+                // One bucket with more facts than a tile: dense windows over it.
+                for (int64_t wlo = lo; wlo < hi; wlo += kDenseW) {
+                    const int64_t whi = (wlo + kDenseW) < hi ? (wlo + kDenseW) : hi;
+                    rsum += dense_window(a, sm, part, p0, p1, wlo, whi, obase, &written);
                 }
             }
         }
@@ -872,9 +971,10 @@ __global__ void __launch_bounds__(kBThreads) hop_backward_kernel(BackwardArgs a)
         a.grad_w[r * a.n + c] = fixed_to_float(acc[2 * c], acc[2 * c + 1], scale);
 }
 
-__global__ void scatter_grad_kernel(const float *grad_sel, const int64_t *src, int64_t n, float *grad_full) {
+__global__ void scatter_grad_kernel(const float *grad_sel, const int64_t *src, int64_t n, const int64_t *n_live,
+                                    float *grad_full) {
     int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-    if (i < n) grad_full[src[i]] = grad_sel[i];
+    if (i < n && (n_live == nullptr || i < *n_live)) grad_full[src[i]] = grad_sel[i];
 }
 
 // ---------------------------------------------------------------------------
@@ -942,7 +1042,7 @@ size_t hop_workspace(int64_t rows, int64_t S) {
 }
 
 size_t hop_output_tmp_bytes(int64_t total_slots) {
-    return carve_bytes<int32_t>(total_slots) + carve_bytes<float>(total_slots);
+    return carve_bytes<int32_t>(total_slots) + carve_bytes<float>(total_slots) + carve_bytes<uint2>(total_slots);
 }
 
 int hop_plan(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *ent, int64_t S, const fl_csr_side &ori,
@@ -955,13 +1055,15 @@ int hop_plan(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *ent,
     FL_REQUIRE(cap && scan_ws, "hop workspace too small");
     (void)row_ptr;
     if (S > 0) {
-        launch(hop_capacity_kernel, static_cast<unsigned>((S + 255) / 256), 256, 0, st, 
-            ent, S, make_side(ori, nullptr), make_side(inv, nullptr), p->topk_edges, (p->flags & FL_WOT_I) ? 1 : 0, cap);
+        launch(hop_capacity_kernel, static_cast<unsigned>((S + 255) / 256), 256, 0, st, ent, row_ptr, p->rows, S,
+               make_side(ori, nullptr), make_side(inv, nullptr), p->topk_edges, (p->flags & FL_WOT_I) ? 1 : 0, cap);
     }
     int rc = exclusive_scan<int64_t>(cap, S, slot_base, scan_ws, sws, st);
     if (rc) return rc;
-    FL_CUDA(cudaMemcpyAsync(total_slots, slot_base + S, sizeof(int64_t), cudaMemcpyDeviceToHost, st));
-    FL_CUDA(cudaStreamSynchronize(st));
+    if (total_slots) {
+        FL_CUDA(cudaMemcpyAsync(total_slots, slot_base + S, sizeof(int64_t), cudaMemcpyDeviceToHost, st));
+        FL_CUDA(cudaStreamSynchronize(st));
+    }
     return check_launch("hop_plan");
 }
 
@@ -973,6 +1075,7 @@ int hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *en
     if (S == 0) return FL_OK;
     ExpandArgs a;
     a.row_ptr = row_ptr; a.ent = ent; a.val = val; a.S = S; a.rows = p->rows; a.n = p->n; a.r_size = p->r_size;
+    a.capacity = p->slot_capacity; a.status = p->status;
     a.topk = p->topk_edges; a.flags = p->flags; a.seed = p->sampling_seed; a.L = p->L; a.w = w;
     a.ori = make_side(ori, mask_csr_ori); a.inv = make_side(inv, mask_csr_inv);
     a.mask_triple = mask_triple; a.edge_weight = edge_weight; a.slot_base = slot_base;
@@ -981,13 +1084,16 @@ int hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *en
     int sms = fl_device_sm_count();
     int64_t cap_blocks = static_cast<int64_t>(sms > 0 ? sms : 148) * 32;
     if (blocks > cap_blocks) blocks = cap_blocks;
-    launch(hop_expand_kernel, static_cast<unsigned>(blocks), kExpandWarps * 32, 0, st, a);
+    if (p->flags & FL_SAMPLED)
+        launch(hop_expand_kernel<true>, static_cast<unsigned>(blocks), kExpandWarps * 32, 0, st, a);
+    else
+        launch(hop_expand_kernel<false>, static_cast<unsigned>(blocks), kExpandWarps * 32, 0, st, a);
     return check_launch("hop_expand");
 }
 
 int row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *slot_base, const int32_t *entry_count,
                const int32_t *fact_dst, const float *fact_val, int64_t total_slots, int32_t *fact_pos, float eps,
-               int64_t *out_row_ptr, int32_t *out_ent, float *out_x, float *out_y, float *out_denom,
+               int64_t *out_row_ptr, int32_t *out_ent, float *out_x, float *out_y, float *out_denom, int32_t *status,
                void *ws, size_t ws_bytes, cudaStream_t st) {
     FL_REQUIRE(total_slots < (int64_t(1) << 32), "too many facts in one hop (%lld)", static_cast<long long>(total_slots));
     FL_REQUIRE(E < (int64_t(1) << 31), "entity count exceeds int32");
@@ -998,12 +1104,14 @@ int row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *s
     void *scan_ws = c.take<char>(sws);
     int32_t *tmp_ent = c.take<int32_t>(total_slots > 0 ? total_slots : 1);
     float *tmp_x = c.take<float>(total_slots > 0 ? total_slots : 1);
-    FL_REQUIRE(out_count && out_sum && scan_ws && tmp_ent && tmp_x, "row_reduce workspace too small");
+    uint2 *part = c.take<uint2>(total_slots > 0 ? total_slots : 1);
+    FL_REQUIRE(out_count && out_sum && scan_ws && tmp_ent && tmp_x && part, "row_reduce workspace too small");
     if (rows > 0) {
         ReduceArgs a;
         a.row_ptr = row_ptr; a.rows = rows; a.slot_base = slot_base; a.entry_count = entry_count;
         a.fact_dst = fact_dst; a.fact_val = fact_val; a.E = E; a.fact_pos = fact_pos;
-        a.tmp_ent = tmp_ent; a.tmp_x = tmp_x; a.out_count = out_count; a.out_sum = out_sum;
+        a.tmp_ent = tmp_ent; a.tmp_x = tmp_x; a.part = part; a.out_count = out_count; a.out_sum = out_sum;
+        a.capacity = total_slots; a.status = status;
         const size_t smem = sizeof(ReduceSmem);
         static bool attr_set = false;
         if (!attr_set) {
@@ -1075,11 +1183,12 @@ int normalize_backward(const int64_t *row_ptr, const float *x, const float *deno
     return check_launch("normalize_backward");
 }
 
-int scatter_grad(const float *grad_sel, const int64_t *src, int64_t n_sel, float *grad_full, int64_t n_full,
-                 cudaStream_t st) {
+int scatter_grad(const float *grad_sel, const int64_t *src, int64_t n_sel, const int64_t *n_live, float *grad_full,
+                 int64_t n_full, cudaStream_t st) {
     FL_CUDA(cudaMemsetAsync(grad_full, 0, static_cast<size_t>(n_full) * sizeof(float), st));
     if (n_sel > 0)
-        launch(scatter_grad_kernel, static_cast<unsigned>((n_sel + 255) / 256), 256, 0, st, grad_sel, src, n_sel, grad_full);
+        launch(scatter_grad_kernel, static_cast<unsigned>((n_sel + 255) / 256), 256, 0, st, grad_sel, src, n_sel, n_live,
+               grad_full);
     return check_launch("scatter_grad");
 }
 

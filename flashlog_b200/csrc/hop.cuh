@@ -18,7 +18,7 @@ int hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *en
                int32_t *entry_count, cudaStream_t st);
 int row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *slot_base, const int32_t *entry_count,
                const int32_t *fact_dst, const float *fact_val, int64_t total_slots, int32_t *fact_pos, float eps,
-               int64_t *out_row_ptr, int32_t *out_ent, float *out_x, float *out_y, float *out_denom,
+               int64_t *out_row_ptr, int32_t *out_ent, float *out_x, float *out_y, float *out_denom, int32_t *status,
                void *ws, size_t ws_bytes, cudaStream_t st);
 int hop_backward(const fl_hop_params *p, const int64_t *row_ptr, const float *val, int64_t S, const float *w,
                  const int64_t *slot_base, const int32_t *entry_count, const int32_t *fact_pos, const int16_t *fact_rel,
@@ -28,11 +28,11 @@ int normalize_forward(const int64_t *row_ptr, const float *x, int64_t rows, floa
                       cudaStream_t st);
 int normalize_backward(const int64_t *row_ptr, const float *x, const float *denom, const float *g, int64_t rows,
                        float eps, float *gx, cudaStream_t st);
-int scatter_grad(const float *grad_sel, const int64_t *src, int64_t n_sel, float *grad_full, int64_t n_full,
-                 cudaStream_t st);
+int scatter_grad(const float *grad_sel, const int64_t *src, int64_t n_sel, const int64_t *n_live, float *grad_full,
+                 int64_t n_full, cudaStream_t st);
 int topc_select(const int64_t *row_ptr, const int32_t *ent, const float *val, int64_t rows, int64_t S, int64_t c1,
                 const double *noise, int64_t *out_row_ptr, int32_t *out_ent, float *out_val, int64_t *out_src,
-                void *ws, size_t ws_bytes, cudaStream_t st);
+                int64_t out_capacity, int32_t *status, void *ws, size_t ws_bytes, cudaStream_t st);
 int topc_candidates(const int64_t *row_ptr, const float *val, int64_t rows, int64_t S, int64_t c1,
                     int64_t *n_candidates, void *ws, size_t ws_bytes, cudaStream_t st);
 }  // namespace fl

@@ -54,7 +54,7 @@ struct KeyOf<true> {
 template <bool kSampled>
 __global__ void __launch_bounds__(kSelThreads) topc_select_kernel(
     const int64_t *row_ptr, const int32_t *ent, const float *val, int64_t rows, int64_t c1,
-    const double *noise, const int64_t *cand_off, const int64_t *out_row_ptr,
+    const double *noise, const int64_t *cand_off, const int64_t *out_row_ptr, const int64_t *kept_count,
     uint64_t *key_scratch, int32_t *out_ent, float *out_val, int64_t *out_src) {
     using Key = typename KeyOf<kSampled>::T;
     __shared__ unsigned int hist[256];
@@ -65,9 +65,10 @@ __global__ void __launch_bounds__(kSelThreads) topc_select_kernel(
     if (r >= rows) return;
     const int64_t a = row_ptr[r], b = row_ptr[r + 1];
     const int64_t out0 = out_row_ptr[r];
-    const int64_t kept = out_row_ptr[r + 1] - out0;
+    const int64_t out_end = out_row_ptr[r + 1];  // clamped to the output capacity
+    const int64_t kept = kept_count[r];
     if (kept == b - a) {  // row kept whole (also covers empty rows)
-        for (int64_t i = a + threadIdx.x; i < b; i += blockDim.x) {
+        for (int64_t i = a + threadIdx.x; i < b && out0 + (i - a) < out_end; i += blockDim.x) {
             out_ent[out0 + (i - a)] = ent[i];
             out_val[out0 + (i - a)] = val[i];
             out_src[out0 + (i - a)] = i;
@@ -132,7 +133,7 @@ __global__ void __launch_bounds__(kSelThreads) topc_select_kernel(
         bool keep = nz && (k > thr || (tie && tie_carry + tex < take_ties));
         int64_t ktot;
         int64_t kex = block_exclusive_scan<int64_t>(keep ? 1 : 0, scan_scratch, &ktot);
-        if (keep) {
+        if (keep && out0 + out_carry + kex < out_end) {
             int64_t o = out0 + out_carry + kex;
             out_ent[o] = ent[i];
             out_val[o] = val[i];
@@ -140,6 +141,17 @@ __global__ void __launch_bounds__(kSelThreads) topc_select_kernel(
         }
         tie_carry += ttot;
         out_carry += ktot;
+    }
+}
+
+// Clamp the output row offsets to the buffers' capacity (rows past it become
+// empty or truncated) and flag the overflow.
+__global__ void clamp_rows_kernel(int64_t *row_ptr, int64_t rows, int64_t cap, int32_t *status) {
+    int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (r > rows) return;
+    if (row_ptr[r] > cap) {
+        row_ptr[r] = cap;
+        if (status && r == rows) atomicOr(status, FL_STATUS_SLOT_OVERFLOW);
     }
 }
 
@@ -151,8 +163,9 @@ size_t topc_workspace(int64_t rows, int64_t S) {
 }
 
 int topc_counts(const int64_t *row_ptr, const float *val, int64_t rows, int64_t c1, int64_t *out_row_ptr,
-                int64_t *cand_off, Carve &c, cudaStream_t st) {
+                int64_t *cand_off, int64_t **kept_out, Carve &c, cudaStream_t st) {
     int64_t *kept = c.take<int64_t>(rows + 1);
+    *kept_out = kept;
     int64_t *cand = c.take<int64_t>(rows + 1);
     size_t sws = scan_workspace(rows);
     void *scan_ws = c.take<char>(sws);
@@ -167,21 +180,24 @@ int topc_counts(const int64_t *row_ptr, const float *val, int64_t rows, int64_t 
 
 int topc_select(const int64_t *row_ptr, const int32_t *ent, const float *val, int64_t rows, int64_t S,
                 int64_t c1, const double *noise, int64_t *out_row_ptr, int32_t *out_ent, float *out_val,
-                int64_t *out_src, void *ws, size_t ws_bytes, cudaStream_t st) {
+                int64_t *out_src, int64_t out_capacity, int32_t *status, void *ws, size_t ws_bytes, cudaStream_t st) {
     FL_REQUIRE(c1 >= 0, "topk_nodes/c must be nonnegative");
     Carve c(ws, ws_bytes);
     int64_t *cand_off = c.take<int64_t>(rows + 1);
-    uint64_t *keys = c.take<uint64_t>(S > 0 ? S : 1);
+    uint64_t *keys = c.take<uint64_t>(noise ? (S > 0 ? S : 1) : 1);
     FL_REQUIRE(cand_off && keys, "topc workspace too small");
-    int rc = topc_counts(row_ptr, val, rows, c1, out_row_ptr, cand_off, c, st);
+    int64_t *kept = nullptr;
+    int rc = topc_counts(row_ptr, val, rows, c1, out_row_ptr, cand_off, &kept, c, st);
     if (rc) return rc;
     if (rows == 0) return FL_OK;
+    const int64_t cap = out_capacity > 0 ? out_capacity : S;
+    launch(clamp_rows_kernel, static_cast<unsigned>((rows + 1 + 255) / 256), 256, 0, st, out_row_ptr, rows, cap, status);
     if (noise)
         launch(topc_select_kernel<true>, static_cast<unsigned>(rows), kSelThreads, 0, st, 
-            row_ptr, ent, val, rows, c1, noise, cand_off, out_row_ptr, keys, out_ent, out_val, out_src);
+            row_ptr, ent, val, rows, c1, noise, cand_off, out_row_ptr, kept, keys, out_ent, out_val, out_src);
     else
         launch(topc_select_kernel<false>, static_cast<unsigned>(rows), kSelThreads, 0, st, 
-            row_ptr, ent, val, rows, c1, nullptr, cand_off, out_row_ptr, keys, out_ent, out_val, out_src);
+            row_ptr, ent, val, rows, c1, nullptr, cand_off, out_row_ptr, kept, keys, out_ent, out_val, out_src);
     return check_launch("topc_select");
 }
 
@@ -191,7 +207,8 @@ int topc_candidates(const int64_t *row_ptr, const float *val, int64_t rows, int6
     int64_t *cand_off = c.take<int64_t>(rows + 1);
     int64_t *kept_ptr = c.take<int64_t>(rows + 1);
     FL_REQUIRE(cand_off && kept_ptr, "topc workspace too small");
-    int rc = topc_counts(row_ptr, val, rows, c1, kept_ptr, cand_off, c, st);
+    int64_t *kept = nullptr;
+    int rc = topc_counts(row_ptr, val, rows, c1, kept_ptr, cand_off, &kept, c, st);
     if (rc) return rc;
     FL_CUDA(cudaMemcpyAsync(n_candidates, cand_off + rows, sizeof(int64_t), cudaMemcpyDeviceToHost, st));
     FL_CUDA(cudaStreamSynchronize(st));

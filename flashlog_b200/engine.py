@@ -3,9 +3,15 @@
 This is the hot path of one sparse DRUM training step
 (src/model_DRUM_kernel_sp.py:92-204 with the deterministic c1/c2 budgets):
 for t in range(T): w_t = softmax(w_all[:, t] / tau_1); state = normalize(hop(state, w_t));
-then the channel readout and log loss of src/utils.py:36-47.  Each hop is
-one autograd node whose forward and backward run in the library's kernels;
-the state never goes through the COO round trip of the operator API.
+then the channel readout and log loss of src/utils.py:36-47.  Each hop is one
+autograd node whose forward and backward run in the library's kernels; the
+state never goes through the COO round trip of the operator API.
+
+Host synchronization: one per hop (the planned fact count sizes the fact
+buffers).  Selected entries and outputs keep capacity-sized buffers whose live
+counts stay on the device (row_ptr[-1]); work that would not fit those
+capacities is skipped and flagged in a sticky device status word, which
+`check_status` reads once after the step (or after many steps).
 """
 from __future__ import annotations
 
@@ -24,19 +30,22 @@ class HopNorm(torch.autograd.Function):
     """
 
     @staticmethod
-    def forward(ctx, val, w, row_ptr, ent, graph, r_size, topk_edges, c1, flags, mask_triple, eps, stats):
+    def forward(ctx, val, w, row_ptr, ent, graph, r_size, topk_edges, c1, flags, mask_triple, eps, stats, status):
         v = val.detach().contiguous()
+        rows = row_ptr.numel() - 1
         ctx.pruned = None
         ctx.n_in = v.numel()
-        if c1 is not None and c1 >= 0 and v.numel() > c1:
-            rp, en, vv, src = ops.topc_select(row_ptr, ent, v, int(c1))
-            if src.numel() != v.numel():
-                row_ptr, ent, v, ctx.pruned = rp, en, vv, src
+        ctx.sel_live = None
+        if c1 is not None and c1 >= 0:
+            cap = min(v.numel(), rows * int(c1))  # explicit zeros could exceed it: flagged in `status`
+            rp, en, vv, src = ops.topc_select(row_ptr, ent, v, int(c1), sync=False, out_capacity=cap, status=status)
+            row_ptr, ent, v, ctx.pruned = rp, en, vv, src
+            ctx.sel_live = rp[rows:]
         wf = w.detach().contiguous()
         fw = ops.hop_forward(row_ptr, ent, v, wf, graph, r_size, topk_edges, flags, mask_triple=mask_triple, eps=eps,
-                             timing=None if stats is None else stats.timer)
+                             timing=None if stats is None else stats.timer, status=status, out_sync=False)
         if stats is not None:
-            stats.append((ent, fw.entry_count[:ent.numel()], fw.out_ent.numel()))
+            stats.append((ent, row_ptr[rows:], fw.entry_count, fw.out_row_ptr[rows:]))
         ctx.fw = fw
         ctx.save_for_backward(row_ptr, v, wf)
         ctx.mark_non_differentiable(fw.out_row_ptr, fw.out_ent)
@@ -47,8 +56,24 @@ class HopNorm(torch.autograd.Function):
         row_ptr, v, wf = ctx.saved_tensors
         grad_v, grad_w = ops.hop_backward(ctx.fw, row_ptr, v, wf, g_y, normalize=True)
         if ctx.pruned is not None:
-            grad_v = ops.scatter_grad(grad_v, ctx.pruned, ctx.n_in)
-        return grad_v, grad_w, None, None, None, None, None, None, None, None, None, None
+            grad_v = ops.scatter_grad(grad_v, ctx.pruned, ctx.n_in, n_live=ctx.sel_live)
+        return grad_v, grad_w, None, None, None, None, None, None, None, None, None, None, None
+
+
+class Readout(torch.autograd.Function):
+    """Channel-summed score of each query's target entity."""
+
+    @staticmethod
+    def forward(ctx, val, row_ptr, ent, targets, N):
+        ctx.save_for_backward(row_ptr, ent, targets)
+        ctx.N = N
+        ctx.n_val = val.numel()
+        return ops.readout(row_ptr, ent, val.detach(), N, targets)
+
+    @staticmethod
+    def backward(ctx, g):
+        row_ptr, ent, targets = ctx.saved_tensors
+        return ops.readout_backward(row_ptr, ent, ctx.N, targets, g, ctx.n_val), None, None, None, None
 
 
 def initial_state(heads: torch.Tensor, N: int):
@@ -63,25 +88,40 @@ def initial_state(heads: torch.Tensor, N: int):
 
 def readout_loss(row_ptr, ent, val, tails, N: int, tau_2: float = 1.0, thr: float = 1e-7):
     """log_loss_common_sp of the channel-summed scores (src/utils.py:36-47)."""
-    Q = tails.numel()
-    rows = row_ptr.numel() - 1
-    counts = row_ptr[1:] - row_ptr[:-1]
-    row_of = torch.repeat_interleave(torch.arange(rows, device=val.device), counts, output_size=ent.numel())
-    q = row_of // N
-    hit = ent.to(torch.int64) == tails[q]
-    score = torch.zeros(Q, dtype=val.dtype, device=val.device).index_add(0, q[hit], val[hit])
+    score = Readout.apply(val, row_ptr, ent, tails, N)
     return -torch.mean(torch.log(torch.maximum(score / tau_2, torch.full_like(score, thr))))
 
 
+def new_status(device):
+    """Sticky device status word for the hop kernels (FL_STATUS_* bits)."""
+    return torch.zeros(1, dtype=torch.int32, device=device)
+
+
+def check_status(status):
+    """Raise if any hop ran out of its buffers (one host sync)."""
+    v = int(status.item())
+    if v & L.FL_STATUS_SLOT_OVERFLOW:
+        raise RuntimeError("a hop exceeded its entry or fact capacity; results of this step are invalid")
+
+
 def drum_propagate(heads, w_all, graph: Graph, r_size: int, *, c1=None, c2=0, mask_triple=None, tau_1=1.0,
-                   eps=1e-7, stats=None):
-    """T hops of the sparse DRUM operator; w_all is [Q, T, N, n] logits."""
+                   eps=1e-7, stats=None, status=None):
+    """T hops of the sparse DRUM operator; w_all is [Q, T, N, n] logits.
+
+    Returns the final state (row_ptr, ent, val) with capacity-sized ent/val
+    (live count row_ptr[-1]).
+    """
     Q, T, N, n = w_all.shape
     row_ptr, ent, val = initial_state(heads, N)
     topk = c2 // 2 if c2 and c2 > 0 else L.NO_BUDGET
     flags = L.FL_SKIP_NONPOS_W | L.FL_DROP_MASKED
+    own_status = status is None
+    if own_status:
+        status = new_status(heads.device)
     for t in range(T):
         w_t = torch.softmax(w_all[:, t] / tau_1, dim=-1)
         val, row_ptr, ent = HopNorm.apply(val, w_t, row_ptr, ent, graph, r_size, topk, c1, flags, mask_triple, eps,
-                                          stats)
+                                          stats, status)
+    if own_status:
+        check_status(status)
     return row_ptr, ent, val

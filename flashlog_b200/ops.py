@@ -62,6 +62,23 @@ class Graph:
         self.ori = L.fl_csr_side(_p(c[0]), _p(c[1]), _p(c[3]), _p(c[8]), _p(c[10]), _p(c[11]), _p(c[9]))
         self.inv = L.fl_csr_side(_p(c[4]), _p(c[5]), _p(c[7]), _p(c[12]), _p(c[14]), _p(c[15]), _p(c[13]))
         self.device = c[0].device
+        self._max_degree = None
+
+    def max_degree(self):
+        """(max out-degree, max in-degree) over entities (one host sync, cached)."""
+        if self._max_degree is None:
+            def side_max(gp, gs, gc):
+                if gs.numel() == 0:
+                    return 0
+                g0, g1 = gp[:-1].long(), gp[1:].long()
+                has = g1 > g0
+                last = (g1 - 1).clamp(min=0)
+                deg = torch.where(has, gs[last].long() + gc[last].long() - gs[g0.clamp(max=gs.numel() - 1)].long(),
+                                  torch.zeros_like(g0))
+                return int(deg.max().item())
+            c = self.csr
+            self._max_degree = (side_max(c[8], c[10], c[11]), side_max(c[12], c[14], c[15]))
+        return self._max_degree
 
     @classmethod
     def of(cls, csr):
@@ -138,21 +155,29 @@ def topc_candidates(row_ptr, val, c1: int) -> int:
     return n.value
 
 
-def topc_select(row_ptr, ent, val, c1: int, noise=None):
-    """c1 selection; returns (row_ptr, ent, val, src_index) of the kept entries."""
+def topc_select(row_ptr, ent, val, c1: int, noise=None, sync: bool = True, out_capacity: int = 0, status=None):
+    """c1 selection; returns (row_ptr, ent, val, src_index) of the kept entries.
+
+    With sync=False the outputs keep the input's capacity and the live count
+    is only on the device (row_ptr[-1]); no host synchronization happens.
+    """
     _require_cuda(row_ptr, ent, val)
     rows = row_ptr.numel() - 1
     S = val.numel()
     dev = val.device
+    cap = int(out_capacity) if out_capacity else S
     out_row_ptr = torch.empty(rows + 1, dtype=torch.int64, device=dev)
-    out_ent = torch.empty(S, dtype=torch.int32, device=dev)
-    out_val = torch.empty(S, dtype=torch.float32, device=dev)
-    out_src = torch.empty(S, dtype=torch.int64, device=dev)
+    out_ent = torch.empty(max(cap, 1), dtype=torch.int32, device=dev)
+    out_val = torch.empty(max(cap, 1), dtype=torch.float32, device=dev)
+    out_src = torch.empty(max(cap, 1), dtype=torch.int64, device=dev)
     ws = _ws(lib().fl_topc_workspace(rows, S), dev)
     if noise is not None:
         noise = noise.to(torch.float64).contiguous()
     check(lib().fl_topc_select(_p(row_ptr), _p(ent), _p(val), rows, S, int(c1), _p(noise), _p(out_row_ptr),
-                               _p(out_ent), _p(out_val), _p(out_src), _p(ws), ws.numel(), _stream()), "topc_select")
+                               _p(out_ent), _p(out_val), _p(out_src), cap, _p(status), _p(ws), ws.numel(),
+                               _stream()), "topc_select")
+    if not sync:
+        return out_row_ptr, out_ent[:cap], out_val[:cap], out_src[:cap]
     k = int(out_row_ptr[-1].item())
     return out_row_ptr, out_ent[:k], out_val[:k], out_src[:k]
 
@@ -178,15 +203,25 @@ class HopForward:
     fact_val: torch.Tensor | None = None
 
 
-def hop_params(rows, Lch, n, r_size, E, topk_edges, flags, seed=-1, eps=EPS):
+def hop_params(rows, Lch, n, r_size, E, topk_edges, flags, seed=-1, eps=EPS, slot_capacity=0, status=None):
     return L.fl_hop_params(rows, Lch, n, r_size, E, int(min(topk_edges, L.NO_BUDGET)), int(flags), int(seed),
-                           float(eps))
+                           float(eps), int(slot_capacity), None if status is None else status.data_ptr())
 
 
 def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int, flags: int, *,
                 mask_triple=None, mask_csr=None, edge_weight=None, seed: int = -1, eps: float = EPS,
-                keep_facts: bool = False, record: bool = True, timing=None) -> HopForward:
-    """Expansion + per-row coalesce-sum + normalization of one hop."""
+                keep_facts: bool = False, record: bool = True, timing=None, slot_capacity=None,
+                status=None, out_sync: bool = True) -> HopForward:
+    """Expansion + per-row coalesce-sum + normalization of one hop.
+
+    slot_capacity=None sizes the fact buffers exactly (one host sync for the
+    fact count, one for the output count).  With an upper bound instead, no
+    host synchronization happens: outputs keep that capacity, their live
+    count is out_row_ptr[-1] on the device, and work that would not fit sets
+    FL_STATUS_SLOT_OVERFLOW in `status` (an int32 device tensor).  With
+    out_sync=False the fact count is still read (one sync) but the outputs keep
+    that capacity and their live count stays on the device.
+    """
     _require_cuda(row_ptr, ent, val, w)
     B, Lch, n = w.shape
     rows = B * Lch
@@ -197,13 +232,16 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
     if n != 2 * r_size + 1:
         raise ValueError(f"w must have 2 * r_size + 1 = {2 * r_size + 1} columns, got {n}")
     w = w.contiguous()
-    params = hop_params(rows, Lch, n, r_size, graph.E, topk_edges, flags, seed, eps)
+    sync = slot_capacity is None
     slot_base = torch.empty(S + 1, dtype=torch.int64, device=dev)
     ws = _ws(lib().fl_hop_workspace(rows, S), dev)
     total = ctypes.c_int64(0)
+    params = hop_params(rows, Lch, n, r_size, graph.E, topk_edges, flags, seed, eps, slot_capacity or 0, status)
     check(lib().fl_hop_plan(ctypes.byref(params), _p(row_ptr), _p(ent), S, graph.ori, graph.inv, _p(slot_base),
-                            ctypes.byref(total), _p(ws), ws.numel(), _stream()), "hop_plan")
-    T = max(total.value, 1)
+                            ctypes.byref(total) if sync else None, _p(ws), ws.numel(), _stream()), "hop_plan")
+    T = max(total.value, 1) if sync else max(int(slot_capacity), 1)
+    if not sync:
+        params.slot_capacity = T
     fact_dst = torch.empty(T, dtype=torch.int32, device=dev)
     fact_val = torch.empty(T, dtype=torch.float32, device=dev)
     fact_rel = torch.empty(T, dtype=torch.int16, device=dev)
@@ -243,10 +281,10 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
     ws2 = _ws(lib().fl_reduce_workspace(rows, T), dev)
     check(lib().fl_row_reduce(_p(row_ptr), rows, graph.E, _p(slot_base), _p(entry_count), _p(fact_dst), _p(fact_val),
                               T, _p(fact_pos), ctypes.c_float(eps), _p(out_row_ptr), _p(out_ent), _p(out_x), _p(out_y),
-                              _p(out_denom), _p(ws2), ws2.numel(), _stream()), "row_reduce")
+                              _p(out_denom), _p(status), _p(ws2), ws2.numel(), _stream()), "row_reduce")
     if timing is not None:
         timing.record_end()
-    u = int(out_row_ptr[rows].item())
+    u = int(out_row_ptr[rows].item()) if (sync and out_sync) else T
     return HopForward(params, slot_base, entry_count, fact_rel, fact_m, fact_pos, out_row_ptr, out_ent[:u],
                       out_x[:u], out_y[:u], out_denom[:rows], total.value,
                       fact_dst if keep_facts else None, fact_val if keep_facts else None)
@@ -260,7 +298,7 @@ def hop_backward(fw: HopForward, row_ptr, val, w, g_y, normalize: bool = True):
     dev = val.device
     params = L.fl_hop_params(fw.params.rows, fw.params.L, fw.params.n, fw.params.r_size, fw.params.E,
                              fw.params.topk_edges, fw.params.flags | (0 if normalize else L.FL_NO_NORMALIZE),
-                             fw.params.sampling_seed, fw.params.eps)
+                             fw.params.sampling_seed, fw.params.eps, fw.params.slot_capacity, fw.params.status)
     grad_val = torch.empty(max(S, 1), dtype=torch.float32, device=dev)
     grad_w = torch.empty((rows, n), dtype=torch.float32, device=dev)
     ws = _ws(lib().fl_hop_backward_workspace(rows, n), dev)
@@ -272,10 +310,11 @@ def hop_backward(fw: HopForward, row_ptr, val, w, g_y, normalize: bool = True):
     return grad_val[:S], grad_w.view(B, Lch, n)
 
 
-def scatter_grad(grad_sel, src_index, n_full: int):
+def scatter_grad(grad_sel, src_index, n_full: int, n_live=None):
+    """grad_full[src_index[j]] = grad_sel[j]; n_live (device int64) bounds j."""
     out = torch.empty(max(n_full, 1), dtype=torch.float32, device=grad_sel.device)
-    check(lib().fl_scatter_grad(_p(grad_sel.contiguous()), _p(src_index), src_index.numel(), _p(out), n_full,
-                                _stream()), "scatter_grad")
+    check(lib().fl_scatter_grad(_p(grad_sel.contiguous()), _p(src_index), src_index.numel(), _p(n_live), _p(out),
+                                n_full, _stream()), "scatter_grad")
     return out[:n_full]
 
 
@@ -334,7 +373,7 @@ def fixed_relation(b, l, e, v, ops_, graph: Graph, r_size: int, B: int, Lr: int)
     ws2 = _ws(lib().fl_reduce_workspace(rows, T), dev)
     check(lib().fl_row_reduce(_p(row_ptr), rows, graph.E, _p(slot_base), _p(entry_count), _p(fact_dst), _p(fact_val),
                               T, None, ctypes.c_float(EPS), _p(out_row_ptr), _p(out_ent), _p(out_x), None,
-                              _p(out_denom), _p(ws2), ws2.numel(), _stream()), "row_reduce")
+                              _p(out_denom), None, _p(ws2), ws2.numel(), _stream()), "row_reduce")
     u = int(out_row_ptr[rows].item())
     return out_row_ptr, out_ent[:u], out_x[:u]
 
@@ -355,3 +394,24 @@ def filtered_ranks(idx_b, idx_e, values, targets, filter_keys, B: int, E: int, u
                                   filter_keys.numel(), B, E, int(bool(use_eql)), _p(ranks), _p(ws), ws.numel(),
                                   _stream()), "filtered_ranks")
     return ranks[:B]
+
+
+# --------------------------------------------------------------------------
+# readout
+# --------------------------------------------------------------------------
+def readout(row_ptr, ent, val, N: int, targets):
+    """Channel-summed scores at each query's target (sum_sp_3d + target lookup)."""
+    Q = targets.numel()
+    scores = torch.empty(max(Q, 1), dtype=torch.float32, device=val.device)
+    check(lib().fl_readout(_p(row_ptr), _p(ent), _p(val.contiguous()), N, _p(targets.to(torch.int64).contiguous()), Q,
+                           _p(scores), _stream()), "readout")
+    return scores[:Q]
+
+
+def readout_backward(row_ptr, ent, N: int, targets, g_scores, n_val: int):
+    Q = targets.numel()
+    grad = torch.empty(max(n_val, 1), dtype=torch.float32, device=g_scores.device)
+    check(lib().fl_readout_backward(_p(row_ptr), _p(ent), N, _p(targets.to(torch.int64).contiguous()), Q,
+                                    _p(g_scores.to(torch.float32).contiguous()), _p(grad), n_val, _stream()),
+          "readout_backward")
+    return grad[:n_val]

@@ -63,7 +63,13 @@ typedef struct {
     int64_t flags;                  /* FL_* flags                                */
     int64_t sampling_seed;          /* FL_SAMPLED only                           */
     float eps;                      /* row normalization epsilon                 */
+    int64_t slot_capacity;          /* > 0: length of the fact / output buffers;
+                                       work beyond it is skipped and flagged      */
+    int32_t *status;                /* device int (or NULL): FL_STATUS_* bits     */
 } fl_hop_params;
+
+/* Device status bits set by the hop kernels. */
+enum { FL_STATUS_SLOT_OVERFLOW = 1 };
 
 const char *fl_last_error(void);
 int fl_version(void);
@@ -95,18 +101,22 @@ int fl_rows_to_coo(const int64_t *row_ptr, const int32_t *ent, int64_t rows, int
  * largest nonzero values, ties to the lower entity.  noise (f64, or NULL)
  * selects the sampled mode: candidate k (nonzero entries of over-budget rows
  * in state order) scores log(v) - log(noise[k]).  out_src[j] is the input
- * index of kept entry j; outputs have capacity S. */
+ * index of kept entry j.  Outputs have out_capacity entries (0: S); rows that
+ * do not fit are truncated in out_row_ptr and set FL_STATUS_SLOT_OVERFLOW in
+ * *status (device int, may be NULL). */
 size_t fl_topc_workspace(int64_t rows, int64_t S);
 int fl_topc_select(const int64_t *row_ptr, const int32_t *ent, const float *val, int64_t rows, int64_t S, int64_t c1,
                    const double *noise, int64_t *out_row_ptr, int32_t *out_ent, float *out_val, int64_t *out_src,
-                   void *ws, size_t ws_bytes, fl_stream_t stream);
+                   int64_t out_capacity, int32_t *status, void *ws, size_t ws_bytes, fl_stream_t stream);
 /* Number of sampled-mode candidates (syncs). */
 int fl_topc_candidates(const int64_t *row_ptr, const float *val, int64_t rows, int64_t S, int64_t c1,
                        int64_t *n_candidates, void *ws, size_t ws_bytes, fl_stream_t stream);
 
 /* Hop planning: per-entry fact capacity (degree capped by topk_edges per
  * direction, + identity) and its scan into slot_base i64[S+1]; *total_slots
- * (host) receives slot_base[S] (syncs).  Replaces the count kernels and the
+ * (host) receives slot_base[S] (syncs), unless total_slots is NULL (no host
+ * synchronization).  S may exceed the live entry count row_ptr[rows]: entries
+ * beyond it get no slots, so callers can run on upper-bound buffers.  Replaces the count kernels and the
  * two .item() calls of flashlog.cu:2040-2062 / 2160-2182. */
 size_t fl_hop_workspace(int64_t rows, int64_t S);
 int fl_hop_plan(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *ent, int64_t S, fl_csr_side ori,
@@ -133,12 +143,14 @@ int fl_hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t 
  * fact's output index within its row.  Outputs out_ent / out_x / out_y have
  * capacity total_slots, out_row_ptr i64[rows+1] (its last entry is the
  * output count), out_denom f32[rows] (raw row sums).  Stream-ordered; no
- * host synchronization. */
+ * host synchronization.  total_slots is the length of the fact and output
+ * buffers; rows whose slots lie beyond it are skipped and set
+ * FL_STATUS_SLOT_OVERFLOW in *status (device int, may be NULL). */
 size_t fl_reduce_workspace(int64_t rows, int64_t total_slots);
 int fl_row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *slot_base, const int32_t *entry_count,
                   const int32_t *fact_dst, const float *fact_val, int64_t total_slots, int32_t *fact_pos, float eps,
                   int64_t *out_row_ptr, int32_t *out_ent, float *out_x, float *out_y, float *out_denom,
-                  void *ws, size_t ws_bytes, fl_stream_t stream);
+                  int32_t *status, void *ws, size_t ws_bytes, fl_stream_t stream);
 
 /* Hop backward (+ normalization backward unless FL_NO_NORMALIZE).  Replaces
  * flashlog_backward_sparse3d_cached_cuda (flashlog.cu:2317-2361) and
@@ -159,10 +171,22 @@ int fl_normalize_forward(const int64_t *row_ptr, const float *x, int64_t rows, f
 int fl_normalize_backward(const int64_t *row_ptr, const float *x, const float *denom, const float *g, int64_t rows,
                           float eps, float *gx, fl_stream_t stream);
 
-/* grad_full[src_index[j]] = grad_sel[j], zeros elsewhere.  Replaces
+/* grad_full[src_index[j]] = grad_sel[j] for j < n_sel (and j < *n_live when
+ * n_live, a device count, is given), zeros elsewhere.  Replaces
  * _restore_pruned_gradient (flashlog_kernel.py:1150-1155). */
-int fl_scatter_grad(const float *grad_sel, const int64_t *src_index, int64_t n_sel, float *grad_full, int64_t n_full,
-                    fl_stream_t stream);
+int fl_scatter_grad(const float *grad_sel, const int64_t *src_index, int64_t n_sel, const int64_t *n_live,
+                    float *grad_full, int64_t n_full, fl_stream_t stream);
+
+/* Channel readout at the targets: scores[q] = sum over channels l (in order)
+ * of the state's value at (q, l, targets[q]) (0 when absent).  Rows are
+ * r = q * N + l.  Replaces sum_sp_3d + the target lookup of
+ * log_loss_common_sp (src/model_DRUM_kernel_sp.py:22-28, src/utils.py:36-47).
+ * The backward writes g_scores[q] at every entry read and zeros the rest of
+ * grad_val (n_val entries). */
+int fl_readout(const int64_t *row_ptr, const int32_t *ent, const float *val, int64_t N, const int64_t *targets,
+               int64_t Q, float *scores, fl_stream_t stream);
+int fl_readout_backward(const int64_t *row_ptr, const int32_t *ent, int64_t N, const int64_t *targets, int64_t Q,
+                        const float *g_scores, float *grad_val, int64_t n_val, fl_stream_t stream);
 
 /* Rule step with one fixed operator per (query, rule) row: ops i64[B, Lr]
  * holds a forward relation, inverse relation + R, or identity 2R.  Replaces
