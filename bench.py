@@ -84,6 +84,13 @@ class ClockSampler:
         except (FileNotFoundError, OSError):
             self.proc = None
 
+    def wait_first(self, timeout=10.0):
+        """Block until nvidia-smi has printed one sample, so its start-up is not timed."""
+        t_end = time.time() + timeout
+        while self.proc is not None and not self.lines and time.time() < t_end and self.proc.poll() is None:
+            time.sleep(0.02)
+        self.skip = len(self.lines)
+
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
@@ -98,7 +105,8 @@ class ClockSampler:
             self.proc.kill()
         sm, smax, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        lines = self.lines[getattr(self, "skip", 0):] or self.lines[-1:]
+        for ln in lines:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -223,13 +231,14 @@ def run_value_arm(args, cfg, train, csr, rank, world, device):
         mask[hide] = 1
         return loss
 
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()  # before the warm-up: nvidia-smi's start-up must not fall in the timed region
     for b in dev_data[:args.warmup]:
         step(*b, collect=False)
     torch.cuda.synchronize()
+    clocks.wait_first()
     if world > 1:
         dist.barrier()
-    clocks = ClockSampler(torch.cuda.current_device())
-    clocks.start()
     launches0 = _lib.lib().fl_launch_count()
     stats.timer.enabled = True
     torch.cuda.synchronize()
