@@ -391,54 +391,85 @@ __global__ void __launch_bounds__(kExpandWarps * 32, kSampled ? 3 : 4) hop_expan
             written += 1;
         }
         if (lane == 0) a.entry_count[i] = static_cast<int32_t>(written);
+        // Slots the entry reserved but did not fill get the destination -1.
+        for (int64_t s = out + written + lane; s < a.slot_base[i + 1]; s += 32) a.fact_dst[s] = -1;
     }
 }
 
 // ---------------------------------------------------------------------------
-// Row reduction: stable radix sort by destination in shared memory.
+// Row reduction: one CTA per row, stable radix sort by destination in shared memory.
+//
+// A row's facts occupy the contiguous slot range
+// [slot_base[row_ptr[r]], slot_base[row_ptr[r + 1]]) in canonical order; slots
+// an entry did not fill hold the destination -1.  A row of at most kTileA
+// slots is sorted in one tile.  A larger row is first histogrammed over
+// kHistBins destination bins and cut into destination ranges of at most
+// kTileB facts, each loaded (in canonical order) and sorted on its own.  A
+// single bin holding more than kTileB facts is summed through dense
+// kDenseW-wide windows.  Keys stay where they were loaded; the sort permutes
+// 16-bit indices with 8-bit LSD passes whose per-warp digit counters keep
+// every pass stable, so facts of one destination stay in canonical order and
+// are summed left to right.
 // ---------------------------------------------------------------------------
-constexpr int kRThreads = 512;
+constexpr int kRThreads = 1024;
 constexpr int kRWarps = kRThreads / 32;
-constexpr int kTile = 8192;                  // facts sorted at once in shared memory
-constexpr int kWarpItems = kTile / kRWarps;  // 512 per warp region
-constexpr int kLoadK = 4;                    // facts per thread per load step
+constexpr int kDigits = 256;
+constexpr int kTileA = 16384;  // whole-row tile: key, val, idx[2]
+constexpr int kTileB = 12288;  // destination-range tile: key, val, idx[2], slot
+constexpr int kTileD = 8192;   // dense-window sub-tile
+constexpr int kDenseW = 4096;  // dense window width (destinations)
+constexpr int kHistBits = 11;
+constexpr int kHistBins = 1 << kHistBits;
+constexpr int kLoadK = 4;  // slots per thread per load step
 constexpr int kLoadStep = kRThreads * kLoadK;
-constexpr int kEChunk = 1024;                // entries per prefix chunk
-constexpr int kBucketBits = 11;
-constexpr int kBuckets = 1 << kBucketBits;   // destination buckets per row
-constexpr int kDenseW = 4096;                // widest destination window summed densely
+
+struct TileA {
+    uint32_t key[kTileA];
+    float val[kTileA];
+    uint16_t idx[2][kTileA];
+};
+struct TileB {
+    uint32_t key[kTileB];
+    float val[kTileB];
+    uint16_t idx[2][kTileB];
+    uint32_t slot[kTileB];
+};
+struct TileD {
+    uint32_t key[kTileD];
+    float val[kTileD];
+    uint16_t idx[2][kTileD];
+    uint32_t slot[kTileD];
+    float acc[kDenseW];
+    uint32_t oidx[kDenseW];
+    uint32_t touched[kDenseW / 32];
+};
 
 struct ReduceSmem {
-    uint32_t key[2][kTile];
-    uint16_t idx[2][kTile];
-    uint32_t val[kTile];  // fact value bits (a destination id while partitioning)
-    uint32_t slot[kTile];
-    uint32_t shist[kRWarps][256];  // sort digit counters; run starts while partitioning
-    uint32_t bstart[kBuckets + 1];
-    uint32_t bcursor[kBuckets];
-    uint16_t items[kBuckets + 1];
-    uint32_t epre[kEChunk + 1];
-    uint32_t eslot[kEChunk];
-    float acc[kDenseW];
-    uint32_t touched[kDenseW / 32];
+    union {
+        TileA a;
+        TileB b;
+        TileD d;
+    } t;
+    uint16_t cnt[kDigits * kRWarps];  // per-warp digit counters, digit-major
+    uint32_t hist[kHistBins + 1];     // exclusive prefix of the row's destination histogram
+    uint16_t chunk[kHistBins + 1];    // first bin of each destination range
     int64_t scan_scratch[kRWarps + 1];
     float fscratch[kRWarps + 1];
-    int n_items;
+    int n_chunks;
 };
 static_assert(sizeof(ReduceSmem) <= 227 * 1024, "row reduction shared memory exceeds one CTA's budget");
+static_assert(kTileA <= 65536 && kTileB <= 65536 && kTileD <= 65536, "tile indices are 16-bit");
 
 struct ReduceArgs {
     const int64_t *row_ptr;      // rows of the (selected) state
     int64_t rows;
     const int64_t *slot_base;    // per entry
-    const int32_t *entry_count;  // per entry
     const int32_t *fact_dst;
     const float *fact_val;
     int64_t E;
     int32_t *fact_pos;           // may be null
     int32_t *tmp_ent;            // outputs at the row's slot base
     float *tmp_x;
-    uint2 *part;                 // (dst, slot) partition scratch at the row's slot base
     int64_t *out_count;
     float *out_sum;
     int64_t capacity;            // length of the fact / output buffers
@@ -451,282 +482,212 @@ __device__ __forceinline__ int bits_for(int64_t width) {  // bits to represent w
     return b;
 }
 
-// Stream the row's facts in canonical order (entries in row order, each
-// entry's facts in emission order).  For a fact whose destination lies in
-// [lo, hi), visit(slot, dst, pos) is called with pos its ordinal among the
-// visited facts.  Before each load step pre(visited) may flush and returns
-// the ordinal base to continue from.  All threads must call it.
-template <typename Visit, typename Pre>
-__device__ int64_t stream_row(const ReduceArgs &a, ReduceSmem &sm, int64_t ea, int64_t eb, int64_t lo, int64_t hi,
-                              Visit visit, Pre pre) {
-    int64_t visited = 0;
-    for (int64_t ec = ea; ec < eb; ec += kEChunk) {
-        const int64_t ne = (eb - ec) < kEChunk ? (eb - ec) : kEChunk;
-        int64_t c0 = 0, c1 = 0;
-        const int64_t j0 = ec + 2 * threadIdx.x, j1 = j0 + 1;
-        if (2 * threadIdx.x < ne) { c0 = a.entry_count[j0]; sm.eslot[2 * threadIdx.x] = static_cast<uint32_t>(a.slot_base[j0]); }
-        if (2 * threadIdx.x + 1 < ne) { c1 = a.entry_count[j1]; sm.eslot[2 * threadIdx.x + 1] = static_cast<uint32_t>(a.slot_base[j1]); }
-        int64_t tot;
-        const int64_t ex = block_exclusive_scan<int64_t>(c0 + c1, sm.scan_scratch, &tot);
-        if (2 * threadIdx.x < ne) sm.epre[2 * threadIdx.x] = static_cast<uint32_t>(ex);
-        if (2 * threadIdx.x + 1 < ne) sm.epre[2 * threadIdx.x + 1] = static_cast<uint32_t>(ex + c0);
-        if (threadIdx.x == 0) sm.epre[ne] = static_cast<uint32_t>(tot);
-        __syncthreads();
-        const uint32_t nf = static_cast<uint32_t>(tot);
-        for (uint32_t fb = 0; fb < nf; fb += kLoadStep) {
-            visited = pre(visited);
-            uint32_t slot[kLoadK];
-            int32_t dst[kLoadK];
-            int cnt = 0;
-#pragma unroll
-            for (int k = 0; k < kLoadK; ++k) {
-                const uint32_t f = fb + threadIdx.x * kLoadK + k;
-                dst[k] = -1;
-                if (f < nf) {
-                    int l2 = 0, h2 = static_cast<int>(ne) - 1;  // last entry with epre <= f
-                    while (l2 < h2) { int mid = (l2 + h2 + 1) >> 1; if (sm.epre[mid] <= f) l2 = mid; else h2 = mid - 1; }
-                    slot[k] = sm.eslot[l2] + (f - sm.epre[l2]);
-                    const int32_t d = a.fact_dst[slot[k]];
-                    if (d >= lo && d < hi) { dst[k] = d; ++cnt; }
-                }
-            }
-            int64_t btot;
-            const int64_t bex = block_exclusive_scan<int64_t>(cnt, sm.scan_scratch, &btot);
-            int64_t pos = visited + bex;
-#pragma unroll
-            for (int k = 0; k < kLoadK; ++k)
-                if (dst[k] >= 0) visit(slot[k], dst[k], pos++);
-            visited += btot;
-            __syncthreads();
-        }
-    }
-    return visited;
-}
-
-template <typename Visit>
-__device__ int64_t stream_row(const ReduceArgs &a, ReduceSmem &sm, int64_t ea, int64_t eb, int64_t lo, int64_t hi,
-                              Visit visit) {
-    return stream_row(a, sm, ea, eb, lo, hi, visit, [](int64_t v) { return v; });
-}
-
-// Stable LSD radix sort of sm.key[0][0..n) with payload sm.idx[0] over `bits`
-// key bits.  Returns the buffer index (0/1) holding the result.
-__device__ int tile_sort(ReduceSmem &sm, int n, int bits) {
+// Stable LSD radix sort of the index permutation idx0[0..n) by key[idx] over
+// the low `bits` bits, 8 bits per pass.  idx0 must hold 0..n-1 in load order.
+// Returns the buffer holding the sorted permutation.
+__device__ uint16_t *lsd_sort(const uint32_t *key, uint16_t *idx0, uint16_t *idx1, int n, int bits, ReduceSmem &sm) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    int cur = 0;
+    int nw = (n + 255) >> 8;
+    nw = nw < 1 ? 1 : (nw > kRWarps ? kRWarps : nw);
+    const int per = (((n + nw - 1) / nw) + 31) & ~31;
+    const int wlo = warp * per;
+    const int whi = (wlo + per) < n ? (wlo + per) : n;  // empty when wlo >= n
+    uint16_t *src = idx0, *dst = idx1;
     for (int shift = 0; shift < bits; shift += 8) {
-        const int nb = (bits - shift) < 8 ? (bits - shift) : 8;
-        const uint32_t dmask = (1u << nb) - 1u;
-        const int ndig = 1 << nb;
-        for (int d = lane; d < 256; d += 32) sm.shist[warp][d] = 0;
-        __syncwarp();
-        const int wbase = warp * kWarpItems;
-        for (int k = 0; k < kWarpItems / 32; ++k) {
-            const int j = wbase + k * 32 + lane;
-            const bool valid = j < n;
-            const uint32_t d = valid ? (sm.key[cur][j] >> shift) & dmask : 0u;
+        const uint32_t dmask = (bits - shift) >= 8 ? 255u : ((1u << (bits - shift)) - 1u);
+        for (int k = threadIdx.x; k < kDigits * kRWarps / 8; k += kRThreads)
+            reinterpret_cast<uint4 *>(sm.cnt)[k] = make_uint4(0u, 0u, 0u, 0u);
+        __syncthreads();
+        for (int base = wlo; base < whi; base += 32) {
+            const int j = base + lane;
+            const bool valid = j < whi;
+            const uint32_t d = valid ? (key[src[j]] >> shift) & dmask : 0u;
             const unsigned act = __ballot_sync(kFull, valid);
             if (valid) {
                 const unsigned peers = __match_any_sync(act, d);
-                if (lane == __ffs(peers) - 1) sm.shist[warp][d] += __popc(peers);
-            }
-            __syncwarp();
-        }
-        __syncthreads();
-        // digit-major exclusive offsets: thread t < ndig owns digit t
-        uint32_t dsum = 0;
-        if (static_cast<int>(threadIdx.x) < ndig)
-            for (int w2 = 0; w2 < kRWarps; ++w2) dsum += sm.shist[w2][threadIdx.x];
-        int64_t tot;
-        const int64_t dex = block_exclusive_scan<int64_t>(
-            static_cast<int64_t>(threadIdx.x < static_cast<unsigned>(ndig) ? dsum : 0), sm.scan_scratch, &tot);
-        if (static_cast<int>(threadIdx.x) < ndig) {
-            uint32_t run = static_cast<uint32_t>(dex);
-            for (int w2 = 0; w2 < kRWarps; ++w2) {
-                const uint32_t h = sm.shist[w2][threadIdx.x];
-                sm.shist[w2][threadIdx.x] = run;
-                run += h;
+                if (lane == __ffs(peers) - 1) sm.cnt[d * kRWarps + warp] += static_cast<uint16_t>(__popc(peers));
             }
         }
         __syncthreads();
-        for (int k = 0; k < kWarpItems / 32; ++k) {
-            const int j = wbase + k * 32 + lane;
-            const bool valid = j < n;
-            const uint32_t key = valid ? sm.key[cur][j] : 0u;
-            const uint32_t d = (key >> shift) & dmask;
+        {  // exclusive prefix over (digit, warp), 8 counters per thread
+            uint16_t *c = sm.cnt + threadIdx.x * 8;
+            int v[8];
+            int s = 0;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) { v[k] = c[k]; s += v[k]; }
+            int64_t tot;
+            int run = static_cast<int>(block_exclusive_scan<int64_t>(s, sm.scan_scratch, &tot));
+#pragma unroll
+            for (int k = 0; k < 8; ++k) { c[k] = static_cast<uint16_t>(run); run += v[k]; }
+        }
+        __syncthreads();
+        for (int base = wlo; base < whi; base += 32) {
+            const int j = base + lane;
+            const bool valid = j < whi;
+            const uint16_t id = valid ? src[j] : 0;
+            const uint32_t d = valid ? (key[id] >> shift) & dmask : 0u;
             const unsigned act = __ballot_sync(kFull, valid);
             if (valid) {
                 const unsigned peers = __match_any_sync(act, d);
-                const int rank = __popc(peers & lanemask_lt());
-                const uint32_t base = sm.shist[warp][d];
-                sm.key[cur ^ 1][base + rank] = key;
-                sm.idx[cur ^ 1][base + rank] = sm.idx[cur][j];
+                const uint32_t b = sm.cnt[d * kRWarps + warp];
+                dst[b + __popc(peers & lanemask_lt())] = id;
                 __syncwarp(act);
-                if (lane == __ffs(peers) - 1) sm.shist[warp][d] = base + __popc(peers);
+                if (lane == __ffs(peers) - 1) sm.cnt[d * kRWarps + warp] = static_cast<uint16_t>(b + __popc(peers));
             }
             __syncwarp();
         }
         __syncthreads();
-        cur ^= 1;
+        uint16_t *t = src; src = dst; dst = t;
     }
-    return cur;
+    return src;
 }
 
-// Sort the loaded tile [0, n) (keys are dst - lo, values in sm.val) and emit
-// one output per destination, summing in canonical order.  Returns the
-// block-sum of the outputs.
-__device__ float emit_sorted(const ReduceArgs &a, ReduceSmem &sm, int n, int bits, int64_t lo, int64_t obase,
-                             int64_t *written) {
-    const int cur = tile_sort(sm, n, bits);
-    uint32_t *seg = sm.key[cur ^ 1];  // free buffer: segment starts
-    int64_t nseg_total = 0;
-    for (int base = 0; base < n; base += kRThreads) {
-        const int j = base + threadIdx.x;
-        const bool head = j < n && (j == 0 || sm.key[cur][j] != sm.key[cur][j - 1]);
-        int64_t tot;
-        const int64_t ex = block_exclusive_scan<int64_t>(head ? 1 : 0, sm.scan_scratch, &tot);
-        if (head) seg[nseg_total + ex] = static_cast<uint32_t>(j);
-        nseg_total += tot;
+// Emit a sorted tile: positions [0, n) of perm, keys key[perm[p]] ascending
+// (destination = lo + key).  Each destination's facts are summed in
+// permutation order (canonical order).  Outputs go to the row's output index
+// *written onwards; slot_of(i) is the row-local slot of tile element i.
+// Returns the block sum of the emitted values.
+template <typename SlotOf>
+__device__ float emit_tile(const ReduceArgs &a, ReduceSmem &sm, const uint32_t *key, const float *val,
+                           const uint16_t *perm, int n, int64_t lo, int64_t s0, int64_t *written, SlotOf slot_of) {
+    const int per = (n + kRThreads - 1) / kRThreads;
+    const int p0 = threadIdx.x * per;
+    const int p1 = (p0 + per) < n ? (p0 + per) : n;
+    int heads = 0;
+    uint32_t prev = p0 > 0 && p0 < n ? key[perm[p0 - 1]] : 0xffffffffu;
+    for (int p = p0; p < p1; ++p) {
+        const uint32_t k = key[perm[p]];
+        heads += (p == 0 || k != prev) ? 1 : 0;
+        prev = k;
     }
-    __syncthreads();
-    const int nseg = static_cast<int>(nseg_total);
+    int64_t tot;
+    const int64_t ex = block_exclusive_scan<int64_t>(heads, sm.scan_scratch, &tot);
+    int64_t oi = *written + ex - 1;
     float local = 0.0f;
-    for (int s = threadIdx.x; s < nseg; s += kRThreads) {
-        const int st = static_cast<int>(seg[s]);
-        const int en = s + 1 < nseg ? static_cast<int>(seg[s + 1]) : n;
+    prev = p0 > 0 && p0 < n ? key[perm[p0 - 1]] : 0xffffffffu;
+    for (int p = p0; p < p1; ++p) {
+        const uint32_t k = key[perm[p]];
+        const bool head = p == 0 || k != prev;
+        prev = k;
+        if (!head) continue;
+        ++oi;
         float x = 0.0f;
-        for (int q = st; q < en; ++q) x += __uint_as_float(sm.val[sm.idx[cur][q]]);
-        const int64_t oi = *written + s;
-        a.tmp_ent[obase + oi] = static_cast<int32_t>(lo + sm.key[cur][st]);
-        a.tmp_x[obase + oi] = x;
+        int q = p;
+        for (; q < n; ++q) {
+            const uint16_t i = perm[q];
+            if (key[i] != k) break;
+            x += val[i];
+        }
+        a.tmp_ent[s0 + oi] = static_cast<int32_t>(lo + k);
+        a.tmp_x[s0 + oi] = x;
         if (a.fact_pos)
-            for (int q = st; q < en; ++q) a.fact_pos[sm.slot[sm.idx[cur][q]]] = static_cast<int32_t>(oi);
+            for (int q2 = p; q2 < q; ++q2) a.fact_pos[s0 + slot_of(perm[q2])] = static_cast<int32_t>(oi);
         local += x;
     }
-    *written += nseg;
+    *written += tot;
     return block_sum(local, sm.fscratch);
 }
 
-// Dense window [lo, hi), hi - lo <= kDenseW, over the contiguous (dst, slot)
-// pairs part[p0, p1) (canonical order; pairs outside the window are
-// skipped).  Tiles are stably sorted and added into acc[] one fact at a time,
-// so every destination is summed in canonical order.
-__device__ float dense_window(const ReduceArgs &a, ReduceSmem &sm, const uint2 *part, int64_t p0, int64_t p1,
-                              int64_t lo, int64_t hi, int64_t obase, int64_t *written) {
-    const int W = static_cast<int>(hi - lo);
-    const int bits = bits_for(W);
-    for (int d = threadIdx.x; d < kDenseW; d += kRThreads) sm.acc[d] = 0.0f;
-    for (int d = threadIdx.x; d < kDenseW / 32; d += kRThreads) sm.touched[d] = 0u;
-    __syncthreads();
-    int64_t in_tile = 0;
-    for (int64_t fb = p0; fb < p1; fb += kLoadStep) {
-        if (in_tile + kLoadStep > kTile) {
-            const int n = static_cast<int>(in_tile);
-            const int cur = tile_sort(sm, n, bits);
-            for (int j = threadIdx.x; j < n; j += kRThreads) {
-                if (!(j == 0 || sm.key[cur][j] != sm.key[cur][j - 1])) continue;
-                const uint32_t d = sm.key[cur][j];
-                float accv = sm.acc[d];
-                for (int q = j; q < n && sm.key[cur][q] == d; ++q) accv += __uint_as_float(sm.val[sm.idx[cur][q]]);
-                sm.acc[d] = accv;
-                atomicOr(&sm.touched[d >> 5], 1u << (d & 31));
-            }
-            __syncthreads();
-            in_tile = 0;
-        }
-        uint2 pr[kLoadK];
-        int cnt = 0;
+// Load, in canonical order, the facts of the row's slot range whose
+// destination lies in [lo, hi) into key (dst - lo), val, slot (row-local) and
+// idx0 (identity), starting at tile position `pos`.  Stops before a load step
+// that would overflow `cap` and returns the slot where it stopped in *next
+// (ns when done).  Returns the new tile length.
+__device__ int load_range(const ReduceArgs &a, ReduceSmem &sm, int64_t s0, int64_t ns, int64_t from, int64_t lo,
+                          int64_t hi, uint32_t *key, float *val, uint32_t *slot, uint16_t *idx0, int pos, int cap,
+                          int64_t *next) {
+    int64_t fb = from;
+    for (; fb < ns; fb += kLoadStep) {
+        if (pos + kLoadStep > cap) break;
+        int32_t d[kLoadK];
+        int c = 0;
 #pragma unroll
         for (int k = 0; k < kLoadK; ++k) {
-            const int64_t f = fb + static_cast<int64_t>(threadIdx.x) * kLoadK + k;
-            pr[k] = make_uint2(0xffffffffu, 0u);
-            if (f < p1) {
-                const uint2 v = part[f];
-                if (static_cast<int64_t>(v.x) >= lo && static_cast<int64_t>(v.x) < hi) { pr[k] = v; ++cnt; }
+            const int64_t j = fb + threadIdx.x * kLoadK + k;
+            d[k] = -1;
+            if (j < ns) {
+                const int32_t dd = a.fact_dst[s0 + j];
+                if (dd >= lo && dd < hi) { d[k] = dd; ++c; }
             }
         }
-        int64_t btot;
-        const int64_t bex = block_exclusive_scan<int64_t>(cnt, sm.scan_scratch, &btot);
-        int64_t pos = in_tile + bex;
+        int64_t tot;
+        const int64_t ex = block_exclusive_scan<int64_t>(c, sm.scan_scratch, &tot);
+        int p = pos + static_cast<int>(ex);
 #pragma unroll
-        for (int k = 0; k < kLoadK; ++k)
-            if (pr[k].x != 0xffffffffu) {
-                sm.key[0][pos] = pr[k].x - static_cast<uint32_t>(lo);
-                sm.idx[0][pos] = static_cast<uint16_t>(pos);
-                sm.val[pos] = __float_as_uint(a.fact_val[pr[k].y]);
-                ++pos;
-            }
-        in_tile += btot;
-        __syncthreads();
+        for (int k = 0; k < kLoadK; ++k) {
+            if (d[k] < 0) continue;
+            const int64_t j = fb + threadIdx.x * kLoadK + k;
+            key[p] = static_cast<uint32_t>(d[k] - lo);
+            val[p] = a.fact_val[s0 + j];
+            slot[p] = static_cast<uint32_t>(j);
+            idx0[p] = static_cast<uint16_t>(p);
+            ++p;
+        }
+        pos += static_cast<int>(tot);
     }
-    if (in_tile > 0) {
-        const int n = static_cast<int>(in_tile);
-        const int cur = tile_sort(sm, n, bits);
-        for (int j = threadIdx.x; j < n; j += kRThreads) {
-            if (!(j == 0 || sm.key[cur][j] != sm.key[cur][j - 1])) continue;
-            const uint32_t d = sm.key[cur][j];
-            float accv = sm.acc[d];
-            for (int q = j; q < n && sm.key[cur][q] == d; ++q) accv += __uint_as_float(sm.val[sm.idx[cur][q]]);
-            sm.acc[d] = accv;
-            atomicOr(&sm.touched[d >> 5], 1u << (d & 31));
+    *next = fb < ns ? fb : ns;
+    __syncthreads();
+    return pos;
+}
+
+// Dense window [lo, hi), hi - lo <= kDenseW: the window's facts are streamed
+// in canonical order in sub-tiles; each sub-tile is stably sorted and added
+// into acc[] one destination run at a time, so every destination is summed in
+// canonical order.  A second stream writes fact_pos.
+__device__ float dense_window(const ReduceArgs &a, ReduceSmem &sm, int64_t s0, int64_t ns, int64_t lo, int64_t hi,
+                              int64_t *written) {
+    TileD &t = sm.t.d;
+    const int W = static_cast<int>(hi - lo);
+    const int bits = bits_for(W);
+    for (int d = threadIdx.x; d < kDenseW; d += kRThreads) t.acc[d] = 0.0f;
+    for (int d = threadIdx.x; d < kDenseW / 32; d += kRThreads) t.touched[d] = 0u;
+    __syncthreads();
+    int64_t from = 0;
+    while (from < ns) {
+        int64_t next;
+        const int n = load_range(a, sm, s0, ns, from, lo, hi, t.key, t.val, t.slot, t.idx[0], 0, kTileD, &next);
+        from = next;
+        if (n == 0) continue;
+        const uint16_t *perm = lsd_sort(t.key, t.idx[0], t.idx[1], n, bits, sm);
+        const int per = (n + kRThreads - 1) / kRThreads;
+        const int p0 = threadIdx.x * per;
+        const int p1 = (p0 + per) < n ? (p0 + per) : n;
+        for (int p = p0; p < p1; ++p) {
+            const uint32_t k = t.key[perm[p]];
+            if (!(p == 0 || k != t.key[perm[p - 1]])) continue;
+            float accv = t.acc[k];
+            for (int q = p; q < n && t.key[perm[q]] == k; ++q) accv += t.val[perm[q]];
+            t.acc[k] = accv;
+            atomicOr(&t.touched[k >> 5], 1u << (k & 31));
         }
         __syncthreads();
     }
     // Output index of every touched destination (ordered compaction).
-    uint32_t *oidx = sm.key[1];
     int64_t nout = 0;
     float local = 0.0f;
     for (int base = 0; base < W; base += kRThreads) {
         const int d = base + threadIdx.x;
-        const bool t = d < W && ((sm.touched[d >> 5] >> (d & 31)) & 1u);
+        const bool hit = d < W && ((t.touched[d >> 5] >> (d & 31)) & 1u);
         int64_t tot;
-        const int64_t ex = block_exclusive_scan<int64_t>(t ? 1 : 0, sm.scan_scratch, &tot);
-        if (t) {
+        const int64_t ex = block_exclusive_scan<int64_t>(hit ? 1 : 0, sm.scan_scratch, &tot);
+        if (hit) {
             const int64_t oi = *written + nout + ex;
-            oidx[d] = static_cast<uint32_t>(oi);
-            a.tmp_ent[obase + oi] = static_cast<int32_t>(lo + d);
-            a.tmp_x[obase + oi] = sm.acc[d];
-            local += sm.acc[d];
+            t.oidx[d] = static_cast<uint32_t>(oi);
+            a.tmp_ent[s0 + oi] = static_cast<int32_t>(lo + d);
+            a.tmp_x[s0 + oi] = t.acc[d];
+            local += t.acc[d];
         }
         nout += tot;
     }
     __syncthreads();
     if (a.fact_pos)
-        for (int64_t f = p0 + threadIdx.x; f < p1; f += kRThreads) {
-            const uint2 v = part[f];
-            if (static_cast<int64_t>(v.x) >= lo && static_cast<int64_t>(v.x) < hi)
-                a.fact_pos[v.y] = static_cast<int32_t>(oidx[v.x - lo]);
+        for (int64_t j = threadIdx.x; j < ns; j += kRThreads) {
+            const int32_t dd = a.fact_dst[s0 + j];
+            if (dd >= lo && dd < hi) a.fact_pos[s0 + j] = static_cast<int32_t>(t.oidx[dd - lo]);
         }
     *written += nout;
     const float total = block_sum(local, sm.fscratch);
     return total;
-}
-
-// Greedy split of consecutive buckets into items of <= kTile facts; a bucket
-// above kTile always forms an item of its own.  Reads counts from
-// bstart[b + 1] - bstart[b]; writes item start buckets and the sentinel.
-__device__ int split_buckets(const uint32_t *bstart, uint16_t *items) {
-    int n = 0, start = 0;
-    uint32_t accum = 0;
-    for (int b = 0; b < kBuckets; ++b) {
-        const uint32_t h = bstart[b + 1] - bstart[b];
-        if (h > static_cast<uint32_t>(kTile)) {
-            if (b > start) items[n++] = static_cast<uint16_t>(start);
-            items[n++] = static_cast<uint16_t>(b);
-            start = b + 1;
-            accum = 0;
-            continue;
-        }
-        if (accum + h > static_cast<uint32_t>(kTile)) {
-            items[n++] = static_cast<uint16_t>(start);
-            start = b;
-            accum = 0;
-        }
-        accum += h;
-    }
-    if (start < kBuckets) items[n++] = static_cast<uint16_t>(start);
-    items[n] = static_cast<uint16_t>(kBuckets);
-    return n;
 }
 
 __global__ void __launch_bounds__(kRThreads, 1) row_reduce_kernel(ReduceArgs a) {
@@ -735,12 +696,8 @@ __global__ void __launch_bounds__(kRThreads, 1) row_reduce_kernel(ReduceArgs a) 
     const int64_t r = blockIdx.x;
     if (r >= a.rows) return;
     const int64_t ea = a.row_ptr[r], eb = a.row_ptr[r + 1];
-    if (ea == eb) {
-        if (threadIdx.x == 0) { a.out_count[r] = 0; a.out_sum[r] = 0.0f; }
-        return;
-    }
-    const int64_t obase = a.slot_base[ea];
-    if (a.slot_base[eb] > a.capacity) {  // the row's slots lie past the buffers: skip it
+    const int64_t s0 = a.slot_base[ea], s1 = a.slot_base[eb];
+    if (s1 > a.capacity) {  // the row's slots lie past the buffers: skip it
         if (threadIdx.x == 0) {
             a.out_count[r] = 0;
             a.out_sum[r] = 0.0f;
@@ -748,107 +705,89 @@ __global__ void __launch_bounds__(kRThreads, 1) row_reduce_kernel(ReduceArgs a) 
         }
         return;
     }
-    int64_t F = 0;
-    for (int64_t e = ea + threadIdx.x; e < eb; e += kRThreads) F += a.entry_count[e];
-    F = block_sum(F, sm.scan_scratch);
+    const int64_t ns = s1 - s0;
     int64_t written = 0;
     float rsum = 0.0f;
-    if (F <= kTile) {
-        // The whole row fits one tile: load, sort by destination, emit.
-        const int64_t n = stream_row(a, sm, ea, eb, 0, a.E, [&](uint32_t slot, int32_t dst, int64_t pos) {
-            sm.key[0][pos] = static_cast<uint32_t>(dst);
-            sm.idx[0][pos] = static_cast<uint16_t>(pos);
-            sm.val[pos] = __float_as_uint(a.fact_val[slot]);
-            sm.slot[pos] = slot;
-        });
-        __syncthreads();
-        if (n > 0) rsum = emit_sorted(a, sm, static_cast<int>(n), bits_for(a.E), 0, obase, &written);
+    if (ns <= kTileA) {
+        // The whole row fits one tile; unused slots get the key E (sorted last).
+        TileA &t = sm.t.a;
+        const uint32_t sentinel = static_cast<uint32_t>(a.E);
+        int valid = 0;
+        for (int j = threadIdx.x; j < ns; j += kRThreads) {
+            const int32_t d = a.fact_dst[s0 + j];
+            const bool ok = d >= 0 && static_cast<int64_t>(d) < a.E;
+            t.key[j] = ok ? static_cast<uint32_t>(d) : sentinel;
+            t.val[j] = ok ? a.fact_val[s0 + j] : 0.0f;
+            t.idx[0][j] = static_cast<uint16_t>(j);
+            valid += ok ? 1 : 0;
+        }
+        const int n = static_cast<int>(block_sum<int64_t>(valid, sm.scan_scratch));
+        if (n > 0) {
+            const uint16_t *perm = lsd_sort(t.key, t.idx[0], t.idx[1], static_cast<int>(ns), bits_for(a.E + 1), sm);
+            rsum = emit_tile(a, sm, t.key, t.val, perm, n, 0, s0, &written,
+                             [](uint16_t i) { return static_cast<uint32_t>(i); });
+        }
     } else {
-        // Pass A: destination histogram over kBuckets buckets.
-        const int b1 = bits_for(a.E);
-        const int shift = b1 > kBucketBits ? b1 - kBucketBits : 0;
-        for (int b = threadIdx.x; b <= kBuckets; b += kRThreads) sm.bstart[b] = 0;
+        // Destination histogram of the row, then ranges of at most kTileB facts.
+        const int hb = bits_for(a.E);
+        const int hshift = hb > kHistBits ? hb - kHistBits : 0;
+        for (int b = threadIdx.x; b <= kHistBins; b += kRThreads) sm.hist[b] = 0u;
         __syncthreads();
-        stream_row(a, sm, ea, eb, 0, a.E,
-                   [&](uint32_t, int32_t dst, int64_t) { atomicAdd(&sm.bstart[(dst >> shift) + 1], 1u); });
-        __syncthreads();
-        {  // inclusive scan of bstart[1..kBuckets] -> bucket starts (4 per thread)
-            uint32_t v[4];
-            uint32_t sum = 0;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) { v[k] = sm.bstart[1 + threadIdx.x * 4 + k]; sum += v[k]; }
-            int64_t tot;
-            int64_t ex = block_exclusive_scan<int64_t>(sum, sm.scan_scratch, &tot);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) { ex += v[k]; sm.bstart[1 + threadIdx.x * 4 + k] = static_cast<uint32_t>(ex); }
+        for (int64_t j = threadIdx.x; j < ns; j += kRThreads) {
+            const int32_t d = a.fact_dst[s0 + j];
+            if (d >= 0 && static_cast<int64_t>(d) < a.E) atomicAdd(&sm.hist[d >> hshift], 1u);
         }
         __syncthreads();
-        for (int b = threadIdx.x; b < kBuckets; b += kRThreads) sm.bcursor[b] = sm.bstart[b];
+        {  // exclusive prefix, 2 bins per thread; hist[kHistBins] = total
+            const uint32_t v0 = sm.hist[2 * threadIdx.x], v1 = sm.hist[2 * threadIdx.x + 1];
+            int64_t tot;
+            const int64_t ex = block_exclusive_scan<int64_t>(v0 + v1, sm.scan_scratch, &tot);
+            sm.hist[2 * threadIdx.x] = static_cast<uint32_t>(ex);
+            sm.hist[2 * threadIdx.x + 1] = static_cast<uint32_t>(ex + v0);
+            if (threadIdx.x == 0) sm.hist[kHistBins] = static_cast<uint32_t>(tot);
+        }
         __syncthreads();
-        // Pass B: stable scatter of (dst, slot) into the buckets' runs.
-        uint32_t *runstart = &sm.shist[0][0];  // kBuckets entries while partitioning
-        auto flush = [&](int n) {
-            if (n == 0) return;
-            const int cur = tile_sort(sm, n, kBucketBits);
-            for (int j = threadIdx.x; j < n; j += kRThreads)
-                if (j == 0 || sm.key[cur][j] != sm.key[cur][j - 1]) runstart[sm.key[cur][j]] = static_cast<uint32_t>(j);
-            __syncthreads();
-            for (int j = threadIdx.x; j < n; j += kRThreads) {
-                const uint32_t b = sm.key[cur][j];
-                const uint16_t src = sm.idx[cur][j];
-                const uint32_t pos = sm.bcursor[b] + (static_cast<uint32_t>(j) - runstart[b]);
-                a.part[obase + pos] = make_uint2(sm.val[src], sm.slot[src]);
-            }
-            __syncthreads();
-            for (int j = threadIdx.x; j < n; j += kRThreads) {
-                const uint32_t b = sm.key[cur][j];
-                if (j + 1 == n || sm.key[cur][j + 1] != b) sm.bcursor[b] += static_cast<uint32_t>(j + 1) - runstart[b];
-            }
-            __syncthreads();
-        };
-        const int64_t residual = stream_row(
-            a, sm, ea, eb, 0, a.E,
-            [&](uint32_t slot, int32_t dst, int64_t pos) {
-                sm.key[0][pos] = static_cast<uint32_t>(dst) >> shift;
-                sm.idx[0][pos] = static_cast<uint16_t>(pos);
-                sm.val[pos] = static_cast<uint32_t>(dst);
-                sm.slot[pos] = slot;
-            },
-            [&](int64_t visited) -> int64_t {
-                if (visited + kLoadStep > kTile) { flush(static_cast<int>(visited)); return 0; }
-                return visited;
-            });
-        flush(static_cast<int>(residual));
-        // Pass C: items of consecutive buckets, each loaded contiguously.
-        if (threadIdx.x == 0) sm.n_items = split_buckets(sm.bstart, sm.items);
-        __syncthreads();
-        const int nit = sm.n_items;
-        const uint2 *part = a.part + obase;
-        for (int it = 0; it < nit; ++it) {
-            const int bl = sm.items[it], bh = sm.items[it + 1];
-            const int64_t p0 = sm.bstart[bl], p1 = sm.bstart[bh];
-            if (p1 == p0) continue;
-            const int64_t lo = static_cast<int64_t>(bl) << shift;
-            int64_t hi = static_cast<int64_t>(bh) << shift;
-            if (hi > a.E) hi = a.E;
-            if (p1 - p0 <= kTile) {
-                const int n = static_cast<int>(p1 - p0);
-                for (int k = threadIdx.x; k < n; k += kRThreads) {
-                    const uint2 v = part[p0 + k];
-                    sm.key[0][k] = v.x - static_cast<uint32_t>(lo);
-                    sm.idx[0][k] = static_cast<uint16_t>(k);
-                    sm.val[k] = __float_as_uint(a.fact_val[v.y]);
-                    sm.slot[k] = v.y;
+        if (threadIdx.x == 0) {
+            int nc = 0, start = 0;
+            while (start < kHistBins) {
+                // largest e in [start, kHistBins] with hist[e] - hist[start] <= kTileB
+                int lo2 = start, hi2 = kHistBins;
+                const uint32_t base = sm.hist[start];
+                while (lo2 < hi2) {
+                    const int mid = (lo2 + hi2 + 1) >> 1;
+                    if (sm.hist[mid] - base <= static_cast<uint32_t>(kTileB)) lo2 = mid; else hi2 = mid - 1;
                 }
-                __syncthreads();
-                rsum += emit_sorted(a, sm, n, bits_for(hi - lo), lo, obase, &written);
+                const int e = lo2 > start ? lo2 : start + 1;  // one bin above a tile: a dense range
+                sm.chunk[nc++] = static_cast<uint16_t>(start);
+                start = e;
+            }
+            sm.chunk[nc] = static_cast<uint16_t>(kHistBins);
+            sm.n_chunks = nc;
+        }
+        __syncthreads();
+        const int nc = sm.n_chunks;
+        for (int c = 0; c < nc; ++c) {
+            const int bl = sm.chunk[c], bh = sm.chunk[c + 1];
+            const uint32_t count = sm.hist[bh] - sm.hist[bl];
+            if (count == 0) continue;
+            const int64_t lo = static_cast<int64_t>(bl) << hshift;
+            int64_t hi = static_cast<int64_t>(bh) << hshift;
+            if (hi > a.E) hi = a.E;
+            if (count <= static_cast<uint32_t>(kTileB)) {
+                TileB &t = sm.t.b;
+                int64_t next;
+                const int n = load_range(a, sm, s0, ns, 0, lo, hi, t.key, t.val, t.slot, t.idx[0], 0, 1 << 30,
+                                         &next);  // count <= kTileB: no early stop
+                const uint16_t *perm = lsd_sort(t.key, t.idx[0], t.idx[1], n, bits_for(hi - lo), sm);
+                rsum += emit_tile(a, sm, t.key, t.val, perm, n, lo, s0, &written,
+                                  [&t](uint16_t i) { return t.slot[i]; });
             } else {
-                // One bucket with more facts than a tile: dense windows over it.
                 for (int64_t wlo = lo; wlo < hi; wlo += kDenseW) {
                     const int64_t whi = (wlo + kDenseW) < hi ? (wlo + kDenseW) : hi;
-                    rsum += dense_window(a, sm, part, p0, p1, wlo, whi, obase, &written);
+                    rsum += dense_window(a, sm, s0, ns, wlo, whi, &written);
                 }
             }
+            __syncthreads();
         }
     }
     if (threadIdx.x == 0) { a.out_count[r] = written; a.out_sum[r] = rsum; }
@@ -1042,7 +981,7 @@ size_t hop_workspace(int64_t rows, int64_t S) {
 }
 
 size_t hop_output_tmp_bytes(int64_t total_slots) {
-    return carve_bytes<int32_t>(total_slots) + carve_bytes<float>(total_slots) + carve_bytes<uint2>(total_slots);
+    return carve_bytes<int32_t>(total_slots) + carve_bytes<float>(total_slots);
 }
 
 int hop_plan(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *ent, int64_t S, const fl_csr_side &ori,
@@ -1104,13 +1043,13 @@ int row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *s
     void *scan_ws = c.take<char>(sws);
     int32_t *tmp_ent = c.take<int32_t>(total_slots > 0 ? total_slots : 1);
     float *tmp_x = c.take<float>(total_slots > 0 ? total_slots : 1);
-    uint2 *part = c.take<uint2>(total_slots > 0 ? total_slots : 1);
-    FL_REQUIRE(out_count && out_sum && scan_ws && tmp_ent && tmp_x && part, "row_reduce workspace too small");
+    FL_REQUIRE(out_count && out_sum && scan_ws && tmp_ent && tmp_x, "row_reduce workspace too small");
+    (void)entry_count;  // unfilled slots carry the destination -1
     if (rows > 0) {
         ReduceArgs a;
-        a.row_ptr = row_ptr; a.rows = rows; a.slot_base = slot_base; a.entry_count = entry_count;
+        a.row_ptr = row_ptr; a.rows = rows; a.slot_base = slot_base;
         a.fact_dst = fact_dst; a.fact_val = fact_val; a.E = E; a.fact_pos = fact_pos;
-        a.tmp_ent = tmp_ent; a.tmp_x = tmp_x; a.part = part; a.out_count = out_count; a.out_sum = out_sum;
+        a.tmp_ent = tmp_ent; a.tmp_x = tmp_x; a.out_count = out_count; a.out_sum = out_sum;
         a.capacity = total_slots; a.status = status;
         const size_t smem = sizeof(ReduceSmem);
         static bool attr_set = false;
