@@ -174,6 +174,11 @@ int fl_hop_plan(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *e
     return hop_plan(p, row_ptr, ent, S, ori, inv, slot_base, total_slots, ws, ws_bytes, as_stream(stream));
 }
 
+int fl_csr_visibility(const int32_t *order, int64_t m, const uint8_t *mask_triple, uint8_t *vis, fl_stream_t stream) {
+    FL_REQUIRE(m >= 0 && (m == 0 || (order && mask_triple && vis)), "fl_csr_visibility: bad arguments");
+    return csr_visibility(order, m, mask_triple, vis, as_stream(stream));
+}
+
 int fl_hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *ent, const float *val, int64_t S,
                   const float *w, fl_csr_side ori, fl_csr_side inv, const float *mask_csr_ori,
                   const float *mask_csr_inv, const uint8_t *mask_triple, const float *edge_weight,

@@ -49,7 +49,8 @@ __device__ __forceinline__ int64_t find_row(const int64_t *row_ptr, int64_t rows
 }
 
 // ---------------------------------------------------------------------------
-// Plan: per-entry fact capacity (budget-capped degree per side + identity).
+// Plan: per-entry fact capacity (budget-capped degree per side + identity)
+// and the entry's row.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ int64_t side_degree(const Side &s, int64_t src) {
     // Groups of a source are contiguous in CSR order, so its degree follows
@@ -59,10 +60,11 @@ __device__ __forceinline__ int64_t side_degree(const Side &s, int64_t src) {
 }
 
 __global__ void hop_capacity_kernel(const int32_t *ent, const int64_t *row_ptr, int64_t rows, int64_t S, Side ori,
-                                    Side inv, int64_t topk, int wot_i, int64_t *cap) {
+                                    Side inv, int64_t topk, int wot_i, int64_t *cap, int32_t *entry_row) {
     int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
     if (i >= S) return;
     if (i >= row_ptr[rows]) { cap[i] = 0; return; }  // beyond the live entries
+    if (entry_row) entry_row[i] = static_cast<int32_t>(find_row(row_ptr, rows, i));
     int64_t src = ent[i];
     int64_t d0 = side_degree(ori, src);
     int64_t d1 = side_degree(inv, src);
@@ -70,10 +72,22 @@ __global__ void hop_capacity_kernel(const int32_t *ent, const int64_t *row_ptr, 
     cap[i] = d0 + d1 + (wot_i ? 0 : 1);
 }
 
+// CSR-ordered visibility of one side: vis[p] = mask_triple[order[p]].
+__global__ void csr_visibility_kernel(const int32_t *order, int64_t m, const uint8_t *mask_triple, uint8_t *vis) {
+    for (int64_t p = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; p < m;
+         p += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        vis[p] = mask_triple[order[p]] != 0 ? 1 : 0;
+}
+
 // ---------------------------------------------------------------------------
-// Expansion: one warp per source entry.
+// Expansion.  Entries whose two sides have at most kTeam relation groups each
+// (most entries) are expanded by 8-lane teams, four entries per warp; the
+// others by a whole warp, with the entry's group keys staged in shared memory
+// for the c2 threshold.
 // ---------------------------------------------------------------------------
 constexpr int kExpandWarps = 8;
+constexpr int kTeam = 8;
+constexpr int kStage = 1024;  // relation groups of one side staged per warp
 
 struct WarpScratch {
     unsigned int hist[256];
@@ -83,6 +97,58 @@ struct WarpScratch {
     int32_t rel[32];
     int32_t quota[32];
 };
+
+// Per-warp staging of one side's group keys (fp32 weight bits, 0 when w <= 0)
+// and counts clamped to the budget.  Clamping leaves the threshold and the
+// take of every group unchanged: a clamped group alone reaches the budget.
+struct StageBuf {
+    uint32_t key[kStage];
+    uint16_t cnt[kStage];
+};
+
+struct ExpandArgs {
+    const int64_t *row_ptr;
+    const int32_t *ent;
+    const float *val;
+    int64_t S, rows, n, r_size, topk, flags, seed, L, capacity;
+    int32_t *status;
+    const float *w;
+    Side ori, inv;
+    const uint8_t *mask_triple;
+    const uint8_t *vis_ori, *vis_inv;  // CSR-ordered visibility (may be null)
+    const float *edge_weight;
+    const int64_t *slot_base;
+    const int32_t *entry_row;          // may be null: rows found by binary search
+    int32_t *fact_dst;
+    float *fact_val;
+    int16_t *fact_rel;
+    float *fact_m;
+    int32_t *entry_count;
+};
+
+// Multiplier m and visibility of the fact at CSR position p.
+__device__ __forceinline__ void fact_mask(const ExpandArgs &a, const Side &sd, const uint8_t *vis, int64_t p,
+                                          bool drop_masked, bool edge_w, bool edge_score, float *m, bool *visible) {
+    *m = 1.0f;
+    *visible = true;
+    if (vis != nullptr && !edge_w) {
+        const bool mv = vis[p] != 0;
+        *m = mv ? 1.0f : 0.0f;
+        if (drop_masked && !mv) *visible = false;
+    } else if (a.mask_triple) {
+        const int64_t edge = sd.order[p];
+        const bool mv = a.mask_triple[edge] != 0;
+        *m = mv ? 1.0f : 0.0f;
+        if (edge_w) {
+            const float ew = a.edge_weight[edge];
+            *m *= edge_score ? ew : 1.0f / (1.0f + expf(-ew));
+        }
+        if (drop_masked && !mv) *visible = false;
+    } else if (sd.mask_csr) {
+        *m = sd.mask_csr[p];
+        if (drop_masked && *m == 0.0f) *visible = false;
+    }
+}
 
 // Weighted order statistic over the groups' weights (flashlog.cu:26-63).
 // Groups with w > 0 count with multiplicity group_count.  When their total
@@ -100,40 +166,21 @@ __device__ __forceinline__ void group_key(const float *wdir, const Side &sd, int
     }
 }
 
-__device__ bool group_threshold(const float *wdir, const Side &sd, int64_t g0, int64_t g1, int64_t budget,
-                                WarpScratch &ws, uint32_t *thr, int64_t *keep) {
+// MSB-first radix select over 8-bit digits of n (key, count) pairs given by
+// get(j, &key, &cnt); the total of the counts must exceed the budget.  Lanes
+// with equal digits are merged with a warp match before the shared-memory
+// add, so equal weights (groups of one relation share it) do not serialize.
+template <typename Get>
+__device__ void radix_threshold(int64_t n, int64_t budget, WarpScratch &ws, Get get, uint32_t *thr, int64_t *keep) {
     const int lane = threadIdx.x & 31;
-    if (g1 - g0 <= 32) {
-        // One group per lane: every lane counts the groups at or above its own key.
-        uint32_t key, cnt;
-        group_key(wdir, sd, g0 + lane, g1, &key, &cnt);
-        const int64_t total = warp_sum(static_cast<int64_t>(cnt));
-        if (total <= budget) return false;
-        int64_t ge = 0, gt = 0;
-#pragma unroll 8
-        for (int j = 0; j < 32; ++j) {
-            const uint32_t kj = __shfl_sync(kFull, key, j);
-            const int64_t cj = __shfl_sync(kFull, cnt, j);
-            ge += kj >= key ? cj : 0;
-            gt += kj > key ? cj : 0;
-        }
-        const unsigned q = __ballot_sync(kFull, cnt > 0u && gt < budget && ge >= budget);
-        const int src = __ffs(q) - 1;
-        *thr = __shfl_sync(kFull, key, src);
-        *keep = budget - __shfl_sync(kFull, gt, src);
-        return true;
-    }
-    // MSB-first radix select over 8-bit digits.  Lanes with equal digits are
-    // merged with a warp match before the shared-memory add, so equal weights
-    // (common: groups of one relation share it) do not serialize.
     uint32_t prefix = 0, pmask = 0;
     int64_t krem = budget;
     for (int shift = 24; shift >= 0; shift -= 8) {
         for (int d = lane; d < 256; d += 32) ws.hist[d] = 0;
         __syncwarp();
-        for (int64_t cb = g0; cb < g1; cb += 32) {
+        for (int64_t cb = 0; cb < n; cb += 32) {
             uint32_t key, cnt;
-            group_key(wdir, sd, cb + lane, g1, &key, &cnt);
+            get(cb + lane, &key, &cnt);
             const bool part = cnt > 0u && (key & pmask) == prefix;
             const unsigned act = __ballot_sync(kFull, part);
             if (part) {
@@ -149,7 +196,6 @@ __device__ bool group_threshold(const float *wdir, const Side &sd, int64_t g0, i
 #pragma unroll
         for (int k = 0; k < 8; ++k) part += ws.hist[255 - (lane * 8 + k)];
         const int64_t incl = warp_inclusive_scan(part);
-        if (shift == 24 && __shfl_sync(kFull, incl, 31) <= budget) return false;
         const int64_t excl = incl - part;
         const unsigned ball = __ballot_sync(kFull, incl >= krem && excl < krem);
         const int src_lane = __ffs(ball) - 1;  // exactly one lane crosses krem
@@ -173,26 +219,69 @@ __device__ bool group_threshold(const float *wdir, const Side &sd, int64_t g0, i
     }
     *thr = prefix;
     *keep = krem;
-    return true;
 }
 
-struct ExpandArgs {
-    const int64_t *row_ptr;
-    const int32_t *ent;
-    const float *val;
-    int64_t S, rows, n, r_size, topk, flags, seed, L, capacity;
-    int32_t *status;
-    const float *w;
-    Side ori, inv;
-    const uint8_t *mask_triple;
-    const float *edge_weight;
-    const int64_t *slot_base;
-    int32_t *fact_dst;
-    float *fact_val;
-    int16_t *fact_rel;
-    float *fact_m;
-    int32_t *entry_count;
-};
+// Threshold of one side of one entry, computed by a whole warp.  With `stg`
+// the side's keys and clamped counts are left in stg for the take pass and
+// *staged is set.
+__device__ bool group_threshold(const float *wdir, const Side &sd, int64_t g0, int64_t g1, int64_t budget,
+                                WarpScratch &ws, StageBuf *stg, bool *staged, uint32_t *thr, int64_t *keep) {
+    const int lane = threadIdx.x & 31;
+    *staged = false;
+    if (g1 - g0 <= 32) {
+        // One group per lane: every lane counts the groups at or above its own key.
+        uint32_t key, cnt;
+        group_key(wdir, sd, g0 + lane, g1, &key, &cnt);
+        const int64_t total = warp_sum(static_cast<int64_t>(cnt));
+        if (total <= budget) return false;
+        int64_t ge = 0, gt = 0;
+#pragma unroll 8
+        for (int j = 0; j < 32; ++j) {
+            const uint32_t kj = __shfl_sync(kFull, key, j);
+            const int64_t cj = __shfl_sync(kFull, cnt, j);
+            ge += kj >= key ? cj : 0;
+            gt += kj > key ? cj : 0;
+        }
+        const unsigned q = __ballot_sync(kFull, cnt > 0u && gt < budget && ge >= budget);
+        const int src = __ffs(q) - 1;
+        *thr = __shfl_sync(kFull, key, src);
+        *keep = budget - __shfl_sync(kFull, gt, src);
+        return true;
+    }
+    const int64_t n = g1 - g0;
+    if (stg != nullptr && n <= kStage && budget < 65536) {
+        int64_t total = 0;
+#pragma unroll 4
+        for (int64_t cb = 0; cb < n; cb += 32) {
+            uint32_t key, cnt;
+            group_key(wdir, sd, g0 + cb + lane, g1, &key, &cnt);
+            if (cb + lane < n) {
+                stg->key[cb + lane] = key;
+                stg->cnt[cb + lane] = static_cast<uint16_t>(cnt < budget ? cnt : budget);
+            }
+            total += cnt;
+        }
+        __syncwarp();
+        *staged = true;
+        if (warp_sum(total) <= budget) return false;
+        radix_threshold(n, budget, ws, [&](int64_t j, uint32_t *key, uint32_t *cnt) {
+            *key = j < n ? stg->key[j] : 0u;
+            *cnt = j < n ? stg->cnt[j] : 0u;
+        }, thr, keep);
+        return true;
+    }
+    int64_t total = 0;
+    for (int64_t cb = g0; cb < g1; cb += 32) {
+        uint32_t key, cnt;
+        group_key(wdir, sd, cb + lane, g1, &key, &cnt);
+        total += cnt;
+    }
+    if (warp_sum(total) <= budget) return false;
+    radix_threshold(n, budget, ws, [&](int64_t j, uint32_t *key, uint32_t *cnt) {
+        group_key(wdir, sd, g0 + j, g1, key, cnt);
+    }, thr, keep);
+    return true;
+}
 
 __device__ __forceinline__ double splitmix_phase(int64_t seed, int64_t b, int64_t l, int64_t src, bool inv) {
     uint64_t z = static_cast<uint64_t>(seed) ^ (static_cast<uint64_t>(b) * 0x9e3779b97f4a7c15ULL) ^
@@ -205,80 +294,103 @@ __device__ __forceinline__ double splitmix_phase(int64_t seed, int64_t b, int64_
     return static_cast<double>(z >> 11) * 0x1.0p-53;
 }
 
+// One source entry expanded by a whole warp: ori groups, inv groups, identity.
 template <bool kSampled>
-__global__ void __launch_bounds__(kExpandWarps * 32, kSampled ? 3 : 4) hop_expand_kernel(ExpandArgs a) {
-    __shared__ WarpScratch scratch[kExpandWarps];
-    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-    WarpScratch &ws = scratch[wib];
-    const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kExpandWarps;
+__device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, StageBuf *stg, int64_t i) {
+    const int lane = threadIdx.x & 31;
     const bool skip_nonpos = (a.flags & FL_SKIP_NONPOS_W) != 0;
     const bool drop_masked = (a.flags & FL_DROP_MASKED) != 0;
     const bool edge_w = (a.flags & FL_EDGE_WEIGHT) != 0 && a.edge_weight != nullptr;
     const bool edge_score = (a.flags & FL_EDGE_SCORE) != 0;
     const bool wot_i = (a.flags & FL_WOT_I) != 0;
-    const int64_t S_live = a.row_ptr[a.rows] < a.S ? a.row_ptr[a.rows] : a.S;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * kExpandWarps + wib; i < S_live; i += nwarps) {
-        if (a.capacity > 0 && a.slot_base[i + 1] > a.capacity) {  // would write past the fact buffers
-            if (lane == 0) { a.entry_count[i] = 0; if (a.status) atomicOr(a.status, FL_STATUS_SLOT_OVERFLOW); }
-            continue;
-        }
-        const int64_t row = find_row(a.row_ptr, a.rows, i);
-        const int64_t src = a.ent[i];
-        const float v = a.val[i];
-        const float *wrow = a.w + row * a.n;
-        const int64_t out = a.slot_base[i];
-        int64_t written = 0;
-        for (int dir = 0; dir < 2; ++dir) {
-            const Side &sd = dir ? a.inv : a.ori;
-            const int64_t off = dir ? a.r_size : 0;
-            const float *wdir = wrow + off;
-            const int64_t g0 = sd.gptr[src], g1 = sd.gptr[src + 1];
-            if (g0 == g1) continue;
-            bool use_thr = false;
-            uint32_t thr = 0;
-            int64_t keep_thr = 0;
-            // sampled-mode state (lane 0 only)
-            int64_t q_target = 0, q_residual = 0, q_spare = 0, q_left = 0, q_capleft = 0, q_prefix = 0;
-            double q_wsum = 0.0, q_phase = 0.0;
-            if constexpr (kSampled) {
-                if (lane == 0) {
-                    int64_t capacity = 0;
-                    double wsum = 0.0;
+    if (a.capacity > 0 && a.slot_base[i + 1] > a.capacity) {  // would write past the fact buffers
+        if (lane == 0) { a.entry_count[i] = 0; if (a.status) atomicOr(a.status, FL_STATUS_SLOT_OVERFLOW); }
+        return;
+    }
+    const int64_t row = a.entry_row ? static_cast<int64_t>(a.entry_row[i]) : find_row(a.row_ptr, a.rows, i);
+    const int64_t src = a.ent[i];
+    const float v = a.val[i];
+    const float *wrow = a.w + row * a.n;
+    const int64_t out = a.slot_base[i];
+    int64_t written = 0;
+    for (int dir = 0; dir < 2; ++dir) {
+        const Side &sd = dir ? a.inv : a.ori;
+        const uint8_t *vis = dir ? a.vis_inv : a.vis_ori;
+        const int64_t off = dir ? a.r_size : 0;
+        const float *wdir = wrow + off;
+        const int64_t g0 = sd.gptr[src], g1 = sd.gptr[src + 1];
+        if (g0 == g1) continue;
+        bool use_thr = false, staged = false;
+        uint32_t thr = 0;
+        int64_t keep_thr = 0;
+        // sampled-mode state (lane 0 only)
+        int64_t q_target = 0, q_residual = 0, q_spare = 0, q_left = 0, q_capleft = 0, q_prefix = 0;
+        double q_wsum = 0.0, q_phase = 0.0;
+        if constexpr (kSampled) {
+            if (lane == 0) {
+                int64_t capacity = 0;
+                double wsum = 0.0;
+                for (int64_t g = g0; g < g1; ++g) {
+                    double wt = wdir[sd.grel[g]];
+                    if (wt > 0 && sd.gcount[g] > 0) { capacity += sd.gcount[g]; wsum += wt; }
+                }
+                q_target = a.topk < capacity ? a.topk : capacity;
+                q_wsum = wsum;
+                int64_t allocated = capacity;
+                if (q_target < capacity) {
+                    allocated = 0;
                     for (int64_t g = g0; g < g1; ++g) {
                         double wt = wdir[sd.grel[g]];
-                        if (wt > 0 && sd.gcount[g] > 0) { capacity += sd.gcount[g]; wsum += wt; }
+                        int64_t c = sd.gcount[g];
+                        if (wt > 0 && c > 0)
+                            allocated += static_cast<int64_t>(fmin(static_cast<double>(c),
+                                                                   floor(static_cast<double>(q_target) * wt / wsum)));
                     }
-                    q_target = a.topk < capacity ? a.topk : capacity;
-                    q_wsum = wsum;
-                    int64_t allocated = capacity;
-                    if (q_target < capacity) {
-                        allocated = 0;
-                        for (int64_t g = g0; g < g1; ++g) {
-                            double wt = wdir[sd.grel[g]];
-                            int64_t c = sd.gcount[g];
-                            if (wt > 0 && c > 0)
-                                allocated += static_cast<int64_t>(fmin(static_cast<double>(c),
-                                                                       floor(static_cast<double>(q_target) * wt / wsum)));
-                        }
-                    }
-                    q_residual = q_target - allocated;
-                    q_spare = capacity - allocated;
-                    q_left = q_residual;
-                    q_capleft = q_spare;
-                    q_phase = splitmix_phase(a.seed, row / a.L, row % a.L, src, dir == 1);
-                    q_prefix = 0;
                 }
-            } else if (skip_nonpos && a.topk < kNoBudget) {
-                use_thr = group_threshold(wdir, sd, g0, g1, a.topk, ws, &thr, &keep_thr);
+                q_residual = q_target - allocated;
+                q_spare = capacity - allocated;
+                q_left = q_residual;
+                q_capleft = q_spare;
+                q_phase = splitmix_phase(a.seed, row / a.L, row % a.L, src, dir == 1);
+                q_prefix = 0;
             }
-            int64_t tie_seen = 0;
-            for (int64_t cb = g0; cb < g1; cb += 32) {
-                const int64_t g = cb + lane;
-                const bool valid = g < g1;
-                int32_t rel = valid ? sd.grel[g] : 0;
-                int32_t cnt = valid ? sd.gcount[g] : 0;
-                float wg = valid ? wdir[rel] : 0.0f;
-                int32_t take;
+        } else if (skip_nonpos && a.topk < kNoBudget) {
+            use_thr = group_threshold(wdir, sd, g0, g1, a.topk, ws, stg, &staged, &thr, &keep_thr);
+        }
+        int64_t tie_seen = 0;
+        for (int64_t cb = g0; cb < g1; cb += 32) {
+            const int64_t g = cb + lane;
+            const bool valid = g < g1;
+            int32_t take;
+            int32_t rel = 0;
+            float wg = 0.0f;
+            if (!kSampled && staged) {
+                // keys and clamped counts from the staging buffer; global
+                // group data only for groups that take edges
+                const uint32_t key = valid ? stg->key[g - g0] : 0u;
+                const int32_t cnt = valid ? stg->cnt[g - g0] : 0;
+                const bool pos = key != 0u;
+                if (!use_thr) {
+                    take = pos ? cnt : 0;
+                } else {
+                    const bool tie = valid && pos && key == thr;
+                    const int64_t tcnt = tie ? cnt : 0;
+                    const int64_t tincl = warp_inclusive_scan(tcnt);
+                    const int64_t texcl = tincl - tcnt + tie_seen;
+                    tie_seen += __shfl_sync(kFull, tincl, 31);
+                    if (!pos || key < thr) take = 0;
+                    else if (key > thr) take = cnt;
+                    else {
+                        const int64_t left = keep_thr - texcl;
+                        take = left > 0 ? static_cast<int32_t>(left < cnt ? left : cnt) : 0;
+                    }
+                }
+                if (!valid) take = 0;
+                if (take > 0) { rel = sd.grel[g]; wg = __uint_as_float(key); }
+            } else {
+                rel = valid ? sd.grel[g] : 0;
+                const int32_t cnt = valid ? sd.gcount[g] : 0;
+                wg = valid ? wdir[rel] : 0.0f;
                 if constexpr (kSampled) {
                     // Sequential quota arithmetic of flashlog.cu:1505-1531, lane 0.
                     ws.rel[lane] = rel;
@@ -331,68 +443,226 @@ __global__ void __launch_bounds__(kExpandWarps * 32, kSampled ? 3 : 4) hop_expan
                     }
                 }
                 if (!valid) take = 0;
-                int32_t incl = warp_inclusive_scan(take);
-                int32_t tot = __shfl_sync(kFull, incl, 31);
-                ws.incl[lane] = incl;
-                ws.start[lane] = valid ? sd.gstart[g] : 0;
-                ws.prod[lane] = v * wg;
-                ws.rel[lane] = rel + static_cast<int32_t>(off);
-                __syncwarp();
-                for (int32_t f0 = 0; f0 < tot; f0 += 32) {
-                    const int32_t f = f0 + lane;
-                    const bool act = f < tot;
-                    bool visible = false;
-                    int32_t dst = 0, frel = 0;
-                    float value = 0.0f, m = 1.0f;
-                    if (act) {
-                        int lo = 0, hi = 31;  // first lane with incl > f
-                        while (lo < hi) { int mid = (lo + hi) >> 1; if (ws.incl[mid] > f) hi = mid; else lo = mid + 1; }
-                        const int32_t eoff = f - (lo ? ws.incl[lo - 1] : 0);
-                        const int64_t p = static_cast<int64_t>(ws.start[lo]) + eoff;
-                        visible = true;
-                        if (a.mask_triple) {
-                            const int64_t edge = sd.order[p];
-                            const bool mv = a.mask_triple[edge] != 0;
-                            m = mv ? 1.0f : 0.0f;
-                            if (edge_w) {
-                                float ew = a.edge_weight[edge];
-                                m *= edge_score ? ew : 1.0f / (1.0f + expf(-ew));
-                            }
-                            if (drop_masked && !mv) visible = false;
-                        } else if (sd.mask_csr) {
-                            m = sd.mask_csr[p];
-                            if (drop_masked && m == 0.0f) visible = false;
-                        }
-                        dst = sd.col[p];
-                        value = ws.prod[lo] * m;
-                        frel = ws.rel[lo];
-                    }
-                    const unsigned ball = __ballot_sync(kFull, act && visible);
-                    if (act && visible) {
-                        const int64_t pos = out + written + __popc(ball & lanemask_lt());
-                        a.fact_dst[pos] = dst;
-                        a.fact_val[pos] = value;
-                        a.fact_rel[pos] = static_cast<int16_t>(frel);
-                        if (a.fact_m) a.fact_m[pos] = m;
-                    }
-                    written += __popc(ball);
+            }
+            int32_t incl = warp_inclusive_scan(take);
+            int32_t tot = __shfl_sync(kFull, incl, 31);
+            if (tot == 0) continue;
+            ws.incl[lane] = incl;
+            ws.start[lane] = take > 0 ? sd.gstart[g] : 0;
+            ws.prod[lane] = v * wg;
+            ws.rel[lane] = rel + static_cast<int32_t>(off);
+            __syncwarp();
+            for (int32_t f0 = 0; f0 < tot; f0 += 32) {
+                const int32_t f = f0 + lane;
+                const bool act = f < tot;
+                bool visible = false;
+                int32_t dst = 0, frel = 0;
+                float value = 0.0f, m = 1.0f;
+                if (act) {
+                    int lo = 0, hi = 31;  // first lane with incl > f
+                    while (lo < hi) { int mid = (lo + hi) >> 1; if (ws.incl[mid] > f) hi = mid; else lo = mid + 1; }
+                    const int32_t eoff = f - (lo ? ws.incl[lo - 1] : 0);
+                    const int64_t p = static_cast<int64_t>(ws.start[lo]) + eoff;
+                    fact_mask(a, sd, vis, p, drop_masked, edge_w, edge_score, &m, &visible);
+                    dst = sd.col[p];
+                    value = ws.prod[lo] * m;
+                    frel = ws.rel[lo];
                 }
-                __syncwarp();
+                const unsigned ball = __ballot_sync(kFull, act && visible);
+                if (act && visible) {
+                    const int64_t pos = out + written + __popc(ball & lanemask_lt());
+                    a.fact_dst[pos] = dst;
+                    a.fact_val[pos] = value;
+                    a.fact_rel[pos] = static_cast<int16_t>(frel);
+                    if (a.fact_m) a.fact_m[pos] = m;
+                }
+                written += __popc(ball);
+            }
+            __syncwarp();
+        }
+    }
+    if (!wot_i) {
+        if (lane == 0) {
+            const int64_t pos = out + written;
+            a.fact_dst[pos] = static_cast<int32_t>(src);
+            a.fact_val[pos] = v * wrow[a.n - 1];
+            a.fact_rel[pos] = static_cast<int16_t>(a.n - 1);
+            if (a.fact_m) a.fact_m[pos] = 1.0f;
+        }
+        written += 1;
+    }
+    if (lane == 0) a.entry_count[i] = static_cast<int32_t>(written);
+    // Slots the entry reserved but did not fill get the destination -1.
+    for (int64_t s = out + written + lane; s < a.slot_base[i + 1]; s += 32) a.fact_dst[s] = -1;
+}
+
+// Sampled c2: one warp per entry.
+__global__ void __launch_bounds__(kExpandWarps * 32, 3) hop_expand_sampled_kernel(ExpandArgs a) {
+    __shared__ WarpScratch scratch[kExpandWarps];
+    const int wib = threadIdx.x >> 5;
+    const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kExpandWarps;
+    const int64_t S_live = a.row_ptr[a.rows] < a.S ? a.row_ptr[a.rows] : a.S;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * kExpandWarps + wib; i < S_live; i += nwarps)
+        expand_entry_warp<true>(a, scratch[wib], nullptr, i);
+}
+
+// One side of one entry expanded by an 8-lane team (at most kTeam groups):
+// one group per lane, the threshold by all-pairs comparison, then the taken
+// edges kTeam at a time.  Returns the updated fact count of the entry.
+__device__ __forceinline__ int64_t team_side(const ExpandArgs &a, const Side &sd, const uint8_t *vis,
+                                             const float *wdir, int32_t off, float v, int64_t g0, int64_t g1,
+                                             unsigned tm, int tl, int tbase, int64_t out, int64_t written,
+                                             bool skip_nonpos, bool drop_masked, bool edge_w, bool edge_score) {
+    const bool valid = tl < (g1 - g0);
+    const int64_t g = g0 + tl;
+    const int32_t rel = valid ? sd.grel[g] : 0;
+    const int32_t cnt = valid ? sd.gcount[g] : 0;
+    const int32_t start = valid ? sd.gstart[g] : 0;
+    const float wg = valid ? wdir[rel] : 0.0f;
+    int32_t take;
+    if (!skip_nonpos) {
+        take = cnt;
+    } else {
+        const bool pos = wg > 0.0f;
+        const int64_t c = pos ? cnt : 0;
+        int64_t total = c;
+#pragma unroll
+        for (int o = 1; o < kTeam; o <<= 1) total += __shfl_xor_sync(tm, total, o, kTeam);
+        if (a.topk >= kNoBudget || total <= a.topk) {
+            take = pos ? cnt : 0;
+        } else {
+            const uint32_t key = pos ? __float_as_uint(wg) : 0u;
+            int64_t ge = 0, gt = 0;
+#pragma unroll
+            for (int j = 0; j < kTeam; ++j) {
+                const uint32_t kj = __shfl_sync(tm, key, j, kTeam);
+                const int64_t cj = __shfl_sync(tm, c, j, kTeam);
+                ge += kj >= key ? cj : 0;
+                gt += kj > key ? cj : 0;
+            }
+            const unsigned q = (__ballot_sync(tm, c > 0 && gt < a.topk && ge >= a.topk) >> tbase) & 0xffu;
+            const int srcl = __ffs(q) - 1;  // one lane holds the threshold key when the total exceeds the budget
+            const uint32_t thr = __shfl_sync(tm, key, srcl, kTeam);
+            const int64_t keep = a.topk - __shfl_sync(tm, gt, srcl, kTeam);
+            // ties at the threshold are taken in group order
+            const int64_t tc = (pos && key == thr) ? c : 0;
+            int64_t tincl = tc;
+#pragma unroll
+            for (int o = 1; o < kTeam; o <<= 1) {
+                const int64_t u = __shfl_up_sync(tm, tincl, o, kTeam);
+                if (tl >= o) tincl += u;
+            }
+            const int64_t texcl = tincl - tc;
+            if (!pos || key < thr) take = 0;
+            else if (key > thr) take = cnt;
+            else {
+                const int64_t left = keep - texcl;
+                take = left > 0 ? static_cast<int32_t>(left < cnt ? left : cnt) : 0;
             }
         }
-        if (!wot_i) {
-            if (lane == 0) {
-                const int64_t pos = out + written;
-                a.fact_dst[pos] = static_cast<int32_t>(src);
-                a.fact_val[pos] = v * wrow[a.n - 1];
-                a.fact_rel[pos] = static_cast<int16_t>(a.n - 1);
-                if (a.fact_m) a.fact_m[pos] = 1.0f;
-            }
-            written += 1;
+    }
+    int32_t incl = take;
+#pragma unroll
+    for (int o = 1; o < kTeam; o <<= 1) {
+        const int32_t u = __shfl_up_sync(tm, incl, o, kTeam);
+        if (tl >= o) incl += u;
+    }
+    const int32_t tot = __shfl_sync(tm, incl, kTeam - 1, kTeam);
+    const float prod = v * wg;
+    for (int32_t f0 = 0; f0 < tot; f0 += kTeam) {
+        const int32_t f = f0 + tl;
+        const bool act = f < tot;
+        int k = 0;  // the group holding fact f: lanes whose inclusive count is <= f
+#pragma unroll
+        for (int j = 0; j < kTeam; ++j) k += (__shfl_sync(tm, incl, j, kTeam) <= f) ? 1 : 0;
+        k = k < kTeam ? k : kTeam - 1;
+        const int32_t prev = __shfl_sync(tm, incl, k > 0 ? k - 1 : 0, kTeam);
+        const int32_t sk = __shfl_sync(tm, start, k, kTeam);
+        const float pk = __shfl_sync(tm, prod, k, kTeam);
+        const int32_t rk = __shfl_sync(tm, rel, k, kTeam);
+        bool visible = false;
+        int32_t dst = 0;
+        float value = 0.0f, m = 1.0f;
+        if (act) {
+            const int64_t p = static_cast<int64_t>(sk) + (f - (k > 0 ? prev : 0));
+            fact_mask(a, sd, vis, p, drop_masked, edge_w, edge_score, &m, &visible);
+            dst = sd.col[p];
+            value = pk * m;
         }
-        if (lane == 0) a.entry_count[i] = static_cast<int32_t>(written);
-        // Slots the entry reserved but did not fill get the destination -1.
-        for (int64_t s = out + written + lane; s < a.slot_base[i + 1]; s += 32) a.fact_dst[s] = -1;
+        const unsigned ball = (__ballot_sync(tm, act && visible) >> tbase) & 0xffu;
+        if (act && visible) {
+            const int64_t pos = out + written + __popc(ball & ((1u << tl) - 1u));
+            a.fact_dst[pos] = dst;
+            a.fact_val[pos] = value;
+            a.fact_rel[pos] = static_cast<int16_t>(rk + off);
+            if (a.fact_m) a.fact_m[pos] = m;
+        }
+        written += __popc(ball);
+    }
+    return written;
+}
+
+// Deterministic c2 (and the all-edges path): four entries per warp in 8-lane
+// teams; entries with more than kTeam groups on a side go to the whole warp.
+__global__ void __launch_bounds__(kExpandWarps * 32, 3) hop_expand_kernel(ExpandArgs a) {
+    __shared__ WarpScratch scratch[kExpandWarps];
+    extern __shared__ __align__(16) unsigned char stage_raw[];
+    StageBuf *stage = reinterpret_cast<StageBuf *>(stage_raw);
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int team = lane / kTeam, tl = lane % kTeam, tbase = team * kTeam;
+    const unsigned tm = 0xffu << tbase;
+    const bool skip_nonpos = (a.flags & FL_SKIP_NONPOS_W) != 0;
+    const bool drop_masked = (a.flags & FL_DROP_MASKED) != 0;
+    const bool edge_w = (a.flags & FL_EDGE_WEIGHT) != 0 && a.edge_weight != nullptr;
+    const bool edge_score = (a.flags & FL_EDGE_SCORE) != 0;
+    const bool wot_i = (a.flags & FL_WOT_I) != 0;
+    const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kExpandWarps;
+    const int64_t S_live = a.row_ptr[a.rows] < a.S ? a.row_ptr[a.rows] : a.S;
+    for (int64_t base = (static_cast<int64_t>(blockIdx.x) * kExpandWarps + wib) * 4; base < S_live;
+         base += nwarps * 4) {
+        const int64_t i = base + team;
+        const bool mine = i < S_live;
+        bool small = false, over = false;
+        int64_t src = 0, g0o = 0, g1o = 0, g0i = 0, g1i = 0;
+        if (mine) {
+            over = a.capacity > 0 && a.slot_base[i + 1] > a.capacity;
+            src = a.ent[i];
+            g0o = a.ori.gptr[src]; g1o = a.ori.gptr[src + 1];
+            g0i = a.inv.gptr[src]; g1i = a.inv.gptr[src + 1];
+            small = !over && (g1o - g0o) <= kTeam && (g1i - g0i) <= kTeam;
+        }
+        if (small) {
+            const int64_t row = a.entry_row ? static_cast<int64_t>(a.entry_row[i]) : find_row(a.row_ptr, a.rows, i);
+            const float v = a.val[i];
+            const float *wrow = a.w + row * a.n;
+            const int64_t out = a.slot_base[i], end = a.slot_base[i + 1];
+            int64_t written = 0;
+            if (g1o > g0o)
+                written = team_side(a, a.ori, a.vis_ori, wrow, 0, v, g0o, g1o, tm, tl, tbase, out, written,
+                                    skip_nonpos, drop_masked, edge_w, edge_score);
+            if (g1i > g0i)
+                written = team_side(a, a.inv, a.vis_inv, wrow + a.r_size, static_cast<int32_t>(a.r_size), v, g0i, g1i,
+                                    tm, tl, tbase, out, written, skip_nonpos, drop_masked, edge_w, edge_score);
+            if (!wot_i) {
+                if (tl == 0) {
+                    const int64_t pos = out + written;
+                    a.fact_dst[pos] = static_cast<int32_t>(src);
+                    a.fact_val[pos] = v * wrow[a.n - 1];
+                    a.fact_rel[pos] = static_cast<int16_t>(a.n - 1);
+                    if (a.fact_m) a.fact_m[pos] = 1.0f;
+                }
+                written += 1;
+            }
+            if (tl == 0) a.entry_count[i] = static_cast<int32_t>(written);
+            for (int64_t s = out + written + tl; s < end; s += kTeam) a.fact_dst[s] = -1;
+        }
+        __syncwarp();
+        unsigned big = __ballot_sync(kFull, mine && !small && tl == 0);
+        while (big) {
+            const int t = (__ffs(big) - 1) / kTeam;
+            big &= big - 1;
+            expand_entry_warp<false>(a, scratch[wib], stage + wib, base + t);
+        }
     }
 }
 
@@ -544,12 +814,14 @@ __device__ uint16_t *lsd_sort(const uint32_t *key, uint16_t *idx0, uint16_t *idx
 
 // Emit a sorted tile: positions [0, n) of perm, keys key[perm[p]] ascending
 // (destination = lo + key).  Each destination's facts are summed in
-// permutation order (canonical order).  Outputs go to the row's output index
-// *written onwards; slot_of(i) is the row-local slot of tile element i.
-// Returns the block sum of the emitted values.
+// permutation order (canonical order), left to right.  Outputs go to the
+// row's output index *written onwards; slot_of(i) is the row-local slot of
+// tile element i.  `segs` (n 16-bit entries, free during the emit) gets the
+// segment starts.  Returns the block sum of the emitted values.
 template <typename SlotOf>
 __device__ float emit_tile(const ReduceArgs &a, ReduceSmem &sm, const uint32_t *key, const float *val,
-                           const uint16_t *perm, int n, int64_t lo, int64_t s0, int64_t *written, SlotOf slot_of) {
+                           const uint16_t *perm, uint16_t *segs, int n, int64_t lo, int64_t s0, int64_t *written,
+                           SlotOf slot_of) {
     const int per = (n + kRThreads - 1) / kRThreads;
     const int p0 = threadIdx.x * per;
     const int p1 = (p0 + per) < n ? (p0 + per) : n;
@@ -562,30 +834,67 @@ __device__ float emit_tile(const ReduceArgs &a, ReduceSmem &sm, const uint32_t *
     }
     int64_t tot;
     const int64_t ex = block_exclusive_scan<int64_t>(heads, sm.scan_scratch, &tot);
-    int64_t oi = *written + ex - 1;
-    float local = 0.0f;
+    // every position: its output index into fact_pos; heads: segment starts
+    int oi = static_cast<int>(ex) - 1;
     prev = p0 > 0 && p0 < n ? key[perm[p0 - 1]] : 0xffffffffu;
     for (int p = p0; p < p1; ++p) {
-        const uint32_t k = key[perm[p]];
-        const bool head = p == 0 || k != prev;
+        const uint16_t i = perm[p];
+        const uint32_t k = key[i];
+        if (p == 0 || k != prev) { ++oi; segs[oi] = static_cast<uint16_t>(p); }
         prev = k;
-        if (!head) continue;
-        ++oi;
+        if (a.fact_pos) a.fact_pos[s0 + slot_of(i)] = static_cast<int32_t>(*written + oi);
+    }
+    const int nseg = static_cast<int>(tot);
+    __syncthreads();
+    float local = 0.0f;
+    for (int sgi = threadIdx.x; sgi < nseg; sgi += kRThreads) {
+        const int st = segs[sgi];
+        const int en = sgi + 1 < nseg ? segs[sgi + 1] : n;
         float x = 0.0f;
-        int q = p;
-        for (; q < n; ++q) {
-            const uint16_t i = perm[q];
-            if (key[i] != k) break;
-            x += val[i];
+        int q = st;
+        for (; q + 4 <= en; q += 4) {  // loads issued ahead of the dependent adds
+            const float v0 = val[perm[q]], v1 = val[perm[q + 1]], v2 = val[perm[q + 2]], v3 = val[perm[q + 3]];
+            x += v0;
+            x += v1;
+            x += v2;
+            x += v3;
         }
-        a.tmp_ent[s0 + oi] = static_cast<int32_t>(lo + k);
-        a.tmp_x[s0 + oi] = x;
-        if (a.fact_pos)
-            for (int q2 = p; q2 < q; ++q2) a.fact_pos[s0 + slot_of(perm[q2])] = static_cast<int32_t>(oi);
+        for (; q < en; ++q) x += val[perm[q]];
+        const int64_t o = *written + sgi;
+        a.tmp_ent[s0 + o] = static_cast<int32_t>(lo + key[perm[st]]);
+        a.tmp_x[s0 + o] = x;
         local += x;
     }
     *written += tot;
     return block_sum(local, sm.fscratch);
+}
+
+// Stable sort of a tiny tile (n <= kRankSortMax): rank of element i among
+// the (key, position) pairs, one pass.
+constexpr int kRankSortMax = 128;
+__device__ uint16_t *rank_sort(const uint32_t *key, uint16_t *out, int n) {
+    for (int i = threadIdx.x; i < n; i += kRThreads) {
+        const uint32_t ki = key[i];
+        int r = 0;
+        for (int j = 0; j < n; ++j) {
+            const uint32_t kj = key[j];
+            r += (kj < ki || (kj == ki && j < i)) ? 1 : 0;
+        }
+        out[r] = static_cast<uint16_t>(i);
+    }
+    __syncthreads();
+    return out;
+}
+
+// Sort a loaded tile (idx0 = identity) by key; returns the permutation and
+// the other 16-bit buffer in *spare.
+__device__ uint16_t *sort_tile(const uint32_t *key, uint16_t *idx0, uint16_t *idx1, int n, int bits, ReduceSmem &sm,
+                               uint16_t **spare) {
+    uint16_t *perm;
+    if (n <= kRankSortMax) perm = rank_sort(key, idx1, n);
+    else perm = lsd_sort(key, idx0, idx1, n, bits, sm);
+    *spare = perm == idx0 ? idx1 : idx0;
+    return perm;
 }
 
 // Load, in canonical order, the facts of the row's slot range whose
@@ -648,7 +957,8 @@ __device__ float dense_window(const ReduceArgs &a, ReduceSmem &sm, int64_t s0, i
         const int n = load_range(a, sm, s0, ns, from, lo, hi, t.key, t.val, t.slot, t.idx[0], 0, kTileD, &next);
         from = next;
         if (n == 0) continue;
-        const uint16_t *perm = lsd_sort(t.key, t.idx[0], t.idx[1], n, bits, sm);
+        uint16_t *spare;
+        const uint16_t *perm = sort_tile(t.key, t.idx[0], t.idx[1], n, bits, sm, &spare);
         const int per = (n + kRThreads - 1) / kRThreads;
         const int p0 = threadIdx.x * per;
         const int p1 = (p0 + per) < n ? (p0 + per) : n;
@@ -723,8 +1033,10 @@ __global__ void __launch_bounds__(kRThreads, 1) row_reduce_kernel(ReduceArgs a) 
         }
         const int n = static_cast<int>(block_sum<int64_t>(valid, sm.scan_scratch));
         if (n > 0) {
-            const uint16_t *perm = lsd_sort(t.key, t.idx[0], t.idx[1], static_cast<int>(ns), bits_for(a.E + 1), sm);
-            rsum = emit_tile(a, sm, t.key, t.val, perm, n, 0, s0, &written,
+            uint16_t *spare;
+            const uint16_t *perm = sort_tile(t.key, t.idx[0], t.idx[1], static_cast<int>(ns), bits_for(a.E + 1), sm,
+                                             &spare);
+            rsum = emit_tile(a, sm, t.key, t.val, perm, spare, n, 0, s0, &written,
                              [](uint16_t i) { return static_cast<uint32_t>(i); });
         }
     } else {
@@ -778,8 +1090,9 @@ __global__ void __launch_bounds__(kRThreads, 1) row_reduce_kernel(ReduceArgs a) 
                 int64_t next;
                 const int n = load_range(a, sm, s0, ns, 0, lo, hi, t.key, t.val, t.slot, t.idx[0], 0, 1 << 30,
                                          &next);  // count <= kTileB: no early stop
-                const uint16_t *perm = lsd_sort(t.key, t.idx[0], t.idx[1], n, bits_for(hi - lo), sm);
-                rsum += emit_tile(a, sm, t.key, t.val, perm, n, lo, s0, &written,
+                uint16_t *spare;
+                const uint16_t *perm = sort_tile(t.key, t.idx[0], t.idx[1], n, bits_for(hi - lo), sm, &spare);
+                rsum += emit_tile(a, sm, t.key, t.val, perm, spare, n, lo, s0, &written,
                                   [&t](uint16_t i) { return t.slot[i]; });
             } else {
                 for (int64_t wlo = lo; wlo < hi; wlo += kDenseW) {
@@ -974,6 +1287,17 @@ static Side make_side(const fl_csr_side &s, const float *mask_csr) {
     return d;
 }
 
+int csr_visibility(const int32_t *order, int64_t m, const uint8_t *mask_triple, uint8_t *vis, cudaStream_t st) {
+    if (m > 0) {
+        int64_t blocks = (m + 255) / 256;
+        const int sms = fl_device_sm_count();
+        const int64_t cap = static_cast<int64_t>(sms > 0 ? sms : 148) * 16;
+        if (blocks > cap) blocks = cap;
+        launch(csr_visibility_kernel, static_cast<unsigned>(blocks), 256, 0, st, order, m, mask_triple, vis);
+    }
+    return check_launch("csr_visibility");
+}
+
 size_t hop_workspace(int64_t rows, int64_t S) {
     size_t s = carve_bytes<int64_t>(S + 1) + scan_workspace(S > rows ? S : rows) + carve_bytes<int64_t>(rows + 1) * 3 +
                carve_bytes<float>(rows + 1);
@@ -995,7 +1319,8 @@ int hop_plan(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *ent,
     (void)row_ptr;
     if (S > 0) {
         launch(hop_capacity_kernel, static_cast<unsigned>((S + 255) / 256), 256, 0, st, ent, row_ptr, p->rows, S,
-               make_side(ori, nullptr), make_side(inv, nullptr), p->topk_edges, (p->flags & FL_WOT_I) ? 1 : 0, cap);
+               make_side(ori, nullptr), make_side(inv, nullptr), p->topk_edges, (p->flags & FL_WOT_I) ? 1 : 0, cap,
+               p->entry_row);
     }
     int rc = exclusive_scan<int64_t>(cap, S, slot_base, scan_ws, sws, st);
     if (rc) return rc;
@@ -1018,15 +1343,27 @@ int hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *en
     a.topk = p->topk_edges; a.flags = p->flags; a.seed = p->sampling_seed; a.L = p->L; a.w = w;
     a.ori = make_side(ori, mask_csr_ori); a.inv = make_side(inv, mask_csr_inv);
     a.mask_triple = mask_triple; a.edge_weight = edge_weight; a.slot_base = slot_base;
+    a.vis_ori = p->vis_ori; a.vis_inv = p->vis_inv; a.entry_row = p->entry_row;
     a.fact_dst = fact_dst; a.fact_val = fact_val; a.fact_rel = fact_rel; a.fact_m = fact_m; a.entry_count = entry_count;
-    int64_t blocks = (S + kExpandWarps - 1) / kExpandWarps;
     int sms = fl_device_sm_count();
-    int64_t cap_blocks = static_cast<int64_t>(sms > 0 ? sms : 148) * 32;
-    if (blocks > cap_blocks) blocks = cap_blocks;
-    if (p->flags & FL_SAMPLED)
-        launch(hop_expand_kernel<true>, static_cast<unsigned>(blocks), kExpandWarps * 32, 0, st, a);
-    else
-        launch(hop_expand_kernel<false>, static_cast<unsigned>(blocks), kExpandWarps * 32, 0, st, a);
+    const int64_t per_sm = 3;  // resident CTAs per SM (registers and staging buffers)
+    int64_t cap_blocks = static_cast<int64_t>(sms > 0 ? sms : 148) * per_sm * 8;
+    if (p->flags & FL_SAMPLED) {
+        int64_t blocks = (S + kExpandWarps - 1) / kExpandWarps;
+        if (blocks > cap_blocks) blocks = cap_blocks;
+        launch(hop_expand_sampled_kernel, static_cast<unsigned>(blocks), kExpandWarps * 32, 0, st, a);
+    } else {
+        int64_t blocks = (S + 4 * kExpandWarps - 1) / (4 * kExpandWarps);
+        if (blocks > cap_blocks) blocks = cap_blocks;
+        const size_t smem = sizeof(StageBuf) * kExpandWarps;
+        static bool attr_set = false;
+        if (!attr_set) {
+            FL_CUDA(cudaFuncSetAttribute(hop_expand_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem)));
+            attr_set = true;
+        }
+        launch(hop_expand_kernel, static_cast<unsigned>(blocks), kExpandWarps * 32, smem, st, a);
+    }
     return check_launch("hop_expand");
 }
 

@@ -30,7 +30,8 @@ class HopNorm(torch.autograd.Function):
     """
 
     @staticmethod
-    def forward(ctx, val, w, row_ptr, ent, graph, r_size, topk_edges, c1, flags, mask_triple, eps, stats, status):
+    def forward(ctx, val, w, row_ptr, ent, graph, r_size, topk_edges, c1, flags, mask_triple, eps, stats, status,
+                vis=None):
         v = val.detach().contiguous()
         rows = row_ptr.numel() - 1
         ctx.pruned = None
@@ -43,7 +44,7 @@ class HopNorm(torch.autograd.Function):
             ctx.sel_live = rp[rows:]
         wf = w.detach().contiguous()
         fw = ops.hop_forward(row_ptr, ent, v, wf, graph, r_size, topk_edges, flags, mask_triple=mask_triple, eps=eps,
-                             timing=None if stats is None else stats.timer, status=status, out_sync=False)
+                             timing=None if stats is None else stats.timer, status=status, out_sync=False, vis=vis)
         if stats is not None:
             stats.append((ent, row_ptr[rows:], fw.entry_count, fw.out_row_ptr[rows:]))
         ctx.fw = fw
@@ -57,7 +58,7 @@ class HopNorm(torch.autograd.Function):
         grad_v, grad_w = ops.hop_backward(ctx.fw, row_ptr, v, wf, g_y, normalize=True)
         if ctx.pruned is not None:
             grad_v = ops.scatter_grad(grad_v, ctx.pruned, ctx.n_in, n_live=ctx.sel_live)
-        return grad_v, grad_w, None, None, None, None, None, None, None, None, None, None, None
+        return grad_v, grad_w, None, None, None, None, None, None, None, None, None, None, None, None
 
 
 class Readout(torch.autograd.Function):
@@ -118,10 +119,12 @@ def drum_propagate(heads, w_all, graph: Graph, r_size: int, *, c1=None, c2=0, ma
     own_status = status is None
     if own_status:
         status = new_status(heads.device)
+    # hidden triples in CSR order, shared by the T hops
+    vis = ops.csr_visibility(graph, mask_triple) if mask_triple is not None else None
     for t in range(T):
         w_t = torch.softmax(w_all[:, t] / tau_1, dim=-1)
         val, row_ptr, ent = HopNorm.apply(val, w_t, row_ptr, ent, graph, r_size, topk, c1, flags, mask_triple, eps,
-                                          stats, status)
+                                          stats, status, vis)
     if own_status:
         check_status(status)
     return row_ptr, ent, val

@@ -203,15 +203,38 @@ class HopForward:
     fact_val: torch.Tensor | None = None
 
 
-def hop_params(rows, Lch, n, r_size, E, topk_edges, flags, seed=-1, eps=EPS, slot_capacity=0, status=None):
+def hop_params(rows, Lch, n, r_size, E, topk_edges, flags, seed=-1, eps=EPS, slot_capacity=0, status=None,
+               entry_row=None, vis=None):
     return L.fl_hop_params(rows, Lch, n, r_size, E, int(min(topk_edges, L.NO_BUDGET)), int(flags), int(seed),
-                           float(eps), int(slot_capacity), None if status is None else status.data_ptr())
+                           float(eps), int(slot_capacity), None if status is None else status.data_ptr(),
+                           None if entry_row is None else entry_row.data_ptr(),
+                           None if vis is None else vis[0].data_ptr(), None if vis is None else vis[1].data_ptr())
+
+
+def csr_visibility(graph: Graph, mask_triple):
+    """CSR-ordered visibility (u8 per edge, both sides) of a per-triple mask.
+
+    The gather of prepare_csr_masks (flashlog_kernel.py:225-255) in one byte
+    per edge; a hop given it reads visibility next to the edge instead of
+    through `order`."""
+    _require_cuda(mask_triple)
+    m = mask_triple.reshape(-1)
+    m = (m if m.dtype == torch.uint8 else (m != 0).to(torch.uint8)).contiguous()
+    M = graph.csr[1].numel()
+    if m.numel() < M:
+        raise ValueError("edge visibility mask must have one entry per triple")
+    out = []
+    for order in (graph.csr[3], graph.csr[7]):
+        v = torch.empty(M, dtype=torch.uint8, device=m.device)
+        check(lib().fl_csr_visibility(_p(order), M, _p(m), _p(v), _stream()), "csr_visibility")
+        out.append(v)
+    return tuple(out)
 
 
 def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int, flags: int, *,
                 mask_triple=None, mask_csr=None, edge_weight=None, seed: int = -1, eps: float = EPS,
                 keep_facts: bool = False, record: bool = True, timing=None, slot_capacity=None,
-                status=None, out_sync: bool = True) -> HopForward:
+                status=None, out_sync: bool = True, vis=None) -> HopForward:
     """Expansion + per-row coalesce-sum + normalization of one hop.
 
     slot_capacity=None sizes the fact buffers exactly (one host sync for the
@@ -220,7 +243,8 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
     count is out_row_ptr[-1] on the device, and work that would not fit sets
     FL_STATUS_SLOT_OVERFLOW in `status` (an int32 device tensor).  With
     out_sync=False the fact count is still read (one sync) but the outputs keep
-    that capacity and their live count stays on the device.
+    that capacity and their live count stays on the device.  `vis` (from
+    csr_visibility of the same mask) replaces the per-fact mask_triple read.
     """
     _require_cuda(row_ptr, ent, val, w)
     B, Lch, n = w.shape
@@ -236,7 +260,12 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
     slot_base = torch.empty(S + 1, dtype=torch.int64, device=dev)
     ws = _ws(lib().fl_hop_workspace(rows, S), dev)
     total = ctypes.c_int64(0)
-    params = hop_params(rows, Lch, n, r_size, graph.E, topk_edges, flags, seed, eps, slot_capacity or 0, status)
+    entry_row = torch.empty(max(S, 1), dtype=torch.int32, device=dev)
+    if vis is not None and (len(vis) != 2 or any(v.numel() < graph.csr[1].numel() or v.dtype != torch.uint8
+                                                 for v in vis)):
+        raise ValueError("vis must be the two u8 CSR-ordered visibility arrays of csr_visibility")
+    params = hop_params(rows, Lch, n, r_size, graph.E, topk_edges, flags, seed, eps, slot_capacity or 0, status,
+                        entry_row, vis)
     check(lib().fl_hop_plan(ctypes.byref(params), _p(row_ptr), _p(ent), S, graph.ori, graph.inv, _p(slot_base),
                             ctypes.byref(total) if sync else None, _p(ws), ws.numel(), _stream()), "hop_plan")
     T = max(total.value, 1) if sync else max(int(slot_capacity), 1)
@@ -249,7 +278,7 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
     # anything but 1: soft edge weights, CSR-ordered float masks, or hidden
     # edges kept as zero-valued facts.
     need_m = bool(flags & L.FL_EDGE_WEIGHT) or mask_csr is not None or (
-        mask_triple is not None and not (flags & L.FL_DROP_MASKED))
+        (mask_triple is not None or vis is not None) and not (flags & L.FL_DROP_MASKED))
     fact_m = torch.empty(T, dtype=torch.float32, device=dev) if need_m else None
     entry_count = torch.empty(max(S, 1), dtype=torch.int32, device=dev)
     mo = mi = None
@@ -267,11 +296,6 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
         edge_weight = edge_weight.reshape(-1).to(torch.float32).contiguous()
         if edge_weight.numel() < M:
             raise ValueError("edge weights must have one entry per triple")
-    if timing is not None:
-        timing.record_start()
-    check(lib().fl_hop_expand(ctypes.byref(params), _p(row_ptr), _p(ent), _p(val), S, _p(w), graph.ori, graph.inv,
-                              _p(mo), _p(mi), _p(mask_triple), _p(edge_weight), _p(slot_base), _p(fact_dst),
-                              _p(fact_val), _p(fact_rel), _p(fact_m), _p(entry_count), _stream()), "hop_expand")
     fact_pos = torch.empty(T, dtype=torch.int32, device=dev) if record else None
     out_row_ptr = torch.empty(rows + 1, dtype=torch.int64, device=dev)
     out_ent = torch.empty(T, dtype=torch.int32, device=dev)
@@ -279,6 +303,12 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
     out_y = torch.empty(T, dtype=torch.float32, device=dev)
     out_denom = torch.empty(max(rows, 1), dtype=torch.float32, device=dev)
     ws2 = _ws(lib().fl_reduce_workspace(rows, T), dev)
+    # every buffer exists before the launches: nothing on the host between them
+    if timing is not None:
+        timing.record_start()
+    check(lib().fl_hop_expand(ctypes.byref(params), _p(row_ptr), _p(ent), _p(val), S, _p(w), graph.ori, graph.inv,
+                              _p(mo), _p(mi), _p(mask_triple), _p(edge_weight), _p(slot_base), _p(fact_dst),
+                              _p(fact_val), _p(fact_rel), _p(fact_m), _p(entry_count), _stream()), "hop_expand")
     check(lib().fl_row_reduce(_p(row_ptr), rows, graph.E, _p(slot_base), _p(entry_count), _p(fact_dst), _p(fact_val),
                               T, _p(fact_pos), ctypes.c_float(eps), _p(out_row_ptr), _p(out_ent), _p(out_x), _p(out_y),
                               _p(out_denom), _p(status), _p(ws2), ws2.numel(), _stream()), "row_reduce")

@@ -66,6 +66,12 @@ typedef struct {
     int64_t slot_capacity;          /* > 0: length of the fact / output buffers;
                                        work beyond it is skipped and flagged      */
     int32_t *status;                /* device int (or NULL): FL_STATUS_* bits     */
+    int32_t *entry_row;             /* i32[S] or NULL: row of each entry, written by
+                                       fl_hop_plan and read by fl_hop_expand (NULL:
+                                       the expansion finds rows by binary search) */
+    const uint8_t *vis_ori, *vis_inv; /* u8[M] or NULL: CSR-ordered visibility from
+                                       fl_csr_visibility; replaces the mask_triple
+                                       read through `order` (same result)         */
 } fl_hop_params;
 
 /* Device status bits set by the hop kernels. */
@@ -123,7 +129,14 @@ int fl_hop_plan(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *e
                 fl_csr_side inv, int64_t *slot_base, int64_t *total_slots, void *ws, size_t ws_bytes,
                 fl_stream_t stream);
 
-/* Hop expansion (one warp per source entry).  Replaces
+/* CSR-ordered visibility of one side: vis[p] = mask_triple[order[p]] != 0.
+ * The gather of prepare_csr_masks / apply_mask_cuda (flashlog_kernel.py:225-255,
+ * flashlog.cu:1291-1340) in one byte per edge; built once per step and shared
+ * by the hops. */
+int fl_csr_visibility(const int32_t *order, int64_t m, const uint8_t *mask_triple, uint8_t *vis, fl_stream_t stream);
+
+/* Hop expansion (8-lane teams for entries with at most 8 relation groups per
+ * side, one warp otherwise).  Replaces
  * fill_sparse3d_topk_kernel / fill_sparse3d_all_edges_kernel /
  * fill_sparse3d_identity_kernel (flashlog.cu:1402-1559, 1759-1854).  The edge
  * visibility comes from mask_triple (u8 per triple, read through order, the

@@ -383,3 +383,58 @@ def test_hop_is_deterministic(fk, g1):
                      wt.grad.cpu().numpy()))
     for a, b in zip(outs[0], outs[1]):
         assert a.tobytes() == b.tobytes()
+
+
+@pytest.mark.parametrize("topk", [5, 40])
+def test_threshold_paths_and_visibility(fk, topk):
+    """Entries with <= 8, 9-32, 33-1024 and > 1024 relation groups per side
+    (team, warp-register, staged and global threshold paths), tied weights,
+    hidden triples read through `order` and through the CSR-ordered
+    visibility: bit-identical to the oracle either way."""
+    from flashlog_b200 import ops
+    from flashlog_b200.ops import Graph
+    rng = np.random.default_rng(77 + topk)
+    E, R = 5000, 1100
+    h = rng.integers(0, E, 60_000)
+    r = rng.integers(0, R, 60_000)
+    t = rng.integers(0, E, 60_000)
+    parts = [np.stack([h, r, t], 1)]
+    for hub in range(5):  # ori side: all 1100 relations (global path)
+        parts.append(np.stack([np.full(R, hub), np.arange(R), rng.integers(0, E, R)], 1))
+    for hub in range(5, 10):  # inv side: 600 relations (staged path), 3 edges each
+        rr = np.repeat(np.arange(600), 3)
+        parts.append(np.stack([rng.integers(0, E, rr.size), rr, np.full(rr.size, hub)], 1))
+    for hub in range(10, 20):  # 20 relations (warp register path)
+        rr = np.repeat(np.arange(20), 2)
+        parts.append(np.stack([np.full(rr.size, hub), rr, rng.integers(0, E, rr.size)], 1))
+    tri = np.unique(np.concatenate(parts), axis=0)
+    csr_np = O.build_csr(tri[:, 0], tri[:, 2], tri[:, 1], E)
+    tt = _cuda(tri)
+    csr = fk.build_csr_structure(tt[:, 0], tt[:, 2], tt[:, 1], E)
+    graph = Graph.of(csr)
+    B, L = 2, 2
+    rows_ = []
+    ents_ = []
+    for rrow in range(B * L):
+        e = np.unique(np.concatenate([np.arange(20), rng.choice(E, 300, replace=False)]))
+        rows_.append(np.full(e.size, rrow))
+        ents_.append(e)
+    row = np.concatenate(rows_).astype(np.int64)
+    ent = np.concatenate(ents_).astype(np.int64)
+    val = rng.random(ent.size).astype(np.float32)
+    w = _w(rng, B, L, 2 * R + 1, True)
+    mask = (rng.random(tri.shape[0]) > 0.1).astype(np.uint8)
+    ref = O.hop_forward(row, ent, val, w, csr_np, R, E, topk_edges=topk, mode=O.MODE_TOPK, mask=mask)
+    rp, en, _ = ops.coo_to_rows(_cuda(row // L), _cuda(row % L), _cuda(ent), B, L, E)
+    mt = _cuda(mask)
+    for vis in (None, ops.csr_visibility(graph, mt)):
+        fw = ops.hop_forward(rp, en, _cuda(val), _cuda(w), graph, R, topk, 1 | 2, mask_triple=mt, vis=vis)
+        counts = (fw.out_row_ptr[1:] - fw.out_row_ptr[:-1]).cpu().numpy()
+        keys = np.repeat(np.arange(B * L), counts) * E + fw.out_ent.cpu().numpy()
+        assert np.array_equal(keys, ref["out_key"])
+        assert np.array_equal(fw.out_x.cpu().numpy(), ref["out_val"])
+        g = rng.standard_normal(keys.size).astype(np.float32)
+        gv, gw = ops.hop_backward(fw, rp, _cuda(val), _cuda(w), _cuda(g), normalize=False)
+        rgv, rgw = O.hop_backward(ref, g, row, val, w, R)
+        np.testing.assert_allclose(gv.cpu().numpy(), rgv, rtol=RTOL, atol=1e-5)
+        np.testing.assert_allclose(gw.cpu().numpy(), rgw, rtol=RTOL, atol=1e-5)
