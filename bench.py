@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--engine", default="graph", choices=["graph", "autograd"],
+                    help="graph: static-buffer step replayed as CUDA graphs; autograd: engine.drum_propagate")
     return ap.parse_args()
 
 
@@ -264,6 +266,105 @@ def run_value_arm(args, cfg, train, csr, rank, world, device):
                 data=data, table=table)
 
 
+def run_graph_arm(args, cfg, train, csr, rank, world, device):
+    """The training step of flashlog_b200.step.DrumTrainStep, one CUDA graph per timed step.
+
+    Each graph holds its own external CUDA events around every hop's
+    expansion + row reduction, so the hop-forward kernel time is read from the
+    timed replays themselves; the work counts (S, G, F, U) are accumulated on
+    the device by the step.  Kernel launches per step are counted while the
+    step is captured.
+    """
+    from flashlog_b200 import _lib
+    from flashlog_b200.ops import Graph
+    from flashlog_b200.step import DrumTrainStep
+    import torch.distributed as dist
+
+    graph = Graph.of(csr)
+    R, T, N = cfg.relations, cfg.T, cfg.N
+    n = 2 * R + 1
+    gen = torch.Generator(device="cpu").manual_seed(1234)
+    table = (torch.randn(2 * R, T, N, n, generator=gen) * 1.0).to(device)
+    nb = args.warmup + args.steps
+    data = batches_for(cfg, train, nb, rank)
+    dev_data = [tuple(torch.from_numpy(x).to(device) for x in b) for b in data]
+    n_ids = dev_data[0][0].numel()
+    step = DrumTrainStep(graph, R, cfg.queries, T, N, cfg.c1 or None, cfg.c2, table, n_hide=n_ids * world,
+                         apply_update=(world == 1))
+    lr = step.lr
+
+    def hide_of(ids):
+        if world == 1:
+            return ids
+        gathered = [torch.empty_like(ids) for _ in range(world)]
+        dist.all_gather(gathered, ids)
+        return torch.cat(gathered)
+
+    def after():
+        if world > 1:
+            dist.all_reduce(step.grad)
+            step.grad.div_(world)
+            table.sub_(lr * step.grad)
+
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()  # before the warm-up: nvidia-smi's start-up must not fall in the timed region
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):  # warm-up (also sets kernel attributes before any capture)
+        for b in dev_data[:args.warmup]:
+            ids, h, r, t = b
+            step.load(h, t, r, hide_of(ids))
+            step.run()
+            after()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    step.check()
+    # one graph per timed step, each with its own hop events
+    graphs, timers = [], []
+    pool = None
+    launches_per_step = 0
+    for k in range(args.steps):
+        timer = [(torch.cuda.Event(enable_timing=True, external=True),
+                  torch.cuda.Event(enable_timing=True, external=True)) for _ in range(T)]
+        step.timer = timer
+        g = torch.cuda.CUDAGraph()
+        l0 = _lib.lib().fl_launch_count()
+        with torch.cuda.graph(g, pool=pool):
+            step.run()
+        launches_per_step = _lib.lib().fl_launch_count() - l0
+        pool = g.pool()
+        graphs.append(g)
+        timers.append(timer)
+    step.timer = None
+    torch.cuda.synchronize()
+    step.stats.zero_()
+    clocks.wait_first()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for k, b in enumerate(dev_data[args.warmup:]):
+        ids, h, r, t = b
+        step.load(h, t, r, hide_of(ids))
+        graphs[k].replay()
+        after()
+    t1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = t0.elapsed_time(t1)
+    clk = clocks.stop()
+    step.check()  # no hop ran out of its buffers
+    S, G, F, U = (int(x) for x in step.stats.tolist())
+    hop_ms = sum(a.elapsed_time(b) for timer in timers for a, b in timer)
+    del graphs
+    return dict(ms=ms, facts=F, S=S, G=G, U=U, hop_ms=hop_ms, n_hops=args.steps * T,
+                launches=launches_per_step * args.steps, clocks=clk, data=data, table=table,
+                memory_gb=step.memory_bytes() / 1e9)
+
+
 def run_e2e_arm(args, cfg, train, csr, data, table, rank, world, device, steps):
     """Same metric through the reference-facing operator API with host buffers."""
     import flashlog_b200.flashlog_kernel as fk
@@ -417,7 +518,10 @@ def main():
         import datetime
         dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=300))
     cfg, train, csr = setup(args, rank, world, device)
-    res = run_value_arm(args, cfg, train, csr, rank, world, device)
+    if args.engine == "graph":
+        res = run_graph_arm(args, cfg, train, csr, rank, world, device)
+    else:
+        res = run_value_arm(args, cfg, train, csr, rank, world, device)
     ms = res["ms"]
     facts = res["facts"]
     hop_ms = res["hop_ms"]
@@ -478,6 +582,8 @@ def main():
                 "config": {"workload": workload_desc(cfg, world), "global_batch": cfg.queries * world,
                            "per_gpu_queries": cfg.queries, "parallelism": f"query-sharded dp{world}",
                            "l2": "inputs larger than L2 (CSR ~0.7 GB; fresh query batch every step)",
+                           "engine": ("static buffers, one CUDA graph per step (flashlog_b200.step)"
+                                      if args.engine == "graph" else "autograd, one host sync per hop"),
                            "facts_per_step": facts / args.steps},
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                              "frac": achieved / peak, "traffic": traffic, "peak_source": peak_src,

@@ -57,7 +57,7 @@ class fl_hop_params(ctypes.Structure):
                 ("r_size", ctypes.c_int64), ("E", ctypes.c_int64), ("topk_edges", ctypes.c_int64),
                 ("flags", ctypes.c_int64), ("sampling_seed", ctypes.c_int64), ("eps", ctypes.c_float),
                 ("slot_capacity", ctypes.c_int64), ("status", ctypes.c_void_p), ("entry_row", ctypes.c_void_p),
-                ("vis_ori", ctypes.c_void_p), ("vis_inv", ctypes.c_void_p)]
+                ("vis_ori", ctypes.c_void_p), ("vis_inv", ctypes.c_void_p), ("work", ctypes.c_void_p)]
 
 
 _P = ctypes.c_void_p
@@ -94,9 +94,10 @@ SIGNATURES = {
                                        _SZ, _P]),
     "fl_normalize_forward": (ctypes.c_int, [_P, _P, _I64, ctypes.c_float, _P, _P, _P]),
     "fl_normalize_backward": (ctypes.c_int, [_P, _P, _P, _P, _I64, ctypes.c_float, _P, _P]),
-    "fl_scatter_grad": (ctypes.c_int, [_P, _P, _I64, _P, _P, _I64, _P]),
+    "fl_hop_stats": (ctypes.c_int, [_P, _I64, _P, _I64, _SIDE, _SIDE, _P, _P, ctypes.c_int, _P, _P]),
+    "fl_scatter_grad": (ctypes.c_int, [_P, _P, _I64, _P, _P, _I64, _P, _P]),
     "fl_readout": (ctypes.c_int, [_P, _P, _P, _I64, _P, _I64, _P, _P]),
-    "fl_readout_backward": (ctypes.c_int, [_P, _P, _I64, _P, _I64, _P, _P, _I64, _P]),
+    "fl_readout_backward": (ctypes.c_int, [_P, _P, _I64, _P, _I64, _P, _P, _I64, _P, _P]),
     "fl_fixed_relation_workspace": (_SZ, [_I64]),
     "fl_fixed_relation_plan": (ctypes.c_int, [_P, _P, _P, _I64, _P, _I64, _I64, _SIDE, _SIDE, _P,
                                               ctypes.POINTER(ctypes.c_int64), _P, _SZ, _P]),

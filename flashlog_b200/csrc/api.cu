@@ -59,7 +59,7 @@ int filtered_ranks_noalloc(const int64_t *ib, const int64_t *ie, const float *v,
 int readout(const int64_t *row_ptr, const int32_t *ent, const float *val, int64_t N, const int64_t *targets, int64_t Q,
             float *scores, cudaStream_t st);
 int readout_backward(const int64_t *row_ptr, const int32_t *ent, int64_t N, const int64_t *targets, int64_t Q,
-                     const float *g, float *grad_val, int64_t n_val, cudaStream_t st);
+                     const float *g, float *grad_val, int64_t n_val, const int64_t *val_live, cudaStream_t st);
 
 namespace {
 
@@ -117,9 +117,14 @@ int fl_version(void) { return 1; }
 unsigned long long fl_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int fl_device_sm_count(void) {
+    // cached per device: launches made while a stream is being captured must
+    // not query the device
+    static std::atomic<int> cache[64];
     int dev = 0, n = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    if (dev >= 0 && dev < 64 && (n = cache[dev].load(std::memory_order_relaxed)) > 0) return n;
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    if (dev >= 0 && dev < 64) cache[dev].store(n, std::memory_order_relaxed);
     return n;
 }
 
@@ -223,9 +228,16 @@ int fl_normalize_backward(const int64_t *row_ptr, const float *x, const float *d
     return normalize_backward(row_ptr, x, denom, g, rows, eps, gx, as_stream(stream));
 }
 
+int fl_hop_stats(const int64_t *row_ptr, int64_t rows, const int32_t *ent, int64_t S, fl_csr_side ori,
+                 fl_csr_side inv, const int32_t *entry_count, const int64_t *out_row_ptr, int wot_i, int64_t *acc,
+                 fl_stream_t stream) {
+    FL_REQUIRE(acc != nullptr && rows >= 0 && S >= 0, "fl_hop_stats: bad arguments");
+    return hop_stats(row_ptr, rows, ent, S, ori, inv, entry_count, out_row_ptr, wot_i, acc, as_stream(stream));
+}
+
 int fl_scatter_grad(const float *grad_sel, const int64_t *src_index, int64_t n_sel, const int64_t *n_live,
-                    float *grad_full, int64_t n_full, fl_stream_t stream) {
-    return scatter_grad(grad_sel, src_index, n_sel, n_live, grad_full, n_full, as_stream(stream));
+                    float *grad_full, int64_t n_full, const int64_t *full_live, fl_stream_t stream) {
+    return scatter_grad(grad_sel, src_index, n_sel, n_live, grad_full, n_full, full_live, as_stream(stream));
 }
 
 size_t fl_fixed_relation_workspace(int64_t nnz) { return fixed_relation_workspace(nnz); }
@@ -267,8 +279,9 @@ int fl_readout(const int64_t *row_ptr, const int32_t *ent, const float *val, int
 }
 
 int fl_readout_backward(const int64_t *row_ptr, const int32_t *ent, int64_t N, const int64_t *targets, int64_t Q,
-                        const float *g_scores, float *grad_val, int64_t n_val, fl_stream_t stream) {
-    return readout_backward(row_ptr, ent, N, targets, Q, g_scores, grad_val, n_val, as_stream(stream));
+                        const float *g_scores, float *grad_val, int64_t n_val, const int64_t *val_live,
+                        fl_stream_t stream) {
+    return readout_backward(row_ptr, ent, N, targets, Q, g_scores, grad_val, n_val, val_live, as_stream(stream));
 }
 
 }  // extern "C"

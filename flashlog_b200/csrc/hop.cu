@@ -119,6 +119,7 @@ struct ExpandArgs {
     const float *edge_weight;
     const int64_t *slot_base;
     const int32_t *entry_row;          // may be null: rows found by binary search
+    uint32_t *work;                    // work-queue counter (zeroed before the launch) or null
     int32_t *fact_dst;
     float *fact_val;
     int16_t *fact_rel;
@@ -618,8 +619,8 @@ __global__ void __launch_bounds__(kExpandWarps * 32, 3) hop_expand_kernel(Expand
     const bool wot_i = (a.flags & FL_WOT_I) != 0;
     const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kExpandWarps;
     const int64_t S_live = a.row_ptr[a.rows] < a.S ? a.row_ptr[a.rows] : a.S;
-    for (int64_t base = (static_cast<int64_t>(blockIdx.x) * kExpandWarps + wib) * 4; base < S_live;
-         base += nwarps * 4) {
+    // Four entries (one per team) starting at `base`.
+    auto four = [&](int64_t base) {
         const int64_t i = base + team;
         const bool mine = i < S_live;
         bool small = false, over = false;
@@ -663,6 +664,23 @@ __global__ void __launch_bounds__(kExpandWarps * 32, 3) hop_expand_kernel(Expand
             big &= big - 1;
             expand_entry_warp<false>(a, scratch[wib], stage + wib, base + t);
         }
+    };
+    if (a.work != nullptr) {
+        // Warps take chunks of kChunk entries from a queue, so a warp held up
+        // by hub entries does not hold up the others of its block.
+        constexpr int64_t kChunk = 16;
+        for (;;) {
+            uint32_t c = 0;
+            if (lane == 0) c = atomicAdd(a.work, 1u);
+            c = __shfl_sync(kFull, c, 0);
+            const int64_t b0 = static_cast<int64_t>(c) * kChunk;
+            if (b0 >= S_live) break;
+            for (int64_t base = b0; base < b0 + kChunk && base < S_live; base += 4) four(base);
+        }
+    } else {
+        for (int64_t base = (static_cast<int64_t>(blockIdx.x) * kExpandWarps + wib) * 4; base < S_live;
+             base += nwarps * 4)
+            four(base);
     }
 }
 
@@ -720,7 +738,7 @@ struct ReduceSmem {
         TileB b;
         TileD d;
     } t;
-    uint16_t cnt[kDigits * kRWarps];  // per-warp digit counters, digit-major
+    uint16_t cnt[kRWarps * kDigits];  // per-warp digit counters, cnt[warp][digit]
     uint32_t hist[kHistBins + 1];     // exclusive prefix of the row's destination histogram
     uint16_t chunk[kHistBins + 1];    // first bin of each destination range
     int64_t scan_scratch[kRWarps + 1];
@@ -775,20 +793,27 @@ __device__ uint16_t *lsd_sort(const uint32_t *key, uint16_t *idx0, uint16_t *idx
             const unsigned act = __ballot_sync(kFull, valid);
             if (valid) {
                 const unsigned peers = __match_any_sync(act, d);
-                if (lane == __ffs(peers) - 1) sm.cnt[d * kRWarps + warp] += static_cast<uint16_t>(__popc(peers));
+                if (lane == __ffs(peers) - 1) sm.cnt[warp * kDigits + d] += static_cast<uint16_t>(__popc(peers));
             }
         }
         __syncthreads();
-        {  // exclusive prefix over (digit, warp), 8 counters per thread
-            uint16_t *c = sm.cnt + threadIdx.x * 8;
+        {  // exclusive prefix in (digit, warp) order, 8 counters per thread
             int v[8];
             int s = 0;
 #pragma unroll
-            for (int k = 0; k < 8; ++k) { v[k] = c[k]; s += v[k]; }
+            for (int k = 0; k < 8; ++k) {
+                const int q = threadIdx.x * 8 + k;
+                v[k] = sm.cnt[(q & (kRWarps - 1)) * kDigits + (q / kRWarps)];
+                s += v[k];
+            }
             int64_t tot;
             int run = static_cast<int>(block_exclusive_scan<int64_t>(s, sm.scan_scratch, &tot));
 #pragma unroll
-            for (int k = 0; k < 8; ++k) { c[k] = static_cast<uint16_t>(run); run += v[k]; }
+            for (int k = 0; k < 8; ++k) {
+                const int q = threadIdx.x * 8 + k;
+                sm.cnt[(q & (kRWarps - 1)) * kDigits + (q / kRWarps)] = static_cast<uint16_t>(run);
+                run += v[k];
+            }
         }
         __syncthreads();
         for (int base = wlo; base < whi; base += 32) {
@@ -799,10 +824,10 @@ __device__ uint16_t *lsd_sort(const uint32_t *key, uint16_t *idx0, uint16_t *idx
             const unsigned act = __ballot_sync(kFull, valid);
             if (valid) {
                 const unsigned peers = __match_any_sync(act, d);
-                const uint32_t b = sm.cnt[d * kRWarps + warp];
+                const uint32_t b = sm.cnt[warp * kDigits + d];
                 dst[b + __popc(peers & lanemask_lt())] = id;
                 __syncwarp(act);
-                if (lane == __ffs(peers) - 1) sm.cnt[d * kRWarps + warp] = static_cast<uint16_t>(b + __popc(peers));
+                if (lane == __ffs(peers) - 1) sm.cnt[warp * kDigits + d] = static_cast<uint16_t>(b + __popc(peers));
             }
             __syncwarp();
         }
@@ -1223,6 +1248,41 @@ __global__ void __launch_bounds__(kBThreads) hop_backward_kernel(BackwardArgs a)
         a.grad_w[r * a.n + c] = fixed_to_float(acc[2 * c], acc[2 * c + 1], scale);
 }
 
+// Work counts of one hop added to acc: [0] live entries S, [1] relation groups
+// of both sides G, [2] facts through graph edges F (entry counts minus the
+// identity terms), [3] live outputs U.
+__global__ void hop_stats_kernel(const int64_t *row_ptr, int64_t rows, const int32_t *ent, int64_t S, Side ori, Side inv,
+                                 const int32_t *entry_count, const int64_t *out_row_ptr, int wot_i,
+                                 unsigned long long *acc) {
+    __shared__ long long scratch[33];
+    const int64_t live = row_ptr[rows] < S ? row_ptr[rows] : S;
+    long long g = 0, f = 0;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < live;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t src = ent[i];
+        g += (ori.gptr[src + 1] - ori.gptr[src]) + (inv.gptr[src + 1] - inv.gptr[src]);
+        f += entry_count[i] - (wot_i ? 0 : 1);
+    }
+    g = block_sum(g, scratch);
+    f = block_sum(f, scratch);
+    if (threadIdx.x == 0) {
+        atomicAdd(acc + 1, static_cast<unsigned long long>(g));
+        atomicAdd(acc + 2, static_cast<unsigned long long>(f));
+        if (blockIdx.x == 0) {
+            atomicAdd(acc + 0, static_cast<unsigned long long>(live));
+            atomicAdd(acc + 3, static_cast<unsigned long long>(out_row_ptr[rows]));
+        }
+    }
+}
+
+// x[0, min(n, *live)) = 0, grid-stride.
+__global__ void zero_prefix_kernel(float *x, int64_t n, const int64_t *live) {
+    const int64_t m = *live < n ? *live : n;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < m;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        x[i] = 0.0f;
+}
+
 __global__ void scatter_grad_kernel(const float *grad_sel, const int64_t *src, int64_t n, const int64_t *n_live,
                                     float *grad_full) {
     int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
@@ -1343,7 +1403,7 @@ int hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *en
     a.topk = p->topk_edges; a.flags = p->flags; a.seed = p->sampling_seed; a.L = p->L; a.w = w;
     a.ori = make_side(ori, mask_csr_ori); a.inv = make_side(inv, mask_csr_inv);
     a.mask_triple = mask_triple; a.edge_weight = edge_weight; a.slot_base = slot_base;
-    a.vis_ori = p->vis_ori; a.vis_inv = p->vis_inv; a.entry_row = p->entry_row;
+    a.vis_ori = p->vis_ori; a.vis_inv = p->vis_inv; a.entry_row = p->entry_row; a.work = p->work;
     a.fact_dst = fact_dst; a.fact_val = fact_val; a.fact_rel = fact_rel; a.fact_m = fact_m; a.entry_count = entry_count;
     int sms = fl_device_sm_count();
     const int64_t per_sm = 3;  // resident CTAs per SM (registers and staging buffers)
@@ -1354,6 +1414,10 @@ int hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *en
         launch(hop_expand_sampled_kernel, static_cast<unsigned>(blocks), kExpandWarps * 32, 0, st, a);
     } else {
         int64_t blocks = (S + 4 * kExpandWarps - 1) / (4 * kExpandWarps);
+        if (a.work != nullptr) {  // resident blocks drain the work queue
+            FL_CUDA(cudaMemsetAsync(a.work, 0, sizeof(uint32_t), st));
+            cap_blocks = static_cast<int64_t>(sms > 0 ? sms : 148) * per_sm;
+        }
         if (blocks > cap_blocks) blocks = cap_blocks;
         const size_t smem = sizeof(StageBuf) * kExpandWarps;
         static bool attr_set = false;
@@ -1459,9 +1523,37 @@ int normalize_backward(const int64_t *row_ptr, const float *x, const float *deno
     return check_launch("normalize_backward");
 }
 
+int hop_stats(const int64_t *row_ptr, int64_t rows, const int32_t *ent, int64_t S, const fl_csr_side &ori,
+              const fl_csr_side &inv, const int32_t *entry_count, const int64_t *out_row_ptr, int wot_i, int64_t *acc,
+              cudaStream_t st) {
+    const int sms = fl_device_sm_count();
+    int64_t blocks = (S + 255) / 256;
+    const int64_t cap = static_cast<int64_t>(sms > 0 ? sms : 148) * 4;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    launch(hop_stats_kernel, static_cast<unsigned>(blocks), 256, 0, st, row_ptr, rows, ent, S, make_side(ori, nullptr),
+           make_side(inv, nullptr), entry_count, out_row_ptr, wot_i, reinterpret_cast<unsigned long long *>(acc));
+    return check_launch("hop_stats");
+}
+
+int zero_prefix(float *x, int64_t n, const int64_t *live, cudaStream_t st) {
+    if (n <= 0) return FL_OK;
+    if (live == nullptr) {
+        FL_CUDA(cudaMemsetAsync(x, 0, static_cast<size_t>(n) * sizeof(float), st));
+        return FL_OK;
+    }
+    const int sms = fl_device_sm_count();
+    int64_t blocks = (n + 255) / 256;
+    const int64_t cap = static_cast<int64_t>(sms > 0 ? sms : 148) * 8;
+    if (blocks > cap) blocks = cap;
+    launch(zero_prefix_kernel, static_cast<unsigned>(blocks), 256, 0, st, x, n, live);
+    return check_launch("zero_prefix");
+}
+
 int scatter_grad(const float *grad_sel, const int64_t *src, int64_t n_sel, const int64_t *n_live, float *grad_full,
-                 int64_t n_full, cudaStream_t st) {
-    FL_CUDA(cudaMemsetAsync(grad_full, 0, static_cast<size_t>(n_full) * sizeof(float), st));
+                 int64_t n_full, const int64_t *full_live, cudaStream_t st) {
+    int rc = zero_prefix(grad_full, n_full, full_live, st);
+    if (rc) return rc;
     if (n_sel > 0)
         launch(scatter_grad_kernel, static_cast<unsigned>((n_sel + 255) / 256), 256, 0, st, grad_sel, src, n_sel, n_live,
                grad_full);

@@ -29,8 +29,12 @@ int normalize_forward(const int64_t *row_ptr, const float *x, int64_t rows, floa
                       cudaStream_t st);
 int normalize_backward(const int64_t *row_ptr, const float *x, const float *denom, const float *g, int64_t rows,
                        float eps, float *gx, cudaStream_t st);
+int zero_prefix(float *x, int64_t n, const int64_t *live, cudaStream_t st);
+int hop_stats(const int64_t *row_ptr, int64_t rows, const int32_t *ent, int64_t S, const fl_csr_side &ori,
+              const fl_csr_side &inv, const int32_t *entry_count, const int64_t *out_row_ptr, int wot_i, int64_t *acc,
+              cudaStream_t st);
 int scatter_grad(const float *grad_sel, const int64_t *src, int64_t n_sel, const int64_t *n_live, float *grad_full,
-                 int64_t n_full, cudaStream_t st);
+                 int64_t n_full, const int64_t *full_live, cudaStream_t st);
 int topc_select(const int64_t *row_ptr, const int32_t *ent, const float *val, int64_t rows, int64_t S, int64_t c1,
                 const double *noise, int64_t *out_row_ptr, int32_t *out_ent, float *out_val, int64_t *out_src,
                 int64_t out_capacity, int32_t *status, void *ws, size_t ws_bytes, cudaStream_t st);

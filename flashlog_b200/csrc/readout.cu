@@ -8,6 +8,7 @@
 // coalesce of the summed sparse tensor does.  The backward writes the score
 // gradient to the entries it read and zeros elsewhere.
 #include "common.cuh"
+#include "hop.cuh"
 
 namespace fl {
 namespace {
@@ -57,8 +58,9 @@ int readout(const int64_t *row_ptr, const int32_t *ent, const float *val, int64_
 }
 
 int readout_backward(const int64_t *row_ptr, const int32_t *ent, int64_t N, const int64_t *targets, int64_t Q,
-                     const float *g, float *grad_val, int64_t n_val, cudaStream_t st) {
-    FL_CUDA(cudaMemsetAsync(grad_val, 0, static_cast<size_t>(n_val) * sizeof(float), st));
+                     const float *g, float *grad_val, int64_t n_val, const int64_t *val_live, cudaStream_t st) {
+    int rc = zero_prefix(grad_val, n_val, val_live, st);
+    if (rc) return rc;
     if (Q > 0)
         launch(readout_backward_kernel, static_cast<unsigned>((Q + 127) / 128), 128, 0, st, row_ptr, ent, N, targets,
                Q, g, grad_val);

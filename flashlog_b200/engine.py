@@ -37,6 +37,7 @@ class HopNorm(torch.autograd.Function):
         ctx.pruned = None
         ctx.n_in = v.numel()
         ctx.sel_live = None
+        ctx.in_live = row_ptr[rows:]  # live entries of the (capacity-sized) input
         if c1 is not None and c1 >= 0:
             cap = min(v.numel(), rows * int(c1))  # explicit zeros could exceed it: flagged in `status`
             rp, en, vv, src = ops.topc_select(row_ptr, ent, v, int(c1), sync=False, out_capacity=cap, status=status)
@@ -57,7 +58,7 @@ class HopNorm(torch.autograd.Function):
         row_ptr, v, wf = ctx.saved_tensors
         grad_v, grad_w = ops.hop_backward(ctx.fw, row_ptr, v, wf, g_y, normalize=True)
         if ctx.pruned is not None:
-            grad_v = ops.scatter_grad(grad_v, ctx.pruned, ctx.n_in, n_live=ctx.sel_live)
+            grad_v = ops.scatter_grad(grad_v, ctx.pruned, ctx.n_in, n_live=ctx.sel_live, full_live=ctx.in_live)
         return grad_v, grad_w, None, None, None, None, None, None, None, None, None, None, None, None
 
 
@@ -74,7 +75,8 @@ class Readout(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g):
         row_ptr, ent, targets = ctx.saved_tensors
-        return ops.readout_backward(row_ptr, ent, ctx.N, targets, g, ctx.n_val), None, None, None, None
+        return (ops.readout_backward(row_ptr, ent, ctx.N, targets, g, ctx.n_val, val_live=row_ptr[-1:]),
+                None, None, None, None)
 
 
 def initial_state(heads: torch.Tensor, N: int):

@@ -204,11 +204,12 @@ class HopForward:
 
 
 def hop_params(rows, Lch, n, r_size, E, topk_edges, flags, seed=-1, eps=EPS, slot_capacity=0, status=None,
-               entry_row=None, vis=None):
+               entry_row=None, vis=None, work=None):
     return L.fl_hop_params(rows, Lch, n, r_size, E, int(min(topk_edges, L.NO_BUDGET)), int(flags), int(seed),
                            float(eps), int(slot_capacity), None if status is None else status.data_ptr(),
                            None if entry_row is None else entry_row.data_ptr(),
-                           None if vis is None else vis[0].data_ptr(), None if vis is None else vis[1].data_ptr())
+                           None if vis is None else vis[0].data_ptr(), None if vis is None else vis[1].data_ptr(),
+                           None if work is None else work.data_ptr())
 
 
 def csr_visibility(graph: Graph, mask_triple):
@@ -264,8 +265,9 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
     if vis is not None and (len(vis) != 2 or any(v.numel() < graph.csr[1].numel() or v.dtype != torch.uint8
                                                  for v in vis)):
         raise ValueError("vis must be the two u8 CSR-ordered visibility arrays of csr_visibility")
+    work = torch.empty(1, dtype=torch.int32, device=dev)
     params = hop_params(rows, Lch, n, r_size, graph.E, topk_edges, flags, seed, eps, slot_capacity or 0, status,
-                        entry_row, vis)
+                        entry_row, vis, work)
     check(lib().fl_hop_plan(ctypes.byref(params), _p(row_ptr), _p(ent), S, graph.ori, graph.inv, _p(slot_base),
                             ctypes.byref(total) if sync else None, _p(ws), ws.numel(), _stream()), "hop_plan")
     T = max(total.value, 1) if sync else max(int(slot_capacity), 1)
@@ -340,11 +342,12 @@ def hop_backward(fw: HopForward, row_ptr, val, w, g_y, normalize: bool = True):
     return grad_val[:S], grad_w.view(B, Lch, n)
 
 
-def scatter_grad(grad_sel, src_index, n_full: int, n_live=None):
-    """grad_full[src_index[j]] = grad_sel[j]; n_live (device int64) bounds j."""
+def scatter_grad(grad_sel, src_index, n_full: int, n_live=None, full_live=None):
+    """grad_full[src_index[j]] = grad_sel[j]; n_live (device int64) bounds j;
+    full_live (device int64) limits the zeroing to the live prefix."""
     out = torch.empty(max(n_full, 1), dtype=torch.float32, device=grad_sel.device)
     check(lib().fl_scatter_grad(_p(grad_sel.contiguous()), _p(src_index), src_index.numel(), _p(n_live), _p(out),
-                                n_full, _stream()), "scatter_grad")
+                                n_full, _p(full_live), _stream()), "scatter_grad")
     return out[:n_full]
 
 
@@ -438,10 +441,11 @@ def readout(row_ptr, ent, val, N: int, targets):
     return scores[:Q]
 
 
-def readout_backward(row_ptr, ent, N: int, targets, g_scores, n_val: int):
+def readout_backward(row_ptr, ent, N: int, targets, g_scores, n_val: int, val_live=None):
     Q = targets.numel()
     grad = torch.empty(max(n_val, 1), dtype=torch.float32, device=g_scores.device)
     check(lib().fl_readout_backward(_p(row_ptr), _p(ent), N, _p(targets.to(torch.int64).contiguous()), Q,
-                                    _p(g_scores.to(torch.float32).contiguous()), _p(grad), n_val, _stream()),
+                                    _p(g_scores.to(torch.float32).contiguous()), _p(grad), n_val, _p(val_live),
+                                    _stream()),
           "readout_backward")
     return grad[:n_val]

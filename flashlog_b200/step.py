@@ -1,0 +1,244 @@
+"""One sparse DRUM training step on static buffers, with no host synchronization.
+
+This is src/model_DRUM_kernel_sp.py:92-204 (T hops of c1 selection,
+expansion with the c2 budget, coalesce-sum and row normalization), the
+channel readout and log loss of src/utils.py:36-47, their backward and an
+SGD update of a per-query-relation attention table, written against buffers
+allocated once.  Every buffer is sized by a static bound:
+
+  selected entries of hop t   S_t = min(C_t, rows * c1)
+  fact slots of hop t         F_t = min(S_t * k_max, rows * K)
+  outputs of hop t            C_{t+1} = min(F_t, rows * E)
+
+where k(e) = min(deg_ori(e), c2//2) + min(deg_inv(e), c2//2) + 1 is the slot
+capacity of entity e, k_max its maximum, K its sum over the entities (a row
+holds every entity at most once) and C_0 = rows.  The kernels
+read the live counts from the device (row_ptr[-1]), so nothing is read back
+to the host and one step can be captured in a CUDA graph and replayed.  A
+device status word flags any capacity overflow (it cannot happen under these
+bounds) and `check` reads it.
+
+The autograd path of engine.drum_propagate computes the same step with one
+host synchronization per hop.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib as L
+from .ops import Graph, _p, _stream, check, lib
+
+
+def _buf(n, dtype, dev):
+    return torch.empty(max(int(n), 1), dtype=dtype, device=dev)
+
+
+class DrumTrainStep:
+    """Static-buffer DRUM step: forward (T hops), loss, backward, SGD.
+
+    table: [2R, T, N, n] attention logits (the parameter); a query with
+    relation r uses table[r].  Inputs per step are copied into the static
+    tensors heads, tails, rels (i64[Q]) and hide (i64[H], triple ids hidden
+    during the step) with `load`.
+    """
+
+    def __init__(self, graph: Graph, r_size: int, Q: int, T: int, N: int, c1, c2: int, table: torch.Tensor,
+                 n_hide: int, lr: float = 0.01, eps: float = 1e-7, thr: float = 1e-7, stats: bool = True,
+                 apply_update: bool = True):
+        dev = table.device
+        self.dev, self.graph, self.r_size, self.Q, self.T, self.N = dev, graph, r_size, Q, T, N
+        self.n = 2 * r_size + 1
+        self.c1 = None if c1 is None or c1 < 0 else int(c1)
+        self.topk = c2 // 2 if c2 and c2 > 0 else L.NO_BUDGET
+        self.flags = L.FL_SKIP_NONPOS_W | L.FL_DROP_MASKED
+        self.eps, self.thr, self.lr = eps, thr, lr
+        self.apply_update = apply_update
+        self.table = table
+        self.grad = torch.zeros_like(table)
+        rows = Q * N
+        self.rows = rows
+        csr = graph.csr
+        M = csr[1].numel()
+        E = graph.E
+        d_o = (csr[0][1:] - csr[0][:-1]).to(torch.int64).clamp_max(self.topk)
+        d_i = (csr[4][1:] - csr[4][:-1]).to(torch.int64).clamp_max(self.topk)
+        k = d_o + d_i + 1
+        k_max, K = (int(k.max().item()), int(k.sum().item())) if E > 0 else (1, 1)
+        # capacities
+        self.C, self.S, self.F, self.U = [], [], [], []
+        C = rows
+        for _ in range(T):
+            S = min(C, rows * self.c1) if self.c1 is not None else C
+            F = min(S * k_max, rows * K)
+            self.C.append(C)
+            self.S.append(S)
+            self.F.append(F)
+            C = min(F, rows * E)
+            self.U.append(C)
+        i64, i32, f32, u8, i16 = torch.int64, torch.int32, torch.float32, torch.uint8, torch.int16
+        # inputs
+        self.heads = _buf(Q, i64, dev)
+        self.tails = _buf(Q, i64, dev)
+        self.rels = _buf(Q, i64, dev)
+        self.hide = _buf(n_hide, i64, dev)
+        self.n_hide = n_hide
+        # visibility in CSR order, with the position of every triple on each side
+        self.vis = (torch.ones(M, dtype=u8, device=dev), torch.ones(M, dtype=u8, device=dev))
+        self.pos = []
+        for order in (csr[3], csr[7]):
+            p = torch.empty(M, dtype=i64, device=dev)
+            p[order.to(i64)] = torch.arange(M, dtype=i64, device=dev)
+            self.pos.append(p)
+        # hop-1 state
+        self.rp0 = torch.arange(rows + 1, dtype=i64, device=dev)
+        self.ent0 = _buf(rows, i32, dev)
+        self.val0 = torch.ones(rows, dtype=f32, device=dev)
+        # per hop: what the backward needs
+        self.w = [_buf(rows * self.n, f32, dev) for _ in range(T)]
+        self.rp_sel = [_buf(rows + 1, i64, dev) for _ in range(T)]
+        self.val_sel = [_buf(self.S[t], f32, dev) for t in range(T)]
+        self.src_sel = [_buf(self.S[t], i64, dev) for t in range(T)]
+        self.slot_base = [_buf(self.S[t] + 1, i64, dev) for t in range(T)]
+        self.entry_count = [_buf(self.S[t], i32, dev) for t in range(T)]
+        self.fact_rel = [_buf(self.F[t], i16, dev) for t in range(T)]
+        self.fact_pos = [_buf(self.F[t], i32, dev) for t in range(T)]
+        self.out_rp = [_buf(rows + 1, i64, dev) for _ in range(T)]
+        self.out_ent = [_buf(self.U[t], i32, dev) for t in range(T)]
+        self.out_x = [_buf(self.U[t], f32, dev) for t in range(T)]
+        self.out_y = [_buf(self.U[t], f32, dev) for t in range(T)]
+        self.out_denom = [_buf(rows, f32, dev) for _ in range(T)]
+        self.g_y = [_buf(self.U[t], f32, dev) for t in range(T)]
+        # transient, shared by the hops
+        Smax, Fmax = max(self.S), max(self.F)
+        self.ent_sel = _buf(Smax, i32, dev)
+        self.entry_row = _buf(Smax, i32, dev)
+        self.fact_dst = _buf(Fmax, i32, dev)
+        self.fact_val = _buf(Fmax, f32, dev)
+        self.grad_sel = _buf(Smax, f32, dev)
+        self.grad_w = _buf(rows * self.n, f32, dev)
+        self.work = _buf(1, i32, dev)
+        self.status = torch.zeros(1, dtype=i32, device=dev)
+        self.scores = _buf(Q, f32, dev)
+        self.loss = torch.zeros((), dtype=f32, device=dev)
+        self.grad_logits = torch.empty((Q, T, N, self.n), dtype=f32, device=dev)
+        ws = 0
+        for t in range(T):
+            ws = max(ws, lib().fl_topc_workspace(rows, self.C[t]), lib().fl_hop_workspace(rows, self.S[t]),
+                     lib().fl_reduce_workspace(rows, self.F[t]))
+        ws = max(ws, lib().fl_hop_backward_workspace(rows, self.n))
+        self.ws = _buf(ws, u8, dev)
+        self.stats = torch.zeros(4, dtype=i64, device=dev) if stats else None
+        self.timer = None  # optional: per-hop (start, end) external events around expand + reduce
+
+    # ------------------------------------------------------------------
+    def memory_bytes(self) -> int:
+        seen, total = set(), 0
+        for v in vars(self).values():
+            for t in (v if isinstance(v, (list, tuple)) else [v]):
+                if isinstance(t, torch.Tensor) and t.is_cuda and t.data_ptr() not in seen:
+                    seen.add(t.data_ptr())
+                    total += t.numel() * t.element_size()
+        return total
+
+    def load(self, heads, tails, rels, hide):
+        """Copy one step's inputs (device tensors) into the static buffers."""
+        if hide.numel() != self.n_hide or heads.numel() != self.Q:
+            raise ValueError("inputs must have the static sizes given at construction")
+        self.heads.copy_(heads)
+        self.tails.copy_(tails)
+        self.rels.copy_(rels)
+        self.hide.copy_(hide)
+
+    def _params(self, t, flags):
+        return L.fl_hop_params(self.rows, self.N, self.n, self.r_size, self.graph.E, int(self.topk), int(flags), -1,
+                               float(self.eps), int(self.F[t]), self.status.data_ptr(), self.entry_row.data_ptr(),
+                               self.vis[0].data_ptr(), self.vis[1].data_ptr(), self.work.data_ptr())
+
+    # ------------------------------------------------------------------
+    def run(self):
+        """Forward, loss, backward and (optionally) the SGD update; returns the loss tensor."""
+        lb, st, g = lib(), _stream(), self.graph
+        rows, N, Q, T = self.rows, self.N, self.Q, self.T
+        ws, wsn = _p(self.ws), self.ws.numel()
+        # hide the batch's own triples (src/main.py:888), remembering what was there
+        hid = [self.pos[k][self.hide] for k in range(2)]
+        old = [self.vis[k][hid[k]] for k in range(2)]
+        for k in range(2):
+            self.vis[k].index_fill_(0, hid[k], 0)
+        w_all = self.table[self.rels]  # [Q, T, N, n]
+        self.ent0[:rows].view(Q, N).copy_(self.heads.view(Q, 1).expand(Q, N))
+        rp_in, ent_in, val_in = self.rp0, self.ent0, self.val0
+        for t in range(T):
+            self.w[t][:rows * self.n].view(Q, N, self.n).copy_(torch.softmax(w_all[:, t], dim=-1))
+            # c1
+            if self.c1 is not None:
+                check(lb.fl_topc_select(_p(rp_in), _p(ent_in), _p(val_in), rows, self.C[t], self.c1, None,
+                                        _p(self.rp_sel[t]), _p(self.ent_sel), _p(self.val_sel[t]),
+                                        _p(self.src_sel[t]), self.S[t], _p(self.status), ws, wsn, st), "topc_select")
+                rp_s, ent_s, val_s = self.rp_sel[t], self.ent_sel, self.val_sel[t]
+            else:
+                rp_s, ent_s, val_s = rp_in, ent_in, val_in
+                self.rp_sel[t].copy_(rp_in)
+                self.val_sel[t][:self.S[t]].copy_(val_in[:self.S[t]])
+            params = self._params(t, self.flags)
+            check(lb.fl_hop_plan(ctypes.byref(params), _p(rp_s), _p(ent_s), self.S[t], g.ori, g.inv,
+                                 _p(self.slot_base[t]), None, ws, wsn, st), "hop_plan")
+            if self.timer is not None:
+                self.timer[t][0].record()
+            check(lb.fl_hop_expand(ctypes.byref(params), _p(rp_s), _p(ent_s), _p(val_s), self.S[t], _p(self.w[t]),
+                                   g.ori, g.inv, None, None, None, None, _p(self.slot_base[t]), _p(self.fact_dst),
+                                   _p(self.fact_val), _p(self.fact_rel[t]), None, _p(self.entry_count[t]), st),
+                  "hop_expand")
+            check(lb.fl_row_reduce(_p(rp_s), rows, g.E, _p(self.slot_base[t]), _p(self.entry_count[t]),
+                                   _p(self.fact_dst), _p(self.fact_val), self.F[t], _p(self.fact_pos[t]),
+                                   ctypes.c_float(self.eps), _p(self.out_rp[t]), _p(self.out_ent[t]),
+                                   _p(self.out_x[t]), _p(self.out_y[t]), _p(self.out_denom[t]), _p(self.status), ws,
+                                   wsn, st), "row_reduce")
+            if self.timer is not None:
+                self.timer[t][1].record()
+            if self.stats is not None:
+                check(lb.fl_hop_stats(_p(rp_s), rows, _p(ent_s), self.S[t], g.ori, g.inv, _p(self.entry_count[t]),
+                                      _p(self.out_rp[t]), 0, _p(self.stats), st), "hop_stats")
+            rp_in, ent_in, val_in = self.out_rp[t], self.out_ent[t], self.out_y[t]
+        # readout + loss (src/utils.py:36-47)
+        check(lb.fl_readout(_p(rp_in), _p(ent_in), _p(val_in), N, _p(self.tails), Q, _p(self.scores), st), "readout")
+        score = self.scores[:Q]
+        self.loss.copy_(-torch.mean(torch.log(torch.clamp_min(score, self.thr))))
+        g_score = torch.where(score > self.thr, -1.0 / (Q * torch.clamp_min(score, self.thr)),
+                              torch.zeros_like(score))
+        check(lb.fl_readout_backward(_p(rp_in), _p(ent_in), N, _p(self.tails), Q, _p(g_score), _p(self.g_y[T - 1]),
+                                     self.U[T - 1], _p(self.out_rp[T - 1][rows:]), st), "readout_backward")
+        # backward through the hops
+        for t in reversed(range(T)):
+            params = self._params(t, self.flags)
+            check(lb.fl_hop_backward(ctypes.byref(params), _p(self.rp_sel[t]), _p(self.val_sel[t]), self.S[t],
+                                     _p(self.w[t]), _p(self.slot_base[t]), _p(self.entry_count[t]),
+                                     _p(self.fact_pos[t]), _p(self.fact_rel[t]), None, _p(self.out_rp[t]),
+                                     _p(self.out_x[t]), _p(self.out_denom[t]), _p(self.g_y[t]), _p(self.grad_sel),
+                                     _p(self.grad_w), ws, wsn, st), "hop_backward")
+            if t > 0:
+                src = self.src_sel[t] if self.c1 is not None else None
+                if src is not None:
+                    check(lb.fl_scatter_grad(_p(self.grad_sel), _p(src), self.S[t], _p(self.rp_sel[t][rows:]),
+                                             _p(self.g_y[t - 1]), self.U[t - 1], _p(self.out_rp[t - 1][rows:]), st),
+                          "scatter_grad")
+                else:
+                    self.g_y[t - 1][:self.S[t]].copy_(self.grad_sel[:self.S[t]])
+            # softmax backward: d logits = w * (g - sum(g * w))
+            wt = self.w[t][:rows * self.n].view(Q, N, self.n)
+            gw = self.grad_w[:rows * self.n].view(Q, N, self.n)
+            self.grad_logits[:, t].copy_(wt * (gw - (gw * wt).sum(-1, keepdim=True)))
+        self.grad.zero_()
+        self.grad.index_add_(0, self.rels, self.grad_logits)
+        if self.apply_update:
+            self.table.sub_(self.lr * self.grad)
+        for k in range(2):
+            self.vis[k].index_put_((hid[k],), old[k])
+        return self.loss
+
+    def check(self):
+        """Raise if any hop ran out of its buffers (one host read)."""
+        if int(self.status.item()) & L.FL_STATUS_SLOT_OVERFLOW:
+            raise RuntimeError("a hop exceeded its static capacity")

@@ -72,6 +72,8 @@ typedef struct {
     const uint8_t *vis_ori, *vis_inv; /* u8[M] or NULL: CSR-ordered visibility from
                                        fl_csr_visibility; replaces the mask_triple
                                        read through `order` (same result)         */
+    uint32_t *work;                 /* device u32 or NULL: work queue of fl_hop_expand
+                                       (it zeroes it); NULL: static assignment    */
 } fl_hop_params;
 
 /* Device status bits set by the hop kernels. */
@@ -184,22 +186,34 @@ int fl_normalize_forward(const int64_t *row_ptr, const float *x, int64_t rows, f
 int fl_normalize_backward(const int64_t *row_ptr, const float *x, const float *denom, const float *g, int64_t rows,
                           float eps, float *gx, fl_stream_t stream);
 
+/* Work counts of one hop, added to acc (device i64[4]): live entries S,
+ * relation groups of both sides G, facts through graph edges F, live
+ * outputs U.  No synchronization; the measurement of bench.py reads them
+ * after its timed region. */
+int fl_hop_stats(const int64_t *row_ptr, int64_t rows, const int32_t *ent, int64_t S, fl_csr_side ori,
+                 fl_csr_side inv, const int32_t *entry_count, const int64_t *out_row_ptr, int wot_i, int64_t *acc,
+                 fl_stream_t stream);
+
 /* grad_full[src_index[j]] = grad_sel[j] for j < n_sel (and j < *n_live when
- * n_live, a device count, is given), zeros elsewhere.  Replaces
- * _restore_pruned_gradient (flashlog_kernel.py:1150-1155). */
+ * n_live, a device count, is given), zeros elsewhere: all of grad_full[0,
+ * n_full), or only its first *full_live entries when full_live (a device
+ * count) is given.  Replaces _restore_pruned_gradient
+ * (flashlog_kernel.py:1150-1155). */
 int fl_scatter_grad(const float *grad_sel, const int64_t *src_index, int64_t n_sel, const int64_t *n_live,
-                    float *grad_full, int64_t n_full, fl_stream_t stream);
+                    float *grad_full, int64_t n_full, const int64_t *full_live, fl_stream_t stream);
 
 /* Channel readout at the targets: scores[q] = sum over channels l (in order)
  * of the state's value at (q, l, targets[q]) (0 when absent).  Rows are
  * r = q * N + l.  Replaces sum_sp_3d + the target lookup of
  * log_loss_common_sp (src/model_DRUM_kernel_sp.py:22-28, src/utils.py:36-47).
  * The backward writes g_scores[q] at every entry read and zeros the rest of
- * grad_val (n_val entries). */
+ * grad_val (n_val entries, or the first *val_live when that device count is
+ * given). */
 int fl_readout(const int64_t *row_ptr, const int32_t *ent, const float *val, int64_t N, const int64_t *targets,
                int64_t Q, float *scores, fl_stream_t stream);
 int fl_readout_backward(const int64_t *row_ptr, const int32_t *ent, int64_t N, const int64_t *targets, int64_t Q,
-                        const float *g_scores, float *grad_val, int64_t n_val, fl_stream_t stream);
+                        const float *g_scores, float *grad_val, int64_t n_val, const int64_t *val_live,
+                        fl_stream_t stream);
 
 /* Rule step with one fixed operator per (query, rule) row: ops i64[B, Lr]
  * holds a forward relation, inverse relation + R, or identity 2R.  Replaces
