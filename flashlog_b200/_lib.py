@@ -56,7 +56,7 @@ class fl_hop_params(ctypes.Structure):
     _fields_ = [("rows", ctypes.c_int64), ("L", ctypes.c_int64), ("n", ctypes.c_int64),
                 ("r_size", ctypes.c_int64), ("E", ctypes.c_int64), ("topk_edges", ctypes.c_int64),
                 ("flags", ctypes.c_int64), ("sampling_seed", ctypes.c_int64), ("eps", ctypes.c_float),
-                ("slot_capacity", ctypes.c_int64), ("status", ctypes.c_void_p), ("entry_row", ctypes.c_void_p),
+                ("slot_capacity", ctypes.c_int64), ("status", ctypes.c_void_p), ("entry_info", ctypes.c_void_p),
                 ("vis_ori", ctypes.c_void_p), ("vis_inv", ctypes.c_void_p), ("work", ctypes.c_void_p)]
 
 

@@ -52,22 +52,30 @@ __device__ __forceinline__ int64_t find_row(const int64_t *row_ptr, int64_t rows
 // Plan: per-entry fact capacity (budget-capped degree per side + identity)
 // and the entry's row.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ int64_t side_degree(const Side &s, int64_t src) {
-    // Groups of a source are contiguous in CSR order, so its degree follows
-    // from the first group's start and the last group's end.
-    const int64_t g0 = s.gptr[src], g1 = s.gptr[src + 1];
-    return g0 == g1 ? 0 : static_cast<int64_t>(s.gstart[g1 - 1]) + s.gcount[g1 - 1] - s.gstart[g0];
-}
+// Per-entry record handed from the plan to the expansion: the entry's row and
+// the group ranges of both sides.
+struct EntryInfo {
+    int32_t row, g0o, g1o, g0i, g1i;
+};
 
 __global__ void hop_capacity_kernel(const int32_t *ent, const int64_t *row_ptr, int64_t rows, int64_t S, Side ori,
-                                    Side inv, int64_t topk, int wot_i, int64_t *cap, int32_t *entry_row) {
+                                    Side inv, int64_t topk, int wot_i, int64_t *cap, EntryInfo *info) {
     int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
     if (i >= S) return;
     if (i >= row_ptr[rows]) { cap[i] = 0; return; }  // beyond the live entries
-    if (entry_row) entry_row[i] = static_cast<int32_t>(find_row(row_ptr, rows, i));
     int64_t src = ent[i];
-    int64_t d0 = side_degree(ori, src);
-    int64_t d1 = side_degree(inv, src);
+    const int64_t g0o = ori.gptr[src], g1o = ori.gptr[src + 1], g0i = inv.gptr[src], g1i = inv.gptr[src + 1];
+    if (info) {
+        EntryInfo e;
+        e.row = static_cast<int32_t>(find_row(row_ptr, rows, i));
+        e.g0o = static_cast<int32_t>(g0o); e.g1o = static_cast<int32_t>(g1o);
+        e.g0i = static_cast<int32_t>(g0i); e.g1i = static_cast<int32_t>(g1i);
+        info[i] = e;
+    }
+    // Groups of a source are contiguous in CSR order, so a side's degree
+    // follows from its first group's start and its last group's end.
+    int64_t d0 = g0o == g1o ? 0 : static_cast<int64_t>(ori.gstart[g1o - 1]) + ori.gcount[g1o - 1] - ori.gstart[g0o];
+    int64_t d1 = g0i == g1i ? 0 : static_cast<int64_t>(inv.gstart[g1i - 1]) + inv.gcount[g1i - 1] - inv.gstart[g0i];
     if (topk < kNoBudget) { d0 = d0 < topk ? d0 : topk; d1 = d1 < topk ? d1 : topk; }
     cap[i] = d0 + d1 + (wot_i ? 0 : 1);
 }
@@ -90,7 +98,10 @@ constexpr int kTeam = 8;
 constexpr int kStage = 1024;  // relation groups of one side staged per warp
 
 struct WarpScratch {
-    unsigned int hist[256];
+    unsigned int hist[256];   // weighted digit counts
+    unsigned int histn[256];  // group counts per digit
+    uint32_t ckey[32];        // threshold candidates
+    uint32_t ccnt[32];
     int32_t incl[32];
     int32_t start[32];
     float prod[32];
@@ -118,7 +129,7 @@ struct ExpandArgs {
     const uint8_t *vis_ori, *vis_inv;  // CSR-ordered visibility (may be null)
     const float *edge_weight;
     const int64_t *slot_base;
-    const int32_t *entry_row;          // may be null: rows found by binary search
+    const EntryInfo *info;             // may be null: rows and group ranges looked up
     uint32_t *work;                    // work-queue counter (zeroed before the launch) or null
     int32_t *fact_dst;
     float *fact_val;
@@ -171,13 +182,15 @@ __device__ __forceinline__ void group_key(const float *wdir, const Side &sd, int
 // get(j, &key, &cnt); the total of the counts must exceed the budget.  Lanes
 // with equal digits are merged with a warp match before the shared-memory
 // add, so equal weights (groups of one relation share it) do not serialize.
+// Once at most 32 groups share the selected prefix they are gathered into
+// one lane each and the threshold is finished by all-pairs comparison.
 template <typename Get>
 __device__ void radix_threshold(int64_t n, int64_t budget, WarpScratch &ws, Get get, uint32_t *thr, int64_t *keep) {
     const int lane = threadIdx.x & 31;
     uint32_t prefix = 0, pmask = 0;
     int64_t krem = budget;
     for (int shift = 24; shift >= 0; shift -= 8) {
-        for (int d = lane; d < 256; d += 32) ws.hist[d] = 0;
+        for (int d = lane; d < 256; d += 32) { ws.hist[d] = 0; ws.histn[d] = 0; }
         __syncwarp();
         for (int64_t cb = 0; cb < n; cb += 32) {
             uint32_t key, cnt;
@@ -188,7 +201,10 @@ __device__ void radix_threshold(int64_t n, int64_t budget, WarpScratch &ws, Get 
                 const uint32_t d = (key >> shift) & 255u;
                 const unsigned peers = __match_any_sync(act, d);
                 const unsigned sum = __reduce_add_sync(peers, cnt);
-                if (lane == __ffs(peers) - 1) atomicAdd(&ws.hist[d], sum);
+                if (lane == __ffs(peers) - 1) {
+                    atomicAdd(&ws.hist[d], sum);
+                    atomicAdd(&ws.histn[d], static_cast<unsigned>(__popc(peers)));
+                }
             }
         }
         __syncwarp();
@@ -216,7 +232,40 @@ __device__ void radix_threshold(int64_t n, int64_t budget, WarpScratch &ws, Get 
         krem -= above;
         prefix |= static_cast<uint32_t>(digit) << shift;
         pmask |= 255u << shift;
+        const unsigned ncand = ws.histn[digit];
         __syncwarp();
+        if (shift > 0 && ncand <= 32u) {
+            unsigned running = 0;
+            for (int64_t cb = 0; cb < n; cb += 32) {
+                uint32_t key, cnt;
+                get(cb + lane, &key, &cnt);
+                const bool cand = cnt > 0u && (key & pmask) == prefix;
+                const unsigned b = __ballot_sync(kFull, cand);
+                if (cand) {
+                    const unsigned p = running + __popc(b & lanemask_lt());
+                    ws.ckey[p] = key;
+                    ws.ccnt[p] = cnt;
+                }
+                running += __popc(b);
+            }
+            __syncwarp();
+            const uint32_t key = static_cast<unsigned>(lane) < ncand ? ws.ckey[lane] : 0u;
+            const int64_t cnt = static_cast<unsigned>(lane) < ncand ? static_cast<int64_t>(ws.ccnt[lane]) : 0;
+            int64_t ge = 0, gt = 0;
+#pragma unroll 8
+            for (int j = 0; j < 32; ++j) {
+                const uint32_t kj = __shfl_sync(kFull, key, j);
+                const int64_t cj = __shfl_sync(kFull, cnt, j);
+                ge += kj >= key ? cj : 0;
+                gt += kj > key ? cj : 0;
+            }
+            const unsigned q = __ballot_sync(kFull, cnt > 0 && gt < krem && ge >= krem);
+            const int src = __ffs(q) - 1;
+            *thr = __shfl_sync(kFull, key, src);
+            *keep = krem - __shfl_sync(kFull, gt, src);
+            __syncwarp();
+            return;
+        }
     }
     *thr = prefix;
     *keep = krem;
@@ -252,15 +301,29 @@ __device__ bool group_threshold(const float *wdir, const Side &sd, int64_t g0, i
     const int64_t n = g1 - g0;
     if (stg != nullptr && n <= kStage && budget < 65536) {
         int64_t total = 0;
-#pragma unroll 4
-        for (int64_t cb = 0; cb < n; cb += 32) {
-            uint32_t key, cnt;
-            group_key(wdir, sd, g0 + cb + lane, g1, &key, &cnt);
-            if (cb + lane < n) {
-                stg->key[cb + lane] = key;
-                stg->cnt[cb + lane] = static_cast<uint16_t>(cnt < budget ? cnt : budget);
+        for (int64_t cb = 0; cb < n; cb += 128) {  // four groups per lane: the loads are issued together
+            int32_t rel[4];
+            uint32_t c[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int64_t j = cb + u * 32 + lane;
+                rel[u] = j < n ? static_cast<int32_t>(sd.grel[g0 + j]) : -1;
+                c[u] = j < n ? static_cast<uint32_t>(sd.gcount[g0 + j]) : 0u;
             }
-            total += cnt;
+            float wv[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) wv[u] = rel[u] >= 0 ? wdir[rel[u]] : 0.0f;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int64_t j = cb + u * 32 + lane;
+                const bool pos = wv[u] > 0.0f;
+                const uint32_t cc = pos ? c[u] : 0u;
+                if (j < n) {
+                    stg->key[j] = pos ? __float_as_uint(wv[u]) : 0u;
+                    stg->cnt[j] = static_cast<uint16_t>(cc < budget ? cc : budget);
+                }
+                total += cc;
+            }
         }
         __syncwarp();
         *staged = true;
@@ -308,8 +371,16 @@ __device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, StageBuf
         if (lane == 0) { a.entry_count[i] = 0; if (a.status) atomicOr(a.status, FL_STATUS_SLOT_OVERFLOW); }
         return;
     }
-    const int64_t row = a.entry_row ? static_cast<int64_t>(a.entry_row[i]) : find_row(a.row_ptr, a.rows, i);
     const int64_t src = a.ent[i];
+    EntryInfo e;
+    if (a.info) {
+        e = a.info[i];
+    } else {
+        e.row = static_cast<int32_t>(find_row(a.row_ptr, a.rows, i));
+        e.g0o = a.ori.gptr[src]; e.g1o = a.ori.gptr[src + 1];
+        e.g0i = a.inv.gptr[src]; e.g1i = a.inv.gptr[src + 1];
+    }
+    const int64_t row = e.row;
     const float v = a.val[i];
     const float *wrow = a.w + row * a.n;
     const int64_t out = a.slot_base[i];
@@ -319,7 +390,7 @@ __device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, StageBuf
         const uint8_t *vis = dir ? a.vis_inv : a.vis_ori;
         const int64_t off = dir ? a.r_size : 0;
         const float *wdir = wrow + off;
-        const int64_t g0 = sd.gptr[src], g1 = sd.gptr[src + 1];
+        const int64_t g0 = dir ? e.g0i : e.g0o, g1 = dir ? e.g1i : e.g1o;
         if (g0 == g1) continue;
         bool use_thr = false, staged = false;
         uint32_t thr = 0;
@@ -374,10 +445,12 @@ __device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, StageBuf
                 if (!use_thr) {
                     take = pos ? cnt : 0;
                 } else {
+                    // chunks without a key at or above the threshold take nothing
+                    if (!__any_sync(kFull, valid && pos && key >= thr)) continue;
                     const bool tie = valid && pos && key == thr;
-                    const int64_t tcnt = tie ? cnt : 0;
-                    const int64_t tincl = warp_inclusive_scan(tcnt);
-                    const int64_t texcl = tincl - tcnt + tie_seen;
+                    const int32_t tcnt = tie ? cnt : 0;
+                    const int32_t tincl = warp_inclusive_scan(tcnt);
+                    const int64_t texcl = static_cast<int64_t>(tincl - tcnt) + tie_seen;
                     tie_seen += __shfl_sync(kFull, tincl, 31);
                     if (!pos || key < thr) take = 0;
                     else if (key > thr) take = cnt;
@@ -498,7 +571,7 @@ __device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, StageBuf
 }
 
 // Sampled c2: one warp per entry.
-__global__ void __launch_bounds__(kExpandWarps * 32, 3) hop_expand_sampled_kernel(ExpandArgs a) {
+__global__ void __launch_bounds__(kExpandWarps * 32, 2) hop_expand_sampled_kernel(ExpandArgs a) {
     __shared__ WarpScratch scratch[kExpandWarps];
     const int wib = threadIdx.x >> 5;
     const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kExpandWarps;
@@ -507,95 +580,110 @@ __global__ void __launch_bounds__(kExpandWarps * 32, 3) hop_expand_sampled_kerne
         expand_entry_warp<true>(a, scratch[wib], nullptr, i);
 }
 
-// One side of one entry expanded by an 8-lane team (at most kTeam groups):
-// one group per lane, the threshold by all-pairs comparison, then the taken
-// edges kTeam at a time.  Returns the updated fact count of the entry.
-__device__ __forceinline__ int64_t team_side(const ExpandArgs &a, const Side &sd, const uint8_t *vis,
-                                             const float *wdir, int32_t off, float v, int64_t g0, int64_t g1,
-                                             unsigned tm, int tl, int tbase, int64_t out, int64_t written,
-                                             bool skip_nonpos, bool drop_masked, bool edge_w, bool edge_score) {
-    const bool valid = tl < (g1 - g0);
-    const int64_t g = g0 + tl;
-    const int32_t rel = valid ? sd.grel[g] : 0;
-    const int32_t cnt = valid ? sd.gcount[g] : 0;
-    const int32_t start = valid ? sd.gstart[g] : 0;
-    const float wg = valid ? wdir[rel] : 0.0f;
-    int32_t take;
-    if (!skip_nonpos) {
-        take = cnt;
-    } else {
-        const bool pos = wg > 0.0f;
-        const int64_t c = pos ? cnt : 0;
-        int64_t total = c;
+// c2 take of the (at most kTeam) groups of one side held one per team lane:
+// the threshold by all-pairs comparison of the keys (flashlog.cu:26-63), ties
+// at the threshold taken in group order.
+__device__ __forceinline__ int32_t team_take(float wg, int32_t cnt, int64_t topk, bool skip_nonpos, unsigned tm,
+                                             int tl, int tbase) {
+    if (!skip_nonpos) return cnt;
+    const bool pos = wg > 0.0f;
+    const int64_t c = pos ? cnt : 0;
+    int64_t total = c;
 #pragma unroll
-        for (int o = 1; o < kTeam; o <<= 1) total += __shfl_xor_sync(tm, total, o, kTeam);
-        if (a.topk >= kNoBudget || total <= a.topk) {
-            take = pos ? cnt : 0;
-        } else {
-            const uint32_t key = pos ? __float_as_uint(wg) : 0u;
-            int64_t ge = 0, gt = 0;
+    for (int o = 1; o < kTeam; o <<= 1) total += __shfl_xor_sync(tm, total, o, kTeam);
+    if (topk >= kNoBudget || total <= topk) return pos ? cnt : 0;
+    const uint32_t key = pos ? __float_as_uint(wg) : 0u;
+    int64_t ge = 0, gt = 0;
 #pragma unroll
-            for (int j = 0; j < kTeam; ++j) {
-                const uint32_t kj = __shfl_sync(tm, key, j, kTeam);
-                const int64_t cj = __shfl_sync(tm, c, j, kTeam);
-                ge += kj >= key ? cj : 0;
-                gt += kj > key ? cj : 0;
-            }
-            const unsigned q = (__ballot_sync(tm, c > 0 && gt < a.topk && ge >= a.topk) >> tbase) & 0xffu;
-            const int srcl = __ffs(q) - 1;  // one lane holds the threshold key when the total exceeds the budget
-            const uint32_t thr = __shfl_sync(tm, key, srcl, kTeam);
-            const int64_t keep = a.topk - __shfl_sync(tm, gt, srcl, kTeam);
-            // ties at the threshold are taken in group order
-            const int64_t tc = (pos && key == thr) ? c : 0;
-            int64_t tincl = tc;
-#pragma unroll
-            for (int o = 1; o < kTeam; o <<= 1) {
-                const int64_t u = __shfl_up_sync(tm, tincl, o, kTeam);
-                if (tl >= o) tincl += u;
-            }
-            const int64_t texcl = tincl - tc;
-            if (!pos || key < thr) take = 0;
-            else if (key > thr) take = cnt;
-            else {
-                const int64_t left = keep - texcl;
-                take = left > 0 ? static_cast<int32_t>(left < cnt ? left : cnt) : 0;
-            }
-        }
+    for (int j = 0; j < kTeam; ++j) {
+        const uint32_t kj = __shfl_sync(tm, key, j, kTeam);
+        const int64_t cj = __shfl_sync(tm, c, j, kTeam);
+        ge += kj >= key ? cj : 0;
+        gt += kj > key ? cj : 0;
     }
-    int32_t incl = take;
+    const unsigned q = (__ballot_sync(tm, c > 0 && gt < topk && ge >= topk) >> tbase) & 0xffu;
+    const int srcl = __ffs(q) - 1;  // one lane holds the threshold key when the total exceeds the budget
+    const uint32_t thr = __shfl_sync(tm, key, srcl, kTeam);
+    const int64_t keep = topk - __shfl_sync(tm, gt, srcl, kTeam);
+    const int32_t tc = (pos && key == thr) ? cnt : 0;
+    int32_t tincl = tc;
 #pragma unroll
     for (int o = 1; o < kTeam; o <<= 1) {
-        const int32_t u = __shfl_up_sync(tm, incl, o, kTeam);
-        if (tl >= o) incl += u;
+        const int32_t u = __shfl_up_sync(tm, tincl, o, kTeam);
+        if (tl >= o) tincl += u;
     }
-    const int32_t tot = __shfl_sync(tm, incl, kTeam - 1, kTeam);
-    const float prod = v * wg;
+    const int64_t texcl = tincl - tc;
+    if (!pos || key < thr) return 0;
+    if (key > thr) return cnt;
+    const int64_t left = keep - texcl;
+    return left > 0 ? static_cast<int32_t>(left < cnt ? left : cnt) : 0;
+}
+
+__device__ __forceinline__ int32_t team_incl(int32_t x, unsigned tm, int tl) {
+#pragma unroll
+    for (int o = 1; o < kTeam; o <<= 1) {
+        const int32_t u = __shfl_up_sync(tm, x, o, kTeam);
+        if (tl >= o) x += u;
+    }
+    return x;
+}
+
+// One entry with at most kTeam groups on each side, expanded by an 8-lane
+// team: both sides' groups are loaded together (lane tl holds group tl of
+// each side), then the taken edges of both sides are emitted kTeam at a time
+// in canonical order (ori facts, then inv facts).  Returns the fact count.
+__device__ __forceinline__ int64_t team_entry(const ExpandArgs &a, const float *wrow, float v, int64_t g0o,
+                                              int64_t g1o, int64_t g0i, int64_t g1i, unsigned tm, int tl, int tbase,
+                                              int64_t out, bool skip_nonpos, bool drop_masked, bool edge_w,
+                                              bool edge_score) {
+    const bool vo = tl < (g1o - g0o), vi = tl < (g1i - g0i);
+    const int32_t rel_o = vo ? a.ori.grel[g0o + tl] : 0, rel_i = vi ? a.inv.grel[g0i + tl] : 0;
+    const int32_t cnt_o = vo ? a.ori.gcount[g0o + tl] : 0, cnt_i = vi ? a.inv.gcount[g0i + tl] : 0;
+    const int32_t st_o = vo ? a.ori.gstart[g0o + tl] : 0, st_i = vi ? a.inv.gstart[g0i + tl] : 0;
+    const float w_o = vo ? wrow[rel_o] : 0.0f, w_i = vi ? wrow[a.r_size + rel_i] : 0.0f;
+    const int32_t take_o = team_take(w_o, cnt_o, a.topk, skip_nonpos, tm, tl, tbase);
+    const int32_t take_i = team_take(w_i, cnt_i, a.topk, skip_nonpos, tm, tl, tbase);
+    const int32_t incl_o = team_incl(vo ? take_o : 0, tm, tl), incl_i = team_incl(vi ? take_i : 0, tm, tl);
+    const int32_t tot_o = __shfl_sync(tm, incl_o, kTeam - 1, kTeam);
+    const int32_t tot = tot_o + __shfl_sync(tm, incl_i, kTeam - 1, kTeam);
+    const float prod_o = v * w_o, prod_i = v * w_i;
+    const int32_t rel_i_abs = rel_i + static_cast<int32_t>(a.r_size);
+    int64_t written = 0;
     for (int32_t f0 = 0; f0 < tot; f0 += kTeam) {
         const int32_t f = f0 + tl;
         const bool act = f < tot;
-        int k = 0;  // the group holding fact f: lanes whose inclusive count is <= f
+        const bool inv = f >= tot_o;
+        const int32_t fs = inv ? f - tot_o : f;
+        int ko = 0, ki = 0;  // the group holding fact fs: lanes whose inclusive count is <= fs
 #pragma unroll
-        for (int j = 0; j < kTeam; ++j) k += (__shfl_sync(tm, incl, j, kTeam) <= f) ? 1 : 0;
-        k = k < kTeam ? k : kTeam - 1;
-        const int32_t prev = __shfl_sync(tm, incl, k > 0 ? k - 1 : 0, kTeam);
-        const int32_t sk = __shfl_sync(tm, start, k, kTeam);
-        const float pk = __shfl_sync(tm, prod, k, kTeam);
-        const int32_t rk = __shfl_sync(tm, rel, k, kTeam);
+        for (int j = 0; j < kTeam; ++j) {
+            ko += (__shfl_sync(tm, incl_o, j, kTeam) <= fs) ? 1 : 0;
+            ki += (__shfl_sync(tm, incl_i, j, kTeam) <= fs) ? 1 : 0;
+        }
+        ko = ko < kTeam ? ko : kTeam - 1;
+        ki = ki < kTeam ? ki : kTeam - 1;
+        const int32_t prev_o = __shfl_sync(tm, incl_o, ko > 0 ? ko - 1 : 0, kTeam);
+        const int32_t prev_i = __shfl_sync(tm, incl_i, ki > 0 ? ki - 1 : 0, kTeam);
+        const int32_t s_o = __shfl_sync(tm, st_o, ko, kTeam), s_i = __shfl_sync(tm, st_i, ki, kTeam);
+        const float p_o = __shfl_sync(tm, prod_o, ko, kTeam), p_i = __shfl_sync(tm, prod_i, ki, kTeam);
+        const int32_t r_o = __shfl_sync(tm, rel_o, ko, kTeam), r_i = __shfl_sync(tm, rel_i_abs, ki, kTeam);
         bool visible = false;
         int32_t dst = 0;
         float value = 0.0f, m = 1.0f;
         if (act) {
-            const int64_t p = static_cast<int64_t>(sk) + (f - (k > 0 ? prev : 0));
-            fact_mask(a, sd, vis, p, drop_masked, edge_w, edge_score, &m, &visible);
+            const Side &sd = inv ? a.inv : a.ori;
+            const int64_t p = inv ? static_cast<int64_t>(s_i) + (fs - (ki > 0 ? prev_i : 0))
+                                  : static_cast<int64_t>(s_o) + (fs - (ko > 0 ? prev_o : 0));
+            fact_mask(a, sd, inv ? a.vis_inv : a.vis_ori, p, drop_masked, edge_w, edge_score, &m, &visible);
             dst = sd.col[p];
-            value = pk * m;
+            value = (inv ? p_i : p_o) * m;
         }
         const unsigned ball = (__ballot_sync(tm, act && visible) >> tbase) & 0xffu;
         if (act && visible) {
             const int64_t pos = out + written + __popc(ball & ((1u << tl) - 1u));
             a.fact_dst[pos] = dst;
             a.fact_val[pos] = value;
-            a.fact_rel[pos] = static_cast<int16_t>(rk + off);
+            a.fact_rel[pos] = static_cast<int16_t>(inv ? r_i : r_o);
             if (a.fact_m) a.fact_m[pos] = m;
         }
         written += __popc(ball);
@@ -624,26 +712,28 @@ __global__ void __launch_bounds__(kExpandWarps * 32, 3) hop_expand_kernel(Expand
         const int64_t i = base + team;
         const bool mine = i < S_live;
         bool small = false, over = false;
-        int64_t src = 0, g0o = 0, g1o = 0, g0i = 0, g1i = 0;
+        int64_t src = 0, out = 0, end = 0;
+        EntryInfo e{0, 0, 0, 0, 0};
+        float v = 0.0f;
         if (mine) {
-            over = a.capacity > 0 && a.slot_base[i + 1] > a.capacity;
+            out = a.slot_base[i];
+            end = a.slot_base[i + 1];
+            over = a.capacity > 0 && end > a.capacity;
             src = a.ent[i];
-            g0o = a.ori.gptr[src]; g1o = a.ori.gptr[src + 1];
-            g0i = a.inv.gptr[src]; g1i = a.inv.gptr[src + 1];
-            small = !over && (g1o - g0o) <= kTeam && (g1i - g0i) <= kTeam;
+            v = a.val[i];
+            if (a.info) {
+                e = a.info[i];
+            } else {
+                e.g0o = a.ori.gptr[src]; e.g1o = a.ori.gptr[src + 1];
+                e.g0i = a.inv.gptr[src]; e.g1i = a.inv.gptr[src + 1];
+            }
+            small = !over && (e.g1o - e.g0o) <= kTeam && (e.g1i - e.g0i) <= kTeam;
         }
         if (small) {
-            const int64_t row = a.entry_row ? static_cast<int64_t>(a.entry_row[i]) : find_row(a.row_ptr, a.rows, i);
-            const float v = a.val[i];
+            const int64_t row = a.info ? static_cast<int64_t>(e.row) : find_row(a.row_ptr, a.rows, i);
             const float *wrow = a.w + row * a.n;
-            const int64_t out = a.slot_base[i], end = a.slot_base[i + 1];
-            int64_t written = 0;
-            if (g1o > g0o)
-                written = team_side(a, a.ori, a.vis_ori, wrow, 0, v, g0o, g1o, tm, tl, tbase, out, written,
-                                    skip_nonpos, drop_masked, edge_w, edge_score);
-            if (g1i > g0i)
-                written = team_side(a, a.inv, a.vis_inv, wrow + a.r_size, static_cast<int32_t>(a.r_size), v, g0i, g1i,
-                                    tm, tl, tbase, out, written, skip_nonpos, drop_masked, edge_w, edge_score);
+            int64_t written = team_entry(a, wrow, v, e.g0o, e.g1o, e.g0i, e.g1i, tm, tl, tbase, out, skip_nonpos,
+                                         drop_masked, edge_w, edge_score);
             if (!wot_i) {
                 if (tl == 0) {
                     const int64_t pos = out + written;
@@ -1380,7 +1470,7 @@ int hop_plan(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *ent,
     if (S > 0) {
         launch(hop_capacity_kernel, static_cast<unsigned>((S + 255) / 256), 256, 0, st, ent, row_ptr, p->rows, S,
                make_side(ori, nullptr), make_side(inv, nullptr), p->topk_edges, (p->flags & FL_WOT_I) ? 1 : 0, cap,
-               p->entry_row);
+               reinterpret_cast<EntryInfo *>(p->entry_info));
     }
     int rc = exclusive_scan<int64_t>(cap, S, slot_base, scan_ws, sws, st);
     if (rc) return rc;
@@ -1403,7 +1493,7 @@ int hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *en
     a.topk = p->topk_edges; a.flags = p->flags; a.seed = p->sampling_seed; a.L = p->L; a.w = w;
     a.ori = make_side(ori, mask_csr_ori); a.inv = make_side(inv, mask_csr_inv);
     a.mask_triple = mask_triple; a.edge_weight = edge_weight; a.slot_base = slot_base;
-    a.vis_ori = p->vis_ori; a.vis_inv = p->vis_inv; a.entry_row = p->entry_row; a.work = p->work;
+    a.vis_ori = p->vis_ori; a.vis_inv = p->vis_inv; a.info = reinterpret_cast<const EntryInfo *>(p->entry_info); a.work = p->work;
     a.fact_dst = fact_dst; a.fact_val = fact_val; a.fact_rel = fact_rel; a.fact_m = fact_m; a.entry_count = entry_count;
     int sms = fl_device_sm_count();
     const int64_t per_sm = 3;  // resident CTAs per SM (registers and staging buffers)

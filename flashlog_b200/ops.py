@@ -204,10 +204,10 @@ class HopForward:
 
 
 def hop_params(rows, Lch, n, r_size, E, topk_edges, flags, seed=-1, eps=EPS, slot_capacity=0, status=None,
-               entry_row=None, vis=None, work=None):
+               entry_info=None, vis=None, work=None):
     return L.fl_hop_params(rows, Lch, n, r_size, E, int(min(topk_edges, L.NO_BUDGET)), int(flags), int(seed),
                            float(eps), int(slot_capacity), None if status is None else status.data_ptr(),
-                           None if entry_row is None else entry_row.data_ptr(),
+                           None if entry_info is None else entry_info.data_ptr(),
                            None if vis is None else vis[0].data_ptr(), None if vis is None else vis[1].data_ptr(),
                            None if work is None else work.data_ptr())
 
@@ -261,13 +261,13 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
     slot_base = torch.empty(S + 1, dtype=torch.int64, device=dev)
     ws = _ws(lib().fl_hop_workspace(rows, S), dev)
     total = ctypes.c_int64(0)
-    entry_row = torch.empty(max(S, 1), dtype=torch.int32, device=dev)
+    entry_info = torch.empty(5 * max(S, 1), dtype=torch.int32, device=dev)
     if vis is not None and (len(vis) != 2 or any(v.numel() < graph.csr[1].numel() or v.dtype != torch.uint8
                                                  for v in vis)):
         raise ValueError("vis must be the two u8 CSR-ordered visibility arrays of csr_visibility")
     work = torch.empty(1, dtype=torch.int32, device=dev)
     params = hop_params(rows, Lch, n, r_size, graph.E, topk_edges, flags, seed, eps, slot_capacity or 0, status,
-                        entry_row, vis, work)
+                        entry_info, vis, work)
     check(lib().fl_hop_plan(ctypes.byref(params), _p(row_ptr), _p(ent), S, graph.ori, graph.inv, _p(slot_base),
                             ctypes.byref(total) if sync else None, _p(ws), ws.numel(), _stream()), "hop_plan")
     T = max(total.value, 1) if sync else max(int(slot_capacity), 1)

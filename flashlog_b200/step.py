@@ -113,7 +113,7 @@ class DrumTrainStep:
         # transient, shared by the hops
         Smax, Fmax = max(self.S), max(self.F)
         self.ent_sel = _buf(Smax, i32, dev)
-        self.entry_row = _buf(Smax, i32, dev)
+        self.entry_info = _buf(5 * Smax, i32, dev)
         self.fact_dst = _buf(Fmax, i32, dev)
         self.fact_val = _buf(Fmax, f32, dev)
         self.grad_sel = _buf(Smax, f32, dev)
@@ -153,7 +153,7 @@ class DrumTrainStep:
 
     def _params(self, t, flags):
         return L.fl_hop_params(self.rows, self.N, self.n, self.r_size, self.graph.E, int(self.topk), int(flags), -1,
-                               float(self.eps), int(self.F[t]), self.status.data_ptr(), self.entry_row.data_ptr(),
+                               float(self.eps), int(self.F[t]), self.status.data_ptr(), self.entry_info.data_ptr(),
                                self.vis[0].data_ptr(), self.vis[1].data_ptr(), self.work.data_ptr())
 
     # ------------------------------------------------------------------

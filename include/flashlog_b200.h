@@ -66,9 +66,10 @@ typedef struct {
     int64_t slot_capacity;          /* > 0: length of the fact / output buffers;
                                        work beyond it is skipped and flagged      */
     int32_t *status;                /* device int (or NULL): FL_STATUS_* bits     */
-    int32_t *entry_row;             /* i32[S] or NULL: row of each entry, written by
+    int32_t *entry_info;            /* i32[5 * S] or NULL: per entry its row and the
+                                       group ranges of both sides, written by
                                        fl_hop_plan and read by fl_hop_expand (NULL:
-                                       the expansion finds rows by binary search) */
+                                       the expansion looks them up)               */
     const uint8_t *vis_ori, *vis_inv; /* u8[M] or NULL: CSR-ordered visibility from
                                        fl_csr_visibility; replaces the mask_triple
                                        read through `order` (same result)         */
