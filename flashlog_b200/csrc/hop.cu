@@ -130,6 +130,8 @@ struct ExpandArgs {
     const float *edge_weight;
     const int64_t *slot_base;
     const EntryInfo *info;             // may be null: rows and group ranges looked up
+    const uint16_t *rel_order;         // per (row, direction): relations by (w desc, id asc), or null
+    const int32_t *rel_npos;           // per (row, direction): relations with w > 0
     uint32_t *work;                    // work-queue counter (zeroed before the launch) or null
     int32_t *fact_dst;
     float *fact_val;
@@ -358,6 +360,112 @@ __device__ __forceinline__ double splitmix_phase(int64_t seed, int64_t b, int64_
     return static_cast<double>(z >> 11) * 0x1.0p-53;
 }
 
+// c2 of one dense side (many groups, degree above the budget) by walking the
+// row's relations in (w descending, id ascending) order, 32 at a time, and
+// finding the side's group of each relation by binary search in the staged
+// group relations.  Taking edges in walk order until the budget is spent is
+// the reference's rule (flashlog.cu:26-63): groups above the threshold whole,
+// groups at it in group order.  The taken groups are then emitted in group
+// order.  Returns false, with nothing written, when more than 32 groups take
+// edges (the caller then uses the staged threshold).
+__device__ bool walk_side(const ExpandArgs &a, WarpScratch &ws, StageBuf *stg, const Side &sd, const uint8_t *vis,
+                          const float *wdir, int64_t off, int64_t row, int dir, float v, int64_t g0, int64_t g1,
+                          int64_t out, int64_t *written, bool drop_masked, bool edge_w, bool edge_score) {
+    const int lane = threadIdx.x & 31;
+    const int n = static_cast<int>(g1 - g0);
+    const int32_t budget = static_cast<int32_t>(a.topk);
+    uint16_t *rels = stg->cnt;  // the side's group relations, ascending (CSR group order)
+    for (int j = lane; j < n; j += 32) rels[j] = static_cast<uint16_t>(sd.grel[g0 + j]);
+    __syncwarp();
+    const uint16_t *ord = a.rel_order + (row * 2 + dir) * a.r_size;
+    const int32_t npos = a.rel_npos[row * 2 + dir];
+    int32_t cum = 0;
+    int ntaken = 0;
+    for (int32_t k0 = 0; k0 < npos && cum < budget; k0 += 32) {
+        const int32_t k = k0 + lane;
+        const bool has = k < npos;
+        const uint16_t rel = has ? ord[k] : 0;
+        int lo = 0, hi = n;  // first group with relation >= rel
+        while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (rels[mid] < rel) lo = mid + 1; else hi = mid;
+        }
+        const bool found = has && lo < n && rels[lo] == rel;
+        const int32_t cnt = found ? sd.gcount[g0 + lo] : 0;
+        const int32_t cc = cnt < budget ? cnt : budget;
+        const int32_t incl = warp_inclusive_scan(cc);
+        const int32_t left = budget - (cum + incl - cc);
+        const int32_t take = found && left > 0 ? (left < cnt ? left : cnt) : 0;
+        const unsigned b = __ballot_sync(kFull, take > 0);
+        if (take > 0) {
+            const int p = ntaken + __popc(b & lanemask_lt());
+            if (p < 32) { ws.ckey[p] = static_cast<uint32_t>(lo); ws.ccnt[p] = static_cast<uint32_t>(take); }
+        }
+        ntaken += __popc(b);
+        cum += __shfl_sync(kFull, incl, 31);
+    }
+    __syncwarp();
+    if (ntaken > 32) return false;
+    // taken groups in group order: rank by group index (distinct)
+    const bool mine = lane < ntaken;
+    const uint32_t gi = mine ? ws.ckey[lane] : 0xffffffffu;
+    const int32_t tk = mine ? static_cast<int32_t>(ws.ccnt[lane]) : 0;
+    int rank = 0;
+#pragma unroll 8
+    for (int j = 0; j < 32; ++j) rank += __shfl_sync(kFull, gi, j) < gi ? 1 : 0;
+    __syncwarp();
+    if (mine) { ws.quota[rank] = tk; ws.incl[rank] = static_cast<int32_t>(gi); }
+    __syncwarp();
+    const int32_t take = lane < ntaken ? ws.quota[lane] : 0;
+    const int32_t g = lane < ntaken ? ws.incl[lane] : 0;
+    int32_t rel = 0;
+    float wg = 0.0f;
+    int32_t start = 0;
+    if (lane < ntaken) {
+        rel = rels[g];
+        wg = wdir[rel];
+        start = sd.gstart[g0 + g];
+    }
+    const int32_t incl = warp_inclusive_scan(take);
+    const int32_t tot = __shfl_sync(kFull, incl, 31);
+    __syncwarp();
+    ws.incl[lane] = incl;
+    ws.start[lane] = start;
+    ws.prod[lane] = v * wg;
+    ws.rel[lane] = rel + static_cast<int32_t>(off);
+    __syncwarp();
+    int64_t wr = *written;
+    for (int32_t f0 = 0; f0 < tot; f0 += 32) {
+        const int32_t f = f0 + lane;
+        const bool act = f < tot;
+        bool visible = false;
+        int32_t dst = 0, frel = 0;
+        float value = 0.0f, m = 1.0f;
+        if (act) {
+            int lo = 0, hi = 31;  // first lane with incl > f
+            while (lo < hi) { int mid = (lo + hi) >> 1; if (ws.incl[mid] > f) hi = mid; else lo = mid + 1; }
+            const int32_t eoff = f - (lo ? ws.incl[lo - 1] : 0);
+            const int64_t p = static_cast<int64_t>(ws.start[lo]) + eoff;
+            fact_mask(a, sd, vis, p, drop_masked, edge_w, edge_score, &m, &visible);
+            dst = sd.col[p];
+            value = ws.prod[lo] * m;
+            frel = ws.rel[lo];
+        }
+        const unsigned ball = __ballot_sync(kFull, act && visible);
+        if (act && visible) {
+            const int64_t pos = out + wr + __popc(ball & lanemask_lt());
+            a.fact_dst[pos] = dst;
+            a.fact_val[pos] = value;
+            a.fact_rel[pos] = static_cast<int16_t>(frel);
+            if (a.fact_m) a.fact_m[pos] = m;
+        }
+        wr += __popc(ball);
+    }
+    __syncwarp();
+    *written = wr;
+    return true;
+}
+
 // One source entry expanded by a whole warp: ori groups, inv groups, identity.
 template <bool kSampled>
 __device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, StageBuf *stg, int64_t i) {
@@ -427,6 +535,12 @@ __device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, StageBuf
                 q_prefix = 0;
             }
         } else if (skip_nonpos && a.topk < kNoBudget) {
+            if (stg != nullptr && a.rel_order != nullptr && g1 - g0 > 32 && g1 - g0 <= kStage && a.topk < 65536 &&
+                (g1 - g0) * 8 >= a.r_size &&
+                static_cast<int64_t>(sd.gstart[g1 - 1]) + sd.gcount[g1 - 1] - sd.gstart[g0] > a.topk &&
+                walk_side(a, ws, stg, sd, vis, wdir, off, row, dir, v, g0, g1, out, &written, drop_masked, edge_w,
+                          edge_score))
+                continue;
             use_thr = group_threshold(wdir, sd, g0, g1, a.topk, ws, stg, &staged, &thr, &keep_thr);
         }
         int64_t tie_seen = 0;
@@ -1425,6 +1539,47 @@ __global__ void __launch_bounds__(256) normalize_backward_kernel(const int64_t *
     for (int64_t i = a0 + threadIdx.x; i < a1; i += 256) gx[i] = g[i] / d - corr;
 }
 
+// Per (row, direction): the relations j in [0, R) with w[row, dir * R + j] > 0
+// ordered by (w descending, j ascending), by a bitonic sort of 64-bit keys in
+// shared memory.  One CTA per (row, direction).
+__global__ void __launch_bounds__(1024) rel_order_kernel(const float *w, int64_t n, int64_t R, int P, uint16_t *order,
+                                                         int32_t *npos) {
+    extern __shared__ __align__(16) unsigned long long keys[];
+    __shared__ int cnt_scratch[33];
+    const int64_t rd = blockIdx.x;
+    const int64_t row = rd >> 1, dir = rd & 1;
+    const float *wd = w + row * n + dir * R;
+    int c = 0;
+    for (int j = threadIdx.x; j < P; j += blockDim.x) {
+        unsigned long long k = ~0ull;
+        if (j < R) {
+            const float x = wd[j];
+            if (x > 0.0f) {
+                k = (static_cast<unsigned long long>(0xffffffffu - __float_as_uint(x)) << 32) | static_cast<unsigned>(j);
+                ++c;
+            }
+        }
+        keys[j] = k;
+    }
+    const int total = block_sum(c, cnt_scratch);
+    for (int k = 2; k <= P; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < P; i += blockDim.x) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const unsigned long long a = keys[i], b = keys[ixj];
+                    const bool up = (i & k) == 0;
+                    if ((a > b) == up) { keys[i] = b; keys[ixj] = a; }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    for (int j = threadIdx.x; j < total; j += blockDim.x)
+        order[rd * R + j] = static_cast<uint16_t>(keys[j] & 0xffffu);
+    if (threadIdx.x == 0) npos[rd] = total;
+}
+
 }  // namespace
 
 // ===========================================================================
@@ -1435,6 +1590,23 @@ static Side make_side(const fl_csr_side &s, const float *mask_csr) {
     d.row_ptr = s.row_ptr; d.col = s.col; d.order = s.order; d.gptr = s.group_ptr;
     d.gstart = s.group_start; d.gcount = s.group_count; d.grel = s.group_rel; d.mask_csr = mask_csr;
     return d;
+}
+
+int relation_order(const float *w, int64_t rows, int64_t r_size, uint16_t *order, int32_t *npos, cudaStream_t st) {
+    FL_REQUIRE(r_size > 0 && r_size <= 16384, "relation order supports 1..16384 relations per direction");
+    int P = 1;
+    while (P < r_size) P <<= 1;
+    const size_t smem = static_cast<size_t>(P) * sizeof(unsigned long long);
+    static bool attr_set = false;
+    if (!attr_set) {
+        FL_CUDA(cudaFuncSetAttribute(rel_order_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(16384 * sizeof(unsigned long long))));
+        attr_set = true;
+    }
+    if (rows > 0)
+        launch(rel_order_kernel, static_cast<unsigned>(rows * 2), 1024, smem, st, w, 2 * r_size + 1, r_size, P, order,
+               npos);
+    return check_launch("relation_order");
 }
 
 int csr_visibility(const int32_t *order, int64_t m, const uint8_t *mask_triple, uint8_t *vis, cudaStream_t st) {
@@ -1494,6 +1666,7 @@ int hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *en
     a.ori = make_side(ori, mask_csr_ori); a.inv = make_side(inv, mask_csr_inv);
     a.mask_triple = mask_triple; a.edge_weight = edge_weight; a.slot_base = slot_base;
     a.vis_ori = p->vis_ori; a.vis_inv = p->vis_inv; a.info = reinterpret_cast<const EntryInfo *>(p->entry_info); a.work = p->work;
+    a.rel_order = p->rel_order; a.rel_npos = p->rel_npos;
     a.fact_dst = fact_dst; a.fact_val = fact_val; a.fact_rel = fact_rel; a.fact_m = fact_m; a.entry_count = entry_count;
     int sms = fl_device_sm_count();
     const int64_t per_sm = 3;  // resident CTAs per SM (registers and staging buffers)

@@ -204,12 +204,27 @@ class HopForward:
 
 
 def hop_params(rows, Lch, n, r_size, E, topk_edges, flags, seed=-1, eps=EPS, slot_capacity=0, status=None,
-               entry_info=None, vis=None, work=None):
+               entry_info=None, vis=None, work=None, rel_order=None):
     return L.fl_hop_params(rows, Lch, n, r_size, E, int(min(topk_edges, L.NO_BUDGET)), int(flags), int(seed),
                            float(eps), int(slot_capacity), None if status is None else status.data_ptr(),
                            None if entry_info is None else entry_info.data_ptr(),
                            None if vis is None else vis[0].data_ptr(), None if vis is None else vis[1].data_ptr(),
-                           None if work is None else work.data_ptr())
+                           None if work is None else work.data_ptr(),
+                           None if rel_order is None else rel_order[0].data_ptr(),
+                           None if rel_order is None else rel_order[1].data_ptr())
+
+
+def relation_order(w, r_size: int):
+    """Per (row, direction) relations with w > 0 by (w desc, id asc); None
+    when r_size is outside the supported range (the expansion then selects
+    thresholds without it)."""
+    if not (0 < r_size <= 16384):
+        return None
+    rows = w.numel() // (2 * r_size + 1)
+    order = torch.empty(max(rows * 2 * r_size, 1), dtype=torch.int16, device=w.device)
+    npos = torch.empty(max(rows * 2, 1), dtype=torch.int32, device=w.device)
+    check(lib().fl_relation_order(_p(w), rows, r_size, _p(order), _p(npos), _stream()), "relation_order")
+    return order, npos
 
 
 def csr_visibility(graph: Graph, mask_triple):
@@ -266,8 +281,10 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
                                                  for v in vis)):
         raise ValueError("vis must be the two u8 CSR-ordered visibility arrays of csr_visibility")
     work = torch.empty(1, dtype=torch.int32, device=dev)
+    rel_order = (relation_order(w, r_size) if (flags & L.FL_SKIP_NONPOS_W) and topk_edges < L.NO_BUDGET
+                 and not (flags & L.FL_SAMPLED) else None)
     params = hop_params(rows, Lch, n, r_size, graph.E, topk_edges, flags, seed, eps, slot_capacity or 0, status,
-                        entry_info, vis, work)
+                        entry_info, vis, work, rel_order)
     check(lib().fl_hop_plan(ctypes.byref(params), _p(row_ptr), _p(ent), S, graph.ori, graph.inv, _p(slot_base),
                             ctypes.byref(total) if sync else None, _p(ws), ws.numel(), _stream()), "hop_plan")
     T = max(total.value, 1) if sync else max(int(slot_capacity), 1)

@@ -75,6 +75,9 @@ typedef struct {
                                        read through `order` (same result)         */
     uint32_t *work;                 /* device u32 or NULL: work queue of fl_hop_expand
                                        (it zeroes it); NULL: static assignment    */
+    const uint16_t *rel_order;      /* u16[rows * 2 * r_size] or NULL: from
+                                       fl_relation_order of the same w            */
+    const int32_t *rel_npos;        /* i32[rows * 2] (with rel_order)            */
 } fl_hop_params;
 
 /* Device status bits set by the hop kernels. */
@@ -131,6 +134,15 @@ size_t fl_hop_workspace(int64_t rows, int64_t S);
 int fl_hop_plan(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *ent, int64_t S, fl_csr_side ori,
                 fl_csr_side inv, int64_t *slot_base, int64_t *total_slots, void *ws, size_t ws_bytes,
                 fl_stream_t stream);
+
+/* Per (row, direction): the relations with w > 0 ordered by (w descending,
+ * relation ascending), order u16[rows * 2 * r_size], and their count npos
+ * i32[rows * 2].  fl_hop_expand uses it (through fl_hop_params) to find the c2
+ * threshold of sides with many relation groups by walking the relations in
+ * weight order instead of selecting over all of the side's groups.
+ * r_size <= 16384. */
+int fl_relation_order(const float *w, int64_t rows, int64_t r_size, uint16_t *order, int32_t *npos,
+                      fl_stream_t stream);
 
 /* CSR-ordered visibility of one side: vis[p] = mask_triple[order[p]] != 0.
  * The gather of prepare_csr_masks / apply_mask_cuda (flashlog_kernel.py:225-255,
