@@ -58,7 +58,7 @@ class fl_hop_params(ctypes.Structure):
                 ("flags", ctypes.c_int64), ("sampling_seed", ctypes.c_int64), ("eps", ctypes.c_float),
                 ("slot_capacity", ctypes.c_int64), ("status", ctypes.c_void_p), ("entry_info", ctypes.c_void_p),
                 ("vis_ori", ctypes.c_void_p), ("vis_inv", ctypes.c_void_p), ("work", ctypes.c_void_p),
-                ("rel_order", ctypes.c_void_p), ("rel_npos", ctypes.c_void_p)]
+                ("rel_order", ctypes.c_void_p), ("rel_npos", ctypes.c_void_p), ("fact_edge", ctypes.c_void_p)]
 
 
 _P = ctypes.c_void_p
@@ -89,6 +89,8 @@ SIGNATURES = {
     "fl_hop_expand": (ctypes.c_int, [_PARAMS, _P, _P, _P, _I64, _P, _SIDE, _SIDE, _P, _P, _P, _P, _P, _P, _P, _P,
                                      _P, _P, _P]),
     "fl_reduce_workspace": (_SZ, [_I64, _I64]),
+    "fl_row_reduce_max": (ctypes.c_int, [_P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _I64, _P, _P, _P, _P, _P, _P,
+                                         _SZ, _P]),
     "fl_row_reduce": (ctypes.c_int, [_P, _I64, _I64, _P, _P, _P, _P, _I64, _P, ctypes.c_float, _P, _P, _P, _P, _P,
                                      _P, _P, _SZ, _P]),
     "fl_hop_backward_workspace": (_SZ, [_I64, _I64]),

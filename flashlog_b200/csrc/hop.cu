@@ -137,6 +137,7 @@ struct ExpandArgs {
     float *fact_val;
     int16_t *fact_rel;
     float *fact_m;
+    int32_t *fact_edge;                // triple id per fact (0 for identity) or null: the MAX tie key
     int32_t *entry_count;
 };
 
@@ -439,7 +440,7 @@ __device__ bool walk_side(const ExpandArgs &a, WarpScratch &ws, StageBuf *stg, c
         const int32_t f = f0 + lane;
         const bool act = f < tot;
         bool visible = false;
-        int32_t dst = 0, frel = 0;
+        int32_t dst = 0, frel = 0, edge = 0;
         float value = 0.0f, m = 1.0f;
         if (act) {
             int lo = 0, hi = 31;  // first lane with incl > f
@@ -450,6 +451,7 @@ __device__ bool walk_side(const ExpandArgs &a, WarpScratch &ws, StageBuf *stg, c
             dst = sd.col[p];
             value = ws.prod[lo] * m;
             frel = ws.rel[lo];
+            if (a.fact_edge) edge = sd.order[p];
         }
         const unsigned ball = __ballot_sync(kFull, act && visible);
         if (act && visible) {
@@ -458,6 +460,7 @@ __device__ bool walk_side(const ExpandArgs &a, WarpScratch &ws, StageBuf *stg, c
             a.fact_val[pos] = value;
             a.fact_rel[pos] = static_cast<int16_t>(frel);
             if (a.fact_m) a.fact_m[pos] = m;
+            if (a.fact_edge) a.fact_edge[pos] = edge;
         }
         wr += __popc(ball);
     }
@@ -644,7 +647,7 @@ __device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, StageBuf
                 const int32_t f = f0 + lane;
                 const bool act = f < tot;
                 bool visible = false;
-                int32_t dst = 0, frel = 0;
+                int32_t dst = 0, frel = 0, edge = 0;
                 float value = 0.0f, m = 1.0f;
                 if (act) {
                     int lo = 0, hi = 31;  // first lane with incl > f
@@ -655,6 +658,7 @@ __device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, StageBuf
                     dst = sd.col[p];
                     value = ws.prod[lo] * m;
                     frel = ws.rel[lo];
+                    if (a.fact_edge) edge = sd.order[p];
                 }
                 const unsigned ball = __ballot_sync(kFull, act && visible);
                 if (act && visible) {
@@ -663,6 +667,7 @@ __device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, StageBuf
                     a.fact_val[pos] = value;
                     a.fact_rel[pos] = static_cast<int16_t>(frel);
                     if (a.fact_m) a.fact_m[pos] = m;
+                    if (a.fact_edge) a.fact_edge[pos] = edge;
                 }
                 written += __popc(ball);
             }
@@ -676,6 +681,7 @@ __device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, StageBuf
             a.fact_val[pos] = v * wrow[a.n - 1];
             a.fact_rel[pos] = static_cast<int16_t>(a.n - 1);
             if (a.fact_m) a.fact_m[pos] = 1.0f;
+            if (a.fact_edge) a.fact_edge[pos] = 0;
         }
         written += 1;
     }
@@ -782,7 +788,7 @@ __device__ __forceinline__ int64_t team_entry(const ExpandArgs &a, const float *
         const float p_o = __shfl_sync(tm, prod_o, ko, kTeam), p_i = __shfl_sync(tm, prod_i, ki, kTeam);
         const int32_t r_o = __shfl_sync(tm, rel_o, ko, kTeam), r_i = __shfl_sync(tm, rel_i_abs, ki, kTeam);
         bool visible = false;
-        int32_t dst = 0;
+        int32_t dst = 0, edge = 0;
         float value = 0.0f, m = 1.0f;
         if (act) {
             const Side &sd = inv ? a.inv : a.ori;
@@ -791,6 +797,7 @@ __device__ __forceinline__ int64_t team_entry(const ExpandArgs &a, const float *
             fact_mask(a, sd, inv ? a.vis_inv : a.vis_ori, p, drop_masked, edge_w, edge_score, &m, &visible);
             dst = sd.col[p];
             value = (inv ? p_i : p_o) * m;
+            if (a.fact_edge) edge = sd.order[p];
         }
         const unsigned ball = (__ballot_sync(tm, act && visible) >> tbase) & 0xffu;
         if (act && visible) {
@@ -799,6 +806,7 @@ __device__ __forceinline__ int64_t team_entry(const ExpandArgs &a, const float *
             a.fact_val[pos] = value;
             a.fact_rel[pos] = static_cast<int16_t>(inv ? r_i : r_o);
             if (a.fact_m) a.fact_m[pos] = m;
+            if (a.fact_edge) a.fact_edge[pos] = edge;
         }
         written += __popc(ball);
     }
@@ -855,6 +863,7 @@ __global__ void __launch_bounds__(kExpandWarps * 32, 3) hop_expand_kernel(Expand
                     a.fact_val[pos] = v * wrow[a.n - 1];
                     a.fact_rel[pos] = static_cast<int16_t>(a.n - 1);
                     if (a.fact_m) a.fact_m[pos] = 1.0f;
+                    if (a.fact_edge) a.fact_edge[pos] = 0;
                 }
                 written += 1;
             }
@@ -908,7 +917,7 @@ constexpr int kRWarps = kRThreads / 32;
 constexpr int kDigits = 256;
 constexpr int kTileA = 16384;  // whole-row tile: key, val, idx[2]
 constexpr int kTileB = 12288;  // destination-range tile: key, val, idx[2], slot
-constexpr int kTileD = 8192;   // dense-window sub-tile
+constexpr int kTileD = 6144;   // dense-window sub-tile
 constexpr int kDenseW = 4096;  // dense window width (destinations)
 constexpr int kHistBits = 11;
 constexpr int kHistBins = 1 << kHistBits;
@@ -934,6 +943,8 @@ struct TileD {
     float acc[kDenseW];
     uint32_t oidx[kDenseW];
     uint32_t touched[kDenseW / 32];
+    unsigned long long bkey[kDenseW];  // MAX: winner's (source, triple id)
+    uint32_t bslot[kDenseW];           // MAX: winner's row-local slot
 };
 
 struct ReduceSmem {
@@ -966,7 +977,22 @@ struct ReduceArgs {
     float *out_sum;
     int64_t capacity;            // length of the fact / output buffers
     int32_t *status;             // device status bits (may be null)
+    // MAX coalesce (flashlog_kernel.py:399-478): each destination keeps its
+    // largest fact; ties go to the smaller source (ori < inv < identity, from
+    // the fact's relation column), then to the smaller triple id.  fact_pos
+    // gets -1 for the facts that do not win.
+    int max_mode;
+    int64_t r_size, n;
+    const int16_t *fact_rel;
+    const int32_t *fact_edge;
 };
+
+// Tie key of a fact for the MAX coalesce: (source, triple id).
+__device__ __forceinline__ unsigned long long max_tie_key(const ReduceArgs &a, int64_t slot) {
+    const int64_t rel = a.fact_rel[slot];
+    const unsigned long long src = rel == a.n - 1 ? 2ull : (rel >= a.r_size ? 1ull : 0ull);
+    return (src << 32) | static_cast<uint32_t>(a.fact_edge[slot]);
+}
 
 __device__ __forceinline__ int bits_for(int64_t width) {  // bits to represent width - 1
     int b = 0;
@@ -1071,7 +1097,7 @@ __device__ float emit_tile(const ReduceArgs &a, ReduceSmem &sm, const uint32_t *
         const uint32_t k = key[i];
         if (p == 0 || k != prev) { ++oi; segs[oi] = static_cast<uint16_t>(p); }
         prev = k;
-        if (a.fact_pos) a.fact_pos[s0 + slot_of(i)] = static_cast<int32_t>(*written + oi);
+        if (a.fact_pos && !a.max_mode) a.fact_pos[s0 + slot_of(i)] = static_cast<int32_t>(*written + oi);
     }
     const int nseg = static_cast<int>(tot);
     __syncthreads();
@@ -1079,17 +1105,39 @@ __device__ float emit_tile(const ReduceArgs &a, ReduceSmem &sm, const uint32_t *
     for (int sgi = threadIdx.x; sgi < nseg; sgi += kRThreads) {
         const int st = segs[sgi];
         const int en = sgi + 1 < nseg ? segs[sgi + 1] : n;
-        float x = 0.0f;
-        int q = st;
-        for (; q + 4 <= en; q += 4) {  // loads issued ahead of the dependent adds
-            const float v0 = val[perm[q]], v1 = val[perm[q + 1]], v2 = val[perm[q + 2]], v3 = val[perm[q + 3]];
-            x += v0;
-            x += v1;
-            x += v2;
-            x += v3;
-        }
-        for (; q < en; ++q) x += val[perm[q]];
         const int64_t o = *written + sgi;
+        float x = 0.0f;
+        if (a.max_mode) {
+            uint16_t bi = perm[st];
+            x = val[bi];
+            if (en - st > 1) {
+                unsigned long long bk = max_tie_key(a, s0 + slot_of(bi));
+                for (int q = st + 1; q < en; ++q) {
+                    const uint16_t i = perm[q];
+                    const float v = val[i];
+                    if (v > x) { x = v; bi = i; bk = max_tie_key(a, s0 + slot_of(i)); }
+                    else if (v == x) {
+                        const unsigned long long k = max_tie_key(a, s0 + slot_of(i));
+                        if (k < bk) { bi = i; bk = k; }
+                    }
+                }
+            }
+            if (a.fact_pos)
+                for (int q = st; q < en; ++q) {
+                    const uint16_t i = perm[q];
+                    a.fact_pos[s0 + slot_of(i)] = i == bi ? static_cast<int32_t>(o) : -1;
+                }
+        } else {
+            int q = st;
+            for (; q + 4 <= en; q += 4) {  // loads issued ahead of the dependent adds
+                const float v0 = val[perm[q]], v1 = val[perm[q + 1]], v2 = val[perm[q + 2]], v3 = val[perm[q + 3]];
+                x += v0;
+                x += v1;
+                x += v2;
+                x += v3;
+            }
+            for (; q < en; ++q) x += val[perm[q]];
+        }
         a.tmp_ent[s0 + o] = static_cast<int32_t>(lo + key[perm[st]]);
         a.tmp_x[s0 + o] = x;
         local += x;
@@ -1177,7 +1225,11 @@ __device__ float dense_window(const ReduceArgs &a, ReduceSmem &sm, int64_t s0, i
     TileD &t = sm.t.d;
     const int W = static_cast<int>(hi - lo);
     const int bits = bits_for(W);
-    for (int d = threadIdx.x; d < kDenseW; d += kRThreads) t.acc[d] = 0.0f;
+    for (int d = threadIdx.x; d < kDenseW; d += kRThreads) {
+        t.acc[d] = a.max_mode ? -INFINITY : 0.0f;
+        t.bkey[d] = ~0ull;
+        t.bslot[d] = 0xffffffffu;
+    }
     for (int d = threadIdx.x; d < kDenseW / 32; d += kRThreads) t.touched[d] = 0u;
     __syncthreads();
     int64_t from = 0;
@@ -1194,9 +1246,24 @@ __device__ float dense_window(const ReduceArgs &a, ReduceSmem &sm, int64_t s0, i
         for (int p = p0; p < p1; ++p) {
             const uint32_t k = t.key[perm[p]];
             if (!(p == 0 || k != t.key[perm[p - 1]])) continue;
-            float accv = t.acc[k];
-            for (int q = p; q < n && t.key[perm[q]] == k; ++q) accv += t.val[perm[q]];
-            t.acc[k] = accv;
+            if (a.max_mode) {
+                float bv = t.acc[k];
+                unsigned long long bk = t.bkey[k];
+                uint32_t bs = t.bslot[k];
+                for (int q = p; q < n && t.key[perm[q]] == k; ++q) {
+                    const uint16_t i = perm[q];
+                    const float v = t.val[i];
+                    const unsigned long long kk = max_tie_key(a, s0 + t.slot[i]);
+                    if (v > bv || (v == bv && kk < bk)) { bv = v; bk = kk; bs = t.slot[i]; }
+                }
+                t.acc[k] = bv;
+                t.bkey[k] = bk;
+                t.bslot[k] = bs;
+            } else {
+                float accv = t.acc[k];
+                for (int q = p; q < n && t.key[perm[q]] == k; ++q) accv += t.val[perm[q]];
+                t.acc[k] = accv;
+            }
             atomicOr(&t.touched[k >> 5], 1u << (k & 31));
         }
         __syncthreads();
@@ -1222,7 +1289,9 @@ __device__ float dense_window(const ReduceArgs &a, ReduceSmem &sm, int64_t s0, i
     if (a.fact_pos)
         for (int64_t j = threadIdx.x; j < ns; j += kRThreads) {
             const int32_t dd = a.fact_dst[s0 + j];
-            if (dd >= lo && dd < hi) a.fact_pos[s0 + j] = static_cast<int32_t>(t.oidx[dd - lo]);
+            if (dd >= lo && dd < hi)
+                a.fact_pos[s0 + j] = (!a.max_mode || t.bslot[dd - lo] == static_cast<uint32_t>(j))
+                                         ? static_cast<int32_t>(t.oidx[dd - lo]) : -1;
         }
     *written += nout;
     const float total = block_sum(local, sm.fscratch);
@@ -1437,7 +1506,9 @@ __global__ void __launch_bounds__(kBThreads) hop_backward_kernel(BackwardArgs a)
         float gv = 0.0f;
         for (int64_t f = lane; f < cnt; f += 32) {
             const int64_t slot = s0 + f;
-            const int64_t u = oa + a.fact_pos[slot];
+            const int32_t fp = a.fact_pos[slot];
+            if (fp < 0) continue;  // a fact that lost a MAX coalesce gets no gradient
+            const int64_t u = oa + fp;
             const float g = a.normalize ? (a.g_y[u] / dd - corr) : a.g_y[u];
             const int c = a.fact_rel[slot];
             const float m = a.fact_m ? a.fact_m[slot] : 1.0f;
@@ -1666,7 +1737,7 @@ int hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *en
     a.ori = make_side(ori, mask_csr_ori); a.inv = make_side(inv, mask_csr_inv);
     a.mask_triple = mask_triple; a.edge_weight = edge_weight; a.slot_base = slot_base;
     a.vis_ori = p->vis_ori; a.vis_inv = p->vis_inv; a.info = reinterpret_cast<const EntryInfo *>(p->entry_info); a.work = p->work;
-    a.rel_order = p->rel_order; a.rel_npos = p->rel_npos;
+    a.rel_order = p->rel_order; a.rel_npos = p->rel_npos; a.fact_edge = p->fact_edge;
     a.fact_dst = fact_dst; a.fact_val = fact_val; a.fact_rel = fact_rel; a.fact_m = fact_m; a.entry_count = entry_count;
     int sms = fl_device_sm_count();
     const int64_t per_sm = 3;  // resident CTAs per SM (registers and staging buffers)
@@ -1694,10 +1765,11 @@ int hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *en
     return check_launch("hop_expand");
 }
 
-int row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *slot_base, const int32_t *entry_count,
-               const int32_t *fact_dst, const float *fact_val, int64_t total_slots, int32_t *fact_pos, float eps,
-               int64_t *out_row_ptr, int32_t *out_ent, float *out_x, float *out_y, float *out_denom, int32_t *status,
-               void *ws, size_t ws_bytes, cudaStream_t st) {
+static int reduce_rows(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *slot_base,
+                       const int32_t *fact_dst, const float *fact_val, int64_t total_slots, int32_t *fact_pos,
+                       float eps, int64_t *out_row_ptr, int32_t *out_ent, float *out_x, float *out_y,
+                       float *out_denom, int32_t *status, int max_mode, int64_t r_size, const int16_t *fact_rel,
+                       const int32_t *fact_edge, void *ws, size_t ws_bytes, cudaStream_t st) {
     FL_REQUIRE(total_slots < (int64_t(1) << 32), "too many facts in one hop (%lld)", static_cast<long long>(total_slots));
     FL_REQUIRE(E < (int64_t(1) << 31), "entity count exceeds int32");
     Carve c(ws, ws_bytes);
@@ -1708,13 +1780,13 @@ int row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *s
     int32_t *tmp_ent = c.take<int32_t>(total_slots > 0 ? total_slots : 1);
     float *tmp_x = c.take<float>(total_slots > 0 ? total_slots : 1);
     FL_REQUIRE(out_count && out_sum && scan_ws && tmp_ent && tmp_x, "row_reduce workspace too small");
-    (void)entry_count;  // unfilled slots carry the destination -1
     if (rows > 0) {
         ReduceArgs a;
         a.row_ptr = row_ptr; a.rows = rows; a.slot_base = slot_base;
         a.fact_dst = fact_dst; a.fact_val = fact_val; a.E = E; a.fact_pos = fact_pos;
         a.tmp_ent = tmp_ent; a.tmp_x = tmp_x; a.out_count = out_count; a.out_sum = out_sum;
         a.capacity = total_slots; a.status = status;
+        a.max_mode = max_mode; a.r_size = r_size; a.n = 2 * r_size + 1; a.fact_rel = fact_rel; a.fact_edge = fact_edge;
         const size_t smem = sizeof(ReduceSmem);
         static bool attr_set = false;
         if (!attr_set) {
@@ -1732,6 +1804,24 @@ int row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *s
         launch(compact_kernel, static_cast<unsigned>(rows), 256, 0, st, row_ptr, slot_base, out_row_ptr, rows, tmp_ent, tmp_x,
                                                                      out_sum, eps, out_ent, out_x, out_y, out_denom);
     return check_launch("row_compact");
+}
+
+int row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *slot_base, const int32_t *entry_count,
+               const int32_t *fact_dst, const float *fact_val, int64_t total_slots, int32_t *fact_pos, float eps,
+               int64_t *out_row_ptr, int32_t *out_ent, float *out_x, float *out_y, float *out_denom, int32_t *status,
+               void *ws, size_t ws_bytes, cudaStream_t st) {
+    (void)entry_count;  // unfilled slots carry the destination -1
+    return reduce_rows(row_ptr, rows, E, slot_base, fact_dst, fact_val, total_slots, fact_pos, eps, out_row_ptr,
+                       out_ent, out_x, out_y, out_denom, status, 0, 0, nullptr, nullptr, ws, ws_bytes, st);
+}
+
+int row_reduce_max(const int64_t *row_ptr, int64_t rows, int64_t E, int64_t r_size, const int64_t *slot_base,
+                   const int32_t *fact_dst, const float *fact_val, const int16_t *fact_rel, const int32_t *fact_edge,
+                   int64_t total_slots, int32_t *fact_pos, int64_t *out_row_ptr, int32_t *out_ent, float *out_x,
+                   int32_t *status, void *ws, size_t ws_bytes, cudaStream_t st) {
+    FL_REQUIRE(fact_rel != nullptr && fact_edge != nullptr, "the MAX reduction needs fact relations and triple ids");
+    return reduce_rows(row_ptr, rows, E, slot_base, fact_dst, fact_val, total_slots, fact_pos, 1e-7f, out_row_ptr,
+                       out_ent, out_x, nullptr, nullptr, status, 1, r_size, fact_rel, fact_edge, ws, ws_bytes, st);
 }
 
 size_t row_reduce_workspace(int64_t rows, int64_t total_slots) {

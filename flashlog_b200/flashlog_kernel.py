@@ -509,15 +509,60 @@ def sampled_sparse_propagation(state, w, csr_struct, mask_values, r_size, weight
 
 
 class FlashLogFunctionSparse3DTopKMax(autograd.Function):
-    """Sparse MAX propagation (flashlog_kernel.py:1450-1626)."""
+    """Sparse MAX propagation of smDRUM / mmDRUM (flashlog_kernel.py:1450-1626), 33 positional arguments.
+
+    The top-k fill keeps hidden edges (value 0: the reference has no
+    visibility filter on this path); every destination keeps its largest fact,
+    ties going to the smaller source (ori, inv, identity) and then to the
+    smaller triple id (flashlog_kernel.py:399-478).  The backward sends each
+    output's gradient to its winning fact only (flashlog.cu:2363-2406).
+    """
 
     @staticmethod
-    def forward(ctx, *args):
-        raise NotImplementedError("sparse MAX propagation (smDRUM/mmDRUM) is not implemented in flashlog_b200 yet")
+    def forward(ctx, sp_batch, sp_level, sp_entity, sp_value, w,
+                ori_row_ptr, ori_col_ind, ori_r_ind, ori_order,
+                inv_row_ptr, inv_col_ind, inv_r_ind, inv_order,
+                ori_row_group_ptr, ori_group_rel, ori_group_edge_start, ori_group_edge_count,
+                inv_row_group_ptr, inv_group_rel, inv_group_edge_start, inv_group_edge_count,
+                mask_values, weight, B, L_, E, r_size, wot_i, topk_edges,
+                edge_weight_is_score=False, topk_nodes=None, cache_backward=True, sampling=False):
+        _cuda_or_raise(sp_value)
+        t0 = time.perf_counter()
+        graph = _graph_topk((ori_row_ptr, ori_col_ind, ori_r_ind, ori_order, inv_row_ptr, inv_col_ind, inv_r_ind,
+                             inv_order, ori_row_group_ptr, ori_group_rel, ori_group_edge_start,
+                             ori_group_edge_count, inv_row_group_ptr, inv_group_rel, inv_group_edge_start,
+                             inv_group_edge_count))
+        val = sp_value.detach().to(torch.float32).contiguous()
+        row_ptr, ent, bad = _rows(sp_batch, sp_level, sp_entity, B, L_, E, graph)
+        _check_bad(bad)
+        row_ptr, ent, val = _select_sources(ctx, row_ptr, ent, val, topk_nodes, sampling)
+        _kernel_log("sparse3d_topk_max.select", t0)
+        t0 = time.perf_counter()
+        wf = w.detach().to(torch.float32).contiguous()
+        _check_w(wf)
+        seed = int(torch.randint(0, 2 ** 63 - 1, ()).item()) if sampling else -1
+        flags = _topk_flags(weight, edge_weight_is_score, sampling, wot_i) & ~L.FL_DROP_MASKED
+        fw = ops.hop_forward(row_ptr, ent, val, wf, graph, r_size, int(topk_edges), flags,
+                             mask_triple=mask_values, edge_weight=None if weight is None else weight.detach(),
+                             seed=seed, reduce="max")
+        _kernel_log("sparse3d_topk_max.cuda_forward", t0)
+        ctx.fw = fw
+        ctx.save_for_backward(row_ptr, val, wf)
+        ctx.B, ctx.L, ctx.E = B, L_, E
+        if weight is not None and bool(getattr(weight, "requires_grad", False)):
+            raise NotImplementedError("learnable edge weights (--use_soft) are not supported by flashlog_b200 yet")
+        out = _coo(fw.out_row_ptr, fw.out_ent, fw.out_x, B, L_, E)
+        ctx.out_indices = out.indices()
+        return out
 
     @staticmethod
     def backward(ctx, grad_out):
-        raise NotImplementedError
+        row_ptr, val, wf = ctx.saved_tensors
+        g = _align_sparse_grad_to_output(grad_out, ctx.out_indices, ctx.L, ctx.E).to(torch.float32)
+        grad_val, grad_w = ops.hop_backward(ctx.fw, row_ptr, val, wf, g, normalize=False)
+        grad_val = _restore(ctx, grad_val)
+        grads = (None, None, None, grad_val, grad_w) + (None,) * 28
+        return grads[:len(ctx.needs_input_grad)]
 
 
 # ---------------------------------------------------------------------------

@@ -250,7 +250,7 @@ def csr_visibility(graph: Graph, mask_triple):
 def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int, flags: int, *,
                 mask_triple=None, mask_csr=None, edge_weight=None, seed: int = -1, eps: float = EPS,
                 keep_facts: bool = False, record: bool = True, timing=None, slot_capacity=None,
-                status=None, out_sync: bool = True, vis=None) -> HopForward:
+                status=None, out_sync: bool = True, vis=None, reduce: str = "sum") -> HopForward:
     """Expansion + per-row coalesce-sum + normalization of one hop.
 
     slot_capacity=None sizes the fact buffers exactly (one host sync for the
@@ -261,7 +261,12 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
     out_sync=False the fact count is still read (one sync) but the outputs keep
     that capacity and their live count stays on the device.  `vis` (from
     csr_visibility of the same mask) replaces the per-fact mask_triple read.
+    reduce="max" coalesces by MAX with exact winners instead
+    (FlashLogFunctionSparse3DTopKMax); its out_x holds the maxima, out_y is
+    None and fact_pos is -1 for the facts that did not win.
     """
+    if reduce not in ("sum", "max"):
+        raise ValueError("reduce must be 'sum' or 'max'")
     _require_cuda(row_ptr, ent, val, w)
     B, Lch, n = w.shape
     rows = B * Lch
@@ -315,7 +320,11 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
         edge_weight = edge_weight.reshape(-1).to(torch.float32).contiguous()
         if edge_weight.numel() < M:
             raise ValueError("edge weights must have one entry per triple")
-    fact_pos = torch.empty(T, dtype=torch.int32, device=dev) if record else None
+    fact_pos = torch.empty(T, dtype=torch.int32, device=dev) if (record or reduce == "max") else None
+    fact_edge = None
+    if reduce == "max":
+        fact_edge = torch.empty(T, dtype=torch.int32, device=dev)
+        params.fact_edge = fact_edge.data_ptr()
     out_row_ptr = torch.empty(rows + 1, dtype=torch.int64, device=dev)
     out_ent = torch.empty(T, dtype=torch.int32, device=dev)
     out_x = torch.empty(T, dtype=torch.float32, device=dev)
@@ -328,14 +337,22 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
     check(lib().fl_hop_expand(ctypes.byref(params), _p(row_ptr), _p(ent), _p(val), S, _p(w), graph.ori, graph.inv,
                               _p(mo), _p(mi), _p(mask_triple), _p(edge_weight), _p(slot_base), _p(fact_dst),
                               _p(fact_val), _p(fact_rel), _p(fact_m), _p(entry_count), _stream()), "hop_expand")
-    check(lib().fl_row_reduce(_p(row_ptr), rows, graph.E, _p(slot_base), _p(entry_count), _p(fact_dst), _p(fact_val),
-                              T, _p(fact_pos), ctypes.c_float(eps), _p(out_row_ptr), _p(out_ent), _p(out_x), _p(out_y),
-                              _p(out_denom), _p(status), _p(ws2), ws2.numel(), _stream()), "row_reduce")
+    if reduce == "max":
+        check(lib().fl_row_reduce_max(_p(row_ptr), rows, graph.E, r_size, _p(slot_base), _p(fact_dst), _p(fact_val),
+                                      _p(fact_rel), _p(fact_edge), T, _p(fact_pos), _p(out_row_ptr), _p(out_ent),
+                                      _p(out_x), _p(status), _p(ws2), ws2.numel(), _stream()), "row_reduce_max")
+    else:
+        check(lib().fl_row_reduce(_p(row_ptr), rows, graph.E, _p(slot_base), _p(entry_count), _p(fact_dst),
+                                  _p(fact_val), T, _p(fact_pos), ctypes.c_float(eps), _p(out_row_ptr), _p(out_ent),
+                                  _p(out_x), _p(out_y), _p(out_denom), _p(status), _p(ws2), ws2.numel(), _stream()),
+              "row_reduce")
     if timing is not None:
         timing.record_end()
     u = int(out_row_ptr[rows].item()) if (sync and out_sync) else T
+    params.fact_edge = None  # the buffer is not kept with the record
     return HopForward(params, slot_base, entry_count, fact_rel, fact_m, fact_pos, out_row_ptr, out_ent[:u],
-                      out_x[:u], out_y[:u], out_denom[:rows], total.value,
+                      out_x[:u], None if reduce == "max" else out_y[:u],
+                      None if reduce == "max" else out_denom[:rows], total.value,
                       fact_dst if keep_facts else None, fact_val if keep_facts else None)
 
 

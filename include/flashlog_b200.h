@@ -78,6 +78,9 @@ typedef struct {
     const uint16_t *rel_order;      /* u16[rows * 2 * r_size] or NULL: from
                                        fl_relation_order of the same w            */
     const int32_t *rel_npos;        /* i32[rows * 2] (with rel_order)            */
+    int32_t *fact_edge;             /* i32[slots] or NULL: fl_hop_expand writes each
+                                       fact's triple id (order[p]; 0 for identity),
+                                       the tie key of fl_row_reduce_max          */
 } fl_hop_params;
 
 /* Device status bits set by the hop kernels. */
@@ -179,6 +182,20 @@ int fl_row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t
                   const int32_t *fact_dst, const float *fact_val, int64_t total_slots, int32_t *fact_pos, float eps,
                   int64_t *out_row_ptr, int32_t *out_ent, float *out_x, float *out_y, float *out_denom,
                   int32_t *status, void *ws, size_t ws_bytes, fl_stream_t stream);
+
+/* MAX coalesce of expanded facts (FlashLogFunctionSparse3DTopKMax,
+ * flashlog_kernel.py:386-478): per (row, destination) the largest fact value;
+ * equal values go to the smaller source (ori < inv < identity, read from the
+ * fact's relation column: < r_size, < 2 r_size, 2 r_size) and then to the
+ * smaller triple id (fact_edge).  fact_pos gets the output index of every
+ * winning fact and -1 for the others, so fl_hop_backward (with
+ * FL_NO_NORMALIZE) sends gradients to the winners only
+ * (flashlog.cu:2363-2406).  Outputs are the unnormalized maxima. */
+int fl_row_reduce_max(const int64_t *row_ptr, int64_t rows, int64_t E, int64_t r_size, const int64_t *slot_base,
+                      const int32_t *fact_dst, const float *fact_val, const int16_t *fact_rel,
+                      const int32_t *fact_edge, int64_t total_slots, int32_t *fact_pos, int64_t *out_row_ptr,
+                      int32_t *out_ent, float *out_x, int32_t *status, void *ws, size_t ws_bytes,
+                      fl_stream_t stream);
 
 /* Hop backward (+ normalization backward unless FL_NO_NORMALIZE).  Replaces
  * flashlog_backward_sparse3d_cached_cuda (flashlog.cu:2317-2361) and

@@ -276,7 +276,10 @@ static int flo_i64_cmp(const void *a, const void *b) {
  * fact_m, fact_out (output position).  Identity facts use rel = n - 1, m = 1.
  * Returns the number of outputs; *n_facts receives the number of facts.
  */
-FLO_EXPORT int64_t flo_hop_forward(
+/* fact_edge (with fact_entry, may be NULL): triple id of each graph fact
+ * (order[p]) and 0 for identity facts: the tie key of the MAX coalesce
+ * (flashlog_kernel.py:399-478, meta_edge of flashlog.cu:1539-1557). */
+FLO_EXPORT int64_t flo_hop_forward_edges(
     int64_t nnz, const int64_t *sp_row, const int64_t *sp_ent, const float *sp_val,
     const float *w, int64_t L, int64_t n, int64_t E, int64_t r_size,
     const int32_t *ori_col, const int32_t *ori_order, const int32_t *ori_gptr,
@@ -286,7 +289,7 @@ FLO_EXPORT int64_t flo_hop_forward(
     const float *mask_ori, const float *mask_inv, const uint8_t *mask_triple,
     const float *edge_weight, int64_t topk_edges, int64_t flags, int64_t sampling_seed,
     int64_t *out_key, float *out_val, int64_t *fact_entry, int32_t *fact_rel,
-    float *fact_m, int64_t *fact_out, int64_t *n_facts) {
+    float *fact_m, int64_t *fact_out, int64_t *fact_edge, int64_t *n_facts) {
     flo_side sides[2] = {
         {ori_col, ori_order, ori_gptr, ori_gstart, ori_gcount, ori_grel},
         {inv_col, inv_order, inv_gptr, inv_gstart, inv_gcount, inv_grel}};
@@ -309,7 +312,7 @@ FLO_EXPORT int64_t flo_hop_forward(
         ntouch = 0;
         row_fact_begin = nf;
         const float *w_row = w + row * n;
-#define FLO_ADD(dst, value, ent_i, relc, mval)                                   \
+#define FLO_ADD(dst, value, ent_i, relc, mval, edge_id)                          \
         do {                                                                      \
             int64_t d_ = (dst);                                                   \
             if (mark[d_] != row) {                                                \
@@ -322,7 +325,8 @@ FLO_EXPORT int64_t flo_hop_forward(
             }                                                                     \
             acc[d_] += (value);                                                   \
             if (fact_entry) { fact_entry[nf] = (ent_i); fact_rel[nf] = (int32_t)(relc); \
-                              fact_m[nf] = (mval); fact_out[nf] = d_; }           \
+                              fact_m[nf] = (mval); fact_out[nf] = d_;             \
+                              if (fact_edge) fact_edge[nf] = (edge_id); }         \
             ++nf;                                                                 \
         } while (0)
         for (int64_t i = s; i < e_end; ++i) {
@@ -367,11 +371,11 @@ FLO_EXPORT int64_t flo_hop_forward(
                             m = csr_mask[dir][p];
                             if ((flags & FLO_DROP_MASKED) && m == 0.0f) continue;
                         }
-                        FLO_ADD(sd->col[p], prod * m, i, rel + off, m);
+                        FLO_ADD(sd->col[p], prod * m, i, rel + off, m, (int64_t)sd->order[p]);
                     }
                 }
             }
-            if (!(flags & FLO_WOT_I)) FLO_ADD(src, sv * w_row[n - 1], i, n - 1, 1.0f);
+            if (!(flags & FLO_WOT_I)) FLO_ADD(src, sv * w_row[n - 1], i, n - 1, 1.0f, (int64_t)0);
         }
 #undef FLO_ADD
         qsort(touched, (size_t)ntouch, sizeof(int64_t), flo_i64_cmp);
@@ -389,6 +393,24 @@ FLO_EXPORT int64_t flo_hop_forward(
     free(acc); free(mark); free(slot); free(touched); free(take_buf);
     *n_facts = nf;
     return nu;
+}
+
+FLO_EXPORT int64_t flo_hop_forward(
+    int64_t nnz, const int64_t *sp_row, const int64_t *sp_ent, const float *sp_val,
+    const float *w, int64_t L, int64_t n, int64_t E, int64_t r_size,
+    const int32_t *ori_col, const int32_t *ori_order, const int32_t *ori_gptr,
+    const int16_t *ori_grel, const int32_t *ori_gstart, const int32_t *ori_gcount,
+    const int32_t *inv_col, const int32_t *inv_order, const int32_t *inv_gptr,
+    const int16_t *inv_grel, const int32_t *inv_gstart, const int32_t *inv_gcount,
+    const float *mask_ori, const float *mask_inv, const uint8_t *mask_triple,
+    const float *edge_weight, int64_t topk_edges, int64_t flags, int64_t sampling_seed,
+    int64_t *out_key, float *out_val, int64_t *fact_entry, int32_t *fact_rel,
+    float *fact_m, int64_t *fact_out, int64_t *n_facts) {
+    return flo_hop_forward_edges(nnz, sp_row, sp_ent, sp_val, w, L, n, E, r_size, ori_col, ori_order, ori_gptr,
+                                 ori_grel, ori_gstart, ori_gcount, inv_col, inv_order, inv_gptr, inv_grel, inv_gstart,
+                                 inv_gcount, mask_ori, mask_inv, mask_triple, edge_weight, topk_edges, flags,
+                                 sampling_seed, out_key, out_val, fact_entry, fact_rel, fact_m, fact_out, NULL,
+                                 n_facts);
 }
 
 /* Upper bound on facts for flo_hop_forward (degree sum + identity). */
@@ -428,6 +450,7 @@ FLO_EXPORT void flo_hop_backward(int64_t n_facts, const int64_t *fact_entry, con
         for (int64_t f = 0; f < n_facts; ++f) {
             int64_t c = fact_rel[f];
             if (c < lo || c >= hi) continue;
+            if (fact_out[f] < 0) continue;  /* a losing fact of a MAX coalesce */
             float g = g_out[fact_out[f]];
             if (g == 0.0f) continue;
             int64_t i = fact_entry[f];

@@ -30,6 +30,8 @@ EDGE_SCORE = 32
 MODE_TOPK = SKIP_NONPOS_W | DROP_MASKED | MASK_BY_TRIPLE   # flashlog.cu:1402-1559 + flashlog_kernel.py:1217-1228
 MODE_CPU = SKIP_NONPOS_W | DROP_MASKED                     # flashlog.cpp:506-578
 MODE_ALL_EDGES = 0                                         # flashlog.cu:1743-1829
+# The MAX path keeps hidden facts (value 0): flashlog_kernel.py:1450-1518 has no visibility filter.
+MODE_TOPK_MAX = SKIP_NONPOS_W | MASK_BY_TRIPLE
 
 
 def lib():
@@ -41,7 +43,7 @@ def lib():
         _lib = ctypes.CDLL(path)
         _lib.flo_group_threshold.restype = ctypes.c_float
         _lib.flo_sampling_phase.restype = ctypes.c_double
-        for name in ("flo_build_side", "flo_topc", "flo_hop_forward", "flo_fact_bound",
+        for name in ("flo_build_side", "flo_topc", "flo_hop_forward", "flo_hop_forward_edges", "flo_fact_bound",
                      "flo_fixed_relation", "flo_coalesce_sum"):
             getattr(_lib, name).restype = ctypes.c_int64
     return _lib
@@ -155,6 +157,80 @@ def hop_forward(row, ent, val, w, csr, r_size, E, topk_edges=1 << 60, mode=MODE_
         res.update(fact_entry=f_entry[:nf].copy(), fact_rel=f_rel[:nf].copy(),
                    fact_m=f_m[:nf].copy(), fact_out=f_out[:nf].copy())
     return res
+
+
+def max_coalesce(keys, values, source, tie):
+    """MAX coalesce with an exact winner (flashlog_kernel.py:399-478).
+
+    Per key: the largest value; among equal values the smallest source (0 ori,
+    1 inv, 2 identity), then the smallest tie key (triple id, 0 for identity),
+    then the earliest fact.  Returns (unique_keys, max_values, winner_index).
+    """
+    keys = np.asarray(keys, np.int64)
+    values = np.asarray(values, np.float32)
+    if keys.size == 0:
+        return keys[:0], values[:0], np.zeros(0, np.int64)
+    pos = np.arange(keys.size)
+    order = np.lexsort((pos, np.asarray(tie, np.int64), np.asarray(source, np.int64), -values, keys))
+    sk = keys[order]
+    first = np.ones(sk.size, bool)
+    first[1:] = sk[1:] != sk[:-1]
+    win = order[first]
+    return keys[win], values[win], win
+
+
+def hop_forward_max(row, ent, val, w, csr, r_size, E, topk_edges=1 << 60, mask=None, wot_i=False):
+    """One hop of FlashLogFunctionSparse3DTopKMax (flashlog_kernel.py:1450-1518):
+    the top-k fill without the visibility filter (hidden edges give facts of
+    value 0), then the MAX coalesce with exact winners.
+
+    Returns a dict with out_key, out_val and the recorded facts (entry, rel,
+    m, edge, value, source) in emission order, fact_out = output index of a
+    winning fact and -1 for the others.
+    """
+    row, ent, val = _c(row, np.int64), _c(ent, np.int64), _c(val, np.float32)
+    w = _c(w, np.float32)
+    B, L, n = w.shape
+    nnz = row.size
+    ori_rp, ori_col, _, ori_order, inv_rp, inv_col, _, inv_order = csr[:8]
+    ori_gptr, ori_grel, ori_gstart, ori_gcount, inv_gptr, inv_grel, inv_gstart, inv_gcount = csr[8:]
+    flags = MODE_TOPK_MAX | (WOT_I if wot_i else 0)
+    if mask is None:
+        mask = np.ones(ori_col.size, np.uint8)
+    mask_triple = _c(np.asarray(mask).reshape(-1) != 0, np.uint8)
+    cap = max(int(lib().flo_fact_bound(ctypes.c_int64(nnz), _p(ent), _p(_c(ori_rp, np.int32)),
+                                        _p(_c(inv_rp, np.int32)))), 1)
+    out_key = np.empty(cap, np.int64)
+    out_val = np.empty(cap, np.float32)
+    f_entry = np.empty(cap, np.int64)
+    f_rel = np.empty(cap, np.int32)
+    f_m = np.empty(cap, np.float32)
+    f_out = np.empty(cap, np.int64)
+    f_edge = np.empty(cap, np.int64)
+    nf = ctypes.c_int64(0)
+    arrs = [_c(a, t) for a, t in ((ori_col, np.int32), (ori_order, np.int32), (ori_gptr, np.int32),
+                                   (ori_grel, np.int16), (ori_gstart, np.int32), (ori_gcount, np.int32),
+                                   (inv_col, np.int32), (inv_order, np.int32), (inv_gptr, np.int32),
+                                   (inv_grel, np.int16), (inv_gstart, np.int32), (inv_gcount, np.int32))]
+    u = lib().flo_hop_forward_edges(
+        ctypes.c_int64(nnz), _p(row), _p(ent), _p(val), _p(w), ctypes.c_int64(L), ctypes.c_int64(n),
+        ctypes.c_int64(E), ctypes.c_int64(r_size), *[_p(a) for a in arrs],
+        None, None, _p(mask_triple), None, ctypes.c_int64(int(min(topk_edges, 1 << 62))),
+        ctypes.c_int64(flags), ctypes.c_int64(-1),
+        _p(out_key), _p(out_val), _p(f_entry), _p(f_rel), _p(f_m), _p(f_out), _p(f_edge), ctypes.byref(nf))
+    nf = nf.value
+    sum_keys = out_key[:u]
+    f_entry, f_rel, f_m, f_edge = f_entry[:nf], f_rel[:nf], f_m[:nf], f_edge[:nf]
+    keys = sum_keys[f_out[:nf]]
+    # fact values as the fill writes them: (v * w) * m in fp32
+    prod = (val[f_entry] * w.reshape(B * L, n)[row[f_entry], f_rel]).astype(np.float32)
+    values = (prod * f_m).astype(np.float32)
+    source = np.where(f_rel == n - 1, 2, np.where(f_rel >= r_size, 1, 0))
+    ukeys, uvals, win = max_coalesce(keys, values, source, f_edge)
+    fact_out = np.full(nf, -1, np.int64)
+    fact_out[win] = np.arange(win.size)
+    return dict(out_key=ukeys, out_val=uvals, n_facts=nf, fact_entry=f_entry, fact_rel=f_rel, fact_m=f_m,
+                fact_edge=f_edge, fact_value=values, fact_source=source, fact_out=fact_out)
 
 
 def hop_backward(fw, g_out, row, val, w, r_size):

@@ -153,6 +153,42 @@ def main():
                     f"{name}_grad_w": wt.grad.numpy()})
     np.savez_compressed(os.path.join(HERE, "hop_config1.npz"), names=np.array([s[0] for s in specs]), **hop)
 
+    # --- MAX coalesce (FlashLogFunctionSparse3DTopKMax, flashlog_kernel.py:1450-1518):
+    # raw facts as the top-k fill emits them (hidden edges kept at value 0, the
+    # triple id as tie key), from the C oracle, reduced by the reference's own
+    # _coalesce_sparse3d_max_raw_parts (flashlog_kernel.py:399-478).
+    from oracle import oracle as O
+    csr_np = tuple(c.numpy() for c in csr1)
+    rng = np.random.default_rng(35)
+    mx = {}
+    mspecs = [("max_ties", 3, True, 6, False), ("max_topk200", 200, False, 30, False),
+              ("max_wot_i", 4, True, 10, True), ("max_notopk", 1 << 60, True, 8, False)]
+    for name, topk, ties, per_row, wot_i in mspecs:
+        B, L = 4, 3
+        row, ent, val = _state(rng, B, L, E, per_row, zero_frac=0.05, ties=ties)
+        w = _w(rng, B, L, n, ties)
+        mask = (rng.random(train.shape[0]) > 0.2).astype(np.uint8)
+        fw = O.hop_forward_max(row, ent, val, w, csr_np, Rr, E, topk_edges=topk, mask=mask, wot_i=wot_i)
+        fb, fl_ = row[fw["fact_entry"]] // L, row[fw["fact_entry"]] % L
+        # destination of every fact: the output it belongs to in the SUM coalesce of the same facts
+        dst = np.empty(fw["n_facts"], np.int64)
+        sfw = O.hop_forward(row, ent, val, w, csr_np, Rr, E, topk_edges=topk,
+                            mode=O.SKIP_NONPOS_W | O.MASK_BY_TRIPLE, mask=mask, wot_i=wot_i)
+        dst[:] = sfw["out_key"][sfw["fact_out"]] % E
+        parts = []
+        for src_id in range(3):
+            sel = np.nonzero(fw["fact_source"] == src_id)[0]
+            t = lambda a, d=torch.long: torch.from_numpy(np.ascontiguousarray(a)).to(d)
+            parts.append((src_id, t(fb[sel]), t(fl_[sel]), t(dst[sel]), t(fw["fact_value"][sel], torch.float32),
+                          t(fw["fact_edge"][sel])))
+        sp, ukeys, win_source, win_raw, out_vals = fk._coalesce_sparse3d_max_raw_parts(tuple(parts), B, L, E)
+        mx.update({f"{name}_row": row, f"{name}_ent": ent, f"{name}_val": val, f"{name}_w": w,
+                   f"{name}_mask": mask, f"{name}_topk": np.array(min(topk, 1 << 62)),
+                   f"{name}_wot_i": np.array(wot_i), f"{name}_out_key": ukeys.numpy(),
+                   f"{name}_out_val": out_vals.numpy(), f"{name}_win_source": win_source.numpy(),
+                   f"{name}_win_raw": win_raw.numpy()})
+    np.savez_compressed(os.path.join(HERE, "max_config1.npz"), names=np.array([s[0] for s in mspecs]), **mx)
+
     # --- three-hop DRUM propagation + readout + loss (src/model_DRUM_kernel_sp.py:92-204)
     rng = np.random.default_rng(41)
     from flashlog_b200.synthetic import training_queries

@@ -438,3 +438,65 @@ def test_threshold_paths_and_visibility(fk, topk):
         rgv, rgw = O.hop_backward(ref, g, row, val, w, R)
         np.testing.assert_allclose(gv.cpu().numpy(), rgv, rtol=RTOL, atol=1e-5)
         np.testing.assert_allclose(gw.cpu().numpy(), rgw, rtol=RTOL, atol=1e-5)
+
+
+@pytest.mark.parametrize("name", ["max_ties", "max_topk200", "max_wot_i", "max_notopk"])
+def test_sparse_max_matches_reference_golden(fk, g1, golden, name):
+    """FlashLogFunctionSparse3DTopKMax: outputs equal the reference MAX
+    coalesce (flashlog_kernel.py:399-478) fixture bit for bit; the backward
+    reaches only the winning facts (flashlog.cu:2363-2406), as in the oracle."""
+    cfg, train, csr_np, csr = g1
+    E, R = cfg.entities, cfg.relations
+    g = golden("max_config1.npz")
+    p = lambda k: g[f"{name}_{k}"]
+    row, ent, val, w, mask = p("row"), p("ent"), p("val"), p("w"), p("mask")
+    B, L = w.shape[0], w.shape[1]
+    topk, wot_i = int(p("topk")), bool(p("wot_i"))
+    sp, v = _sp(row, ent, val, B, L, E, requires_grad=True)
+    wt = _cuda(w).requires_grad_(True)
+    out = fk.FlashLogFunctionSparse3DTopKMax.apply(
+        sp.indices()[0], sp.indices()[1], sp.indices()[2], v, wt, *csr, _cuda(mask), None, B, L, E, R, wot_i, topk,
+        False, None, True, False)
+    assert np.array_equal(_keys(out, L, E), p("out_key"))
+    assert np.array_equal(out.values().detach().cpu().numpy(), p("out_val"))
+    ref = O.hop_forward_max(row, ent, val, w, csr_np, R, E, topk_edges=topk, mask=mask, wot_i=wot_i)
+    gout = np.random.default_rng(3).standard_normal(ref["out_key"].size).astype(np.float32)
+    (out.values() * _cuda(gout)).sum().backward()
+    rgv, rgw = O.hop_backward(ref, gout, row, val, w, R)
+    np.testing.assert_allclose(v.grad.cpu().numpy(), rgv, rtol=RTOL, atol=1e-6)
+    np.testing.assert_allclose(wt.grad.cpu().numpy(), rgw, rtol=RTOL, atol=1e-6)
+
+
+def test_sparse_max_large_rows(fk):
+    """MAX coalesce through the histogram-cut and dense-window paths (a hub
+    destination with more facts than a tile), against the oracle."""
+    from flashlog_b200 import ops
+    from flashlog_b200.ops import Graph
+    rng = np.random.default_rng(19)
+    E, R = 60_000, 6
+    h = rng.integers(0, 30_000, 120_000)
+    t = rng.integers(0, E, 120_000)
+    r = rng.integers(0, R, 120_000)
+    hub = E - 17
+    hs = np.repeat(np.arange(2500), R)
+    hr = np.tile(np.arange(R), 2500)
+    tri = np.unique(np.concatenate([np.stack([h, r, t], 1), np.stack([hs, hr, np.full(hs.size, hub)], 1)]), axis=0)
+    csr_np = O.build_csr(tri[:, 0], tri[:, 2], tri[:, 1], E)
+    tt = _cuda(tri)
+    csr = fk.build_csr_structure(tt[:, 0], tt[:, 2], tt[:, 1], E)
+    ent = np.concatenate([np.arange(0, 2500), np.sort(rng.choice(np.arange(2500, 30_000), 1500, replace=False))])
+    row = np.zeros(ent.size, np.int64)
+    val = (rng.integers(1, 4, ent.size) / 4.0).astype(np.float32)  # ties in value
+    w = _w(rng, 1, 1, 2 * R + 1, True)
+    mask = (rng.random(tri.shape[0]) > 0.1).astype(np.uint8)
+    rp, en, _ = ops.coo_to_rows(_cuda(row), _cuda(row * 0), _cuda(ent), 1, 1, E)
+    fw = ops.hop_forward(rp, en, _cuda(val), _cuda(w), Graph.of(csr), R, 1 << 62, 1, mask_triple=_cuda(mask),
+                         reduce="max")
+    ref = O.hop_forward_max(row, ent, val, w, csr_np, R, E, mask=mask)
+    assert np.array_equal(fw.out_ent.cpu().numpy().astype(np.int64), ref["out_key"] % E)
+    assert np.array_equal(fw.out_x.cpu().numpy(), ref["out_val"])
+    g = rng.standard_normal(ref["out_key"].size).astype(np.float32)
+    gv, gw = ops.hop_backward(fw, rp, _cuda(val), _cuda(w), _cuda(g), normalize=False)
+    rgv, rgw = O.hop_backward(ref, g, row, val, w, R)
+    np.testing.assert_allclose(gv.cpu().numpy(), rgv, rtol=RTOL, atol=1e-5)
+    np.testing.assert_allclose(gw.cpu().numpy(), rgw, rtol=RTOL, atol=1e-5)

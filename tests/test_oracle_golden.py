@@ -130,3 +130,28 @@ def test_drum3_matches_reference(golden):
     total = sum((ws[t] * torch.from_numpy(gws[t])).sum() for t in range(T))
     total.backward()
     np.testing.assert_allclose(logits.grad.numpy(), d["grad_logits"], rtol=1e-4, atol=1e-6)
+
+
+@pytest.mark.parametrize("name", ["max_ties", "max_topk200", "max_wot_i", "max_notopk"])
+def test_max_coalesce_matches_reference(golden, name):
+    """The MAX hop (FlashLogFunctionSparse3DTopKMax): outputs and exact winners
+    (source, position within that source's raw facts) equal what the
+    reference's _coalesce_sparse3d_max_raw_parts (flashlog_kernel.py:399-478)
+    computed from the same raw facts."""
+    g = golden("max_config1.npz")
+    cfg, train, csr = config1_graph()
+    E, R = cfg.entities, cfg.relations
+    p = lambda k: g[f"{name}_{k}"]
+    fw = O.hop_forward_max(p("row"), p("ent"), p("val"), p("w"), csr, R, E, topk_edges=int(p("topk")),
+                           mask=p("mask"), wot_i=bool(p("wot_i")))
+    assert np.array_equal(fw["out_key"], p("out_key"))
+    assert np.array_equal(fw["out_val"], p("out_val"))
+    win = np.nonzero(fw["fact_out"] >= 0)[0]
+    win = win[np.argsort(fw["fact_out"][win])]
+    src = fw["fact_source"]
+    within = np.empty(src.size, np.int64)
+    for s in range(3):
+        sel = src == s
+        within[sel] = np.arange(int(sel.sum()))
+    assert np.array_equal(src[win], p("win_source"))
+    assert np.array_equal(within[win], p("win_raw"))
