@@ -5,12 +5,15 @@ The names exported here are those of the reference package
 kernels behind the C ABI of include/flashlog_b200.h.
 """
 from .flashlog_kernel import (  # noqa: F401
+    FlashLogDenseMaxFunction,
+    FlashLogDenseSumFunction,
     FlashLogFunction,
     FlashLogFunctionSparse3DAllEdgesSum,
     FlashLogFunctionSparse3DTopKMax,
     FlashLogFunctionSparse3DTopKSum,
     Sparse3DNormalizeFunction,
     _compute_active_nodes,
+    _dense_topc_state,
     _group_starts_and_counts,
     build_csr_structure,
     configure_flashlog_cpu_threads,

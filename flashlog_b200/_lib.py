@@ -22,7 +22,11 @@ FL_WOT_I = 8
 FL_SAMPLED = 16
 FL_EDGE_SCORE = 32
 FL_EDGE_WEIGHT = 64
+FL_NO_ORI = 256
+FL_NO_INV = 512
+FL_EDGE_POS = 1024
 FL_NO_NORMALIZE = 1 << 20
+FL_MAX_BITS = 1
 NO_BUDGET = 1 << 62
 FL_STATUS_SLOT_OVERFLOW = 1
 
@@ -89,8 +93,8 @@ SIGNATURES = {
     "fl_hop_expand": (ctypes.c_int, [_PARAMS, _P, _P, _P, _I64, _P, _SIDE, _SIDE, _P, _P, _P, _P, _P, _P, _P, _P,
                                      _P, _P, _P]),
     "fl_reduce_workspace": (_SZ, [_I64, _I64]),
-    "fl_row_reduce_max": (ctypes.c_int, [_P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _I64, _P, _P, _P, _P, _P, _P,
-                                         _SZ, _P]),
+    "fl_row_reduce_max": (ctypes.c_int, [_P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _I64, _P, _P, _P, _P,
+                                         ctypes.c_int, _P, _P, _SZ, _P]),
     "fl_row_reduce": (ctypes.c_int, [_P, _I64, _I64, _P, _P, _P, _P, _I64, _P, ctypes.c_float, _P, _P, _P, _P, _P,
                                      _P, _P, _SZ, _P]),
     "fl_hop_backward_workspace": (_SZ, [_I64, _I64]),

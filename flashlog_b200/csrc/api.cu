@@ -207,10 +207,11 @@ size_t fl_reduce_workspace(int64_t rows, int64_t total_slots) { return row_reduc
 int fl_row_reduce_max(const int64_t *row_ptr, int64_t rows, int64_t E, int64_t r_size, const int64_t *slot_base,
                       const int32_t *fact_dst, const float *fact_val, const int16_t *fact_rel,
                       const int32_t *fact_edge, int64_t total_slots, int32_t *fact_pos, int64_t *out_row_ptr,
-                      int32_t *out_ent, float *out_x, int32_t *status, void *ws, size_t ws_bytes,
+                      int32_t *out_ent, float *out_x, int max_flags, int32_t *status, void *ws, size_t ws_bytes,
                       fl_stream_t stream) {
     return row_reduce_max(row_ptr, rows, E, r_size, slot_base, fact_dst, fact_val, fact_rel, fact_edge, total_slots,
-                          fact_pos, out_row_ptr, out_ent, out_x, status, ws, ws_bytes, as_stream(stream));
+                          fact_pos, out_row_ptr, out_ent, out_x, (max_flags & FL_MAX_BITS) ? 2 : 1, status, ws,
+                          ws_bytes, as_stream(stream));
 }
 
 int fl_row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *slot_base, const int32_t *entry_count,

@@ -59,12 +59,14 @@ struct EntryInfo {
 };
 
 __global__ void hop_capacity_kernel(const int32_t *ent, const int64_t *row_ptr, int64_t rows, int64_t S, Side ori,
-                                    Side inv, int64_t topk, int wot_i, int64_t *cap, EntryInfo *info) {
+                                    Side inv, int64_t topk, int wot_i, int sides, int64_t *cap, EntryInfo *info) {
     int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
     if (i >= S) return;
     if (i >= row_ptr[rows]) { cap[i] = 0; return; }  // beyond the live entries
     int64_t src = ent[i];
-    const int64_t g0o = ori.gptr[src], g1o = ori.gptr[src + 1], g0i = inv.gptr[src], g1i = inv.gptr[src + 1];
+    // sides: bit 0 forward, bit 1 inverse; a disabled side gets an empty group range
+    const int64_t g0o = ori.gptr[src], g1o = (sides & 1) ? ori.gptr[src + 1] : g0o;
+    const int64_t g0i = inv.gptr[src], g1i = (sides & 2) ? inv.gptr[src + 1] : g0i;
     if (info) {
         EntryInfo e;
         e.row = static_cast<int32_t>(find_row(row_ptr, rows, i));
@@ -451,7 +453,7 @@ __device__ bool walk_side(const ExpandArgs &a, WarpScratch &ws, StageBuf *stg, c
             dst = sd.col[p];
             value = ws.prod[lo] * m;
             frel = ws.rel[lo];
-            if (a.fact_edge) edge = sd.order[p];
+            if (a.fact_edge) edge = (a.flags & FL_EDGE_POS) ? static_cast<int32_t>(p) : sd.order[p];
         }
         const unsigned ball = __ballot_sync(kFull, act && visible);
         if (act && visible) {
@@ -488,8 +490,8 @@ __device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, StageBuf
         e = a.info[i];
     } else {
         e.row = static_cast<int32_t>(find_row(a.row_ptr, a.rows, i));
-        e.g0o = a.ori.gptr[src]; e.g1o = a.ori.gptr[src + 1];
-        e.g0i = a.inv.gptr[src]; e.g1i = a.inv.gptr[src + 1];
+        e.g0o = a.ori.gptr[src]; e.g1o = (a.flags & FL_NO_ORI) ? e.g0o : a.ori.gptr[src + 1];
+        e.g0i = a.inv.gptr[src]; e.g1i = (a.flags & FL_NO_INV) ? e.g0i : a.inv.gptr[src + 1];
     }
     const int64_t row = e.row;
     const float v = a.val[i];
@@ -658,7 +660,7 @@ __device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, StageBuf
                     dst = sd.col[p];
                     value = ws.prod[lo] * m;
                     frel = ws.rel[lo];
-                    if (a.fact_edge) edge = sd.order[p];
+                    if (a.fact_edge) edge = (a.flags & FL_EDGE_POS) ? static_cast<int32_t>(p) : sd.order[p];
                 }
                 const unsigned ball = __ballot_sync(kFull, act && visible);
                 if (act && visible) {
@@ -797,7 +799,7 @@ __device__ __forceinline__ int64_t team_entry(const ExpandArgs &a, const float *
             fact_mask(a, sd, inv ? a.vis_inv : a.vis_ori, p, drop_masked, edge_w, edge_score, &m, &visible);
             dst = sd.col[p];
             value = (inv ? p_i : p_o) * m;
-            if (a.fact_edge) edge = sd.order[p];
+            if (a.fact_edge) edge = (a.flags & FL_EDGE_POS) ? static_cast<int32_t>(p) : sd.order[p];
         }
         const unsigned ball = (__ballot_sync(tm, act && visible) >> tbase) & 0xffu;
         if (act && visible) {
@@ -846,8 +848,8 @@ __global__ void __launch_bounds__(kExpandWarps * 32, 3) hop_expand_kernel(Expand
             if (a.info) {
                 e = a.info[i];
             } else {
-                e.g0o = a.ori.gptr[src]; e.g1o = a.ori.gptr[src + 1];
-                e.g0i = a.inv.gptr[src]; e.g1i = a.inv.gptr[src + 1];
+                e.g0o = a.ori.gptr[src]; e.g1o = (a.flags & FL_NO_ORI) ? e.g0o : a.ori.gptr[src + 1];
+                e.g0i = a.inv.gptr[src]; e.g1i = (a.flags & FL_NO_INV) ? e.g0i : a.inv.gptr[src + 1];
             }
             small = !over && (e.g1o - e.g0o) <= kTeam && (e.g1i - e.g0i) <= kTeam;
         }
@@ -987,6 +989,15 @@ struct ReduceArgs {
     const int32_t *fact_edge;
 };
 
+// MAX order of values: fp32 order (mode 1) or the unsigned order of the fp32
+// bit patterns (mode 2, the packed CAS-max of the dense path).
+__device__ __forceinline__ bool max_greater(int mode, float v, float x) {
+    return mode == 2 ? __float_as_uint(v) > __float_as_uint(x) : v > x;
+}
+__device__ __forceinline__ bool max_equal(int mode, float v, float x) {
+    return mode == 2 ? __float_as_uint(v) == __float_as_uint(x) : v == x;
+}
+
 // Tie key of a fact for the MAX coalesce: (source, triple id).
 __device__ __forceinline__ unsigned long long max_tie_key(const ReduceArgs &a, int64_t slot) {
     const int64_t rel = a.fact_rel[slot];
@@ -1115,8 +1126,8 @@ __device__ float emit_tile(const ReduceArgs &a, ReduceSmem &sm, const uint32_t *
                 for (int q = st + 1; q < en; ++q) {
                     const uint16_t i = perm[q];
                     const float v = val[i];
-                    if (v > x) { x = v; bi = i; bk = max_tie_key(a, s0 + slot_of(i)); }
-                    else if (v == x) {
+                    if (max_greater(a.max_mode, v, x)) { x = v; bi = i; bk = max_tie_key(a, s0 + slot_of(i)); }
+                    else if (max_equal(a.max_mode, v, x)) {
                         const unsigned long long k = max_tie_key(a, s0 + slot_of(i));
                         if (k < bk) { bi = i; bk = k; }
                     }
@@ -1254,7 +1265,9 @@ __device__ float dense_window(const ReduceArgs &a, ReduceSmem &sm, int64_t s0, i
                     const uint16_t i = perm[q];
                     const float v = t.val[i];
                     const unsigned long long kk = max_tie_key(a, s0 + t.slot[i]);
-                    if (v > bv || (v == bv && kk < bk)) { bv = v; bk = kk; bs = t.slot[i]; }
+                    if (bs == 0xffffffffu || max_greater(a.max_mode, v, bv) || (max_equal(a.max_mode, v, bv) && kk < bk)) {
+                        bv = v; bk = kk; bs = t.slot[i];
+                    }
                 }
                 t.acc[k] = bv;
                 t.bkey[k] = bk;
@@ -1712,7 +1725,8 @@ int hop_plan(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *ent,
     (void)row_ptr;
     if (S > 0) {
         launch(hop_capacity_kernel, static_cast<unsigned>((S + 255) / 256), 256, 0, st, ent, row_ptr, p->rows, S,
-               make_side(ori, nullptr), make_side(inv, nullptr), p->topk_edges, (p->flags & FL_WOT_I) ? 1 : 0, cap,
+               make_side(ori, nullptr), make_side(inv, nullptr), p->topk_edges, (p->flags & FL_WOT_I) ? 1 : 0,
+               ((p->flags & FL_NO_ORI) ? 0 : 1) | ((p->flags & FL_NO_INV) ? 0 : 2), cap,
                reinterpret_cast<EntryInfo *>(p->entry_info));
     }
     int rc = exclusive_scan<int64_t>(cap, S, slot_base, scan_ws, sws, st);
@@ -1818,10 +1832,12 @@ int row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *s
 int row_reduce_max(const int64_t *row_ptr, int64_t rows, int64_t E, int64_t r_size, const int64_t *slot_base,
                    const int32_t *fact_dst, const float *fact_val, const int16_t *fact_rel, const int32_t *fact_edge,
                    int64_t total_slots, int32_t *fact_pos, int64_t *out_row_ptr, int32_t *out_ent, float *out_x,
-                   int32_t *status, void *ws, size_t ws_bytes, cudaStream_t st) {
+                   int max_mode, int32_t *status, void *ws, size_t ws_bytes, cudaStream_t st) {
     FL_REQUIRE(fact_rel != nullptr && fact_edge != nullptr, "the MAX reduction needs fact relations and triple ids");
+    FL_REQUIRE(max_mode == 1 || max_mode == 2, "bad MAX mode");
     return reduce_rows(row_ptr, rows, E, slot_base, fact_dst, fact_val, total_slots, fact_pos, 1e-7f, out_row_ptr,
-                       out_ent, out_x, nullptr, nullptr, status, 1, r_size, fact_rel, fact_edge, ws, ws_bytes, st);
+                       out_ent, out_x, nullptr, nullptr, status, max_mode, r_size, fact_rel, fact_edge, ws, ws_bytes,
+                       st);
 }
 
 size_t row_reduce_workspace(int64_t rows, int64_t total_slots) {

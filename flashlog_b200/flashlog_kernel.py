@@ -601,23 +601,249 @@ def _compute_active_nodes(A):
     return torch.unique(non_zero[:, 1])
 
 
+# ---------------------------------------------------------------------------
+# Dense [B, L, E] propagation (config-1 models: src/model_DRUM_kernel.py,
+# src/model_NeuralLP_kernel.py, src/model_{sm,mm}DRUM_kernel.py)
+# ---------------------------------------------------------------------------
+def _dense_state(A, active_nodes=None):
+    """Nonzero entries of A [B, L, E] (entities in active_nodes only, when given)
+    as a row layout in entity order; also their flat indices into A."""
+    B, L_, E = A.shape
+    BL = B * L_
+    Af = A.detach().reshape(BL, E)
+    nz = Af != 0
+    if active_nodes is not None:
+        act = torch.zeros(E, dtype=torch.bool, device=A.device)
+        if active_nodes.numel():
+            act[active_nodes.long()] = True
+        nz &= act.unsqueeze(0)
+    idx = nz.nonzero()
+    rows, ent = idx[:, 0], idx[:, 1]
+    counts = torch.bincount(rows, minlength=BL)
+    row_ptr = torch.zeros(BL + 1, dtype=torch.int64, device=A.device)
+    row_ptr[1:] = torch.cumsum(counts, 0)
+    val = Af[rows, ent].to(torch.float32).contiguous()
+    return row_ptr, ent.to(torch.int32).contiguous(), val, rows * E + ent
+
+
+@torch.no_grad()
+def _dense_topc_keep(A, topk_nodes):
+    """Boolean keep mask of the dense c1 selection (flashlog_kernel.py:814-842)."""
+    B, L_, E = A.shape
+    row_ptr, ent, val, flat = _dense_state(A)
+    _, _, _, src = ops.topc_select(row_ptr, ent, val, int(topk_nodes))
+    counts = row_ptr[1:] - row_ptr[:-1]
+    keep = torch.ones(B * L_ * E, dtype=torch.bool, device=A.device)
+    over = (counts > topk_nodes).repeat_interleave(E)  # rows over the budget keep their chosen entries only
+    keep[over] = False
+    keep[flat[src]] = True
+    return keep.view(B, L_, E)
+
+
+def _dense_topc_state(A, topk_nodes):
+    """Prune all propagation sources, identity included, per (item, rule)
+    (flashlog_kernel.py:814-842): the topk_nodes largest nonzero entries, ties
+    to the lower entity; rows with at most topk_nodes nonzeros stay whole."""
+    if topk_nodes is None:
+        return A
+    if topk_nodes < 0:
+        raise ValueError("topk_nodes/c must be nonnegative")
+    if topk_nodes >= A.shape[-1]:
+        return A
+    _cuda_or_raise(A)
+    keep = _dense_topc_keep(A, topk_nodes)
+    return A * keep
+
+
+def _dense_hops(A, w, graph, masks, r_size, wot_i, topk_edges, active_nodes, mode):
+    """Forward and inverse expansions of the nonzero entries of A, reduced per
+    (row, destination) by SUM or by MAX, as dense [B, L, E] outputs."""
+    B, L_, E = A.shape
+    BL = B * L_
+    n = w.shape[-1]
+    row_ptr, ent, val, flat = _dense_state(A, active_nodes)
+    wf = w.detach().reshape(B, L_, n).to(torch.float32).contiguous()
+    _check_w(wf)
+    topk = int(min(topk_edges, L.NO_BUDGET)) if topk_edges and topk_edges > 0 else L.NO_BUDGET
+    flags = L.FL_SKIP_NONPOS_W | L.FL_DROP_MASKED | L.FL_WOT_I
+    if mode == "max":
+        flags |= L.FL_EDGE_POS  # ties go to the lower CSR position (flashlog.cu:103-121)
+    outs, fws = [], []
+    for side_flag in (L.FL_NO_INV, L.FL_NO_ORI):
+        fw = ops.hop_forward(row_ptr, ent, val, wf, graph, r_size, topk, flags | side_flag, mask_csr=masks,
+                             reduce=mode, max_bits=(mode == "max"))
+        counts = fw.out_row_ptr[1:] - fw.out_row_ptr[:-1]
+        orow = torch.repeat_interleave(torch.arange(BL, device=A.device), counts)
+        oflat = orow * E + fw.out_ent.to(torch.int64)
+        dense = torch.zeros(BL * E, dtype=torch.float32, device=A.device)
+        dense[oflat] = fw.out_x
+        outs.append(dense.view(B, L_, E))
+        fws.append((fw, oflat))
+    out_ind = (A.detach().to(torch.float32) * wf[..., n - 1:n]) if not wot_i else torch.zeros_like(outs[0])
+    return out_ind, outs[0], outs[1], (row_ptr, val, flat, wf, fws)
+
+
+def _dense_backward(A, w, rec, grad_ind, grad_ori, grad_inv, wot_i):
+    row_ptr, val, flat, wf, fws = rec
+    B, L_, E = A.shape
+    n = wf.shape[-1]
+    gA = torch.zeros(B * L_ * E, dtype=torch.float32, device=A.device)
+    gw = torch.zeros_like(wf)
+    gv_total = torch.zeros_like(val)
+    for (fw, oflat), g in zip(fws, (grad_ori, grad_inv)):
+        if g is None:
+            continue
+        gy = g.reshape(-1).to(torch.float32)[oflat].contiguous()
+        gv, gws = ops.hop_backward(fw, row_ptr, val, wf, gy, normalize=False)
+        gv_total += gv
+        gw += gws
+    gA[flat] = gv_total
+    gA = gA.view(B, L_, E)
+    if grad_ind is not None and not wot_i:
+        gi = grad_ind.to(torch.float32)
+        gA = gA + gi * wf[..., n - 1:n]
+        gw[..., n - 1] += (gi * A.detach().to(torch.float32)).sum(-1)
+    return gA.to(A.dtype), gw.to(w.dtype)
+
+
 class FlashLogFunction(autograd.Function):
-    @staticmethod
-    def forward(ctx, *args):
-        raise NotImplementedError("the dense [B, L, E] propagation path is not implemented in flashlog_b200 yet")
+    """Dense propagation with CSR-ordered masks (flashlog_kernel.py:700-811): returns
+    (out_ind, out_ori, out_inv), each [B, L, E]; the caller sums them."""
 
     @staticmethod
-    def backward(ctx, *grads):
-        raise NotImplementedError
+    def forward(ctx, A, w, active_nodes,
+                ori_col_ind, ori_mask,
+                ori_row_group_ptr, ori_group_rel, ori_group_edge_start, ori_group_edge_count,
+                inv_col_ind, inv_mask,
+                inv_row_group_ptr, inv_group_rel, inv_group_edge_start, inv_group_edge_count,
+                r_size, wot_i, topk_edges):
+        _cuda_or_raise(A)
+        graph = _graph_groups(ori_col_ind, ori_row_group_ptr, ori_group_rel, ori_group_edge_start,
+                              ori_group_edge_count, inv_col_ind, inv_row_group_ptr, inv_group_rel,
+                              inv_group_edge_start, inv_group_edge_count)
+        masks = (ori_mask.reshape(-1).to(torch.float32).contiguous(),
+                 inv_mask.reshape(-1).to(torch.float32).contiguous())
+        out_ind, out_ori, out_inv, rec = _dense_hops(A, w, graph, masks, r_size, wot_i, topk_edges, active_nodes,
+                                                     "sum")
+        ctx.rec, ctx.wot_i = rec, wot_i
+        ctx.save_for_backward(A, w)
+        return out_ind.to(A.dtype), out_ori.to(A.dtype), out_inv.to(A.dtype)
+
+    @staticmethod
+    def backward(ctx, grad_ind, grad_ori, grad_inv):
+        A, w = ctx.saved_tensors
+        gA, gw = _dense_backward(A, w, ctx.rec, grad_ind, grad_ori, grad_inv, ctx.wot_i)
+        return (gA, gw) + (None,) * 16
 
 
-def vectorized_operation_csr(*args, **kwargs):
-    raise NotImplementedError("the dense [B, L, E] propagation path is not implemented in flashlog_b200 yet")
+def vectorized_operation_csr(A, w, csr_struct, mask_values, r_size, weight=None, wot_i=False,
+                             use_topk=False, topk_nodes=100000, topk_edges=0, prepared_masks=None):
+    """Dense entry point (flashlog_kernel.py:845-882): returns (s_i, s_h, s_t)."""
+    (ori_row_ptr, ori_col_ind, ori_r_ind, order_ori,
+     inv_row_ptr, inv_col_ind, inv_r_ind, order_inv,
+     ori_gp, ori_gr, ori_gs, ori_gc, inv_gp, inv_gr, inv_gs, inv_gc) = csr_struct
+    prepared = _prepared_mask_pair(prepared_masks) if prepared_masks is not None else _prepared_mask_pair(mask_values)
+    if prepared is not None:
+        ori_mask, inv_mask = prepared
+    else:
+        ori_mask, inv_mask = prepare_csr_masks(csr_struct, mask_values, weight)
+    A = _dense_topc_state(A, topk_nodes if use_topk else None)
+    active_nodes = _compute_active_nodes(A)
+    effective_topk = topk_edges if (use_topk and topk_edges > 0) else (1 << 60)
+    return FlashLogFunction.apply(A, w, active_nodes, ori_col_ind, ori_mask, ori_gp, ori_gr, ori_gs, ori_gc,
+                                  inv_col_ind, inv_mask, inv_gp, inv_gr, inv_gs, inv_gc, r_size, wot_i,
+                                  effective_topk)
 
 
-def dense_csr_sum_cuda(*args, **kwargs):
-    raise NotImplementedError("the dense [B, L, E] propagation path is not implemented in flashlog_b200 yet")
+def _dense_masks(csr_parts, mask_values, weight):
+    prepared = _prepared_mask_pair(mask_values)
+    if prepared is not None:
+        return prepared
+    return prepare_csr_masks(csr_parts, mask_values, weight)
 
 
-def dense_csr_max(*args, **kwargs):
-    raise NotImplementedError("the dense [B, L, E] propagation path is not implemented in flashlog_b200 yet")
+class FlashLogDenseSumFunction(autograd.Function):
+    """Dense SUM propagation from raw masks (flashlog_kernel.py:885-989), 26 positional arguments."""
+
+    @staticmethod
+    def forward(ctx, A, w, ori_row_ptr, ori_col_ind, ori_r_ind, ori_order,
+                inv_row_ptr, inv_col_ind, inv_r_ind, inv_order,
+                ori_row_group_ptr, ori_group_rel, ori_group_edge_start, ori_group_edge_count,
+                inv_row_group_ptr, inv_group_rel, inv_group_edge_start, inv_group_edge_count,
+                mask_values, weight, r_size, wot_i, use_topk, topk_nodes, topk_edges, agg_mode):
+        _cuda_or_raise(A)
+        if agg_mode not in (0, "sum"):
+            raise NotImplementedError("dense aggregation 'max' through the sum operator is not supported; "
+                                      "use dense_csr_max")
+        csr_parts = (ori_row_ptr, ori_col_ind, ori_r_ind, ori_order, inv_row_ptr, inv_col_ind, inv_r_ind, inv_order,
+                     ori_row_group_ptr, ori_group_rel, ori_group_edge_start, ori_group_edge_count,
+                     inv_row_group_ptr, inv_group_rel, inv_group_edge_start, inv_group_edge_count)
+        graph = _graph_topk(csr_parts)
+        masks = _dense_masks(csr_parts, mask_values, weight)
+        topk = topk_edges if (use_topk and topk_edges > 0) else (1 << 60)
+        out_ind, out_ori, out_inv, rec = _dense_hops(A, w, graph, masks, r_size, wot_i, topk,
+                                                     _compute_active_nodes(A), "sum")
+        ctx.rec, ctx.wot_i = rec, wot_i
+        ctx.save_for_backward(A, w)
+        return out_ind.to(A.dtype), out_ori.to(A.dtype), out_inv.to(A.dtype)
+
+    @staticmethod
+    def backward(ctx, grad_ind, grad_ori, grad_inv):
+        A, w = ctx.saved_tensors
+        gA, gw = _dense_backward(A, w, ctx.rec, grad_ind, grad_ori, grad_inv, ctx.wot_i)
+        return (gA, gw) + (None,) * 24
+
+
+class FlashLogDenseMaxFunction(autograd.Function):
+    """Dense MAX propagation (flashlog_kernel.py:992-1089), 25 positional arguments.
+
+    Every (row, destination) keeps its largest fact of each direction, compared
+    as in the reference's packed (value bits, ~CSR position) CAS-max, ties to the
+    lower CSR position; the gradient reaches the winning edge only
+    (flashlog.cu:523-726, 997-1255).  Hidden edges (mask 0) take no part."""
+
+    @staticmethod
+    def forward(ctx, A, w, ori_row_ptr, ori_col_ind, ori_r_ind, ori_order,
+                inv_row_ptr, inv_col_ind, inv_r_ind, inv_order,
+                ori_row_group_ptr, ori_group_rel, ori_group_edge_start, ori_group_edge_count,
+                inv_row_group_ptr, inv_group_rel, inv_group_edge_start, inv_group_edge_count,
+                mask_values, weight, r_size, wot_i, use_topk, topk_nodes, topk_edges):
+        _cuda_or_raise(A)
+        csr_parts = (ori_row_ptr, ori_col_ind, ori_r_ind, ori_order, inv_row_ptr, inv_col_ind, inv_r_ind, inv_order,
+                     ori_row_group_ptr, ori_group_rel, ori_group_edge_start, ori_group_edge_count,
+                     inv_row_group_ptr, inv_group_rel, inv_group_edge_start, inv_group_edge_count)
+        graph = _graph_topk(csr_parts)
+        masks = _dense_masks(csr_parts, mask_values, weight)
+        topk = topk_edges if (use_topk and topk_edges > 0) else (1 << 60)
+        out_ind, out_ori, out_inv, rec = _dense_hops(A, w, graph, masks, r_size, wot_i, topk,
+                                                     _compute_active_nodes(A), "max")
+        ctx.rec, ctx.wot_i = rec, wot_i
+        ctx.save_for_backward(A, w)
+        return out_ind.to(A.dtype), out_ori.to(A.dtype), out_inv.to(A.dtype)
+
+    @staticmethod
+    def backward(ctx, grad_ind, grad_ori, grad_inv):
+        A, w = ctx.saved_tensors
+        gA, gw = _dense_backward(A, w, ctx.rec, grad_ind, grad_ori, grad_inv, ctx.wot_i)
+        return (gA, gw) + (None,) * 23
+
+
+def dense_csr_sum_cuda(A, w, csr_struct, mask_values, r_size, weight=None, wot_i=False, use_topk=False,
+                       topk_nodes=100000, topk_edges=0, agg_mode="sum", prepared_masks=None):
+    """Dense SUM entry point (flashlog_kernel.py:1629-1663): returns (s_i, s_h, s_t)."""
+    agg_id = 1 if agg_mode == "max" else 0
+    A = _dense_topc_state(A, topk_nodes if use_topk else None)
+    mask_input = prepared_masks if prepared_masks is not None else mask_values
+    weight_input = None if prepared_masks is not None else weight
+    return FlashLogDenseSumFunction.apply(A, w, *csr_struct, mask_input, weight_input, r_size, wot_i, use_topk,
+                                          topk_nodes, topk_edges, agg_id)
+
+
+def dense_csr_max(A, w, csr_struct, mask_values, r_size, weight=None, wot_i=False, use_topk=False,
+                  topk_nodes=100000, topk_edges=0, prepared_masks=None):
+    """Dense MAX entry point (flashlog_kernel.py:1666-1688): returns (s_i, s_h, s_t)."""
+    A = _dense_topc_state(A, topk_nodes if use_topk else None)
+    mask_input = prepared_masks if prepared_masks is not None else mask_values
+    weight_input = None if prepared_masks is not None else weight
+    return FlashLogDenseMaxFunction.apply(A, w, *csr_struct, mask_input, weight_input, r_size, wot_i, use_topk,
+                                          topk_nodes, topk_edges)

@@ -250,7 +250,8 @@ def csr_visibility(graph: Graph, mask_triple):
 def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int, flags: int, *,
                 mask_triple=None, mask_csr=None, edge_weight=None, seed: int = -1, eps: float = EPS,
                 keep_facts: bool = False, record: bool = True, timing=None, slot_capacity=None,
-                status=None, out_sync: bool = True, vis=None, reduce: str = "sum") -> HopForward:
+                status=None, out_sync: bool = True, vis=None, reduce: str = "sum",
+                max_bits: bool = False) -> HopForward:
     """Expansion + per-row coalesce-sum + normalization of one hop.
 
     slot_capacity=None sizes the fact buffers exactly (one host sync for the
@@ -263,7 +264,8 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
     csr_visibility of the same mask) replaces the per-fact mask_triple read.
     reduce="max" coalesces by MAX with exact winners instead
     (FlashLogFunctionSparse3DTopKMax); its out_x holds the maxima, out_y is
-    None and fact_pos is -1 for the facts that did not win.
+    None and fact_pos is -1 for the facts that did not win.  max_bits compares
+    fact values by their fp32 bit patterns (the dense MAX order).
     """
     if reduce not in ("sum", "max"):
         raise ValueError("reduce must be 'sum' or 'max'")
@@ -340,7 +342,8 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
     if reduce == "max":
         check(lib().fl_row_reduce_max(_p(row_ptr), rows, graph.E, r_size, _p(slot_base), _p(fact_dst), _p(fact_val),
                                       _p(fact_rel), _p(fact_edge), T, _p(fact_pos), _p(out_row_ptr), _p(out_ent),
-                                      _p(out_x), _p(status), _p(ws2), ws2.numel(), _stream()), "row_reduce_max")
+                                      _p(out_x), L.FL_MAX_BITS if max_bits else 0, _p(status), _p(ws2), ws2.numel(),
+                                      _stream()), "row_reduce_max")
     else:
         check(lib().fl_row_reduce(_p(row_ptr), rows, graph.E, _p(slot_base), _p(entry_count), _p(fact_dst),
                                   _p(fact_val), T, _p(fact_pos), ctypes.c_float(eps), _p(out_row_ptr), _p(out_ent),

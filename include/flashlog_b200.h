@@ -49,6 +49,9 @@ enum {
     FL_SAMPLED = 16,       /* c2 by weighted quotas, SplitMix64 phase (flashlog.cu:1458-1528) */
     FL_EDGE_SCORE = 32,    /* edge_weight holds scores, not logits                         */
     FL_EDGE_WEIGHT = 64,   /* multiply facts by sigmoid(edge_weight[triple])               */
+    FL_NO_ORI = 256,       /* expand the inverse side only (dense outputs by source)       */
+    FL_NO_INV = 512,       /* expand the forward side only                                 */
+    FL_EDGE_POS = 1024,    /* fact_edge holds the CSR position p instead of order[p]        */
     FL_NO_NORMALIZE = 1 << 20  /* backward: g_y is the gradient of the sums, not of the normalized rows */
 };
 
@@ -194,8 +197,12 @@ int fl_row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t
 int fl_row_reduce_max(const int64_t *row_ptr, int64_t rows, int64_t E, int64_t r_size, const int64_t *slot_base,
                       const int32_t *fact_dst, const float *fact_val, const int16_t *fact_rel,
                       const int32_t *fact_edge, int64_t total_slots, int32_t *fact_pos, int64_t *out_row_ptr,
-                      int32_t *out_ent, float *out_x, int32_t *status, void *ws, size_t ws_bytes,
+                      int32_t *out_ent, float *out_x, int max_flags, int32_t *status, void *ws, size_t ws_bytes,
                       fl_stream_t stream);
+/* max_flags of fl_row_reduce_max: compare values by their fp32 bit patterns as
+ * unsigned integers, the order of the packed (value, ~position) CAS-max of the
+ * dense MAX path (flashlog.cu:103-121, 523-581). */
+enum { FL_MAX_BITS = 1 };
 
 /* Hop backward (+ normalization backward unless FL_NO_NORMALIZE).  Replaces
  * flashlog_backward_sparse3d_cached_cuda (flashlog.cu:2317-2361) and

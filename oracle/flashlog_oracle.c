@@ -254,7 +254,8 @@ enum {
     FLO_MASK_BY_TRIPLE = 4,  /* mask indexed by triple id via order[p] (top-k CUDA path) */
     FLO_WOT_I = 8,           /* no identity term                                        */
     FLO_SAMPLED = 16,        /* c2 by weighted quotas with a SplitMix64 phase            */
-    FLO_EDGE_SCORE = 32      /* edge_weight already holds scores (no sigmoid)            */
+    FLO_EDGE_SCORE = 32,     /* edge_weight already holds scores (no sigmoid)            */
+    FLO_EDGE_POS = 1024      /* fact_edge records the CSR position p, not order[p]       */
 };
 
 typedef struct { float *acc; int64_t *mark; int64_t *touched; int64_t ntouched; int64_t *pos; } flo_row_acc;
@@ -371,7 +372,8 @@ FLO_EXPORT int64_t flo_hop_forward_edges(
                             m = csr_mask[dir][p];
                             if ((flags & FLO_DROP_MASKED) && m == 0.0f) continue;
                         }
-                        FLO_ADD(sd->col[p], prod * m, i, rel + off, m, (int64_t)sd->order[p]);
+                        FLO_ADD(sd->col[p], prod * m, i, rel + off, m,
+                                (flags & FLO_EDGE_POS) ? p : (int64_t)sd->order[p]);
                     }
                 }
             }

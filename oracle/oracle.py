@@ -233,6 +233,108 @@ def hop_forward_max(row, ent, val, w, csr, r_size, E, topk_edges=1 << 60, mask=N
                 fact_edge=f_edge, fact_value=values, fact_source=source, fact_out=fact_out)
 
 
+def dense_forward(A, w, csr, mask, r_size, topk_edges=1 << 60, wot_i=False, mode="sum", active=None):
+    """Dense propagation of A [B, L, E] (flashlog.cpp:151-393 for SUM; the
+    packed CAS-max of flashlog.cu:103-121, 523-637 for MAX): the outputs
+    (out_ind, out_ori, out_inv) and the per-side facts.
+
+    Sources are the nonzero entries of A over the active entities (those with a
+    nonzero sum over the channels, flashlog_kernel.py:617-623); hidden edges
+    (CSR mask 0) emit nothing.  SUM adds a side's facts per (row, destination)
+    in source-entity, group and edge order; MAX keeps the fact whose fp32 bit
+    pattern is largest, ties to the lower CSR position.
+    """
+    A = _c(A, np.float32)
+    B, L, E = A.shape
+    n = w.shape[-1]
+    act = (A.sum(1) != 0).any(0) if active is None else np.isin(np.arange(E), active)
+    Af = A.reshape(B * L, E)
+    rows, ents = np.nonzero((Af != 0) & act[None, :])
+    vals = Af[rows, ents]
+    ori_rp, ori_col, _, ori_order, inv_rp, inv_col, _, inv_order = csr[:8]
+    ori_gptr, ori_grel, ori_gstart, ori_gcount, inv_gptr, inv_grel, inv_gstart, inv_gcount = csr[8:]
+    mo, mi = csr_masks(csr, mask, None)
+    flags = SKIP_NONPOS_W | DROP_MASKED | WOT_I | (1024 if mode == "max" else 0)
+    nnz = rows.size
+    ent64 = _c(ents, np.int64)
+    cap = max(int(lib().flo_fact_bound(ctypes.c_int64(nnz), _p(ent64), _p(_c(ori_rp, np.int32)),
+                                        _p(_c(inv_rp, np.int32)))), 1)
+    out_key = np.empty(cap, np.int64)
+    out_val = np.empty(cap, np.float32)
+    f_entry = np.empty(cap, np.int64)
+    f_rel = np.empty(cap, np.int32)
+    f_m = np.empty(cap, np.float32)
+    f_out = np.empty(cap, np.int64)
+    f_edge = np.empty(cap, np.int64)
+    nf = ctypes.c_int64(0)
+    arrs = [_c(a, t) for a, t in ((ori_col, np.int32), (ori_order, np.int32), (ori_gptr, np.int32),
+                                   (ori_grel, np.int16), (ori_gstart, np.int32), (ori_gcount, np.int32),
+                                   (inv_col, np.int32), (inv_order, np.int32), (inv_gptr, np.int32),
+                                   (inv_grel, np.int16), (inv_gstart, np.int32), (inv_gcount, np.int32))]
+    wr = _c(w.reshape(B, L, n), np.float32)
+    u = lib().flo_hop_forward_edges(
+        ctypes.c_int64(nnz), _p(_c(rows, np.int64)), _p(ent64), _p(_c(vals, np.float32)), _p(wr),
+        ctypes.c_int64(L), ctypes.c_int64(n), ctypes.c_int64(E), ctypes.c_int64(r_size), *[_p(a) for a in arrs],
+        _p(mo), _p(mi), None, None, ctypes.c_int64(int(min(topk_edges, 1 << 62))), ctypes.c_int64(flags),
+        ctypes.c_int64(-1), _p(out_key), _p(out_val), _p(f_entry), _p(f_rel), _p(f_m), _p(f_out), _p(f_edge),
+        ctypes.byref(nf))
+    nf = nf.value
+    f_entry, f_rel, f_m, f_edge = f_entry[:nf], f_rel[:nf], f_m[:nf], f_edge[:nf]
+    keys = out_key[:u][f_out[:nf]]  # row * E + destination of every fact
+    prod = (vals[f_entry] * wr.reshape(B * L, n)[rows[f_entry], f_rel]).astype(np.float32)
+    fval = (prod * f_m).astype(np.float32)
+    outs, side_facts = [], []
+    for lo, hi in ((0, r_size), (r_size, 2 * r_size)):
+        sel = np.nonzero((f_rel >= lo) & (f_rel < hi))[0]
+        dense = np.zeros(B * L * E, np.float32)
+        fout = np.full(nf, -1, np.int64)
+        if mode == "max":
+            bits = fval[sel].view(np.uint32).astype(np.int64)
+            order = np.lexsort((f_edge[sel], -bits, keys[sel]))
+            sk = keys[sel][order]
+            first = np.ones(sk.size, bool)
+            first[1:] = sk[1:] != sk[:-1]
+            win = sel[order[first]]
+            dense[keys[win]] = fval[win]
+            fout[win] = keys[win]
+        else:
+            np.add.at(dense, keys[sel], fval[sel])  # in fact order
+            fout[sel] = keys[sel]
+        outs.append(dense.reshape(B, L, E))
+        side_facts.append(fout)
+    out_ind = np.zeros_like(A) if wot_i else (A * w.reshape(B, L, n)[..., n - 1:n]).astype(np.float32)
+    return dict(out_ind=out_ind, out_ori=outs[0], out_inv=outs[1], rows=rows, ents=ents, vals=vals,
+                fact_entry=f_entry, fact_rel=f_rel, fact_m=f_m, fact_dense=side_facts, n_facts=nf)
+
+
+def dense_backward(fw, A, w, grad_ind, grad_ori, grad_inv, r_size, wot_i=False):
+    """Gradients of the dense propagation (flashlog.cpp:222-283 for SUM; winning
+    edges only for MAX, flashlog.cu:639-726)."""
+    A = _c(A, np.float32)
+    B, L, E = A.shape
+    n = w.shape[-1]
+    wr = w.reshape(B * L, n).astype(np.float32)
+    gA = np.zeros(B * L * E, np.float64)
+    gw = np.zeros((B * L, n), np.float64)
+    if not wot_i:
+        gi = np.asarray(grad_ind, np.float64).reshape(B * L, E)
+        gA += (gi * wr[:, n - 1:n]).reshape(-1)
+        gw[:, n - 1] += (gi * A.reshape(B * L, E)).sum(1)
+    rows, ents, vals = fw["rows"], fw["ents"], fw["vals"]
+    for side, g in ((0, grad_ori), (1, grad_inv)):
+        gf = np.asarray(g, np.float64).reshape(-1)
+        fo = fw["fact_dense"][side]
+        sel = np.nonzero(fo >= 0)[0]
+        e = fw["fact_entry"][sel]
+        go = gf[fo[sel]]
+        rel = fw["fact_rel"][sel]
+        m = fw["fact_m"][sel].astype(np.float64)
+        r = rows[e]
+        np.add.at(gA, r * E + ents[e], go * wr[r, rel] * m)
+        np.add.at(gw, (r, rel), go * vals[e] * m)
+    return gA.reshape(B, L, E).astype(np.float32), gw.reshape(B, L, n).astype(np.float32)
+
+
 def hop_backward(fw, g_out, row, val, w, r_size):
     """grad of the entry values and of w from a recorded forward (flashlog.cpp:991-1134)."""
     row, val, w = _c(row, np.int64), _c(val, np.float32), _c(w, np.float32)

@@ -189,6 +189,39 @@ def main():
                    f"{name}_win_raw": win_raw.numpy()})
     np.savez_compressed(os.path.join(HERE, "max_config1.npz"), names=np.array([s[0] for s in mspecs]), **mx)
 
+    # --- dense propagation (FlashLogFunction on the reference CPU path,
+    # flashlog.cpp:151-393, with the dense c1 of flashlog_kernel.py:814-842)
+    rng = np.random.default_rng(37)
+    dn = {}
+    dspecs = [("dense_plain", False, 0, 0, False), ("dense_topk", True, 6, 3, False),
+              ("dense_wot_i", True, 4, 5, True), ("dense_ties", True, 3, 2, False)]
+    for name, use_topk, c1, c2, wot_i in dspecs:
+        B, L = 3, 3
+        A = np.zeros((B, L, E), np.float32)
+        for b in range(B):
+            for l in range(L):
+                k = int(rng.integers(4, 14))
+                e = rng.choice(E, k, replace=False)
+                A[b, l, e] = (rng.integers(1, 5, k) / 4.0) if name == "dense_ties" else rng.random(k)
+        w = _w(rng, B, L, n, name == "dense_ties")
+        mask = rng.random(train.shape[0]) > 0.15
+        At = torch.from_numpy(A).requires_grad_(True)
+        wt = torch.from_numpy(w).requires_grad_(True)
+        s_i, s_h, s_t = fk.vectorized_operation_csr(At, wt, ctuple, torch.from_numpy(mask), Rr, wot_i=wot_i,
+                                                    use_topk=use_topk, topk_nodes=c1, topk_edges=c2)
+        gi = rng.standard_normal(A.shape).astype(np.float32)
+        gh = rng.standard_normal(A.shape).astype(np.float32)
+        gt = rng.standard_normal(A.shape).astype(np.float32)
+        ((s_i * torch.from_numpy(gi)).sum() + (s_h * torch.from_numpy(gh)).sum() +
+         (s_t * torch.from_numpy(gt)).sum()).backward()
+        dn.update({f"{name}_A": A, f"{name}_w": w, f"{name}_mask": mask.astype(np.uint8),
+                   f"{name}_use_topk": np.array(use_topk), f"{name}_c1": np.array(c1), f"{name}_c2": np.array(c2),
+                   f"{name}_wot_i": np.array(wot_i), f"{name}_s_i": s_i.detach().numpy(),
+                   f"{name}_s_h": s_h.detach().numpy(), f"{name}_s_t": s_t.detach().numpy(),
+                   f"{name}_gi": gi, f"{name}_gh": gh, f"{name}_gt": gt, f"{name}_grad_A": At.grad.numpy(),
+                   f"{name}_grad_w": wt.grad.numpy()})
+    np.savez_compressed(os.path.join(HERE, "dense_config1.npz"), names=np.array([s[0] for s in dspecs]), **dn)
+
     # --- three-hop DRUM propagation + readout + loss (src/model_DRUM_kernel_sp.py:92-204)
     rng = np.random.default_rng(41)
     from flashlog_b200.synthetic import training_queries

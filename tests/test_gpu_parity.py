@@ -500,3 +500,55 @@ def test_sparse_max_large_rows(fk):
     rgv, rgw = O.hop_backward(ref, g, row, val, w, R)
     np.testing.assert_allclose(gv.cpu().numpy(), rgv, rtol=RTOL, atol=1e-5)
     np.testing.assert_allclose(gw.cpu().numpy(), rgw, rtol=RTOL, atol=1e-5)
+
+
+@pytest.mark.parametrize("name", ["dense_plain", "dense_topk", "dense_wot_i", "dense_ties"])
+def test_dense_sum_matches_reference_golden(fk, g1, golden, name):
+    """Dense propagation through vectorized_operation_csr and dense_csr_sum_cuda:
+    outputs bit for bit equal to the reference CPU path, gradients to rel 1e-5."""
+    cfg, train, csr_np, csr = g1
+    R = cfg.relations
+    g = golden("dense_config1.npz")
+    p = lambda k: g[f"{name}_{k}"]
+    use_topk, c1, c2, wot_i = bool(p("use_topk")), int(p("c1")), int(p("c2")), bool(p("wot_i"))
+    for entry in (fk.vectorized_operation_csr, fk.dense_csr_sum_cuda):
+        A = _cuda(p("A")).requires_grad_(True)
+        w = _cuda(p("w")).requires_grad_(True)
+        s_i, s_h, s_t = entry(A, w, csr, _cuda(p("mask")).bool(), R, wot_i=wot_i, use_topk=use_topk, topk_nodes=c1,
+                              topk_edges=c2)
+        assert np.array_equal(s_i.detach().cpu().numpy(), p("s_i"))
+        assert np.array_equal(s_h.detach().cpu().numpy(), p("s_h"))
+        assert np.array_equal(s_t.detach().cpu().numpy(), p("s_t"))
+        ((s_i * _cuda(p("gi"))).sum() + (s_h * _cuda(p("gh"))).sum() + (s_t * _cuda(p("gt"))).sum()).backward()
+        np.testing.assert_allclose(A.grad.cpu().numpy(), p("grad_A"), rtol=RTOL, atol=1e-6)
+        np.testing.assert_allclose(w.grad.cpu().numpy(), p("grad_w"), rtol=RTOL, atol=1e-6)
+
+
+@pytest.mark.parametrize("name", ["dense_plain", "dense_topk", "dense_ties"])
+def test_dense_max_matches_oracle(fk, g1, golden, name):
+    """dense_csr_max: per direction the fact with the largest fp32 bit pattern,
+    ties to the lower CSR position (flashlog.cu:103-121, 523-637); gradients to
+    the winning edges only (flashlog.cu:639-726)."""
+    cfg, train, csr_np, csr = g1
+    R = cfg.relations
+    g = golden("dense_config1.npz")
+    p = lambda k: g[f"{name}_{k}"]
+    use_topk, c1, c2, wot_i = bool(p("use_topk")), int(p("c1")), int(p("c2")), bool(p("wot_i"))
+    A_np, w_np, mask = p("A"), p("w"), p("mask")
+    A = _cuda(A_np).requires_grad_(True)
+    w = _cuda(w_np).requires_grad_(True)
+    s_i, s_h, s_t = fk.dense_csr_max(A, w, csr, _cuda(mask).bool(), R, wot_i=wot_i, use_topk=use_topk,
+                                     topk_nodes=c1, topk_edges=c2)
+    from test_oracle_golden import _dense_keep
+    keep = _dense_keep(A_np, c1) if use_topk else np.ones(A_np.shape, bool)
+    Ap = (A_np * keep).astype(np.float32)
+    topk = c2 if (use_topk and c2 > 0) else 1 << 60
+    ref = O.dense_forward(Ap, w_np, csr_np, mask, R, topk_edges=topk, wot_i=wot_i, mode="max")
+    assert np.array_equal(s_i.detach().cpu().numpy(), ref["out_ind"])
+    assert np.array_equal(s_h.detach().cpu().numpy(), ref["out_ori"])
+    assert np.array_equal(s_t.detach().cpu().numpy(), ref["out_inv"])
+    gi, gh, gt = p("gi"), p("gh"), p("gt")
+    ((s_i * _cuda(gi)).sum() + (s_h * _cuda(gh)).sum() + (s_t * _cuda(gt)).sum()).backward()
+    rgA, rgw = O.dense_backward(ref, Ap, w_np, gi, gh, gt, R, wot_i=wot_i)
+    np.testing.assert_allclose(A.grad.cpu().numpy(), np.where(keep, rgA, 0), rtol=RTOL, atol=1e-6)
+    np.testing.assert_allclose(w.grad.cpu().numpy(), rgw, rtol=RTOL, atol=1e-6)

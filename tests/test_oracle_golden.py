@@ -155,3 +155,40 @@ def test_max_coalesce_matches_reference(golden, name):
         within[sel] = np.arange(int(sel.sum()))
     assert np.array_equal(src[win], p("win_source"))
     assert np.array_equal(within[win], p("win_raw"))
+
+
+def _dense_keep(A, c1):
+    """Keep mask of the dense c1 of flashlog_kernel.py:814-842, through the oracle's c1."""
+    B, L, E = A.shape
+    Af = A.reshape(B * L, E)
+    rows, ents = np.nonzero(Af != 0)
+    kept = O.topc(rows, Af[rows, ents], c1)
+    keep = np.ones(B * L * E, bool)
+    if kept is None:
+        return keep.reshape(A.shape)
+    counts = np.bincount(rows, minlength=B * L)
+    keep[np.repeat(counts > c1, E)] = False
+    keep[rows[kept] * E + ents[kept]] = True
+    return keep.reshape(A.shape)
+
+
+@pytest.mark.parametrize("name", ["dense_plain", "dense_topk", "dense_wot_i", "dense_ties"])
+def test_dense_sum_matches_reference(golden, name):
+    """Dense propagation (FlashLogFunction): the oracle reproduces the reference
+    CPU outputs bit for bit and its gradients to rounding."""
+    g = golden("dense_config1.npz")
+    cfg, train, csr = config1_graph()
+    R = cfg.relations
+    p = lambda k: g[f"{name}_{k}"]
+    A = p("A")
+    use_topk, c1, c2, wot_i = bool(p("use_topk")), int(p("c1")), int(p("c2")), bool(p("wot_i"))
+    keep = _dense_keep(A, c1) if use_topk else np.ones(A.shape, bool)
+    Ap = (A * keep).astype(np.float32)
+    topk = c2 if (use_topk and c2 > 0) else 1 << 60
+    fw = O.dense_forward(Ap, p("w"), csr, p("mask"), R, topk_edges=topk, wot_i=wot_i)
+    assert np.array_equal(fw["out_ind"], p("s_i"))
+    assert np.array_equal(fw["out_ori"], p("s_h"))
+    assert np.array_equal(fw["out_inv"], p("s_t"))
+    gA, gw = O.dense_backward(fw, Ap, p("w"), p("gi"), p("gh"), p("gt"), R, wot_i=wot_i)
+    np.testing.assert_allclose(np.where(keep, gA, 0), p("grad_A"), rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(gw, p("grad_w"), rtol=1e-5, atol=1e-6)
