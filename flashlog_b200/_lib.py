@@ -103,6 +103,7 @@ SIGNATURES = {
     "fl_normalize_forward": (ctypes.c_int, [_P, _P, _I64, ctypes.c_float, _P, _P, _P]),
     "fl_normalize_backward": (ctypes.c_int, [_P, _P, _P, _P, _I64, ctypes.c_float, _P, _P]),
     "fl_hop_stats": (ctypes.c_int, [_P, _I64, _P, _I64, _SIDE, _SIDE, _P, _P, ctypes.c_int, _P, _P]),
+    "fl_rule_max_reduce": (ctypes.c_int, [_P, _I64, _P, _P, _I64, _P, _I64, _I64, _I64, _P, _P]),
     "fl_scatter_grad": (ctypes.c_int, [_P, _P, _I64, _P, _P, _I64, _P, _P]),
     "fl_readout": (ctypes.c_int, [_P, _P, _P, _I64, _P, _I64, _P, _P]),
     "fl_readout_backward": (ctypes.c_int, [_P, _P, _I64, _P, _I64, _P, _P, _I64, _P, _P]),

@@ -49,6 +49,8 @@ int fixed_relation_fill(const int64_t *b, const int64_t *l, const int32_t *ent, 
                         const int64_t *slot_base, int32_t *fact_dst, float *fact_val, int32_t *entry_count,
                         cudaStream_t st);
 size_t filtered_ranks_workspace(int64_t B);
+int rule_max_reduce(const int64_t *row_ptr, int64_t rows, const int32_t *ent, const float *val, int64_t C,
+                    const float *weights, int64_t ranks, int64_t B, int64_t E, unsigned int *acc, cudaStream_t st);
 int filtered_ranks(const int64_t *ib, const int64_t *ie, const float *v, int64_t nnz, const int64_t *targets,
                    const int64_t *fk, int64_t nf, int64_t B, int64_t E, int use_eql, float *ranks, void *ws,
                    size_t ws_bytes, cudaStream_t st);
@@ -274,6 +276,11 @@ int fl_fixed_relation_fill(const int64_t *b, const int64_t *l, const int32_t *en
 }
 
 size_t fl_filtered_ranks_workspace(int64_t B) { return filtered_ranks_workspace(B); }
+
+int fl_rule_max_reduce(const int64_t *row_ptr, int64_t rows, const int32_t *ent, const float *val, int64_t C,
+                       const float *weights, int64_t ranks, int64_t B, int64_t E, uint32_t *acc, fl_stream_t stream) {
+    return rule_max_reduce(row_ptr, rows, ent, val, C, weights, ranks, B, E, acc, as_stream(stream));
+}
 
 int fl_filtered_ranks(const int64_t *idx_b, const int64_t *idx_e, const float *values, int64_t nnz,
                       const int64_t *targets, const int64_t *filter_keys, int64_t n_filter, int64_t B, int64_t E,

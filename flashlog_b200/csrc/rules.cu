@@ -127,6 +127,31 @@ SideR make_side_r(const fl_csr_side &s) {
     return r;
 }
 
+// Max-product rule scores (rules/shared_inference.py:123-206 with
+// reduction 'max'): every reached (query, rule, entity) of a Boolean rule state
+// raises acc[rank][query * E + entity] to the rule's rank weight.  Weights are
+// finite and nonnegative, so the fp32 bit patterns order like the values and
+// an unsigned atomic max is exact and order-independent.  One warp per
+// (query, rule) row.
+__global__ void rule_max_kernel(const int64_t *row_ptr, int64_t rows, const int32_t *ent, const float *val,
+                                int64_t C, const float *weights, int64_t ranks, int64_t B, int64_t E,
+                                unsigned int *acc) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t r = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
+        const int64_t q = r / C, c = r % C;
+        const int64_t a = row_ptr[r], b = row_ptr[r + 1];
+        for (int64_t k = a + lane; k < b; k += 32) {
+            if (!(val[k] > 0.0f)) continue;
+            const int64_t e = ent[k];
+            for (int64_t rk = 0; rk < ranks; ++rk) {
+                const unsigned int wbits = __float_as_uint(weights[c * ranks + rk]);
+                if (wbits != 0u) atomicMax(acc + rk * B * E + q * E + e, wbits);
+            }
+        }
+    }
+}
+
 }  // namespace
 
 size_t fixed_relation_workspace(int64_t nnz) { return carve_bytes<int64_t>(nnz + 1) + scan_workspace(nnz) + 1024; }
@@ -163,6 +188,20 @@ int fixed_relation_fill(const int64_t *b, const int64_t *l, const int32_t *ent, 
 }
 
 size_t filtered_ranks_workspace(int64_t B) { return carve_bytes<float>(B) + 4 * carve_bytes<int32_t>(B) + 1024; }
+
+int rule_max_reduce(const int64_t *row_ptr, int64_t rows, const int32_t *ent, const float *val, int64_t C,
+                    const float *weights, int64_t ranks, int64_t B, int64_t E, unsigned int *acc, cudaStream_t st) {
+    FL_REQUIRE(C > 0 && ranks > 0 && B >= 0 && E > 0 && rows == B * C, "rule_max_reduce: bad sizes");
+    if (rows > 0) {
+        const int sms = fl_device_sm_count();
+        int64_t blocks = (rows + 7) / 8;
+        const int64_t cap = static_cast<int64_t>(sms > 0 ? sms : 148) * 16;
+        if (blocks > cap) blocks = cap;
+        launch(rule_max_kernel, static_cast<unsigned>(blocks), 256, 0, st, row_ptr, rows, ent, val, C, weights, ranks,
+               B, E, acc);
+    }
+    return check_launch("rule_max_reduce");
+}
 
 int filtered_ranks(const int64_t *ib, const int64_t *ie, const float *v, int64_t nnz, const int64_t *targets,
                    const int64_t *fk, int64_t nf, int64_t B, int64_t E, int use_eql, float *ranks, void *ws,

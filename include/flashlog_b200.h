@@ -268,6 +268,16 @@ int fl_fixed_relation_fill(const int64_t *b, const int64_t *l, const int32_t *en
 
 /* Filtered tie-averaged ranks; filter_keys (b * E + e) sorted ascending.
  * Replaces sparse2d_filtered_ranks_cuda (flashlog.cu:2839-2910). */
+/* Max-product rule scores of one chunk of C rules (rules/shared_inference.py
+ * :123-206 with reduction 'max', the dense accumulator of 200-206): the state
+ * has rows q * C + c (query q, rule c) with Boolean values; every entry with a
+ * positive value raises acc[rank * B * E + q * E + entity] to the fp32 bit
+ * pattern of weights[c * ranks + rank].  acc (u32, caller zeroed) then holds,
+ * as fp32, the largest rank weight of the rules reaching each entity.
+ * weights must be finite and nonnegative.  Order-independent and exact. */
+int fl_rule_max_reduce(const int64_t *row_ptr, int64_t rows, const int32_t *ent, const float *val, int64_t C,
+                       const float *weights, int64_t ranks, int64_t B, int64_t E, uint32_t *acc, fl_stream_t stream);
+
 size_t fl_filtered_ranks_workspace(int64_t B);
 int fl_filtered_ranks(const int64_t *idx_b, const int64_t *idx_e, const float *values, int64_t nnz,
                       const int64_t *targets, const int64_t *filter_keys, int64_t n_filter, int64_t B, int64_t E,

@@ -387,6 +387,33 @@ def fixed_relation(b, l, e, v, ops, csr, r_size, E):
     return coalesce_sum(keys, ov[:nf])
 
 
+def max_product(sources, bodies, weights, csr, r_size, E, final_max=False):
+    """Max-product rule scores (rules/shared_inference.py:12-245, reduction
+    'max'): Boolean fixed-relation grounding of every (source, rule), per rank
+    the largest weight of the rules reaching an entity, rows normalized by
+    their sums, ranks combined by sum or max.  Returns (keys q * E + e, values)."""
+    sources = np.asarray(sources, np.int64)
+    weights = np.asarray(weights, np.float32)
+    B, K, ranks = sources.size, len(bodies), weights.shape[1]
+    acc = np.zeros((ranks, B * E), np.float32)
+    for k, body in enumerate(bodies):
+        keys = np.arange(B, dtype=np.int64) * E + sources
+        for op in body:
+            if keys.size == 0:
+                break
+            b, e = keys // E, keys % E
+            ops_ = np.full((B, 1), int(op), np.int64)
+            out, vals = fixed_relation(b, np.zeros_like(b), e, np.ones(b.size, np.float32), ops_, csr, r_size, E)
+            keys = out[vals > 0]
+        for r in range(ranks):
+            np.maximum.at(acc[r], keys, weights[k, r])
+    totals = acc.reshape(ranks, B, E).sum(-1, keepdims=True, dtype=np.float64).astype(np.float32)
+    norm = (acc.reshape(ranks, B, E) / np.maximum(totals, np.float32(1e-30))).astype(np.float32)
+    combined = (norm.max(0) if final_max else norm.sum(0)).reshape(-1)
+    keys = np.nonzero(combined)[0]
+    return keys, combined[keys]
+
+
 def coalesce_sum(keys, vals):
     keys, vals = _c(keys, np.int64), _c(vals, np.float32)
     ok = np.empty(max(keys.size, 1), np.int64)

@@ -222,6 +222,53 @@ def main():
                    f"{name}_grad_w": wt.grad.numpy()})
     np.savez_compressed(os.path.join(HERE, "dense_config1.npz"), names=np.array([s[0] for s in dspecs]), **dn)
 
+    # --- max-product rule-bank scores: the reference's own rules/shared_inference.py
+    # score(reduction='max') on CPU; its CUDA-only fixed-relation step is the C
+    # oracle's restatement of flashlog.cu:1561-1741.
+    import types
+    sys.path.insert(0, args.reference)
+    import rules.evaluate as ref_ev
+    from rules.max_inference import score as ref_max_score
+
+    def cpu_fixed_relation(sp_state, operators, csr_struct, r_size):
+        st = sp_state.coalesce()
+        ix = st.indices().numpy()
+        Bq, Lq, Eq = st.shape
+        keys, vals = O.fixed_relation(ix[0], ix[1], ix[2], st.values().numpy(), operators.numpy(), csr_np, r_size,
+                                      Eq)
+        kk = torch.from_numpy(keys)
+        return torch.sparse_coo_tensor(torch.stack([kk // (Lq * Eq), (kk // Eq) % Lq, kk % Eq]),
+                                       torch.from_numpy(vals), (Bq, Lq, Eq), is_coalesced=True)
+
+    ev = types.SimpleNamespace(**{k: getattr(ref_ev, k) for k in dir(ref_ev) if not k.startswith("__")})
+    ev.vectorized_operation_sparse3d_fixed_relation = cpu_fixed_relation
+    rng = np.random.default_rng(71)
+    rb = {}
+    for ci, (nrules, final_max, chunk) in enumerate([(40, False, 16), (40, True, 7), (25, False, 25)]):
+        rules_ = []
+        for k in range(nrules):
+            blen = int(rng.integers(1, 4))
+            body = tuple(int(x) for x in rng.integers(0, 2 * Rr, blen))
+            if k % 9 == 0:
+                body = body + (2 * Rr,)
+            wts = rng.random(3).astype(np.float32)
+            if k % 7 == 0:
+                wts[int(rng.integers(0, 3))] = 0.0
+            if k % 5 == 0:
+                wts = np.round(wts * 4) / 4
+            rules_.append({"body": body, "rank_weights": [float(x) for x in wts]})
+        sources = torch.from_numpy(rng.choice(E, 10, replace=False).astype(np.int64))
+        out = ref_max_score(ev, sources, rules_, ctuple, Rr, E, chunk, final_max=final_max,
+                            dense_budget_bytes=1 << 28).coalesce()
+        oi = out.indices().numpy()
+        lens = np.array([len(r["body"]) for r in rules_])
+        rb.update({f"r{ci}_sources": sources.numpy(), f"r{ci}_body_len": lens,
+                   f"r{ci}_body": np.concatenate([np.array(r["body"], np.int64) for r in rules_]),
+                   f"r{ci}_weights": np.array([r["rank_weights"] for r in rules_], np.float32),
+                   f"r{ci}_final_max": np.array(final_max), f"r{ci}_chunk": np.array(chunk),
+                   f"r{ci}_key": oi[0] * E + oi[1], f"r{ci}_val": out.values().numpy()})
+    np.savez_compressed(os.path.join(HERE, "maxproduct_config1.npz"), n=np.array(3), **rb)
+
     # --- three-hop DRUM propagation + readout + loss (src/model_DRUM_kernel_sp.py:92-204)
     rng = np.random.default_rng(41)
     from flashlog_b200.synthetic import training_queries

@@ -552,3 +552,20 @@ def test_dense_max_matches_oracle(fk, g1, golden, name):
     rgA, rgw = O.dense_backward(ref, Ap, w_np, gi, gh, gt, R, wot_i=wot_i)
     np.testing.assert_allclose(A.grad.cpu().numpy(), np.where(keep, rgA, 0), rtol=RTOL, atol=1e-6)
     np.testing.assert_allclose(w.grad.cpu().numpy(), rgw, rtol=RTOL, atol=1e-6)
+
+
+@pytest.mark.parametrize("ci", [0, 1, 2])
+def test_max_product_matches_reference_golden(fk, g1, golden, ci):
+    """flashlog_b200.rules.score (max-product rule bank, smDRUM sum / mmDRUM max
+    over ranks) against the reference's own score(reduction='max')."""
+    from flashlog_b200 import rules as RB
+    from test_oracle_golden import _rule_bank
+    cfg, train, csr_np, csr = g1
+    g = golden("maxproduct_config1.npz")
+    bodies, weights = _rule_bank(g, ci)
+    rules = [{"body": b, "rank_weights": [float(x) for x in w]} for b, w in zip(bodies, weights)]
+    out = RB.score(None, _cuda(g[f"r{ci}_sources"]), rules, csr, cfg.relations, cfg.entities,
+                   int(g[f"r{ci}_chunk"]), final_max=bool(g[f"r{ci}_final_max"])).coalesce()
+    oi = out.indices().cpu().numpy()
+    assert np.array_equal(oi[0] * cfg.entities + oi[1], g[f"r{ci}_key"])
+    np.testing.assert_allclose(out.values().cpu().numpy(), g[f"r{ci}_val"], rtol=RTOL, atol=1e-9)

@@ -192,3 +192,26 @@ def test_dense_sum_matches_reference(golden, name):
     gA, gw = O.dense_backward(fw, Ap, p("w"), p("gi"), p("gh"), p("gt"), R, wot_i=wot_i)
     np.testing.assert_allclose(np.where(keep, gA, 0), p("grad_A"), rtol=1e-5, atol=1e-6)
     np.testing.assert_allclose(gw, p("grad_w"), rtol=1e-5, atol=1e-6)
+
+
+def _rule_bank(g, ci):
+    lens = g[f"r{ci}_body_len"]
+    flat = g[f"r{ci}_body"]
+    bodies, k = [], 0
+    for n in lens:
+        bodies.append(tuple(int(x) for x in flat[k:k + n]))
+        k += n
+    return bodies, g[f"r{ci}_weights"]
+
+
+@pytest.mark.parametrize("ci", [0, 1, 2])
+def test_max_product_matches_reference(golden, ci):
+    """Max-product rule scores: the oracle gives the entries and values of the
+    reference's rules/shared_inference.py score(reduction='max')."""
+    g = golden("maxproduct_config1.npz")
+    cfg, train, csr = config1_graph()
+    bodies, weights = _rule_bank(g, ci)
+    keys, vals = O.max_product(g[f"r{ci}_sources"], bodies, weights, csr, cfg.relations, cfg.entities,
+                               final_max=bool(g[f"r{ci}_final_max"]))
+    assert np.array_equal(keys, g[f"r{ci}_key"])
+    np.testing.assert_allclose(vals, g[f"r{ci}_val"], rtol=1e-5, atol=1e-9)
