@@ -212,12 +212,8 @@ def run_value_arm(args, cfg, train, csr, rank, world, device):
     lr = 0.01
 
     def step(ids, h, r, t, collect):
-        if world > 1:
-            gathered = [torch.empty_like(ids) for _ in range(world)]
-            dist.all_gather(gathered, ids)
-            hide = torch.cat(gathered)
-        else:
-            hide = ids
+        from flashlog_b200 import multigpu as MG
+        hide = MG.gather_hidden_triples(ids) if world > 1 else ids
         mask[hide] = 0
         w_all = table[r]
         rp, ent, val = engine.drum_propagate(h, w_all, graph, R, c1=cfg.c1 or None, c2=cfg.c2, mask_triple=mask,
@@ -226,8 +222,7 @@ def run_value_arm(args, cfg, train, csr, rank, world, device):
         table.grad = None
         loss.backward()
         if world > 1:
-            dist.all_reduce(table.grad)
-            table.grad.div_(world)
+            MG.allreduce_mean_(table.grad)
         with torch.no_grad():
             table.sub_(lr * table.grad)
         mask[hide] = 1
@@ -293,17 +288,14 @@ def run_graph_arm(args, cfg, train, csr, rank, world, device):
                          apply_update=(world == 1))
     lr = step.lr
 
+    from flashlog_b200 import multigpu as MG
+
     def hide_of(ids):
-        if world == 1:
-            return ids
-        gathered = [torch.empty_like(ids) for _ in range(world)]
-        dist.all_gather(gathered, ids)
-        return torch.cat(gathered)
+        return MG.gather_hidden_triples(ids) if world > 1 else ids
 
     def after():
         if world > 1:
-            dist.all_reduce(step.grad)
-            step.grad.div_(world)
+            MG.allreduce_mean_(step.grad)
             table.sub_(lr * step.grad)
 
     clocks = ClockSampler(torch.cuda.current_device())
@@ -381,12 +373,8 @@ def run_e2e_arm(args, cfg, train, csr, data, table, rank, world, device, steps):
         h = h_h.to(device, non_blocking=True)
         r = r_h.to(device, non_blocking=True)
         t = t_h.to(device, non_blocking=True)
-        if world > 1:
-            gathered = [torch.empty_like(ids) for _ in range(world)]
-            dist.all_gather(gathered, ids)
-            hide = torch.cat(gathered)
-        else:
-            hide = ids
+        from flashlog_b200 import multigpu as MG
+        hide = MG.gather_hidden_triples(ids) if world > 1 else ids
         mask[hide] = False
         Q = h.numel()
         w_all = tab[r]
@@ -406,8 +394,7 @@ def run_e2e_arm(args, cfg, train, csr, data, table, rank, world, device, steps):
         tab.grad = None
         loss.backward()
         if world > 1:
-            dist.all_reduce(tab.grad)
-            tab.grad.div_(world)
+            MG.allreduce_mean_(tab.grad)
         with torch.no_grad():
             tab.sub_(0.01 * tab.grad)
         mask[hide] = True
@@ -526,12 +513,9 @@ def main():
     facts = res["facts"]
     hop_ms = res["hop_ms"]
     if world > 1:
-        t = torch.tensor([ms, float(facts)], dtype=torch.float64, device=device)
-        mx = t.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        sm = t.clone()
-        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
-        ms, facts = float(mx[0].item()), int(sm[1].item())
+        from flashlog_b200 import multigpu as MG
+        ms, facts = MG.max_time_sum_work(ms, facts, device)
+        facts = int(facts)
     value = facts / (ms / 1000.0)
     e2e = None
     if not args.no_e2e:
@@ -540,12 +524,8 @@ def main():
                                        steps_e2e)
         local_facts = res["facts"] * steps_e2e / args.steps
         if world > 1:
-            t = torch.tensor([e2e_ms, local_facts], dtype=torch.float64, device=device)
-            mx = t.clone()
-            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-            sm = t.clone()
-            dist.all_reduce(sm, op=dist.ReduceOp.SUM)
-            e2e_ms, local_facts = float(mx[0].item()), float(sm[1].item())
+            from flashlog_b200 import multigpu as MG
+            e2e_ms, local_facts = MG.max_time_sum_work(e2e_ms, local_facts, device)
         e2e = {"value": local_facts / (e2e_ms / 1000.0), "unit": "facts/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / steps_e2e,
                "api": "vectorized_operation_sparse3d_csr_sum_norm per hop (COO in/out)"}
