@@ -27,6 +27,7 @@ FL_NO_INV = 512
 FL_EDGE_POS = 1024
 FL_NO_NORMALIZE = 1 << 20
 FL_MAX_BITS = 1
+FL_ENTRY_INFO_INTS = 5  # int32 values per entry in fl_hop_params.entry_info
 NO_BUDGET = 1 << 62
 FL_STATUS_SLOT_OVERFLOW = 1
 

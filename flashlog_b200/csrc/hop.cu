@@ -57,6 +57,7 @@ __device__ __forceinline__ int64_t find_row(const int64_t *row_ptr, int64_t rows
 struct EntryInfo {
     int32_t row, g0o, g1o, g0i, g1i;
 };
+static_assert(sizeof(EntryInfo) == FL_ENTRY_INFO_INTS * sizeof(int32_t), "entry record size of the C ABI");
 
 __global__ void hop_capacity_kernel(const int32_t *ent, const int64_t *row_ptr, int64_t rows, int64_t S, Side ori,
                                     Side inv, int64_t topk, int wot_i, int sides, int64_t *cap, EntryInfo *info) {

@@ -283,7 +283,7 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
     slot_base = torch.empty(S + 1, dtype=torch.int64, device=dev)
     ws = _ws(lib().fl_hop_workspace(rows, S), dev)
     total = ctypes.c_int64(0)
-    entry_info = torch.empty(5 * max(S, 1), dtype=torch.int32, device=dev)
+    entry_info = torch.empty(L.FL_ENTRY_INFO_INTS * max(S, 1), dtype=torch.int32, device=dev)
     if vis is not None and (len(vis) != 2 or any(v.numel() < graph.csr[1].numel() or v.dtype != torch.uint8
                                                  for v in vis)):
         raise ValueError("vis must be the two u8 CSR-ordered visibility arrays of csr_visibility")

@@ -113,7 +113,7 @@ class DrumTrainStep:
         # transient, shared by the hops
         Smax, Fmax = max(self.S), max(self.F)
         self.ent_sel = _buf(Smax, i32, dev)
-        self.entry_info = _buf(5 * Smax, i32, dev)
+        self.entry_info = _buf(L.FL_ENTRY_INFO_INTS * Smax, i32, dev)
         self.use_order = 0 < r_size <= 16384 and self.topk < L.NO_BUDGET
         self.rel_order = _buf(rows * 2 * r_size, i16, dev) if self.use_order else None
         self.rel_npos = _buf(rows * 2, i32, dev) if self.use_order else None

@@ -69,8 +69,9 @@ typedef struct {
     int64_t slot_capacity;          /* > 0: length of the fact / output buffers;
                                        work beyond it is skipped and flagged      */
     int32_t *status;                /* device int (or NULL): FL_STATUS_* bits     */
-    int32_t *entry_info;            /* i32[5 * S] or NULL: per entry its row and the
-                                       group ranges of both sides, written by
+    int32_t *entry_info;            /* i32[FL_ENTRY_INFO_INTS * S] or NULL: per entry
+                                       its row and the group ranges of both sides,
+                                       written by
                                        fl_hop_plan and read by fl_hop_expand (NULL:
                                        the expansion looks them up)               */
     const uint8_t *vis_ori, *vis_inv; /* u8[M] or NULL: CSR-ordered visibility from
@@ -85,6 +86,9 @@ typedef struct {
                                        fact's triple id (order[p]; 0 for identity),
                                        the tie key of fl_row_reduce_max          */
 } fl_hop_params;
+
+/* int32 values per entry in fl_hop_params.entry_info. */
+enum { FL_ENTRY_INFO_INTS = 5 };
 
 /* Device status bits set by the hop kernels. */
 enum { FL_STATUS_SLOT_OVERFLOW = 1 };

@@ -105,3 +105,17 @@ def test_synthetic_graph_is_seeded_and_shaped():
     ids, h, r, t = training_queries(train, cfg)
     assert h.size == 2 * cfg.batch_size
     assert np.array_equal(r[1::2], r[0::2] + cfg.relations)
+
+
+def test_python_constants_match_header():
+    """Every FL_* constant the Python side uses has the header's value."""
+    import re
+    from flashlog_b200 import _lib as L
+    src = open(os.path.join(REPO, "include", "flashlog_b200.h")).read()
+    header = {m.group(1): m.group(2) for m in re.finditer(r"\b(FL_[A-Z0-9_]+)\s*=\s*([^,}\n/]+)", src)}
+    checked = 0
+    for name in dir(L):
+        if name.startswith("FL_") and name in header:
+            assert getattr(L, name) == eval(header[name].strip()), name
+            checked += 1
+    assert checked >= 12
