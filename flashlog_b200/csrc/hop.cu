@@ -884,7 +884,8 @@ __global__ void __launch_bounds__(kExpandWarps * 32, 3) hop_expand_kernel(Expand
     if (a.work != nullptr) {
         // Warps take chunks of kChunk entries from a queue, so a warp held up
         // by hub entries does not hold up the others of its block.
-        constexpr int64_t kChunk = 16;
+        // 16 entries per grab, fewer when there are not 16 per resident warp
+        const int64_t kChunk = S_live >= nwarps * 16 ? 16 : (S_live >= nwarps * 8 ? 8 : 4);
         for (;;) {
             uint32_t c = 0;
             if (lane == 0) c = atomicAdd(a.work, 1u);
@@ -1647,8 +1648,28 @@ __global__ void __launch_bounds__(1024) rel_order_kernel(const float *w, int64_t
         keys[j] = k;
     }
     const int total = block_sum(c, cnt_scratch);
+    // Bitonic sort.  With one element per thread (P <= blockDim.x), partners
+    // closer than 32 are in the same warp and exchange by shuffles; only the
+    // wider stages go through shared memory with block barriers.
+    const bool one_per_thread = P <= static_cast<int>(blockDim.x) && P >= 32;
     for (int k = 2; k <= P; k <<= 1) {
         for (int j = k >> 1; j > 0; j >>= 1) {
+            if (one_per_thread && j < 32) {
+                // finish this k's stages j < 32 in registers
+                const int i = threadIdx.x;
+                unsigned long long x = i < P ? keys[i] : ~0ull;
+                for (int jj = j; jj > 0; jj >>= 1) {
+                    const unsigned long long y = __shfl_xor_sync(kFull, x, jj);
+                    const bool up = (i & k) == 0;
+                    const bool lower = (i & jj) == 0;
+                    // the lower index keeps the smaller key when sorting up
+                    const bool take_min = (lower == up);
+                    x = take_min ? (x < y ? x : y) : (x < y ? y : x);
+                }
+                if (i < P) keys[i] = x;
+                __syncthreads();
+                break;
+            }
             for (int i = threadIdx.x; i < P; i += blockDim.x) {
                 const int ixj = i ^ j;
                 if (ixj > i) {
