@@ -1519,16 +1519,32 @@ __global__ void __launch_bounds__(kBThreads) hop_backward_kernel(BackwardArgs a)
         const float v = a.val[e];
         const int64_t s0 = a.slot_base[e], cnt = a.entry_count[e];
         float gv = 0.0f;
-        for (int64_t f = lane; f < cnt; f += 32) {
-            const int64_t slot = s0 + f;
-            const int32_t fp = a.fact_pos[slot];
-            if (fp < 0) continue;  // a fact that lost a MAX coalesce gets no gradient
-            const int64_t u = oa + fp;
-            const float g = a.normalize ? (a.g_y[u] / dd - corr) : a.g_y[u];
-            const int c = a.fact_rel[slot];
-            const float m = a.fact_m ? a.fact_m[slot] : 1.0f;
-            gv += g * wrow[c] * m;
-            fixed_atomic_add(acc + 2 * c, to_fixed(g * v * m, scale));
+        for (int64_t f0 = 0; f0 < cnt; f0 += 128) {  // four facts per lane: the loads go out together
+            int32_t fp[4];
+            int c[4];
+            float m[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int64_t f = f0 + k * 32 + lane;
+                fp[k] = -1;
+                c[k] = 0;
+                m[k] = 1.0f;
+                if (f < cnt) {
+                    fp[k] = a.fact_pos[s0 + f];
+                    c[k] = a.fact_rel[s0 + f];
+                    if (a.fact_m) m[k] = a.fact_m[s0 + f];
+                }
+            }
+            float gy[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) gy[k] = fp[k] >= 0 ? a.g_y[oa + fp[k]] : 0.0f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                if (fp[k] < 0) continue;  // an empty slot or a fact that lost a MAX coalesce
+                const float g = a.normalize ? (gy[k] / dd - corr) : gy[k];
+                gv += g * wrow[c[k]] * m[k];
+                fixed_atomic_add(acc + 2 * c[k], to_fixed(g * v * m[k], scale));
+            }
         }
         gv = warp_sum(gv);
         if (lane == 0) a.grad_val[e] = gv;
