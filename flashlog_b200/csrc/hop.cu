@@ -99,10 +99,13 @@ __global__ void csr_visibility_kernel(const int32_t *order, int64_t m, const uin
 constexpr int kExpandWarps = 8;
 constexpr int kTeam = 8;
 constexpr int kStage = 1024;  // relation groups of one side staged per warp
+constexpr int kRankBins = 512;  // bins of the rank select (WarpScratch::hist)
+constexpr uint32_t kNoRank = 0xffffu;
 
 struct WarpScratch {
-    unsigned int hist[256];   // weighted digit counts
-    unsigned int histn[256];  // group counts per digit
+    // radix select: weighted digit counts [0, 256) and group counts per digit
+    // [256, 512); rank select: the weighted counts of 512 rank bins
+    unsigned int hist[512];
     uint32_t ckey[32];        // threshold candidates
     uint32_t ccnt[32];
     int32_t incl[32];
@@ -133,8 +136,9 @@ struct ExpandArgs {
     const float *edge_weight;
     const int64_t *slot_base;
     const EntryInfo *info;             // may be null: rows and group ranges looked up
-    const uint16_t *rel_order;         // per (row, direction): relations by (w desc, id asc), or null
-    const int32_t *rel_npos;           // per (row, direction): relations with w > 0
+    const uint16_t *rel_rank;          // per (row, direction, relation): position in (w desc, id asc) order,
+                                       // kNoRank for w <= 0; or null
+    int32_t rank_bin;                  // relation ranks per bin of the rank select (ceil(r_size / kRankBins))
     uint32_t *work;                    // work-queue counter (zeroed before the launch) or null
     int32_t *fact_dst;
     float *fact_val;
@@ -196,7 +200,7 @@ __device__ void radix_threshold(int64_t n, int64_t budget, WarpScratch &ws, Get 
     uint32_t prefix = 0, pmask = 0;
     int64_t krem = budget;
     for (int shift = 24; shift >= 0; shift -= 8) {
-        for (int d = lane; d < 256; d += 32) { ws.hist[d] = 0; ws.histn[d] = 0; }
+        for (int d = lane; d < 512; d += 32) ws.hist[d] = 0;
         __syncwarp();
         for (int64_t cb = 0; cb < n; cb += 32) {
             uint32_t key, cnt;
@@ -209,7 +213,7 @@ __device__ void radix_threshold(int64_t n, int64_t budget, WarpScratch &ws, Get 
                 const unsigned sum = __reduce_add_sync(peers, cnt);
                 if (lane == __ffs(peers) - 1) {
                     atomicAdd(&ws.hist[d], sum);
-                    atomicAdd(&ws.histn[d], static_cast<unsigned>(__popc(peers)));
+                    atomicAdd(&ws.hist[256 + d], static_cast<unsigned>(__popc(peers)));
                 }
             }
         }
@@ -238,7 +242,7 @@ __device__ void radix_threshold(int64_t n, int64_t budget, WarpScratch &ws, Get 
         krem -= above;
         prefix |= static_cast<uint32_t>(digit) << shift;
         pmask |= 255u << shift;
-        const unsigned ncand = ws.histn[digit];
+        const unsigned ncand = ws.hist[256 + digit];
         __syncwarp();
         if (shift > 0 && ncand <= 32u) {
             unsigned running = 0;
@@ -277,13 +281,66 @@ __device__ void radix_threshold(int64_t n, int64_t budget, WarpScratch &ws, Get 
     *keep = krem;
 }
 
+// c2 threshold in rank space.  rk[rel] is the relation's position in the
+// row's (w descending, relation ascending) order; kNoRank marks w <= 0.  On
+// one side of one source every relation has at most one group and groups are
+// in relation order, so the reference's rule (flashlog.cu:26-63: groups above
+// the weight threshold whole, groups at it in group order until the budget is
+// spent) takes exactly the groups of smallest rank until the budget is
+// reached.  The select therefore needs no comparison of weights: the groups'
+// counts (clamped to the budget, which changes no take) are summed into
+// kRankBins bins of rank_bin consecutive ranks, a warp scan over the bins
+// finds the bin where the running total reaches the budget, and the at most
+// rank_bin <= 32 groups of that bin, one per lane, finish it.
+//
+// Pass 1 (`scatter`) has filled ws.hist; `members(lo, hi, quota)` must store
+// the clamped count of each group with rank in [lo, hi) at quota[rank - lo].
+// Returns *thr = the rank of the group at which the budget is reached and
+// *keep = the edges that group still takes.
+template <typename Members>
+__device__ void rank_select(int64_t budget, int rank_bin, WarpScratch &ws, Members members, uint32_t *thr,
+                            int64_t *keep) {
+    const int lane = threadIdx.x & 31;
+    constexpr int kPer = kRankBins / 32;  // bins per lane, contiguous
+    uint32_t part = 0;
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) part += ws.hist[lane * kPer + ((k + (lane >> 1)) & (kPer - 1))];
+    const uint32_t krem = static_cast<uint32_t>(budget);
+    const uint32_t incl = warp_inclusive_scan(part);
+    const unsigned ball = __ballot_sync(kFull, incl >= krem && incl - part < krem);
+    const int src = __ffs(ball) - 1;  // the clamped total reaches the budget, so one lane crosses it
+    const uint32_t base = __shfl_sync(kFull, incl - part, src);
+    const uint32_t hb = lane < kPer ? ws.hist[src * kPer + lane] : 0u;
+    const uint32_t hi = warp_inclusive_scan(hb);
+    const unsigned bb = __ballot_sync(kFull, lane < kPer && base + hi >= krem && base + hi - hb < krem);
+    const int bl = __ffs(bb) - 1;
+    const int bin = src * kPer + bl;
+    const uint32_t above = __shfl_sync(kFull, base + hi - hb, bl);
+    __syncwarp();
+    ws.quota[lane] = 0;
+    __syncwarp();
+    const uint32_t lo = static_cast<uint32_t>(bin) * static_cast<uint32_t>(rank_bin);
+    members(lo, lo + static_cast<uint32_t>(rank_bin), ws.quota);
+    __syncwarp();
+    const int32_t qc = lane < rank_bin ? ws.quota[lane] : 0;
+    const int32_t qi = warp_inclusive_scan(qc);
+    const int32_t rem = static_cast<int32_t>(krem - above);  // >= 1
+    const unsigned qb = __ballot_sync(kFull, qc > 0 && qi >= rem && qi - qc < rem);
+    const int ql = __ffs(qb) - 1;
+    *thr = lo + static_cast<uint32_t>(ql);
+    *keep = rem - (__shfl_sync(kFull, qi, ql) - __shfl_sync(kFull, qc, ql));
+    __syncwarp();
+}
+
 // Threshold of one side of one entry, computed by a whole warp.  With `stg`
 // the side's keys and clamped counts are left in stg for the take pass and
 // *staged is set.
-__device__ bool group_threshold(const float *wdir, const Side &sd, int64_t g0, int64_t g1, int64_t budget,
-                                WarpScratch &ws, StageBuf *stg, bool *staged, uint32_t *thr, int64_t *keep) {
+__device__ bool group_threshold(const float *wdir, const uint16_t *rk, int rank_bin, const Side &sd, int64_t g0,
+                                int64_t g1, int64_t budget, WarpScratch &ws, StageBuf *stg, bool *staged, bool *ranked,
+                                uint32_t *thr, int64_t *keep) {
     const int lane = threadIdx.x & 31;
     *staged = false;
+    *ranked = false;
     if (g1 - g0 <= 32) {
         // One group per lane: every lane counts the groups at or above its own key.
         uint32_t key, cnt;
@@ -305,6 +362,69 @@ __device__ bool group_threshold(const float *wdir, const Side &sd, int64_t g0, i
         return true;
     }
     const int64_t n = g1 - g0;
+    if (rk != nullptr && budget >= 1 && budget < 65536) {
+        // rank select; staged keys are (rank << 16) | relation
+        *ranked = true;
+        for (int d = lane; d < kRankBins; d += 32) ws.hist[d] = 0u;
+        __syncwarp();
+        const uint32_t cap = static_cast<uint32_t>(budget);
+        int64_t total = 0;
+        if (stg != nullptr && n <= kStage) {
+            for (int64_t cb = 0; cb < n; cb += 128) {  // four groups per lane: the loads are issued together
+                int32_t rel[4];
+                uint32_t c[4], r[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int64_t j = cb + u * 32 + lane;
+                    rel[u] = j < n ? static_cast<int32_t>(sd.grel[g0 + j]) : -1;
+                    c[u] = j < n ? static_cast<uint32_t>(sd.gcount[g0 + j]) : 0u;
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) r[u] = rel[u] >= 0 ? static_cast<uint32_t>(rk[rel[u]]) : kNoRank;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int64_t j = cb + u * 32 + lane;
+                    const uint32_t cc = r[u] != kNoRank ? c[u] : 0u;
+                    const uint32_t cl = cc < cap ? cc : cap;
+                    if (j < n) {
+                        stg->key[j] = (r[u] << 16) | static_cast<uint32_t>(rel[u]);
+                        stg->cnt[j] = static_cast<uint16_t>(cl);
+                        if (cl > 0u) atomicAdd(&ws.hist[r[u] / static_cast<uint32_t>(rank_bin)], cl);
+                    }
+                    total += cc;
+                }
+            }
+            __syncwarp();
+            *staged = true;
+            if (warp_sum(total) <= budget) return false;
+            rank_select(budget, rank_bin, ws, [&](uint32_t lo, uint32_t hi, int32_t *quota) {
+                for (int64_t j = lane; j < n; j += 32) {
+                    const uint32_t r = stg->key[j] >> 16;
+                    if (r >= lo && r < hi) quota[r - lo] = stg->cnt[j];
+                }
+            }, thr, keep);
+            return true;
+        }
+        for (int64_t j = lane; j < n; j += 32) {
+            const uint32_t r = rk[sd.grel[g0 + j]];
+            const uint32_t cc = r != kNoRank ? static_cast<uint32_t>(sd.gcount[g0 + j]) : 0u;
+            const uint32_t cl = cc < cap ? cc : cap;
+            if (cl > 0u) atomicAdd(&ws.hist[r / static_cast<uint32_t>(rank_bin)], cl);
+            total += cc;
+        }
+        __syncwarp();
+        if (warp_sum(total) <= budget) return false;
+        rank_select(budget, rank_bin, ws, [&](uint32_t lo, uint32_t hi, int32_t *quota) {
+            for (int64_t j = lane; j < n; j += 32) {
+                const uint32_t r = rk[sd.grel[g0 + j]];
+                if (r >= lo && r < hi) {
+                    const uint32_t c = static_cast<uint32_t>(sd.gcount[g0 + j]);
+                    quota[r - lo] = static_cast<int32_t>(c < cap ? c : cap);
+                }
+            }
+        }, thr, keep);
+        return true;
+    }
     if (stg != nullptr && n <= kStage && budget < 65536) {
         int64_t total = 0;
         for (int64_t cb = 0; cb < n; cb += 128) {  // four groups per lane: the loads are issued together
@@ -364,79 +484,19 @@ __device__ __forceinline__ double splitmix_phase(int64_t seed, int64_t b, int64_
     return static_cast<double>(z >> 11) * 0x1.0p-53;
 }
 
-// c2 of one dense side (many groups, degree above the budget) by walking the
-// row's relations in (w descending, id ascending) order, 32 at a time, and
-// finding the side's group of each relation by binary search in the staged
-// group relations.  Taking edges in walk order until the budget is spent is
-// the reference's rule (flashlog.cu:26-63): groups above the threshold whole,
-// groups at it in group order.  The taken groups are then emitted in group
-// order.  Returns false, with nothing written, when more than 32 groups take
-// edges (the caller then uses the staged threshold).
-__device__ bool walk_side(const ExpandArgs &a, WarpScratch &ws, StageBuf *stg, const Side &sd, const uint8_t *vis,
-                          const float *wdir, int64_t off, int64_t row, int dir, float v, int64_t g0, int64_t g1,
-                          int64_t out, int64_t *written, bool drop_masked, bool edge_w, bool edge_score) {
+// Emits, in lane order, the facts of the (at most 32) groups held one per
+// lane: `take` edges from CSR position `start`, each with value prod * m and
+// relation column rel_abs; facts the mask hides are dropped when drop_masked.
+__device__ __forceinline__ void emit_groups(const ExpandArgs &a, WarpScratch &ws, const Side &sd, const uint8_t *vis,
+                                            int32_t take, int32_t start, float prod, int32_t rel_abs, int64_t out,
+                                            int64_t *written, bool drop_masked, bool edge_w, bool edge_score) {
     const int lane = threadIdx.x & 31;
-    const int n = static_cast<int>(g1 - g0);
-    const int32_t budget = static_cast<int32_t>(a.topk);
-    uint16_t *rels = stg->cnt;  // the side's group relations, ascending (CSR group order)
-    for (int j = lane; j < n; j += 32) rels[j] = static_cast<uint16_t>(sd.grel[g0 + j]);
-    __syncwarp();
-    const uint16_t *ord = a.rel_order + (row * 2 + dir) * a.r_size;
-    const int32_t npos = a.rel_npos[row * 2 + dir];
-    int32_t cum = 0;
-    int ntaken = 0;
-    for (int32_t k0 = 0; k0 < npos && cum < budget; k0 += 32) {
-        const int32_t k = k0 + lane;
-        const bool has = k < npos;
-        const uint16_t rel = has ? ord[k] : 0;
-        int lo = 0, hi = n;  // first group with relation >= rel
-        while (lo < hi) {
-            const int mid = (lo + hi) >> 1;
-            if (rels[mid] < rel) lo = mid + 1; else hi = mid;
-        }
-        const bool found = has && lo < n && rels[lo] == rel;
-        const int32_t cnt = found ? sd.gcount[g0 + lo] : 0;
-        const int32_t cc = cnt < budget ? cnt : budget;
-        const int32_t incl = warp_inclusive_scan(cc);
-        const int32_t left = budget - (cum + incl - cc);
-        const int32_t take = found && left > 0 ? (left < cnt ? left : cnt) : 0;
-        const unsigned b = __ballot_sync(kFull, take > 0);
-        if (take > 0) {
-            const int p = ntaken + __popc(b & lanemask_lt());
-            if (p < 32) { ws.ckey[p] = static_cast<uint32_t>(lo); ws.ccnt[p] = static_cast<uint32_t>(take); }
-        }
-        ntaken += __popc(b);
-        cum += __shfl_sync(kFull, incl, 31);
-    }
-    __syncwarp();
-    if (ntaken > 32) return false;
-    // taken groups in group order: rank by group index (distinct)
-    const bool mine = lane < ntaken;
-    const uint32_t gi = mine ? ws.ckey[lane] : 0xffffffffu;
-    const int32_t tk = mine ? static_cast<int32_t>(ws.ccnt[lane]) : 0;
-    int rank = 0;
-#pragma unroll 8
-    for (int j = 0; j < 32; ++j) rank += __shfl_sync(kFull, gi, j) < gi ? 1 : 0;
-    __syncwarp();
-    if (mine) { ws.quota[rank] = tk; ws.incl[rank] = static_cast<int32_t>(gi); }
-    __syncwarp();
-    const int32_t take = lane < ntaken ? ws.quota[lane] : 0;
-    const int32_t g = lane < ntaken ? ws.incl[lane] : 0;
-    int32_t rel = 0;
-    float wg = 0.0f;
-    int32_t start = 0;
-    if (lane < ntaken) {
-        rel = rels[g];
-        wg = wdir[rel];
-        start = sd.gstart[g0 + g];
-    }
     const int32_t incl = warp_inclusive_scan(take);
     const int32_t tot = __shfl_sync(kFull, incl, 31);
-    __syncwarp();
     ws.incl[lane] = incl;
     ws.start[lane] = start;
-    ws.prod[lane] = v * wg;
-    ws.rel[lane] = rel + static_cast<int32_t>(off);
+    ws.prod[lane] = prod;
+    ws.rel[lane] = rel_abs;
     __syncwarp();
     int64_t wr = *written;
     for (int32_t f0 = 0; f0 < tot; f0 += 32) {
@@ -469,7 +529,6 @@ __device__ bool walk_side(const ExpandArgs &a, WarpScratch &ws, StageBuf *stg, c
     }
     __syncwarp();
     *written = wr;
-    return true;
 }
 
 // One source entry expanded by a whole warp: ori groups, inv groups, identity.
@@ -506,7 +565,8 @@ __device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, StageBuf
         const float *wdir = wrow + off;
         const int64_t g0 = dir ? e.g0i : e.g0o, g1 = dir ? e.g1i : e.g1o;
         if (g0 == g1) continue;
-        bool use_thr = false, staged = false;
+        bool use_thr = false, staged = false, ranked = false;
+        const uint16_t *rk = nullptr;
         uint32_t thr = 0;
         int64_t keep_thr = 0;
         // sampled-mode state (lane 0 only)
@@ -541,13 +601,43 @@ __device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, StageBuf
                 q_prefix = 0;
             }
         } else if (skip_nonpos && a.topk < kNoBudget) {
-            if (stg != nullptr && a.rel_order != nullptr && g1 - g0 > 32 && g1 - g0 <= kStage && a.topk < 65536 &&
-                (g1 - g0) * 8 >= a.r_size &&
-                static_cast<int64_t>(sd.gstart[g1 - 1]) + sd.gcount[g1 - 1] - sd.gstart[g0] > a.topk &&
-                walk_side(a, ws, stg, sd, vis, wdir, off, row, dir, v, g0, g1, out, &written, drop_masked, edge_w,
-                          edge_score))
-                continue;
-            use_thr = group_threshold(wdir, sd, g0, g1, a.topk, ws, stg, &staged, &thr, &keep_thr);
+            rk = a.rel_rank != nullptr ? a.rel_rank + (row * 2 + dir) * a.r_size : nullptr;
+            use_thr = group_threshold(wdir, rk, a.rank_bin, sd, g0, g1, a.topk, ws, stg, &staged, &ranked, &thr,
+                                      &keep_thr);
+        }
+        if (!kSampled && staged && ranked) {
+            // The taking groups, compacted in group order in place:
+            // key = (group offset << 16) | relation, cnt = edges taken.
+            const uint32_t last = use_thr ? thr : 0xfffffffeu;
+            const int n = static_cast<int>(g1 - g0);
+            int ntk = 0;
+            for (int cb = 0; cb < n; cb += 32) {
+                const int j = cb + lane;
+                const uint32_t key = j < n ? stg->key[j] : (kNoRank << 16);
+                const int32_t cnt = j < n ? stg->cnt[j] : 0;
+                const uint32_t r = key >> 16;
+                const int32_t take = r == kNoRank || r > last ? 0 : (r < last ? cnt : static_cast<int32_t>(keep_thr));
+                const unsigned b = __ballot_sync(kFull, take > 0);
+                if (take > 0) {  // positions below cb + 32: entries of this chunk are read already
+                    const int p = ntk + __popc(b & lanemask_lt());
+                    stg->key[p] = (static_cast<uint32_t>(j) << 16) | (key & 0xffffu);
+                    stg->cnt[p] = static_cast<uint16_t>(take);
+                }
+                ntk += __popc(b);
+                __syncwarp();
+            }
+            for (int k0 = 0; k0 < ntk; k0 += 32) {
+                const int k = k0 + lane;
+                const bool has = k < ntk;
+                const uint32_t key = has ? stg->key[k] : 0u;
+                const int32_t take = has ? stg->cnt[k] : 0;
+                const int32_t rel = static_cast<int32_t>(key & 0xffffu);
+                const int32_t start = has ? sd.gstart[g0 + (key >> 16)] : 0;
+                const float wg = has ? wdir[rel] : 0.0f;
+                emit_groups(a, ws, sd, vis, take, start, v * wg, rel + static_cast<int32_t>(off), out, &written,
+                            drop_masked, edge_w, edge_score);
+            }
+            continue;
         }
         int64_t tie_seen = 0;
         for (int64_t cb = g0; cb < g1; cb += 32) {
@@ -619,6 +709,9 @@ __device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, StageBuf
                     take = valid ? ws.quota[lane] : 0;
                 } else if (!skip_nonpos) {
                     take = cnt;
+                } else if (ranked) {
+                    const uint32_t r = valid ? static_cast<uint32_t>(rk[rel]) : kNoRank;
+                    take = r == kNoRank ? 0 : (!use_thr || r < thr ? cnt : (r == thr ? static_cast<int32_t>(keep_thr) : 0));
                 } else if (!use_thr) {
                     take = wg > 0.0f ? cnt : 0;
                 } else {
@@ -638,43 +731,9 @@ __device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, StageBuf
                 }
                 if (!valid) take = 0;
             }
-            int32_t incl = warp_inclusive_scan(take);
-            int32_t tot = __shfl_sync(kFull, incl, 31);
-            if (tot == 0) continue;
-            ws.incl[lane] = incl;
-            ws.start[lane] = take > 0 ? sd.gstart[g] : 0;
-            ws.prod[lane] = v * wg;
-            ws.rel[lane] = rel + static_cast<int32_t>(off);
-            __syncwarp();
-            for (int32_t f0 = 0; f0 < tot; f0 += 32) {
-                const int32_t f = f0 + lane;
-                const bool act = f < tot;
-                bool visible = false;
-                int32_t dst = 0, frel = 0, edge = 0;
-                float value = 0.0f, m = 1.0f;
-                if (act) {
-                    int lo = 0, hi = 31;  // first lane with incl > f
-                    while (lo < hi) { int mid = (lo + hi) >> 1; if (ws.incl[mid] > f) hi = mid; else lo = mid + 1; }
-                    const int32_t eoff = f - (lo ? ws.incl[lo - 1] : 0);
-                    const int64_t p = static_cast<int64_t>(ws.start[lo]) + eoff;
-                    fact_mask(a, sd, vis, p, drop_masked, edge_w, edge_score, &m, &visible);
-                    dst = sd.col[p];
-                    value = ws.prod[lo] * m;
-                    frel = ws.rel[lo];
-                    if (a.fact_edge) edge = (a.flags & FL_EDGE_POS) ? static_cast<int32_t>(p) : sd.order[p];
-                }
-                const unsigned ball = __ballot_sync(kFull, act && visible);
-                if (act && visible) {
-                    const int64_t pos = out + written + __popc(ball & lanemask_lt());
-                    a.fact_dst[pos] = dst;
-                    a.fact_val[pos] = value;
-                    a.fact_rel[pos] = static_cast<int16_t>(frel);
-                    if (a.fact_m) a.fact_m[pos] = m;
-                    if (a.fact_edge) a.fact_edge[pos] = edge;
-                }
-                written += __popc(ball);
-            }
-            __syncwarp();
+            if (!__any_sync(kFull, take > 0)) continue;
+            emit_groups(a, ws, sd, vis, take, take > 0 ? sd.gstart[g] : 0, v * wg, rel + static_cast<int32_t>(off), out,
+                        &written, drop_masked, edge_w, edge_score);
         }
     }
     if (!wot_i) {
@@ -1641,29 +1700,28 @@ __global__ void __launch_bounds__(256) normalize_backward_kernel(const int64_t *
     for (int64_t i = a0 + threadIdx.x; i < a1; i += 256) gx[i] = g[i] / d - corr;
 }
 
-// Per (row, direction): the relations j in [0, R) with w[row, dir * R + j] > 0
-// ordered by (w descending, j ascending), by a bitonic sort of 64-bit keys in
-// shared memory.  One CTA per (row, direction).
-__global__ void __launch_bounds__(1024) rel_order_kernel(const float *w, int64_t n, int64_t R, int P, uint16_t *order,
-                                                         int32_t *npos) {
+// Per (row, direction): rank[j] = the position of relation j in the order
+// (w[row, dir * R + j] descending, j ascending) of the relations with w > 0,
+// kNoRank for the others; by a bitonic sort of 64-bit keys in shared memory.
+// One CTA per (row, direction).
+__global__ void __launch_bounds__(1024) rel_rank_kernel(const float *w, int64_t n, int64_t R, int P, uint16_t *rank) {
     extern __shared__ __align__(16) unsigned long long keys[];
-    __shared__ int cnt_scratch[33];
     const int64_t rd = blockIdx.x;
     const int64_t row = rd >> 1, dir = rd & 1;
     const float *wd = w + row * n + dir * R;
-    int c = 0;
+    uint16_t *rk = rank + rd * R;
     for (int j = threadIdx.x; j < P; j += blockDim.x) {
         unsigned long long k = ~0ull;
         if (j < R) {
             const float x = wd[j];
-            if (x > 0.0f) {
+            if (x > 0.0f)
                 k = (static_cast<unsigned long long>(0xffffffffu - __float_as_uint(x)) << 32) | static_cast<unsigned>(j);
-                ++c;
-            }
+            else
+                rk[j] = static_cast<uint16_t>(kNoRank);
         }
         keys[j] = k;
     }
-    const int total = block_sum(c, cnt_scratch);
+    __syncthreads();
     // Bitonic sort.  With one element per thread (P <= blockDim.x), partners
     // closer than 32 are in the same warp and exchange by shuffles; only the
     // wider stages go through shared memory with block barriers.
@@ -1697,9 +1755,10 @@ __global__ void __launch_bounds__(1024) rel_order_kernel(const float *w, int64_t
             __syncthreads();
         }
     }
-    for (int j = threadIdx.x; j < total; j += blockDim.x)
-        order[rd * R + j] = static_cast<uint16_t>(keys[j] & 0xffffu);
-    if (threadIdx.x == 0) npos[rd] = total;
+    for (int k = threadIdx.x; k < P; k += blockDim.x) {
+        const unsigned long long key = keys[k];
+        if (key != ~0ull) rk[key & 0xffffu] = static_cast<uint16_t>(k);
+    }
 }
 
 }  // namespace
@@ -1714,21 +1773,20 @@ static Side make_side(const fl_csr_side &s, const float *mask_csr) {
     return d;
 }
 
-int relation_order(const float *w, int64_t rows, int64_t r_size, uint16_t *order, int32_t *npos, cudaStream_t st) {
-    FL_REQUIRE(r_size > 0 && r_size <= 16384, "relation order supports 1..16384 relations per direction");
+int relation_rank(const float *w, int64_t rows, int64_t r_size, uint16_t *rank, cudaStream_t st) {
+    FL_REQUIRE(r_size > 0 && r_size <= 16384, "relation ranks support 1..16384 relations per direction");
     int P = 1;
     while (P < r_size) P <<= 1;
     const size_t smem = static_cast<size_t>(P) * sizeof(unsigned long long);
     static bool attr_set = false;
     if (!attr_set) {
-        FL_CUDA(cudaFuncSetAttribute(rel_order_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        FL_CUDA(cudaFuncSetAttribute(rel_rank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(16384 * sizeof(unsigned long long))));
         attr_set = true;
     }
     if (rows > 0)
-        launch(rel_order_kernel, static_cast<unsigned>(rows * 2), 1024, smem, st, w, 2 * r_size + 1, r_size, P, order,
-               npos);
-    return check_launch("relation_order");
+        launch(rel_rank_kernel, static_cast<unsigned>(rows * 2), 1024, smem, st, w, 2 * r_size + 1, r_size, P, rank);
+    return check_launch("relation_rank");
 }
 
 int csr_visibility(const int32_t *order, int64_t m, const uint8_t *mask_triple, uint8_t *vis, cudaStream_t st) {
@@ -1789,7 +1847,9 @@ int hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *en
     a.ori = make_side(ori, mask_csr_ori); a.inv = make_side(inv, mask_csr_inv);
     a.mask_triple = mask_triple; a.edge_weight = edge_weight; a.slot_base = slot_base;
     a.vis_ori = p->vis_ori; a.vis_inv = p->vis_inv; a.info = reinterpret_cast<const EntryInfo *>(p->entry_info); a.work = p->work;
-    a.rel_order = p->rel_order; a.rel_npos = p->rel_npos; a.fact_edge = p->fact_edge;
+    a.rel_rank = p->rel_rank; a.fact_edge = p->fact_edge;
+    a.rank_bin = static_cast<int32_t>((p->r_size + kRankBins - 1) / kRankBins);
+    if (a.rel_rank != nullptr && (a.rank_bin < 1 || a.rank_bin > 32)) a.rel_rank = nullptr;
     a.fact_dst = fact_dst; a.fact_val = fact_val; a.fact_rel = fact_rel; a.fact_m = fact_m; a.entry_count = entry_count;
     int sms = fl_device_sm_count();
     const int64_t per_sm = 3;  // resident CTAs per SM (registers and staging buffers)

@@ -204,27 +204,26 @@ class HopForward:
 
 
 def hop_params(rows, Lch, n, r_size, E, topk_edges, flags, seed=-1, eps=EPS, slot_capacity=0, status=None,
-               entry_info=None, vis=None, work=None, rel_order=None):
+               entry_info=None, vis=None, work=None, rel_rank=None):
     return L.fl_hop_params(rows, Lch, n, r_size, E, int(min(topk_edges, L.NO_BUDGET)), int(flags), int(seed),
                            float(eps), int(slot_capacity), None if status is None else status.data_ptr(),
                            None if entry_info is None else entry_info.data_ptr(),
                            None if vis is None else vis[0].data_ptr(), None if vis is None else vis[1].data_ptr(),
                            None if work is None else work.data_ptr(),
-                           None if rel_order is None else rel_order[0].data_ptr(),
-                           None if rel_order is None else rel_order[1].data_ptr())
+                           None if rel_rank is None else rel_rank.data_ptr())
 
 
-def relation_order(w, r_size: int):
-    """Per (row, direction) relations with w > 0 by (w desc, id asc); None
-    when r_size is outside the supported range (the expansion then selects
-    thresholds without it)."""
+def relation_rank(w, r_size: int):
+    """Per (row, direction, relation) the relation's position in the order
+    (w desc, id asc) of the relations with w > 0 (0xffff, i.e. -1 as int16,
+    for w <= 0); None when r_size is outside the supported range (the
+    expansion then selects thresholds over the weights)."""
     if not (0 < r_size <= 16384):
         return None
     rows = w.numel() // (2 * r_size + 1)
-    order = torch.empty(max(rows * 2 * r_size, 1), dtype=torch.int16, device=w.device)
-    npos = torch.empty(max(rows * 2, 1), dtype=torch.int32, device=w.device)
-    check(lib().fl_relation_order(_p(w), rows, r_size, _p(order), _p(npos), _stream()), "relation_order")
-    return order, npos
+    rank = torch.empty(max(rows * 2 * r_size, 1), dtype=torch.int16, device=w.device)
+    check(lib().fl_relation_rank(_p(w), rows, r_size, _p(rank), _stream()), "relation_rank")
+    return rank
 
 
 def csr_visibility(graph: Graph, mask_triple):
@@ -251,7 +250,7 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
                 mask_triple=None, mask_csr=None, edge_weight=None, seed: int = -1, eps: float = EPS,
                 keep_facts: bool = False, record: bool = True, timing=None, slot_capacity=None,
                 status=None, out_sync: bool = True, vis=None, reduce: str = "sum",
-                max_bits: bool = False) -> HopForward:
+                max_bits: bool = False, rank_select: bool = True) -> HopForward:
     """Expansion + per-row coalesce-sum + normalization of one hop.
 
     slot_capacity=None sizes the fact buffers exactly (one host sync for the
@@ -266,6 +265,9 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
     (FlashLogFunctionSparse3DTopKMax); its out_x holds the maxima, out_y is
     None and fact_pos is -1 for the facts that did not win.  max_bits compares
     fact values by their fp32 bit patterns (the dense MAX order).
+    rank_select=False makes the expansion select c2 thresholds by a radix
+    select over the groups' weights instead of over relation ranks (same
+    result; the path used when r_size exceeds 16384).
     """
     if reduce not in ("sum", "max"):
         raise ValueError("reduce must be 'sum' or 'max'")
@@ -288,10 +290,10 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
                                                  for v in vis)):
         raise ValueError("vis must be the two u8 CSR-ordered visibility arrays of csr_visibility")
     work = torch.empty(1, dtype=torch.int32, device=dev)
-    rel_order = (relation_order(w, r_size) if (flags & L.FL_SKIP_NONPOS_W) and topk_edges < L.NO_BUDGET
-                 and not (flags & L.FL_SAMPLED) else None)
+    rel_rank = (relation_rank(w, r_size) if rank_select and (flags & L.FL_SKIP_NONPOS_W)
+                and topk_edges < L.NO_BUDGET and not (flags & L.FL_SAMPLED) else None)
     params = hop_params(rows, Lch, n, r_size, graph.E, topk_edges, flags, seed, eps, slot_capacity or 0, status,
-                        entry_info, vis, work, rel_order)
+                        entry_info, vis, work, rel_rank)
     check(lib().fl_hop_plan(ctypes.byref(params), _p(row_ptr), _p(ent), S, graph.ori, graph.inv, _p(slot_base),
                             ctypes.byref(total) if sync else None, _p(ws), ws.numel(), _stream()), "hop_plan")
     T = max(total.value, 1) if sync else max(int(slot_capacity), 1)

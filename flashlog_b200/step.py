@@ -114,9 +114,8 @@ class DrumTrainStep:
         Smax, Fmax = max(self.S), max(self.F)
         self.ent_sel = _buf(Smax, i32, dev)
         self.entry_info = _buf(L.FL_ENTRY_INFO_INTS * Smax, i32, dev)
-        self.use_order = 0 < r_size <= 16384 and self.topk < L.NO_BUDGET
-        self.rel_order = _buf(rows * 2 * r_size, i16, dev) if self.use_order else None
-        self.rel_npos = _buf(rows * 2, i32, dev) if self.use_order else None
+        self.use_rank = 0 < r_size <= 16384 and self.topk < L.NO_BUDGET
+        self.rel_rank = _buf(rows * 2 * r_size, i16, dev) if self.use_rank else None
         self.fact_dst = _buf(Fmax, i32, dev)
         self.fact_val = _buf(Fmax, f32, dev)
         self.grad_sel = _buf(Smax, f32, dev)
@@ -158,8 +157,7 @@ class DrumTrainStep:
         return L.fl_hop_params(self.rows, self.N, self.n, self.r_size, self.graph.E, int(self.topk), int(flags), -1,
                                float(self.eps), int(self.F[t]), self.status.data_ptr(), self.entry_info.data_ptr(),
                                self.vis[0].data_ptr(), self.vis[1].data_ptr(), self.work.data_ptr(),
-                               self.rel_order.data_ptr() if self.use_order else None,
-                               self.rel_npos.data_ptr() if self.use_order else None)
+                               self.rel_rank.data_ptr() if self.use_rank else None)
 
     # ------------------------------------------------------------------
     def run(self):
@@ -187,9 +185,8 @@ class DrumTrainStep:
                 rp_s, ent_s, val_s = rp_in, ent_in, val_in
                 self.rp_sel[t].copy_(rp_in)
                 self.val_sel[t][:self.S[t]].copy_(val_in[:self.S[t]])
-            if self.use_order:
-                check(lb.fl_relation_order(_p(self.w[t]), rows, self.r_size, _p(self.rel_order), _p(self.rel_npos),
-                                           st), "relation_order")
+            if self.use_rank:
+                check(lb.fl_relation_rank(_p(self.w[t]), rows, self.r_size, _p(self.rel_rank), st), "relation_rank")
             params = self._params(t, self.flags)
             check(lb.fl_hop_plan(ctypes.byref(params), _p(rp_s), _p(ent_s), self.S[t], g.ori, g.inv,
                                  _p(self.slot_base[t]), None, ws, wsn, st), "hop_plan")

@@ -79,9 +79,8 @@ typedef struct {
                                        read through `order` (same result)         */
     uint32_t *work;                 /* device u32 or NULL: work queue of fl_hop_expand
                                        (it zeroes it); NULL: static assignment    */
-    const uint16_t *rel_order;      /* u16[rows * 2 * r_size] or NULL: from
-                                       fl_relation_order of the same w            */
-    const int32_t *rel_npos;        /* i32[rows * 2] (with rel_order)            */
+    const uint16_t *rel_rank;       /* u16[rows * 2 * r_size] or NULL: from
+                                       fl_relation_rank of the same w             */
     int32_t *fact_edge;             /* i32[slots] or NULL: fl_hop_expand writes each
                                        fact's triple id (order[p]; 0 for identity),
                                        the tie key of fl_row_reduce_max          */
@@ -145,14 +144,15 @@ int fl_hop_plan(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *e
                 fl_csr_side inv, int64_t *slot_base, int64_t *total_slots, void *ws, size_t ws_bytes,
                 fl_stream_t stream);
 
-/* Per (row, direction): the relations with w > 0 ordered by (w descending,
- * relation ascending), order u16[rows * 2 * r_size], and their count npos
- * i32[rows * 2].  fl_hop_expand uses it (through fl_hop_params) to find the c2
- * threshold of sides with many relation groups by walking the relations in
- * weight order instead of selecting over all of the side's groups.
+/* Per (row, direction): rank u16[rows * 2 * r_size], the position of each
+ * relation in the order (w descending, relation ascending) of the relations
+ * with w > 0, and 0xffff for w <= 0.  fl_hop_expand uses it (through
+ * fl_hop_params.rel_rank) for the c2 threshold of sides with more than 32
+ * relation groups: taking a side's groups in rank order until the budget is
+ * spent is the reference's selection (flashlog.cu:26-63), found by a scan
+ * over rank bins instead of a radix select over the groups' weights.
  * r_size <= 16384. */
-int fl_relation_order(const float *w, int64_t rows, int64_t r_size, uint16_t *order, int32_t *npos,
-                      fl_stream_t stream);
+int fl_relation_rank(const float *w, int64_t rows, int64_t r_size, uint16_t *rank, fl_stream_t stream);
 
 /* CSR-ordered visibility of one side: vis[p] = mask_triple[order[p]] != 0.
  * The gather of prepare_csr_masks / apply_mask_cuda (flashlog_kernel.py:225-255,

@@ -385,16 +385,18 @@ def test_hop_is_deterministic(fk, g1):
         assert a.tobytes() == b.tobytes()
 
 
-@pytest.mark.parametrize("topk", [5, 40])
-def test_threshold_paths_and_visibility(fk, topk):
+@pytest.mark.parametrize("R,ties", [(1100, True), (9000, True), (9000, False)])
+@pytest.mark.parametrize("topk", [5, 40, 300])
+def test_threshold_paths_and_visibility(fk, topk, R, ties):
     """Entries with <= 8, 9-32, 33-1024 and > 1024 relation groups per side
-    (team, warp-register, staged and global threshold paths), tied weights,
-    hidden triples read through `order` and through the CSR-ordered
-    visibility: bit-identical to the oracle either way."""
+    (team, warp-register, staged and global threshold paths; rank bins of 3
+    and 18 relations), tied and distinct weights, hidden triples read through
+    `order` and through the CSR-ordered visibility: bit-identical to the
+    oracle either way."""
     from flashlog_b200 import ops
     from flashlog_b200.ops import Graph
-    rng = np.random.default_rng(77 + topk)
-    E, R = 5000, 1100
+    rng = np.random.default_rng(77 + topk + R)
+    E = 5000
     h = rng.integers(0, E, 60_000)
     r = rng.integers(0, R, 60_000)
     t = rng.integers(0, E, 60_000)
@@ -422,13 +424,14 @@ def test_threshold_paths_and_visibility(fk, topk):
     row = np.concatenate(rows_).astype(np.int64)
     ent = np.concatenate(ents_).astype(np.int64)
     val = rng.random(ent.size).astype(np.float32)
-    w = _w(rng, B, L, 2 * R + 1, True)
+    w = _w(rng, B, L, 2 * R + 1, ties)
     mask = (rng.random(tri.shape[0]) > 0.1).astype(np.uint8)
     ref = O.hop_forward(row, ent, val, w, csr_np, R, E, topk_edges=topk, mode=O.MODE_TOPK, mask=mask)
     rp, en, _ = ops.coo_to_rows(_cuda(row // L), _cuda(row % L), _cuda(ent), B, L, E)
     mt = _cuda(mask)
-    for vis in (None, ops.csr_visibility(graph, mt)):
-        fw = ops.hop_forward(rp, en, _cuda(val), _cuda(w), graph, R, topk, 1 | 2, mask_triple=mt, vis=vis)
+    for vis, rank_select in ((None, True), (ops.csr_visibility(graph, mt), True), (None, False)):
+        fw = ops.hop_forward(rp, en, _cuda(val), _cuda(w), graph, R, topk, 1 | 2, mask_triple=mt, vis=vis,
+                             rank_select=rank_select)
         counts = (fw.out_row_ptr[1:] - fw.out_row_ptr[:-1]).cpu().numpy()
         keys = np.repeat(np.arange(B * L), counts) * E + fw.out_ent.cpu().numpy()
         assert np.array_equal(keys, ref["out_key"])
@@ -438,6 +441,26 @@ def test_threshold_paths_and_visibility(fk, topk):
         rgv, rgw = O.hop_backward(ref, g, row, val, w, R)
         np.testing.assert_allclose(gv.cpu().numpy(), rgv, rtol=RTOL, atol=1e-5)
         np.testing.assert_allclose(gw.cpu().numpy(), rgw, rtol=RTOL, atol=1e-5)
+
+
+@pytest.mark.parametrize("R", [7, 822, 14824])
+def test_relation_rank(R):
+    """fl_relation_rank: each relation's position in (w desc, id asc) order
+    among the relations with w > 0, 0xffff (-1 as int16) for the others."""
+    from flashlog_b200 import ops
+    rng = np.random.default_rng(R)
+    rows = 5
+    w = (rng.integers(-2, 6, size=(rows, 2 * R + 1)) / 4.0).astype(np.float32)  # ties, zeros, negatives
+    w[0] = rng.random(2 * R + 1).astype(np.float32)
+    rank = ops.relation_rank(_cuda(w), R).cpu().numpy().reshape(rows, 2, R)
+    for r in range(rows):
+        for d in range(2):
+            x = w[r, d * R:(d + 1) * R]
+            want = np.full(R, -1, dtype=np.int16)
+            pos = np.flatnonzero(x > 0)
+            order = pos[np.lexsort((pos, -x[pos]))]
+            want[order] = np.arange(order.size)
+            assert np.array_equal(rank[r, d], want)
 
 
 @pytest.mark.parametrize("name", ["max_ties", "max_topk200", "max_wot_i", "max_notopk"])
