@@ -961,44 +961,55 @@ __global__ void __launch_bounds__(kExpandWarps * 32, 3) hop_expand_kernel(Expand
 }
 
 // ---------------------------------------------------------------------------
-// Row reduction: one CTA per row, stable radix sort by destination in shared memory.
+// Row reduction: one CTA per row; facts bucketed by destination in shared memory.
 //
 // A row's facts occupy the contiguous slot range
 // [slot_base[row_ptr[r]], slot_base[row_ptr[r + 1]]) in canonical order; slots
-// an entry did not fill hold the destination -1.  A row of at most kTileA
-// slots is sorted in one tile.  A larger row is first histogrammed over
-// kHistBins destination bins and cut into destination ranges of at most
-// kTileB facts, each loaded (in canonical order) and sorted on its own.  A
-// single bin holding more than kTileB facts is summed through dense
-// kDenseW-wide windows.  Keys stay where they were loaded; the sort permutes
-// 16-bit indices with 8-bit LSD passes whose per-warp digit counters keep
-// every pass stable, so facts of one destination stay in canonical order and
-// are summed left to right.
+// an entry did not fill hold the destination -1.  The row's destinations are
+// counted into at most kKBins bins of 2^shift consecutive entities; the bins
+// are cut into chunks of at most kTileK facts.  Each chunk's facts are
+// scattered into their bins in shared memory as keys
+// ((destination - chunk base) << 32 | row-local slot), so the key order is
+// destination order and, within a destination, canonical order.  A fact of
+// a bin of at most kRankBinMax facts finds its sorted position by counting
+// the smaller keys of its bin (an inverse permutation, inv); larger bins are
+// sorted in place by one warp, or by the whole block above kWarpSortMax.
+// Then every thread walks a contiguous range of sorted positions: a block
+// scan of the destination-run heads gives each run its output index, the
+// head sums its run left to right (the reference CPU's order) or picks the
+// MAX winner, and each fact gets its output position.  A single bin of more
+// than kTileK facts is summed through dense kDenseW-wide windows that stream
+// the row in canonical order.
+// Rows of at most kRankSortMax slots are sorted in one tile by rank.
 // ---------------------------------------------------------------------------
 constexpr int kRThreads = 1024;
 constexpr int kRWarps = kRThreads / 32;
 constexpr int kDigits = 256;
-constexpr int kTileA = 16384;  // whole-row tile: key, val, idx[2]
-constexpr int kTileB = 12288;  // destination-range tile: key, val, idx[2], slot
+constexpr int kRankSortMax = 128;  // rows of at most this many slots: one tile, sorted by rank
 constexpr int kTileD = 6144;   // dense-window sub-tile
 constexpr int kDenseW = 4096;  // dense window width (destinations)
-constexpr int kHistBits = 11;
-constexpr int kHistBins = 1 << kHistBits;
 constexpr int kLoadK = 4;  // slots per thread per load step
 constexpr int kLoadStep = kRThreads * kLoadK;
+constexpr int kKBitsMax = 13;
+constexpr int kKBins = 1 << kKBitsMax;  // destination bins per row (at most)
+constexpr int kTileK = 12288;           // facts per chunk
+constexpr int kRankBinMax = 64;        // bins up to this size: each fact ranked within its bin
+constexpr int kWarpSortMax = 1024;      // bins up to this size are sorted by one warp
+constexpr int kBigBinsMax = kTileK / kWarpSortMax + 1;
 
 struct TileA {
-    uint32_t key[kTileA];
-    float val[kTileA];
-    uint16_t idx[2][kTileA];
+    uint32_t key[kRankSortMax];
+    float val[kRankSortMax];
+    uint16_t idx[2][kRankSortMax];
 };
-struct TileB {
-    uint32_t key[kTileB];
-    float val[kTileB];
-    uint16_t idx[2][kTileB];
-    uint32_t slot[kTileB];
+struct TileK {
+    unsigned long long key[kTileK];  // ((destination - chunk base) << 32) | row-local slot
+    float val[kTileK];
+    uint16_t inv[kTileK];            // sorted position -> tile position
+    uint32_t off[kKBins + 1];        // bin starts; the scatter advances off[b] to the bin's end
 };
 struct TileD {
+    uint16_t cnt[kRWarps * kDigits];  // per-warp digit counters of the sub-tile sorts (cleared as uint4)
     uint32_t key[kTileD];
     float val[kTileD];
     uint16_t idx[2][kTileD];
@@ -1013,18 +1024,19 @@ struct TileD {
 struct ReduceSmem {
     union {
         TileA a;
-        TileB b;
+        TileK k;
         TileD d;
     } t;
-    uint16_t cnt[kRWarps * kDigits];  // per-warp digit counters, cnt[warp][digit]
-    uint32_t hist[kHistBins + 1];     // exclusive prefix of the row's destination histogram
-    uint16_t chunk[kHistBins + 1];    // first bin of each destination range
     int64_t scan_scratch[kRWarps + 1];
     float fscratch[kRWarps + 1];
-    int n_chunks;
+    int chunk_end;
+    int big_n;
+    int big_bin[kBigBinsMax];
 };
 static_assert(sizeof(ReduceSmem) <= 227 * 1024, "row reduction shared memory exceeds one CTA's budget");
-static_assert(kTileA <= 65536 && kTileB <= 65536 && kTileD <= 65536, "tile indices are 16-bit");
+static_assert(offsetof(TileD, cnt) == 0, "digit counters are cleared with 16-byte stores");
+static_assert(kTileD <= 65536, "tile indices are 16-bit");
+static_assert(kTileK <= 65536, "tile positions are 16-bit");
 
 struct ReduceArgs {
     const int64_t *row_ptr;      // rows of the (selected) state
@@ -1086,7 +1098,7 @@ __device__ uint16_t *lsd_sort(const uint32_t *key, uint16_t *idx0, uint16_t *idx
     for (int shift = 0; shift < bits; shift += 8) {
         const uint32_t dmask = (bits - shift) >= 8 ? 255u : ((1u << (bits - shift)) - 1u);
         for (int k = threadIdx.x; k < kDigits * kRWarps / 8; k += kRThreads)
-            reinterpret_cast<uint4 *>(sm.cnt)[k] = make_uint4(0u, 0u, 0u, 0u);
+            reinterpret_cast<uint4 *>(sm.t.d.cnt)[k] = make_uint4(0u, 0u, 0u, 0u);
         __syncthreads();
         for (int base = wlo; base < whi; base += 32) {
             const int j = base + lane;
@@ -1095,7 +1107,7 @@ __device__ uint16_t *lsd_sort(const uint32_t *key, uint16_t *idx0, uint16_t *idx
             const unsigned act = __ballot_sync(kFull, valid);
             if (valid) {
                 const unsigned peers = __match_any_sync(act, d);
-                if (lane == __ffs(peers) - 1) sm.cnt[warp * kDigits + d] += static_cast<uint16_t>(__popc(peers));
+                if (lane == __ffs(peers) - 1) sm.t.d.cnt[warp * kDigits + d] += static_cast<uint16_t>(__popc(peers));
             }
         }
         __syncthreads();
@@ -1105,7 +1117,7 @@ __device__ uint16_t *lsd_sort(const uint32_t *key, uint16_t *idx0, uint16_t *idx
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
                 const int q = threadIdx.x * 8 + k;
-                v[k] = sm.cnt[(q & (kRWarps - 1)) * kDigits + (q / kRWarps)];
+                v[k] = sm.t.d.cnt[(q & (kRWarps - 1)) * kDigits + (q / kRWarps)];
                 s += v[k];
             }
             int64_t tot;
@@ -1113,7 +1125,7 @@ __device__ uint16_t *lsd_sort(const uint32_t *key, uint16_t *idx0, uint16_t *idx
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
                 const int q = threadIdx.x * 8 + k;
-                sm.cnt[(q & (kRWarps - 1)) * kDigits + (q / kRWarps)] = static_cast<uint16_t>(run);
+                sm.t.d.cnt[(q & (kRWarps - 1)) * kDigits + (q / kRWarps)] = static_cast<uint16_t>(run);
                 run += v[k];
             }
         }
@@ -1126,10 +1138,10 @@ __device__ uint16_t *lsd_sort(const uint32_t *key, uint16_t *idx0, uint16_t *idx
             const unsigned act = __ballot_sync(kFull, valid);
             if (valid) {
                 const unsigned peers = __match_any_sync(act, d);
-                const uint32_t b = sm.cnt[warp * kDigits + d];
+                const uint32_t b = sm.t.d.cnt[warp * kDigits + d];
                 dst[b + __popc(peers & lanemask_lt())] = id;
                 __syncwarp(act);
-                if (lane == __ffs(peers) - 1) sm.cnt[warp * kDigits + d] = static_cast<uint16_t>(b + __popc(peers));
+                if (lane == __ffs(peers) - 1) sm.t.d.cnt[warp * kDigits + d] = static_cast<uint16_t>(b + __popc(peers));
             }
             __syncwarp();
         }
@@ -1220,7 +1232,6 @@ __device__ float emit_tile(const ReduceArgs &a, ReduceSmem &sm, const uint32_t *
 
 // Stable sort of a tiny tile (n <= kRankSortMax): rank of element i among
 // the (key, position) pairs, one pass.
-constexpr int kRankSortMax = 128;
 __device__ uint16_t *rank_sort(const uint32_t *key, uint16_t *out, int n) {
     for (int i = threadIdx.x; i < n; i += kRThreads) {
         const uint32_t ki = key[i];
@@ -1372,6 +1383,280 @@ __device__ float dense_window(const ReduceArgs &a, ReduceSmem &sm, int64_t s0, i
     return total;
 }
 
+// Bucketed row reduction ---------------------------------------------------
+
+__device__ __forceinline__ void cas_kv(unsigned long long *key, float *val, int i, int l) {
+    const unsigned long long ki = key[i], kl = key[l];
+    if (kl < ki) {
+        key[i] = kl;
+        key[l] = ki;
+        const float t = val[i];
+        val[i] = val[l];
+        val[l] = t;
+    }
+}
+
+// Ascending sort of key[0, n) (val alongside) by the bitonic network whose
+// comparators all put the smaller key first: the first step of each merge
+// compares mirrored positions, the others are half-cleaners.  Comparators
+// reaching n or beyond are skipped: those positions stand for +infinity,
+// which is already in place.  Threads tid, tid + nt, ... take the
+// comparators of a step; sync() separates the steps.
+template <typename Sync>
+__device__ void bitonic_sort_kv(unsigned long long *key, float *val, int n, int tid, int nt, Sync sync) {
+    int m = 1;
+    while (m < n) m <<= 1;
+    for (int k = 2; k <= m; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const int lj = 31 - __clz(j);
+            for (int q = tid; q < (m >> 1); q += nt) {
+                const int i = ((q >> lj) << (lj + 1)) | (q & (j - 1));
+                const int l = j == (k >> 1) ? (i ^ (k - 1)) : (i + j);
+                if (l < n) cas_kv(key, val, i, l);
+            }
+            sync();
+        }
+    }
+}
+
+// Bin b of the current chunk: its tile range.
+__device__ __forceinline__ void bin_range(const TileK &t, int b, int bl, uint32_t base, int *beg, int *n) {
+    const uint32_t e = t.off[b] - base;
+    const uint32_t s = b == bl ? 0u : t.off[b - 1] - base;
+    *beg = static_cast<int>(s);
+    *n = static_cast<int>(e - s);
+}
+
+// Destination histogram of the row over nbins bins of 2^shift entities,
+// turned into bin starts: off[b] = facts in bins < b (off[nbins] = total).
+__device__ void bucket_hist(const ReduceArgs &a, ReduceSmem &sm, int64_t s0, int64_t ns, int shift, int nbins) {
+    TileK &t = sm.t.k;
+    for (int b = threadIdx.x; b <= nbins; b += kRThreads) t.off[b] = 0u;
+    __syncthreads();
+    for (int64_t fb = 0; fb < ns; fb += kLoadStep) {
+        int32_t d[kLoadK];
+#pragma unroll
+        for (int k = 0; k < kLoadK; ++k) {
+            const int64_t j = fb + k * kRThreads + threadIdx.x;
+            d[k] = j < ns ? a.fact_dst[s0 + j] : -1;
+        }
+#pragma unroll
+        for (int k = 0; k < kLoadK; ++k)
+            if (d[k] >= 0 && static_cast<int64_t>(d[k]) < a.E) atomicAdd(&t.off[d[k] >> shift], 1u);
+    }
+    __syncthreads();
+    const int per = (nbins + kRThreads - 1) / kRThreads;  // <= 8
+    const int b0 = threadIdx.x * per;
+    uint32_t v[kKBins / kRThreads];
+    int64_t part = 0;
+#pragma unroll
+    for (int k = 0; k < kKBins / kRThreads; ++k) {
+        v[k] = (k < per && b0 + k < nbins) ? t.off[b0 + k] : 0u;
+        part += v[k];
+    }
+    int64_t tot;
+    int64_t run = block_exclusive_scan<int64_t>(part, sm.scan_scratch, &tot);
+#pragma unroll
+    for (int k = 0; k < kKBins / kRThreads; ++k) {
+        if (k < per && b0 + k < nbins) t.off[b0 + k] = static_cast<uint32_t>(run);
+        run += v[k];
+    }
+    if (threadIdx.x == 0) t.off[nbins] = static_cast<uint32_t>(tot);
+    __syncthreads();
+}
+
+// The row's facts bucketed by destination (see the section comment).
+// Returns this thread's share of the row's output sum; *written counts outputs.
+__device__ float bucket_row(const ReduceArgs &a, ReduceSmem &sm, int64_t s0, int64_t ns, int64_t *written) {
+    TileK &t = sm.t.k;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int kb = 8;  // bins ~ half the slots, 2^8 .. 2^13
+    while (kb < kKBitsMax && (int64_t(1) << (kb + 1)) < ns) ++kb;
+    const int eb = bits_for(a.E);
+    const int shift = eb > kb ? eb - kb : 0;
+    const int nbins = static_cast<int>(((a.E - 1) >> shift) + 1);
+    float local = 0.0f;
+    float dense_sum = 0.0f;
+    bucket_hist(a, sm, s0, ns, shift, nbins);
+    int start = 0;
+    while (start < nbins) {
+        if (threadIdx.x == 0) {
+            // largest e in (start, nbins] with off[e] - off[start] <= kTileK (bins >= start are untouched)
+            const uint32_t base = t.off[start];
+            int lo = start, hi = nbins;
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (t.off[mid] - base <= static_cast<uint32_t>(kTileK)) lo = mid; else hi = mid - 1;
+            }
+            sm.chunk_end = lo;  // == start: bin `start` alone exceeds the tile
+            sm.big_n = 0;
+        }
+        __syncthreads();
+        const int bl = start;
+        const int bh = sm.chunk_end;
+        if (bh == bl) {
+            // one bin above a tile: dense windows over its entities, then the bin starts again
+            const int64_t lo = static_cast<int64_t>(bl) << shift;
+            int64_t hi = static_cast<int64_t>(bl + 1) << shift;
+            if (hi > a.E) hi = a.E;
+            for (int64_t wlo = lo; wlo < hi; wlo += kDenseW) {
+                const int64_t whi = (wlo + kDenseW) < hi ? (wlo + kDenseW) : hi;
+                dense_sum += dense_window(a, sm, s0, ns, wlo, whi, written);
+            }
+            __syncthreads();
+            bucket_hist(a, sm, s0, ns, shift, nbins);
+            start = bl + 1;
+            continue;
+        }
+        const uint32_t base = t.off[bl];
+        const int C = static_cast<int>(t.off[bh] - base);  // off[bh] is not advanced by this chunk
+        const int64_t cbase = static_cast<int64_t>(bl) << shift;
+        __syncthreads();  // every thread has read off[bl], off[bh] before the scatter advances them
+        // scatter the chunk's facts into their bins
+        for (int64_t fb = 0; fb < ns; fb += kLoadStep) {
+            int32_t d[kLoadK];
+#pragma unroll
+            for (int k = 0; k < kLoadK; ++k) {
+                const int64_t j = fb + k * kRThreads + threadIdx.x;
+                d[k] = j < ns ? a.fact_dst[s0 + j] : -1;
+            }
+#pragma unroll
+            for (int k = 0; k < kLoadK; ++k) {
+                if (d[k] < 0 || static_cast<int64_t>(d[k]) >= a.E) continue;
+                const int b = d[k] >> shift;
+                if (b < bl || b >= bh) continue;
+                const int64_t j = fb + k * kRThreads + threadIdx.x;
+                const uint32_t pos = atomicAdd(&t.off[b], 1u) - base;
+                t.key[pos] = (static_cast<unsigned long long>(d[k] - cbase) << 32) | static_cast<uint32_t>(j);
+                t.val[pos] = a.fact_val[s0 + j];
+            }
+        }
+        __syncthreads();
+        // sorted positions: by rank within bins of at most kRankBinMax facts ...
+        for (int p = threadIdx.x; p < C; p += kRThreads) {
+            const unsigned long long k = t.key[p];
+            const int b = bl + static_cast<int>((k >> 32) >> shift);
+            int beg, n;
+            bin_range(t, b, bl, base, &beg, &n);
+            if (n > kRankBinMax) continue;
+            int r = 0;
+            for (int q = beg; q < beg + n; ++q) r += t.key[q] < k ? 1 : 0;
+            t.inv[beg + r] = static_cast<uint16_t>(p);
+        }
+        // ... larger bins sorted in place (one warp each; above kWarpSortMax the whole block)
+        for (int bb = bl + warp * 32; bb < bh; bb += kRThreads) {
+            const int b = bb + lane;
+            int beg = 0, n = 0;
+            if (b < bh) bin_range(t, b, bl, base, &beg, &n);
+            unsigned big = __ballot_sync(kFull, n > kRankBinMax);
+            while (big) {
+                const int src = __ffs(big) - 1;
+                big &= big - 1;
+                const int mb = __shfl_sync(kFull, b, src);
+                const int mbeg = __shfl_sync(kFull, beg, src);
+                const int mn = __shfl_sync(kFull, n, src);
+                if (mn > kWarpSortMax) {
+                    if (lane == 0) {
+                        const int slot = atomicAdd(&sm.big_n, 1);
+                        if (slot < kBigBinsMax) sm.big_bin[slot] = mb;
+                    }
+                    continue;
+                }
+                bitonic_sort_kv(t.key + mbeg, t.val + mbeg, mn, lane, 32, [] { __syncwarp(); });
+                for (int i = lane; i < mn; i += 32) t.inv[mbeg + i] = static_cast<uint16_t>(mbeg + i);
+                __syncwarp();
+            }
+        }
+        __syncthreads();
+        // each holds more than kWarpSortMax of the chunk's <= kTileK facts: at most kBigBinsMax
+        const int nbig = sm.big_n < kBigBinsMax ? sm.big_n : kBigBinsMax;
+        for (int k = 0; k < nbig; ++k) {
+            int beg, n;
+            bin_range(t, sm.big_bin[k], bl, base, &beg, &n);
+            bitonic_sort_kv(t.key + beg, t.val + beg, n, threadIdx.x, kRThreads, [] { __syncthreads(); });
+            for (int i = threadIdx.x; i < n; i += kRThreads) t.inv[beg + i] = static_cast<uint16_t>(beg + i);
+            __syncthreads();
+        }
+        // destination runs over a contiguous range of sorted positions per thread
+        const int64_t wbase = *written;
+        const int per = (C + kRThreads - 1) / kRThreads;
+        const int i0 = threadIdx.x * per < C ? threadIdx.x * per : C;
+        const int i1 = i0 + per < C ? i0 + per : C;
+        uint32_t prev = i0 > 0 ? static_cast<uint32_t>(t.key[t.inv[i0 - 1]] >> 32) : 0xffffffffu;
+        int heads = 0;
+        for (int i = i0; i < i1; ++i) {
+            const uint32_t d = static_cast<uint32_t>(t.key[t.inv[i]] >> 32);
+            heads += d != prev ? 1 : 0;
+            prev = d;
+        }
+        int64_t tot;
+        int64_t o = wbase + block_exclusive_scan<int64_t>(heads, sm.scan_scratch, &tot) - 1;
+        prev = i0 > 0 ? static_cast<uint32_t>(t.key[t.inv[i0 - 1]] >> 32) : 0xffffffffu;
+        for (int i = i0; i < i1; ++i) {
+            const int p = t.inv[i];
+            const unsigned long long k = t.key[p];
+            const uint32_t d = static_cast<uint32_t>(k >> 32);
+            if (d != prev) {
+                ++o;
+                float x = t.val[p];
+                int q = i + 1;
+                if (a.max_mode) {
+                    int bq = i;
+                    unsigned long long bk = 0;
+                    bool have_bk = false;
+                    for (; q < C; ++q) {
+                        const int pq = t.inv[q];
+                        const unsigned long long kq = t.key[pq];
+                        if (static_cast<uint32_t>(kq >> 32) != d) break;
+                        const float v = t.val[pq];
+                        if (max_greater(a.max_mode, v, x)) {
+                            x = v; bq = q; have_bk = false;
+                        } else if (max_equal(a.max_mode, v, x)) {
+                            if (!have_bk) {
+                                bk = max_tie_key(a, s0 + static_cast<uint32_t>(t.key[t.inv[bq]]));
+                                have_bk = true;
+                            }
+                            const unsigned long long tk = max_tie_key(a, s0 + static_cast<uint32_t>(kq));
+                            if (tk < bk) { bq = q; bk = tk; }
+                        }
+                    }
+                    if (a.fact_pos)
+                        for (int r = i; r < q; ++r)
+                            a.fact_pos[s0 + static_cast<uint32_t>(t.key[t.inv[r]])] =
+                                r == bq ? static_cast<int32_t>(o) : -1;
+                } else {
+                    for (; q + 4 <= C; q += 4) {  // loads issued ahead of the dependent adds
+                        const int p0 = t.inv[q], p1 = t.inv[q + 1], p2 = t.inv[q + 2], p3 = t.inv[q + 3];
+                        const uint32_t d0 = static_cast<uint32_t>(t.key[p0] >> 32);
+                        const uint32_t d1 = static_cast<uint32_t>(t.key[p1] >> 32);
+                        const uint32_t d2 = static_cast<uint32_t>(t.key[p2] >> 32);
+                        const uint32_t d3 = static_cast<uint32_t>(t.key[p3] >> 32);
+                        const float v0 = t.val[p0], v1 = t.val[p1], v2 = t.val[p2], v3 = t.val[p3];
+                        if (d0 != d) break;
+                        x += v0;
+                        if (d1 != d) { q += 1; break; }
+                        x += v1;
+                        if (d2 != d) { q += 2; break; }
+                        x += v2;
+                        if (d3 != d) { q += 3; break; }
+                        x += v3;
+                    }
+                    for (; q < C && static_cast<uint32_t>(t.key[t.inv[q]] >> 32) == d; ++q) x += t.val[t.inv[q]];
+                }
+                a.tmp_ent[s0 + o] = static_cast<int32_t>(cbase + d);
+                a.tmp_x[s0 + o] = x;
+                local += x;
+            }
+            prev = d;
+            if (!a.max_mode && a.fact_pos) a.fact_pos[s0 + static_cast<uint32_t>(k)] = static_cast<int32_t>(o);
+        }
+        *written = wbase + tot;
+        __syncthreads();
+        start = bh;
+    }
+    return local + (threadIdx.x == 0 ? dense_sum : 0.0f);
+}
+
 __global__ void __launch_bounds__(kRThreads, 1) row_reduce_kernel(ReduceArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     ReduceSmem &sm = *reinterpret_cast<ReduceSmem *>(smem_raw);
@@ -1390,8 +1675,8 @@ __global__ void __launch_bounds__(kRThreads, 1) row_reduce_kernel(ReduceArgs a) 
     const int64_t ns = s1 - s0;
     int64_t written = 0;
     float rsum = 0.0f;
-    if (ns <= kTileA) {
-        // The whole row fits one tile; unused slots get the key E (sorted last).
+    if (ns <= kRankSortMax) {
+        // A tiny row: one tile sorted by rank; unused slots get the key E (sorted last).
         TileA &t = sm.t.a;
         const uint32_t sentinel = static_cast<uint32_t>(a.E);
         int valid = 0;
@@ -1405,75 +1690,12 @@ __global__ void __launch_bounds__(kRThreads, 1) row_reduce_kernel(ReduceArgs a) 
         }
         const int n = static_cast<int>(block_sum<int64_t>(valid, sm.scan_scratch));
         if (n > 0) {
-            uint16_t *spare;
-            const uint16_t *perm = sort_tile(t.key, t.idx[0], t.idx[1], static_cast<int>(ns), bits_for(a.E + 1), sm,
-                                             &spare);
-            rsum = emit_tile(a, sm, t.key, t.val, perm, spare, n, 0, s0, &written,
+            const uint16_t *perm = rank_sort(t.key, t.idx[1], static_cast<int>(ns));
+            rsum = emit_tile(a, sm, t.key, t.val, perm, t.idx[0], n, 0, s0, &written,
                              [](uint16_t i) { return static_cast<uint32_t>(i); });
         }
     } else {
-        // Destination histogram of the row, then ranges of at most kTileB facts.
-        const int hb = bits_for(a.E);
-        const int hshift = hb > kHistBits ? hb - kHistBits : 0;
-        for (int b = threadIdx.x; b <= kHistBins; b += kRThreads) sm.hist[b] = 0u;
-        __syncthreads();
-        for (int64_t j = threadIdx.x; j < ns; j += kRThreads) {
-            const int32_t d = a.fact_dst[s0 + j];
-            if (d >= 0 && static_cast<int64_t>(d) < a.E) atomicAdd(&sm.hist[d >> hshift], 1u);
-        }
-        __syncthreads();
-        {  // exclusive prefix, 2 bins per thread; hist[kHistBins] = total
-            const uint32_t v0 = sm.hist[2 * threadIdx.x], v1 = sm.hist[2 * threadIdx.x + 1];
-            int64_t tot;
-            const int64_t ex = block_exclusive_scan<int64_t>(v0 + v1, sm.scan_scratch, &tot);
-            sm.hist[2 * threadIdx.x] = static_cast<uint32_t>(ex);
-            sm.hist[2 * threadIdx.x + 1] = static_cast<uint32_t>(ex + v0);
-            if (threadIdx.x == 0) sm.hist[kHistBins] = static_cast<uint32_t>(tot);
-        }
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            int nc = 0, start = 0;
-            while (start < kHistBins) {
-                // largest e in [start, kHistBins] with hist[e] - hist[start] <= kTileB
-                int lo2 = start, hi2 = kHistBins;
-                const uint32_t base = sm.hist[start];
-                while (lo2 < hi2) {
-                    const int mid = (lo2 + hi2 + 1) >> 1;
-                    if (sm.hist[mid] - base <= static_cast<uint32_t>(kTileB)) lo2 = mid; else hi2 = mid - 1;
-                }
-                const int e = lo2 > start ? lo2 : start + 1;  // one bin above a tile: a dense range
-                sm.chunk[nc++] = static_cast<uint16_t>(start);
-                start = e;
-            }
-            sm.chunk[nc] = static_cast<uint16_t>(kHistBins);
-            sm.n_chunks = nc;
-        }
-        __syncthreads();
-        const int nc = sm.n_chunks;
-        for (int c = 0; c < nc; ++c) {
-            const int bl = sm.chunk[c], bh = sm.chunk[c + 1];
-            const uint32_t count = sm.hist[bh] - sm.hist[bl];
-            if (count == 0) continue;
-            const int64_t lo = static_cast<int64_t>(bl) << hshift;
-            int64_t hi = static_cast<int64_t>(bh) << hshift;
-            if (hi > a.E) hi = a.E;
-            if (count <= static_cast<uint32_t>(kTileB)) {
-                TileB &t = sm.t.b;
-                int64_t next;
-                const int n = load_range(a, sm, s0, ns, 0, lo, hi, t.key, t.val, t.slot, t.idx[0], 0, 1 << 30,
-                                         &next);  // count <= kTileB: no early stop
-                uint16_t *spare;
-                const uint16_t *perm = sort_tile(t.key, t.idx[0], t.idx[1], n, bits_for(hi - lo), sm, &spare);
-                rsum += emit_tile(a, sm, t.key, t.val, perm, spare, n, lo, s0, &written,
-                                  [&t](uint16_t i) { return t.slot[i]; });
-            } else {
-                for (int64_t wlo = lo; wlo < hi; wlo += kDenseW) {
-                    const int64_t whi = (wlo + kDenseW) < hi ? (wlo + kDenseW) : hi;
-                    rsum += dense_window(a, sm, s0, ns, wlo, whi, &written);
-                }
-            }
-            __syncthreads();
-        }
+        rsum = block_sum(bucket_row(a, sm, s0, ns, &written), sm.fscratch);
     }
     if (threadIdx.x == 0) { a.out_count[r] = written; a.out_sum[r] = rsum; }
 }

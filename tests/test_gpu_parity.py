@@ -62,6 +62,19 @@ def _w(rng, B, L, n, ties):
     return (e / e.sum(-1, keepdims=True)).astype(np.float32)
 
 
+def _grad_w_exact(ref, g, row, val, w):
+    """grad_w of a recorded oracle forward, accumulated in float64: the
+    library's grad_w is the exactly rounded sum, while the fp32 sequential
+    sum of the reference CPU (and the oracle) drifts with the term count."""
+    f = ref["fact_out"] >= 0
+    c = ref["fact_rel"][f].astype(np.int64)
+    i = ref["fact_entry"][f]
+    terms = g[ref["fact_out"][f]].astype(np.float64) * val[i].astype(np.float64) * ref["fact_m"][f].astype(np.float64)
+    out = np.zeros(w.shape, np.float64).reshape(-1, w.shape[-1])
+    np.add.at(out, (row[i], c), terms)
+    return out.reshape(w.shape)
+
+
 def _sp(row, ent, val, B, L, E, requires_grad=False):
     idx = _cuda(np.stack([row // L, row % L, ent]))
     v = _cuda(val).requires_grad_(requires_grad)
@@ -255,11 +268,15 @@ def test_drum3_engine_matches_reference_golden(fk, g1, golden):
     np.testing.assert_allclose(fv_, d["final_val"], rtol=RTOL, atol=1e-9)
 
 
-def test_large_rows_histogram_and_dense_paths(fk):
-    """Rows above one shared-memory tile, a hub destination (dense window) and a wide entity range."""
+@pytest.mark.parametrize("nh", [2500, 500, 100])
+def test_large_rows_histogram_and_dense_paths(fk, nh):
+    """Rows above one shared-memory tile, a hub destination reached by nh x 6
+    facts (2500: above a tile, dense windows; 500: a bin sorted by the whole
+    block; 100: a bin sorted by one warp in shared memory) and a wide entity
+    range."""
     from flashlog_b200 import ops
     from flashlog_b200.ops import Graph
-    rng = np.random.default_rng(12)
+    rng = np.random.default_rng(12 + nh)
     for E in (60_000, 5_000_000):
         R = 6
         m_rand = 120_000
@@ -267,8 +284,8 @@ def test_large_rows_histogram_and_dense_paths(fk):
         t = rng.integers(0, E, m_rand)
         r = rng.integers(0, R, m_rand)
         hub = E - 17
-        hs = np.repeat(np.arange(2500), R)
-        hr = np.tile(np.arange(R), 2500)
+        hs = np.repeat(np.arange(nh), R)
+        hr = np.tile(np.arange(R), nh)
         tri = np.unique(np.concatenate([np.stack([h, r, t], 1), np.stack([hs, hr, np.full(hs.size, hub)], 1)]), axis=0)
         csr_np = O.build_csr(tri[:, 0], tri[:, 2], tri[:, 1], E)
         tt = _cuda(tri)
@@ -288,15 +305,15 @@ def test_large_rows_histogram_and_dense_paths(fk):
         ref = O.hop_forward(row, ent, val, w, csr_np, R, E, mode=O.MODE_TOPK, mask=mask)
         counts = (fw.out_row_ptr[1:] - fw.out_row_ptr[:-1]).cpu().numpy()
         keys = np.repeat(np.arange(B * L), counts) * E + fw.out_ent.cpu().numpy()
-        assert ref["n_facts"] > 8192 * 2
+        assert ref["n_facts"] > 12288
         assert np.array_equal(keys, ref["out_key"]), E
         assert np.array_equal(fw.out_x.cpu().numpy(), ref["out_val"]), E
         # backward through the dense window as well
         g = rng.standard_normal(keys.size).astype(np.float32)
         gv, gw = ops.hop_backward(fw, rp, _cuda(val), _cuda(w), _cuda(g), normalize=False)
-        rgv, rgw = O.hop_backward(ref, g, row, val, w, R)
+        rgv, _ = O.hop_backward(ref, g, row, val, w, R)
         np.testing.assert_allclose(gv.cpu().numpy(), rgv, rtol=RTOL, atol=1e-5)
-        np.testing.assert_allclose(gw.cpu().numpy(), rgw, rtol=RTOL, atol=1e-5)
+        np.testing.assert_allclose(gw.cpu().numpy(), _grad_w_exact(ref, g, row, val, w), rtol=RTOL, atol=1e-5)
 
 
 def test_sampled_c2_matches_oracle(fk, g1):
@@ -490,19 +507,21 @@ def test_sparse_max_matches_reference_golden(fk, g1, golden, name):
     np.testing.assert_allclose(wt.grad.cpu().numpy(), rgw, rtol=RTOL, atol=1e-6)
 
 
-def test_sparse_max_large_rows(fk):
-    """MAX coalesce through the histogram-cut and dense-window paths (a hub
-    destination with more facts than a tile), against the oracle."""
+@pytest.mark.parametrize("nh", [2500, 500, 100])
+def test_sparse_max_large_rows(fk, nh):
+    """MAX coalesce of rows above a tile with a hub destination of nh x 6
+    facts (dense windows, a block-sorted bin, a warp-sorted bin), against the
+    oracle."""
     from flashlog_b200 import ops
     from flashlog_b200.ops import Graph
-    rng = np.random.default_rng(19)
+    rng = np.random.default_rng(19 + nh)
     E, R = 60_000, 6
     h = rng.integers(0, 30_000, 120_000)
     t = rng.integers(0, E, 120_000)
     r = rng.integers(0, R, 120_000)
     hub = E - 17
-    hs = np.repeat(np.arange(2500), R)
-    hr = np.tile(np.arange(R), 2500)
+    hs = np.repeat(np.arange(nh), R)
+    hr = np.tile(np.arange(R), nh)
     tri = np.unique(np.concatenate([np.stack([h, r, t], 1), np.stack([hs, hr, np.full(hs.size, hub)], 1)]), axis=0)
     csr_np = O.build_csr(tri[:, 0], tri[:, 2], tri[:, 1], E)
     tt = _cuda(tri)
@@ -520,9 +539,9 @@ def test_sparse_max_large_rows(fk):
     assert np.array_equal(fw.out_x.cpu().numpy(), ref["out_val"])
     g = rng.standard_normal(ref["out_key"].size).astype(np.float32)
     gv, gw = ops.hop_backward(fw, rp, _cuda(val), _cuda(w), _cuda(g), normalize=False)
-    rgv, rgw = O.hop_backward(ref, g, row, val, w, R)
+    rgv, _ = O.hop_backward(ref, g, row, val, w, R)
     np.testing.assert_allclose(gv.cpu().numpy(), rgv, rtol=RTOL, atol=1e-5)
-    np.testing.assert_allclose(gw.cpu().numpy(), rgw, rtol=RTOL, atol=1e-5)
+    np.testing.assert_allclose(gw.cpu().numpy(), _grad_w_exact(ref, g, row, val, w), rtol=RTOL, atol=1e-5)
 
 
 @pytest.mark.parametrize("name", ["dense_plain", "dense_topk", "dense_wot_i", "dense_ties"])
