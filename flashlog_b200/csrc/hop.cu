@@ -1032,6 +1032,7 @@ struct ReduceSmem {
     int chunk_end;
     int big_n;
     int big_bin[kBigBinsMax];
+    int32_t win[kTileK / 32];  // per 32 sorted positions: run heads, then their exclusive prefix
 };
 static_assert(sizeof(ReduceSmem) <= 227 * 1024, "row reduction shared memory exceeds one CTA's budget");
 static_assert(offsetof(TileD, cnt) == 0, "digit counters are cleared with 16-byte stores");
@@ -1577,78 +1578,90 @@ __device__ float bucket_row(const ReduceArgs &a, ReduceSmem &sm, int64_t s0, int
             for (int i = threadIdx.x; i < n; i += kRThreads) t.inv[beg + i] = static_cast<uint16_t>(beg + i);
             __syncthreads();
         }
-        // destination runs over a contiguous range of sorted positions per thread
+        // destination runs, 32 sorted positions per warp step: heads counted per
+        // window, one scan over the windows, then outputs and fact positions
         const int64_t wbase = *written;
-        const int per = (C + kRThreads - 1) / kRThreads;
-        const int i0 = threadIdx.x * per < C ? threadIdx.x * per : C;
-        const int i1 = i0 + per < C ? i0 + per : C;
-        uint32_t prev = i0 > 0 ? static_cast<uint32_t>(t.key[t.inv[i0 - 1]] >> 32) : 0xffffffffu;
-        int heads = 0;
-        for (int i = i0; i < i1; ++i) {
-            const uint32_t d = static_cast<uint32_t>(t.key[t.inv[i]] >> 32);
-            heads += d != prev ? 1 : 0;
-            prev = d;
+        const int nwin = (C + 31) >> 5;
+        auto dst_at = [&](int i) { return static_cast<uint32_t>(t.key[t.inv[i]] >> 32); };
+        for (int w = warp; w < nwin; w += kRWarps) {
+            const int i = w * 32 + lane;
+            const uint32_t d = i < C ? dst_at(i) : 0xffffffffu;
+            uint32_t dp = __shfl_up_sync(kFull, d, 1);
+            if (lane == 0) dp = i > 0 ? dst_at(i - 1) : 0xffffffffu;
+            const unsigned hb = __ballot_sync(kFull, i < C && d != dp);
+            if (lane == 0) sm.win[w] = static_cast<int32_t>(__popc(hb));
         }
+        __syncthreads();
         int64_t tot;
-        int64_t o = wbase + block_exclusive_scan<int64_t>(heads, sm.scan_scratch, &tot) - 1;
-        prev = i0 > 0 ? static_cast<uint32_t>(t.key[t.inv[i0 - 1]] >> 32) : 0xffffffffu;
-        for (int i = i0; i < i1; ++i) {
-            const int p = t.inv[i];
-            const unsigned long long k = t.key[p];
-            const uint32_t d = static_cast<uint32_t>(k >> 32);
-            if (d != prev) {
-                ++o;
+        {
+            const int64_t wc = threadIdx.x < nwin ? sm.win[threadIdx.x] : 0;
+            const int64_t wex = block_exclusive_scan<int64_t>(wc, sm.scan_scratch, &tot);
+            if (threadIdx.x < nwin) sm.win[threadIdx.x] = static_cast<int32_t>(wex);
+            __syncthreads();
+        }
+        for (int w = warp; w < nwin; w += kRWarps) {
+            const int i = w * 32 + lane;
+            const bool has = i < C;
+            int p = 0;
+            unsigned long long k = 0;
+            uint32_t d = 0xffffffffu;
+            if (has) { p = t.inv[i]; k = t.key[p]; d = static_cast<uint32_t>(k >> 32); }
+            uint32_t dp = __shfl_up_sync(kFull, d, 1);
+            uint32_t dn = __shfl_down_sync(kFull, d, 1);
+            if (lane == 0) dp = i > 0 && has ? dst_at(i - 1) : 0xffffffffu;
+            if (lane == 31) dn = i + 1 < C ? dst_at(i + 1) : 0xffffffffu;
+            const bool head = has && d != dp;
+            const unsigned hb = __ballot_sync(kFull, head);
+            const int64_t o = wbase + sm.win[w] + __popc(hb & (lanemask_lt() | (1u << lane))) - 1;
+            if (head) {
                 float x = t.val[p];
                 int q = i + 1;
                 if (a.max_mode) {
                     int bq = i;
-                    unsigned long long bk = 0;
-                    bool have_bk = false;
-                    for (; q < C; ++q) {
-                        const int pq = t.inv[q];
-                        const unsigned long long kq = t.key[pq];
-                        if (static_cast<uint32_t>(kq >> 32) != d) break;
-                        const float v = t.val[pq];
-                        if (max_greater(a.max_mode, v, x)) {
-                            x = v; bq = q; have_bk = false;
-                        } else if (max_equal(a.max_mode, v, x)) {
-                            if (!have_bk) {
-                                bk = max_tie_key(a, s0 + static_cast<uint32_t>(t.key[t.inv[bq]]));
-                                have_bk = true;
+                    if (dn == d) {
+                        unsigned long long bk = 0;
+                        bool have_bk = false;
+                        for (; q < C; ++q) {
+                            const int pq = t.inv[q];
+                            const unsigned long long kq = t.key[pq];
+                            if (static_cast<uint32_t>(kq >> 32) != d) break;
+                            const float v = t.val[pq];
+                            if (max_greater(a.max_mode, v, x)) {
+                                x = v; bq = q; have_bk = false;
+                            } else if (max_equal(a.max_mode, v, x)) {
+                                if (!have_bk) {
+                                    bk = max_tie_key(a, s0 + static_cast<uint32_t>(t.key[t.inv[bq]]));
+                                    have_bk = true;
+                                }
+                                const unsigned long long tk = max_tie_key(a, s0 + static_cast<uint32_t>(kq));
+                                if (tk < bk) { bq = q; bk = tk; }
                             }
-                            const unsigned long long tk = max_tie_key(a, s0 + static_cast<uint32_t>(kq));
-                            if (tk < bk) { bq = q; bk = tk; }
                         }
                     }
                     if (a.fact_pos)
                         for (int r = i; r < q; ++r)
                             a.fact_pos[s0 + static_cast<uint32_t>(t.key[t.inv[r]])] =
                                 r == bq ? static_cast<int32_t>(o) : -1;
-                } else {
-                    for (; q + 4 <= C; q += 4) {  // loads issued ahead of the dependent adds
-                        const int p0 = t.inv[q], p1 = t.inv[q + 1], p2 = t.inv[q + 2], p3 = t.inv[q + 3];
-                        const uint32_t d0 = static_cast<uint32_t>(t.key[p0] >> 32);
-                        const uint32_t d1 = static_cast<uint32_t>(t.key[p1] >> 32);
-                        const uint32_t d2 = static_cast<uint32_t>(t.key[p2] >> 32);
-                        const uint32_t d3 = static_cast<uint32_t>(t.key[p3] >> 32);
-                        const float v0 = t.val[p0], v1 = t.val[p1], v2 = t.val[p2], v3 = t.val[p3];
-                        if (d0 != d) break;
-                        x += v0;
-                        if (d1 != d) { q += 1; break; }
-                        x += v1;
-                        if (d2 != d) { q += 2; break; }
-                        x += v2;
-                        if (d3 != d) { q += 3; break; }
-                        x += v3;
+                } else if (dn == d) {
+                    for (; q + 8 <= C; q += 8) {  // loads issued ahead of the dependent adds
+                        int pq[8];
+                        uint32_t dq[8];
+                        float vq[8];
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) pq[u] = t.inv[q + u];
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) { dq[u] = static_cast<uint32_t>(t.key[pq[u]] >> 32); vq[u] = t.val[pq[u]]; }
+                        int u = 0;
+                        for (; u < 8 && dq[u] == d; ++u) x += vq[u];
+                        if (u < 8) { q += u; break; }
                     }
-                    for (; q < C && static_cast<uint32_t>(t.key[t.inv[q]] >> 32) == d; ++q) x += t.val[t.inv[q]];
+                    for (; q < C && dst_at(q) == d; ++q) x += t.val[t.inv[q]];
                 }
                 a.tmp_ent[s0 + o] = static_cast<int32_t>(cbase + d);
                 a.tmp_x[s0 + o] = x;
                 local += x;
             }
-            prev = d;
-            if (!a.max_mode && a.fact_pos) a.fact_pos[s0 + static_cast<uint32_t>(k)] = static_cast<int32_t>(o);
+            if (has && !a.max_mode && a.fact_pos) a.fact_pos[s0 + static_cast<uint32_t>(k)] = static_cast<int32_t>(o);
         }
         *written = wbase + tot;
         __syncthreads();
