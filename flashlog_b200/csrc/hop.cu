@@ -993,7 +993,8 @@ constexpr int kLoadStep = kRThreads * kLoadK;
 constexpr int kKBitsMax = 13;
 constexpr int kKBins = 1 << kKBitsMax;  // destination bins per row (at most)
 constexpr int kTileK = 12288;           // facts per chunk
-constexpr int kRankBinMax = 64;        // bins up to this size: each fact ranked within its bin
+constexpr int kRankBinMax = 32;        // bins up to this size: each fact ranked within its bin
+constexpr int kMultiPairs = 2 * kRThreads;  // comparator pairs of the block-wide sort of the larger bins
 constexpr int kWarpSortMax = 1024;      // bins up to this size are sorted by one warp
 constexpr int kBigBinsMax = kTileK / kWarpSortMax + 1;
 
@@ -1033,7 +1034,13 @@ struct ReduceSmem {
     int big_n;
     int big_bin[kBigBinsMax];
     int32_t win[kTileK / 32];  // per 32 sorted positions: run heads, then their exclusive prefix
+    // bins of more than kRankBinMax facts: tile start, size, first comparator pair
+    uint16_t mb_beg[kTileK / (kRankBinMax + 1) + 1];
+    uint16_t mb_n[kTileK / (kRankBinMax + 1) + 1];
+    int32_t mb_pair[kTileK / (kRankBinMax + 1) + 2];
+    int mb_count, mb_mmax;
 };
+static_assert(kTileK / (kRankBinMax + 1) + 1 < kRThreads, "listed bins are scanned one per thread");
 static_assert(sizeof(ReduceSmem) <= 227 * 1024, "row reduction shared memory exceeds one CTA's budget");
 static_assert(offsetof(TileD, cnt) == 0, "digit counters are cleared with 16-byte stores");
 static_assert(kTileD <= 65536, "tile indices are 16-bit");
@@ -1544,8 +1551,82 @@ __device__ float bucket_row(const ReduceArgs &a, ReduceSmem &sm, int64_t s0, int
             for (int q = beg; q < beg + n; ++q) r += t.key[q] < k ? 1 : 0;
             t.inv[beg + r] = static_cast<uint16_t>(p);
         }
-        // ... larger bins sorted in place (one warp each; above kWarpSortMax the whole block)
+        // ... the larger bins listed ...
+        if (threadIdx.x == 0) { sm.mb_count = 0; sm.mb_mmax = 0; }
+        __syncthreads();
         for (int bb = bl + warp * 32; bb < bh; bb += kRThreads) {
+            const int b = bb + lane;
+            int beg = 0, n = 0;
+            if (b < bh) bin_range(t, b, bl, base, &beg, &n);
+            if (n > kRankBinMax) {
+                const int slot = atomicAdd(&sm.mb_count, 1);  // at most kTileK / (kRankBinMax + 1)
+                sm.mb_beg[slot] = static_cast<uint16_t>(beg);
+                sm.mb_n[slot] = static_cast<uint16_t>(n);
+                int m = 1;
+                while (m < n) m <<= 1;
+                atomicMax(&sm.mb_mmax, m);
+            }
+        }
+        __syncthreads();
+        const int nmb = sm.mb_count;
+        {  // first comparator pair of each listed bin (m / 2 pairs each; nmb < kRThreads)
+            int m = 0;
+            if (threadIdx.x < nmb) {
+                m = 1;
+                while (m < sm.mb_n[threadIdx.x]) m <<= 1;
+            }
+            int64_t pairs;
+            const int64_t first = block_exclusive_scan<int64_t>(m >> 1, sm.scan_scratch, &pairs);
+            if (threadIdx.x < nmb) sm.mb_pair[threadIdx.x] = static_cast<int32_t>(first);
+            if (threadIdx.x == 0) sm.mb_pair[nmb] = static_cast<int32_t>(pairs);
+            __syncthreads();
+        }
+        const bool multi = sm.mb_pair[nmb] <= kMultiPairs;
+        if (multi && nmb > 0) {
+            // ... all sorted at once by the block, one bitonic step per barrier: each
+            // thread keeps the (at most two) comparator pairs it owns across the steps
+            int pb[2], pn[2], pq[2], pm[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int g = threadIdx.x + u * kRThreads;
+                pb[u] = 0; pn[u] = 0; pq[u] = -1; pm[u] = 0;
+                if (g < sm.mb_pair[nmb]) {
+                    int lo = 0, hi = nmb - 1;  // last bin whose first pair is <= g
+                    while (lo < hi) {
+                        const int mid = (lo + hi + 1) >> 1;
+                        if (sm.mb_pair[mid] <= g) lo = mid; else hi = mid - 1;
+                    }
+                    pb[u] = sm.mb_beg[lo];
+                    pn[u] = sm.mb_n[lo];
+                    pq[u] = g - sm.mb_pair[lo];
+                    pm[u] = 2 * (sm.mb_pair[lo + 1] - sm.mb_pair[lo]);
+                }
+            }
+            const int mmax = sm.mb_mmax;
+            for (int k = 2; k <= mmax; k <<= 1) {
+                for (int j = k >> 1; j > 0; j >>= 1) {
+                    const int lj = 31 - __clz(j);
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        if (pq[u] < 0 || k > pm[u]) continue;  // that bin is sorted after its own stages
+                        const int q = pq[u];
+                        const int i = ((q >> lj) << (lj + 1)) | (q & (j - 1));
+                        const int l = j == (k >> 1) ? (i ^ (k - 1)) : (i + j);
+                        if (l < pn[u]) cas_kv(t.key + pb[u], t.val + pb[u], i, l);
+                    }
+                    __syncthreads();
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                if (pq[u] < 0) continue;
+                const int i0 = 2 * pq[u];
+                if (i0 < pn[u]) t.inv[pb[u] + i0] = static_cast<uint16_t>(pb[u] + i0);
+                if (i0 + 1 < pn[u]) t.inv[pb[u] + i0 + 1] = static_cast<uint16_t>(pb[u] + i0 + 1);
+            }
+        }
+        // (when they hold too many pairs: one warp per bin, above kWarpSortMax the whole block)
+        for (int bb = bl + warp * 32; bb < bh && !multi; bb += kRThreads) {
             const int b = bb + lane;
             int beg = 0, n = 0;
             if (b < bh) bin_range(t, b, bl, base, &beg, &n);

@@ -507,6 +507,47 @@ def test_sparse_max_matches_reference_golden(fk, g1, golden, name):
     np.testing.assert_allclose(wt.grad.cpu().numpy(), rgw, rtol=RTOL, atol=1e-6)
 
 
+@pytest.mark.parametrize("reduce", ["sum", "max"])
+def test_rows_of_many_duplicates(fk, reduce):
+    """A row of ~100k facts over 2000 destinations (about 50 facts each):
+    every destination bin is above the per-fact rank size, together above one
+    block-wide sort, so they are sorted one warp per bin; against the oracle."""
+    from flashlog_b200 import ops
+    from flashlog_b200.ops import Graph
+    rng = np.random.default_rng(31 if reduce == "sum" else 32)
+    E, R = 2000, 4
+    h = rng.integers(0, E, 110_000)
+    t = rng.integers(0, E, 110_000)
+    r = rng.integers(0, R, 110_000)
+    tri = np.unique(np.stack([h, r, t], 1), axis=0)
+    csr_np = O.build_csr(tri[:, 0], tri[:, 2], tri[:, 1], E)
+    tt = _cuda(tri)
+    csr = fk.build_csr_structure(tt[:, 0], tt[:, 2], tt[:, 1], E)
+    ent = np.arange(E, dtype=np.int64)
+    row = np.zeros(E, np.int64)
+    val = ((rng.integers(1, 4, E) / 4.0) if reduce == "max" else rng.random(E)).astype(np.float32)
+    w = _w(rng, 1, 1, 2 * R + 1, reduce == "max")
+    mask = (rng.random(tri.shape[0]) > 0.05).astype(np.uint8)
+    rp, en, _ = ops.coo_to_rows(_cuda(row), _cuda(row * 0), _cuda(ent), 1, 1, E)
+    fw = ops.hop_forward(rp, en, _cuda(val), _cuda(w), Graph.of(csr), R, 1 << 62, 1, mask_triple=_cuda(mask),
+                         reduce=reduce)
+    if reduce == "max":
+        ref = O.hop_forward_max(row, ent, val, w, csr_np, R, E, mask=mask)
+        assert np.array_equal(fw.out_ent.cpu().numpy().astype(np.int64), ref["out_key"] % E)
+    else:
+        ref = O.hop_forward(row, ent, val, w, csr_np, R, E, mode=O.MODE_TOPK, mask=mask)
+        counts = (fw.out_row_ptr[1:] - fw.out_row_ptr[:-1]).cpu().numpy()
+        keys = np.repeat(np.arange(1), counts) * E + fw.out_ent.cpu().numpy()
+        assert np.array_equal(keys, ref["out_key"])
+    assert ref["n_facts"] > 100_000
+    assert np.array_equal(fw.out_x.cpu().numpy(), ref["out_val"])
+    g = rng.standard_normal(ref["out_key"].size).astype(np.float32)
+    gv, gw = ops.hop_backward(fw, rp, _cuda(val), _cuda(w), _cuda(g), normalize=False)
+    rgv, _ = O.hop_backward(ref, g, row, val, w, R)
+    np.testing.assert_allclose(gv.cpu().numpy(), rgv, rtol=RTOL, atol=1e-5)
+    np.testing.assert_allclose(gw.cpu().numpy(), _grad_w_exact(ref, g, row, val, w), rtol=RTOL, atol=1e-5)
+
+
 @pytest.mark.parametrize("nh", [2500, 500, 100])
 def test_sparse_max_large_rows(fk, nh):
     """MAX coalesce of rows above a tile with a hub destination of nh x 6
