@@ -2016,12 +2016,76 @@ __global__ void __launch_bounds__(256) normalize_backward_kernel(const int64_t *
     for (int64_t i = a0 + threadIdx.x; i < a1; i += 256) gx[i] = g[i] / d - corr;
 }
 
+// rel_rank for R <= 1024: one warp per (row, direction).  The 1024 keys
+// (padded with the largest key) sit 32 per lane in registers, position
+// lane * 32 + e; the bitonic network's steps below 32 compare inside a lane,
+// the wider ones across lanes by shuffles: no shared memory, no barriers.
+__global__ void __launch_bounds__(256) rel_rank_warp_kernel(const float *w, int64_t n, int64_t R, int64_t pairs,
+                                                            uint16_t *rank) {
+    __shared__ uint16_t staged[8][1024];  // the warp's ranks, written out coalesced
+    const int lane = threadIdx.x & 31;
+    const int64_t rd = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+    if (rd >= pairs) return;
+    const int64_t row = rd >> 1, dir = rd & 1;
+    const float *wd = w + row * n + dir * R;
+    uint16_t *rk = rank + rd * R;
+    uint16_t *srk = staged[threadIdx.x >> 5];
+    unsigned long long x[32];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+        const int j = e * 32 + lane;  // any placement: the network sorts all positions
+        unsigned long long k = ~0ull;
+        if (j < R) {
+            const float v = wd[j];
+            if (v > 0.0f)
+                k = (static_cast<unsigned long long>(0xffffffffu - __float_as_uint(v)) << 32) | static_cast<unsigned>(j);
+            else
+                srk[j] = static_cast<uint16_t>(kNoRank);
+        }
+        x[e] = k;
+    }
+#pragma unroll
+    for (int k = 2; k <= 1024; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            if (j >= 32) {
+                const int pl = j >> 5;
+                const bool lower = (lane & pl) == 0;
+                const bool up = ((lane << 5) & k) == 0;
+                const bool keep_min = lower == up;
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    const unsigned long long y = __shfl_xor_sync(kFull, x[e], pl);
+                    x[e] = keep_min ? (y < x[e] ? y : x[e]) : (y > x[e] ? y : x[e]);
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    if (e & j) continue;
+                    const int f = e | j;
+                    const bool up = (((lane << 5) | e) & k) == 0;
+                    const unsigned long long lo = x[e], hi = x[f];
+                    const bool swap = up ? (lo > hi) : (lo < hi);
+                    x[e] = swap ? hi : lo;
+                    x[f] = swap ? lo : hi;
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < 32; ++e)
+        if (x[e] != ~0ull) srk[x[e] & 0xffffu] = static_cast<uint16_t>((lane << 5) | e);
+    __syncwarp();
+    for (int j = lane; j < R; j += 32) rk[j] = srk[j];
+}
+
 // Per (row, direction): rank[j] = the position of relation j in the order
 // (w[row, dir * R + j] descending, j ascending) of the relations with w > 0,
 // kNoRank for the others; by a bitonic sort of 64-bit keys in shared memory.
 // One CTA per (row, direction).
 __global__ void __launch_bounds__(1024) rel_rank_kernel(const float *w, int64_t n, int64_t R, int P, uint16_t *rank) {
     extern __shared__ __align__(16) unsigned long long keys[];
+    uint16_t *srk = reinterpret_cast<uint16_t *>(keys + P);  // ranks, written out coalesced
     const int64_t rd = blockIdx.x;
     const int64_t row = rd >> 1, dir = rd & 1;
     const float *wd = w + row * n + dir * R;
@@ -2033,7 +2097,7 @@ __global__ void __launch_bounds__(1024) rel_rank_kernel(const float *w, int64_t 
             if (x > 0.0f)
                 k = (static_cast<unsigned long long>(0xffffffffu - __float_as_uint(x)) << 32) | static_cast<unsigned>(j);
             else
-                rk[j] = static_cast<uint16_t>(kNoRank);
+                srk[j] = static_cast<uint16_t>(kNoRank);
         }
         keys[j] = k;
     }
@@ -2073,8 +2137,10 @@ __global__ void __launch_bounds__(1024) rel_rank_kernel(const float *w, int64_t 
     }
     for (int k = threadIdx.x; k < P; k += blockDim.x) {
         const unsigned long long key = keys[k];
-        if (key != ~0ull) rk[key & 0xffffu] = static_cast<uint16_t>(k);
+        if (key != ~0ull) srk[key & 0xffffu] = static_cast<uint16_t>(k);
     }
+    __syncthreads();
+    for (int j = threadIdx.x; j < R; j += blockDim.x) rk[j] = srk[j];
 }
 
 }  // namespace
@@ -2093,14 +2159,17 @@ int relation_rank(const float *w, int64_t rows, int64_t r_size, uint16_t *rank, 
     FL_REQUIRE(r_size > 0 && r_size <= 16384, "relation ranks support 1..16384 relations per direction");
     int P = 1;
     while (P < r_size) P <<= 1;
-    const size_t smem = static_cast<size_t>(P) * sizeof(unsigned long long);
+    const size_t smem = static_cast<size_t>(P) * (sizeof(unsigned long long) + sizeof(uint16_t));
     static bool attr_set = false;
     if (!attr_set) {
         FL_CUDA(cudaFuncSetAttribute(rel_rank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(16384 * sizeof(unsigned long long))));
+                                     static_cast<int>(16384 * (sizeof(unsigned long long) + sizeof(uint16_t)))));
         attr_set = true;
     }
-    if (rows > 0)
+    if (rows > 0 && r_size <= 1024)
+        launch(rel_rank_warp_kernel, static_cast<unsigned>((rows * 2 + 7) / 8), 256, 0, st, w, 2 * r_size + 1, r_size,
+               rows * 2, rank);
+    else if (rows > 0)
         launch(rel_rank_kernel, static_cast<unsigned>(rows * 2), 1024, smem, st, w, 2 * r_size + 1, r_size, P, rank);
     return check_launch("relation_rank");
 }
