@@ -2016,10 +2016,39 @@ __global__ void __launch_bounds__(256) normalize_backward_kernel(const int64_t *
     for (int64_t i = a0 + threadIdx.x; i < a1; i += 256) gx[i] = g[i] / d - corr;
 }
 
+// One step of the in-register bitonic network over 32 keys per lane
+// (position lane * 32 + e): partners J < 32 apart inside the lane.
+template <int J>
+__device__ __forceinline__ void rank_step_lane(unsigned long long (&x)[32], int lane, int k) {
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+        if (e & J) continue;
+        const int f = e | J;
+        const bool up = (((lane << 5) | e) & k) == 0;
+        const unsigned long long lo = x[e], hi = x[f];
+        const bool swap = up ? (lo > hi) : (lo < hi);
+        x[e] = swap ? hi : lo;
+        x[f] = swap ? lo : hi;
+    }
+}
+
+// Partners j >= 32 apart: the same slot of lane ^ (j / 32).
+__device__ __forceinline__ void rank_step_cross(unsigned long long (&x)[32], int lane, int j, int k) {
+    const int pl = j >> 5;
+    const bool lower = (lane & pl) == 0;
+    const bool up = ((lane << 5) & k) == 0;
+    const bool keep_min = lower == up;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+        const unsigned long long y = __shfl_xor_sync(kFull, x[e], pl);
+        x[e] = keep_min ? (y < x[e] ? y : x[e]) : (y > x[e] ? y : x[e]);
+    }
+}
+
 // rel_rank for R <= 1024: one warp per (row, direction).  The 1024 keys
 // (padded with the largest key) sit 32 per lane in registers, position
 // lane * 32 + e; the bitonic network's steps below 32 compare inside a lane,
-// the wider ones across lanes by shuffles: no shared memory, no barriers.
+// the wider ones across lanes by shuffles: no barriers.
 __global__ void __launch_bounds__(256) rel_rank_warp_kernel(const float *w, int64_t n, int64_t R, int64_t pairs,
                                                             uint16_t *rank) {
     __shared__ uint16_t staged[8][1024];  // the warp's ranks, written out coalesced
@@ -2044,31 +2073,19 @@ __global__ void __launch_bounds__(256) rel_rank_warp_kernel(const float *w, int6
         }
         x[e] = k;
     }
-#pragma unroll
+    // the network's loops stay rolled (one copy of each step kind): unrolled
+    // whole it outgrows the instruction cache
+#pragma unroll 1
     for (int k = 2; k <= 1024; k <<= 1) {
-#pragma unroll
+#pragma unroll 1
         for (int j = k >> 1; j > 0; j >>= 1) {
-            if (j >= 32) {
-                const int pl = j >> 5;
-                const bool lower = (lane & pl) == 0;
-                const bool up = ((lane << 5) & k) == 0;
-                const bool keep_min = lower == up;
-#pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const unsigned long long y = __shfl_xor_sync(kFull, x[e], pl);
-                    x[e] = keep_min ? (y < x[e] ? y : x[e]) : (y > x[e] ? y : x[e]);
-                }
-            } else {
-#pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    if (e & j) continue;
-                    const int f = e | j;
-                    const bool up = (((lane << 5) | e) & k) == 0;
-                    const unsigned long long lo = x[e], hi = x[f];
-                    const bool swap = up ? (lo > hi) : (lo < hi);
-                    x[e] = swap ? hi : lo;
-                    x[f] = swap ? lo : hi;
-                }
+            switch (j) {
+                case 1: rank_step_lane<1>(x, lane, k); break;
+                case 2: rank_step_lane<2>(x, lane, k); break;
+                case 4: rank_step_lane<4>(x, lane, k); break;
+                case 8: rank_step_lane<8>(x, lane, k); break;
+                case 16: rank_step_lane<16>(x, lane, k); break;
+                default: rank_step_cross(x, lane, j, k); break;
             }
         }
     }
