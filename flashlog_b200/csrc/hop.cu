@@ -334,7 +334,10 @@ __device__ void rank_select(int64_t budget, int rank_bin, WarpScratch &ws, Membe
 
 // Threshold of one side of one entry, computed by a whole warp.  With `stg`
 // the side's keys and clamped counts are left in stg for the take pass and
-// *staged is set.
+// *staged is set.  kRanked compiles the rank-select paths only (rk given),
+// otherwise the radix select over the weights: each expansion kernel carries
+// one of the two, which keeps it within the instruction cache.
+template <bool kRanked>
 __device__ bool group_threshold(const float *wdir, const uint16_t *rk, int rank_bin, const Side &sd, int64_t g0,
                                 int64_t g1, int64_t budget, WarpScratch &ws, StageBuf *stg, bool *staged, bool *ranked,
                                 uint32_t *thr, int64_t *keep) {
@@ -362,7 +365,7 @@ __device__ bool group_threshold(const float *wdir, const uint16_t *rk, int rank_
         return true;
     }
     const int64_t n = g1 - g0;
-    if (rk != nullptr && budget >= 1 && budget < 65536) {
+    if constexpr (kRanked) {
         // rank select; staged keys are (rank << 16) | relation
         *ranked = true;
         for (int d = lane; d < kRankBins; d += 32) ws.hist[d] = 0u;
@@ -424,7 +427,7 @@ __device__ bool group_threshold(const float *wdir, const uint16_t *rk, int rank_
             }
         }, thr, keep);
         return true;
-    }
+    } else {
     if (stg != nullptr && n <= kStage && budget < 65536) {
         int64_t total = 0;
         for (int64_t cb = 0; cb < n; cb += 128) {  // four groups per lane: the loads are issued together
@@ -471,6 +474,7 @@ __device__ bool group_threshold(const float *wdir, const uint16_t *rk, int rank_
         group_key(wdir, sd, g0 + j, g1, key, cnt);
     }, thr, keep);
     return true;
+    }
 }
 
 __device__ __forceinline__ double splitmix_phase(int64_t seed, int64_t b, int64_t l, int64_t src, bool inv) {
@@ -532,7 +536,7 @@ __device__ __forceinline__ void emit_groups(const ExpandArgs &a, WarpScratch &ws
 }
 
 // One source entry expanded by a whole warp: ori groups, inv groups, identity.
-template <bool kSampled>
+template <bool kSampled, bool kRanked>
 __device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, StageBuf *stg, int64_t i) {
     const int lane = threadIdx.x & 31;
     const bool skip_nonpos = (a.flags & FL_SKIP_NONPOS_W) != 0;
@@ -602,10 +606,10 @@ __device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, StageBuf
             }
         } else if (skip_nonpos && a.topk < kNoBudget) {
             rk = a.rel_rank != nullptr ? a.rel_rank + (row * 2 + dir) * a.r_size : nullptr;
-            use_thr = group_threshold(wdir, rk, a.rank_bin, sd, g0, g1, a.topk, ws, stg, &staged, &ranked, &thr,
+            use_thr = group_threshold<kRanked>(wdir, rk, a.rank_bin, sd, g0, g1, a.topk, ws, stg, &staged, &ranked, &thr,
                                       &keep_thr);
         }
-        if (!kSampled && staged && ranked) {
+        if (kRanked && staged && ranked) {
             // The taking groups, compacted in group order in place:
             // key = (group offset << 16) | relation, cnt = edges taken.
             const uint32_t last = use_thr ? thr : 0xfffffffeu;
@@ -646,7 +650,7 @@ __device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, StageBuf
             int32_t take;
             int32_t rel = 0;
             float wg = 0.0f;
-            if (!kSampled && staged) {
+            if (!kSampled && !kRanked && staged) {
                 // keys and clamped counts from the staging buffer; global
                 // group data only for groups that take edges
                 const uint32_t key = valid ? stg->key[g - g0] : 0u;
@@ -709,7 +713,7 @@ __device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, StageBuf
                     take = valid ? ws.quota[lane] : 0;
                 } else if (!skip_nonpos) {
                     take = cnt;
-                } else if (ranked) {
+                } else if (kRanked && ranked) {
                     const uint32_t r = valid ? static_cast<uint32_t>(rk[rel]) : kNoRank;
                     take = r == kNoRank ? 0 : (!use_thr || r < thr ? cnt : (r == thr ? static_cast<int32_t>(keep_thr) : 0));
                 } else if (!use_thr) {
@@ -759,7 +763,7 @@ __global__ void __launch_bounds__(kExpandWarps * 32, 2) hop_expand_sampled_kerne
     const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kExpandWarps;
     const int64_t S_live = a.row_ptr[a.rows] < a.S ? a.row_ptr[a.rows] : a.S;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * kExpandWarps + wib; i < S_live; i += nwarps)
-        expand_entry_warp<true>(a, scratch[wib], nullptr, i);
+        expand_entry_warp<true, false>(a, scratch[wib], nullptr, i);
 }
 
 // c2 take of the (at most kTeam) groups of one side held one per team lane:
@@ -877,6 +881,7 @@ __device__ __forceinline__ int64_t team_entry(const ExpandArgs &a, const float *
 
 // Deterministic c2 (and the all-edges path): four entries per warp in 8-lane
 // teams; entries with more than kTeam groups on a side go to the whole warp.
+template <bool kRanked>
 __global__ void __launch_bounds__(kExpandWarps * 32, 3) hop_expand_kernel(ExpandArgs a) {
     __shared__ WarpScratch scratch[kExpandWarps];
     extern __shared__ __align__(16) unsigned char stage_raw[];
@@ -937,7 +942,7 @@ __global__ void __launch_bounds__(kExpandWarps * 32, 3) hop_expand_kernel(Expand
         while (big) {
             const int t = (__ffs(big) - 1) / kTeam;
             big &= big - 1;
-            expand_entry_warp<false>(a, scratch[wib], stage + wib, base + t);
+            expand_entry_warp<false, kRanked>(a, scratch[wib], stage + wib, base + t);
         }
     };
     if (a.work != nullptr) {
@@ -2270,11 +2275,18 @@ int hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *en
         const size_t smem = sizeof(StageBuf) * kExpandWarps;
         static bool attr_set = false;
         if (!attr_set) {
-            FL_CUDA(cudaFuncSetAttribute(hop_expand_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            FL_CUDA(cudaFuncSetAttribute(hop_expand_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem)));
+            FL_CUDA(cudaFuncSetAttribute(hop_expand_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem)));
             attr_set = true;
         }
-        launch(hop_expand_kernel, static_cast<unsigned>(blocks), kExpandWarps * 32, smem, st, a);
+        // the rank select needs the ranks and a budget that fits the 16-bit staged counts
+        const bool ranked = a.rel_rank != nullptr && a.topk >= 1 && a.topk < 65536;
+        if (ranked)
+            launch(hop_expand_kernel<true>, static_cast<unsigned>(blocks), kExpandWarps * 32, smem, st, a);
+        else
+            launch(hop_expand_kernel<false>, static_cast<unsigned>(blocks), kExpandWarps * 32, smem, st, a);
     }
     return check_launch("hop_expand");
 }
