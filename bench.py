@@ -540,12 +540,15 @@ def main():
     S, G, U = res["S"], res["G"], res["U"]
     alg_bytes = 24 * S + 14 * G + 5 * res["facts"] + 8 * U
     achieved = alg_bytes / (hop_ms / 1000.0) / 1e9 if hop_ms > 0 else 0.0
+    # DRAM bytes per hop forward: ncu's count on a small case of the same
+    # configuration (profiles/hop_forward_traffic.json), scaled to this run's
+    # hops by their algorithmic bytes
     traffic = None
-    if os.path.exists(PROFILE_TRAFFIC):
+    if os.path.exists(PROFILE_TRAFFIC) and res["n_hops"] > 0:
         try:
             prof = json.load(open(PROFILE_TRAFFIC))
             if prof.get("config") == cfg.index:
-                traffic = prof.get("dram_bytes_per_hop_forward")
+                traffic = float(prof["dram_bytes_per_algorithmic_byte"]) * alg_bytes / res["n_hops"]
         except Exception:
             traffic = None
     cpu = None
@@ -569,6 +572,7 @@ def main():
                              "frac": achieved / peak, "traffic": traffic, "peak_source": peak_src,
                              "kernel": "hop forward (expand + row reduction), rank 0",
                              "algorithmic_bytes": "24*S + 14*G + 5*F + 8*U per hop",
+                             "algorithmic_bytes_per_hop": alg_bytes / max(res["n_hops"], 1),
                              "units": {"S": S, "G": G, "F": res["facts"], "U": U, "hops": res["n_hops"],
                                        "hop_forward_ms": hop_ms}},
                 "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": res["launches"], "clocks": res["clocks"]}
