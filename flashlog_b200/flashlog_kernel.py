@@ -11,6 +11,8 @@ from __future__ import annotations
 import os
 import time
 
+import weakref
+
 import torch
 from torch import autograd
 
@@ -169,6 +171,10 @@ def _align_sparse_grad_to_output(grad, out_indices, Lch, E):
     """Gradient values at the forward's output coordinates (flashlog_kernel.py:360-376)."""
     if not grad.is_sparse:
         return grad[tuple(out_indices)].contiguous()
+    raw = grad._indices()
+    if raw.shape == out_indices.shape and raw.data_ptr() == out_indices.data_ptr():
+        # the gradient sits on the output's own index tensor: values align one to one
+        return grad._values().contiguous()
     grad = grad.coalesce()
     if grad.indices().shape == out_indices.shape and torch.equal(grad.indices(), out_indices):
         return grad.values().contiguous()
@@ -222,10 +228,30 @@ def _select_sources(ctx, row_ptr, ent, val, topk_nodes, sampling):
     return sel_row_ptr, sel_ent, sel_val
 
 
+def _select_sources_async(ctx, row_ptr, ent, val, topk_nodes, rows):
+    """Deterministic c1 without a host sync: outputs keep min(S, rows * c1)
+    entries, their live count stays on the device (row_ptr[rows])."""
+    ctx.pruned = None
+    ctx.n_live = None
+    ctx.original_input_size = val.numel()
+    if topk_nodes is None:
+        return row_ptr, ent, val
+    if topk_nodes < 0:
+        raise ValueError("topk_nodes/c must be nonnegative")
+    if val.numel() <= topk_nodes:
+        return row_ptr, ent, val
+    cap = min(val.numel(), rows * int(topk_nodes))
+    sel_row_ptr, sel_ent, sel_val, src = ops.topc_select(row_ptr, ent, val, int(topk_nodes), sync=False,
+                                                         out_capacity=cap)
+    ctx.pruned = src
+    ctx.n_live = sel_row_ptr[rows:]
+    return sel_row_ptr, sel_ent, sel_val
+
+
 def _restore(ctx, grad):
     if ctx.pruned is None:
         return grad
-    return ops.scatter_grad(grad, ctx.pruned, ctx.original_input_size)
+    return ops.scatter_grad(grad, ctx.pruned, ctx.original_input_size, n_live=getattr(ctx, "n_live", None))
 
 
 def _graph_topk(csr_args):
@@ -258,6 +284,39 @@ def _topk_flags(weight, edge_weight_is_score, sampling, wot_i):
 
 def _check_w(w):
     if not bool(torch.isfinite(w).all()):
+        raise RuntimeError("FlashLog sparse top-k received non-finite attention weights; "
+                           "aborting before edge count/fill to prevent uninitialized indices")
+
+
+# Sparse states returned by the fused operator, keyed by the address of
+# their index storage (with the object kept weakly): their indices were
+# written by the library, in range and coalesced, so the next hop skips the
+# host read of the index check.
+_OWN_OUTPUTS = {}
+
+
+def _mark_own_output(t):
+    idx = t._indices()
+    key = (idx.data_ptr(), tuple(idx.shape))
+    _OWN_OUTPUTS[key] = weakref.ref(t)
+    if len(_OWN_OUTPUTS) > 64:  # drop entries whose tensor is gone
+        for k in [k for k, r in _OWN_OUTPUTS.items() if r() is None]:
+            del _OWN_OUTPUTS[k]
+
+
+def _is_own_output(t):
+    idx = t._indices()
+    r = _OWN_OUTPUTS.get((idx.data_ptr(), tuple(idx.shape)))
+    return r is not None and r() is t
+
+
+def _check_bad_and_w(bad, w):
+    """_check_bad then _check_w with one host read of both device flags."""
+    flags = torch.stack([bad.reshape(-1)[0].to(torch.int32),
+                         (~torch.isfinite(w)).any().to(torch.int32)]).cpu()
+    if int(flags[0]):
+        raise ValueError("sparse state indices are out of range or not coalesced")
+    if int(flags[1]):
         raise RuntimeError("FlashLog sparse top-k received non-finite attention weights; "
                            "aborting before edge count/fill to prevent uninitialized indices")
 
@@ -363,18 +422,29 @@ class _Sparse3DSumNormFused(autograd.Function):
 
     @staticmethod
     def forward(ctx, sp_value, w, sp_batch, sp_level, sp_entity, csr, mask_values, weight, B, L_, E, r_size, wot_i,
-                topk_edges, topk_nodes, sampling, all_edges, masks_csr, eps):
+                topk_edges, topk_nodes, sampling, all_edges, masks_csr, eps, trusted=False):
         _cuda_or_raise(sp_value)
         val = sp_value.detach().to(torch.float32).contiguous()
         graph = Graph.of(csr)
         row_ptr, ent, bad = _rows(sp_batch, sp_level, sp_entity, B, L_, E, graph)
-        _check_bad(bad)
         wf = w.detach().to(torch.float32).contiguous()
         if all_edges:
+            _check_bad(bad)
             ctx.pruned = None
             fw = ops.hop_forward(row_ptr, ent, val, wf, graph, r_size, L.NO_BUDGET, L.FL_WOT_I if wot_i else 0,
                                  mask_csr=masks_csr, eps=eps)
+        elif not sampling:
+            if topk_nodes is not None and topk_nodes < 0:
+                raise ValueError("topk_nodes/c must be nonnegative")
+            if not trusted:
+                _check_bad(bad)
+            row_ptr, ent, val = _select_sources_async(ctx, row_ptr, ent, val, topk_nodes, B * L_)
+            fw = ops.hop_forward(row_ptr, ent, val, wf, graph, r_size, int(topk_edges),
+                                 _topk_flags(weight, False, sampling, wot_i), mask_triple=mask_values,
+                                 edge_weight=None if weight is None else weight.detach(), seed=-1, eps=eps,
+                                 check_w=True)
         else:
+            _check_bad(bad)
             row_ptr, ent, val = _select_sources(ctx, row_ptr, ent, val, topk_nodes, sampling)
             _check_w(wf)
             seed = int(torch.randint(0, 2 ** 63 - 1, ()).item()) if sampling else -1
@@ -394,7 +464,7 @@ class _Sparse3DSumNormFused(autograd.Function):
         g = _align_sparse_grad_to_output(grad_out, ctx.out_indices, ctx.L, ctx.E).to(torch.float32)
         grad_val, grad_w = ops.hop_backward(ctx.fw, row_ptr, val, wf, g, normalize=True)
         grad_val = _restore(ctx, grad_val)
-        return (grad_val, grad_w) + (None,) * 17
+        return (grad_val, grad_w) + (None,) * 18
 
 
 class Sparse3DNormalizeFunction(autograd.Function):
@@ -490,9 +560,13 @@ def vectorized_operation_sparse3d_csr_sum_norm(sp_state, w, csr_struct, mask_val
     if all_edges:
         prepared = _prepared_mask_pair(prepared_masks) if prepared_masks is not None else _prepared_mask_pair(mask_values)
         masks_csr = prepared if prepared is not None else prepare_csr_masks(csr_struct, mask_values, weight)
-    return _Sparse3DSumNormFused.apply(sp_state.values(), w, idx[0], idx[1], idx[2], _csr_parts(csr_struct),
-                                       mask_values, weight, B, L_, E, r_size, wot_i, eff, nodes, sampled,
-                                       all_edges, masks_csr, eps)
+    # a state this operator returned has valid, coalesced indices by construction
+    trusted = _is_own_output(sp_state)
+    out = _Sparse3DSumNormFused.apply(sp_state.values(), w, idx[0], idx[1], idx[2], _csr_parts(csr_struct),
+                                      mask_values, weight, B, L_, E, r_size, wot_i, eff, nodes, sampled,
+                                      all_edges, masks_csr, eps, trusted)
+    _mark_own_output(out)
+    return out
 
 
 def sampled_sparse_propagation(state, w, csr_struct, mask_values, r_size, weight=None, wot_i=False,

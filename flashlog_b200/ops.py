@@ -250,7 +250,7 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
                 mask_triple=None, mask_csr=None, edge_weight=None, seed: int = -1, eps: float = EPS,
                 keep_facts: bool = False, record: bool = True, timing=None, slot_capacity=None,
                 status=None, out_sync: bool = True, vis=None, reduce: str = "sum",
-                max_bits: bool = False, rank_select: bool = True) -> HopForward:
+                max_bits: bool = False, rank_select: bool = True, check_w: bool = False) -> HopForward:
     """Expansion + per-row coalesce-sum + normalization of one hop.
 
     slot_capacity=None sizes the fact buffers exactly (one host sync for the
@@ -267,7 +267,9 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
     fact values by their fp32 bit patterns (the dense MAX order).
     rank_select=False makes the expansion select c2 thresholds by a radix
     select over the groups' weights instead of over relation ranks (same
-    result; the path used when r_size exceeds 16384).
+    result; the path used when r_size exceeds 16384).  check_w raises the
+    non-finite-weights RuntimeError of the top-k operators before the
+    expansion, read in the same host sync as the fact count.
     """
     if reduce not in ("sum", "max"):
         raise ValueError("reduce must be 'sum' or 'max'")
@@ -294,8 +296,17 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
                 and topk_edges < L.NO_BUDGET and not (flags & L.FL_SAMPLED) else None)
     params = hop_params(rows, Lch, n, r_size, graph.E, topk_edges, flags, seed, eps, slot_capacity or 0, status,
                         entry_info, vis, work, rel_rank)
+    nonfinite = (~torch.isfinite(w)).any() if check_w else None
     check(lib().fl_hop_plan(ctypes.byref(params), _p(row_ptr), _p(ent), S, graph.ori, graph.inv, _p(slot_base),
-                            ctypes.byref(total) if sync else None, _p(ws), ws.numel(), _stream()), "hop_plan")
+                            ctypes.byref(total) if (sync and not check_w) else None, _p(ws), ws.numel(), _stream()),
+          "hop_plan")
+    if check_w:
+        # one host read: the fact count and the weights' finiteness
+        got = torch.stack([slot_base[S], nonfinite.to(torch.int64)]).cpu()
+        if int(got[1]):
+            raise RuntimeError("FlashLog sparse top-k received non-finite attention weights; "
+                               "aborting before edge count/fill to prevent uninitialized indices")
+        total.value = int(got[0])
     T = max(total.value, 1) if sync else max(int(slot_capacity), 1)
     if not sync:
         params.slot_capacity = T
@@ -317,7 +328,11 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
             raise ValueError("CSR-ordered masks must have one value per edge")
     if mask_triple is not None:
         mask_triple = mask_triple.reshape(-1)
-        mask_triple = (mask_triple if mask_triple.dtype == torch.uint8 else (mask_triple != 0).to(torch.uint8)).contiguous()
+        if mask_triple.dtype == torch.bool:
+            mask_triple = mask_triple.contiguous().view(torch.uint8)  # one byte, 0 or 1: the same visibility
+        elif mask_triple.dtype != torch.uint8:
+            mask_triple = (mask_triple != 0).to(torch.uint8)
+        mask_triple = mask_triple.contiguous()
         if mask_triple.numel() < M:
             raise ValueError("edge visibility mask must have one entry per triple")
     if edge_weight is not None:

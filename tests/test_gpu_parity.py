@@ -243,6 +243,69 @@ def test_sum_norm_matches_reference_golden(fk, g1, golden, name):
     np.testing.assert_allclose(wt.grad.cpu().numpy(), d[f"{name}_grad_w"], rtol=RTOL, atol=1e-6)
 
 
+def test_sum_norm_errors_and_own_outputs(fk, g1):
+    """Out-of-range state indices raise ValueError and non-finite weights
+    RuntimeError, before any expansion; a state the operator returned chains
+    without the index check and gives the same result as a rebuilt copy."""
+    cfg, train, csr_np, csr = g1
+    E, R = cfg.entities, cfg.relations
+    rng = np.random.default_rng(5)
+    row, ent, val = _state(rng, 2, 3, E, 20)
+    w = _cuda(_w(rng, 2, 3, 2 * R + 1, False))
+    mask = torch.ones(train.shape[0], dtype=torch.bool, device="cuda")
+    sp, _ = _sp(row, ent, val, 2, 3, E)
+    kw = dict(use_topk=True, topk_edges=4, topk_nodes=10)
+    idx = sp.indices().clone()
+    idx[2, -1] = E + 5
+    bad = torch.sparse_coo_tensor(idx, sp.values(), (2, 3, E), is_coalesced=True)
+    with pytest.raises(ValueError):
+        fk.vectorized_operation_sparse3d_csr_sum_norm(bad, w, csr, mask, R, **kw)
+    wbad = w.clone()
+    wbad[1, 2, 3] = float("nan")
+    with pytest.raises(RuntimeError):
+        fk.vectorized_operation_sparse3d_csr_sum_norm(sp, wbad, csr, mask, R, **kw)
+    y = fk.vectorized_operation_sparse3d_csr_sum_norm(sp, w, csr, mask, R, **kw)
+    y2 = fk.vectorized_operation_sparse3d_csr_sum_norm(y, w, csr, mask, R, **kw)
+    copy = torch.sparse_coo_tensor(y.indices().clone(), y.values().clone(), y.shape, is_coalesced=True)
+    y3 = fk.vectorized_operation_sparse3d_csr_sum_norm(copy, w, csr, mask, R, **kw)
+    assert torch.equal(y2.indices(), y3.indices())
+    assert torch.equal(y2.values(), y3.values())
+
+
+def test_drum3_dropin_chain_matches_reference_golden(fk, g1, golden):
+    """Three chained drop-in sum+normalize hops, as the reference model calls
+    them, and the readout loss: outputs, loss and logits gradient against the
+    reference's own run of the same chain.  Covers the c1 selection without a
+    host sync and the gradient handed over on the output's own indices."""
+    d = golden("drum3_config1.npz")
+    cfg, train, csr_np, csr = g1
+    E, R = cfg.entities, cfg.relations
+    logits = _cuda(d["logits"]).requires_grad_(True)
+    heads, tails = _cuda(d["heads"]), _cuda(d["tails"])
+    B, T, L = logits.shape[0], logits.shape[1], logits.shape[2]
+    sb = torch.arange(B, device="cuda").repeat_interleave(L)
+    sl = torch.arange(L, device="cuda").repeat(B)
+    se = heads.repeat_interleave(L)
+    state = torch.sparse_coo_tensor(torch.stack([sb, sl, se]), torch.ones(B * L, device="cuda"), (B, L, E),
+                                    is_coalesced=True)
+    mask = _cuda(d["mask"].astype(bool))
+    for t in range(T):
+        state = fk.vectorized_operation_sparse3d_csr_sum_norm(
+            state, torch.softmax(logits[:, t], dim=-1), csr, mask, R, use_topk=True, topk_edges=int(d["c2"]) // 2,
+            topk_nodes=int(d["c1"]))
+    idx, vals = state.indices(), state.values()
+    hit = idx[2] == tails[idx[0]]
+    score = torch.zeros(B, device="cuda").index_add(0, idx[0][hit], vals[hit])
+    loss = -torch.mean(torch.log(torch.clamp(score, min=1e-7)))
+    np.testing.assert_allclose(loss.item(), float(d["loss"]), rtol=RTOL)
+    loss.backward()
+    np.testing.assert_allclose(logits.grad.cpu().numpy(), d["grad_logits"], rtol=1e-4, atol=1e-6)
+    final = torch.sparse_coo_tensor(torch.stack([idx[0], idx[2]]), vals.detach(), (B, E)).coalesce()
+    fi = final.indices().cpu().numpy()
+    assert np.array_equal(fi[0] * E + fi[1], d["final_key"])
+    np.testing.assert_allclose(final.values().cpu().numpy(), d["final_val"], rtol=RTOL, atol=1e-7)
+
+
 def test_drum3_engine_matches_reference_golden(fk, g1, golden):
     from flashlog_b200 import engine
     from flashlog_b200.ops import Graph
