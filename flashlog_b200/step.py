@@ -41,7 +41,10 @@ class DrumTrainStep:
     table: [2R, T, N, n] attention logits (the parameter); a query with
     relation r uses table[r].  Inputs per step are copied into the static
     tensors heads, tails, rels (i64[Q]) and hide (i64[H], triple ids hidden
-    during the step) with `load`.
+    during the step) with `load`.  With apply_update the step ends with the
+    SGD update table[rels] -= lr * d loss / d logits (only the batch's rows
+    are touched); without it the dense gradient of the table is left in
+    `grad` (for an all-reduce across ranks before the caller's update).
     """
 
     def __init__(self, graph: Graph, r_size: int, Q: int, T: int, N: int, c1, c2: int, table: torch.Tensor,
@@ -56,7 +59,7 @@ class DrumTrainStep:
         self.eps, self.thr, self.lr = eps, thr, lr
         self.apply_update = apply_update
         self.table = table
-        self.grad = torch.zeros_like(table)
+        self.grad = None if apply_update else torch.zeros_like(table)
         rows = Q * N
         self.rows = rows
         csr = graph.csr
@@ -235,10 +238,12 @@ class DrumTrainStep:
             wt = self.w[t][:rows * self.n].view(Q, N, self.n)
             gw = self.grad_w[:rows * self.n].view(Q, N, self.n)
             self.grad_logits[:, t].copy_(wt * (gw - (gw * wt).sum(-1, keepdim=True)))
-        self.grad.zero_()
-        self.grad.index_add_(0, self.rels, self.grad_logits)
         if self.apply_update:
-            self.table.sub_(self.lr * self.grad)
+            # SGD on the rows of the batch's relations only: no dense gradient
+            self.table.index_add_(0, self.rels, self.grad_logits, alpha=-self.lr)
+        else:
+            self.grad.zero_()
+            self.grad.index_add_(0, self.rels, self.grad_logits)
         for k in range(2):
             self.vis[k].index_put_((hid[k],), old[k])
         return self.loss

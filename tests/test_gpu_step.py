@@ -103,3 +103,31 @@ def test_static_step_replays_as_cuda_graph(setup):
         assert float(step.loss) == pytest.approx(l_ref, rel=1e-6)
         np.testing.assert_allclose(step.grad.cpu().numpy(), g_ref.cpu().numpy(), rtol=RTOL, atol=1e-7)
     step.check()
+
+
+def test_step_update_touches_only_the_batch_rows(setup):
+    """apply_update: table[rels] -= lr * gradient, equal to the dense update
+    from the gradient of a step run without it; other rows unchanged."""
+    from flashlog_b200.step import DrumTrainStep
+    from flashlog_b200.synthetic import training_queries
+    cfg, train, graph = setup
+    R, T, N = cfg.relations, 3, 3
+    n = 2 * R + 1
+    dev = torch.device("cuda")
+    d = lambda a: torch.from_numpy(a).to(dev)
+    gen = torch.Generator(device="cpu").manual_seed(11)
+    table = torch.randn(2 * R, T, N, n, generator=gen).cuda()
+    ids, h, r, t = training_queries(train, cfg, step=21)
+    args = (d(h[:16]), d(t[:16]), d(r[:16]), d(ids[:8]))
+    plain = DrumTrainStep(graph, R, 16, T, N, 40, 16, table.clone(), n_hide=8, apply_update=False, lr=0.05)
+    plain.load(*args)
+    plain.run()
+    upd = DrumTrainStep(graph, R, 16, T, N, 40, 16, table.clone(), n_hide=8, apply_update=True, lr=0.05)
+    upd.load(*args)
+    upd.run()
+    torch.cuda.synchronize()
+    want = table - 0.05 * plain.grad
+    np.testing.assert_allclose(upd.table.cpu().numpy(), want.cpu().numpy(), rtol=1e-6, atol=1e-6)
+    untouched = torch.ones(2 * R, dtype=torch.bool, device=dev)
+    untouched[d(r[:16])] = False
+    assert torch.equal(upd.table[untouched], table[untouched])
