@@ -122,6 +122,13 @@ struct StageBuf {
     uint32_t key[kStage];
     uint16_t cnt[kStage];
 };
+// The rank select's staging: each group's relation rank and clamped count
+// (4 KB per warp, so four expansion CTAs fit on an SM).  After the select
+// the taking groups are compacted in place: rank = group offset, cnt = take.
+struct StageRank {
+    uint16_t rank[kStage];
+    uint16_t cnt[kStage];
+};
 
 struct ExpandArgs {
     const int64_t *row_ptr;
@@ -339,7 +346,7 @@ __device__ void rank_select(int64_t budget, int rank_bin, WarpScratch &ws, Membe
 // one of the two, which keeps it within the instruction cache.
 template <bool kRanked>
 __device__ bool group_threshold(const float *wdir, const uint16_t *rk, int rank_bin, const Side &sd, int64_t g0,
-                                int64_t g1, int64_t budget, WarpScratch &ws, StageBuf *stg, bool *staged, bool *ranked,
+                                int64_t g1, int64_t budget, WarpScratch &ws, void *stgv, bool *staged, bool *ranked,
                                 uint32_t *thr, int64_t *keep) {
     const int lane = threadIdx.x & 31;
     *staged = false;
@@ -366,7 +373,8 @@ __device__ bool group_threshold(const float *wdir, const uint16_t *rk, int rank_
     }
     const int64_t n = g1 - g0;
     if constexpr (kRanked) {
-        // rank select; staged keys are (rank << 16) | relation
+        // rank select; staged: each group's rank and clamped count
+        StageRank *stg = static_cast<StageRank *>(stgv);
         *ranked = true;
         for (int d = lane; d < kRankBins; d += 32) ws.hist[d] = 0u;
         __syncwarp();
@@ -390,7 +398,7 @@ __device__ bool group_threshold(const float *wdir, const uint16_t *rk, int rank_
                     const uint32_t cc = r[u] != kNoRank ? c[u] : 0u;
                     const uint32_t cl = cc < cap ? cc : cap;
                     if (j < n) {
-                        stg->key[j] = (r[u] << 16) | static_cast<uint32_t>(rel[u]);
+                        stg->rank[j] = static_cast<uint16_t>(r[u]);
                         stg->cnt[j] = static_cast<uint16_t>(cl);
                         if (cl > 0u) atomicAdd(&ws.hist[r[u] / static_cast<uint32_t>(rank_bin)], cl);
                     }
@@ -402,7 +410,7 @@ __device__ bool group_threshold(const float *wdir, const uint16_t *rk, int rank_
             if (warp_sum(total) <= budget) return false;
             rank_select(budget, rank_bin, ws, [&](uint32_t lo, uint32_t hi, int32_t *quota) {
                 for (int64_t j = lane; j < n; j += 32) {
-                    const uint32_t r = stg->key[j] >> 16;
+                    const uint32_t r = stg->rank[j];
                     if (r >= lo && r < hi) quota[r - lo] = stg->cnt[j];
                 }
             }, thr, keep);
@@ -428,6 +436,7 @@ __device__ bool group_threshold(const float *wdir, const uint16_t *rk, int rank_
         }, thr, keep);
         return true;
     } else {
+    StageBuf *stg = static_cast<StageBuf *>(stgv);
     if (stg != nullptr && n <= kStage && budget < 65536) {
         int64_t total = 0;
         for (int64_t cb = 0; cb < n; cb += 128) {  // four groups per lane: the loads are issued together
@@ -537,7 +546,7 @@ __device__ __forceinline__ void emit_groups(const ExpandArgs &a, WarpScratch &ws
 
 // One source entry expanded by a whole warp: ori groups, inv groups, identity.
 template <bool kSampled, bool kRanked>
-__device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, StageBuf *stg, int64_t i) {
+__device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, void *stgv, int64_t i) {
     const int lane = threadIdx.x & 31;
     const bool skip_nonpos = (a.flags & FL_SKIP_NONPOS_W) != 0;
     const bool drop_masked = (a.flags & FL_DROP_MASKED) != 0;
@@ -606,25 +615,25 @@ __device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, StageBuf
             }
         } else if (skip_nonpos && a.topk < kNoBudget) {
             rk = a.rel_rank != nullptr ? a.rel_rank + (row * 2 + dir) * a.r_size : nullptr;
-            use_thr = group_threshold<kRanked>(wdir, rk, a.rank_bin, sd, g0, g1, a.topk, ws, stg, &staged, &ranked, &thr,
+            use_thr = group_threshold<kRanked>(wdir, rk, a.rank_bin, sd, g0, g1, a.topk, ws, stgv, &staged, &ranked, &thr,
                                       &keep_thr);
         }
         if (kRanked && staged && ranked) {
             // The taking groups, compacted in group order in place:
-            // key = (group offset << 16) | relation, cnt = edges taken.
+            // rank = group offset, cnt = edges taken.
+            StageRank *stg = static_cast<StageRank *>(stgv);
             const uint32_t last = use_thr ? thr : 0xfffffffeu;
             const int n = static_cast<int>(g1 - g0);
             int ntk = 0;
             for (int cb = 0; cb < n; cb += 32) {
                 const int j = cb + lane;
-                const uint32_t key = j < n ? stg->key[j] : (kNoRank << 16);
+                const uint32_t r = j < n ? stg->rank[j] : kNoRank;
                 const int32_t cnt = j < n ? stg->cnt[j] : 0;
-                const uint32_t r = key >> 16;
                 const int32_t take = r == kNoRank || r > last ? 0 : (r < last ? cnt : static_cast<int32_t>(keep_thr));
                 const unsigned b = __ballot_sync(kFull, take > 0);
                 if (take > 0) {  // positions below cb + 32: entries of this chunk are read already
                     const int p = ntk + __popc(b & lanemask_lt());
-                    stg->key[p] = (static_cast<uint32_t>(j) << 16) | (key & 0xffffu);
+                    stg->rank[p] = static_cast<uint16_t>(j);
                     stg->cnt[p] = static_cast<uint16_t>(take);
                 }
                 ntk += __popc(b);
@@ -633,10 +642,10 @@ __device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, StageBuf
             for (int k0 = 0; k0 < ntk; k0 += 32) {
                 const int k = k0 + lane;
                 const bool has = k < ntk;
-                const uint32_t key = has ? stg->key[k] : 0u;
+                const int64_t g = g0 + (has ? stg->rank[k] : 0);
                 const int32_t take = has ? stg->cnt[k] : 0;
-                const int32_t rel = static_cast<int32_t>(key & 0xffffu);
-                const int32_t start = has ? sd.gstart[g0 + (key >> 16)] : 0;
+                const int32_t rel = has ? static_cast<int32_t>(sd.grel[g]) : 0;
+                const int32_t start = has ? sd.gstart[g] : 0;
                 const float wg = has ? wdir[rel] : 0.0f;
                 emit_groups(a, ws, sd, vis, take, start, v * wg, rel + static_cast<int32_t>(off), out, &written,
                             drop_masked, edge_w, edge_score);
@@ -653,6 +662,7 @@ __device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, StageBuf
             if (!kSampled && !kRanked && staged) {
                 // keys and clamped counts from the staging buffer; global
                 // group data only for groups that take edges
+                const StageBuf *stg = static_cast<const StageBuf *>(stgv);
                 const uint32_t key = valid ? stg->key[g - g0] : 0u;
                 const int32_t cnt = valid ? stg->cnt[g - g0] : 0;
                 const bool pos = key != 0u;
@@ -882,10 +892,10 @@ __device__ __forceinline__ int64_t team_entry(const ExpandArgs &a, const float *
 // Deterministic c2 (and the all-edges path): four entries per warp in 8-lane
 // teams; entries with more than kTeam groups on a side go to the whole warp.
 template <bool kRanked>
-__global__ void __launch_bounds__(kExpandWarps * 32, 3) hop_expand_kernel(ExpandArgs a) {
+__global__ void __launch_bounds__(kExpandWarps * 32, kRanked ? 4 : 3) hop_expand_kernel(ExpandArgs a) {
     __shared__ WarpScratch scratch[kExpandWarps];
     extern __shared__ __align__(16) unsigned char stage_raw[];
-    StageBuf *stage = reinterpret_cast<StageBuf *>(stage_raw);
+    constexpr size_t kStageBytes = kRanked ? sizeof(StageRank) : sizeof(StageBuf);
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const int team = lane / kTeam, tl = lane % kTeam, tbase = team * kTeam;
     const unsigned tm = 0xffu << tbase;
@@ -942,7 +952,7 @@ __global__ void __launch_bounds__(kExpandWarps * 32, 3) hop_expand_kernel(Expand
         while (big) {
             const int t = (__ffs(big) - 1) / kTeam;
             big &= big - 1;
-            expand_entry_warp<false, kRanked>(a, scratch[wib], stage + wib, base + t);
+            expand_entry_warp<false, kRanked>(a, scratch[wib], stage_raw + wib * kStageBytes, base + t);
         }
     };
     if (a.work != nullptr) {
@@ -2266,27 +2276,27 @@ int hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *en
         if (blocks > cap_blocks) blocks = cap_blocks;
         launch(hop_expand_sampled_kernel, static_cast<unsigned>(blocks), kExpandWarps * 32, 0, st, a);
     } else {
+        // the rank select needs the ranks and a budget that fits the 16-bit staged counts
+        const bool ranked = a.rel_rank != nullptr && a.topk >= 1 && a.topk < 65536;
         int64_t blocks = (S + 4 * kExpandWarps - 1) / (4 * kExpandWarps);
-        if (a.work != nullptr) {  // resident blocks drain the work queue
+        if (a.work != nullptr) {  // resident blocks drain the work queue (4 per SM with the rank staging)
             FL_CUDA(cudaMemsetAsync(a.work, 0, sizeof(uint32_t), st));
-            cap_blocks = static_cast<int64_t>(sms > 0 ? sms : 148) * per_sm;
+            cap_blocks = static_cast<int64_t>(sms > 0 ? sms : 148) * (ranked ? 4 : per_sm);
         }
         if (blocks > cap_blocks) blocks = cap_blocks;
-        const size_t smem = sizeof(StageBuf) * kExpandWarps;
+        const size_t smem_rank = sizeof(StageRank) * kExpandWarps, smem_radix = sizeof(StageBuf) * kExpandWarps;
         static bool attr_set = false;
         if (!attr_set) {
             FL_CUDA(cudaFuncSetAttribute(hop_expand_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem)));
+                                         static_cast<int>(smem_rank)));
             FL_CUDA(cudaFuncSetAttribute(hop_expand_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem)));
+                                         static_cast<int>(smem_radix)));
             attr_set = true;
         }
-        // the rank select needs the ranks and a budget that fits the 16-bit staged counts
-        const bool ranked = a.rel_rank != nullptr && a.topk >= 1 && a.topk < 65536;
         if (ranked)
-            launch(hop_expand_kernel<true>, static_cast<unsigned>(blocks), kExpandWarps * 32, smem, st, a);
+            launch(hop_expand_kernel<true>, static_cast<unsigned>(blocks), kExpandWarps * 32, smem_rank, st, a);
         else
-            launch(hop_expand_kernel<false>, static_cast<unsigned>(blocks), kExpandWarps * 32, smem, st, a);
+            launch(hop_expand_kernel<false>, static_cast<unsigned>(blocks), kExpandWarps * 32, smem_radix, st, a);
     }
     return check_launch("hop_expand");
 }
