@@ -1857,7 +1857,7 @@ struct BackwardArgs {
     unsigned long long *gacc;  // rows * n * 2 exact accumulators when n > kSmemRel
 };
 
-__global__ void __launch_bounds__(kBThreads) hop_backward_kernel(BackwardArgs a) {
+__global__ void __launch_bounds__(kBThreads, 6) hop_backward_kernel(BackwardArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     unsigned long long *sacc = reinterpret_cast<unsigned long long *>(smem_raw);
     __shared__ float fscratch[kBThreads / 32 + 1];
