@@ -63,7 +63,8 @@ class fl_hop_params(ctypes.Structure):
                 ("flags", ctypes.c_int64), ("sampling_seed", ctypes.c_int64), ("eps", ctypes.c_float),
                 ("slot_capacity", ctypes.c_int64), ("status", ctypes.c_void_p), ("entry_info", ctypes.c_void_p),
                 ("vis_ori", ctypes.c_void_p), ("vis_inv", ctypes.c_void_p), ("work", ctypes.c_void_p),
-                ("rel_rank", ctypes.c_void_p), ("fact_edge", ctypes.c_void_p)]
+                ("rel_rank", ctypes.c_void_p), ("rank_row", ctypes.c_void_p),
+                ("fact_edge", ctypes.c_void_p)]
 
 
 _P = ctypes.c_void_p
@@ -90,7 +91,7 @@ SIGNATURES = {
     "fl_hop_plan": (ctypes.c_int, [_PARAMS, _P, _P, _I64, _SIDE, _SIDE, _P, ctypes.POINTER(ctypes.c_int64), _P,
                                    _SZ, _P]),
     "fl_csr_visibility": (ctypes.c_int, [_P, _I64, _P, _P, _P]),
-    "fl_relation_rank": (ctypes.c_int, [_P, _I64, _I64, _P, _P]),
+    "fl_relation_rank": (ctypes.c_int, [_P, _I64, _I64, _P, _P, _P]),
     "fl_hop_expand": (ctypes.c_int, [_PARAMS, _P, _P, _P, _I64, _P, _SIDE, _SIDE, _P, _P, _P, _P, _P, _P, _P, _P,
                                      _P, _P, _P]),
     "fl_reduce_workspace": (_SZ, [_I64, _I64]),

@@ -181,9 +181,10 @@ int fl_hop_plan(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *e
     return hop_plan(p, row_ptr, ent, S, ori, inv, slot_base, total_slots, ws, ws_bytes, as_stream(stream));
 }
 
-int fl_relation_rank(const float *w, int64_t rows, int64_t r_size, uint16_t *rank, fl_stream_t stream) {
+int fl_relation_rank(const float *w, int64_t rows, int64_t r_size, const int32_t *rank_row, uint16_t *rank,
+                     fl_stream_t stream) {
     FL_REQUIRE(rows >= 0 && (rows == 0 || (w && rank)), "fl_relation_rank: bad arguments");
-    return relation_rank(w, rows, r_size, rank, as_stream(stream));
+    return relation_rank(w, rows, r_size, rank_row, rank, as_stream(stream));
 }
 
 int fl_csr_visibility(const int32_t *order, int64_t m, const uint8_t *mask_triple, uint8_t *vis, fl_stream_t stream) {

@@ -146,6 +146,7 @@ struct ExpandArgs {
     const uint16_t *rel_rank;          // per (row, direction, relation): position in (w desc, id asc) order,
                                        // kNoRank for w <= 0; or null
     int32_t rank_bin;                  // relation ranks per bin of the rank select (ceil(r_size / kRankBins))
+    const int32_t *rank_row;           // per row: the row whose ranks it uses, or null (itself)
     uint32_t *work;                    // work-queue counter (zeroed before the launch) or null
     int32_t *fact_dst;
     float *fact_val;
@@ -614,7 +615,9 @@ __device__ void expand_entry_warp(const ExpandArgs &a, WarpScratch &ws, void *st
                 q_prefix = 0;
             }
         } else if (skip_nonpos && a.topk < kNoBudget) {
-            rk = a.rel_rank != nullptr ? a.rel_rank + (row * 2 + dir) * a.r_size : nullptr;
+            rk = a.rel_rank != nullptr
+                     ? a.rel_rank + ((a.rank_row != nullptr ? a.rank_row[row] : row) * 2 + dir) * a.r_size
+                     : nullptr;
             use_thr = group_threshold<kRanked>(wdir, rk, a.rank_bin, sd, g0, g1, a.topk, ws, stgv, &staged, &ranked, &thr,
                                       &keep_thr);
         }
@@ -2065,12 +2068,13 @@ __device__ __forceinline__ void rank_step_cross(unsigned long long (&x)[32], int
 // lane * 32 + e; the bitonic network's steps below 32 compare inside a lane,
 // the wider ones across lanes by shuffles: no barriers.
 __global__ void __launch_bounds__(256) rel_rank_warp_kernel(const float *w, int64_t n, int64_t R, int64_t pairs,
-                                                            uint16_t *rank) {
+                                                            const int32_t *rank_row, uint16_t *rank) {
     __shared__ uint16_t staged[8][1024];  // the warp's ranks, written out coalesced
     const int lane = threadIdx.x & 31;
     const int64_t rd = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
     if (rd >= pairs) return;
     const int64_t row = rd >> 1, dir = rd & 1;
+    if (rank_row != nullptr && rank_row[row] != row) return;  // shares another row's ranks
     const float *wd = w + row * n + dir * R;
     uint16_t *rk = rank + rd * R;
     uint16_t *srk = staged[threadIdx.x >> 5];
@@ -2115,11 +2119,13 @@ __global__ void __launch_bounds__(256) rel_rank_warp_kernel(const float *w, int6
 // (w[row, dir * R + j] descending, j ascending) of the relations with w > 0,
 // kNoRank for the others; by a bitonic sort of 64-bit keys in shared memory.
 // One CTA per (row, direction).
-__global__ void __launch_bounds__(1024) rel_rank_kernel(const float *w, int64_t n, int64_t R, int P, uint16_t *rank) {
+__global__ void __launch_bounds__(1024) rel_rank_kernel(const float *w, int64_t n, int64_t R, int P,
+                                                        const int32_t *rank_row, uint16_t *rank) {
     extern __shared__ __align__(16) unsigned long long keys[];
     uint16_t *srk = reinterpret_cast<uint16_t *>(keys + P);  // ranks, written out coalesced
     const int64_t rd = blockIdx.x;
     const int64_t row = rd >> 1, dir = rd & 1;
+    if (rank_row != nullptr && rank_row[row] != row) return;  // shares another row's ranks
     const float *wd = w + row * n + dir * R;
     uint16_t *rk = rank + rd * R;
     for (int j = threadIdx.x; j < P; j += blockDim.x) {
@@ -2187,7 +2193,8 @@ static Side make_side(const fl_csr_side &s, const float *mask_csr) {
     return d;
 }
 
-int relation_rank(const float *w, int64_t rows, int64_t r_size, uint16_t *rank, cudaStream_t st) {
+int relation_rank(const float *w, int64_t rows, int64_t r_size, const int32_t *rank_row, uint16_t *rank,
+                  cudaStream_t st) {
     FL_REQUIRE(r_size > 0 && r_size <= 16384, "relation ranks support 1..16384 relations per direction");
     int P = 1;
     while (P < r_size) P <<= 1;
@@ -2200,9 +2207,10 @@ int relation_rank(const float *w, int64_t rows, int64_t r_size, uint16_t *rank, 
     }
     if (rows > 0 && r_size <= 1024)
         launch(rel_rank_warp_kernel, static_cast<unsigned>((rows * 2 + 7) / 8), 256, 0, st, w, 2 * r_size + 1, r_size,
-               rows * 2, rank);
+               rows * 2, rank_row, rank);
     else if (rows > 0)
-        launch(rel_rank_kernel, static_cast<unsigned>(rows * 2), 1024, smem, st, w, 2 * r_size + 1, r_size, P, rank);
+        launch(rel_rank_kernel, static_cast<unsigned>(rows * 2), 1024, smem, st, w, 2 * r_size + 1, r_size, P,
+               rank_row, rank);
     return check_launch("relation_rank");
 }
 
@@ -2264,7 +2272,7 @@ int hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *en
     a.ori = make_side(ori, mask_csr_ori); a.inv = make_side(inv, mask_csr_inv);
     a.mask_triple = mask_triple; a.edge_weight = edge_weight; a.slot_base = slot_base;
     a.vis_ori = p->vis_ori; a.vis_inv = p->vis_inv; a.info = reinterpret_cast<const EntryInfo *>(p->entry_info); a.work = p->work;
-    a.rel_rank = p->rel_rank; a.fact_edge = p->fact_edge;
+    a.rel_rank = p->rel_rank; a.rank_row = p->rank_row; a.fact_edge = p->fact_edge;
     a.rank_bin = static_cast<int32_t>((p->r_size + kRankBins - 1) / kRankBins);
     if (a.rel_rank != nullptr && (a.rank_bin < 1 || a.rank_bin > 32)) a.rel_rank = nullptr;
     a.fact_dst = fact_dst; a.fact_val = fact_val; a.fact_rel = fact_rel; a.fact_m = fact_m; a.entry_count = entry_count;

@@ -210,7 +210,7 @@ def hop_params(rows, Lch, n, r_size, E, topk_edges, flags, seed=-1, eps=EPS, slo
                            None if entry_info is None else entry_info.data_ptr(),
                            None if vis is None else vis[0].data_ptr(), None if vis is None else vis[1].data_ptr(),
                            None if work is None else work.data_ptr(),
-                           None if rel_rank is None else rel_rank.data_ptr())
+                           None if rel_rank is None else rel_rank.data_ptr(), None)
 
 
 def relation_rank(w, r_size: int):
@@ -222,7 +222,7 @@ def relation_rank(w, r_size: int):
         return None
     rows = w.numel() // (2 * r_size + 1)
     rank = torch.empty(max(rows * 2 * r_size, 1), dtype=torch.int16, device=w.device)
-    check(lib().fl_relation_rank(_p(w), rows, r_size, _p(rank), _stream()), "relation_rank")
+    check(lib().fl_relation_rank(_p(w), rows, r_size, None, _p(rank), _stream()), "relation_rank")
     return rank
 
 

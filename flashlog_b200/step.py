@@ -119,6 +119,9 @@ class DrumTrainStep:
         self.entry_info = _buf(L.FL_ENTRY_INFO_INTS * Smax, i32, dev)
         self.use_rank = 0 < r_size <= 16384 and self.topk < L.NO_BUDGET
         self.rel_rank = _buf(rows * 2 * r_size, i16, dev) if self.use_rank else None
+        # rows of queries with one relation have one w: they share the first such row's ranks
+        self.rank_row = _buf(rows, i32, dev) if self.use_rank else None
+        self.chan = torch.arange(N, dtype=torch.int64, device=dev)
         self.fact_dst = _buf(Fmax, i32, dev)
         self.fact_val = _buf(Fmax, f32, dev)
         self.grad_sel = _buf(Smax, f32, dev)
@@ -160,7 +163,8 @@ class DrumTrainStep:
         return L.fl_hop_params(self.rows, self.N, self.n, self.r_size, self.graph.E, int(self.topk), int(flags), -1,
                                float(self.eps), int(self.F[t]), self.status.data_ptr(), self.entry_info.data_ptr(),
                                self.vis[0].data_ptr(), self.vis[1].data_ptr(), self.work.data_ptr(),
-                               self.rel_rank.data_ptr() if self.use_rank else None)
+                               self.rel_rank.data_ptr() if self.use_rank else None,
+                               self.rank_row.data_ptr() if self.use_rank else None)
 
     # ------------------------------------------------------------------
     def run(self):
@@ -174,6 +178,10 @@ class DrumTrainStep:
         for k in range(2):
             self.vis[k].index_fill_(0, hid[k], 0)
         w_all = self.table[self.rels]  # [Q, T, N, n]
+        if self.use_rank:
+            # first query with the same relation (argmax returns the first maximum)
+            first = (self.rels[:, None] == self.rels[None, :]).to(torch.int32).argmax(dim=1)
+            self.rank_row.view(Q, N).copy_(first[:, None] * N + self.chan[None, :])
         self.ent0[:rows].view(Q, N).copy_(self.heads.view(Q, 1).expand(Q, N))
         rp_in, ent_in, val_in = self.rp0, self.ent0, self.val0
         for t in range(T):
@@ -189,7 +197,8 @@ class DrumTrainStep:
                 self.rp_sel[t].copy_(rp_in)
                 self.val_sel[t][:self.S[t]].copy_(val_in[:self.S[t]])
             if self.use_rank:
-                check(lb.fl_relation_rank(_p(self.w[t]), rows, self.r_size, _p(self.rel_rank), st), "relation_rank")
+                check(lb.fl_relation_rank(_p(self.w[t]), rows, self.r_size, _p(self.rank_row), _p(self.rel_rank), st),
+                      "relation_rank")
             params = self._params(t, self.flags)
             check(lb.fl_hop_plan(ctypes.byref(params), _p(rp_s), _p(ent_s), self.S[t], g.ori, g.inv,
                                  _p(self.slot_base[t]), None, ws, wsn, st), "hop_plan")

@@ -81,6 +81,8 @@ typedef struct {
                                        (it zeroes it); NULL: static assignment    */
     const uint16_t *rel_rank;       /* u16[rows * 2 * r_size] or NULL: from
                                        fl_relation_rank of the same w             */
+    const int32_t *rank_row;        /* i32[rows] or NULL: the row whose ranks a
+                                       row uses (rows with equal w share one)     */
     int32_t *fact_edge;             /* i32[slots] or NULL: fl_hop_expand writes each
                                        fact's triple id (order[p]; 0 for identity),
                                        the tie key of fl_row_reduce_max          */
@@ -151,8 +153,11 @@ int fl_hop_plan(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *e
  * relation groups: taking a side's groups in rank order until the budget is
  * spent is the reference's selection (flashlog.cu:26-63), found by a scan
  * over rank bins instead of a radix select over the groups' weights.
+ * rank_row (i32[rows] or NULL): rows with rank_row[r] != r are skipped (they
+ * read the ranks of row rank_row[r], whose w must equal theirs).
  * r_size <= 16384. */
-int fl_relation_rank(const float *w, int64_t rows, int64_t r_size, uint16_t *rank, fl_stream_t stream);
+int fl_relation_rank(const float *w, int64_t rows, int64_t r_size, const int32_t *rank_row, uint16_t *rank,
+                     fl_stream_t stream);
 
 /* CSR-ordered visibility of one side: vis[p] = mask_triple[order[p]] != 0.
  * The gather of prepare_csr_masks / apply_mask_cuda (flashlog_kernel.py:225-255,
