@@ -177,7 +177,6 @@ class DrumTrainStep:
         old = [self.vis[k][hid[k]] for k in range(2)]
         for k in range(2):
             self.vis[k].index_fill_(0, hid[k], 0)
-        w_all = self.table[self.rels]  # [Q, T, N, n]
         if self.use_rank:
             # first query with the same relation (argmax returns the first maximum)
             first = (self.rels[:, None] == self.rels[None, :]).to(torch.int32).argmax(dim=1)
@@ -185,7 +184,9 @@ class DrumTrainStep:
         self.ent0[:rows].view(Q, N).copy_(self.heads.view(Q, 1).expand(Q, N))
         rp_in, ent_in, val_in = self.rp0, self.ent0, self.val0
         for t in range(T):
-            self.w[t][:rows * self.n].view(Q, N, self.n).copy_(torch.softmax(w_all[:, t], dim=-1))
+            # this hop's attention rows [Q, N, n], gathered contiguous, then softmax
+            self.w[t][:rows * self.n].view(Q, N, self.n).copy_(
+                torch.softmax(self.table[:, t].index_select(0, self.rels), dim=-1))
             # c1
             if self.c1 is not None:
                 check(lb.fl_topc_select(_p(rp_in), _p(ent_in), _p(val_in), rows, self.C[t], self.c1, None,
@@ -243,10 +244,10 @@ class DrumTrainStep:
                           "scatter_grad")
                 else:
                     self.g_y[t - 1][:self.S[t]].copy_(self.grad_sel[:self.S[t]])
-            # softmax backward: d logits = w * (g - sum(g * w))
+            # softmax backward, d logits = w * (g - sum(g * w)): torch's own kernel
             wt = self.w[t][:rows * self.n].view(Q, N, self.n)
             gw = self.grad_w[:rows * self.n].view(Q, N, self.n)
-            self.grad_logits[:, t].copy_(wt * (gw - (gw * wt).sum(-1, keepdim=True)))
+            self.grad_logits[:, t].copy_(torch._softmax_backward_data(gw, wt, -1, torch.float32))
         if self.apply_update:
             # SGD on the rows of the batch's relations only: no dense gradient
             self.table.index_add_(0, self.rels, self.grad_logits, alpha=-self.lr)
