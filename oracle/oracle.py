@@ -84,6 +84,34 @@ def build_csr(head, tail, rel, nodes):
     return (*ori[:4], *inv[:4], *ori[4:], *inv[4:])
 
 
+def filter_indices(x, r, relation_size, csr):
+    """Known answers of each query (x, r) from a 16-tuple CSR
+    (src/main.py:196-278): the forward-side group of relation r of x for
+    r < R, the inverse-side group of relation r - R otherwise; a head
+    outside [0, E) has none.  Returns (batch, entity) sorted by (batch,
+    entity) -- the reference's pairs up to order."""
+    x, r = _c(x, np.int64), _c(r, np.int64)
+    R = int(relation_size)
+    E = csr[0].size - 1
+    out_b, out_e = [], []
+    for j in range(x.size):
+        if not (0 <= x[j] < E):
+            continue
+        inv = r[j] >= R
+        rel = r[j] - R if inv else r[j]
+        gptr, grel, gstart, gcount = (csr[12], csr[13], csr[14], csr[15]) if inv else (csr[8], csr[9], csr[10], csr[11])
+        col = csr[5] if inv else csr[1]
+        g0, g1 = int(gptr[x[j]]), int(gptr[x[j] + 1])
+        k = g0 + int(np.searchsorted(grel[g0:g1], rel))
+        if k < g1 and grel[k] == rel:
+            ents = np.sort(col[gstart[k]:gstart[k] + gcount[k]].astype(np.int64))
+            out_b.append(np.full(ents.size, j, np.int64))
+            out_e.append(ents)
+    if not out_b:
+        return np.empty(0, np.int64), np.empty(0, np.int64)
+    return np.concatenate(out_b), np.concatenate(out_e)
+
+
 def topc(row, val, c1):
     """c1 kept-entry indices, or None when no row exceeds c1 nonzeros."""
     row, val = _c(row, np.int64), _c(val, np.float32)

@@ -73,10 +73,20 @@ def _w(rng, B, L, n, ties):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.path.join(os.sep, "root", "reference"))
+    ap.add_argument("--only", choices=["filter"], help="write only this fixture")
     args = ap.parse_args()
     import torch
     torch.set_num_threads(1)
     fk = _import_reference(args.reference)
+    if args.only == "filter":
+        from flashlog_b200.synthetic import CONFIGS, load_or_generate
+        import main as ref_main
+        cfg = CONFIGS[1]
+        train, valid, test = load_or_generate(cfg)
+        csr1 = fk.build_csr_structure(torch.from_numpy(train[:, 0]), torch.from_numpy(train[:, 2]),
+                                      torch.from_numpy(train[:, 1]), cfg.entities)
+        filter_fixture(ref_main, cfg, train, valid, test, tuple(csr1))
+        return
     out = {}
 
     # --- CSR: a tiny graph in full, the config-1 graph by digest -------------
@@ -334,7 +344,32 @@ def main():
                    f"r{ci}_mrr": np.array(mrr), f"r{ci}_hits": hits, f"r{ci}_B": np.array(Bq),
                    f"r{ci}_E": np.array(Eq)})
     np.savez_compressed(os.path.join(HERE, "ranks.npz"), n=np.array(3), **rk)
+
+    filter_fixture(ref_main, cfg, train, valid, test, ctuple)
     print("golden fixtures written to", HERE)
+
+
+def filter_fixture(ref_main, cfg, train, valid, test, ctuple):
+    """Filter indices for filtered ranking (src/main.py:136-318): queries are
+    every test triple in both directions (r and r + R) plus two heads outside
+    the graph; the training-CSR path and the per-split lookup path (train,
+    valid+test) of the reference itself."""
+    import pandas as pd
+    import torch
+    E, R0 = cfg.entities, cfg.relations
+    qx = np.concatenate([test[:, 0], test[:, 2], np.array([E + 3, E + 9])]).astype(np.int64)
+    qr = np.concatenate([test[:, 1], test[:, 1] + R0, np.array([1, R0 + 2])]).astype(np.int64)
+    fb, fe = ref_main.build_filter_indices_csr(torch.from_numpy(qx), torch.from_numpy(qr), R0, ctuple)
+
+    class _Split:
+        kg = pd.DataFrame(train)
+        valid_data = pd.DataFrame(valid)
+        test_data = pd.DataFrame(test)
+        relation_size = R0
+    lk, _, _ = ref_main.create_eval_filter_csr(_Split, E, "cpu")
+    lb, le = ref_main.build_filter_indices_csr(torch.from_numpy(qx), torch.from_numpy(qr), R0, lk)
+    np.savez_compressed(os.path.join(HERE, "filter_config1.npz"), qx=qx, qr=qr, csr_batch=fb.numpy(),
+                        csr_entity=fe.numpy(), lookup_batch=lb.numpy(), lookup_entity=le.numpy())
 
 
 if __name__ == "__main__":

@@ -215,3 +215,14 @@ def test_max_product_matches_reference(golden, ci):
                                final_max=bool(g[f"r{ci}_final_max"]))
     assert np.array_equal(keys, g[f"r{ci}_key"])
     np.testing.assert_allclose(vals, g[f"r{ci}_val"], rtol=1e-5, atol=1e-9)
+
+
+def test_filter_indices_oracle_matches_reference_golden(golden):
+    """The oracle's known-answer lookup against the reference's own
+    build_filter_indices_csr (training-CSR path): the same (query, entity)
+    multiset."""
+    d = golden("filter_config1.npz")
+    cfg, train, csr_np = config1_graph()
+    E = cfg.entities
+    b, e = O.filter_indices(d["qx"], d["qr"], cfg.relations, csr_np)
+    assert np.array_equal(np.sort(b * E + e), np.sort(d["csr_batch"] * E + d["csr_entity"]))
