@@ -465,6 +465,37 @@ def fixed_relation(b, l, e, v, ops_, graph: Graph, r_size: int, B: int, Lr: int)
     return out_row_ptr, out_ent[:u], out_x[:u]
 
 
+def channel_merge(row_ptr, ent, val, B: int, Lch: int, E: int):
+    """Rows (b, l) of a [B, L, E] state merged into rows b: per query the
+    sorted union of its channels' entities with each entity's values summed
+    in channel order (the row reduction with one fact per entry).  Returns
+    (out_row_ptr i64[B+1], out_ent, out_x, position i64[nnz]) where position
+    is each input entry's global output index."""
+    _require_cuda(row_ptr, ent, val)
+    dev = val.device
+    nnz = ent.numel()
+    if row_ptr.numel() != B * Lch + 1:
+        raise ValueError("row_ptr must have B * L + 1 entries")
+    entry_row_ptr = row_ptr[::Lch].contiguous()
+    slot_base = torch.arange(nnz + 1, dtype=torch.int64, device=dev)
+    entry_count = torch.ones(max(nnz, 1), dtype=torch.int32, device=dev)
+    fact_pos = torch.empty(max(nnz, 1), dtype=torch.int32, device=dev)
+    out_row_ptr = torch.empty(B + 1, dtype=torch.int64, device=dev)
+    out_ent = torch.empty(max(nnz, 1), dtype=torch.int32, device=dev)
+    out_x = torch.empty(max(nnz, 1), dtype=torch.float32, device=dev)
+    out_denom = torch.empty(max(B, 1), dtype=torch.float32, device=dev)
+    ws = _ws(lib().fl_reduce_workspace(B, max(nnz, 1)), dev)
+    check(lib().fl_row_reduce(_p(entry_row_ptr), B, int(E), _p(slot_base), _p(entry_count), _p(ent.contiguous()),
+                              _p(val.to(torch.float32).contiguous()), max(nnz, 1), _p(fact_pos), ctypes.c_float(EPS),
+                              _p(out_row_ptr), _p(out_ent), _p(out_x), None, _p(out_denom), None, _p(ws), ws.numel(),
+                              _stream()), "channel_merge")
+    u = int(out_row_ptr[B].item())
+    row_of = torch.repeat_interleave(torch.arange(B, device=dev), entry_row_ptr[1:] - entry_row_ptr[:-1],
+                                     output_size=nnz)
+    position = out_row_ptr[row_of] + fact_pos[:nnz].to(torch.int64)
+    return out_row_ptr, out_ent[:u], out_x[:u], position
+
+
 def filtered_ranks(idx_b, idx_e, values, targets, filter_keys, B: int, E: int, use_eql: bool = False):
     _require_cuda(idx_b, idx_e, values, targets, filter_keys)
     idx_b, idx_e, targets, filter_keys = (x.to(torch.int64).contiguous() for x in (idx_b, idx_e, targets, filter_keys))

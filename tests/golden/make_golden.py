@@ -73,7 +73,7 @@ def _w(rng, B, L, n, ties):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.path.join(os.sep, "root", "reference"))
-    ap.add_argument("--only", choices=["filter"], help="write only this fixture")
+    ap.add_argument("--only", choices=["filter", "readout"], help="write only this fixture")
     args = ap.parse_args()
     import torch
     torch.set_num_threads(1)
@@ -86,6 +86,9 @@ def main():
         csr1 = fk.build_csr_structure(torch.from_numpy(train[:, 0]), torch.from_numpy(train[:, 2]),
                                       torch.from_numpy(train[:, 1]), cfg.entities)
         filter_fixture(ref_main, cfg, train, valid, test, tuple(csr1))
+        return
+    if args.only == "readout":
+        readout_fixture()
         return
     out = {}
 
@@ -370,6 +373,31 @@ def filter_fixture(ref_main, cfg, train, valid, test, ctuple):
     lb, le = ref_main.build_filter_indices_csr(torch.from_numpy(qx), torch.from_numpy(qr), R0, lk)
     np.savez_compressed(os.path.join(HERE, "filter_config1.npz"), qx=qx, qr=qr, csr_batch=fb.numpy(),
                         csr_entity=fe.numpy(), lookup_batch=lb.numpy(), lookup_entity=le.numpy())
+
+
+def readout_fixture():
+    """Channel readouts of the model files (src/model_DRUM_kernel_sp.py:22-28,
+    src/model_mmDRUM_kernel_sp.py:17-32): outputs and the gradient of the
+    values for a fixed upstream gradient, on states with channel ties."""
+    import torch
+    from model_DRUM_kernel_sp import sum_sp_3d
+    from model_mmDRUM_kernel_sp import max_sp_3d
+    out = {}
+    for ci, (B, L, E, per_row, ties) in enumerate([(6, 3, 500, 60, False), (5, 3, 300, 120, True),
+                                                  (4, 2, 2000, 400, True)]):
+        rng = np.random.default_rng(81 + ci)
+        row, ent, val = _state(rng, B, L, E, per_row, zero_frac=0.05, ties=ties)
+        idx = torch.from_numpy(np.stack([row // L, row % L, ent]))
+        for name, fn in (("sum", sum_sp_3d), ("max", max_sp_3d)):
+            v = torch.from_numpy(val.copy()).requires_grad_(True)
+            y = fn(torch.sparse_coo_tensor(idx, v, (B, L, E)).coalesce())
+            g = torch.from_numpy(rng.standard_normal(y.values().numel()).astype(np.float32))
+            (y.values() * g).sum().backward()
+            yi = y.indices().numpy()
+            out.update({f"c{ci}_{name}_key": yi[0] * E + yi[1], f"c{ci}_{name}_val": y.values().detach().numpy(),
+                        f"c{ci}_{name}_g": g.numpy(), f"c{ci}_{name}_grad": v.grad.numpy()})
+        out.update({f"c{ci}_row": row, f"c{ci}_ent": ent, f"c{ci}_val": val, f"c{ci}_shape": np.array([B, L, E])})
+    np.savez_compressed(os.path.join(HERE, "readout.npz"), n=np.array(3), **out)
 
 
 if __name__ == "__main__":

@@ -94,3 +94,26 @@ def test_filter_keys_for_batch(data):
     extra = [bi * E + a for bi, (s, r, t) in enumerate(batch) for a in known.get((s, r), set()) | {t}]
     want = np.unique(np.concatenate([ob * E + oe, np.array(extra, np.int64)]))
     assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("case", [0, 1, 2])
+@pytest.mark.parametrize("name", ["sum", "max"])
+def test_channel_readouts_match_reference_golden(golden, case, name):
+    """sum_sp_3d / max_sp_3d against the model files' own functions: output
+    coordinates exact, values (sums in channel order; maxima exact) and the
+    values' gradient, ties in max split evenly."""
+    from flashlog_b200 import readout
+    d = golden("readout.npz")
+    B, L, E = (int(x) for x in d[f"c{case}_shape"])
+    row, ent, val = d[f"c{case}_row"], d[f"c{case}_ent"], d[f"c{case}_val"]
+    idx = torch.from_numpy(np.stack([row // L, row % L, ent])).cuda()
+    v = torch.from_numpy(val.copy()).cuda().requires_grad_(True)
+    y = getattr(readout, f"{name}_sp_3d")(torch.sparse_coo_tensor(idx, v, (B, L, E), is_coalesced=True))
+    yi = y.indices().cpu().numpy()
+    assert np.array_equal(yi[0] * E + yi[1], d[f"c{case}_{name}_key"])
+    if name == "max":
+        assert np.array_equal(y.values().detach().cpu().numpy(), d[f"c{case}_{name}_val"])
+    else:
+        np.testing.assert_allclose(y.values().detach().cpu().numpy(), d[f"c{case}_{name}_val"], rtol=1e-6, atol=0)
+    (y.values() * torch.from_numpy(d[f"c{case}_{name}_g"]).cuda()).sum().backward()
+    np.testing.assert_allclose(v.grad.cpu().numpy(), d[f"c{case}_{name}_grad"], rtol=1e-6, atol=1e-7)
