@@ -360,6 +360,7 @@ def run_graph_arm(args, cfg, train, csr, rank, world, device):
 def run_e2e_arm(args, cfg, train, csr, data, table, rank, world, device, steps):
     """Same metric through the reference-facing operator API with host buffers."""
     import flashlog_b200.flashlog_kernel as fk
+    from flashlog_b200 import engine, ops
     import torch.distributed as dist
 
     R, T, N, E = cfg.relations, cfg.T, cfg.N, cfg.entities
@@ -387,10 +388,10 @@ def run_e2e_arm(args, cfg, train, csr, data, table, rank, world, device, steps):
             w_t = torch.softmax(w_all[:, hop], dim=-1)
             state = fk.vectorized_operation_sparse3d_csr_sum_norm(state, w_t, csr, mask, R, use_topk=True,
                                                                  topk_edges=cfg.c2 // 2, topk_nodes=cfg.c1)
+        # readout + log loss (src/utils.py:36-47) through the library's readout
         idx = state.indices()
-        hit = idx[2] == t[idx[0]]
-        score = torch.zeros(Q, device=device).index_add(0, idx[0][hit], state.values()[hit])
-        loss = -torch.mean(torch.log(torch.clamp(score, min=1e-7)))
+        rp, ent, _ = ops.coo_to_rows(idx[0], idx[1], idx[2], Q, N, E)
+        loss = engine.readout_loss(rp, ent, state.values(), t, N)
         tab.grad = None
         loss.backward()
         if world > 1:
