@@ -9,6 +9,12 @@ queries with no exchange inside a hop.  Per step:
   * the attention gradients are averaged with one all-reduce;
   * timing is the maximum over ranks, work counts the sum.
 
+Evaluation (filtered ranks, rule-bank scores) shards the queries the same
+way: shard_bounds gives each rank a contiguous query range and
+gather_varlen concatenates the per-rank results in rank order, so the
+gathered ranks equal an unsharded run (a query's rank does not depend on the
+others).
+
 Each function takes the process group (default: the global group); NCCL on
 GPUs, gloo on CPU for tests.
 """
@@ -47,3 +53,52 @@ def max_time_sum_work(ms: float, work: float, device, group=None):
     sm = t.clone()
     dist.all_reduce(sm, op=dist.ReduceOp.SUM, group=group)
     return float(mx[0].item()), float(sm[1].item())
+
+
+def shard_bounds(n: int, rank: int, world: int):
+    """[lo, hi) of this rank's share of n queries: contiguous, sizes differ by at most one."""
+    if world < 1 or not (0 <= rank < world) or n < 0:
+        raise ValueError("bad shard arguments")
+    base, extra = divmod(n, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+def gather_varlen(t: torch.Tensor, group=None) -> torch.Tensor:
+    """Concatenation in rank order of every rank's 1-D tensor t (lengths may differ)."""
+    world = dist.get_world_size(group)
+    if world == 1:
+        return t
+    t = t.contiguous().reshape(-1)
+    n = torch.tensor([t.numel()], dtype=torch.int64, device=t.device)
+    sizes = [torch.empty_like(n) for _ in range(world)]
+    dist.all_gather(sizes, n, group=group)
+    sizes = [int(x.item()) for x in sizes]
+    cap = max(sizes)
+    padded = torch.zeros(cap, dtype=t.dtype, device=t.device)
+    padded[:t.numel()] = t
+    parts = [torch.empty_like(padded) for _ in range(world)]
+    dist.all_gather(parts, padded, group=group)
+    return torch.cat([p[:k] for p, k in zip(parts, sizes)])
+
+
+def sharded_filtered_ranks(idx_b, idx_e, values, targets, filter_keys, B: int, E: int, use_eql: bool = False,
+                           group=None, rank_fn=None):
+    """Filtered ranks of B queries with each rank scoring its query shard
+    (sparse2d_filtered_ranks_cuda on the shard's slice of the scores and of
+    the sorted filter keys), gathered in query order.  The scores are a
+    coalesced [B, E] COO (idx_b sorted); rank_fn defaults to the library's
+    kernel."""
+    if rank_fn is None:
+        from .flashlog_kernel import sparse2d_filtered_ranks_cuda as rank_fn
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    rank = dist.get_rank(group) if dist.is_initialized() else 0
+    lo, hi = shard_bounds(int(B), rank, world)
+    dev = idx_b.device
+    a, b = (int(x) for x in torch.searchsorted(idx_b, torch.tensor([lo, hi], dtype=idx_b.dtype, device=dev)))
+    keys = torch.tensor([lo * int(E), hi * int(E)], dtype=filter_keys.dtype, device=filter_keys.device)
+    ka, kb = (int(x) for x in torch.searchsorted(filter_keys, keys))
+    local = rank_fn(idx_b[a:b] - lo, idx_e[a:b], values[a:b], targets[lo:hi], filter_keys[ka:kb] - lo * int(E),
+                    hi - lo, int(E), use_eql)
+    local = torch.as_tensor(local, device=values.device, dtype=torch.float32)
+    return gather_varlen(local, group) if world > 1 else local

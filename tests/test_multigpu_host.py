@@ -29,7 +29,10 @@ def _worker(rank, world, port, out):
         grad = torch.full((3, 2), float(rank + 1))
         MG.allreduce_mean_(grad)
         ms, work = MG.max_time_sum_work(10.0 + rank, 7 * (rank + 1), torch.device("cpu"))
-        out.put((rank, hidden.tolist(), grad.tolist(), ms, work))
+        # sharded evaluation: 5 queries over 2 ranks, per-query results gathered in rank order
+        lo, hi = MG.shard_bounds(5, rank, world)
+        ranks_all = MG.gather_varlen(torch.arange(lo, hi, dtype=torch.float32) * 10)
+        out.put((rank, hidden.tolist(), grad.tolist(), ms, work, (lo, hi), ranks_all.tolist()))
     finally:
         dist.destroy_process_group()
 
@@ -45,10 +48,12 @@ def test_collectives_on_two_gloo_ranks():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    for rank, hidden, grad, ms, work in res:
+    for rank, hidden, grad, ms, work, bounds, ranks_all in res:
         assert hidden == [0, 1, 2, 3, 100, 101, 102, 103]  # every replica hides the union
         assert grad == [[1.5, 1.5]] * 3                       # mean of the ranks' gradients
         assert ms == 11.0 and work == 21.0                    # max time, summed work
+        assert bounds == ((0, 3) if rank == 0 else (3, 5))    # contiguous shards
+        assert ranks_all == [0.0, 10.0, 20.0, 30.0, 40.0]     # unsharded order
 
 
 def test_single_process_is_identity():
@@ -67,3 +72,59 @@ def test_single_process_is_identity():
         assert MG.max_time_sum_work(3.0, 4, torch.device("cpu")) == (3.0, 4)
     finally:
         dist.destroy_process_group()
+
+
+def test_shard_bounds_cover_every_query_once():
+    from flashlog_b200 import multigpu as MG
+    for n in (0, 1, 7, 64, 1001):
+        for world in (1, 2, 3, 8):
+            spans = [MG.shard_bounds(n, r, world) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == n
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+            sizes = [hi - lo for lo, hi in spans]
+            assert max(sizes) - min(sizes) <= 1
+    with pytest.raises(ValueError):
+        MG.shard_bounds(4, 2, 2)
+
+
+def _rank_worker(rank, world, port, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import numpy as np
+        from flashlog_b200 import multigpu as MG
+        from oracle import oracle as O
+        rng = np.random.default_rng(5)
+        B, E = 9, 40
+        keys = np.unique(rng.integers(0, B * E, 150))
+        vals = (rng.integers(0, 6, keys.size) / 5.0).astype(np.float32)
+        targets = rng.integers(0, E, B)
+        filt = np.unique(rng.integers(0, B * E, 60))
+
+        def oracle_ranks(ib, ie, v, t, fk, b, e, eql):
+            return torch.from_numpy(O.filtered_ranks(ib.numpy(), ie.numpy(), v.numpy(), t.numpy(), fk.numpy(), b, e,
+                                                     eql))
+        got = MG.sharded_filtered_ranks(torch.from_numpy(keys // E), torch.from_numpy(keys % E),
+                                        torch.from_numpy(vals), torch.from_numpy(targets), torch.from_numpy(filt),
+                                        B, E, True, rank_fn=oracle_ranks)
+        want = O.filtered_ranks(keys // E, keys % E, vals, targets, filt, B, E, True)
+        out.put((rank, got.tolist(), want.tolist()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_filtered_ranks_on_two_gloo_ranks():
+    """Each rank ranks its query shard; the gathered ranks equal the unsharded ones."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, got, want in res:
+        assert got == want
