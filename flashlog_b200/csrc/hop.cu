@@ -98,6 +98,7 @@ __global__ void csr_visibility_kernel(const int32_t *order, int64_t m, const uin
 // ---------------------------------------------------------------------------
 constexpr int kExpandWarps = 8;
 constexpr int kTeam = 8;
+constexpr int kTeamMaxSlots = 24;  // entries with more reserved slots go to the whole-warp path
 constexpr int kStage = 1024;  // relation groups of one side staged per warp
 constexpr int kRankBins = 512;  // bins of the rank select (WarpScratch::hist)
 constexpr uint32_t kNoRank = 0xffffu;
@@ -929,7 +930,9 @@ __global__ void __launch_bounds__(kExpandWarps * 32, kRanked ? 4 : 3) hop_expand
                 e.g0o = a.ori.gptr[src]; e.g1o = (a.flags & FL_NO_ORI) ? e.g0o : a.ori.gptr[src + 1];
                 e.g0i = a.inv.gptr[src]; e.g1i = (a.flags & FL_NO_INV) ? e.g0i : a.inv.gptr[src + 1];
             }
-            small = !over && (e.g1o - e.g0o) <= kTeam && (e.g1i - e.g0i) <= kTeam;
+            // few groups and few facts: a team emits kTeam facts per step, so an
+            // entry with many reserved slots is emitted faster by the whole warp
+            small = !over && (e.g1o - e.g0o) <= kTeam && (e.g1i - e.g0i) <= kTeam && end - out <= kTeamMaxSlots;
         }
         if (small) {
             const int64_t row = a.info ? static_cast<int64_t>(e.row) : find_row(a.row_ptr, a.rows, i);
@@ -1011,7 +1014,7 @@ constexpr int kLoadStep = kRThreads * kLoadK;
 constexpr int kKBitsMax = 13;
 constexpr int kKBins = 1 << kKBitsMax;  // destination bins per row (at most)
 constexpr int kTileK = 12288;           // facts per chunk
-constexpr int kRankBinMax = 32;        // bins up to this size: each fact ranked within its bin
+constexpr int kRankBinMax = 64;        // bins up to this size: each fact ranked within its bin
 constexpr int kMultiPairs = 2 * kRThreads;  // comparator pairs of the block-wide sort of the larger bins
 constexpr int kWarpSortMax = 1024;      // bins up to this size are sorted by one warp
 constexpr int kBigBinsMax = kTileK / kWarpSortMax + 1;
