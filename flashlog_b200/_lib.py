@@ -64,7 +64,7 @@ class fl_hop_params(ctypes.Structure):
                 ("slot_capacity", ctypes.c_int64), ("status", ctypes.c_void_p), ("entry_info", ctypes.c_void_p),
                 ("vis_ori", ctypes.c_void_p), ("vis_inv", ctypes.c_void_p), ("work", ctypes.c_void_p),
                 ("rel_rank", ctypes.c_void_p), ("rank_row", ctypes.c_void_p),
-                ("fact_edge", ctypes.c_void_p)]
+                ("row_order", ctypes.c_void_p), ("fact_edge", ctypes.c_void_p)]
 
 
 _P = ctypes.c_void_p
@@ -98,7 +98,7 @@ SIGNATURES = {
     "fl_row_reduce_max": (ctypes.c_int, [_P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _I64, _P, _P, _P, _P,
                                          ctypes.c_int, _P, _P, _SZ, _P]),
     "fl_row_reduce": (ctypes.c_int, [_P, _I64, _I64, _P, _P, _P, _P, _I64, _P, ctypes.c_float, _P, _P, _P, _P, _P,
-                                     _P, _P, _SZ, _P]),
+                                     _P, _P, _P, _SZ, _P]),
     "fl_hop_backward_workspace": (_SZ, [_I64, _I64]),
     "fl_hop_backward": (ctypes.c_int, [_PARAMS, _P, _P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                        _SZ, _P]),

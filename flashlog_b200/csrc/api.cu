@@ -219,9 +219,10 @@ int fl_row_reduce_max(const int64_t *row_ptr, int64_t rows, int64_t E, int64_t r
 int fl_row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *slot_base, const int32_t *entry_count,
                   const int32_t *fact_dst, const float *fact_val, int64_t total_slots, int32_t *fact_pos, float eps,
                   int64_t *out_row_ptr, int32_t *out_ent, float *out_x, float *out_y, float *out_denom,
-                  int32_t *status, void *ws, size_t ws_bytes, fl_stream_t stream) {
+                  int32_t *status, const int32_t *row_order, void *ws, size_t ws_bytes, fl_stream_t stream) {
     return row_reduce(row_ptr, rows, E, slot_base, entry_count, fact_dst, fact_val, total_slots, fact_pos, eps,
-                      out_row_ptr, out_ent, out_x, out_y, out_denom, status, ws, ws_bytes, as_stream(stream));
+                      out_row_ptr, out_ent, out_x, out_y, out_denom, status, row_order, ws, ws_bytes,
+                      as_stream(stream));
 }
 
 size_t fl_hop_backward_workspace(int64_t rows, int64_t n) { return hop_backward_workspace(rows, n); }

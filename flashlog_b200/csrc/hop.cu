@@ -1089,6 +1089,7 @@ struct ReduceArgs {
     int64_t r_size, n;
     const int16_t *fact_rel;
     const int32_t *fact_edge;
+    const int32_t *row_order;    // block -> row (a permutation), or null
 };
 
 // MAX order of values: fp32 order (mode 1) or the unsigned order of the fp32
@@ -1775,7 +1776,7 @@ __device__ float bucket_row(const ReduceArgs &a, ReduceSmem &sm, int64_t s0, int
 __global__ void __launch_bounds__(kRThreads, 1) row_reduce_kernel(ReduceArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     ReduceSmem &sm = *reinterpret_cast<ReduceSmem *>(smem_raw);
-    const int64_t r = blockIdx.x;
+    const int64_t r = a.row_order != nullptr ? static_cast<int64_t>(a.row_order[blockIdx.x]) : blockIdx.x;
     if (r >= a.rows) return;
     const int64_t ea = a.row_ptr[r], eb = a.row_ptr[r + 1];
     const int64_t s0 = a.slot_base[ea], s1 = a.slot_base[eb];
@@ -1861,6 +1862,7 @@ struct BackwardArgs {
     float *grad_val;
     float *grad_w;
     unsigned long long *gacc;  // rows * n * 2 exact accumulators when n > kSmemRel
+    const int32_t *row_order;  // block -> row (a permutation), or null
 };
 
 __global__ void __launch_bounds__(kBThreads, 6) hop_backward_kernel(BackwardArgs a) {
@@ -1868,7 +1870,7 @@ __global__ void __launch_bounds__(kBThreads, 6) hop_backward_kernel(BackwardArgs
     unsigned long long *sacc = reinterpret_cast<unsigned long long *>(smem_raw);
     __shared__ float fscratch[kBThreads / 32 + 1];
     __shared__ int64_t iscratch[kBThreads / 32 + 1];
-    const int64_t r = blockIdx.x;
+    const int64_t r = a.row_order != nullptr ? static_cast<int64_t>(a.row_order[blockIdx.x]) : blockIdx.x;
     if (r >= a.rows) return;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t oa = a.out_row_ptr[r], ob = a.out_row_ptr[r + 1];
@@ -2316,7 +2318,8 @@ static int reduce_rows(const int64_t *row_ptr, int64_t rows, int64_t E, const in
                        const int32_t *fact_dst, const float *fact_val, int64_t total_slots, int32_t *fact_pos,
                        float eps, int64_t *out_row_ptr, int32_t *out_ent, float *out_x, float *out_y,
                        float *out_denom, int32_t *status, int max_mode, int64_t r_size, const int16_t *fact_rel,
-                       const int32_t *fact_edge, void *ws, size_t ws_bytes, cudaStream_t st) {
+                       const int32_t *fact_edge, const int32_t *row_order, void *ws, size_t ws_bytes,
+                       cudaStream_t st) {
     FL_REQUIRE(total_slots < (int64_t(1) << 32), "too many facts in one hop (%lld)", static_cast<long long>(total_slots));
     FL_REQUIRE(E < (int64_t(1) << 31), "entity count exceeds int32");
     Carve c(ws, ws_bytes);
@@ -2334,6 +2337,7 @@ static int reduce_rows(const int64_t *row_ptr, int64_t rows, int64_t E, const in
         a.tmp_ent = tmp_ent; a.tmp_x = tmp_x; a.out_count = out_count; a.out_sum = out_sum;
         a.capacity = total_slots; a.status = status;
         a.max_mode = max_mode; a.r_size = r_size; a.n = 2 * r_size + 1; a.fact_rel = fact_rel; a.fact_edge = fact_edge;
+        a.row_order = row_order;
         const size_t smem = sizeof(ReduceSmem);
         static bool attr_set = false;
         if (!attr_set) {
@@ -2356,10 +2360,10 @@ static int reduce_rows(const int64_t *row_ptr, int64_t rows, int64_t E, const in
 int row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *slot_base, const int32_t *entry_count,
                const int32_t *fact_dst, const float *fact_val, int64_t total_slots, int32_t *fact_pos, float eps,
                int64_t *out_row_ptr, int32_t *out_ent, float *out_x, float *out_y, float *out_denom, int32_t *status,
-               void *ws, size_t ws_bytes, cudaStream_t st) {
+               const int32_t *row_order, void *ws, size_t ws_bytes, cudaStream_t st) {
     (void)entry_count;  // unfilled slots carry the destination -1
     return reduce_rows(row_ptr, rows, E, slot_base, fact_dst, fact_val, total_slots, fact_pos, eps, out_row_ptr,
-                       out_ent, out_x, out_y, out_denom, status, 0, 0, nullptr, nullptr, ws, ws_bytes, st);
+                       out_ent, out_x, out_y, out_denom, status, 0, 0, nullptr, nullptr, row_order, ws, ws_bytes, st);
 }
 
 int row_reduce_max(const int64_t *row_ptr, int64_t rows, int64_t E, int64_t r_size, const int64_t *slot_base,
@@ -2369,8 +2373,8 @@ int row_reduce_max(const int64_t *row_ptr, int64_t rows, int64_t E, int64_t r_si
     FL_REQUIRE(fact_rel != nullptr && fact_edge != nullptr, "the MAX reduction needs fact relations and triple ids");
     FL_REQUIRE(max_mode == 1 || max_mode == 2, "bad MAX mode");
     return reduce_rows(row_ptr, rows, E, slot_base, fact_dst, fact_val, total_slots, fact_pos, 1e-7f, out_row_ptr,
-                       out_ent, out_x, nullptr, nullptr, status, max_mode, r_size, fact_rel, fact_edge, ws, ws_bytes,
-                       st);
+                       out_ent, out_x, nullptr, nullptr, status, max_mode, r_size, fact_rel, fact_edge, nullptr, ws,
+                       ws_bytes, st);
 }
 
 size_t row_reduce_workspace(int64_t rows, int64_t total_slots) {
@@ -2392,7 +2396,7 @@ int hop_backward(const fl_hop_params *p, const int64_t *row_ptr, const float *va
     a.normalize = (p->flags & FL_NO_NORMALIZE) ? 0 : 1;
     a.slot_base = slot_base; a.entry_count = entry_count; a.fact_pos = fact_pos; a.fact_rel = fact_rel;
     a.fact_m = fact_m; a.out_row_ptr = out_row_ptr; a.out_x = out_x; a.out_denom = out_denom; a.g_y = g_y;
-    a.grad_val = grad_val; a.grad_w = grad_w; a.gacc = nullptr;
+    a.grad_val = grad_val; a.grad_w = grad_w; a.gacc = nullptr; a.row_order = p->row_order;
     size_t smem = 0;
     if (p->n > kSmemRel) {
         Carve c(ws, ws_bytes);

@@ -26,7 +26,7 @@ int row_reduce_max(const int64_t *row_ptr, int64_t rows, int64_t E, int64_t r_si
 int row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *slot_base, const int32_t *entry_count,
                const int32_t *fact_dst, const float *fact_val, int64_t total_slots, int32_t *fact_pos, float eps,
                int64_t *out_row_ptr, int32_t *out_ent, float *out_x, float *out_y, float *out_denom, int32_t *status,
-               void *ws, size_t ws_bytes, cudaStream_t st);
+               const int32_t *row_order, void *ws, size_t ws_bytes, cudaStream_t st);
 int hop_backward(const fl_hop_params *p, const int64_t *row_ptr, const float *val, int64_t S, const float *w,
                  const int64_t *slot_base, const int32_t *entry_count, const int32_t *fact_pos, const int16_t *fact_rel,
                  const float *fact_m, const int64_t *out_row_ptr, const float *out_x, const float *out_denom,

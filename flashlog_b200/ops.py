@@ -364,7 +364,8 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
     else:
         check(lib().fl_row_reduce(_p(row_ptr), rows, graph.E, _p(slot_base), _p(entry_count), _p(fact_dst),
                                   _p(fact_val), T, _p(fact_pos), ctypes.c_float(eps), _p(out_row_ptr), _p(out_ent),
-                                  _p(out_x), _p(out_y), _p(out_denom), _p(status), _p(ws2), ws2.numel(), _stream()),
+                                  _p(out_x), _p(out_y), _p(out_denom), _p(status), None, _p(ws2), ws2.numel(),
+                                  _stream()),
               "row_reduce")
     if timing is not None:
         timing.record_end()
@@ -460,7 +461,7 @@ def fixed_relation(b, l, e, v, ops_, graph: Graph, r_size: int, B: int, Lr: int)
     ws2 = _ws(lib().fl_reduce_workspace(rows, T), dev)
     check(lib().fl_row_reduce(_p(row_ptr), rows, graph.E, _p(slot_base), _p(entry_count), _p(fact_dst), _p(fact_val),
                               T, None, ctypes.c_float(EPS), _p(out_row_ptr), _p(out_ent), _p(out_x), None,
-                              _p(out_denom), None, _p(ws2), ws2.numel(), _stream()), "row_reduce")
+                              _p(out_denom), None, None, _p(ws2), ws2.numel(), _stream()), "row_reduce")
     u = int(out_row_ptr[rows].item())
     return out_row_ptr, out_ent[:u], out_x[:u]
 
@@ -487,8 +488,8 @@ def channel_merge(row_ptr, ent, val, B: int, Lch: int, E: int):
     ws = _ws(lib().fl_reduce_workspace(B, max(nnz, 1)), dev)
     check(lib().fl_row_reduce(_p(entry_row_ptr), B, int(E), _p(slot_base), _p(entry_count), _p(ent.contiguous()),
                               _p(val.to(torch.float32).contiguous()), max(nnz, 1), _p(fact_pos), ctypes.c_float(EPS),
-                              _p(out_row_ptr), _p(out_ent), _p(out_x), None, _p(out_denom), None, _p(ws), ws.numel(),
-                              _stream()), "channel_merge")
+                              _p(out_row_ptr), _p(out_ent), _p(out_x), None, _p(out_denom), None, None, _p(ws),
+                              ws.numel(), _stream()), "channel_merge")
     u = int(out_row_ptr[B].item())
     row_of = torch.repeat_interleave(torch.arange(B, device=dev), entry_row_ptr[1:] - entry_row_ptr[:-1],
                                      output_size=nnz)

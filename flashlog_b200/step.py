@@ -122,6 +122,8 @@ class DrumTrainStep:
         # rows of queries with one relation have one w: they share the first such row's ranks
         self.rank_row = _buf(rows, i32, dev) if self.use_rank else None
         self.chan = torch.arange(N, dtype=torch.int64, device=dev)
+        # per hop: rows by descending slot count, the reduction's and the backward's block order
+        self.row_order = [_buf(rows, i32, dev) for _ in range(T)]
         self.fact_dst = _buf(Fmax, i32, dev)
         self.fact_val = _buf(Fmax, f32, dev)
         self.grad_sel = _buf(Smax, f32, dev)
@@ -164,7 +166,8 @@ class DrumTrainStep:
                                float(self.eps), int(self.F[t]), self.status.data_ptr(), self.entry_info.data_ptr(),
                                self.vis[0].data_ptr(), self.vis[1].data_ptr(), self.work.data_ptr(),
                                self.rel_rank.data_ptr() if self.use_rank else None,
-                               self.rank_row.data_ptr() if self.use_rank else None)
+                               self.rank_row.data_ptr() if self.use_rank else None,
+                               self.row_order[t].data_ptr())
 
     # ------------------------------------------------------------------
     def run(self):
@@ -203,6 +206,9 @@ class DrumTrainStep:
             params = self._params(t, self.flags)
             check(lb.fl_hop_plan(ctypes.byref(params), _p(rp_s), _p(ent_s), self.S[t], g.ori, g.inv,
                                  _p(self.slot_base[t]), None, ws, wsn, st), "hop_plan")
+            # rows by descending slot count: the reduction and the backward take the heaviest first
+            rows_facts = self.slot_base[t][rp_s[1:]] - self.slot_base[t][rp_s[:-1]]
+            self.row_order[t].copy_(torch.argsort(rows_facts, descending=True, stable=True))
             if self.timer is not None:
                 self.timer[t][0].record()
             check(lb.fl_hop_expand(ctypes.byref(params), _p(rp_s), _p(ent_s), _p(val_s), self.S[t], _p(self.w[t]),
@@ -212,8 +218,8 @@ class DrumTrainStep:
             check(lb.fl_row_reduce(_p(rp_s), rows, g.E, _p(self.slot_base[t]), _p(self.entry_count[t]),
                                    _p(self.fact_dst), _p(self.fact_val), self.F[t], _p(self.fact_pos[t]),
                                    ctypes.c_float(self.eps), _p(self.out_rp[t]), _p(self.out_ent[t]),
-                                   _p(self.out_x[t]), _p(self.out_y[t]), _p(self.out_denom[t]), _p(self.status), ws,
-                                   wsn, st), "row_reduce")
+                                   _p(self.out_x[t]), _p(self.out_y[t]), _p(self.out_denom[t]), _p(self.status),
+                                   _p(self.row_order[t]), ws, wsn, st), "row_reduce")
             if self.timer is not None:
                 self.timer[t][1].record()
             if self.stats is not None:

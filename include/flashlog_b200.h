@@ -83,6 +83,10 @@ typedef struct {
                                        fl_relation_rank of the same w             */
     const int32_t *rank_row;        /* i32[rows] or NULL: the row whose ranks a
                                        row uses (rows with equal w share one)     */
+    const int32_t *row_order;       /* i32[rows] or NULL: the order in which
+                                       fl_hop_backward takes the rows (a
+                                       permutation; heaviest first balances the
+                                       tail), NULL: row order                     */
     int32_t *fact_edge;             /* i32[slots] or NULL: fl_hop_expand writes each
                                        fact's triple id (order[p]; 0 for identity),
                                        the tie key of fl_row_reduce_max          */
@@ -188,12 +192,14 @@ int fl_hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t 
  * output count), out_denom f32[rows] (raw row sums).  Stream-ordered; no
  * host synchronization.  total_slots is the length of the fact and output
  * buffers; rows whose slots lie beyond it are skipped and set
- * FL_STATUS_SLOT_OVERFLOW in *status (device int, may be NULL). */
+ * FL_STATUS_SLOT_OVERFLOW in *status (device int, may be NULL).  row_order
+ * (i32[rows], a permutation, or NULL) is the order in which the rows are
+ * taken: heaviest first shortens the tail; results do not depend on it. */
 size_t fl_reduce_workspace(int64_t rows, int64_t total_slots);
 int fl_row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *slot_base, const int32_t *entry_count,
                   const int32_t *fact_dst, const float *fact_val, int64_t total_slots, int32_t *fact_pos, float eps,
                   int64_t *out_row_ptr, int32_t *out_ent, float *out_x, float *out_y, float *out_denom,
-                  int32_t *status, void *ws, size_t ws_bytes, fl_stream_t stream);
+                  int32_t *status, const int32_t *row_order, void *ws, size_t ws_bytes, fl_stream_t stream);
 
 /* MAX coalesce of expanded facts (FlashLogFunctionSparse3DTopKMax,
  * flashlog_kernel.py:386-478): per (row, destination) the largest fact value;
