@@ -962,17 +962,20 @@ __global__ void __launch_bounds__(kExpandWarps * 32, kRanked ? 4 : 3) hop_expand
         }
     };
     if (a.work != nullptr) {
-        // Warps take chunks of kChunk entries from a queue, so a warp held up
-        // by hub entries does not hold up the others of its block.
-        // 16 entries per grab, fewer when there are not 16 per resident warp
-        const int64_t kChunk = S_live >= nwarps * 16 ? 16 : (S_live >= nwarps * 8 ? 8 : 4);
+        // Warps take runs of entries from a queue (counted in entries), so a
+        // warp held up by hub entries does not hold up the others of its
+        // block: 16 entries per grab while more than 64 per resident warp
+        // remain, then 4, so the last grabs are short (guided scheduling).
+        int64_t seen = 0;  // this warp's last grab: the queue has passed it
         for (;;) {
+            const uint32_t take = (S_live - seen > nwarps * 64) ? 16u : 4u;
             uint32_t c = 0;
-            if (lane == 0) c = atomicAdd(a.work, 1u);
+            if (lane == 0) c = atomicAdd(a.work, take);
             c = __shfl_sync(kFull, c, 0);
-            const int64_t b0 = static_cast<int64_t>(c) * kChunk;
+            const int64_t b0 = static_cast<int64_t>(c);
             if (b0 >= S_live) break;
-            for (int64_t base = b0; base < b0 + kChunk && base < S_live; base += 4) four(base);
+            seen = b0;
+            for (int64_t base = b0; base < b0 + take && base < S_live; base += 4) four(base);
         }
     } else {
         for (int64_t base = (static_cast<int64_t>(blockIdx.x) * kExpandWarps + wib) * 4; base < S_live;
