@@ -98,6 +98,7 @@ __global__ void csr_visibility_kernel(const int32_t *order, int64_t m, const uin
 // ---------------------------------------------------------------------------
 constexpr int kExpandWarps = 8;
 constexpr int kTeam = 8;
+constexpr int kBigPass = 0, kSmallPass = 1, kBothPasses = 2;  // work-queue passes of the expansion
 constexpr int kTeamMaxSlots = 24;  // entries with more reserved slots go to the whole-warp path
 constexpr int kStage = 1024;  // relation groups of one side staged per warp
 constexpr int kRankBins = 512;  // bins of the rank select (WarpScratch::hist)
@@ -910,8 +911,9 @@ __global__ void __launch_bounds__(kExpandWarps * 32, kRanked ? 4 : 3) hop_expand
     const bool wot_i = (a.flags & FL_WOT_I) != 0;
     const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kExpandWarps;
     const int64_t S_live = a.row_ptr[a.rows] < a.S ? a.row_ptr[a.rows] : a.S;
-    // Four entries (one per team) starting at `base`.
-    auto four = [&](int64_t base) {
+    // Four entries (one per team) starting at `base`; `which` selects the
+    // whole-warp entries (kBigPass), the team entries (kSmallPass) or both.
+    auto four = [&](int64_t base, int which) {
         const int64_t i = base + team;
         const bool mine = i < S_live;
         bool small = false, over = false;
@@ -934,7 +936,7 @@ __global__ void __launch_bounds__(kExpandWarps * 32, kRanked ? 4 : 3) hop_expand
             // entry with many reserved slots is emitted faster by the whole warp
             small = !over && (e.g1o - e.g0o) <= kTeam && (e.g1i - e.g0i) <= kTeam && end - out <= kTeamMaxSlots;
         }
-        if (small) {
+        if (small && which != kBigPass) {
             const int64_t row = a.info ? static_cast<int64_t>(e.row) : find_row(a.row_ptr, a.rows, i);
             const float *wrow = a.w + row * a.n;
             int64_t written = team_entry(a, wrow, v, e.g0o, e.g1o, e.g0i, e.g1i, tm, tl, tbase, out, skip_nonpos,
@@ -954,7 +956,7 @@ __global__ void __launch_bounds__(kExpandWarps * 32, kRanked ? 4 : 3) hop_expand
             for (int64_t s = out + written + tl; s < end; s += kTeam) a.fact_dst[s] = -1;
         }
         __syncwarp();
-        unsigned big = __ballot_sync(kFull, mine && !small && tl == 0);
+        unsigned big = __ballot_sync(kFull, mine && !small && tl == 0 && which != kSmallPass);
         while (big) {
             const int t = (__ffs(big) - 1) / kTeam;
             big &= big - 1;
@@ -962,25 +964,28 @@ __global__ void __launch_bounds__(kExpandWarps * 32, kRanked ? 4 : 3) hop_expand
         }
     };
     if (a.work != nullptr) {
-        // Warps take runs of entries from a queue (counted in entries), so a
-        // warp held up by hub entries does not hold up the others of its
-        // block: 16 entries per grab while more than 64 per resident warp
-        // remain, then 4, so the last grabs are short (guided scheduling).
-        int64_t seen = 0;  // this warp's last grab: the queue has passed it
-        for (;;) {
-            const uint32_t take = (S_live - seen > nwarps * 64) ? 16u : 4u;
-            uint32_t c = 0;
-            if (lane == 0) c = atomicAdd(a.work, take);
-            c = __shfl_sync(kFull, c, 0);
-            const int64_t b0 = static_cast<int64_t>(c);
-            if (b0 >= S_live) break;
-            seen = b0;
-            for (int64_t base = b0; base < b0 + take && base < S_live; base += 4) four(base);
+        // Warps take runs of entries from two queues (counted in entries):
+        // first the whole-warp entries, then the team entries, so the
+        // kernel's tail is made of short team work; a warp held up by a hub
+        // does not hold up the others of its block.  16 entries per grab
+        // while more than 64 per resident warp remain, then 4 (guided).
+        for (int pass = kBigPass; pass <= kSmallPass; ++pass) {
+            int64_t seen = 0;  // this warp's last grab: the queue has passed it
+            for (;;) {
+                const uint32_t take = (S_live - seen > nwarps * 64) ? 16u : 4u;
+                uint32_t c = 0;
+                if (lane == 0) c = atomicAdd(a.work + pass, take);
+                c = __shfl_sync(kFull, c, 0);
+                const int64_t b0 = static_cast<int64_t>(c);
+                if (b0 >= S_live) break;
+                seen = b0;
+                for (int64_t base = b0; base < b0 + take && base < S_live; base += 4) four(base, pass);
+            }
         }
     } else {
         for (int64_t base = (static_cast<int64_t>(blockIdx.x) * kExpandWarps + wib) * 4; base < S_live;
              base += nwarps * 4)
-            four(base);
+            four(base, kBothPasses);
     }
 }
 
@@ -2296,7 +2301,7 @@ int hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *en
         const bool ranked = a.rel_rank != nullptr && a.topk >= 1 && a.topk < 65536;
         int64_t blocks = (S + 4 * kExpandWarps - 1) / (4 * kExpandWarps);
         if (a.work != nullptr) {  // resident blocks drain the work queue (4 per SM with the rank staging)
-            FL_CUDA(cudaMemsetAsync(a.work, 0, sizeof(uint32_t), st));
+            FL_CUDA(cudaMemsetAsync(a.work, 0, 2 * sizeof(uint32_t), st));
             cap_blocks = static_cast<int64_t>(sms > 0 ? sms : 148) * (ranked ? 4 : per_sm);
         }
         if (blocks > cap_blocks) blocks = cap_blocks;

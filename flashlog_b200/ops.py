@@ -291,7 +291,7 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
     if vis is not None and (len(vis) != 2 or any(v.numel() < graph.csr[1].numel() or v.dtype != torch.uint8
                                                  for v in vis)):
         raise ValueError("vis must be the two u8 CSR-ordered visibility arrays of csr_visibility")
-    work = torch.empty(1, dtype=torch.int32, device=dev)
+    work = torch.empty(2, dtype=torch.int32, device=dev)  # the expansion's two work queues
     rel_rank = (relation_rank(w, r_size) if rank_select and (flags & L.FL_SKIP_NONPOS_W)
                 and topk_edges < L.NO_BUDGET and not (flags & L.FL_SAMPLED) else None)
     params = hop_params(rows, Lch, n, r_size, graph.E, topk_edges, flags, seed, eps, slot_capacity or 0, status,

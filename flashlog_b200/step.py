@@ -128,7 +128,7 @@ class DrumTrainStep:
         self.fact_val = _buf(Fmax, f32, dev)
         self.grad_sel = _buf(Smax, f32, dev)
         self.grad_w = _buf(rows * self.n, f32, dev)
-        self.work = _buf(1, i32, dev)
+        self.work = _buf(2, i32, dev)  # the expansion's two work queues
         self.status = torch.zeros(1, dtype=i32, device=dev)
         self.scores = _buf(Q, f32, dev)
         self.loss = torch.zeros((), dtype=f32, device=dev)

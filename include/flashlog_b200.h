@@ -77,8 +77,9 @@ typedef struct {
     const uint8_t *vis_ori, *vis_inv; /* u8[M] or NULL: CSR-ordered visibility from
                                        fl_csr_visibility; replaces the mask_triple
                                        read through `order` (same result)         */
-    uint32_t *work;                 /* device u32 or NULL: work queue of fl_hop_expand
-                                       (it zeroes it); NULL: static assignment    */
+    uint32_t *work;                 /* device u32[2] or NULL: the two work queues of
+                                       fl_hop_expand (it zeroes them); NULL:
+                                       static assignment                          */
     const uint16_t *rel_rank;       /* u16[rows * 2 * r_size] or NULL: from
                                        fl_relation_rank of the same w             */
     const int32_t *rank_row;        /* i32[rows] or NULL: the row whose ranks a
