@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--dropout", type=float, default=0.1,
+                    help="training dropout of each hop's values (src/main.py:1008 default 0.1)")
     ap.add_argument("--engine", default="graph", choices=["graph", "autograd"],
                     help="graph: static-buffer step replayed as CUDA graphs; autograd: engine.drum_propagate")
     return ap.parse_args()
@@ -210,14 +212,18 @@ def run_value_arm(args, cfg, train, csr, rank, world, device):
     stats = Stats(graph)
     status = engine.new_status(device)
     lr = 0.01
+    k = 0  # steps so far: the dropout counter
 
     def step(ids, h, r, t, collect):
         from flashlog_b200 import multigpu as MG
         hide = MG.gather_hidden_triples(ids) if world > 1 else ids
         mask[hide] = 0
         w_all = table[r]
+        nonlocal k
+        k += 1
         rp, ent, val = engine.drum_propagate(h, w_all, graph, R, c1=cfg.c1 or None, c2=cfg.c2, mask_triple=mask,
-                                             stats=stats if collect else None, status=status)
+                                             stats=stats if collect else None, status=status, dropout=args.dropout,
+                                             dropout_seed=1234 + rank, dropout_counter=k)
         loss = engine.readout_loss(rp, ent, val, t, N)
         table.grad = None
         loss.backward()
@@ -285,7 +291,7 @@ def run_graph_arm(args, cfg, train, csr, rank, world, device):
     dev_data = [tuple(torch.from_numpy(x).to(device) for x in b) for b in data]
     n_ids = dev_data[0][0].numel()
     step = DrumTrainStep(graph, R, cfg.queries, T, N, cfg.c1 or None, cfg.c2, table, n_hide=n_ids * world,
-                         apply_update=(world == 1))
+                         apply_update=(world == 1), dropout=args.dropout, dropout_seed=1234 + rank)
     lr = step.lr
 
     from flashlog_b200 import multigpu as MG
@@ -363,13 +369,17 @@ def run_e2e_arm(args, cfg, train, csr, data, table, rank, world, device, steps):
     from flashlog_b200 import engine, ops
     import torch.distributed as dist
 
+    from flashlog_b200.dropout import sparse_dropout
     R, T, N, E = cfg.relations, cfg.T, cfg.N, cfg.entities
     mask = torch.ones(train.shape[0], dtype=torch.bool, device=device)
     pinned = [tuple(torch.from_numpy(x).pin_memory() for x in b) for b in data]
+    k = 0  # steps so far: the dropout counter
     h2d = sum(x.numel() * x.element_size() for x in pinned[0])
     tab = table.detach().clone().requires_grad_(True)
 
     def step(ids_h, h_h, r_h, t_h):
+        nonlocal k
+        k += 1
         ids = ids_h.to(device, non_blocking=True)
         h = h_h.to(device, non_blocking=True)
         r = r_h.to(device, non_blocking=True)
@@ -388,6 +398,8 @@ def run_e2e_arm(args, cfg, train, csr, data, table, rank, world, device, steps):
             w_t = torch.softmax(w_all[:, hop], dim=-1)
             state = fk.vectorized_operation_sparse3d_csr_sum_norm(state, w_t, csr, mask, R, use_topk=True,
                                                                  topk_edges=cfg.c2 // 2, topk_nodes=cfg.c1)
+            # the models' training dropout of the values (src/model_DRUM_kernel_sp.py:189-192)
+            state = sparse_dropout(state, args.dropout, seed=1234 + rank, counter=k, subseq=hop)
         # readout + log loss (src/utils.py:36-47) through the library's readout
         idx = state.indices()
         rp, ent, _ = ops.coo_to_rows(idx[0], idx[1], idx[2], Q, N, E)
@@ -568,7 +580,7 @@ def main():
                            "l2": "inputs larger than L2 (CSR ~0.7 GB; fresh query batch every step)",
                            "engine": ("static buffers, one CUDA graph per step (flashlog_b200.step)"
                                       if args.engine == "graph" else "autograd, one host sync per hop"),
-                           "facts_per_step": facts / args.steps},
+                           "facts_per_step": facts / args.steps, "dropout": args.dropout},
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                              "frac": achieved / peak, "traffic": traffic, "peak_source": peak_src,
                              "kernel": "hop forward (expand + row reduction), rank 0",

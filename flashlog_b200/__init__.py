@@ -4,7 +4,7 @@ The names exported here are those of the reference package
 (flashlog_kernel/__init__.py); the implementation runs in hand-written sm_100a
 kernels behind the C ABI of include/flashlog_b200.h.
 """
-from . import filters, readout  # noqa: F401  (filter keys; channel readouts)
+from . import dropout, filters, readout  # noqa: F401  (value dropout; filter keys; channel readouts)
 from .flashlog_kernel import (  # noqa: F401
     FlashLogDenseMaxFunction,
     FlashLogDenseSumFunction,

@@ -109,6 +109,8 @@ SIGNATURES = {
     "fl_scatter_grad": (ctypes.c_int, [_P, _P, _I64, _P, _P, _I64, _P, _P]),
     "fl_readout": (ctypes.c_int, [_P, _P, _P, _I64, _P, _I64, _P, _P]),
     "fl_readout_backward": (ctypes.c_int, [_P, _P, _I64, _P, _I64, _P, _P, _I64, _P, _P]),
+    "fl_value_dropout": (ctypes.c_int, [_P, _P, _I64, _P, ctypes.c_double, ctypes.c_uint64, _P, ctypes.c_uint64,
+                                        _P]),
     "fl_fixed_relation_workspace": (_SZ, [_I64]),
     "fl_fixed_relation_plan": (ctypes.c_int, [_P, _P, _P, _I64, _P, _I64, _I64, _SIDE, _SIDE, _P,
                                               ctypes.POINTER(ctypes.c_int64), _P, _SZ, _P]),

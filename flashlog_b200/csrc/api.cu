@@ -60,6 +60,8 @@ int filtered_ranks_noalloc(const int64_t *ib, const int64_t *ie, const float *v,
 
 int readout(const int64_t *row_ptr, const int32_t *ent, const float *val, int64_t N, const int64_t *targets, int64_t Q,
             float *scores, cudaStream_t st);
+int value_dropout(const float *x, float *y, int64_t n, const int64_t *live, double p, uint64_t seed,
+                  const int64_t *counter, uint64_t subseq, cudaStream_t st);
 int readout_backward(const int64_t *row_ptr, const int32_t *ent, int64_t N, const int64_t *targets, int64_t Q,
                      const float *g, float *grad_val, int64_t n_val, const int64_t *val_live, cudaStream_t st);
 
@@ -306,6 +308,11 @@ int fl_readout_backward(const int64_t *row_ptr, const int32_t *ent, int64_t N, c
                         const float *g_scores, float *grad_val, int64_t n_val, const int64_t *val_live,
                         fl_stream_t stream) {
     return readout_backward(row_ptr, ent, N, targets, Q, g_scores, grad_val, n_val, val_live, as_stream(stream));
+}
+
+int fl_value_dropout(const float *x, float *y, int64_t n, const int64_t *live, double p, uint64_t seed,
+                     const int64_t *counter, uint64_t subseq, fl_stream_t st) {
+    return value_dropout(x, y, n, live, p, seed, counter, subseq, as_stream(st));
 }
 
 }  // extern "C"

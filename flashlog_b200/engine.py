@@ -31,7 +31,7 @@ class HopNorm(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, val, w, row_ptr, ent, graph, r_size, topk_edges, c1, flags, mask_triple, eps, stats, status,
-                vis=None):
+                vis=None, keep_zeros=False):
         v = val.detach().contiguous()
         rows = row_ptr.numel() - 1
         ctx.pruned = None
@@ -39,7 +39,11 @@ class HopNorm(torch.autograd.Function):
         ctx.sel_live = None
         ctx.in_live = row_ptr[rows:]  # live entries of the (capacity-sized) input
         if c1 is not None and c1 >= 0:
-            cap = min(v.numel(), rows * int(c1))  # explicit zeros could exceed it: flagged in `status`
+            # a row with at most c1 nonzero values keeps its explicit zeros too
+            # (flashlog_kernel.py:1114-1117): with zeros in the state (dropout)
+            # only the input's size bounds the selection; otherwise an
+            # underflow to zero past rows * c1 is flagged in `status`
+            cap = v.numel() if keep_zeros else min(v.numel(), rows * int(c1))
             rp, en, vv, src = ops.topc_select(row_ptr, ent, v, int(c1), sync=False, out_capacity=cap, status=status)
             row_ptr, ent, v, ctx.pruned = rp, en, vv, src
             ctx.sel_live = rp[rows:]
@@ -59,7 +63,7 @@ class HopNorm(torch.autograd.Function):
         grad_v, grad_w = ops.hop_backward(ctx.fw, row_ptr, v, wf, g_y, normalize=True)
         if ctx.pruned is not None:
             grad_v = ops.scatter_grad(grad_v, ctx.pruned, ctx.n_in, n_live=ctx.sel_live, full_live=ctx.in_live)
-        return grad_v, grad_w, None, None, None, None, None, None, None, None, None, None, None, None
+        return grad_v, grad_w, None, None, None, None, None, None, None, None, None, None, None, None, None
 
 
 class Readout(torch.autograd.Function):
@@ -108,8 +112,13 @@ def check_status(status):
 
 
 def drum_propagate(heads, w_all, graph: Graph, r_size: int, *, c1=None, c2=0, mask_triple=None, tau_1=1.0,
-                   eps=1e-7, stats=None, status=None):
+                   eps=1e-7, stats=None, status=None, dropout=0.0, dropout_seed=None, dropout_counter=0):
     """T hops of the sparse DRUM operator; w_all is [Q, T, N, n] logits.
+
+    dropout > 0: the training dropout of each hop's values
+    (src/model_DRUM_kernel_sp.py:189-192), hop t drawing its keep bits from
+    (dropout_seed, dropout_counter, t) -- the masks DrumTrainStep draws on its
+    replay number dropout_counter.
 
     Returns the final state (row_ptr, ent, val) with capacity-sized ent/val
     (live count row_ptr[-1]).
@@ -123,10 +132,17 @@ def drum_propagate(heads, w_all, graph: Graph, r_size: int, *, c1=None, c2=0, ma
         status = new_status(heads.device)
     # hidden triples in CSR order, shared by the T hops
     vis = ops.csr_visibility(graph, mask_triple) if mask_triple is not None else None
+    drop = None
+    if dropout:
+        from .dropout import device_counter, draw_seed, ValueDropout
+        drop = (float(dropout), draw_seed() if dropout_seed is None else int(dropout_seed),
+                device_counter(dropout_counter, heads.device))
     for t in range(T):
         w_t = torch.softmax(w_all[:, t] / tau_1, dim=-1)
         val, row_ptr, ent = HopNorm.apply(val, w_t, row_ptr, ent, graph, r_size, topk, c1, flags, mask_triple, eps,
-                                          stats, status, vis)
+                                          stats, status, vis, drop is not None)
+        if drop is not None:
+            val = ValueDropout.apply(val, drop[0], drop[1], drop[2], t, row_ptr[-1:])
     if own_status:
         check_status(status)
     return row_ptr, ent, val

@@ -228,9 +228,15 @@ def _select_sources(ctx, row_ptr, ent, val, topk_nodes, sampling):
     return sel_row_ptr, sel_ent, sel_val
 
 
-def _select_sources_async(ctx, row_ptr, ent, val, topk_nodes, rows):
-    """Deterministic c1 without a host sync: outputs keep min(S, rows * c1)
-    entries, their live count stays on the device (row_ptr[rows])."""
+def _select_sources_async(ctx, row_ptr, ent, val, topk_nodes, rows, status=None, full=False):
+    """Deterministic c1 without a host sync: outputs keep min(S, 2 * rows * c1)
+    entries (S with full=True), their live count stays on the device
+    (row_ptr[rows]).  A row with at most c1 nonzero values keeps its explicit
+    zeros too (flashlog_kernel.py:1114-1117), so rows * c1 is no bound once
+    the state holds zeros (training dropout puts a few percent past it; the
+    factor 2 absorbs that).  When even that falls short,
+    FL_STATUS_SLOT_OVERFLOW is set in `status` and the caller selects again
+    with full=True."""
     ctx.pruned = None
     ctx.n_live = None
     ctx.original_input_size = val.numel()
@@ -240,9 +246,9 @@ def _select_sources_async(ctx, row_ptr, ent, val, topk_nodes, rows):
         raise ValueError("topk_nodes/c must be nonnegative")
     if val.numel() <= topk_nodes:
         return row_ptr, ent, val
-    cap = min(val.numel(), rows * int(topk_nodes))
+    cap = val.numel() if full else min(val.numel(), 2 * rows * int(topk_nodes))
     sel_row_ptr, sel_ent, sel_val, src = ops.topc_select(row_ptr, ent, val, int(topk_nodes), sync=False,
-                                                         out_capacity=cap)
+                                                         out_capacity=cap, status=status)
     ctx.pruned = src
     ctx.n_live = sel_row_ptr[rows:]
     return sel_row_ptr, sel_ent, sel_val
@@ -438,11 +444,18 @@ class _Sparse3DSumNormFused(autograd.Function):
                 raise ValueError("topk_nodes/c must be nonnegative")
             if not trusted:
                 _check_bad(bad)
-            row_ptr, ent, val = _select_sources_async(ctx, row_ptr, ent, val, topk_nodes, B * L_)
-            fw = ops.hop_forward(row_ptr, ent, val, wf, graph, r_size, int(topk_edges),
-                                 _topk_flags(weight, False, sampling, wot_i), mask_triple=mask_values,
-                                 edge_weight=None if weight is None else weight.detach(), seed=-1, eps=eps,
-                                 check_w=True)
+            state = (row_ptr, ent, val)
+            sel_status = torch.zeros(1, dtype=torch.int32, device=val.device)
+            for full in (False, True):
+                row_ptr, ent, val = _select_sources_async(ctx, *state, topk_nodes, B * L_, sel_status, full)
+                try:
+                    fw = ops.hop_forward(row_ptr, ent, val, wf, graph, r_size, int(topk_edges),
+                                         _topk_flags(weight, False, sampling, wot_i), mask_triple=mask_values,
+                                         edge_weight=None if weight is None else weight.detach(), seed=-1,
+                                         eps=eps, check_w=True, sel_status=None if full else sel_status)
+                    break
+                except ops.SelectionOverflow:
+                    continue  # explicit zeros past rows * c1: select again at the input's size
         else:
             _check_bad(bad)
             row_ptr, ent, val = _select_sources(ctx, row_ptr, ent, val, topk_nodes, sampling)

@@ -185,6 +185,10 @@ def topc_select(row_ptr, ent, val, c1: int, noise=None, sync: bool = True, out_c
 # --------------------------------------------------------------------------
 # one hop
 # --------------------------------------------------------------------------
+class SelectionOverflow(RuntimeError):
+    """The c1 selection that fed a hop ran out of its output capacity."""
+
+
 @dataclass
 class HopForward:
     params: L.fl_hop_params
@@ -250,7 +254,8 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
                 mask_triple=None, mask_csr=None, edge_weight=None, seed: int = -1, eps: float = EPS,
                 keep_facts: bool = False, record: bool = True, timing=None, slot_capacity=None,
                 status=None, out_sync: bool = True, vis=None, reduce: str = "sum",
-                max_bits: bool = False, rank_select: bool = True, check_w: bool = False) -> HopForward:
+                max_bits: bool = False, rank_select: bool = True, check_w: bool = False,
+                sel_status=None) -> HopForward:
     """Expansion + per-row coalesce-sum + normalization of one hop.
 
     slot_capacity=None sizes the fact buffers exactly (one host sync for the
@@ -269,7 +274,9 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
     select over the groups' weights instead of over relation ranks (same
     result; the path used when r_size exceeds 16384).  check_w raises the
     non-finite-weights RuntimeError of the top-k operators before the
-    expansion, read in the same host sync as the fact count.
+    expansion, read in the same host sync as the fact count.  sel_status (with
+    check_w): the status word of the c1 selection that produced the state,
+    read in that sync too; SelectionOverflow is raised when it is set.
     """
     if reduce not in ("sum", "max"):
         raise ValueError("reduce must be 'sum' or 'max'")
@@ -301,8 +308,13 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
                             ctypes.byref(total) if (sync and not check_w) else None, _p(ws), ws.numel(), _stream()),
           "hop_plan")
     if check_w:
-        # one host read: the fact count and the weights' finiteness
-        got = torch.stack([slot_base[S], nonfinite.to(torch.int64)]).cpu()
+        # one host read: the fact count, the weights' finiteness and the selection's status
+        parts = [slot_base[S], nonfinite.to(torch.int64)]
+        if sel_status is not None:
+            parts.append(sel_status[0].to(torch.int64))
+        got = torch.stack(parts).cpu()
+        if sel_status is not None and int(got[2]) & L.FL_STATUS_SLOT_OVERFLOW:
+            raise SelectionOverflow("the c1 selection exceeded its capacity")
         if int(got[1]):
             raise RuntimeError("FlashLog sparse top-k received non-finite attention weights; "
                                "aborting before edge count/fill to prevent uninitialized indices")
@@ -513,6 +525,27 @@ def filtered_ranks(idx_b, idx_e, values, targets, filter_keys, B: int, E: int, u
                                   filter_keys.numel(), B, E, int(bool(use_eql)), _p(ranks), _p(ws), ws.numel(),
                                   _stream()), "filtered_ranks")
     return ranks[:B]
+
+
+# --------------------------------------------------------------------------
+# dropout of hop values
+# --------------------------------------------------------------------------
+def value_dropout(x, p: float, seed: int, counter=None, subseq: int = 0, live=None, out=None):
+    """nn.Dropout(p) on a float32 value vector (src/model_DRUM_kernel_sp.py:189-192)
+    with counter-based keep bits (fl_value_dropout): the mask is a function of
+    (seed, counter[0], subseq, position), so the same call on the gradient is
+    the backward.  counter: device int64 tensor or None (0); live: device
+    count of the entries to write (the rest of `out` is left as it is)."""
+    _require_cuda(x, counter, live)
+    if x.dtype != torch.float32:
+        raise ValueError("value_dropout takes float32 values")
+    if not 0.0 <= float(p) <= 1.0:
+        raise ValueError(f"dropout probability must lie in [0, 1], got {p}")
+    x = x.contiguous()
+    y = torch.empty_like(x) if out is None else out
+    check(lib().fl_value_dropout(_p(x), _p(y), x.numel(), _p(live), ctypes.c_double(float(p)),
+                                 int(seed) & 0xFFFFFFFFFFFFFFFF, _p(counter), int(subseq), _stream()), "value_dropout")
+    return y
 
 
 # --------------------------------------------------------------------------

@@ -6,17 +6,21 @@ channel readout and log loss of src/utils.py:36-47, their backward and an
 SGD update of a per-query-relation attention table, written against buffers
 allocated once.  Every buffer is sized by a static bound:
 
-  selected entries of hop t   S_t = min(C_t, rows * c1)
+  selected entries of hop t   S_t = min(C_t, ceil(rows * c1 * zero_slack))
   fact slots of hop t         F_t = min(S_t * k_max, rows * K)
   outputs of hop t            C_{t+1} = min(F_t, rows * E)
 
 where k(e) = min(deg_ori(e), c2//2) + min(deg_inv(e), c2//2) + 1 is the slot
 capacity of entity e, k_max its maximum, K its sum over the entities (a row
-holds every entity at most once) and C_0 = rows.  The kernels
+holds every entity at most once) and C_0 = rows.  zero_slack is 1 without
+dropout: a row keeps at most c1 entries unless it has at most c1 nonzero
+values, and then all of them.  Such a row also keeps its explicit zeros
+(flashlog_kernel.py:1114-1117), so with dropout the selection has no useful
+static bound and zero_slack (default 2) sizes it.  The kernels
 read the live counts from the device (row_ptr[-1]), so nothing is read back
 to the host and one step can be captured in a CUDA graph and replayed.  A
 device status word flags any capacity overflow (it cannot happen under these
-bounds) and `check` reads it.
+bounds without dropout) and `check` reads it.
 
 The autograd path of engine.drum_propagate computes the same step with one
 host synchronization per hop.
@@ -24,6 +28,7 @@ host synchronization per hop.
 from __future__ import annotations
 
 import ctypes
+import math
 
 import torch
 
@@ -45,11 +50,14 @@ class DrumTrainStep:
     SGD update table[rels] -= lr * d loss / d logits (only the batch's rows
     are touched); without it the dense gradient of the table is left in
     `grad` (for an all-reduce across ranks before the caller's update).
+    dropout > 0 applies the training dropout of each hop's values
+    (src/model_DRUM_kernel_sp.py:189-192) in place; replay k (from 1) draws
+    hop t's keep bits from (dropout_seed, k, t), counted on the device.
     """
 
     def __init__(self, graph: Graph, r_size: int, Q: int, T: int, N: int, c1, c2: int, table: torch.Tensor,
                  n_hide: int, lr: float = 0.01, eps: float = 1e-7, thr: float = 1e-7, stats: bool = True,
-                 apply_update: bool = True):
+                 apply_update: bool = True, dropout: float = 0.0, dropout_seed: int = 0, zero_slack=None):
         dev = table.device
         self.dev, self.graph, self.r_size, self.Q, self.T, self.N = dev, graph, r_size, Q, T, N
         self.n = 2 * r_size + 1
@@ -58,6 +66,11 @@ class DrumTrainStep:
         self.flags = L.FL_SKIP_NONPOS_W | L.FL_DROP_MASKED
         self.eps, self.thr, self.lr = eps, thr, lr
         self.apply_update = apply_update
+        if not 0.0 <= float(dropout) <= 1.0:
+            raise ValueError(f"dropout probability must lie in [0, 1], got {dropout}")
+        self.dropout, self.dropout_seed = float(dropout), int(dropout_seed) & 0xFFFFFFFFFFFFFFFF
+        self.drop_counter = torch.zeros(1, dtype=torch.int64, device=dev)  # replays so far
+        self.zero_slack = (2.0 if self.dropout > 0 else 1.0) if zero_slack is None else float(zero_slack)
         self.table = table
         self.grad = None if apply_update else torch.zeros_like(table)
         rows = Q * N
@@ -73,7 +86,7 @@ class DrumTrainStep:
         self.C, self.S, self.F, self.U = [], [], [], []
         C = rows
         for _ in range(T):
-            S = min(C, rows * self.c1) if self.c1 is not None else C
+            S = min(C, math.ceil(rows * self.c1 * self.zero_slack)) if self.c1 is not None else C
             F = min(S * k_max, rows * K)
             self.C.append(C)
             self.S.append(S)
@@ -175,6 +188,8 @@ class DrumTrainStep:
         lb, st, g = lib(), _stream(), self.graph
         rows, N, Q, T = self.rows, self.N, self.Q, self.T
         ws, wsn = _p(self.ws), self.ws.numel()
+        if self.dropout > 0:
+            self.drop_counter.add_(1)
         # hide the batch's own triples (src/main.py:888), remembering what was there
         hid = [self.pos[k][self.hide] for k in range(2)]
         old = [self.vis[k][hid[k]] for k in range(2)]
@@ -222,6 +237,8 @@ class DrumTrainStep:
                                    _p(self.row_order[t]), ws, wsn, st), "row_reduce")
             if self.timer is not None:
                 self.timer[t][1].record()
+            if self.dropout > 0:
+                self._dropout(self.out_y[t], t, st)
             if self.stats is not None:
                 check(lb.fl_hop_stats(_p(rp_s), rows, _p(ent_s), self.S[t], g.ori, g.inv, _p(self.entry_count[t]),
                                       _p(self.out_rp[t]), 0, _p(self.stats), st), "hop_stats")
@@ -236,6 +253,8 @@ class DrumTrainStep:
                                      self.U[T - 1], _p(self.out_rp[T - 1][rows:]), st), "readout_backward")
         # backward through the hops
         for t in reversed(range(T)):
+            if self.dropout > 0:  # d/d(normalized values): the same keep bits and scale
+                self._dropout(self.g_y[t], t, st)
             params = self._params(t, self.flags)
             check(lb.fl_hop_backward(ctypes.byref(params), _p(self.rp_sel[t]), _p(self.val_sel[t]), self.S[t],
                                      _p(self.w[t]), _p(self.slot_base[t]), _p(self.entry_count[t]),
@@ -263,6 +282,11 @@ class DrumTrainStep:
         for k in range(2):
             self.vis[k].index_put_((hid[k],), old[k])
         return self.loss
+
+    def _dropout(self, x, t, st):
+        check(lib().fl_value_dropout(_p(x), _p(x), self.U[t], _p(self.out_rp[t][self.rows:]),
+                                     ctypes.c_double(self.dropout), self.dropout_seed, _p(self.drop_counter), t, st),
+              "value_dropout")
 
     def check(self):
         """Raise if any hop ran out of its buffers (one host read)."""

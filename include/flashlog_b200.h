@@ -268,6 +268,20 @@ int fl_readout_backward(const int64_t *row_ptr, const int32_t *ent, int64_t N, c
                         const float *g_scores, float *grad_val, int64_t n_val, const int64_t *val_live,
                         fl_stream_t stream);
 
+/* Dropout of hop values (nn.Dropout on s.values() in training,
+ * src/model_DRUM_kernel_sp.py:189-192; the other sparse models do the same).
+ * y[i] = x[i] * (keep(i) ? scale : 0) for i < n (or the first
+ * *live, a device count, when live is given); y may be x.  keep(i) is a pure
+ * function of (seed, *counter, subseq, i): with
+ *   key = splitmix64(seed ^ splitmix64((*counter << 16) | subseq)),
+ * i is kept iff (splitmix64(key + i) >> 32) >= floor(p * 2^32)
+ * (splitmix64: the SplitMix64 output function; *counter is 0 when counter is
+ * NULL) and scale = (float)(1 / (double)(float)(1 - p)), torch's rounding.  A device counter lets a captured step draw a new mask per replay;
+ * the backward is the same call on the gradient.  Needs 0 <= p <= 1 and
+ * subseq < 65536 (FL_EINVAL otherwise). */
+int fl_value_dropout(const float *x, float *y, int64_t n, const int64_t *live, double p, uint64_t seed,
+                     const int64_t *counter, uint64_t subseq, fl_stream_t stream);
+
 /* Rule step with one fixed operator per (query, rule) row: ops i64[B, Lr]
  * holds a forward relation, inverse relation + R, or identity 2R.  Replaces
  * flashlog_forward_sparse3d_fixed_relation_cuda (flashlog.cu:1677-1741); the

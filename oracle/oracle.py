@@ -469,3 +469,38 @@ def sampled_takes(w_dir, grel, gcount, budget, seed, b, l, src, is_inv):
                             ctypes.c_int64(budget), ctypes.c_int64(seed), ctypes.c_int64(b), ctypes.c_int64(l),
                             ctypes.c_int64(src), ctypes.c_int(int(bool(is_inv))), _p(take))
     return take[:grel.size]
+
+
+def _splitmix64(z):
+    """SplitMix64 output function (Steele, Lea and Flood, OOPSLA 2014) on uint64 arrays."""
+    z = np.asarray(z, dtype=np.uint64)
+    with np.errstate(over="ignore"):
+        z = z + np.uint64(0x9E3779B97F4A7C15)
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+    return z ^ (z >> np.uint64(31))
+
+
+def value_dropout(x, p, seed, counter=0, subseq=0):
+    """nn.Dropout(p) on hop values (src/model_DRUM_kernel_sp.py:189-192) with
+    the library's counter-based keep bits; returns (y, keep).
+
+    key = splitmix64(seed ^ splitmix64((counter << 16) | subseq)); entry i is
+    kept iff (splitmix64(key + i) >> 32) >= floor(p * 2^32); kept entries are
+    x * float32(1 / float32(1 - p)) (torch's rounding of the scale), dropped
+    ones x * 0.  The
+    reference draws its mask from torch's generator, so parity with it is in
+    distribution (keep rate 1 - p, the scale, the gradient through the same
+    mask), and bit-exact against this restatement."""
+    x = np.asarray(x, dtype=np.float32).reshape(-1)
+    p = float(p)
+    m64 = (1 << 64) - 1
+    off = _splitmix64(np.array([((int(counter) << 16) | int(subseq)) & m64], dtype=np.uint64))
+    key = _splitmix64(np.array([int(seed) & m64], dtype=np.uint64) ^ off)
+    with np.errstate(over="ignore"):
+        h = _splitmix64(key + np.arange(x.size, dtype=np.uint64))
+    cut = (1 << 32) if p >= 1.0 else int(p * 4294967296.0)
+    keep = (h >> np.uint64(32)) >= np.uint64(cut)
+    scale = np.float32(0.0) if p >= 1.0 else np.float32(1.0 / float(np.float32(1.0 - p)))
+    y = (x * np.where(keep, scale, np.float32(0.0))).astype(np.float32)  # dropped: x * 0, as in torch
+    return y, keep

@@ -1,0 +1,62 @@
+"""Dropout of hop values (nn.Dropout on s.values(), src/model_DRUM_kernel_sp.py:189-192)
+on the GPU: fl_value_dropout bit-exact against the oracle's keep bits, the
+live-count and in-place forms, the autograd op and the sparse-state helper."""
+import numpy as np
+import pytest
+import torch
+
+from helpers import O
+
+pytestmark = pytest.mark.gpu
+
+
+def _x(n, seed=0):
+    return np.random.default_rng(seed).standard_normal(n).astype(np.float32)
+
+
+@pytest.mark.parametrize("p", [0.0, 0.1, 0.5, 0.9, 1.0])
+def test_value_dropout_matches_oracle(p):
+    from flashlog_b200 import ops
+    x = _x(100_003)
+    seed, counter, subseq = (1 << 63) + 5, 7, 2
+    y = ops.value_dropout(torch.from_numpy(x).cuda(), p, seed, torch.tensor([counter], device="cuda"), subseq)
+    want, _ = O.value_dropout(x, p, seed, counter, subseq)
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), want.view(np.uint32))
+
+
+def test_value_dropout_live_count_in_place_and_errors():
+    from flashlog_b200 import ops
+    x = _x(10_000, 1)
+    xd = torch.from_numpy(x).cuda()
+    live = torch.tensor([6_001], device="cuda")
+    ops.value_dropout(xd, 0.3, 11, None, 4, live=live, out=xd)
+    want, _ = O.value_dropout(x, 0.3, 11, 0, 4)
+    got = xd.cpu().numpy()
+    assert np.array_equal(got[:6_001], want[:6_001]) and np.array_equal(got[6_001:], x[6_001:])
+    with pytest.raises(ValueError):
+        ops.value_dropout(xd, 1.5, 0)
+    with pytest.raises(ValueError):
+        ops.value_dropout(xd, 0.1, 0, None, 1 << 16)
+    with pytest.raises(ValueError):
+        ops.value_dropout(xd.double(), 0.1, 0)
+
+
+def test_sparse_dropout_autograd():
+    """Values and the gradient (the upstream gradient through the same keep
+    bits and scale) against the oracle; indices unchanged; identity outside
+    training."""
+    from flashlog_b200.dropout import sparse_dropout
+    rng = np.random.default_rng(2)
+    B, L, E, nnz = 4, 3, 500, 900
+    key = np.unique(rng.integers(0, B * L * E, nnz))
+    idx = torch.from_numpy(np.stack([key // (L * E), (key // E) % L, key % E])).cuda()
+    v = torch.from_numpy(_x(key.size, 3)).cuda().requires_grad_(True)
+    s = torch.sparse_coo_tensor(idx, v, (B, L, E), is_coalesced=True)
+    assert sparse_dropout(s, 0.2, training=False) is s
+    y = sparse_dropout(s, 0.2, seed=17, counter=3, subseq=1)
+    assert torch.equal(y.indices(), s.indices())
+    want, keep = O.value_dropout(v.detach().cpu().numpy(), 0.2, 17, 3, 1)
+    assert np.array_equal(y.values().detach().cpu().numpy(), want)
+    g = _x(key.size, 4)
+    (y.values() * torch.from_numpy(g).cuda()).sum().backward()
+    assert np.array_equal(v.grad.cpu().numpy(), O.value_dropout(g, 0.2, 17, 3, 1)[0])

@@ -272,6 +272,47 @@ def test_sum_norm_errors_and_own_outputs(fk, g1):
     assert torch.equal(y2.values(), y3.values())
 
 
+def test_sum_norm_keeps_explicit_zeros_past_rows_times_c1(fk, g1):
+    """A row with at most c1 nonzero values keeps all its entries, explicit
+    zeros included (flashlog_kernel.py:1114-1117).  Here the kept total is
+    far above rows * c1, so the operator's sync-free selection overflows and
+    selects again at the input's size: outputs and gradients against the
+    oracle."""
+    cfg, train, csr_np, csr = g1
+    E, R = cfg.entities, cfg.relations
+    n = 2 * R + 1
+    rng = np.random.default_rng(21)
+    B, L, c1 = 2, 3, 6
+    rows_, ents, vals = [], [], []
+    for r in range(B * L):
+        k = 30
+        e = np.sort(rng.choice(E, k, replace=False))
+        v = rng.random(k).astype(np.float32) + 0.1
+        nz = 12 if r % 3 == 0 else 4  # rows 0 and 3 are over the limit; the others keep all 30 entries
+        v[rng.permutation(k)[nz:]] = 0
+        rows_.append(np.full(k, r))
+        ents.append(e)
+        vals.append(v)
+    row = np.concatenate(rows_).astype(np.int64)
+    ent = np.concatenate(ents).astype(np.int64)
+    val = np.concatenate(vals).astype(np.float32)
+    w = _w(rng, B, L, n, False)
+    mask = rng.random(train.shape[0]) > 0.15
+    sp, v = _sp(row, ent, val, B, L, E, requires_grad=True)
+    wt = _cuda(w).requires_grad_(True)
+    y = fk.vectorized_operation_sparse3d_csr_sum_norm(sp, wt, csr, _cuda(mask), R, use_topk=True, topk_edges=4,
+                                                      topk_nodes=c1)
+    h = oracle_hop_norm(row, ent, val, w, csr_np, R, E, 4, True, c1, mask, False, mode=O.MODE_TOPK)
+    assert h["sel"].size > B * L * c1
+    assert np.array_equal(_keys(y, L, E), h["fw"]["out_key"])
+    np.testing.assert_allclose(y.values().detach().cpu().numpy(), h["y"], rtol=RTOL, atol=0)
+    g = rng.standard_normal(h["y"].size).astype(np.float32)
+    (y.values() * _cuda(g)).sum().backward()
+    gv, gw = oracle_hop_norm_backward(h, g, row, val, w, R)
+    np.testing.assert_allclose(v.grad.cpu().numpy(), gv, rtol=RTOL, atol=1e-6)
+    np.testing.assert_allclose(wt.grad.cpu().numpy(), gw, rtol=RTOL, atol=1e-6)
+
+
 def test_drum3_dropin_chain_matches_reference_golden(fk, g1, golden):
     """Three chained drop-in sum+normalize hops, as the reference model calls
     them, and the readout loss: outputs, loss and logits gradient against the

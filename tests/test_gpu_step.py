@@ -27,8 +27,10 @@ def setup():
     return cfg, train, Graph.of(csr)
 
 
-@pytest.mark.parametrize("c1,c2", [(40, 16), (None, 0), (5, 6)])
-def test_static_step_matches_autograd_engine(setup, c1, c2):
+@pytest.mark.parametrize("c1,c2,dropout", [(40, 16, 0.0), (None, 0, 0.0), (5, 6, 0.0), (40, 16, 0.1)])
+def test_static_step_matches_autograd_engine(setup, c1, c2, dropout):
+    """With dropout, the step's first replay (counter 1) and the engine with
+    dropout_counter=1 draw the same keep bits per hop."""
     from flashlog_b200 import engine
     from flashlog_b200.step import DrumTrainStep
     from flashlog_b200.synthetic import training_queries
@@ -46,11 +48,13 @@ def test_static_step_matches_autograd_engine(setup, c1, c2):
     tab = table.clone().requires_grad_(True)
     mask = torch.ones(train.shape[0], dtype=torch.uint8, device=dev)
     mask[d(ids)] = 0
-    rp, ent, val = engine.drum_propagate(d(h), tab[d(r)], graph, R, c1=c1, c2=c2, mask_triple=mask)
+    rp, ent, val = engine.drum_propagate(d(h), tab[d(r)], graph, R, c1=c1, c2=c2, mask_triple=mask,
+                                         dropout=dropout, dropout_seed=5, dropout_counter=1)
     loss = engine.readout_loss(rp, ent, val, d(t), N)
     loss.backward()
     # static step
-    step = DrumTrainStep(graph, R, Q, T, N, c1, c2, table.clone(), n_hide=ids.size, apply_update=False)
+    step = DrumTrainStep(graph, R, Q, T, N, c1, c2, table.clone(), n_hide=ids.size, apply_update=False,
+                         dropout=dropout, dropout_seed=5)
     step.load(d(h), d(t), d(r), d(ids))
     sloss = step.run()
     torch.cuda.synchronize()
@@ -66,7 +70,10 @@ def test_static_step_matches_autograd_engine(setup, c1, c2):
     assert int(step.vis[0].min()) == 1 and int(step.vis[1].min()) == 1
 
 
-def test_static_step_replays_as_cuda_graph(setup):
+@pytest.mark.parametrize("dropout", [0.0, 0.1])
+def test_static_step_replays_as_cuda_graph(setup, dropout):
+    """Replays equal eager runs; with dropout, replay k draws the masks of
+    eager run k (the device counter advances inside the graph)."""
     from flashlog_b200.step import DrumTrainStep
     from flashlog_b200.synthetic import training_queries
     cfg, train, graph = setup
@@ -80,12 +87,12 @@ def test_static_step_replays_as_cuda_graph(setup):
     for s in range(3):
         ids, h, r, t = training_queries(train, cfg, step=10 + s)
         batches.append((d(ids[:8]), d(h[:16]), d(r[:16]), d(t[:16])))
-    eager = DrumTrainStep(graph, R, 16, T, N, 40, 16, table.clone(), n_hide=8, apply_update=False)
+    eager = DrumTrainStep(graph, R, 16, T, N, 40, 16, table.clone(), n_hide=8, apply_update=False, dropout=dropout)
     ref = []
     for ids, h, r, t in batches:
         eager.load(h, t, r, ids)
         ref.append((float(eager.run()), eager.grad.clone()))
-    step = DrumTrainStep(graph, R, 16, T, N, 40, 16, table.clone(), n_hide=8, apply_update=False)
+    step = DrumTrainStep(graph, R, 16, T, N, 40, 16, table.clone(), n_hide=8, apply_update=False, dropout=dropout)
     ids, h, r, t = batches[0]
     side = torch.cuda.Stream()
     side.wait_stream(torch.cuda.current_stream())
@@ -96,6 +103,7 @@ def test_static_step_replays_as_cuda_graph(setup):
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
         step.run()
+    step.drop_counter.zero_()  # the warm-up run counted once
     for (ids, h, r, t), (l_ref, g_ref) in zip(batches, ref):
         step.load(h, t, r, ids)
         g.replay()

@@ -58,6 +58,11 @@ def test_cpu_tensors_are_rejected():
         fk.vectorized_operation_sparse3d_csr_sum_norm(sp, w, csr, torch.ones(1, dtype=torch.bool), 1)
     with pytest.raises(ValueError):
         fk.vectorized_operation_sparse3d_fixed_relation(sp, torch.zeros(1, 1, dtype=torch.long), csr, 1)
+    from flashlog_b200 import dropout, ops
+    with pytest.raises(ValueError):
+        ops.value_dropout(torch.ones(8), 0.1, 0)
+    with pytest.raises(ValueError):
+        dropout.sparse_dropout(sp, 0.1, seed=1)
 
 
 def test_exports_match_reference_names():

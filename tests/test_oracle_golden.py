@@ -226,3 +226,29 @@ def test_filter_indices_oracle_matches_reference_golden(golden):
     E = cfg.entities
     b, e = O.filter_indices(d["qx"], d["qr"], cfg.relations, csr_np)
     assert np.array_equal(np.sort(b * E + e), np.sort(d["csr_batch"] * E + d["csr_entity"]))
+
+
+def test_dropout_oracle_keep_bits_and_torch_semantics():
+    """The oracle's SplitMix64 against the published seed-0 sequence, and the
+    dropout restatement against nn.Dropout's semantics (keep rate, torch's
+    scale, x * 0 for dropped entries)."""
+    import torch
+    g = 0x9E3779B97F4A7C15
+    seq = [int(O._splitmix64(np.array([(k * g) % (1 << 64)], np.uint64))[0]) for k in range(4)]
+    assert seq == [0xE220A8397B1DCDAF, 0x6E789E6AA1B965F4, 0x06C45D188009454F, 0xF88BB8A8724C81EC]
+    x = np.random.default_rng(5).standard_normal(200_000).astype(np.float32)
+    for p in (0.1, 0.123, 0.5, 0.9):
+        y, keep = O.value_dropout(x, p, seed=3, counter=1, subseq=2)
+        n = x.size
+        assert abs(keep.mean() - (1 - p)) < 5 * np.sqrt(p * (1 - p) / n)
+        t = torch.nn.functional.dropout(torch.ones(4096), p, training=True)
+        scale = float(t[t != 0][0])
+        assert np.array_equal(y[keep], x[keep] * np.float32(scale))
+        assert np.array_equal(np.signbit(y[~keep]), np.signbit(x[~keep])) and not y[~keep].any()
+    assert np.array_equal(O.value_dropout(x, 0.0, 1)[0], x)
+    assert not O.value_dropout(x, 1.0, 1)[0].any()
+    # masks differ across counters and sub-sequences, and repeat for the same arguments
+    k0 = O.value_dropout(x, 0.5, 9, 1, 0)[1]
+    assert np.array_equal(k0, O.value_dropout(x, 0.5, 9, 1, 0)[1])
+    assert not np.array_equal(k0, O.value_dropout(x, 0.5, 9, 2, 0)[1])
+    assert not np.array_equal(k0, O.value_dropout(x, 0.5, 9, 1, 1)[1])
