@@ -107,6 +107,8 @@ SIGNATURES = {
     "fl_hop_stats": (ctypes.c_int, [_P, _I64, _P, _I64, _SIDE, _SIDE, _P, _P, ctypes.c_int, _P, _P]),
     "fl_rule_max_reduce": (ctypes.c_int, [_P, _I64, _P, _P, _I64, _P, _I64, _I64, _I64, _P, _P]),
     "fl_scatter_grad": (ctypes.c_int, [_P, _P, _I64, _P, _P, _I64, _P, _P]),
+    "fl_edge_weight_grad": (ctypes.c_int, [_PARAMS, _P, _P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                           _P]),
     "fl_readout": (ctypes.c_int, [_P, _P, _P, _I64, _P, _I64, _P, _P]),
     "fl_readout_backward": (ctypes.c_int, [_P, _P, _I64, _P, _I64, _P, _P, _I64, _P, _P]),
     "fl_value_dropout": (ctypes.c_int, [_P, _P, _I64, _P, ctypes.c_double, ctypes.c_uint64, _P, ctypes.c_uint64,

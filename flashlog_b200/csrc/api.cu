@@ -256,6 +256,15 @@ int fl_hop_stats(const int64_t *row_ptr, int64_t rows, const int32_t *ent, int64
     return hop_stats(row_ptr, rows, ent, S, ori, inv, entry_count, out_row_ptr, wot_i, acc, as_stream(stream));
 }
 
+int fl_edge_weight_grad(const fl_hop_params *p, const int64_t *row_ptr, const float *val, int64_t S, const float *w,
+                        const int64_t *slot_base, const int32_t *entry_count, const int32_t *fact_pos,
+                        const int16_t *fact_rel, const float *fact_m, const int32_t *fact_edge,
+                        const int64_t *out_row_ptr, const float *g, const float *edge_weight, float *grad_edge,
+                        fl_stream_t stream) {
+    return edge_weight_grad(p, row_ptr, val, S, w, slot_base, entry_count, fact_pos, fact_rel, fact_m, fact_edge,
+                            out_row_ptr, g, edge_weight, grad_edge, as_stream(stream));
+}
+
 int fl_scatter_grad(const float *grad_sel, const int64_t *src_index, int64_t n_sel, const int64_t *n_live,
                     float *grad_full, int64_t n_full, const int64_t *full_live, fl_stream_t stream) {
     return scatter_grad(grad_sel, src_index, n_sel, n_live, grad_full, n_full, full_live, as_stream(stream));

@@ -1987,6 +1987,41 @@ __global__ void hop_stats_kernel(const int64_t *row_ptr, int64_t rows, const int
     }
 }
 
+// Gradient of learnable edge weights (flashlog_kernel.py:1306-1336 for SUM,
+// 1590-1614 for MAX): every edge fact f of a live entry that reached an
+// output (fact_pos >= 0, the position within its row's outputs) adds
+// g[out_row_ptr[row] + fact_pos] * v * w[row, rel] * m * (1 - sigmoid(ew)) to
+// grad_edge[triple id].  One warp per entry, lanes over its facts; the
+// identity fact (rel = n - 1) has no edge.  Float atomics, as the
+// reference's index_add_.
+__global__ void edge_weight_grad_kernel(const int64_t *row_ptr, int64_t rows, int64_t n, const float *val, int64_t S,
+                                        const float *w, const int64_t *slot_base, const int32_t *entry_count,
+                                        const int32_t *fact_pos, const int16_t *fact_rel, const float *fact_m,
+                                        const int32_t *fact_edge, const int64_t *out_row_ptr, const float *g,
+                                        const float *edge_weight, float *grad_edge) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+    const int64_t nw = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+    const int64_t S_live = row_ptr[rows] < S ? row_ptr[rows] : S;
+    for (int64_t i = warp; i < S_live; i += nw) {
+        const int64_t row = find_row(row_ptr, rows, i);
+        const float v = val[i];
+        const float *wrow = w + row * n;
+        const float *grow = g + out_row_ptr[row];
+        const int64_t f0 = slot_base[i];
+        const int32_t cnt = entry_count[i];
+        for (int32_t k = lane; k < cnt; k += 32) {
+            const int64_t f = f0 + k;
+            const int32_t rel = fact_rel[f];
+            const int32_t pos = fact_pos[f];
+            if (rel >= n - 1 || pos < 0) continue;
+            const int32_t e = fact_edge[f];
+            const float score = 1.0f / (1.0f + expf(-edge_weight[e]));
+            atomicAdd(grad_edge + e, grow[pos] * v * wrow[rel] * fact_m[f] * (1.0f - score));
+        }
+    }
+}
+
 // x[0, min(n, *live)) = 0, grid-stride.
 __global__ void zero_prefix_kernel(float *x, int64_t n, const int64_t *live) {
     const int64_t m = *live < n ? *live : n;
@@ -2448,6 +2483,25 @@ int hop_stats(const int64_t *row_ptr, int64_t rows, const int32_t *ent, int64_t 
     launch(hop_stats_kernel, static_cast<unsigned>(blocks), 256, 0, st, row_ptr, rows, ent, S, make_side(ori, nullptr),
            make_side(inv, nullptr), entry_count, out_row_ptr, wot_i, reinterpret_cast<unsigned long long *>(acc));
     return check_launch("hop_stats");
+}
+
+int edge_weight_grad(const fl_hop_params *p, const int64_t *row_ptr, const float *val, int64_t S, const float *w,
+                     const int64_t *slot_base, const int32_t *entry_count, const int32_t *fact_pos,
+                     const int16_t *fact_rel, const float *fact_m, const int32_t *fact_edge,
+                     const int64_t *out_row_ptr, const float *g, const float *edge_weight, float *grad_edge,
+                     cudaStream_t st) {
+    FL_REQUIRE(p != nullptr && S >= 0, "edge_weight_grad: bad arguments");
+    FL_REQUIRE(slot_base && entry_count && fact_pos && fact_rel && fact_m && fact_edge && out_row_ptr && g &&
+                   edge_weight && grad_edge,
+               "edge_weight_grad needs the recorded facts (positions, relations, masks, triple ids)");
+    if (S == 0) return FL_OK;
+    const int sms = fl_device_sm_count();
+    int64_t blocks = (S + 7) / 8;
+    const int64_t cap = static_cast<int64_t>(sms > 0 ? sms : 148) * 8;
+    if (blocks > cap) blocks = cap;
+    launch(edge_weight_grad_kernel, static_cast<unsigned>(blocks), 256, 0, st, row_ptr, p->rows, p->n, val, S, w,
+           slot_base, entry_count, fact_pos, fact_rel, fact_m, fact_edge, out_row_ptr, g, edge_weight, grad_edge);
+    return check_launch("edge_weight_grad");
 }
 
 int zero_prefix(float *x, int64_t n, const int64_t *live, cudaStream_t st) {

@@ -36,6 +36,11 @@ int normalize_forward(const int64_t *row_ptr, const float *x, int64_t rows, floa
 int normalize_backward(const int64_t *row_ptr, const float *x, const float *denom, const float *g, int64_t rows,
                        float eps, float *gx, cudaStream_t st);
 int zero_prefix(float *x, int64_t n, const int64_t *live, cudaStream_t st);
+int edge_weight_grad(const fl_hop_params *p, const int64_t *row_ptr, const float *val, int64_t S, const float *w,
+                     const int64_t *slot_base, const int32_t *entry_count, const int32_t *fact_pos,
+                     const int16_t *fact_rel, const float *fact_m, const int32_t *fact_edge,
+                     const int64_t *out_row_ptr, const float *g, const float *edge_weight, float *grad_edge,
+                     cudaStream_t st);
 int hop_stats(const int64_t *row_ptr, int64_t rows, const int32_t *ent, int64_t S, const fl_csr_side &ori,
               const fl_csr_side &inv, const int32_t *entry_count, const int64_t *out_row_ptr, int wot_i, int64_t *acc,
               cudaStream_t st);

@@ -45,15 +45,42 @@ def device_counter(value: int, device) -> torch.Tensor:
     return torch.full((1,), int(value), dtype=torch.int64, device=device)
 
 
+class SparseValueDropout(torch.autograd.Function):
+    """Dropout of a coalesced sparse state's values as one node: the output
+    shares the input's index tensor, and the backward hands back a sparse
+    gradient on that same index tensor.  A gradient that arrives on the
+    output's own indices (as the next hop's gives it) aligns without a sort,
+    and torch's generic sparse-constructor backward (a coalesce and a
+    masked projection of the gradient) never runs."""
+
+    @staticmethod
+    def forward(ctx, s, p, seed, counter, subseq):
+        idx = s._indices()
+        ctx.args = (float(p), int(seed), counter, int(subseq))
+        ctx.idx, ctx.shape = idx, s.shape
+        val = ops.value_dropout(s._values().detach(), p, seed, counter, subseq)
+        return torch.sparse_coo_tensor(idx, val, s.shape, is_coalesced=True)
+
+    @staticmethod
+    def backward(ctx, g):
+        p, seed, counter, subseq = ctx.args
+        B, Lch, E = ctx.shape
+        gv = _fk._align_sparse_grad_to_output(g, ctx.idx, Lch, E).to(torch.float32)
+        gx = ops.value_dropout(gv, p, seed, counter, subseq)
+        return torch.sparse_coo_tensor(ctx.idx, gx, ctx.shape, is_coalesced=True), None, None, None, None
+
+
 def sparse_dropout(s: torch.Tensor, p: float, training: bool = True, seed: int | None = None, counter: int = 0,
                    subseq: int = 0) -> torch.Tensor:
-    """The models' value dropout of a coalesced sparse state (identity outside training or for p = 0)."""
+    """The models' value dropout of a coalesced sparse [B, L, E] state
+    (identity outside training or for p = 0)."""
     if not training or p == 0.0:
         return s
     s = s if s.is_coalesced() else s.coalesce()
+    if s.dim() != 3:
+        raise ValueError("sparse_dropout takes a [B, L, E] state")
     seed = draw_seed() if seed is None else seed
-    val = ValueDropout.apply(s.values(), p, seed, device_counter(counter, s.device), subseq, None)
-    out = torch.sparse_coo_tensor(s.indices(), val, s.shape, is_coalesced=True)
+    out = SparseValueDropout.apply(s, p, seed, device_counter(counter, s.device), subseq)
     if _fk._is_own_output(s):
         _fk._mark_own_output(out)  # the same indices, written by the library: the next hop trusts them
     return out

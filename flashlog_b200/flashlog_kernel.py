@@ -356,16 +356,16 @@ class FlashLogFunctionSparse3DTopKSum(autograd.Function):
         wf = w.detach().to(torch.float32).contiguous()
         _check_w(wf)
         seed = int(torch.randint(0, 2 ** 63 - 1, ()).item()) if sampling else -1
+        learn_ew = weight is not None and bool(getattr(weight, "requires_grad", False))
         fw = ops.hop_forward(row_ptr, ent, val, wf, graph, r_size, int(topk_edges),
                              _topk_flags(weight, edge_weight_is_score, sampling, wot_i),
                              mask_triple=mask_values, edge_weight=None if weight is None else weight.detach(),
-                             seed=seed)
+                             seed=seed, record_edge=learn_ew)
         _kernel_log("sparse3d_topk_sum.cuda_forward", t0)
         ctx.fw = fw
         ctx.save_for_backward(row_ptr, val, wf)
         ctx.B, ctx.L, ctx.E = B, L_, E
-        if weight is not None and bool(getattr(weight, "requires_grad", False)):
-            raise NotImplementedError("learnable edge weights (--use_soft) are not supported by flashlog_b200 yet")
+        ctx.edge_weight = weight.detach() if learn_ew else None
         out = _coo(fw.out_row_ptr, fw.out_ent, fw.out_x, B, L_, E)
         ctx.out_indices = out.indices()
         return out
@@ -375,9 +375,19 @@ class FlashLogFunctionSparse3DTopKSum(autograd.Function):
         row_ptr, val, wf = ctx.saved_tensors
         g = _align_sparse_grad_to_output(grad_out, ctx.out_indices, ctx.L, ctx.E).to(torch.float32)
         grad_val, grad_w = ops.hop_backward(ctx.fw, row_ptr, val, wf, g, normalize=False)
+        grad_ew = _edge_weight_grad(ctx, row_ptr, val, wf, g)
         grad_val = _restore(ctx, grad_val)
-        grads = (None, None, None, grad_val, grad_w) + (None,) * 28
+        grads = (None, None, None, grad_val, grad_w) + (None,) * 17 + (grad_ew,) + (None,) * 10
         return grads[:len(ctx.needs_input_grad)]
+
+
+def _edge_weight_grad(ctx, row_ptr, val, wf, g):
+    """Gradient of the learnable edge weights (argument 22 of the top-k
+    operators), or None when they take none (flashlog_kernel.py:1306-1336,
+    1590-1614)."""
+    if ctx.edge_weight is None:
+        return None
+    return ops.edge_weight_grad(ctx.fw, row_ptr, val, wf, g, ctx.edge_weight)
 
 
 class FlashLogFunctionSparse3DAllEdgesSum(autograd.Function):
@@ -629,15 +639,15 @@ class FlashLogFunctionSparse3DTopKMax(autograd.Function):
         _check_w(wf)
         seed = int(torch.randint(0, 2 ** 63 - 1, ()).item()) if sampling else -1
         flags = _topk_flags(weight, edge_weight_is_score, sampling, wot_i) & ~L.FL_DROP_MASKED
+        learn_ew = weight is not None and bool(getattr(weight, "requires_grad", False))
         fw = ops.hop_forward(row_ptr, ent, val, wf, graph, r_size, int(topk_edges), flags,
                              mask_triple=mask_values, edge_weight=None if weight is None else weight.detach(),
-                             seed=seed, reduce="max")
+                             seed=seed, reduce="max", record_edge=learn_ew)
         _kernel_log("sparse3d_topk_max.cuda_forward", t0)
         ctx.fw = fw
         ctx.save_for_backward(row_ptr, val, wf)
         ctx.B, ctx.L, ctx.E = B, L_, E
-        if weight is not None and bool(getattr(weight, "requires_grad", False)):
-            raise NotImplementedError("learnable edge weights (--use_soft) are not supported by flashlog_b200 yet")
+        ctx.edge_weight = weight.detach() if learn_ew else None
         out = _coo(fw.out_row_ptr, fw.out_ent, fw.out_x, B, L_, E)
         ctx.out_indices = out.indices()
         return out
@@ -647,8 +657,9 @@ class FlashLogFunctionSparse3DTopKMax(autograd.Function):
         row_ptr, val, wf = ctx.saved_tensors
         g = _align_sparse_grad_to_output(grad_out, ctx.out_indices, ctx.L, ctx.E).to(torch.float32)
         grad_val, grad_w = ops.hop_backward(ctx.fw, row_ptr, val, wf, g, normalize=False)
+        grad_ew = _edge_weight_grad(ctx, row_ptr, val, wf, g)  # winning facts only (fact_pos -1 elsewhere)
         grad_val = _restore(ctx, grad_val)
-        grads = (None, None, None, grad_val, grad_w) + (None,) * 28
+        grads = (None, None, None, grad_val, grad_w) + (None,) * 17 + (grad_ew,) + (None,) * 10
         return grads[:len(ctx.needs_input_grad)]
 
 

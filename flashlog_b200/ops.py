@@ -205,6 +205,7 @@ class HopForward:
     n_facts_slots: int
     fact_dst: torch.Tensor | None = None
     fact_val: torch.Tensor | None = None
+    fact_edge: torch.Tensor | None = None  # triple id per fact (record_edge)
 
 
 def hop_params(rows, Lch, n, r_size, E, topk_edges, flags, seed=-1, eps=EPS, slot_capacity=0, status=None,
@@ -255,7 +256,7 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
                 keep_facts: bool = False, record: bool = True, timing=None, slot_capacity=None,
                 status=None, out_sync: bool = True, vis=None, reduce: str = "sum",
                 max_bits: bool = False, rank_select: bool = True, check_w: bool = False,
-                sel_status=None) -> HopForward:
+                sel_status=None, record_edge: bool = False) -> HopForward:
     """Expansion + per-row coalesce-sum + normalization of one hop.
 
     slot_capacity=None sizes the fact buffers exactly (one host sync for the
@@ -277,6 +278,8 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
     expansion, read in the same host sync as the fact count.  sel_status (with
     check_w): the status word of the c1 selection that produced the state,
     read in that sync too; SelectionOverflow is raised when it is set.
+    record_edge keeps the triple id of every fact (fact_edge) for
+    edge_weight_grad.
     """
     if reduce not in ("sum", "max"):
         raise ValueError("reduce must be 'sum' or 'max'")
@@ -348,12 +351,16 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
         if mask_triple.numel() < M:
             raise ValueError("edge visibility mask must have one entry per triple")
     if edge_weight is not None:
+        if mask_triple is None:
+            # the multiplier is mask[triple] * sigmoid(edge_weight[triple]): the
+            # weights are read through the triple-indexed mask
+            raise ValueError("edge weights need the triple-indexed mask (mask_values)")
         edge_weight = edge_weight.reshape(-1).to(torch.float32).contiguous()
         if edge_weight.numel() < M:
             raise ValueError("edge weights must have one entry per triple")
     fact_pos = torch.empty(T, dtype=torch.int32, device=dev) if (record or reduce == "max") else None
     fact_edge = None
-    if reduce == "max":
+    if reduce == "max" or record_edge:
         fact_edge = torch.empty(T, dtype=torch.int32, device=dev)
         params.fact_edge = fact_edge.data_ptr()
     out_row_ptr = torch.empty(rows + 1, dtype=torch.int64, device=dev)
@@ -386,7 +393,8 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
     return HopForward(params, slot_base, entry_count, fact_rel, fact_m, fact_pos, out_row_ptr, out_ent[:u],
                       out_x[:u], None if reduce == "max" else out_y[:u],
                       None if reduce == "max" else out_denom[:rows], total.value,
-                      fact_dst if keep_facts else None, fact_val if keep_facts else None)
+                      fact_dst if keep_facts else None, fact_val if keep_facts else None,
+                      fact_edge if record_edge else None)
 
 
 def hop_backward(fw: HopForward, row_ptr, val, w, g_y, normalize: bool = True):
@@ -407,6 +415,23 @@ def hop_backward(fw: HopForward, row_ptr, val, w, g_y, normalize: bool = True):
                                 _p(fw.out_row_ptr), _p(fw.out_x), _p(fw.out_denom), _p(g_y), _p(grad_val),
                                 _p(grad_w), _p(ws), ws.numel(), _stream()), "hop_backward")
     return grad_val[:S], grad_w.view(B, Lch, n)
+
+
+def edge_weight_grad(fw: HopForward, row_ptr, val, w, g_x, edge_weight):
+    """d loss / d edge_weight of a top-k hop with learnable edge weights
+    (flashlog_kernel.py:1306-1336, 1590-1614); g_x is the gradient at the
+    outputs (the MAX outputs, or the sums before normalization).  The forward
+    must have run with the edge weights and record_edge=True."""
+    if fw.fact_edge is None or fw.fact_m is None or fw.fact_pos is None:
+        raise ValueError("edge_weight_grad needs a forward recorded with edge weights and record_edge=True")
+    ew = edge_weight.detach().reshape(-1).to(torch.float32).contiguous()
+    grad = torch.zeros_like(ew)
+    check(lib().fl_edge_weight_grad(ctypes.byref(fw.params), _p(row_ptr), _p(val), val.numel(), _p(w.contiguous()),
+                                    _p(fw.slot_base), _p(fw.entry_count), _p(fw.fact_pos), _p(fw.fact_rel),
+                                    _p(fw.fact_m), _p(fw.fact_edge), _p(fw.out_row_ptr),
+                                    _p(g_x.to(torch.float32).contiguous()), _p(ew), _p(grad), _stream()),
+          "edge_weight_grad")
+    return grad.view_as(edge_weight)
 
 
 def scatter_grad(grad_sel, src_index, n_full: int, n_live=None, full_live=None):

@@ -247,6 +247,22 @@ int fl_hop_stats(const int64_t *row_ptr, int64_t rows, const int32_t *ent, int64
                  fl_csr_side inv, const int32_t *entry_count, const int64_t *out_row_ptr, int wot_i, int64_t *acc,
                  fl_stream_t stream);
 
+/* Gradient of learnable edge weights (the --use_soft path): replaces the
+ * chunk loops of flashlog_kernel.py:1306-1336 (SUM) and 1590-1614 (MAX).
+ * Every edge fact f of the first min(S, row_ptr[rows]) entries with
+ * fact_pos[f] >= 0 (its position within its row's outputs) adds
+ *   g[out_row_ptr[r] + fact_pos[f]] * val[i] * w[r, fact_rel[f]] * fact_m[f] * (1 - sigmoid(edge_weight[e]))
+ * to grad_edge[e], r = row(i), e = fact_edge[f] (the triple id).  The facts
+ * are those fl_hop_expand recorded with fact_m and fact_edge and the row
+ * reduction placed (fact_pos, out_row_ptr); g is the gradient at the outputs
+ * (before any normalization); the identity fact has no edge.  grad_edge is
+ * accumulated (zero it first) with float atomics. */
+int fl_edge_weight_grad(const fl_hop_params *p, const int64_t *row_ptr, const float *val, int64_t S, const float *w,
+                        const int64_t *slot_base, const int32_t *entry_count, const int32_t *fact_pos,
+                        const int16_t *fact_rel, const float *fact_m, const int32_t *fact_edge,
+                        const int64_t *out_row_ptr, const float *g, const float *edge_weight, float *grad_edge,
+                        fl_stream_t stream);
+
 /* grad_full[src_index[j]] = grad_sel[j] for j < n_sel (and j < *n_live when
  * n_live, a device count, is given), zeros elsewhere: all of grad_full[0,
  * n_full), or only its first *full_live entries when full_live (a device

@@ -131,11 +131,12 @@ def csr_masks(csr, mask, edge_weight=None):
 
 
 def hop_forward(row, ent, val, w, csr, r_size, E, topk_edges=1 << 60, mode=MODE_TOPK,
-                mask=None, edge_weight=None, wot_i=False, sampling_seed=-1, record=True):
+                mask=None, edge_weight=None, wot_i=False, sampling_seed=-1, record=True, record_edges=False):
     """One propagation hop with coalesce-sum; returns a dict of numpy arrays.
 
     out_key = row * E + e (sorted), out_val = pre-normalization sums, and the
-    per-fact provenance (entry, relation column, m, output position).
+    per-fact provenance (entry, relation column, m, output position; with
+    record_edges also the triple id, fact_edge).
     """
     row, ent, val = _c(row, np.int64), _c(ent, np.int64), _c(val, np.float32)
     w = _c(w, np.float32)
@@ -168,23 +169,52 @@ def hop_forward(row, ent, val, w, csr, r_size, E, topk_edges=1 << 60, mode=MODE_
         f_out = np.empty(cap, np.int64)
     else:
         f_entry = f_rel = f_m = f_out = None
+    f_edge = np.empty(cap, np.int64) if (record and record_edges) else None
     nf = ctypes.c_int64(0)
     arrs = [_c(a, t) for a, t in ((ori_col, np.int32), (ori_order, np.int32), (ori_gptr, np.int32),
                                    (ori_grel, np.int16), (ori_gstart, np.int32), (ori_gcount, np.int32),
                                    (inv_col, np.int32), (inv_order, np.int32), (inv_gptr, np.int32),
                                    (inv_grel, np.int16), (inv_gstart, np.int32), (inv_gcount, np.int32))]
-    u = lib().flo_hop_forward(
+    u = lib().flo_hop_forward_edges(
         ctypes.c_int64(nnz), _p(row), _p(ent), _p(val), _p(w), ctypes.c_int64(L), ctypes.c_int64(n),
         ctypes.c_int64(E), ctypes.c_int64(r_size), *[_p(a) for a in arrs],
         _p(mo), _p(mi), _p(mask_triple), _p(ew), ctypes.c_int64(int(min(topk_edges, 1 << 62))),
         ctypes.c_int64(flags), ctypes.c_int64(sampling_seed),
-        _p(out_key), _p(out_val), _p(f_entry), _p(f_rel), _p(f_m), _p(f_out), ctypes.byref(nf))
+        _p(out_key), _p(out_val), _p(f_entry), _p(f_rel), _p(f_m), _p(f_out), _p(f_edge), ctypes.byref(nf))
     nf = nf.value
     res = dict(out_key=out_key[:u].copy(), out_val=out_val[:u].copy(), n_facts=nf)
     if record:
         res.update(fact_entry=f_entry[:nf].copy(), fact_rel=f_rel[:nf].copy(),
                    fact_m=f_m[:nf].copy(), fact_out=f_out[:nf].copy())
+        if f_edge is not None:
+            res["fact_edge"] = f_edge[:nf].copy()
     return res
+
+
+def edge_weight_grad(fw, g_out, row, val, w, edge_weight):
+    """Gradient of learnable edge weights (flashlog_kernel.py:1306-1336 for
+    SUM, 1590-1614 for MAX): every edge fact that reached an output
+    (fact_out >= 0; MAX records -1 for the facts that lost) adds
+    g_out[fact_out] * v * w[row, rel] * m * (1 - sigmoid(ew[edge])), the
+    product in fp32 in the reference's order, summed in float64 per triple.
+    fw: a forward recorded with record_edges (hop_forward_max records them)."""
+    row, val, w = _c(row, np.int64), _c(val, np.float32), _c(w, np.float32)
+    n = w.shape[-1]
+    ew = np.asarray(edge_weight, np.float32).reshape(-1)
+    f = (np.asarray(fw["fact_rel"]) < n - 1) & (np.asarray(fw["fact_out"]) >= 0)
+    e = fw["fact_entry"][f]
+    rel = fw["fact_rel"][f].astype(np.int64)
+    edge = fw["fact_edge"][f].astype(np.int64)
+    score = (np.float32(1) / (np.float32(1) + np.exp(-ew[edge]))).astype(np.float32)
+    wv = w.reshape(-1, n)[row[e], rel]
+    g = np.asarray(g_out, np.float32)[fw["fact_out"][f]]
+    c = (g * val[e]).astype(np.float32)
+    c = (c * wv).astype(np.float32)
+    c = (c * fw["fact_m"][f]).astype(np.float32)
+    c = (c * (np.float32(1) - score)).astype(np.float32)
+    grad = np.zeros(ew.size, np.float64)
+    np.add.at(grad, edge, c.astype(np.float64))
+    return grad
 
 
 def max_coalesce(keys, values, source, tie):
@@ -207,7 +237,8 @@ def max_coalesce(keys, values, source, tie):
     return keys[win], values[win], win
 
 
-def hop_forward_max(row, ent, val, w, csr, r_size, E, topk_edges=1 << 60, mask=None, wot_i=False):
+def hop_forward_max(row, ent, val, w, csr, r_size, E, topk_edges=1 << 60, mask=None, wot_i=False, edge_weight=None,
+                    edge_score=False):
     """One hop of FlashLogFunctionSparse3DTopKMax (flashlog_kernel.py:1450-1518):
     the top-k fill without the visibility filter (hidden edges give facts of
     value 0), then the MAX coalesce with exact winners.
@@ -222,10 +253,11 @@ def hop_forward_max(row, ent, val, w, csr, r_size, E, topk_edges=1 << 60, mask=N
     nnz = row.size
     ori_rp, ori_col, _, ori_order, inv_rp, inv_col, _, inv_order = csr[:8]
     ori_gptr, ori_grel, ori_gstart, ori_gcount, inv_gptr, inv_grel, inv_gstart, inv_gcount = csr[8:]
-    flags = MODE_TOPK_MAX | (WOT_I if wot_i else 0)
+    flags = MODE_TOPK_MAX | (WOT_I if wot_i else 0) | (EDGE_SCORE if edge_score else 0)
     if mask is None:
         mask = np.ones(ori_col.size, np.uint8)
     mask_triple = _c(np.asarray(mask).reshape(-1) != 0, np.uint8)
+    ew = _c(edge_weight, np.float32).reshape(-1) if edge_weight is not None else None
     cap = max(int(lib().flo_fact_bound(ctypes.c_int64(nnz), _p(ent), _p(_c(ori_rp, np.int32)),
                                         _p(_c(inv_rp, np.int32)))), 1)
     out_key = np.empty(cap, np.int64)
@@ -243,7 +275,7 @@ def hop_forward_max(row, ent, val, w, csr, r_size, E, topk_edges=1 << 60, mask=N
     u = lib().flo_hop_forward_edges(
         ctypes.c_int64(nnz), _p(row), _p(ent), _p(val), _p(w), ctypes.c_int64(L), ctypes.c_int64(n),
         ctypes.c_int64(E), ctypes.c_int64(r_size), *[_p(a) for a in arrs],
-        None, None, _p(mask_triple), None, ctypes.c_int64(int(min(topk_edges, 1 << 62))),
+        None, None, _p(mask_triple), _p(ew), ctypes.c_int64(int(min(topk_edges, 1 << 62))),
         ctypes.c_int64(flags), ctypes.c_int64(-1),
         _p(out_key), _p(out_val), _p(f_entry), _p(f_rel), _p(f_m), _p(f_out), _p(f_edge), ctypes.byref(nf))
     nf = nf.value

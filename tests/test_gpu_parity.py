@@ -185,6 +185,70 @@ def test_hop_topk_forward_backward(fk, g1, topk, ties, wot_i):
     np.testing.assert_allclose(wt.grad.cpu().numpy(), gw, rtol=RTOL, atol=1e-6)
 
 
+def _topk_apply(fn, sp, v, w, csr, mask, weight, R, topk, score):
+    """The reference's 33-argument positional call of a top-k operator."""
+    idx = sp.indices()
+    B, L, E = sp.shape
+    return fn.apply(idx[0], idx[1], idx[2], v, w, *csr, mask, weight, B, L, E, R, False, topk, score, None, True,
+                    False)
+
+
+@pytest.mark.parametrize("score", [False, True])
+@pytest.mark.parametrize("op", ["sum", "max"])
+def test_topk_learnable_edge_weights(fk, g1, op, score):
+    """Learnable edge weights (--use_soft): the forward multiplies each fact by
+    mask * sigmoid(ew) (or mask * ew for scores), and the weights' gradient
+    is the reference's g * v * w * m * (1 - sigmoid(ew)) per fact that reached
+    an output (flashlog_kernel.py:1306-1336; MAX: winners only, 1590-1614).
+    Against the oracle: outputs, and the gradients of values, w and ew."""
+    cfg, train, csr_np, csr = g1
+    E, R = cfg.entities, cfg.relations
+    n = 2 * R + 1
+    rng = np.random.default_rng(41 + 2 * int(score) + (op == "max"))
+    B, L, topk = 4, 3, 7
+    row, ent, val = _state(rng, B, L, E, 30, zero_frac=0.0)
+    w = _w(rng, B, L, n, False)
+    mask = rng.random(train.shape[0]) > 0.15
+    M = train.shape[0]
+    ew = (rng.random(M) if score else rng.standard_normal(M)).astype(np.float32)
+    sp, v = _sp(row, ent, val, B, L, E, requires_grad=True)
+    wt = _cuda(w).requires_grad_(True)
+    ewt = _cuda(ew).requires_grad_(True)
+    fn = fk.FlashLogFunctionSparse3DTopKSum if op == "sum" else fk.FlashLogFunctionSparse3DTopKMax
+    out = _topk_apply(fn, sp, v, wt, csr, _cuda(mask), ewt, R, topk, score)
+    if op == "sum":
+        fw = O.hop_forward(row, ent, val, w, csr_np, R, E, topk_edges=topk,
+                           mode=O.MODE_TOPK | (O.EDGE_SCORE if score else 0), mask=mask, edge_weight=ew,
+                           record_edges=True)
+    else:
+        fw = O.hop_forward_max(row, ent, val, w, csr_np, R, E, topk_edges=topk, mask=mask, edge_weight=ew,
+                               edge_score=score)
+    assert np.array_equal(_keys(out, L, E), fw["out_key"])
+    np.testing.assert_allclose(out.values().detach().cpu().numpy(), fw["out_val"], rtol=RTOL, atol=0)
+    g = rng.standard_normal(fw["out_key"].size).astype(np.float32)
+    (out.values() * _cuda(g)).sum().backward()
+    want = O.edge_weight_grad(fw, g, row, val, w, ew)
+    assert np.count_nonzero(want) > 50
+    got = ewt.grad.cpu().numpy()
+    np.testing.assert_allclose(got, want, rtol=RTOL, atol=1e-6 * np.abs(want).max())
+    if op == "sum":
+        gv, gw = O.hop_backward(fw, g, row, val, w, R)
+        np.testing.assert_allclose(v.grad.cpu().numpy(), gv, rtol=RTOL, atol=1e-6)
+        np.testing.assert_allclose(wt.grad.cpu().numpy(), gw, rtol=RTOL, atol=1e-6)
+
+
+def test_edge_weights_without_a_mask_are_rejected(fk, g1):
+    cfg, train, csr_np, csr = g1
+    E, R = cfg.entities, cfg.relations
+    rng = np.random.default_rng(3)
+    row, ent, val = _state(rng, 2, 2, E, 10)
+    sp, v = _sp(row, ent, val, 2, 2, E)
+    w = _cuda(_w(rng, 2, 2, 2 * R + 1, False))
+    with pytest.raises(ValueError):
+        _topk_apply(fk.FlashLogFunctionSparse3DTopKSum, sp, v, w, csr, None,
+                    torch.zeros(train.shape[0], device="cuda"), R, 5, False)
+
+
 def test_hop_all_edges_forward_backward(fk, g1):
     cfg, train, csr_np, csr = g1
     E, R = cfg.entities, cfg.relations

@@ -252,3 +252,43 @@ def test_dropout_oracle_keep_bits_and_torch_semantics():
     assert np.array_equal(k0, O.value_dropout(x, 0.5, 9, 1, 0)[1])
     assert not np.array_equal(k0, O.value_dropout(x, 0.5, 9, 2, 0)[1])
     assert not np.array_equal(k0, O.value_dropout(x, 0.5, 9, 1, 1)[1])
+
+
+def test_edge_weight_grad_oracle_is_the_derivative_of_its_forward():
+    """The oracle's edge-weight gradient (the formula of
+    flashlog_kernel.py:1306-1336) against central differences of the oracle's
+    own forward, whose facts the golden vectors pin: d/d ew of
+    sum(g * out) = sum over facts of g * v * w * mask * sigmoid' (ew)."""
+    cfg, train, csr = config1_graph()
+    E, R = cfg.entities, cfg.relations
+    n = 2 * R + 1
+    rng = np.random.default_rng(17)
+    B, L = 3, 2
+    rows, ents = [], []
+    for r in range(B * L):
+        k = int(rng.integers(5, 25))
+        rows.append(np.full(k, r))
+        ents.append(np.sort(rng.choice(E, k, replace=False)))
+    row = np.concatenate(rows).astype(np.int64)
+    ent = np.concatenate(ents).astype(np.int64)
+    val = rng.random(row.size).astype(np.float32)
+    x = rng.standard_normal((B, L, n))
+    w = (np.exp(x) / np.exp(x).sum(-1, keepdims=True)).astype(np.float32)
+    mask = rng.random(train.shape[0]) > 0.1
+    ew = rng.standard_normal(train.shape[0]).astype(np.float32)
+    kw = dict(topk_edges=6, mode=O.MODE_TOPK, mask=mask)
+    fw = O.hop_forward(row, ent, val, w, csr, R, E, edge_weight=ew, record_edges=True, **kw)
+    g = rng.standard_normal(fw["out_key"].size)
+    grad = O.edge_weight_grad(fw, g.astype(np.float32), row, val, w, ew)
+    edges = np.unique(fw["fact_edge"][(fw["fact_rel"] < n - 1)])
+    assert edges.size > 20
+    delta = 1e-2
+    for e in rng.choice(edges, 20, replace=False):
+        lo, hi = ew.copy(), ew.copy()
+        lo[e] -= delta
+        hi[e] += delta
+        f_lo = O.hop_forward(row, ent, val, w, csr, R, E, edge_weight=lo, **kw)
+        f_hi = O.hop_forward(row, ent, val, w, csr, R, E, edge_weight=hi, **kw)
+        assert np.array_equal(f_lo["out_key"], fw["out_key"]) and np.array_equal(f_hi["out_key"], fw["out_key"])
+        fd = (np.dot(g, f_hi["out_val"].astype(np.float64)) - np.dot(g, f_lo["out_val"].astype(np.float64))) / (2 * delta)
+        assert abs(fd - grad[e]) <= 2e-3 * abs(grad[e]) + 1e-5, (e, fd, grad[e])
