@@ -73,6 +73,15 @@ _SZ = ctypes.c_size_t
 _SIDE = fl_csr_side
 _PARAMS = ctypes.POINTER(fl_hop_params)
 
+
+class fl_dropout(ctypes.Structure):
+    """Mirror of fl_dropout (include/flashlog_b200.h): a fused dropout of hop values."""
+    _fields_ = [("p", ctypes.c_double), ("seed", ctypes.c_uint64), ("counter", ctypes.c_void_p),
+                ("subseq", ctypes.c_uint64)]
+
+
+_DROP = ctypes.POINTER(fl_dropout)
+
 # name -> (restype, argtypes)
 SIGNATURES = {
     "fl_last_error": (ctypes.c_char_p, []),
@@ -98,7 +107,7 @@ SIGNATURES = {
     "fl_row_reduce_max": (ctypes.c_int, [_P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _I64, _P, _P, _P, _P,
                                          ctypes.c_int, _P, _P, _SZ, _P]),
     "fl_row_reduce": (ctypes.c_int, [_P, _I64, _I64, _P, _P, _P, _P, _I64, _P, ctypes.c_float, _P, _P, _P, _P, _P,
-                                     _P, _P, _P, _SZ, _P]),
+                                     _P, _P, _P, _SZ, _DROP, _P]),
     "fl_hop_backward_workspace": (_SZ, [_I64, _I64]),
     "fl_hop_backward": (ctypes.c_int, [_PARAMS, _P, _P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                        _SZ, _P]),
@@ -106,11 +115,11 @@ SIGNATURES = {
     "fl_normalize_backward": (ctypes.c_int, [_P, _P, _P, _P, _I64, ctypes.c_float, _P, _P]),
     "fl_hop_stats": (ctypes.c_int, [_P, _I64, _P, _I64, _SIDE, _SIDE, _P, _P, ctypes.c_int, _P, _P]),
     "fl_rule_max_reduce": (ctypes.c_int, [_P, _I64, _P, _P, _I64, _P, _I64, _I64, _I64, _P, _P]),
-    "fl_scatter_grad": (ctypes.c_int, [_P, _P, _I64, _P, _P, _I64, _P, _P]),
+    "fl_scatter_grad": (ctypes.c_int, [_P, _P, _I64, _P, _P, _I64, _P, _DROP, _P]),
     "fl_edge_weight_grad": (ctypes.c_int, [_PARAMS, _P, _P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                            _P]),
     "fl_readout": (ctypes.c_int, [_P, _P, _P, _I64, _P, _I64, _P, _P]),
-    "fl_readout_backward": (ctypes.c_int, [_P, _P, _I64, _P, _I64, _P, _P, _I64, _P, _P]),
+    "fl_readout_backward": (ctypes.c_int, [_P, _P, _I64, _P, _I64, _P, _P, _I64, _P, _DROP, _P]),
     "fl_value_dropout": (ctypes.c_int, [_P, _P, _I64, _P, ctypes.c_double, ctypes.c_uint64, _P, ctypes.c_uint64,
                                         _P]),
     "fl_fixed_relation_workspace": (_SZ, [_I64]),

@@ -63,7 +63,8 @@ int readout(const int64_t *row_ptr, const int32_t *ent, const float *val, int64_
 int value_dropout(const float *x, float *y, int64_t n, const int64_t *live, double p, uint64_t seed,
                   const int64_t *counter, uint64_t subseq, cudaStream_t st);
 int readout_backward(const int64_t *row_ptr, const int32_t *ent, int64_t N, const int64_t *targets, int64_t Q,
-                     const float *g, float *grad_val, int64_t n_val, const int64_t *val_live, cudaStream_t st);
+                     const float *g, float *grad_val, int64_t n_val, const int64_t *val_live, const fl_dropout *drop,
+                     cudaStream_t st);
 
 namespace {
 
@@ -221,9 +222,10 @@ int fl_row_reduce_max(const int64_t *row_ptr, int64_t rows, int64_t E, int64_t r
 int fl_row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *slot_base, const int32_t *entry_count,
                   const int32_t *fact_dst, const float *fact_val, int64_t total_slots, int32_t *fact_pos, float eps,
                   int64_t *out_row_ptr, int32_t *out_ent, float *out_x, float *out_y, float *out_denom,
-                  int32_t *status, const int32_t *row_order, void *ws, size_t ws_bytes, fl_stream_t stream) {
+                  int32_t *status, const int32_t *row_order, void *ws, size_t ws_bytes, const fl_dropout *drop,
+                  fl_stream_t stream) {
     return row_reduce(row_ptr, rows, E, slot_base, entry_count, fact_dst, fact_val, total_slots, fact_pos, eps,
-                      out_row_ptr, out_ent, out_x, out_y, out_denom, status, row_order, ws, ws_bytes,
+                      out_row_ptr, out_ent, out_x, out_y, out_denom, status, row_order, ws, ws_bytes, drop,
                       as_stream(stream));
 }
 
@@ -266,8 +268,9 @@ int fl_edge_weight_grad(const fl_hop_params *p, const int64_t *row_ptr, const fl
 }
 
 int fl_scatter_grad(const float *grad_sel, const int64_t *src_index, int64_t n_sel, const int64_t *n_live,
-                    float *grad_full, int64_t n_full, const int64_t *full_live, fl_stream_t stream) {
-    return scatter_grad(grad_sel, src_index, n_sel, n_live, grad_full, n_full, full_live, as_stream(stream));
+                    float *grad_full, int64_t n_full, const int64_t *full_live, const fl_dropout *drop,
+                    fl_stream_t stream) {
+    return scatter_grad(grad_sel, src_index, n_sel, n_live, grad_full, n_full, full_live, drop, as_stream(stream));
 }
 
 size_t fl_fixed_relation_workspace(int64_t nnz) { return fixed_relation_workspace(nnz); }
@@ -315,8 +318,9 @@ int fl_readout(const int64_t *row_ptr, const int32_t *ent, const float *val, int
 
 int fl_readout_backward(const int64_t *row_ptr, const int32_t *ent, int64_t N, const int64_t *targets, int64_t Q,
                         const float *g_scores, float *grad_val, int64_t n_val, const int64_t *val_live,
-                        fl_stream_t stream) {
-    return readout_backward(row_ptr, ent, N, targets, Q, g_scores, grad_val, n_val, val_live, as_stream(stream));
+                        const fl_dropout *drop, fl_stream_t stream) {
+    return readout_backward(row_ptr, ent, N, targets, Q, g_scores, grad_val, n_val, val_live, drop,
+                            as_stream(stream));
 }
 
 int fl_value_dropout(const float *x, float *y, int64_t n, const int64_t *live, double p, uint64_t seed,

@@ -46,6 +46,38 @@ inline void launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
     kernel<<<grid, block, smem, st>>>(static_cast<KArgs>(args)...);
 }
 
+// ---- dropout keep bits (fl_value_dropout and the fused forms) --------------
+// SplitMix64 output function (G. Steele, D. Lea, C. Flood, "Fast splittable
+// pseudorandom number generators", OOPSLA 2014): a bijective 64-bit mix.
+__device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+// Kernel-side dropout: position i is kept iff the high 32 bits of
+// splitmix64(key + i) reach cut; a kept value is scaled by `scale`, a
+// dropped one multiplied by 0.  on == 0: no dropout.
+struct DropoutArgs {
+    uint64_t seed, subseq, cut;
+    const int64_t *counter;
+    float scale;
+    int on;
+};
+
+// key of one launch: splitmix64(seed ^ splitmix64((*counter << 16) | subseq))
+__device__ __forceinline__ uint64_t dropout_key(const DropoutArgs &d) {
+    const uint64_t c = d.counter != nullptr ? static_cast<uint64_t>(*d.counter) : 0ull;
+    return splitmix64(d.seed ^ splitmix64((c << 16) | d.subseq));
+}
+__device__ __forceinline__ float dropout_factor(const DropoutArgs &d, uint64_t key, int64_t i) {
+    return (splitmix64(key + static_cast<uint64_t>(i)) >> 32) >= d.cut ? d.scale : 0.0f;
+}
+
+// Host: DropoutArgs of fl_dropout (NULL: off); FL_EINVAL for a bad p or subseq.
+int dropout_args(const fl_dropout *drop, DropoutArgs *out);
+
 // ---- workspace carving ---------------------------------------------------
 struct Carve {
     char *base;

@@ -1828,7 +1828,8 @@ __global__ void __launch_bounds__(kRThreads, 1) row_reduce_kernel(ReduceArgs a) 
 // write normalized values.
 __global__ void compact_kernel(const int64_t *row_ptr, const int64_t *slot_base, const int64_t *out_row_ptr,
                                int64_t rows, const int32_t *tmp_ent, const float *tmp_x, const float *out_sum,
-                               float eps, int32_t *out_ent, float *out_x, float *out_y, float *out_denom) {
+                               float eps, int32_t *out_ent, float *out_x, float *out_y, float *out_denom,
+                               DropoutArgs drop) {
     const int64_t r = blockIdx.x;
     if (r >= rows) return;
     const int64_t o0 = out_row_ptr[r], n = out_row_ptr[r + 1] - o0;
@@ -1837,11 +1838,16 @@ __global__ void compact_kernel(const int64_t *row_ptr, const int64_t *slot_base,
     if (n == 0) return;
     const int64_t src0 = slot_base[row_ptr[r]];
     const float dd = d > eps ? d : eps;
+    const uint64_t key = drop.on ? dropout_key(drop) : 0ull;
     for (int64_t k = threadIdx.x; k < n; k += blockDim.x) {
         float x = tmp_x[src0 + k];
         out_ent[o0 + k] = tmp_ent[src0 + k];
         if (out_x) out_x[o0 + k] = x;
-        if (out_y) out_y[o0 + k] = x / dd;
+        if (out_y) {
+            float y = x / dd;
+            if (drop.on) y *= dropout_factor(drop, key, o0 + k);  // the values' training dropout, in place
+            out_y[o0 + k] = y;
+        }
     }
 }
 
@@ -2031,9 +2037,13 @@ __global__ void zero_prefix_kernel(float *x, int64_t n, const int64_t *live) {
 }
 
 __global__ void scatter_grad_kernel(const float *grad_sel, const int64_t *src, int64_t n, const int64_t *n_live,
-                                    float *grad_full) {
+                                    float *grad_full, DropoutArgs d) {
     int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-    if (i < n && (n_live == nullptr || i < *n_live)) grad_full[src[i]] = grad_sel[i];
+    if (i < n && (n_live == nullptr || i < *n_live)) {
+        const int64_t j = src[i];
+        // with dropout: the factor of position j, the backward of the full vector's dropout
+        grad_full[j] = d.on ? grad_sel[i] * dropout_factor(d, dropout_key(d), j) : grad_sel[i];
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -2362,7 +2372,12 @@ static int reduce_rows(const int64_t *row_ptr, int64_t rows, int64_t E, const in
                        float eps, int64_t *out_row_ptr, int32_t *out_ent, float *out_x, float *out_y,
                        float *out_denom, int32_t *status, int max_mode, int64_t r_size, const int16_t *fact_rel,
                        const int32_t *fact_edge, const int32_t *row_order, void *ws, size_t ws_bytes,
-                       cudaStream_t st) {
+                       const fl_dropout *drop, cudaStream_t st) {
+    DropoutArgs dargs;
+    {
+        int rc = dropout_args(drop, &dargs);
+        if (rc) return rc;
+    }
     FL_REQUIRE(total_slots < (int64_t(1) << 32), "too many facts in one hop (%lld)", static_cast<long long>(total_slots));
     FL_REQUIRE(E < (int64_t(1) << 31), "entity count exceeds int32");
     Carve c(ws, ws_bytes);
@@ -2396,17 +2411,18 @@ static int reduce_rows(const int64_t *row_ptr, int64_t rows, int64_t E, const in
     if (rc) return rc;
     if (rows > 0)
         launch(compact_kernel, static_cast<unsigned>(rows), 256, 0, st, row_ptr, slot_base, out_row_ptr, rows, tmp_ent, tmp_x,
-                                                                     out_sum, eps, out_ent, out_x, out_y, out_denom);
+               out_sum, eps, out_ent, out_x, out_y, out_denom, dargs);
     return check_launch("row_compact");
 }
 
 int row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *slot_base, const int32_t *entry_count,
                const int32_t *fact_dst, const float *fact_val, int64_t total_slots, int32_t *fact_pos, float eps,
                int64_t *out_row_ptr, int32_t *out_ent, float *out_x, float *out_y, float *out_denom, int32_t *status,
-               const int32_t *row_order, void *ws, size_t ws_bytes, cudaStream_t st) {
+               const int32_t *row_order, void *ws, size_t ws_bytes, const fl_dropout *drop, cudaStream_t st) {
     (void)entry_count;  // unfilled slots carry the destination -1
     return reduce_rows(row_ptr, rows, E, slot_base, fact_dst, fact_val, total_slots, fact_pos, eps, out_row_ptr,
-                       out_ent, out_x, out_y, out_denom, status, 0, 0, nullptr, nullptr, row_order, ws, ws_bytes, st);
+                       out_ent, out_x, out_y, out_denom, status, 0, 0, nullptr, nullptr, row_order, ws, ws_bytes, drop,
+                       st);
 }
 
 int row_reduce_max(const int64_t *row_ptr, int64_t rows, int64_t E, int64_t r_size, const int64_t *slot_base,
@@ -2417,7 +2433,7 @@ int row_reduce_max(const int64_t *row_ptr, int64_t rows, int64_t E, int64_t r_si
     FL_REQUIRE(max_mode == 1 || max_mode == 2, "bad MAX mode");
     return reduce_rows(row_ptr, rows, E, slot_base, fact_dst, fact_val, total_slots, fact_pos, 1e-7f, out_row_ptr,
                        out_ent, out_x, nullptr, nullptr, status, max_mode, r_size, fact_rel, fact_edge, nullptr, ws,
-                       ws_bytes, st);
+                       ws_bytes, nullptr, st);
 }
 
 size_t row_reduce_workspace(int64_t rows, int64_t total_slots) {
@@ -2519,12 +2535,15 @@ int zero_prefix(float *x, int64_t n, const int64_t *live, cudaStream_t st) {
 }
 
 int scatter_grad(const float *grad_sel, const int64_t *src, int64_t n_sel, const int64_t *n_live, float *grad_full,
-                 int64_t n_full, const int64_t *full_live, cudaStream_t st) {
-    int rc = zero_prefix(grad_full, n_full, full_live, st);
+                 int64_t n_full, const int64_t *full_live, const fl_dropout *drop, cudaStream_t st) {
+    DropoutArgs d;
+    int rc = dropout_args(drop, &d);
+    if (rc) return rc;
+    rc = zero_prefix(grad_full, n_full, full_live, st);
     if (rc) return rc;
     if (n_sel > 0)
         launch(scatter_grad_kernel, static_cast<unsigned>((n_sel + 255) / 256), 256, 0, st, grad_sel, src, n_sel, n_live,
-               grad_full);
+               grad_full, d);
     return check_launch("scatter_grad");
 }
 

@@ -26,7 +26,7 @@ int row_reduce_max(const int64_t *row_ptr, int64_t rows, int64_t E, int64_t r_si
 int row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *slot_base, const int32_t *entry_count,
                const int32_t *fact_dst, const float *fact_val, int64_t total_slots, int32_t *fact_pos, float eps,
                int64_t *out_row_ptr, int32_t *out_ent, float *out_x, float *out_y, float *out_denom, int32_t *status,
-               const int32_t *row_order, void *ws, size_t ws_bytes, cudaStream_t st);
+               const int32_t *row_order, void *ws, size_t ws_bytes, const fl_dropout *drop, cudaStream_t st);
 int hop_backward(const fl_hop_params *p, const int64_t *row_ptr, const float *val, int64_t S, const float *w,
                  const int64_t *slot_base, const int32_t *entry_count, const int32_t *fact_pos, const int16_t *fact_rel,
                  const float *fact_m, const int64_t *out_row_ptr, const float *out_x, const float *out_denom,
@@ -45,7 +45,7 @@ int hop_stats(const int64_t *row_ptr, int64_t rows, const int32_t *ent, int64_t 
               const fl_csr_side &inv, const int32_t *entry_count, const int64_t *out_row_ptr, int wot_i, int64_t *acc,
               cudaStream_t st);
 int scatter_grad(const float *grad_sel, const int64_t *src, int64_t n_sel, const int64_t *n_live, float *grad_full,
-                 int64_t n_full, const int64_t *full_live, cudaStream_t st);
+                 int64_t n_full, const int64_t *full_live, const fl_dropout *drop, cudaStream_t st);
 int topc_select(const int64_t *row_ptr, const int32_t *ent, const float *val, int64_t rows, int64_t S, int64_t c1,
                 const double *noise, int64_t *out_row_ptr, int32_t *out_ent, float *out_val, int64_t *out_src,
                 int64_t out_capacity, int32_t *status, void *ws, size_t ws_bytes, cudaStream_t st);

@@ -384,7 +384,7 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
         check(lib().fl_row_reduce(_p(row_ptr), rows, graph.E, _p(slot_base), _p(entry_count), _p(fact_dst),
                                   _p(fact_val), T, _p(fact_pos), ctypes.c_float(eps), _p(out_row_ptr), _p(out_ent),
                                   _p(out_x), _p(out_y), _p(out_denom), _p(status), None, _p(ws2), ws2.numel(),
-                                  _stream()),
+                                  None, _stream()),
               "row_reduce")
     if timing is not None:
         timing.record_end()
@@ -439,7 +439,7 @@ def scatter_grad(grad_sel, src_index, n_full: int, n_live=None, full_live=None):
     full_live (device int64) limits the zeroing to the live prefix."""
     out = torch.empty(max(n_full, 1), dtype=torch.float32, device=grad_sel.device)
     check(lib().fl_scatter_grad(_p(grad_sel.contiguous()), _p(src_index), src_index.numel(), _p(n_live), _p(out),
-                                n_full, _p(full_live), _stream()), "scatter_grad")
+                                n_full, _p(full_live), None, _stream()), "scatter_grad")
     return out[:n_full]
 
 
@@ -498,7 +498,7 @@ def fixed_relation(b, l, e, v, ops_, graph: Graph, r_size: int, B: int, Lr: int)
     ws2 = _ws(lib().fl_reduce_workspace(rows, T), dev)
     check(lib().fl_row_reduce(_p(row_ptr), rows, graph.E, _p(slot_base), _p(entry_count), _p(fact_dst), _p(fact_val),
                               T, None, ctypes.c_float(EPS), _p(out_row_ptr), _p(out_ent), _p(out_x), None,
-                              _p(out_denom), None, None, _p(ws2), ws2.numel(), _stream()), "row_reduce")
+                              _p(out_denom), None, None, _p(ws2), ws2.numel(), None, _stream()), "row_reduce")
     u = int(out_row_ptr[rows].item())
     return out_row_ptr, out_ent[:u], out_x[:u]
 
@@ -526,7 +526,7 @@ def channel_merge(row_ptr, ent, val, B: int, Lch: int, E: int):
     check(lib().fl_row_reduce(_p(entry_row_ptr), B, int(E), _p(slot_base), _p(entry_count), _p(ent.contiguous()),
                               _p(val.to(torch.float32).contiguous()), max(nnz, 1), _p(fact_pos), ctypes.c_float(EPS),
                               _p(out_row_ptr), _p(out_ent), _p(out_x), None, _p(out_denom), None, None, _p(ws),
-                              ws.numel(), _stream()), "channel_merge")
+                              ws.numel(), None, _stream()), "channel_merge")
     u = int(out_row_ptr[B].item())
     row_of = torch.repeat_interleave(torch.arange(B, device=dev), entry_row_ptr[1:] - entry_row_ptr[:-1],
                                      output_size=nnz)
@@ -590,6 +590,6 @@ def readout_backward(row_ptr, ent, N: int, targets, g_scores, n_val: int, val_li
     grad = torch.empty(max(n_val, 1), dtype=torch.float32, device=g_scores.device)
     check(lib().fl_readout_backward(_p(row_ptr), _p(ent), N, _p(targets.to(torch.int64).contiguous()), Q,
                                     _p(g_scores.to(torch.float32).contiguous()), _p(grad), n_val, _p(val_live),
-                                    _stream()),
+                                    None, _stream()),
           "readout_backward")
     return grad[:n_val]

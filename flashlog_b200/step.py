@@ -234,11 +234,9 @@ class DrumTrainStep:
                                    _p(self.fact_dst), _p(self.fact_val), self.F[t], _p(self.fact_pos[t]),
                                    ctypes.c_float(self.eps), _p(self.out_rp[t]), _p(self.out_ent[t]),
                                    _p(self.out_x[t]), _p(self.out_y[t]), _p(self.out_denom[t]), _p(self.status),
-                                   _p(self.row_order[t]), ws, wsn, st), "row_reduce")
+                                   _p(self.row_order[t]), ws, wsn, self._drop(t), st), "row_reduce")
             if self.timer is not None:
                 self.timer[t][1].record()
-            if self.dropout > 0:
-                self._dropout(self.out_y[t], t, st)
             if self.stats is not None:
                 check(lb.fl_hop_stats(_p(rp_s), rows, _p(ent_s), self.S[t], g.ori, g.inv, _p(self.entry_count[t]),
                                       _p(self.out_rp[t]), 0, _p(self.stats), st), "hop_stats")
@@ -250,11 +248,11 @@ class DrumTrainStep:
         g_score = torch.where(score > self.thr, -1.0 / (Q * torch.clamp_min(score, self.thr)),
                               torch.zeros_like(score))
         check(lb.fl_readout_backward(_p(rp_in), _p(ent_in), N, _p(self.tails), Q, _p(g_score), _p(self.g_y[T - 1]),
-                                     self.U[T - 1], _p(self.out_rp[T - 1][rows:]), st), "readout_backward")
-        # backward through the hops
+                                     self.U[T - 1], _p(self.out_rp[T - 1][rows:]), self._drop(T - 1), st),
+              "readout_backward")
+        # backward through the hops; g_y[t] arrives through hop t's dropout
+        # (the same keep bits and scale), applied where it is written
         for t in reversed(range(T)):
-            if self.dropout > 0:  # d/d(normalized values): the same keep bits and scale
-                self._dropout(self.g_y[t], t, st)
             params = self._params(t, self.flags)
             check(lb.fl_hop_backward(ctypes.byref(params), _p(self.rp_sel[t]), _p(self.val_sel[t]), self.S[t],
                                      _p(self.w[t]), _p(self.slot_base[t]), _p(self.entry_count[t]),
@@ -265,10 +263,13 @@ class DrumTrainStep:
                 src = self.src_sel[t] if self.c1 is not None else None
                 if src is not None:
                     check(lb.fl_scatter_grad(_p(self.grad_sel), _p(src), self.S[t], _p(self.rp_sel[t][rows:]),
-                                             _p(self.g_y[t - 1]), self.U[t - 1], _p(self.out_rp[t - 1][rows:]), st),
+                                             _p(self.g_y[t - 1]), self.U[t - 1], _p(self.out_rp[t - 1][rows:]),
+                                             self._drop(t - 1), st),
                           "scatter_grad")
                 else:
                     self.g_y[t - 1][:self.S[t]].copy_(self.grad_sel[:self.S[t]])
+                    if self.dropout > 0:
+                        self._dropout(self.g_y[t - 1], t - 1, st)
             # softmax backward, d logits = w * (g - sum(g * w)): torch's own kernel
             wt = self.w[t][:rows * self.n].view(Q, N, self.n)
             gw = self.grad_w[:rows * self.n].view(Q, N, self.n)
@@ -282,6 +283,12 @@ class DrumTrainStep:
         for k in range(2):
             self.vis[k].index_put_((hid[k],), old[k])
         return self.loss
+
+    def _drop(self, t):
+        """fl_dropout of hop t for the kernels that write its values or their gradient (None: no dropout)."""
+        if self.dropout <= 0:
+            return None
+        return ctypes.byref(L.fl_dropout(self.dropout, self.dropout_seed, self.drop_counter.data_ptr(), t))
 
     def _dropout(self, x, t, st):
         check(lib().fl_value_dropout(_p(x), _p(x), self.U[t], _p(self.out_rp[t][self.rows:]),

@@ -93,6 +93,17 @@ typedef struct {
                                        the tie key of fl_row_reduce_max          */
 } fl_hop_params;
 
+/* Dropout of hop values fused into the kernels that write them (the models'
+ * training dropout, src/model_DRUM_kernel_sp.py:189-192), with the keep bits
+ * of fl_value_dropout: the same (seed, *counter, subseq, position) gives the
+ * same mask.  Passed as an optional pointer; NULL means no dropout. */
+typedef struct fl_dropout {
+    double p;                /* drop probability, 0 <= p <= 1                   */
+    uint64_t seed;
+    const int64_t *counter;  /* device int64 or NULL (counts as 0)              */
+    uint64_t subseq;         /* < 65536, e.g. the hop index                     */
+} fl_dropout;
+
 /* int32 values per entry in fl_hop_params.entry_info. */
 enum { FL_ENTRY_INFO_INTS = 5 };
 
@@ -195,12 +206,15 @@ int fl_hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t 
  * buffers; rows whose slots lie beyond it are skipped and set
  * FL_STATUS_SLOT_OVERFLOW in *status (device int, may be NULL).  row_order
  * (i32[rows], a permutation, or NULL) is the order in which the rows are
- * taken: heaviest first shortens the tail; results do not depend on it. */
+ * taken: heaviest first shortens the tail; results do not depend on it.
+ * drop (or NULL): out_y[i] is written as fl_value_dropout would leave it
+ * (out_x and out_denom are not affected). */
 size_t fl_reduce_workspace(int64_t rows, int64_t total_slots);
 int fl_row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *slot_base, const int32_t *entry_count,
                   const int32_t *fact_dst, const float *fact_val, int64_t total_slots, int32_t *fact_pos, float eps,
                   int64_t *out_row_ptr, int32_t *out_ent, float *out_x, float *out_y, float *out_denom,
-                  int32_t *status, const int32_t *row_order, void *ws, size_t ws_bytes, fl_stream_t stream);
+                  int32_t *status, const int32_t *row_order, void *ws, size_t ws_bytes, const fl_dropout *drop,
+                  fl_stream_t stream);
 
 /* MAX coalesce of expanded facts (FlashLogFunctionSparse3DTopKMax,
  * flashlog_kernel.py:386-478): per (row, destination) the largest fact value;
@@ -267,9 +281,12 @@ int fl_edge_weight_grad(const fl_hop_params *p, const int64_t *row_ptr, const fl
  * n_live, a device count, is given), zeros elsewhere: all of grad_full[0,
  * n_full), or only its first *full_live entries when full_live (a device
  * count) is given.  Replaces _restore_pruned_gradient
- * (flashlog_kernel.py:1150-1155). */
+ * (flashlog_kernel.py:1150-1155).  drop (or NULL): each written value is
+ * multiplied by the dropout factor of its position in grad_full (the backward
+ * of a dropout of the full vector), as fl_value_dropout on grad_full would. */
 int fl_scatter_grad(const float *grad_sel, const int64_t *src_index, int64_t n_sel, const int64_t *n_live,
-                    float *grad_full, int64_t n_full, const int64_t *full_live, fl_stream_t stream);
+                    float *grad_full, int64_t n_full, const int64_t *full_live, const fl_dropout *drop,
+                    fl_stream_t stream);
 
 /* Channel readout at the targets: scores[q] = sum over channels l (in order)
  * of the state's value at (q, l, targets[q]) (0 when absent).  Rows are
@@ -277,12 +294,13 @@ int fl_scatter_grad(const float *grad_sel, const int64_t *src_index, int64_t n_s
  * log_loss_common_sp (src/model_DRUM_kernel_sp.py:22-28, src/utils.py:36-47).
  * The backward writes g_scores[q] at every entry read and zeros the rest of
  * grad_val (n_val entries, or the first *val_live when that device count is
- * given). */
+ * given).  drop (or NULL): the written gradients get the dropout factor of
+ * their position, as fl_value_dropout on grad_val would. */
 int fl_readout(const int64_t *row_ptr, const int32_t *ent, const float *val, int64_t N, const int64_t *targets,
                int64_t Q, float *scores, fl_stream_t stream);
 int fl_readout_backward(const int64_t *row_ptr, const int32_t *ent, int64_t N, const int64_t *targets, int64_t Q,
                         const float *g_scores, float *grad_val, int64_t n_val, const int64_t *val_live,
-                        fl_stream_t stream);
+                        const fl_dropout *drop, fl_stream_t stream);
 
 /* Dropout of hop values (nn.Dropout on s.values() in training,
  * src/model_DRUM_kernel_sp.py:189-192; the other sparse models do the same).

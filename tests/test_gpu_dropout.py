@@ -60,3 +60,33 @@ def test_sparse_dropout_autograd():
     g = _x(key.size, 4)
     (y.values() * torch.from_numpy(g).cuda()).sum().backward()
     assert np.array_equal(v.grad.cpu().numpy(), O.value_dropout(g, 0.2, 17, 3, 1)[0])
+
+
+def test_fused_dropout_equals_the_separate_pass():
+    """fl_scatter_grad with an fl_dropout descriptor writes exactly what the
+    plain scatter followed by fl_value_dropout over the full vector leaves
+    (the graph step fuses the gradients' dropout this way); a bad descriptor
+    is rejected."""
+    import ctypes
+    from flashlog_b200 import _lib as L
+    from flashlog_b200.ops import _p, _stream
+    lib = L.lib()
+    rng = np.random.default_rng(8)
+    n_full, n_sel = 50_000, 12_000
+    src = torch.from_numpy(np.sort(rng.choice(n_full, n_sel, replace=False))).cuda()
+    g = torch.from_numpy(_x(n_sel, 9)).cuda()
+    counter = torch.tensor([5], device="cuda")
+    drop = L.fl_dropout(0.25, 77, counter.data_ptr(), 3)
+    fused = torch.empty(n_full, device="cuda")
+    plain = torch.empty(n_full, device="cuda")
+    assert lib.fl_scatter_grad(_p(g), _p(src), n_sel, None, _p(fused), n_full, None, ctypes.byref(drop), _stream()) == 0
+    assert lib.fl_scatter_grad(_p(g), _p(src), n_sel, None, _p(plain), n_full, None, None, _stream()) == 0
+    assert lib.fl_value_dropout(_p(plain), _p(plain), n_full, None, ctypes.c_double(0.25), 77, _p(counter), 3,
+                                _stream()) == 0
+    assert torch.equal(fused.view(torch.int32), plain.view(torch.int32))
+    full = np.zeros(n_full, np.float32)
+    full[src.cpu().numpy()] = g.cpu().numpy()
+    assert np.array_equal(fused.cpu().numpy(), O.value_dropout(full, 0.25, 77, 5, 3)[0])
+    bad = L.fl_dropout(1.5, 0, None, 0)
+    assert lib.fl_scatter_grad(_p(g), _p(src), n_sel, None, _p(fused), n_full, None, ctypes.byref(bad),
+                               _stream()) == 1
