@@ -40,6 +40,24 @@ def _buf(n, dtype, dev):
     return torch.empty(max(int(n), 1), dtype=dtype, device=dev)
 
 
+def capacities(rows: int, T: int, c1, k_max: int, K: int, E: int, zero_slack: float = 1.0):
+    """Static bounds of the step's buffers per hop, as lists (C, S, F, U):
+    C_t inputs, S_t selected entries, F_t fact slots, U_t = C_{t+1} outputs,
+    with C_0 = rows, S_t = min(C_t, ceil(rows * c1 * zero_slack)) (C_t
+    without c1), F_t = min(S_t * k_max, rows * K), U_t = min(F_t, rows * E)."""
+    Cs, Ss, Fs, Us = [], [], [], []
+    C = rows
+    for _ in range(T):
+        S = min(C, math.ceil(rows * c1 * zero_slack)) if c1 is not None else C
+        F = min(S * k_max, rows * K)
+        Cs.append(C)
+        Ss.append(S)
+        Fs.append(F)
+        C = min(F, rows * E)
+        Us.append(C)
+    return Cs, Ss, Fs, Us
+
+
 class DrumTrainStep:
     """Static-buffer DRUM step: forward (T hops), loss, backward, SGD.
 
@@ -82,17 +100,7 @@ class DrumTrainStep:
         d_i = (csr[4][1:] - csr[4][:-1]).to(torch.int64).clamp_max(self.topk)
         k = d_o + d_i + 1
         k_max, K = (int(k.max().item()), int(k.sum().item())) if E > 0 else (1, 1)
-        # capacities
-        self.C, self.S, self.F, self.U = [], [], [], []
-        C = rows
-        for _ in range(T):
-            S = min(C, math.ceil(rows * self.c1 * self.zero_slack)) if self.c1 is not None else C
-            F = min(S * k_max, rows * K)
-            self.C.append(C)
-            self.S.append(S)
-            self.F.append(F)
-            C = min(F, rows * E)
-            self.U.append(C)
+        self.C, self.S, self.F, self.U = capacities(rows, T, self.c1, k_max, K, E, self.zero_slack)
         i64, i32, f32, u8, i16 = torch.int64, torch.int32, torch.float32, torch.uint8, torch.int16
         # inputs
         self.heads = _buf(Q, i64, dev)

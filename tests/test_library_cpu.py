@@ -124,3 +124,21 @@ def test_python_constants_match_header():
             assert getattr(L, name) == eval(header[name].strip()), name
             checked += 1
     assert checked >= 12
+
+
+def test_step_capacity_bounds():
+    """The graph step's static buffer bounds (host arithmetic): each hop's
+    input is the previous hop's output bound; c1 caps the selection at
+    rows * c1 (times zero_slack when dropout keeps explicit zeros); facts
+    are capped by k_max per entry and by the per-row entity capacities K;
+    outputs by one per entity and row."""
+    from flashlog_b200.step import capacities
+    rows, k_max, K, E = 1536, 401, 46_000_000, 4_600_000
+    C, S, F, U = capacities(rows, 3, 1000, k_max, K, E)
+    assert C[0] == rows and S[0] == rows and F[0] == rows * k_max
+    assert all(C[t + 1] == U[t] for t in range(2))
+    assert S[2] == rows * 1000 and F[2] == rows * 1000 * k_max
+    C2, S2, F2, U2 = capacities(rows, 3, 1000, k_max, K, E, zero_slack=2.0)
+    assert S2[2] == 2 * S[2] and F2[2] == 2 * F[2] and S2[:2] == S[:2]
+    Cn, Sn, Fn, Un = capacities(4, 2, None, 3, 10, 5)
+    assert Sn == Cn == [4, 12] and Fn == [12, 36] and Un == [12, 20]
