@@ -292,3 +292,48 @@ def test_edge_weight_grad_oracle_is_the_derivative_of_its_forward():
         assert np.array_equal(f_lo["out_key"], fw["out_key"]) and np.array_equal(f_hi["out_key"], fw["out_key"])
         fd = (np.dot(g, f_hi["out_val"].astype(np.float64)) - np.dot(g, f_lo["out_val"].astype(np.float64))) / (2 * delta)
         assert abs(fd - grad[e]) <= 2e-3 * abs(grad[e]) + 1e-5, (e, fd, grad[e])
+
+
+def test_edge_weight_grad_oracle_max_winners_only():
+    """MAX: only each destination's winning fact passes gradient
+    (flashlog_kernel.py:1590-1614); central differences of the oracle's MAX
+    forward agree wherever the perturbation leaves the winners unchanged."""
+    cfg, train, csr = config1_graph()
+    E, R = cfg.entities, cfg.relations
+    n = 2 * R + 1
+    rng = np.random.default_rng(23)
+    B, L = 2, 2
+    rows, ents = [], []
+    for r in range(B * L):
+        k = int(rng.integers(5, 20))
+        rows.append(np.full(k, r))
+        ents.append(np.sort(rng.choice(E, k, replace=False)))
+    row = np.concatenate(rows).astype(np.int64)
+    ent = np.concatenate(ents).astype(np.int64)
+    val = rng.random(row.size).astype(np.float32)
+    x = rng.standard_normal((B, L, n))
+    w = (np.exp(x) / np.exp(x).sum(-1, keepdims=True)).astype(np.float32)
+    mask = rng.random(train.shape[0]) > 0.1
+    ew = rng.standard_normal(train.shape[0]).astype(np.float32)
+    kw = dict(topk_edges=6, mask=mask)
+    fw = O.hop_forward_max(row, ent, val, w, csr, R, E, edge_weight=ew, **kw)
+    g = rng.standard_normal(fw["out_key"].size)
+    grad = O.edge_weight_grad(fw, g.astype(np.float32), row, val, w, ew)
+    won = (fw["fact_out"] >= 0) & (fw["fact_rel"] < n - 1)
+    edges = np.unique(fw["fact_edge"][won])
+    assert edges.size > 10
+    delta, checked = 1e-3, 0
+    for e in rng.choice(edges, min(20, edges.size), replace=False):
+        lo, hi = ew.copy(), ew.copy()
+        lo[e] -= delta
+        hi[e] += delta
+        f_lo = O.hop_forward_max(row, ent, val, w, csr, R, E, edge_weight=lo, **kw)
+        f_hi = O.hop_forward_max(row, ent, val, w, csr, R, E, edge_weight=hi, **kw)
+        if not (np.array_equal(f_lo["fact_out"], fw["fact_out"]) and np.array_equal(f_hi["fact_out"], fw["fact_out"])):
+            continue  # a winner changed: the max is not differentiable across that step
+        fd = (np.dot(g, f_hi["out_val"].astype(np.float64)) - np.dot(g, f_lo["out_val"].astype(np.float64))) / (2 * delta)
+        assert abs(fd - grad[e]) <= 1e-2 * abs(grad[e]) + 1e-4, (e, fd, grad[e])
+        checked += 1
+    assert checked >= 10
+    lost = np.setdiff1d(np.unique(fw["fact_edge"][(fw["fact_out"] < 0) & (fw["fact_rel"] < n - 1)]), edges)
+    assert lost.size == 0 or not grad[lost].any()  # edges whose facts all lost get nothing
