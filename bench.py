@@ -40,7 +40,7 @@ import torch
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
-from flashlog_b200.synthetic import CONFIGS, load_or_generate, training_queries  # noqa: E402
+from flashlog_b200.synthetic import CONFIGS, load_graph, load_or_generate, training_queries  # noqa: E402
 
 PROFILE_TRAFFIC = os.path.join(REPO, "profiles", "hop_forward_traffic.json")
 
@@ -179,11 +179,11 @@ def setup(args, rank, world, device):
     if args.batch_size:
         import dataclasses
         cfg = dataclasses.replace(cfg, batch_size=args.batch_size)
-    train, _, _ = load_or_generate(cfg)
+    train, tt = load_graph(cfg, device)
     from flashlog_b200.flashlog_kernel import build_csr_structure
-    tt = torch.from_numpy(train).to(device)
     csr = build_csr_structure(tt[:, 0], tt[:, 2], tt[:, 1], cfg.entities)
     del tt
+    torch.cuda.empty_cache()
     return cfg, train, csr
 
 
@@ -195,6 +195,29 @@ def batches_for(cfg, train, n, rank, seed_base=1234):
     return out
 
 
+TABLE_MAX_BYTES = 4 << 30
+
+
+def attention_table(cfg, data, device):
+    """The learnable attention logits [rows, T, N, n] and the batches with
+    their query relations mapped to table rows.
+
+    Up to TABLE_MAX_BYTES the table has one row per query relation (2R rows,
+    drawn on the host from seed 1234).  Beyond (config 5: 29,648 x 9 x
+    29,649 fp32 would take 31.6 GB) it has one row per distinct query
+    relation of the run's batches, drawn on the device; only the row index
+    changes, the softmax, propagation and update are the same."""
+    R, T, N = cfg.relations, cfg.T, cfg.N
+    n = 2 * R + 1
+    if 2 * R * T * N * n * 4 <= TABLE_MAX_BYTES:
+        gen = torch.Generator(device="cpu").manual_seed(1234)
+        return torch.randn(2 * R, T, N, n, generator=gen).to(device), data
+    rels = np.unique(np.concatenate([b[2] for b in data]))
+    mapped = [(ids, h, np.searchsorted(rels, r).astype(np.int64), t) for ids, h, r, t in data]
+    gen = torch.Generator(device=device).manual_seed(1234)
+    return torch.randn(rels.size, T, N, n, generator=gen, device=device), mapped
+
+
 def run_value_arm(args, cfg, train, csr, rank, world, device):
     from flashlog_b200 import _lib, engine
     from flashlog_b200.ops import Graph
@@ -203,11 +226,10 @@ def run_value_arm(args, cfg, train, csr, rank, world, device):
     graph = Graph.of(csr)
     R, T, N = cfg.relations, cfg.T, cfg.N
     n = 2 * R + 1
-    gen = torch.Generator(device="cpu").manual_seed(1234)
-    table = (torch.randn(2 * R, T, N, n, generator=gen) * 1.0).to(device).requires_grad_(True)
     mask = torch.ones(train.shape[0], dtype=torch.uint8, device=device)
     nb = args.warmup + args.steps
-    data = batches_for(cfg, train, nb, rank)
+    table, data = attention_table(cfg, batches_for(cfg, train, nb, rank), device)
+    table.requires_grad_(True)
     dev_data = [tuple(torch.from_numpy(x).to(device) for x in b) for b in data]
     stats = Stats(graph)
     status = engine.new_status(device)
@@ -284,10 +306,8 @@ def run_graph_arm(args, cfg, train, csr, rank, world, device):
     graph = Graph.of(csr)
     R, T, N = cfg.relations, cfg.T, cfg.N
     n = 2 * R + 1
-    gen = torch.Generator(device="cpu").manual_seed(1234)
-    table = (torch.randn(2 * R, T, N, n, generator=gen) * 1.0).to(device)
     nb = args.warmup + args.steps
-    data = batches_for(cfg, train, nb, rank)
+    table, data = attention_table(cfg, batches_for(cfg, train, nb, rank), device)
     dev_data = [tuple(torch.from_numpy(x).to(device) for x in b) for b in data]
     n_ids = dev_data[0][0].numel()
     step = DrumTrainStep(graph, R, cfg.queries, T, N, cfg.c1 or None, cfg.c2, table, n_hide=n_ids * world,
@@ -299,10 +319,23 @@ def run_graph_arm(args, cfg, train, csr, rank, world, device):
     def hide_of(ids):
         return MG.gather_hidden_triples(ids) if world > 1 else ids
 
-    def after():
+    # N > 1: the step runs as T + 1 parts; as soon as the part that completes
+    # hop t's table gradient has been issued, that gradient's all-reduce is
+    # issued on a communication stream, so it overlaps the remaining backward
+    # parts; the update waits for all of them.
+    comm = torch.cuda.Stream() if world > 1 else None
+
+    def run_parts(parts):
+        for j, part in enumerate(parts):
+            part()
+            if world > 1 and j < T:
+                hop = T - 1 - j
+                comm.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(comm):
+                    dist.all_reduce(step.grad_hop[hop])
         if world > 1:
-            MG.allreduce_mean_(step.grad)
-            table.sub_(lr * step.grad)
+            torch.cuda.current_stream().wait_stream(comm)
+            table.sub_(step.grad, alpha=lr / world)
 
     clocks = ClockSampler(torch.cuda.current_device())
     clocks.start()  # before the warm-up: nvidia-smi's start-up must not fall in the timed region
@@ -312,12 +345,12 @@ def run_graph_arm(args, cfg, train, csr, rank, world, device):
         for b in dev_data[:args.warmup]:
             ids, h, r, t = b
             step.load(h, t, r, hide_of(ids))
-            step.run()
-            after()
+            run_parts(step.parts())
     torch.cuda.current_stream().wait_stream(side)
     torch.cuda.synchronize()
     step.check()
-    # one graph per timed step, each with its own hop events
+    # graphs per timed step (one for the whole step at N = 1, one per part at
+    # N > 1, the collectives between them), each step with its own hop events
     graphs, timers = [], []
     pool = None
     launches_per_step = 0
@@ -325,13 +358,17 @@ def run_graph_arm(args, cfg, train, csr, rank, world, device):
         timer = [(torch.cuda.Event(enable_timing=True, external=True),
                   torch.cuda.Event(enable_timing=True, external=True)) for _ in range(T)]
         step.timer = timer
-        g = torch.cuda.CUDAGraph()
         l0 = _lib.lib().fl_launch_count()
-        with torch.cuda.graph(g, pool=pool):
-            step.run()
+        chunks = [step.run] if world == 1 else step.parts()[:T]  # the last part is empty without the update
+        gs = []
+        for fn in chunks:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=pool):
+                fn()
+            pool = g.pool()
+            gs.append(g)
         launches_per_step = _lib.lib().fl_launch_count() - l0
-        pool = g.pool()
-        graphs.append(g)
+        graphs.append(gs)
         timers.append(timer)
     step.timer = None
     torch.cuda.synchronize()
@@ -346,8 +383,10 @@ def run_graph_arm(args, cfg, train, csr, rank, world, device):
     for k, b in enumerate(dev_data[args.warmup:]):
         ids, h, r, t = b
         step.load(h, t, r, hide_of(ids))
-        graphs[k].replay()
-        after()
+        if world == 1:
+            graphs[k][0].replay()
+        else:
+            run_parts([g.replay for g in graphs[k]])
     t1.record()
     torch.cuda.synchronize()
     if world > 1:
@@ -448,11 +487,13 @@ def cpu_baseline(args, cfg, train, csr):
         mask[ids] = 0
         batches.append((h, t, w_all, mask))
     rate, facts, secs, steps, kind = CB.time_sample(csr_np, batches, R, cfg.entities, cfg.c1, cfg.c2,
-                                                    min_seconds=args.cpu_seconds, max_seconds=3 * args.cpu_seconds)
+                                                    min_seconds=args.cpu_seconds, max_seconds=3 * args.cpu_seconds,
+                                                    dropout=args.dropout)
     return dict(value=rate, unit="facts/s", cores=torch.get_num_threads(), kind=kind,
                 sample=f"{steps} steps x {args.cpu_queries} queries of config {cfg.index} "
                        f"({facts} facts in {secs:.1f} s); c1 via the oracle port, expansion/reduction/"
-                       f"normalization fwd+bwd in the reference's compiled OpenMP extension")
+                       f"normalization fwd+bwd in the reference's compiled OpenMP extension; "
+                       f"dropout {args.dropout} on every hop's values")
 
 
 def workload_desc(cfg, world):
@@ -474,9 +515,18 @@ def main():
             return
         import dataclasses
         cfg = dataclasses.replace(cfg0, batch_size=args.batch_size) if args.batch_size else cfg0
-        train, _, _ = load_or_generate(cfg)
         from oracle import oracle as O
-        csr_np = O.build_csr(train[:, 0], train[:, 2], train[:, 1], cfg.entities)
+        from oracle import reference as Rf
+        from flashlog_b200.synthetic import host_generation_fits
+        if host_generation_fits(cfg):
+            train, _, _ = load_or_generate(cfg)
+        else:  # config 5: drawn on the device (the host generator cannot key 68-bit triples)
+            train, tt = load_graph(cfg, torch.device("cuda", local))
+            del tt
+            torch.cuda.empty_cache()
+        # the reference's own CSR builder (csr.cpp) when built, else the oracle's restatement
+        build = Rf.build_csr if Rf.available() else O.build_csr
+        csr_np = build(train[:, 0], train[:, 2], train[:, 1], cfg.entities)
         from oracle import cpu_baseline as CB
         torch.set_num_threads(os.cpu_count() or 1)
         rng = np.random.default_rng(99)
@@ -491,7 +541,8 @@ def main():
             mask = np.ones(train.shape[0], np.uint8)
             mask[ids[:q // 2]] = 0
             t0 = time.perf_counter()
-            f, _, kind = CB.drum_step(csr_np, h[:q], t[:q], w_all, mask, R, cfg.entities, cfg.c1, cfg.c2)
+            f, _, kind = CB.drum_step(csr_np, h[:q], t[:q], w_all, mask, R, cfg.entities, cfg.c1, cfg.c2,
+                                      dropout=args.dropout, seed=2000 + s)
             el = time.perf_counter() - t0
             if s >= args.warmup:
                 vals.append((f, el))

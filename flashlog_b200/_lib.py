@@ -12,7 +12,7 @@ import subprocess
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libflashlog_b200.so")
 CSRC = os.path.join(HERE, "csrc")
-SOURCES = ["api.cu", "scan.cu", "topc.cu", "hop.cu", "rules.cu", "csr.cu", "readout.cu"]
+SOURCES = ["api.cu", "scan.cu", "topc.cu", "hop.cu", "rules.cu", "csr.cu", "readout.cu", "masks.cu"]
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
               "-fmad=false", "-Xcompiler", "-fPIC", "-shared"]
 
@@ -27,6 +27,8 @@ FL_NO_INV = 512
 FL_EDGE_POS = 1024
 FL_NO_NORMALIZE = 1 << 20
 FL_MAX_BITS = 1
+FL_MASK_U8 = 0
+FL_MASK_F32 = 1
 FL_ENTRY_INFO_INTS = 5  # int32 values per entry in fl_hop_params.entry_info
 NO_BUDGET = 1 << 62
 FL_STATUS_SLOT_OVERFLOW = 1
@@ -100,6 +102,8 @@ SIGNATURES = {
     "fl_hop_plan": (ctypes.c_int, [_PARAMS, _P, _P, _I64, _SIDE, _SIDE, _P, ctypes.POINTER(ctypes.c_int64), _P,
                                    _SZ, _P]),
     "fl_csr_visibility": (ctypes.c_int, [_P, _I64, _P, _P, _P]),
+    "fl_csr_mask": (ctypes.c_int, [_P, ctypes.c_int, _P, _I64, _P, _P, _P]),
+    "fl_align_rows": (ctypes.c_int, [_P, _P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P]),
     "fl_relation_rank": (ctypes.c_int, [_P, _I64, _I64, _P, _P, _P]),
     "fl_hop_expand": (ctypes.c_int, [_PARAMS, _P, _P, _P, _I64, _P, _SIDE, _SIDE, _P, _P, _P, _P, _P, _P, _P, _P,
                                      _P, _P, _P]),

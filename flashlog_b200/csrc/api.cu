@@ -58,6 +58,11 @@ int filtered_ranks_noalloc(const int64_t *ib, const int64_t *ie, const float *v,
                            const int64_t *fk, int64_t nf, int64_t B, int64_t E, int use_eql, float *ranks,
                            cudaStream_t st);
 
+int csr_mask(const void *mask, int mask_kind, const int32_t *order, int64_t m, const float *weight, float *out,
+             cudaStream_t st);
+int align_rows(const int64_t *out_b, const int64_t *out_l, const int64_t *out_e, int64_t n, int64_t L, int64_t rows,
+               const int64_t *g_row_ptr, const int32_t *g_ent, const float *g_val, float *out, cudaStream_t st);
+
 int readout(const int64_t *row_ptr, const int32_t *ent, const float *val, int64_t N, const int64_t *targets, int64_t Q,
             float *scores, cudaStream_t st);
 int value_dropout(const float *x, float *y, int64_t n, const int64_t *live, double p, uint64_t seed,
@@ -193,6 +198,17 @@ int fl_relation_rank(const float *w, int64_t rows, int64_t r_size, const int32_t
 int fl_csr_visibility(const int32_t *order, int64_t m, const uint8_t *mask_triple, uint8_t *vis, fl_stream_t stream) {
     FL_REQUIRE(m >= 0 && (m == 0 || (order && mask_triple && vis)), "fl_csr_visibility: bad arguments");
     return csr_visibility(order, m, mask_triple, vis, as_stream(stream));
+}
+
+int fl_csr_mask(const void *mask, int mask_kind, const int32_t *order, int64_t m, const float *weight, float *out,
+                fl_stream_t stream) {
+    return csr_mask(mask, mask_kind, order, m, weight, out, as_stream(stream));
+}
+
+int fl_align_rows(const int64_t *out_b, const int64_t *out_l, const int64_t *out_e, int64_t n, int64_t L,
+                  int64_t rows, const int64_t *g_row_ptr, const int32_t *g_ent, const float *g_val, float *out,
+                  fl_stream_t stream) {
+    return align_rows(out_b, out_l, out_e, n, L, rows, g_row_ptr, g_ent, g_val, out, as_stream(stream));
 }
 
 int fl_hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *ent, const float *val, int64_t S,

@@ -81,23 +81,30 @@ __device__ __forceinline__ bool bsearch64(const int64_t *keys, int64_t n, int64_
     return lo < n && keys[lo] == key;
 }
 
+// Score entries and filter keys whose query lies outside [0, B) are skipped
+// (the reference does not check them); the counters are never indexed by them.
 __global__ void ranks_truth_kernel(const int64_t *ib, const int64_t *ie, const float *v, int64_t nnz,
-                                   const int64_t *targets, float *truth) {
-    int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-    if (i < nnz && ie[i] == targets[ib[i]]) truth[ib[i]] = v[i];
-}
-
-__global__ void ranks_filter_kernel(const int64_t *fk, int64_t nf, int64_t E, int32_t *fcount) {
-    int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-    if (i < nf) atomicAdd(&fcount[fk[i] / E], 1);
-}
-
-__global__ void ranks_count_kernel(const int64_t *ib, const int64_t *ie, const float *v, int64_t nnz,
-                                   const float *truth, const int64_t *fk, int64_t nf, int64_t E, int32_t *greater,
-                                   int32_t *equal, int32_t *expl) {
+                                   const int64_t *targets, int64_t B, float *truth) {
     int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
     if (i >= nnz) return;
     const int64_t b = ib[i];
+    if (b >= 0 && b < B && ie[i] == targets[b]) truth[b] = v[i];
+}
+
+__global__ void ranks_filter_kernel(const int64_t *fk, int64_t nf, int64_t E, int64_t B, int32_t *fcount) {
+    int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (i >= nf || fk[i] < 0) return;
+    const int64_t b = fk[i] / E;
+    if (b < B) atomicAdd(&fcount[b], 1);
+}
+
+__global__ void ranks_count_kernel(const int64_t *ib, const int64_t *ie, const float *v, int64_t nnz,
+                                   const float *truth, const int64_t *fk, int64_t nf, int64_t E, int64_t B,
+                                   int32_t *greater, int32_t *equal, int32_t *expl) {
+    int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (i >= nnz) return;
+    const int64_t b = ib[i];
+    if (b < 0 || b >= B) return;
     if (bsearch64(fk, nf, b * E + ie[i])) return;
     const float t = truth[b];
     atomicAdd(&expl[b], 1);
@@ -217,11 +224,13 @@ int filtered_ranks(const int64_t *ib, const int64_t *ie, const float *v, int64_t
     FL_CUDA(cudaMemsetAsync(equal, 0, B * sizeof(int32_t), st));
     FL_CUDA(cudaMemsetAsync(expl, 0, B * sizeof(int32_t), st));
     FL_CUDA(cudaMemsetAsync(fcount, 0, B * sizeof(int32_t), st));
-    if (nnz > 0) launch(ranks_truth_kernel, static_cast<unsigned>((nnz + 255) / 256), 256, 0, st, ib, ie, v, nnz, targets, truth);
-    if (nf > 0) launch(ranks_filter_kernel, static_cast<unsigned>((nf + 255) / 256), 256, 0, st, fk, nf, E, fcount);
+    if (nnz > 0)
+        launch(ranks_truth_kernel, static_cast<unsigned>((nnz + 255) / 256), 256, 0, st, ib, ie, v, nnz, targets, B,
+               truth);
+    if (nf > 0) launch(ranks_filter_kernel, static_cast<unsigned>((nf + 255) / 256), 256, 0, st, fk, nf, E, B, fcount);
     if (nnz > 0)
         launch(ranks_count_kernel, static_cast<unsigned>((nnz + 255) / 256), 256, 0, st, ib, ie, v, nnz, truth, fk, nf, E,
-                                                                                   greater, equal, expl);
+               B, greater, equal, expl);
     launch(ranks_finalize_kernel, static_cast<unsigned>((B + 255) / 256), 256, 0, st, truth, greater, equal, expl, fcount, B,
                                                                                 E, use_eql, ranks);
     return check_launch("filtered_ranks");
@@ -251,7 +260,10 @@ static int rank_scratch_address(void **out) {
     std::lock_guard<std::mutex> lock(g_rank_scratch_mutex);
     if (g_rank_scratch_addr[dev] == nullptr) {
         // The symbol's host-side name is not a device address; look the
-        // address up once per device, with that device current.
+        // address up once per device, with that device current.  The address
+        // stays valid while the device's primary context lives: a
+        // cudaDeviceReset between calls would leave it stale, so callers of
+        // fl_filtered_ranks_noalloc must not reset the device in between.
         void *p = nullptr;
         FL_CUDA(cudaGetSymbolAddress(&p, g_rank_scratch));
         g_rank_scratch_addr[dev] = p;

@@ -138,12 +138,14 @@ def build_csr_structure(row_indices, col_indices, r_indices, num_nodes):
 
 
 def _apply_mask_order(mask_values, order, weight=None):
+    """CSR-ordered float mask of one side through fl_csr_mask (flashlog.cu:1286-1340)."""
     mask_f = (mask_values if mask_values.dtype == torch.bool else mask_values.float()).contiguous().view(-1)
     _cuda_or_raise(mask_f, "mask preparation")
-    m = mask_f[order.to(device=mask_f.device, dtype=torch.long)].float()
+    order_i = order.to(device=mask_f.device, dtype=torch.int32).contiguous()
+    wt = None
     if weight is not None:
-        m = m * score_function(weight.to(device=mask_f.device, dtype=torch.float).squeeze(-1).view(-1)[order.long()])
-    return m.contiguous()
+        wt = weight.to(device=mask_f.device, dtype=torch.float32).squeeze(-1).contiguous().view(-1)
+    return ops.csr_mask(mask_f, order_i, wt)
 
 
 def _prepared_mask_pair(mask_values):
@@ -168,26 +170,23 @@ def _coo(row_ptr, ent, values, B, Lch, E):
 
 
 def _align_sparse_grad_to_output(grad, out_indices, Lch, E):
-    """Gradient values at the forward's output coordinates (flashlog_kernel.py:360-376)."""
+    """Upstream gradient at the forward's output coordinates (the role of
+    flashlog_kernel.py:360-376), looked up on the row layout by fl_align_rows.
+
+    A dense gradient is indexed directly.  A sparse gradient that sits on the
+    output's own index tensor aligns one to one.  Any other sparse gradient is
+    coalesced, put in the row layout, and every output coordinate is searched
+    in its own row (missing coordinates get 0)."""
     if not grad.is_sparse:
         return grad[tuple(out_indices)].contiguous()
     raw = grad._indices()
     if raw.shape == out_indices.shape and raw.data_ptr() == out_indices.data_ptr():
-        # the gradient sits on the output's own index tensor: values align one to one
         return grad._values().contiguous()
     grad = grad.coalesce()
-    if grad.indices().shape == out_indices.shape and torch.equal(grad.indices(), out_indices):
-        return grad.values().contiguous()
-    keys = out_indices[0] * (Lch * E) + out_indices[1] * E + out_indices[2]
-    gidx = grad.indices()
-    gkeys = gidx[0] * (Lch * E) + gidx[1] * E + gidx[2]
-    values = torch.zeros(keys.numel(), device=grad.device, dtype=grad.dtype)
-    if gkeys.numel() and keys.numel():
-        pos = torch.searchsorted(gkeys, keys)
-        safe = pos.clamp(max=gkeys.numel() - 1)
-        valid = (pos < gkeys.numel()) & (gkeys[safe] == keys)
-        values[valid] = grad.values()[safe[valid]]
-    return values
+    B = int(grad.shape[0])
+    gi = grad.indices()
+    g_row_ptr, g_ent, _ = ops.coo_to_rows(gi[0], gi[1], gi[2], B, Lch, E)
+    return ops.align_rows(out_indices, Lch, B * Lch, g_row_ptr, g_ent, grad.values().to(torch.float32).contiguous())
 
 
 def _rows(sp_batch, sp_level, sp_entity, B, Lch, E, graph=None):

@@ -231,6 +231,37 @@ def relation_rank(w, r_size: int):
     return rank
 
 
+def csr_mask(mask, order, weight=None):
+    """CSR-ordered float mask: mask[order[p]] (* sigmoid(weight[order[p]])), fl_csr_mask."""
+    _require_cuda(mask, order)
+    m = order.numel()
+    out = torch.empty(m, dtype=torch.float32, device=mask.device)
+    if mask.dtype == torch.bool:
+        mk, kind = mask.view(torch.uint8), L.FL_MASK_U8
+    else:
+        mk, kind = mask.to(torch.float32).contiguous(), L.FL_MASK_F32
+    # order is a permutation of the M triple ids (one CSR position per triple):
+    # the mask and the weights need one entry per triple
+    if mk.numel() < m:
+        raise ValueError(f"edge visibility mask must have one entry per triple ({mk.numel()} < {m})")
+    if weight is not None:
+        _require_cuda(weight)
+        if weight.numel() < m:
+            raise ValueError(f"edge weights must have one entry per triple ({weight.numel()} < {m})")
+    check(lib().fl_csr_mask(_p(mk), kind, _p(order), m, _p(weight), _p(out), _stream()), "csr_mask")
+    return out
+
+
+def align_rows(out_indices, Lch: int, rows: int, g_row_ptr, g_ent, g_val):
+    """Gradient values at out_indices (3 x n, int64) from a row-layout gradient (fl_align_rows)."""
+    n = out_indices.shape[1]
+    out = torch.empty(n, dtype=torch.float32, device=g_val.device)
+    oi = out_indices.to(torch.int64).contiguous()
+    check(lib().fl_align_rows(_p(oi[0]), _p(oi[1]), _p(oi[2]), n, Lch, rows, _p(g_row_ptr), _p(g_ent), _p(g_val),
+                              _p(out), _stream()), "align_rows")
+    return out
+
+
 def csr_visibility(graph: Graph, mask_triple):
     """CSR-ordered visibility (u8 per edge, both sides) of a per-triple mask.
 

@@ -15,8 +15,10 @@ capacity of entity e, k_max its maximum, K its sum over the entities (a row
 holds every entity at most once) and C_0 = rows.  zero_slack is 1 without
 dropout: a row keeps at most c1 entries unless it has at most c1 nonzero
 values, and then all of them.  Such a row also keeps its explicit zeros
-(flashlog_kernel.py:1114-1117), so with dropout the selection has no useful
-static bound and zero_slack (default 2) sizes it.  The kernels
+(flashlog_kernel.py:1114-1117).  With dropout p, a row of n entries holds
+about n (1 - p) nonzero values, so the rows kept whole hold up to about
+c1 / (1 - p) entries: zero_slack defaults to 1 / (1 - p) + 0.25 (see
+default_zero_slack; p = 1 leaves the selection unbounded).  The kernels
 read the live counts from the device (row_ptr[-1]), so nothing is read back
 to the host and one step can be captured in a CUDA graph and replayed.  A
 device status word flags any capacity overflow (it cannot happen under these
@@ -40,15 +42,26 @@ def _buf(n, dtype, dev):
     return torch.empty(max(int(n), 1), dtype=dtype, device=dev)
 
 
+def default_zero_slack(p: float) -> float:
+    """Selection slack for dropout p: rows kept whole hold up to about
+    c1 / (1 - p) entries (their explicit zeros included), plus a margin."""
+    if p <= 0.0:
+        return 1.0
+    if p >= 1.0:
+        return math.inf
+    return 1.0 / (1.0 - p) + 0.25
+
+
 def capacities(rows: int, T: int, c1, k_max: int, K: int, E: int, zero_slack: float = 1.0):
     """Static bounds of the step's buffers per hop, as lists (C, S, F, U):
     C_t inputs, S_t selected entries, F_t fact slots, U_t = C_{t+1} outputs,
     with C_0 = rows, S_t = min(C_t, ceil(rows * c1 * zero_slack)) (C_t
-    without c1), F_t = min(S_t * k_max, rows * K), U_t = min(F_t, rows * E)."""
+    without c1, or with an infinite slack), F_t = min(S_t * k_max, rows * K),
+    U_t = min(F_t, rows * E)."""
     Cs, Ss, Fs, Us = [], [], [], []
     C = rows
     for _ in range(T):
-        S = min(C, math.ceil(rows * c1 * zero_slack)) if c1 is not None else C
+        S = min(C, math.ceil(rows * c1 * zero_slack)) if (c1 is not None and math.isfinite(zero_slack)) else C
         F = min(S * k_max, rows * K)
         Cs.append(C)
         Ss.append(S)
@@ -67,15 +80,20 @@ class DrumTrainStep:
     during the step) with `load`.  With apply_update the step ends with the
     SGD update table[rels] -= lr * d loss / d logits (only the batch's rows
     are touched); without it the dense gradient of the table is left in
-    `grad` (for an all-reduce across ranks before the caller's update).
+    `grad` (for an all-reduce across ranks before the caller's update),
+    hop by hop in grad_hop[t] as the backward reaches it (see `parts`).
     dropout > 0 applies the training dropout of each hop's values
     (src/model_DRUM_kernel_sp.py:189-192) in place; replay k (from 1) draws
     hop t's keep bits from (dropout_seed, k, t), counted on the device.
+    A step whose forward overflowed a buffer (status word nonzero) leaves
+    the table and the gradient untouched (the gradient is scaled by 0 on the
+    device); `check` then raises.
     """
 
     def __init__(self, graph: Graph, r_size: int, Q: int, T: int, N: int, c1, c2: int, table: torch.Tensor,
                  n_hide: int, lr: float = 0.01, eps: float = 1e-7, thr: float = 1e-7, stats: bool = True,
-                 apply_update: bool = True, dropout: float = 0.0, dropout_seed: int = 0, zero_slack=None):
+                 apply_update: bool = True, dropout: float = 0.0, dropout_seed: int = 0, zero_slack=None,
+                 record_grad_w: bool = False):
         dev = table.device
         self.dev, self.graph, self.r_size, self.Q, self.T, self.N = dev, graph, r_size, Q, T, N
         self.n = 2 * r_size + 1
@@ -88,9 +106,13 @@ class DrumTrainStep:
             raise ValueError(f"dropout probability must lie in [0, 1], got {dropout}")
         self.dropout, self.dropout_seed = float(dropout), int(dropout_seed) & 0xFFFFFFFFFFFFFFFF
         self.drop_counter = torch.zeros(1, dtype=torch.int64, device=dev)  # replays so far
-        self.zero_slack = (2.0 if self.dropout > 0 else 1.0) if zero_slack is None else float(zero_slack)
+        self.zero_slack = default_zero_slack(self.dropout) if zero_slack is None else float(zero_slack)
         self.table = table
-        self.grad = None if apply_update else torch.zeros_like(table)
+        # without the update: the dense table gradient, one contiguous [2R, N, n]
+        # block per hop (grad_hop[t]); grad views it as the table's [2R, T, N, n]
+        self.grad_hop = None if apply_update else torch.zeros((T,) + tuple(table.shape[:1]) + tuple(table.shape[2:]),
+                                                              dtype=table.dtype, device=dev)
+        self.grad = None if apply_update else self.grad_hop.permute(1, 0, 2, 3)
         rows = Q * N
         self.rows = rows
         csr = graph.csr
@@ -148,9 +170,12 @@ class DrumTrainStep:
         self.fact_dst = _buf(Fmax, i32, dev)
         self.fact_val = _buf(Fmax, f32, dev)
         self.grad_sel = _buf(Smax, f32, dev)
-        self.grad_w = _buf(rows * self.n, f32, dev)
+        # d loss / d w of the hop being differentiated; with record_grad_w one slice per hop is kept
+        self.record_grad_w = bool(record_grad_w)
+        self.grad_w = _buf((T if self.record_grad_w else 1) * rows * self.n, f32, dev)
         self.work = _buf(2, i32, dev)  # the expansion's two work queues
         self.status = torch.zeros(1, dtype=i32, device=dev)
+        self.ok = torch.ones((), dtype=f32, device=dev)  # 1 while the status word is clear
         self.scores = _buf(Q, f32, dev)
         self.loss = torch.zeros((), dtype=f32, device=dev)
         self.grad_logits = torch.empty((Q, T, N, self.n), dtype=f32, device=dev)
@@ -182,6 +207,12 @@ class DrumTrainStep:
         self.rels.copy_(rels)
         self.hide.copy_(hide)
 
+    def grad_w_of(self, t):
+        """d loss / d w of hop t as [Q, N, n] (kept for every hop only with record_grad_w)."""
+        k = t if self.record_grad_w else 0
+        m = self.rows * self.n
+        return self.grad_w[k * m:(k + 1) * m].view(self.Q, self.N, self.n)
+
     def _params(self, t, flags):
         return L.fl_hop_params(self.rows, self.N, self.n, self.r_size, self.graph.E, int(self.topk), int(flags), -1,
                                float(self.eps), int(self.F[t]), self.status.data_ptr(), self.entry_info.data_ptr(),
@@ -193,6 +224,23 @@ class DrumTrainStep:
     # ------------------------------------------------------------------
     def run(self):
         """Forward, loss, backward and (optionally) the SGD update; returns the loss tensor."""
+        for part in self.parts():
+            part()
+        return self.loss
+
+    def parts(self):
+        """The step as T + 1 stream-ordered callables, run in order: the
+        forward, the loss and the backward of hop T-1; then the backward of
+        hops T-2, ..., 0, one per part; last the update.  After part k < T the
+        gradient of hop T-1-k is complete (in grad_hop[T-1-k] when the step
+        does not apply the update itself), so a caller can start that hop's
+        collective while the later parts run; each part can be captured in a
+        CUDA graph of its own."""
+        T = self.T
+        return [self._part_forward] + [lambda t=t: self._backward_hop(t) for t in reversed(range(T - 1))] + \
+            [self._finish]
+
+    def _part_forward(self):
         lb, st, g = lib(), _stream(), self.graph
         rows, N, Q, T = self.rows, self.N, self.Q, self.T
         ws, wsn = _p(self.ws), self.ws.numel()
@@ -249,6 +297,9 @@ class DrumTrainStep:
                 check(lb.fl_hop_stats(_p(rp_s), rows, _p(ent_s), self.S[t], g.ori, g.inv, _p(self.entry_count[t]),
                                       _p(self.out_rp[t]), 0, _p(self.stats), st), "hop_stats")
             rp_in, ent_in, val_in = self.out_rp[t], self.out_ent[t], self.out_y[t]
+        # the backward reads no visibility: restore what the batch hid
+        for k in range(2):
+            self.vis[k].index_put_((hid[k],), old[k])
         # readout + loss (src/utils.py:36-47)
         check(lb.fl_readout(_p(rp_in), _p(ent_in), _p(val_in), N, _p(self.tails), Q, _p(self.scores), st), "readout")
         score = self.scores[:Q]
@@ -258,39 +309,46 @@ class DrumTrainStep:
         check(lb.fl_readout_backward(_p(rp_in), _p(ent_in), N, _p(self.tails), Q, _p(g_score), _p(self.g_y[T - 1]),
                                      self.U[T - 1], _p(self.out_rp[T - 1][rows:]), self._drop(T - 1), st),
               "readout_backward")
-        # backward through the hops; g_y[t] arrives through hop t's dropout
-        # (the same keep bits and scale), applied where it is written
-        for t in reversed(range(T)):
-            params = self._params(t, self.flags)
-            check(lb.fl_hop_backward(ctypes.byref(params), _p(self.rp_sel[t]), _p(self.val_sel[t]), self.S[t],
-                                     _p(self.w[t]), _p(self.slot_base[t]), _p(self.entry_count[t]),
-                                     _p(self.fact_pos[t]), _p(self.fact_rel[t]), None, _p(self.out_rp[t]),
-                                     _p(self.out_x[t]), _p(self.out_denom[t]), _p(self.g_y[t]), _p(self.grad_sel),
-                                     _p(self.grad_w), ws, wsn, st), "hop_backward")
-            if t > 0:
-                src = self.src_sel[t] if self.c1 is not None else None
-                if src is not None:
-                    check(lb.fl_scatter_grad(_p(self.grad_sel), _p(src), self.S[t], _p(self.rp_sel[t][rows:]),
-                                             _p(self.g_y[t - 1]), self.U[t - 1], _p(self.out_rp[t - 1][rows:]),
-                                             self._drop(t - 1), st),
-                          "scatter_grad")
-                else:
-                    self.g_y[t - 1][:self.S[t]].copy_(self.grad_sel[:self.S[t]])
-                    if self.dropout > 0:
-                        self._dropout(self.g_y[t - 1], t - 1, st)
-            # softmax backward, d logits = w * (g - sum(g * w)): torch's own kernel
-            wt = self.w[t][:rows * self.n].view(Q, N, self.n)
-            gw = self.grad_w[:rows * self.n].view(Q, N, self.n)
-            self.grad_logits[:, t].copy_(torch._softmax_backward_data(gw, wt, -1, torch.float32))
+        # a forward that overflowed a buffer updates nothing: its gradient is scaled by 0
+        self.ok.copy_(self.status == 0)
+        self._backward_hop(T - 1)
+
+    def _backward_hop(self, t):
+        """Backward of hop t; g_y[t] arrived through hop t's dropout (the same
+        keep bits and scale), applied where it is written."""
+        lb, st = lib(), _stream()
+        rows, N, Q = self.rows, self.N, self.Q
+        ws, wsn = _p(self.ws), self.ws.numel()
+        params = self._params(t, self.flags)
+        check(lb.fl_hop_backward(ctypes.byref(params), _p(self.rp_sel[t]), _p(self.val_sel[t]), self.S[t],
+                                 _p(self.w[t]), _p(self.slot_base[t]), _p(self.entry_count[t]),
+                                 _p(self.fact_pos[t]), _p(self.fact_rel[t]), None, _p(self.out_rp[t]),
+                                 _p(self.out_x[t]), _p(self.out_denom[t]), _p(self.g_y[t]), _p(self.grad_sel),
+                                 _p(self.grad_w_of(t)), ws, wsn, st), "hop_backward")
+        if t > 0:
+            src = self.src_sel[t] if self.c1 is not None else None
+            if src is not None:
+                check(lb.fl_scatter_grad(_p(self.grad_sel), _p(src), self.S[t], _p(self.rp_sel[t][rows:]),
+                                         _p(self.g_y[t - 1]), self.U[t - 1], _p(self.out_rp[t - 1][rows:]),
+                                         self._drop(t - 1), st),
+                      "scatter_grad")
+            else:
+                self.g_y[t - 1][:self.S[t]].copy_(self.grad_sel[:self.S[t]])
+                if self.dropout > 0:
+                    self._dropout(self.g_y[t - 1], t - 1, st)
+        # softmax backward, d logits = w * (g - sum(g * w)): torch's own kernel
+        wt = self.w[t][:rows * self.n].view(Q, N, self.n)
+        gw = self.grad_w_of(t)
+        torch.mul(torch._softmax_backward_data(gw, wt, -1, torch.float32), self.ok, out=self.grad_logits[:, t])
+        if not self.apply_update:
+            # hop t's dense table gradient, complete once this part has run
+            self.grad_hop[t].zero_()
+            self.grad_hop[t].index_add_(0, self.rels, self.grad_logits[:, t])
+
+    def _finish(self):
         if self.apply_update:
             # SGD on the rows of the batch's relations only: no dense gradient
             self.table.index_add_(0, self.rels, self.grad_logits, alpha=-self.lr)
-        else:
-            self.grad.zero_()
-            self.grad.index_add_(0, self.rels, self.grad_logits)
-        for k in range(2):
-            self.vis[k].index_put_((hid[k],), old[k])
-        return self.loss
 
     def _drop(self, t):
         """fl_dropout of hop t for the kernels that write its values or their gradient (None: no dropout)."""

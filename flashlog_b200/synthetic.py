@@ -144,6 +144,70 @@ def generate_triples(cfg: KGConfig, seed: int = SEED):
     return train, valid, test
 
 
+def generate_triples_device(cfg: KGConfig, seed: int = SEED, device="cuda"):
+    """(train, valid, test) int64 [m, 3] tensors on `device`, drawn there.
+
+    For graphs too large for the host generator (config 5: 86M entities,
+    14,824 relations, 405.6M triples before the split, whose (h, r, t) key
+    needs 68 bits): the same distributions -- relation Zipf(s_rel) over a
+    seeded permutation, uniform (or Zipf) heads, tail Zipf(s_tail) over a
+    seeded entity permutation, duplicates dropped and redrawn, draw order
+    kept -- with torch's device generator seeded by `seed` (a different
+    stream from the host generator's, so the graph is its own seeded
+    instance).  Duplicates are found by two stable sorts, tail then
+    (head, relation)."""
+    import torch
+    dev = torch.device(device)
+    g = torch.Generator(device=dev).manual_seed(int(seed))
+    E, R = cfg.entities, cfg.relations
+    rel_perm = torch.randperm(R, generator=g, device=dev)
+    tail_perm = torch.randperm(E, generator=g, device=dev)
+    head_perm = torch.randperm(E, generator=g, device=dev)
+
+    def zipf_cdf(K, s):
+        c = torch.cumsum(torch.arange(1, K + 1, dtype=torch.float64, device=dev).pow_(-s), 0)
+        return c / c[-1]
+
+    rel_cdf = zipf_cdf(R, cfg.s_rel)
+    tail_cdf = zipf_cdf(E, cfg.s_tail)
+    head_cdf = zipf_cdf(E, cfg.head_zipf) if cfg.head_zipf > 0 else None
+
+    def draw_zipf(cdf, n):
+        u = torch.rand(n, generator=g, dtype=torch.float64, device=dev)
+        return torch.searchsorted(cdf, u, right=True).clamp_max_(cdf.numel() - 1)
+
+    total = cfg.split_all or cfg.train_triples + 2 * (cfg.train_triples // 10)
+    kept = torch.empty((0, 3), dtype=torch.int64, device=dev)
+    while kept.shape[0] < total:
+        need = total - kept.shape[0]
+        draw = int(need * 1.05) + 1024
+        r = rel_perm[draw_zipf(rel_cdf, draw)]
+        t = tail_perm[draw_zipf(tail_cdf, draw)]
+        h = (torch.randint(0, E, (draw,), generator=g, device=dev) if head_cdf is None
+             else head_perm[draw_zipf(head_cdf, draw)])
+        cand = torch.cat([kept, torch.stack([h, r, t], 1)])
+        del h, r, t
+        # lexicographic order of (h * R + r, t), draw order among equals
+        o = torch.sort(cand[:, 2], stable=True)[1]
+        hr = cand[:, 0] * R + cand[:, 1]
+        o = o[torch.sort(hr[o], stable=True)[1]]
+        hr_s, t_s = hr[o], cand[o, 2]
+        first = torch.ones(o.numel(), dtype=torch.bool, device=dev)
+        first[1:] = (hr_s[1:] != hr_s[:-1]) | (t_s[1:] != t_s[:-1])
+        keep_idx = torch.sort(o[first])[0]  # first occurrences, in draw order
+        del o, hr, hr_s, t_s, first
+        kept = cand[keep_idx[:total]]
+        del cand, keep_idx
+    n_train = cfg.train_triples if not cfg.split_all else int(round(total * 0.8))
+    n_valid = cfg.train_triples // 10 if not cfg.split_all else int(round(total * 0.1))
+    return kept[:n_train], kept[n_train:n_train + n_valid], kept[n_train + n_valid:]
+
+
+def host_generation_fits(cfg: KGConfig) -> bool:
+    """Whether generate_triples handles cfg (its duplicate key needs E * R * E < 2^62)."""
+    return float(cfg.entities) * cfg.relations * cfg.entities < 2.0 ** 62
+
+
 def load_or_generate(cfg: KGConfig, seed: int = SEED, cache_dir: str | None = None):
     """Generate the graph once and cache it as .npy under ``cache_dir``."""
     cache_dir = cache_dir or os.environ.get(
@@ -159,6 +223,21 @@ def load_or_generate(cfg: KGConfig, seed: int = SEED, cache_dir: str | None = No
     np.savez(tmp, train=train, valid=valid, test=test)
     os.replace(tmp, path)
     return train, valid, test
+
+
+def load_graph(cfg: KGConfig, device, seed: int = SEED):
+    """The training triples as (host int64 [m, 3] array, device tensor).
+
+    Configs the host generator handles come from load_or_generate (cached);
+    larger ones (config 5) are drawn on the device by generate_triples_device
+    and copied to the host once."""
+    import torch
+    if host_generation_fits(cfg):
+        train, _, _ = load_or_generate(cfg, seed)
+        return train, torch.from_numpy(train).to(device)
+    train_dev, valid, test = generate_triples_device(cfg, seed, device)
+    del valid, test
+    return train_dev.cpu().numpy(), train_dev
 
 
 def training_queries(train: np.ndarray, cfg: KGConfig, step: int = 0, seed: int = SEED):

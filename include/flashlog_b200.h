@@ -181,6 +181,27 @@ int fl_relation_rank(const float *w, int64_t rows, int64_t r_size, const int32_t
  * by the hops. */
 int fl_csr_visibility(const int32_t *order, int64_t m, const uint8_t *mask_triple, uint8_t *vis, fl_stream_t stream);
 
+/* Kinds of the triple-indexed mask of fl_csr_mask. */
+enum { FL_MASK_U8 = 0, FL_MASK_F32 = 1 };
+
+/* CSR-ordered float mask of one side: out[p] = mask[order[p]], times
+ * 1 / (1 + exp(-weight[order[p]])) when weight is not NULL (learnable edge
+ * weights, --use_soft).  Replaces prepare_csr_masks / _apply_mask_order /
+ * apply_mask_cuda (flashlog_kernel.py:225-255, flashlog.cu:1286-1340).
+ * mask is u8 (0 / 1, a bool tensor's bytes) or f32 per triple. */
+int fl_csr_mask(const void *mask, int mask_kind, const int32_t *order, int64_t m, const float *weight, float *out,
+                fl_stream_t stream);
+
+/* Upstream gradient of a hop's output at the output's coordinates: out[i] =
+ * the value of the gradient state at (out_b[i], out_l[i], out_e[i]), or 0
+ * where the gradient has no entry.  The gradient is a row layout (g_row_ptr
+ * i64[rows+1], g_ent i32 ascending per row, g_val f32); every lookup is a
+ * binary search in its own row.  Replaces _align_sparse_grad_to_output
+ * (flashlog_kernel.py:360-376). */
+int fl_align_rows(const int64_t *out_b, const int64_t *out_l, const int64_t *out_e, int64_t n, int64_t L,
+                  int64_t rows, const int64_t *g_row_ptr, const int32_t *g_ent, const float *g_val, float *out,
+                  fl_stream_t stream);
+
 /* Hop expansion (8-lane teams for entries with at most 8 relation groups per
  * side, one warp otherwise).  Replaces
  * fill_sparse3d_topk_kernel / fill_sparse3d_all_edges_kernel /
@@ -355,7 +376,9 @@ int fl_filtered_ranks(const int64_t *idx_b, const int64_t *idx_e, const float *v
  * process exits; the call itself allocates nothing.  At most 65536 queries
  * (B) per call -- larger B returns FL_EINVAL.  The first call on each device
  * looks up that array's device address (cudaGetSymbolAddress) with the device
- * current; make that first call before any stream capture.  All calls share
+ * current; make that first call before any stream capture, and do not reset
+ * the device (cudaDeviceReset) between calls, since the looked-up address
+ * belongs to the context that was current then.  All calls share
  * the one array and each call clears it before counting, so calls that
  * overlap on the GPU (concurrent streams, or host threads sharing a device)
  * race and must be serialized by the caller. */

@@ -72,7 +72,9 @@ def _w(rng, B, L, n, ties):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.path.join(os.sep, "root", "reference"))
+    from oracle.build import reference_root
+    ap.add_argument("--reference", default=reference_root(),
+                    help="reference checkout (default: $FLASHLOG_REFERENCE, else BASELINE.json reference_path)")
     ap.add_argument("--only", choices=["filter", "readout"], help="write only this fixture")
     args = ap.parse_args()
     import torch

@@ -1,0 +1,115 @@
+"""The benchmarked training step on slices of configs 2-5, against the reference CPU.
+
+bench.py times flashlog_b200.step.DrumTrainStep on config 4.  Here the same
+step runs on the first 16 queries of the bench's own first batch (dropout 0,
+every buffer sized as in the bench) for configs 2, 3, 4 and 5 (338M triples,
+86M entities, 29,649 relation columns: the global grad_w accumulators and
+wide relation ranks), and every hop is
+compared with the reference's compiled OpenMP extension
+(flashlog.cpp:1231-1933, built into oracle/_ref) run on the same queries and
+the same fp32 attention weights:
+
+* the c1 selection of every hop and the output coordinates: bit-exact;
+* the normalized values: rel 1e-5 (they are in fact bit-identical: both sum
+  every destination left to right in canonical order);
+* d loss / d w of every hop and d loss / d y of every hop's output:
+  rel 1e-5, with an absolute floor of 1e-6 x the largest magnitude of the
+  hop's reference gradient (the normalization backward subtracts terms, so
+  single entries can cancel to near zero);
+* the loss: rel 1e-6.
+"""
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-5
+QUERIES = 16
+
+
+_cached = {}
+
+
+def _graph(index):
+    """Config `index`'s training graph: device CSR and the host CSR for the
+    reference.  Configs 2-4 build the host CSR with the oracle (pinned to
+    csr.cpp); config 5 (338M triples, drawn on the device) copies the device
+    CSR, whose builder other tests pin bit for bit to csr.cpp.  One config is
+    held at a time."""
+    if index in _cached:
+        return _cached[index]
+    _cached.clear()
+    torch.cuda.empty_cache()
+    from flashlog_b200.flashlog_kernel import build_csr_structure
+    from flashlog_b200.ops import Graph
+    from flashlog_b200.synthetic import CONFIGS, host_generation_fits, load_graph
+    from oracle import oracle as O
+    cfg = CONFIGS[index]
+    train, tt = load_graph(cfg, torch.device("cuda"))
+    csr = build_csr_structure(tt[:, 0], tt[:, 2], tt[:, 1], cfg.entities)
+    del tt
+    torch.cuda.empty_cache()
+    if host_generation_fits(cfg):
+        csr_np = O.build_csr(train[:, 0], train[:, 2], train[:, 1], cfg.entities)
+    else:
+        csr_np = tuple(c.cpu().numpy() for c in csr)
+    _cached[index] = (cfg, train, Graph.of(csr), csr_np)
+    return _cached[index]
+
+
+def _close(got, want, what):
+    scale = float(np.abs(want).max()) if want.size else 0.0
+    np.testing.assert_allclose(got, want, rtol=RTOL, atol=1e-6 * scale, err_msg=what)
+
+
+@pytest.mark.parametrize("index", [2, 3, 4, 5])
+def test_train_step_slice_matches_reference_cpu(index):
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from oracle import cpu_baseline as CB
+    from oracle import reference as Rf
+    if not Rf.available():
+        pytest.skip("the reference CPU extension (oracle/_ref) is not built")
+    from flashlog_b200.step import DrumTrainStep
+    from flashlog_b200.synthetic import training_queries
+    cfg, train, graph, csr_np = _graph(index)
+    R, T, N, E = cfg.relations, cfg.T, cfg.N, cfg.entities
+    n = 2 * R + 1
+    # the bench's first batch of rank 0 (bench.batches_for), first 16 queries = 8 triples
+    ids, h, r, t = training_queries(train, cfg, step=0, seed=1234)
+    ids, h, r, t = ids[:QUERIES // 2], h[:QUERIES], r[:QUERIES], t[:QUERIES]
+    # one table row per distinct query relation of the slice (config 5's full
+    # [2R, T, N, n] table would take 31.6 GB); only the row index changes
+    rels, r = np.unique(r, return_inverse=True)
+    gen = torch.Generator(device="cpu").manual_seed(1234)
+    table = torch.randn(rels.size, T, N, n, generator=gen).cuda()
+    dev = torch.device("cuda")
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.int64)).to(dev)
+    step = DrumTrainStep(graph, R, QUERIES, T, N, cfg.c1 or None, cfg.c2, table, n_hide=ids.size,
+                         apply_update=False, dropout=0.0, record_grad_w=True)
+    step.load(d(h), d(t), d(r), d(ids))
+    loss = float(step.run())
+    torch.cuda.synchronize()
+    step.check()
+    rows = QUERIES * N
+    w_hops = [step.w[k][:rows * n].view(QUERIES, N, n).cpu().numpy() for k in range(T)]
+    mask = np.ones(train.shape[0], np.uint8)
+    mask[ids] = 0
+    ref = CB.drum_step_trace(csr_np, h, t, w_hops, mask, R, E, cfg.c1, cfg.c2)
+    assert loss == pytest.approx(ref["loss"], rel=1e-6)
+    for k, hop in enumerate(ref["hops"]):
+        s_live = int(step.rp_sel[k][rows])
+        assert np.array_equal(step.src_sel[k][:s_live].cpu().numpy(), hop["sel"]), f"hop {k}: c1 selection"
+        counts = (step.out_rp[k][1:rows + 1] - step.out_rp[k][:rows]).cpu().numpy()
+        u = int(counts.sum())
+        assert np.array_equal(np.repeat(np.arange(rows), counts), hop["out_row"]), f"hop {k}: output rows"
+        assert np.array_equal(step.out_ent[k][:u].cpu().numpy().astype(np.int64), hop["out_ent"]), \
+            f"hop {k}: output entities"
+        _close(step.out_y[k][:u].cpu().numpy(), hop["y"], f"hop {k}: values")
+        _close(step.g_y[k][:u].cpu().numpy(), hop["g_out"], f"hop {k}: d loss / d y")
+        _close(step.grad_w_of(k).cpu().numpy(), hop["gw"], f"hop {k}: d loss / d w")
+    # the slice is not trivial: the last hop expands hub frontiers under both budgets
+    last = ref["hops"][-1]
+    assert last["facts"] > 1000 and last["out_ent"].size > 1000

@@ -550,6 +550,26 @@ def test_filtered_ranks_match_oracle_and_golden(fk, golden):
         np.testing.assert_array_equal(hits, d[f"r{ci}_hits"])
 
 
+def test_filtered_ranks_skip_queries_out_of_range(fk, golden):
+    """A score entry or a filter key whose query lies outside [0, B) is
+    skipped: the ranks equal those computed without it (the counters are
+    never indexed by it)."""
+    d = golden("ranks.npz")
+    keys, B, E = d["r0_keys"], int(d["r0_B"]), int(d["r0_E"])
+    targets = d["r0_targets"]
+    filt = np.unique(np.concatenate([d["r0_fb"] * E + d["r0_fe"], np.arange(B) * E + targets]))
+    vals = d["r0_vals"]
+    want = fk.sparse2d_filtered_ranks_cuda(_cuda(keys // E), _cuda(keys % E), _cuda(vals), _cuda(targets),
+                                           _cuda(filt), B, E, True).cpu().numpy()
+    ib = np.concatenate([keys // E, [B, B + 5]])
+    ie = np.concatenate([keys % E, [0, 1]])
+    v = np.concatenate([vals, np.float32([0.5, 0.25])]).astype(np.float32)
+    filt2 = np.concatenate([filt, [B * E + 3, (B + 7) * E]])
+    got = fk.sparse2d_filtered_ranks_cuda(_cuda(ib), _cuda(ie), _cuda(v), _cuda(targets), _cuda(filt2), B, E,
+                                          True).cpu().numpy()
+    assert np.array_equal(got, want)
+
+
 def test_hop_is_deterministic(fk, g1):
     cfg, train, csr_np, csr = g1
     E, R = cfg.entities, cfg.relations

@@ -142,3 +142,30 @@ def test_step_capacity_bounds():
     assert S2[2] == 2 * S[2] and F2[2] == 2 * F[2] and S2[:2] == S[:2]
     Cn, Sn, Fn, Un = capacities(4, 2, None, 3, 10, 5)
     assert Sn == Cn == [4, 12] and Fn == [12, 36] and Un == [12, 20]
+
+
+def test_default_zero_slack_covers_rows_kept_whole():
+    """With dropout p a row of n entries keeps all of them (zeros included)
+    while at most c1 values survive, so the rows kept whole hold about
+    c1 / (1 - p) entries: the default slack covers the largest such row in a
+    simulation of 1536 rows per p, including p = 0.5 and beyond; p = 1
+    leaves the selection unbounded."""
+    import math
+
+    import numpy as np
+
+    from flashlog_b200.step import capacities, default_zero_slack
+    assert default_zero_slack(0.0) == 1.0
+    assert math.isinf(default_zero_slack(1.0))
+    rng = np.random.default_rng(5)
+    c1, rows = 1000, 1536
+    for p in (0.1, 0.3, 0.5, 0.7):
+        slack = default_zero_slack(p)
+        assert slack >= 1.0 / (1.0 - p)
+        n = rng.integers(0, 4 * int(c1 / (1 - p)), rows)
+        survivors = rng.binomial(n, 1.0 - p)
+        kept = np.where(survivors <= c1, n, c1)
+        assert kept.max() <= c1 * slack, p
+        assert kept.sum() <= rows * c1 * slack, p
+    C, S, F, U = capacities(8, 2, 10, 3, 100, 50, zero_slack=math.inf)
+    assert S == C
