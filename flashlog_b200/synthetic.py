@@ -262,3 +262,52 @@ def random_attention(queries: int, T: int, N: int, n: int, seed: int = SEED, std
     logits -= logits.max(axis=-1, keepdims=True)
     e = np.exp(logits)
     return (e / e.sum(axis=-1, keepdims=True)).astype(np.float32)
+
+
+def evaluation_queries(test: np.ndarray, relations: int, max_triples: int | None = None):
+    """Test queries as in rules/evaluate.py:122-128: every triple (h, r, t)
+    gives (h, r, t) and (t, r + R, h).  Returns (sources, relations, targets)."""
+    test = test if max_triples is None else test[:max_triples]
+    h, r, t = test[:, 0], test[:, 1], test[:, 2]
+    src = np.stack([h, t], 1).reshape(-1).astype(np.int64)
+    rel = np.stack([r, r + relations], 1).reshape(-1).astype(np.int64)
+    dst = np.stack([t, h], 1).reshape(-1).astype(np.int64)
+    return src, rel, dst
+
+
+def rule_bank(train: np.ndarray, query_relations: np.ndarray, relations: int, n_rules: int = 50_000,
+              seed: int = SEED, uniform_ops: bool = False, groups: int = 3):
+    """A seeded Horn-rule bank in the reference's rule format (rules/evaluate.py:63-92).
+
+    Heads are drawn in proportion to the frequency of the query relations;
+    body lengths are uniform on {1, 2, 3}; body operators are directed
+    relations (r forward, r + R inverse) drawn in proportion to their edge
+    counts in the training graph, so bodies ground (uniform over the 2R
+    operators with uniform_ops); weights ~ U(0, 1); group_id ~ U{0, 1, 2}.
+    Each rule is a dict with rule_id, head, body (tuple), weight, group_id
+    and rank_weights None, as load_rules returns."""
+    rng = np.random.Generator(np.random.PCG64([seed, 11]))
+    R = relations
+    head_freq = np.bincount(np.asarray(query_relations, np.int64), minlength=2 * R).astype(np.float64)
+    heads = rng.choice(2 * R, size=n_rules, p=head_freq / head_freq.sum())
+    lengths = rng.integers(1, 4, size=n_rules)
+    if uniform_ops:
+        op_p = np.full(2 * R, 1.0 / (2 * R))
+    else:
+        edge = np.bincount(np.asarray(train[:, 1], np.int64), minlength=R).astype(np.float64)
+        op_p = np.concatenate([edge, edge])
+        op_p /= op_p.sum()
+    ops_ = rng.choice(2 * R, size=(n_rules, 3), p=op_p)
+    weights = rng.random(n_rules)
+    group = rng.integers(0, groups, size=n_rules)
+    return [{"rule_id": k, "head": int(heads[k]), "body": tuple(int(o) for o in ops_[k, :lengths[k]]),
+             "weight": float(weights[k]), "rank_weights": None, "group_id": int(group[k])}
+            for k in range(n_rules)]
+
+
+def write_rules_tsv(path: str, rules) -> None:
+    """The rule TSV read by rules/evaluate.py:63-92 (head_id, body_ids, weight, group_id)."""
+    with open(path, "w") as f:
+        f.write("head_id\tbody_ids\tweight\tgroup_id\n")
+        for r in rules:
+            f.write(f"{r['head']}\t{' '.join(str(o) for o in r['body'])}\t{r['weight']!r}\t{r['group_id']}\n")
