@@ -62,6 +62,11 @@ def parse():
                     help="training dropout of each hop's values (src/main.py:1008 default 0.1)")
     ap.add_argument("--engine", default="graph", choices=["graph", "autograd"],
                     help="graph: static-buffer step replayed as CUDA graphs; autograd: engine.drum_propagate")
+    ap.add_argument("--rules", type=int, default=0,
+                    help="instead of the training step: max-product rule-bank evaluation of this many test "
+                         "queries (sharded over the ranks), --rule-bank rules, queries/s")
+    ap.add_argument("--rule-bank", type=int, default=50_000)
+    ap.add_argument("--rule-max", action="store_true", help="mmDRUM (max over ranks); default smDRUM (sum)")
     return ap.parse_args()
 
 
@@ -496,6 +501,76 @@ def cpu_baseline(args, cfg, train, csr):
                        f"dropout {args.dropout} on every hop's values")
 
 
+def run_rules(args, rank, world, device):
+    """Max-product rule-bank evaluation (rules/evaluate.py routed_normalized,
+    reduction 'max'): the config's test split gives args.rules queries
+    (both directions of each triple), a seeded bank of args.rule_bank rules
+    (heads by query-relation frequency, bodies of 1-3 operators by edge
+    frequency, weights U(0, 1), three groups) routes to them, and every rank
+    ranks its contiguous share of the queries (filtered by the targets).
+    value = queries / device time (max over ranks)."""
+    from flashlog_b200 import multigpu as MG
+    from flashlog_b200 import rules as RB
+    from flashlog_b200.flashlog_kernel import build_csr_structure
+    from flashlog_b200.synthetic import (evaluation_queries, generate_triples_device, host_generation_fits,
+                                         rule_bank)
+    import torch.distributed as dist
+    cfg = CONFIGS[args.config]
+    if host_generation_fits(cfg):
+        train, _, test = load_or_generate(cfg)
+        tt = torch.from_numpy(train).to(device)
+    else:
+        tt, _, test_dev = generate_triples_device(cfg, device=device)
+        train, test = tt.cpu().numpy(), test_dev.cpu().numpy()
+        del test_dev
+    csr = build_csr_structure(tt[:, 0], tt[:, 2], tt[:, 1], cfg.entities)
+    del tt
+    torch.cuda.empty_cache()
+    src, rel, dst = evaluation_queries(test, cfg.relations, (args.rules + 1) // 2)
+    src, rel, dst = src[:args.rules], rel[:args.rules], dst[:args.rules]
+    rules = rule_bank(train, rel, cfg.relations, args.rule_bank)
+    lo, hi = MG.shard_bounds(src.size, rank, world)
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a[lo:hi])).to(device)
+    s_d, r_d, t_d = d(src), d(rel), d(dst)
+    stats = {}
+    # warm-up: the first relation group (kernel attributes, allocator)
+    w_n = min(64, hi - lo)
+    RB.evaluate_rule_bank(s_d[:w_n], r_d[:w_n], t_d[:w_n], rules, csr, cfg.relations, cfg.entities,
+                          final_max=args.rule_max)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    from flashlog_b200 import _lib
+    l0 = _lib.lib().fl_launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_wall = time.perf_counter()
+    e0.record()
+    ranks = RB.evaluate_rule_bank(s_d, r_d, t_d, rules, csr, cfg.relations, cfg.entities, final_max=args.rule_max,
+                                  stats=stats)
+    e1.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t_wall
+    ms = e0.elapsed_time(e1)
+    launches = _lib.lib().fl_launch_count() - l0
+    all_ranks = MG.gather_varlen(ranks) if world > 1 else ranks
+    n_q = hi - lo
+    if world > 1:
+        ms, n_q = MG.max_time_sum_work(ms, n_q, device)
+    if rank == 0:
+        r = all_ranks.cpu().numpy()
+        line = {"metric": "rule-bank queries/sec (max-product, routed_normalized)", "value": n_q / (ms / 1000.0),
+                "unit": "queries/s", "n_gpus": world, "ms_total": ms, "wall_s_rank0": wall,
+                "higher_is_better": True, "scaling": "strong", "dtype": "f32", "data": "synthetic",
+                "config": {"workload": f"config {cfg.index}: {cfg.entities} entities, {cfg.train_triples} triples; "
+                                       f"{args.rules} test queries, {args.rule_bank} rules, "
+                                       f"{'mmDRUM (max)' if args.rule_max else 'smDRUM (sum)'} over 3 ranks",
+                           "parallelism": f"query-sharded dp{world}"},
+                "metrics": {"mrr": float((1.0 / r).mean()), "hits@10": float((r <= 10).mean())},
+                "rules_after_pruning_last_batch": stats.get("rules_after"),
+                "gpu_launches": launches}
+        print(json.dumps(line))
+
+
 def workload_desc(cfg, world):
     return (f"config {cfg.index}: {cfg.entities} entities, {cfg.relations} relations (+inverses), "
             f"{cfg.train_triples} triples; DRUM T={cfg.T} N={cfg.N}, batch {cfg.batch_size} "
@@ -568,6 +643,12 @@ def main():
     if world > 1:
         import datetime
         dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=300))
+    if args.rules:
+        run_rules(args, rank, world, device)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     cfg, train, csr = setup(args, rank, world, device)
     if args.engine == "graph":
         res = run_graph_arm(args, cfg, train, csr, rank, world, device)

@@ -27,6 +27,7 @@ FL_NO_INV = 512
 FL_EDGE_POS = 1024
 FL_NO_NORMALIZE = 1 << 20
 FL_MAX_BITS = 1
+FL_MAX_VALUE_ONLY = 2
 FL_MASK_U8 = 0
 FL_MASK_F32 = 1
 FL_ENTRY_INFO_INTS = 5  # int32 values per entry in fl_hop_params.entry_info
@@ -131,6 +132,7 @@ SIGNATURES = {
                                               ctypes.POINTER(ctypes.c_int64), _P, _SZ, _P]),
     "fl_fixed_relation_fill": (ctypes.c_int, [_P, _P, _P, _P, _I64, _P, _I64, _I64, _SIDE, _SIDE, _P, _P, _P, _P,
                                               _P]),
+    "fl_rule_rank_facts": (ctypes.c_int, [_P, _P, _P, _I64, _I64, _P, _I64, _P, _P, _P, _P, _P, _P, _P]),
     "fl_filtered_ranks_workspace": (_SZ, [_I64]),
     "fl_filtered_ranks": (ctypes.c_int, [_P, _P, _P, _I64, _P, _P, _I64, _I64, _I64, ctypes.c_int, _P, _P, _SZ,
                                          _P]),

@@ -49,6 +49,9 @@ int fixed_relation_fill(const int64_t *b, const int64_t *l, const int32_t *ent, 
                         const int64_t *slot_base, int32_t *fact_dst, float *fact_val, int32_t *entry_count,
                         cudaStream_t st);
 size_t filtered_ranks_workspace(int64_t B);
+int rule_rank_facts(const int64_t *st_rp, const int32_t *st_ent, const float *st_val, int64_t B, int64_t C,
+                    const float *w, int64_t ranks, const int64_t *run_rp, const int32_t *run_ent, const float *run_val,
+                    int64_t *slot_base, int32_t *fact_dst, float *fact_val, cudaStream_t st);
 int rule_max_reduce(const int64_t *row_ptr, int64_t rows, const int32_t *ent, const float *val, int64_t C,
                     const float *weights, int64_t ranks, int64_t B, int64_t E, unsigned int *acc, cudaStream_t st);
 int filtered_ranks(const int64_t *ib, const int64_t *ie, const float *v, int64_t nnz, const int64_t *targets,
@@ -231,8 +234,8 @@ int fl_row_reduce_max(const int64_t *row_ptr, int64_t rows, int64_t E, int64_t r
                       int32_t *out_ent, float *out_x, int max_flags, int32_t *status, void *ws, size_t ws_bytes,
                       fl_stream_t stream) {
     return row_reduce_max(row_ptr, rows, E, r_size, slot_base, fact_dst, fact_val, fact_rel, fact_edge, total_slots,
-                          fact_pos, out_row_ptr, out_ent, out_x, (max_flags & FL_MAX_BITS) ? 2 : 1, status, ws,
-                          ws_bytes, as_stream(stream));
+                          fact_pos, out_row_ptr, out_ent, out_x, (max_flags & FL_MAX_BITS) ? 2 : 1,
+                          (max_flags & FL_MAX_VALUE_ONLY) != 0, status, ws, ws_bytes, as_stream(stream));
 }
 
 int fl_row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *slot_base, const int32_t *entry_count,
@@ -311,6 +314,14 @@ size_t fl_filtered_ranks_workspace(int64_t B) { return filtered_ranks_workspace(
 int fl_rule_max_reduce(const int64_t *row_ptr, int64_t rows, const int32_t *ent, const float *val, int64_t C,
                        const float *weights, int64_t ranks, int64_t B, int64_t E, uint32_t *acc, fl_stream_t stream) {
     return rule_max_reduce(row_ptr, rows, ent, val, C, weights, ranks, B, E, acc, as_stream(stream));
+}
+
+int fl_rule_rank_facts(const int64_t *st_rp, const int32_t *st_ent, const float *st_val, int64_t B, int64_t C,
+                       const float *w, int64_t ranks, const int64_t *run_rp, const int32_t *run_ent,
+                       const float *run_val, int64_t *slot_base, int32_t *fact_dst, float *fact_val,
+                       fl_stream_t stream) {
+    return rule_rank_facts(st_rp, st_ent, st_val, B, C, w, ranks, run_rp, run_ent, run_val, slot_base, fact_dst,
+                           fact_val, as_stream(stream));
 }
 
 int fl_filtered_ranks(const int64_t *idx_b, const int64_t *idx_e, const float *values, int64_t nnz,

@@ -1111,6 +1111,7 @@ __device__ __forceinline__ bool max_equal(int mode, float v, float x) {
 
 // Tie key of a fact for the MAX coalesce: (source, triple id).
 __device__ __forceinline__ unsigned long long max_tie_key(const ReduceArgs &a, int64_t slot) {
+    if (a.fact_rel == nullptr) return 0ull;  // FL_MAX_VALUE_ONLY: no tie keys
     const int64_t rel = a.fact_rel[slot];
     const unsigned long long src = rel == a.n - 1 ? 2ull : (rel >= a.r_size ? 1ull : 0ull);
     return (src << 32) | static_cast<uint32_t>(a.fact_edge[slot]);
@@ -2428,9 +2429,11 @@ int row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *s
 int row_reduce_max(const int64_t *row_ptr, int64_t rows, int64_t E, int64_t r_size, const int64_t *slot_base,
                    const int32_t *fact_dst, const float *fact_val, const int16_t *fact_rel, const int32_t *fact_edge,
                    int64_t total_slots, int32_t *fact_pos, int64_t *out_row_ptr, int32_t *out_ent, float *out_x,
-                   int max_mode, int32_t *status, void *ws, size_t ws_bytes, cudaStream_t st) {
-    FL_REQUIRE(fact_rel != nullptr && fact_edge != nullptr, "the MAX reduction needs fact relations and triple ids");
+                   int max_mode, bool value_only, int32_t *status, void *ws, size_t ws_bytes, cudaStream_t st) {
     FL_REQUIRE(max_mode == 1 || max_mode == 2, "bad MAX mode");
+    if (value_only) fact_rel = nullptr, fact_edge = nullptr;
+    FL_REQUIRE(fact_rel != nullptr && fact_edge != nullptr,
+               "the MAX reduction needs fact relations and triple ids (or FL_MAX_VALUE_ONLY)");
     return reduce_rows(row_ptr, rows, E, slot_base, fact_dst, fact_val, total_slots, fact_pos, 1e-7f, out_row_ptr,
                        out_ent, out_x, nullptr, nullptr, status, max_mode, r_size, fact_rel, fact_edge, nullptr, ws,
                        ws_bytes, nullptr, st);

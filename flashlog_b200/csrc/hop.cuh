@@ -22,7 +22,7 @@ int hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *en
 int row_reduce_max(const int64_t *row_ptr, int64_t rows, int64_t E, int64_t r_size, const int64_t *slot_base,
                    const int32_t *fact_dst, const float *fact_val, const int16_t *fact_rel, const int32_t *fact_edge,
                    int64_t total_slots, int32_t *fact_pos, int64_t *out_row_ptr, int32_t *out_ent, float *out_x,
-                   int max_mode, int32_t *status, void *ws, size_t ws_bytes, cudaStream_t st);
+                   int max_mode, bool value_only, int32_t *status, void *ws, size_t ws_bytes, cudaStream_t st);
 int row_reduce(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *slot_base, const int32_t *entry_count,
                const int32_t *fact_dst, const float *fact_val, int64_t total_slots, int32_t *fact_pos, float eps,
                int64_t *out_row_ptr, int32_t *out_ent, float *out_x, float *out_y, float *out_denom, int32_t *status,

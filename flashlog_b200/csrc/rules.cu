@@ -159,7 +159,61 @@ __global__ void rule_max_kernel(const int64_t *row_ptr, int64_t rows, const int3
     }
 }
 
+// Row starts of the rank rows (q, r): the running maxima of the row, then r
+// copies of query q's entries before it, after every earlier query's.
+__global__ void rank_slots_kernel(const int64_t *st_rp, int64_t B, int64_t C, int64_t ranks, const int64_t *run_rp,
+                                  int64_t *slot_base) {
+    const int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (row > B * ranks) return;
+    const int64_t q = row / ranks, r = row % ranks;
+    const int64_t base = st_rp[q * C];
+    const int64_t nq = q < B ? st_rp[(q + 1) * C] - base : 0;
+    slot_base[row] = (run_rp != nullptr ? run_rp[row] : 0) + ranks * base + r * nq;
+}
+
+// One block per rank row (q, r): the running maxima, then the entries of the
+// rule rows (q, c) in rule order with the weight of rule c at rank r.
+__global__ void rank_facts_kernel(const int64_t *st_rp, const int32_t *st_ent, const float *st_val, int64_t C,
+                                  const float *w, int64_t ranks, const int64_t *run_rp, const int32_t *run_ent,
+                                  const float *run_val, const int64_t *slot_base, int32_t *fact_dst,
+                                  float *fact_val) {
+    const int64_t row = blockIdx.x;
+    const int64_t q = row / ranks, r = row % ranks;
+    int64_t s = slot_base[row];
+    if (run_rp != nullptr) {
+        const int64_t a = run_rp[row], n = run_rp[row + 1] - a;
+        for (int64_t j = threadIdx.x; j < n; j += blockDim.x) {
+            fact_dst[s + j] = run_ent[a + j];
+            fact_val[s + j] = run_val[a + j];
+        }
+        s += n;
+    }
+    const int64_t base = st_rp[q * C];
+    for (int64_t c = 0; c < C; ++c) {
+        const int64_t a = st_rp[q * C + c], b = st_rp[q * C + c + 1];
+        const float wv = w[c * ranks + r];
+        for (int64_t i = a + threadIdx.x; i < b; i += blockDim.x) {
+            const bool ok = wv != 0.0f && st_val[i] > 0.0f;
+            fact_dst[s + (i - base)] = ok ? st_ent[i] : -1;
+            fact_val[s + (i - base)] = wv;
+        }
+    }
+}
+
 }  // namespace
+
+int rule_rank_facts(const int64_t *st_rp, const int32_t *st_ent, const float *st_val, int64_t B, int64_t C,
+                    const float *w, int64_t ranks, const int64_t *run_rp, const int32_t *run_ent, const float *run_val,
+                    int64_t *slot_base, int32_t *fact_dst, float *fact_val, cudaStream_t st) {
+    FL_REQUIRE(B >= 0 && C > 0 && ranks > 0 && st_rp && slot_base && w, "fl_rule_rank_facts: bad arguments");
+    const int64_t rows = B * ranks;
+    launch(rank_slots_kernel, static_cast<unsigned>((rows + 1 + 255) / 256), 256, 0, st, st_rp, B, C, ranks, run_rp,
+           slot_base);
+    if (rows > 0)
+        launch(rank_facts_kernel, static_cast<unsigned>(rows), 256, 0, st, st_rp, st_ent, st_val, C, w, ranks, run_rp,
+               run_ent, run_val, slot_base, fact_dst, fact_val);
+    return check_launch("rule_rank_facts");
+}
 
 size_t fixed_relation_workspace(int64_t nnz) { return carve_bytes<int64_t>(nnz + 1) + scan_workspace(nnz) + 1024; }
 

@@ -534,6 +534,42 @@ def fixed_relation(b, l, e, v, ops_, graph: Graph, r_size: int, B: int, Lr: int)
     return out_row_ptr, out_ent[:u], out_x[:u]
 
 
+def row_max(slot_base, fact_dst, fact_val, rows: int, E: int):
+    """Per row r, the maximum fact value of every destination among the slots
+    [slot_base[r], slot_base[r + 1]) (destination -1: no fact); returns the
+    row layout (row_ptr, ent, val).  One host read sizes the outputs."""
+    dev = fact_val.device
+    T = max(int(fact_dst.numel()), 1)
+    entries = torch.arange(rows + 1, dtype=torch.int64, device=dev)
+    out_row_ptr = torch.empty(rows + 1, dtype=torch.int64, device=dev)
+    out_ent = torch.empty(T, dtype=torch.int32, device=dev)
+    out_x = torch.empty(T, dtype=torch.float32, device=dev)
+    ws = _ws(lib().fl_reduce_workspace(rows, T), dev)
+    check(lib().fl_row_reduce_max(_p(entries), rows, E, 1, _p(slot_base), _p(fact_dst), _p(fact_val), None, None,
+                                  fact_dst.numel(), None, _p(out_row_ptr), _p(out_ent), _p(out_x),
+                                  L.FL_MAX_VALUE_ONLY, None, _p(ws), ws.numel(), _stream()), "row_max")
+    u = int(out_row_ptr[rows].item())
+    return out_row_ptr, out_ent[:u], out_x[:u]
+
+
+def rule_rank_maxima(st_rp, st_ent, st_val, B: int, C: int, w, ranks: int, E: int, running=None):
+    """Rank rows (q, r) of the largest rule weight reaching each entity: the
+    grounded rows q * C + c of one rule chunk (weights w [C, ranks]) merged
+    with the running maxima of earlier chunks (a rank-row layout or None)."""
+    dev = st_val.device
+    rows = B * ranks
+    run_rp, run_ent, run_val = running if running is not None else (None, None, None)
+    slot_base = torch.empty(rows + 1, dtype=torch.int64, device=dev)
+    n_run = 0 if running is None else run_ent.numel()
+    T = n_run + ranks * st_ent.numel()
+    fact_dst = torch.empty(max(T, 1), dtype=torch.int32, device=dev)
+    fact_val = torch.empty(max(T, 1), dtype=torch.float32, device=dev)
+    check(lib().fl_rule_rank_facts(_p(st_rp), _p(st_ent), _p(st_val), B, C, _p(w.contiguous()), ranks, _p(run_rp),
+                                   _p(run_ent), _p(run_val), _p(slot_base), _p(fact_dst), _p(fact_val), _stream()),
+          "rule_rank_facts")
+    return row_max(slot_base, fact_dst[:T], fact_val[:T], rows, E)
+
+
 def channel_merge(row_ptr, ent, val, B: int, Lch: int, E: int):
     """Rows (b, l) of a [B, L, E] state merged into rows b: per query the
     sorted union of its channels' entities with each entity's values summed

@@ -253,7 +253,9 @@ int fl_row_reduce_max(const int64_t *row_ptr, int64_t rows, int64_t E, int64_t r
 /* max_flags of fl_row_reduce_max: compare values by their fp32 bit patterns as
  * unsigned integers, the order of the packed (value, ~position) CAS-max of the
  * dense MAX path (flashlog.cu:103-121, 523-581). */
-enum { FL_MAX_BITS = 1 };
+enum { FL_MAX_BITS = 1,
+       FL_MAX_VALUE_ONLY = 2 /* only the maxima are wanted: fact_rel and fact_edge may be NULL,
+                                equal values tie at no key (any of them gives the same value) */ };
 
 /* Hop backward (+ normalization backward unless FL_NO_NORMALIZE).  Replaces
  * flashlog_backward_sparse3d_cached_cuda (flashlog.cu:2317-2361) and
@@ -362,6 +364,22 @@ int fl_fixed_relation_fill(const int64_t *b, const int64_t *l, const int32_t *en
  * weights must be finite and nonnegative.  Order-independent and exact. */
 int fl_rule_max_reduce(const int64_t *row_ptr, int64_t rows, const int32_t *ent, const float *val, int64_t C,
                        const float *weights, int64_t ranks, int64_t B, int64_t E, uint32_t *acc, fl_stream_t stream);
+
+/* Sparse max-product accumulation (rules/shared_inference.py:176-206 when
+ * the dense [ranks, B, E] accumulator does not fit, as with 86M entities): the
+ * facts of the rank rows (q, r), r < ranks, laid out for fl_row_reduce_max.
+ * The grounded state has rows q * C + c (row_ptr st_rp[B*C+1], entities
+ * st_ent, values st_val); the running maxima of earlier chunks are rank rows
+ * (run_rp[B*ranks+1], run_ent, run_val), or NULL for the first chunk.  Row
+ * (q, r) holds its running maxima, then every entry of the rows (q, c) with
+ * its rule's weight w[c * ranks + r] as value (destination -1, no fact, where
+ * the weight or the state value is 0).  slot_base i64[B*ranks+1] gets the row
+ * starts (run_rp[row] + ranks * st_rp[q*C] + r * (entries of query q)),
+ * fact_dst / fact_val i32 / f32[slot_base[B*ranks]] the facts. */
+int fl_rule_rank_facts(const int64_t *st_rp, const int32_t *st_ent, const float *st_val, int64_t B, int64_t C,
+                       const float *w, int64_t ranks, const int64_t *run_rp, const int32_t *run_ent,
+                       const float *run_val, int64_t *slot_base, int32_t *fact_dst, float *fact_val,
+                       fl_stream_t stream);
 
 size_t fl_filtered_ranks_workspace(int64_t B);
 int fl_filtered_ranks(const int64_t *idx_b, const int64_t *idx_e, const float *values, int64_t nnz,

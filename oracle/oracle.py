@@ -474,6 +474,56 @@ def max_product(sources, bodies, weights, csr, r_size, E, final_max=False):
     return keys, combined[keys]
 
 
+def max_product_sparse(sources, bodies, weights, csr, r_size, E, final_max=False):
+    """max_product without the dense [ranks, B, E] accumulator, for graphs
+    with tens of millions of entities: the same Boolean grounding
+    (flashlog.cu:1561-1741 then values > 0), per rank the largest weight of
+    the rules reaching an entity (zero weights contribute nothing, as the
+    dense accumulator's nonzero() drops them), rows normalized by their
+    float64 sums clamped at 1e-30 (rules/evaluate.py:366-378), ranks combined
+    by sum or max (rules/shared_inference.py:209-225).  Returns (keys, values)."""
+    sources = np.asarray(sources, np.int64)
+    weights = np.asarray(weights, np.float32)
+    B, ranks = sources.size, weights.shape[1]
+    reach_keys, reach_rule = [], []
+    for k, body in enumerate(bodies):
+        keys = np.arange(B, dtype=np.int64) * E + sources
+        for op in body:
+            if keys.size == 0:
+                break
+            b, e = keys // E, keys % E
+            ops_ = np.full((B, 1), int(op), np.int64)
+            out, vals = fixed_relation(b, np.zeros_like(b), e, np.ones(b.size, np.float32), ops_, csr, r_size, E)
+            keys = out[vals > 0]
+        reach_keys.append(keys)
+        reach_rule.append(np.full(keys.size, k, np.int64))
+    keys = np.concatenate(reach_keys) if reach_keys else np.zeros(0, np.int64)
+    rule = np.concatenate(reach_rule) if reach_rule else np.zeros(0, np.int64)
+    parts_k, parts_v = [], []
+    for r in range(ranks):
+        w = weights[rule, r]
+        m = w > 0
+        uk, inv = np.unique(keys[m], return_inverse=True)
+        mx = np.zeros(uk.size, np.float32)
+        np.maximum.at(mx, inv, w[m])
+        tot = np.zeros(B, np.float64)
+        np.add.at(tot, uk // E, mx.astype(np.float64))
+        norm = (mx / np.maximum(tot.astype(np.float32), np.float32(1e-30))[uk // E]).astype(np.float32)
+        parts_k.append(uk)
+        parts_v.append(norm)
+    allk = np.concatenate(parts_k)
+    allv = np.concatenate(parts_v)
+    uk, inv = np.unique(allk, return_inverse=True)
+    out = np.zeros(uk.size, np.float32)
+    if final_max:
+        np.maximum.at(out, inv, allv)
+    else:
+        for pk, pv in zip(parts_k, parts_v):  # rank order, as the dense accumulation
+            out[np.searchsorted(uk, pk)] += pv
+    nz = out != 0
+    return uk[nz], out[nz]
+
+
 def coalesce_sum(keys, vals):
     keys, vals = _c(keys, np.int64), _c(vals, np.float32)
     ok = np.empty(max(keys.size, 1), np.int64)

@@ -217,6 +217,35 @@ def test_max_product_matches_reference(golden, ci):
     np.testing.assert_allclose(vals, g[f"r{ci}_val"], rtol=1e-5, atol=1e-9)
 
 
+@pytest.mark.parametrize("ci", [0, 1, 2])
+def test_sparse_max_product_oracle_matches_reference(golden, ci):
+    """The oracle's sparse max-product (no dense accumulator, for 86M
+    entities) gives the reference's score() entries and values too."""
+    g = golden("maxproduct_config1.npz")
+    cfg, train, csr = config1_graph()
+    bodies, weights = _rule_bank(g, ci)
+    keys, vals = O.max_product_sparse(g[f"r{ci}_sources"], bodies, weights, csr, cfg.relations, cfg.entities,
+                                      final_max=bool(g[f"r{ci}_final_max"]))
+    assert np.array_equal(keys, g[f"r{ci}_key"])
+    np.testing.assert_allclose(vals, g[f"r{ci}_val"], rtol=1e-5, atol=1e-9)
+
+
+def test_rule_bank_generator_shape():
+    """The seeded rule bank: heads among the query relations, bodies of 1-3
+    directed operators, weights in [0, 1), three groups; deterministic."""
+    from flashlog_b200.synthetic import CONFIGS, evaluation_queries, load_or_generate, rule_bank
+    cfg = CONFIGS[1]
+    train, valid, test = load_or_generate(cfg)
+    src, rel, dst = evaluation_queries(test, cfg.relations, 200)
+    assert src.size == rel.size == dst.size == 400
+    rb = rule_bank(train, rel, cfg.relations, 3000)
+    assert rb == rule_bank(train, rel, cfg.relations, 3000)
+    assert set(r["head"] for r in rb) <= set(rel.tolist())
+    assert {len(r["body"]) for r in rb} == {1, 2, 3}
+    assert all(0 <= o < 2 * cfg.relations for r in rb for o in r["body"])
+    assert all(0.0 <= r["weight"] < 1.0 for r in rb) and {r["group_id"] for r in rb} == {0, 1, 2}
+
+
 def test_filter_indices_oracle_matches_reference_golden(golden):
     """The oracle's known-answer lookup against the reference's own
     build_filter_indices_csr (training-CSR path): the same (query, entity)
