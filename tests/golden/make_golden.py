@@ -75,7 +75,7 @@ def main():
     from oracle.build import reference_root
     ap.add_argument("--reference", default=reference_root(),
                     help="reference checkout (default: $FLASHLOG_REFERENCE, else BASELINE.json reference_path)")
-    ap.add_argument("--only", choices=["filter", "readout"], help="write only this fixture")
+    ap.add_argument("--only", choices=["filter", "readout", "model"], help="write only this fixture")
     args = ap.parse_args()
     import torch
     torch.set_num_threads(1)
@@ -91,6 +91,9 @@ def main():
         return
     if args.only == "readout":
         readout_fixture()
+        return
+    if args.only == "model":
+        model_fixture()
         return
     out = {}
 
@@ -400,6 +403,52 @@ def readout_fixture():
                         f"c{ci}_{name}_g": g.numpy(), f"c{ci}_{name}_grad": v.grad.numpy()})
         out.update({f"c{ci}_row": row, f"c{ci}_ent": ent, f"c{ci}_val": val, f"c{ci}_shape": np.array([B, L, E])})
     np.savez_compressed(os.path.join(HERE, "readout.npz"), n=np.array(3), **out)
+
+
+def model_fixture():
+    """The reference's sparse DRUM model file (src/model_DRUM_kernel_sp.py,
+    unmodified) on its CPU path with the reference's own operators: one
+    forward (is_training=False, use_topk with c1 = 40, c2 = 16) and the
+    log loss on a config-1 batch, then backward.  Records the attention
+    logits the model's linear layer produced for each channel (hooked), the
+    final [B, E] scores, the loss and the gradient of every logits tensor, so
+    a test can drive the hops of the same forward through the drop-in."""
+    import torch
+    import model_DRUM_kernel_sp as M
+    from flashlog_b200.synthetic import CONFIGS, load_or_generate, training_queries
+    cfg = CONFIGS[1]
+    train, _, _ = load_or_generate(cfg)
+    E, R = cfg.entities, cfg.relations
+    n = 2 * R + 1
+    torch.manual_seed(1234)
+    model = M.Model(n, 3, 3, E, train.shape[0], 32, use_gpu=False, dropout=0.0, c1=40, use_topk=True, c2=16)
+    csr = M.build_csr_structure(torch.from_numpy(train[:, 0]), torch.from_numpy(train[:, 2]),
+                                torch.from_numpy(train[:, 1]), E)
+    ids, h, r, t = training_queries(train, cfg, step=5)
+    h, r, t, ids = h[:24], r[:24], t[:24], ids[:12]
+    mask = torch.ones(train.shape[0], dtype=torch.bool)
+    mask[torch.from_numpy(ids)] = False
+    logits = []
+
+    def keep(_m, _i, o):
+        o.retain_grad()
+        logits.append(o)
+    handle = model.linear.register_forward_hook(keep)
+    final = model(torch.from_numpy(h), torch.from_numpy(r), None, None, None, is_training=False,
+                  csr_struct=tuple(csr), mask_values=mask)
+    loss = model.log_loss(final, torch.from_numpy(t))
+    loss.backward()
+    handle.remove()
+    final = final.coalesce()
+    fi = final.indices().numpy()
+    out = {"heads": h, "rels": r, "tails": t, "hidden": ids, "loss": np.array(float(loss)),
+           "final_key": fi[0] * E + fi[1], "final_val": final.values().detach().numpy(),
+           "tau_1": np.array(float(model.tau_1)), "tau_2": np.array(float(model.tau_2)),
+           "c1": np.array(40), "c2": np.array(16)}
+    for l, o in enumerate(logits):
+        out[f"logits{l}"] = o.detach().numpy()
+        out[f"grad{l}"] = o.grad.numpy()
+    np.savez_compressed(os.path.join(HERE, "model_drum_sp.npz"), **out)
 
 
 if __name__ == "__main__":
