@@ -61,6 +61,35 @@ __global__ void __launch_bounds__(kScanThreads) scan_apply(const In *in, int64_t
     }
     if (blockIdx.x == gridDim.x - 1 && threadIdx.x == kScanThreads - 1) out[n] = ex;
 }
+// Arrays of at most kSmallTiles tiles: one block walks the tiles in order,
+// carrying the running total (one launch instead of three).
+constexpr int64_t kSmallTiles = 4;
+
+template <typename In>
+__global__ void __launch_bounds__(kScanThreads) scan_small(const In *in, int64_t n, int64_t *out) {
+    __shared__ int64_t scratch[kScanThreads / 32 + 1];
+    int64_t carry = 0;
+    for (int64_t base = 0; base < n; base += kScanTile) {
+        int64_t v[kScanItems];
+        int64_t s = 0;
+#pragma unroll
+        for (int k = 0; k < kScanItems; ++k) {
+            const int64_t i = base + static_cast<int64_t>(threadIdx.x) * kScanItems + k;
+            v[k] = i < n ? static_cast<int64_t>(in[i]) : 0;
+            s += v[k];
+        }
+        int64_t tot;
+        int64_t ex = block_exclusive_scan(s, scratch, &tot) + carry;
+#pragma unroll
+        for (int k = 0; k < kScanItems; ++k) {
+            const int64_t i = base + static_cast<int64_t>(threadIdx.x) * kScanItems + k;
+            if (i < n) out[i] = ex;
+            ex += v[k];
+        }
+        carry += tot;
+    }
+    if (threadIdx.x == 0) out[n] = carry;
+}
 }  // namespace
 
 size_t scan_workspace(int64_t n) {
@@ -75,6 +104,10 @@ int exclusive_scan(const In *in, int64_t n, int64_t *out, void *ws, size_t ws_by
         return FL_OK;
     }
     int64_t tiles = (n + kScanTile - 1) / kScanTile;
+    if (tiles <= kSmallTiles) {
+        launch(scan_small<In>, 1, kScanThreads, 0, st, in, n, out);
+        return check_launch("exclusive_scan");
+    }
     Carve c(ws, ws_bytes);
     int64_t *tile = c.take<int64_t>(static_cast<size_t>(tiles + 1));
     FL_REQUIRE(tile != nullptr, "scan workspace too small");
