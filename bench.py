@@ -360,8 +360,7 @@ def run_graph_arm(args, cfg, train, csr, rank, world, device):
     pool = None
     launches_per_step = 0
     for k in range(args.steps):
-        timer = [(torch.cuda.Event(enable_timing=True, external=True),
-                  torch.cuda.Event(enable_timing=True, external=True)) for _ in range(T)]
+        timer = [tuple(torch.cuda.Event(enable_timing=True, external=True) for _ in range(3)) for _ in range(T)]
         step.timer = timer
         l0 = _lib.lib().fl_launch_count()
         chunks = [step.run] if world == 1 else step.parts()[:T]  # the last part is empty without the update
@@ -400,9 +399,12 @@ def run_graph_arm(args, cfg, train, csr, rank, world, device):
     clk = clocks.stop()
     step.check()  # no hop ran out of its buffers
     S, G, F, U = (int(x) for x in step.stats.tolist())
-    hop_ms = sum(a.elapsed_time(b) for timer in timers for a, b in timer)
+    hop_ms = sum(a.elapsed_time(c) for timer in timers for a, b, c in timer)
+    expand_ms = sum(a.elapsed_time(b) for timer in timers for a, b, c in timer)
+    reduce_ms = sum(b.elapsed_time(c) for timer in timers for a, b, c in timer)
     del graphs
-    return dict(ms=ms, facts=F, S=S, G=G, U=U, hop_ms=hop_ms, n_hops=args.steps * T,
+    return dict(ms=ms, facts=F, S=S, G=G, U=U, hop_ms=hop_ms, expand_ms=expand_ms, reduce_ms=reduce_ms,
+                n_hops=args.steps * T,
                 launches=launches_per_step * args.steps, clocks=clk, data=data, table=table,
                 memory_gb=step.memory_bytes() / 1e9)
 
@@ -684,6 +686,19 @@ def main():
             pass
     S, G, U = res["S"], res["G"], res["U"]
     alg_bytes = 24 * S + 14 * G + 5 * res["facts"] + 8 * U
+    # per kernel, the kernel's own compulsory I/O over the timed hops
+    # (expansion: its inputs 24 S + 14 G + 5 F and the facts it writes, 10 F
+    # with S identity facts; reduction + compaction: the facts it reads 8 F,
+    # fact positions 4 F, per-row outputs 8 U written and re-read, 12 U
+    # packed), each over its own CUDA-event time
+    per_kernel = None
+    if res.get("expand_ms") is not None and res["expand_ms"] > 0 and res["reduce_ms"] > 0:
+        Fi = res["facts"] + S
+        kb = {"hop_expand": 24 * S + 14 * G + 5 * res["facts"] + 10 * Fi, "row_reduce+compact": 12 * Fi + 28 * U}
+        kt = {"hop_expand": res["expand_ms"], "row_reduce+compact": res["reduce_ms"]}
+        per_kernel = {k: {"bytes": kb[k], "ms": kt[k], "achieved_gbs": kb[k] / (kt[k] / 1000.0) / 1e9,
+                          "frac": kb[k] / (kt[k] / 1000.0) / 1e9 / peak}
+                      for k in kb}
     achieved = alg_bytes / (hop_ms / 1000.0) / 1e9 if hop_ms > 0 else 0.0
     # DRAM bytes per hop forward: ncu's count on a small case of the same
     # configuration (profiles/hop_forward_traffic.json), scaled to this run's
@@ -719,7 +734,8 @@ def main():
                              "algorithmic_bytes": "24*S + 14*G + 5*F + 8*U per hop",
                              "algorithmic_bytes_per_hop": alg_bytes / max(res["n_hops"], 1),
                              "units": {"S": S, "G": G, "F": res["facts"], "U": U, "hops": res["n_hops"],
-                                       "hop_forward_ms": hop_ms}},
+                                       "hop_forward_ms": hop_ms},
+                             "per_kernel": per_kernel},
                 "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": res["launches"], "clocks": res["clocks"]}
         print(json.dumps(line))
     if world > 1:

@@ -186,7 +186,7 @@ class DrumTrainStep:
         ws = max(ws, lib().fl_hop_backward_workspace(rows, self.n))
         self.ws = _buf(ws, u8, dev)
         self.stats = torch.zeros(4, dtype=i64, device=dev) if stats else None
-        self.timer = None  # optional: per-hop (start, end) external events around expand + reduce
+        self.timer = None  # optional: per hop (start, after expand, after reduce) external events
 
     # ------------------------------------------------------------------
     def memory_bytes(self) -> int:
@@ -286,13 +286,15 @@ class DrumTrainStep:
                                    g.ori, g.inv, None, None, None, None, _p(self.slot_base[t]), _p(self.fact_dst),
                                    _p(self.fact_val), _p(self.fact_rel[t]), None, _p(self.entry_count[t]), st),
                   "hop_expand")
+            if self.timer is not None and len(self.timer[t]) > 2:
+                self.timer[t][1].record()
             check(lb.fl_row_reduce(_p(rp_s), rows, g.E, _p(self.slot_base[t]), _p(self.entry_count[t]),
                                    _p(self.fact_dst), _p(self.fact_val), self.F[t], _p(self.fact_pos[t]),
                                    ctypes.c_float(self.eps), _p(self.out_rp[t]), _p(self.out_ent[t]),
                                    _p(self.out_x[t]), _p(self.out_y[t]), _p(self.out_denom[t]), _p(self.status),
                                    _p(self.row_order[t]), ws, wsn, self._drop(t), st), "row_reduce")
             if self.timer is not None:
-                self.timer[t][1].record()
+                self.timer[t][-1].record()
             if self.stats is not None:
                 check(lb.fl_hop_stats(_p(rp_s), rows, _p(ent_s), self.S[t], g.ori, g.inv, _p(self.entry_count[t]),
                                       _p(self.out_rp[t]), 0, _p(self.stats), st), "hop_stats")
