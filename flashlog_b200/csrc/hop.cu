@@ -2008,6 +2008,7 @@ __global__ void compact_kernel(const int64_t *row_ptr, const int64_t *slot_base,
 // ---------------------------------------------------------------------------
 constexpr int kBThreads = 256;
 constexpr int kSmemRel = 4096;  // relations whose exact grad_w accumulators fit in shared memory
+constexpr int64_t kBTeamMax = 32;  // entries with at most this many facts: an 8-lane team each
 
 struct BackwardArgs {
     const int64_t *row_ptr;
@@ -2031,7 +2032,7 @@ struct BackwardArgs {
     const int32_t *row_order;  // block -> row (a permutation), or null
 };
 
-__global__ void __launch_bounds__(kBThreads, 6) hop_backward_kernel(BackwardArgs a) {
+__global__ void __launch_bounds__(kBThreads, 5) hop_backward_kernel(BackwardArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     unsigned long long *sacc = reinterpret_cast<unsigned long long *>(smem_raw);
     __shared__ float fscratch[kBThreads / 32 + 1];
@@ -2079,9 +2080,57 @@ __global__ void __launch_bounds__(kBThreads, 6) hop_backward_kernel(BackwardArgs
     const int scale = fixed_scale_for(bound, F + 1);
     __syncthreads();
     const float *wrow = a.w + r * a.n;
+    // Entries of at most kBTeamMax facts: one 8-lane team each, four per
+    // warp; each lane keeps two facts in flight.
+    {
+        const int team = lane / kTeam, tl = lane % kTeam;
+        const unsigned tm = 0xffu << (team * kTeam);
+        for (int64_t e0 = ea + (warp * 4); e0 < eb; e0 += kBThreads / 8) {
+            const int64_t e = e0 + team;
+            int64_t cnt = e < eb ? a.entry_count[e] : 0;
+            const bool mine = e < eb && cnt <= kBTeamMax;
+            if (mine) {
+                const float v = a.val[e];
+                const int64_t s0 = a.slot_base[e];
+                float gv = 0.0f;
+                for (int64_t f0 = 0; f0 < cnt; f0 += 2 * kTeam) {
+                    int32_t fp[2];
+                    int c[2];
+                    float m[2];
+#pragma unroll
+                    for (int k = 0; k < 2; ++k) {
+                        const int64_t f = f0 + k * kTeam + tl;
+                        fp[k] = -1;
+                        c[k] = 0;
+                        m[k] = 1.0f;
+                        if (f < cnt) {
+                            fp[k] = a.fact_pos[s0 + f];
+                            c[k] = a.fact_rel[s0 + f];
+                            if (a.fact_m) m[k] = a.fact_m[s0 + f];
+                        }
+                    }
+                    float gy[2];
+#pragma unroll
+                    for (int k = 0; k < 2; ++k) gy[k] = fp[k] >= 0 ? a.g_y[oa + fp[k]] : 0.0f;
+#pragma unroll
+                    for (int k = 0; k < 2; ++k) {
+                        if (fp[k] < 0) continue;
+                        const float g = a.normalize ? (gy[k] / dd - corr) : gy[k];
+                        gv += g * wrow[c[k]] * m[k];
+                        fixed_atomic_add(acc + 2 * c[k], to_fixed(g * v * m[k], scale));
+                    }
+                }
+#pragma unroll
+                for (int o = 1; o < kTeam; o <<= 1) gv += __shfl_xor_sync(tm, gv, o, kTeam);
+                if (tl == 0) a.grad_val[e] = gv;
+            }
+        }
+    }
     for (int64_t e = ea + warp; e < eb; e += kBThreads / 32) {
+        const int64_t cnt = a.entry_count[e];
+        if (cnt <= kBTeamMax) continue;  // taken by a team above
         const float v = a.val[e];
-        const int64_t s0 = a.slot_base[e], cnt = a.entry_count[e];
+        const int64_t s0 = a.slot_base[e];
         float gv = 0.0f;
         for (int64_t f0 = 0; f0 < cnt; f0 += 128) {  // four facts per lane: the loads go out together
             int32_t fp[4];
