@@ -2631,9 +2631,13 @@ int row_reduce_max(const int64_t *row_ptr, int64_t rows, int64_t E, int64_t r_si
                    int64_t total_slots, int32_t *fact_pos, int64_t *out_row_ptr, int32_t *out_ent, float *out_x,
                    int max_mode, bool value_only, int32_t *status, void *ws, size_t ws_bytes, cudaStream_t st) {
     FL_REQUIRE(max_mode == 1 || max_mode == 2, "bad MAX mode");
-    if (value_only) fact_rel = nullptr, fact_edge = nullptr;
-    FL_REQUIRE(fact_rel != nullptr && fact_edge != nullptr,
-               "the MAX reduction needs fact relations and triple ids (or FL_MAX_VALUE_ONLY)");
+    if (value_only) {
+        fact_rel = nullptr;
+        fact_edge = nullptr;
+    } else {
+        FL_REQUIRE(fact_rel != nullptr && fact_edge != nullptr,
+                   "the MAX reduction needs fact relations and triple ids (or FL_MAX_VALUE_ONLY)");
+    }
     return reduce_rows(row_ptr, rows, E, slot_base, fact_dst, fact_val, total_slots, fact_pos, 1e-7f, out_row_ptr,
                        out_ent, out_x, nullptr, nullptr, status, max_mode, r_size, fact_rel, fact_edge, nullptr, ws,
                        ws_bytes, nullptr, st);

@@ -175,7 +175,7 @@ class DrumTrainStep:
         self.grad_w = _buf((T if self.record_grad_w else 1) * rows * self.n, f32, dev)
         self.work = _buf(2, i32, dev)  # the expansion's two work queues
         self.status = torch.zeros(1, dtype=i32, device=dev)
-        self.ok = torch.ones((), dtype=f32, device=dev)  # 1 while the status word is clear
+        self.ok = torch.ones(1, dtype=f32, device=dev)  # 1 while the status word is clear
         self.scores = _buf(Q, f32, dev)
         self.loss = torch.zeros((), dtype=f32, device=dev)
         self.grad_logits = torch.empty((Q, T, N, self.n), dtype=f32, device=dev)

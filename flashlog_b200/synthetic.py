@@ -300,9 +300,18 @@ def rule_bank(train: np.ndarray, query_relations: np.ndarray, relations: int, n_
     ops_ = rng.choice(2 * R, size=(n_rules, 3), p=op_p)
     weights = rng.random(n_rules)
     group = rng.integers(0, groups, size=n_rules)
-    return [{"rule_id": k, "head": int(heads[k]), "body": tuple(int(o) for o in ops_[k, :lengths[k]]),
-             "weight": float(weights[k]), "rank_weights": None, "group_id": int(group[k])}
-            for k in range(n_rules)]
+    # a (head, body, group) instance appears once (rules/evaluate.py:110-111
+    # rejects duplicates); later draws of the same instance are dropped
+    seen, out = set(), []
+    for k in range(n_rules):
+        body = tuple(int(o) for o in ops_[k, :lengths[k]])
+        key = (int(heads[k]), body, int(group[k]))
+        if key in seen:
+            continue
+        seen.add(key)
+        out.append({"rule_id": len(out), "head": key[0], "body": body, "weight": float(weights[k]),
+                    "rank_weights": None, "group_id": key[2]})
+    return out
 
 
 def write_rules_tsv(path: str, rules) -> None:

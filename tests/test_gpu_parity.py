@@ -565,9 +565,18 @@ def test_filtered_ranks_skip_queries_out_of_range(fk, golden):
     ie = np.concatenate([keys % E, [0, 1]])
     v = np.concatenate([vals, np.float32([0.5, 0.25])]).astype(np.float32)
     filt2 = np.concatenate([filt, [B * E + 3, (B + 7) * E]])
-    got = fk.sparse2d_filtered_ranks_cuda(_cuda(ib), _cuda(ie), _cuda(v), _cuda(targets), _cuda(filt2), B, E,
-                                          True).cpu().numpy()
-    assert np.array_equal(got, want)
+    # through the C ABI: the Python operator rejects such indices before the launch
+    import ctypes
+    from flashlog_b200 import _lib
+    lb = _lib.lib()
+    t = [_cuda(x) for x in (ib, ie, v, targets, filt2)]
+    ranks = torch.empty(B, dtype=torch.float32, device="cuda")
+    ws = torch.empty(lb.fl_filtered_ranks_workspace(B), dtype=torch.uint8, device="cuda")
+    rc = lb.fl_filtered_ranks(t[0].data_ptr(), t[1].data_ptr(), t[2].data_ptr(), v.size, t[3].data_ptr(),
+                              t[4].data_ptr(), filt2.size, B, E, 1, ranks.data_ptr(), ws.data_ptr(), ws.numel(),
+                              ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0
+    assert np.array_equal(ranks.cpu().numpy(), want)
 
 
 def test_hop_is_deterministic(fk, g1):
