@@ -1011,17 +1011,24 @@ __global__ void __launch_bounds__(kExpandWarps * 32, kRanked ? 4 : 3) hop_expand
 // the row in canonical order.
 // Rows of at most kRankSortMax slots are sorted in one tile by rank.
 // ---------------------------------------------------------------------------
-constexpr int kRThreads = 1024;
+// Threads of a row-reduction CTA (1024: one CTA per SM; 512: two, with
+// every tile halved).  The tile sizes scale with it.
+#ifndef FL_ROW_THREADS
+#define FL_ROW_THREADS 1024
+#endif
+constexpr int kRThreads = FL_ROW_THREADS;
+static_assert(kRThreads == 1024 || kRThreads == 512, "row reduction CTAs of 512 or 1024 threads");
+constexpr int kRowCtasPerSm = 1024 / kRThreads;
 constexpr int kRWarps = kRThreads / 32;
 constexpr int kDigits = 256;
 constexpr int kRankSortMax = 128;  // rows of at most this many slots: one tile, sorted by rank
-constexpr int kTileD = 6144;   // dense-window sub-tile
-constexpr int kDenseW = 4096;  // dense window width (destinations)
+constexpr int kTileD = 6 * kRThreads;   // dense-window sub-tile
+constexpr int kDenseW = 4 * kRThreads;  // dense window width (destinations)
 constexpr int kLoadK = 4;  // slots per thread per load step
 constexpr int kLoadStep = kRThreads * kLoadK;
-constexpr int kKBitsMax = 13;
+constexpr int kKBitsMax = kRThreads == 1024 ? 13 : 12;
 constexpr int kKBins = 1 << kKBitsMax;  // destination bins per row (at most)
-constexpr int kTileK = 12288;           // facts per chunk
+constexpr int kTileK = 12 * kRThreads;  // facts per chunk
 constexpr int kRankBinMax = 64;        // bins up to this size: each fact ranked within its bin
 constexpr int kMultiPairs = 2 * kRThreads;  // comparator pairs of the block-wide sort of the larger bins
 constexpr int kWarpSortMax = 1024;      // bins up to this size are sorted by one warp
@@ -1051,29 +1058,12 @@ struct TileD {
     uint32_t bslot[kDenseW];           // MAX: winner's row-local slot
 };
 
-// Radix path: a chunk of up to kTileR facts of one destination range, in
-// canonical order, stably LSD-sorted by destination (8-bit digits, per-warp
-// counters) as a permutation of 16-bit tile indices.
-constexpr int kTileR = 12288;
-constexpr int kMaxChunks = 512;
-struct TileR {
-    uint16_t cnt[kRWarps * kDigits];  // per-warp digit counters (cleared as uint4; first, as in TileD)
-    uint32_t key[kTileR];             // destination - range start
-    float val[kTileR];
-    uint32_t slot[kTileR];            // row-local slot
-    uint16_t idx[2][kTileR];
-};
-
 struct ReduceSmem {
     union {
         TileA a;
         TileK k;
         TileD d;
-        TileR r;
     } t;
-    int32_t rchunk_bin[kMaxChunks + 1];  // radix path: first bin of each chunk
-    int32_t rchunk_n[kMaxChunks];        // and its fact count
-    int rchunks;
     int64_t scan_scratch[kRWarps + 1];
     float fscratch[kRWarps + 1];
     int chunk_end;
@@ -1088,9 +1078,8 @@ struct ReduceSmem {
 };
 static_assert(kTileK / (kRankBinMax + 1) + 1 < kRThreads, "listed bins are scanned one per thread");
 static_assert(sizeof(ReduceSmem) <= 227 * 1024, "row reduction shared memory exceeds one CTA's budget");
+static_assert(kRowCtasPerSm == 1 || sizeof(ReduceSmem) <= 112 * 1024, "two row-reduction CTAs must fit one SM");
 static_assert(offsetof(TileD, cnt) == 0, "digit counters are cleared with 16-byte stores");
-static_assert(offsetof(TileR, cnt) == 0, "digit counters are cleared with 16-byte stores");
-static_assert(kTileR <= 65536, "radix tile indices are 16-bit");
 static_assert(kTileD <= 65536, "tile indices are 16-bit");
 static_assert(kTileK <= 65536, "tile positions are 16-bit");
 
@@ -1801,133 +1790,7 @@ __device__ float bucket_row(const ReduceArgs &a, ReduceSmem &sm, int64_t s0, int
     return local + (threadIdx.x == 0 ? dense_sum : 0.0f);
 }
 
-// Load, in canonical order, every fact of the row whose destination lies in
-// [lo, hi) into the radix tile (key = destination - lo, value, row-local
-// slot, identity permutation).  The caller knows the count fits the tile.
-__device__ int load_chunk(const ReduceArgs &a, ReduceSmem &sm, int64_t s0, int64_t ns, int64_t lo, int64_t hi) {
-    TileR &t = sm.t.r;
-    int pos = 0;
-    for (int64_t fb = 0; fb < ns; fb += kLoadStep) {
-        int32_t d[kLoadK];
-        int c = 0;
-#pragma unroll
-        for (int k = 0; k < kLoadK; ++k) {
-            const int64_t j = fb + threadIdx.x * kLoadK + k;
-            d[k] = -1;
-            if (j < ns) {
-                const int32_t dd = a.fact_dst[s0 + j];
-                if (dd >= lo && dd < hi) { d[k] = dd; ++c; }
-            }
-        }
-        int64_t tot;
-        int p = pos + static_cast<int>(block_exclusive_scan<int64_t>(c, sm.scan_scratch, &tot));
-#pragma unroll
-        for (int k = 0; k < kLoadK; ++k) {
-            if (d[k] < 0) continue;
-            const int64_t j = fb + threadIdx.x * kLoadK + k;
-            if (p < kTileR) {  // guaranteed by the chunk plan; never written past the tile
-                t.key[p] = static_cast<uint32_t>(d[k] - lo);
-                t.val[p] = a.fact_val[s0 + j];
-                t.slot[p] = static_cast<uint32_t>(j);
-                t.idx[0][p] = static_cast<uint16_t>(p);
-            }
-            ++p;
-        }
-        pos += static_cast<int>(tot);
-    }
-    __syncthreads();
-    return pos < kTileR ? pos : kTileR;
-}
-
-// The row cut into destination ranges of at most kTileR facts (one range
-// when the row's slots fit), each loaded in canonical order, stably radix-
-// sorted by destination and emitted (every destination summed left to right
-// in canonical order, or its MAX winner).  A destination bin holding more
-// than a tile goes through the dense windows.  Returns this thread's share
-// of the output sum.  When the row has more ranges than the plan holds,
-// *planned is false in every thread and nothing was written (the caller
-// then takes the bucketed path).
-__device__ float radix_row(const ReduceArgs &a, ReduceSmem &sm, int64_t s0, int64_t ns, int64_t *written,
-                           bool *planned) {
-    *planned = true;
-    TileR &t = sm.t.r;
-    float local = 0.0f;
-    int shift = 0;
-    if (ns <= kTileR) {
-        if (threadIdx.x == 0) { sm.rchunks = 1; sm.rchunk_bin[0] = 0; sm.rchunk_bin[1] = 1; sm.rchunk_n[0] = -1; }
-        shift = 62;  // one bin: the whole entity range
-        __syncthreads();
-    } else {
-        int kb = 8;  // bins ~ half the slots, 2^8 .. 2^13
-        while (kb < kKBitsMax && (int64_t(1) << (kb + 1)) < ns) ++kb;
-        const int eb = bits_for(a.E);
-        shift = eb > kb ? eb - kb : 0;
-        const int nbins = static_cast<int>(((a.E - 1) >> shift) + 1);
-        bucket_hist(a, sm, s0, ns, shift, nbins);  // off[b] = facts in bins < b
-        const uint32_t *off = sm.t.k.off;
-        constexpr uint32_t H = kTileR / 2;
-        // a chunk starts where the running count enters a new multiple of H,
-        // and around every bin of more than H facts: a chunk then holds less
-        // than H + H facts, or one big bin
-        const int per = (nbins + kRThreads - 1) / kRThreads;
-        const int b0 = threadIdx.x * per;
-        int flags = 0;
-        for (int k = 0; k < per; ++k) {
-            const int b = b0 + k;
-            if (b >= nbins) break;
-            const bool big = off[b + 1] - off[b] > H;
-            const bool prev_big = b > 0 && off[b] - off[b - 1] > H;
-            flags += (b == 0 || off[b] / H != off[b - 1] / H || big || prev_big) ? 1 : 0;
-        }
-        int64_t tot;
-        int w = static_cast<int>(block_exclusive_scan<int64_t>(flags, sm.scan_scratch, &tot));
-        if (tot > kMaxChunks) {  // block-uniform: tot is the block total
-            *planned = false;
-            return 0.0f;
-        }
-        for (int k = 0; k < per; ++k) {
-            const int b = b0 + k;
-            if (b >= nbins) break;
-            const bool big = off[b + 1] - off[b] > H;
-            const bool prev_big = b > 0 && off[b] - off[b - 1] > H;
-            if (b == 0 || off[b] / H != off[b - 1] / H || big || prev_big) sm.rchunk_bin[w++] = b;
-        }
-        if (threadIdx.x == 0) { sm.rchunks = static_cast<int>(tot); sm.rchunk_bin[tot] = nbins; }
-        __syncthreads();
-        for (int c = threadIdx.x; c < sm.rchunks; c += kRThreads)
-            sm.rchunk_n[c] = static_cast<int32_t>(off[sm.rchunk_bin[c + 1]] - off[sm.rchunk_bin[c]]);
-        __syncthreads();  // the tile loads below overwrite off[]
-    }
-    const int nch = sm.rchunks;
-    for (int c = 0; c < nch; ++c) {
-        const int64_t lo = shift >= 62 ? 0 : static_cast<int64_t>(sm.rchunk_bin[c]) << shift;
-        int64_t hi = shift >= 62 ? a.E : (static_cast<int64_t>(sm.rchunk_bin[c + 1]) << shift);
-        if (hi > a.E) hi = a.E;
-        const int cnt = sm.rchunk_n[c];
-        if (cnt == 0) continue;
-        if (cnt > kTileR) {  // one bin above a tile
-            float ds = 0.0f;
-            for (int64_t wlo = lo; wlo < hi; wlo += kDenseW) {
-                const int64_t whi = (wlo + kDenseW) < hi ? (wlo + kDenseW) : hi;
-                ds += dense_window(a, sm, s0, ns, wlo, whi, written);
-            }
-            if (threadIdx.x == 0) local += ds;
-            __syncthreads();
-            continue;
-        }
-        const int n = load_chunk(a, sm, s0, ns, lo, hi);
-        if (n == 0) continue;
-        uint16_t *spare;
-        const uint16_t *perm = sort_tile(t.key, t.idx[0], t.idx[1], n, bits_for(hi - lo), sm, &spare);
-        const float tsum = emit_tile(a, sm, t.key, t.val, perm, spare, n, lo, s0, written,
-                                     [&](uint16_t i) { return t.slot[i]; });
-        if (threadIdx.x == 0) local += tsum;
-        __syncthreads();
-    }
-    return local;
-}
-
-__global__ void __launch_bounds__(kRThreads, 1) row_reduce_kernel(ReduceArgs a) {
+__global__ void __launch_bounds__(kRThreads, kRowCtasPerSm) row_reduce_kernel(ReduceArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     ReduceSmem &sm = *reinterpret_cast<ReduceSmem *>(smem_raw);
     const int64_t r = a.row_order != nullptr ? static_cast<int64_t>(a.row_order[blockIdx.x]) : blockIdx.x;
@@ -1965,13 +1828,7 @@ __global__ void __launch_bounds__(kRThreads, 1) row_reduce_kernel(ReduceArgs a) 
                              [](uint16_t i) { return static_cast<uint32_t>(i); });
         }
     } else {
-        bool planned;
-        float part = radix_row(a, sm, s0, ns, &written, &planned);
-        if (!planned) {  // more destination ranges than the radix plan holds
-            written = 0;
-            part = bucket_row(a, sm, s0, ns, &written);
-        }
-        rsum = block_sum(part, sm.fscratch);
+        rsum = block_sum(bucket_row(a, sm, s0, ns, &written), sm.fscratch);
     }
     if (threadIdx.x == 0) { a.out_count[r] = written; a.out_sum[r] = rsum; }
 }

@@ -13,9 +13,13 @@ the same fp32 attention weights:
 * the normalized values: rel 1e-5 (they are in fact bit-identical: both sum
   every destination left to right in canonical order);
 * d loss / d w of every hop and d loss / d y of every hop's output:
-  rel 1e-5, with an absolute floor of 1e-6 x the largest magnitude of the
-  hop's reference gradient (the normalization backward subtracts terms, so
-  single entries can cancel to near zero);
+  rel 1e-5, with an absolute floor of 5e-5 x the largest magnitude of the
+  hop's reference gradient.  Both sides sum thousands of fp32 terms in
+  different orders: the reference CPU accumulates grad_w in fp32 (on config
+  2 one entry of 22,800 drifts 1.5e-5 from the exactly rounded sum this
+  library returns), and the normalization backward g / d - sum(g y) / d
+  cancels in small entries, so their rounding shows at about 1e-5 of the
+  tensor's scale after two backward hops;
 * the loss: rel 1e-6.
 """
 
@@ -26,6 +30,7 @@ torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
 RTOL = 1e-5
+GRAD_FLOOR = 5e-5  # absolute floor of the gradient comparisons, relative to the tensor's largest magnitude
 QUERIES = 16
 
 
@@ -59,9 +64,9 @@ def _graph(index):
     return _cached[index]
 
 
-def _close(got, want, what):
+def _close(got, want, what, floor=1e-6):
     scale = float(np.abs(want).max()) if want.size else 0.0
-    np.testing.assert_allclose(got, want, rtol=RTOL, atol=1e-6 * scale, err_msg=what)
+    np.testing.assert_allclose(got, want, rtol=RTOL, atol=floor * scale, err_msg=what)
 
 
 @pytest.mark.parametrize("index", [2, 3, 4, 5])
@@ -108,8 +113,8 @@ def test_train_step_slice_matches_reference_cpu(index):
         assert np.array_equal(step.out_ent[k][:u].cpu().numpy().astype(np.int64), hop["out_ent"]), \
             f"hop {k}: output entities"
         _close(step.out_y[k][:u].cpu().numpy(), hop["y"], f"hop {k}: values")
-        _close(step.g_y[k][:u].cpu().numpy(), hop["g_out"], f"hop {k}: d loss / d y")
-        _close(step.grad_w_of(k).cpu().numpy(), hop["gw"], f"hop {k}: d loss / d w")
+        _close(step.g_y[k][:u].cpu().numpy(), hop["g_out"], f"hop {k}: d loss / d y", GRAD_FLOOR)
+        _close(step.grad_w_of(k).cpu().numpy(), hop["gw"], f"hop {k}: d loss / d w", GRAD_FLOOR)
     # the slice is not trivial: the last hop expands hub frontiers under both budgets
     last = ref["hops"][-1]
     assert last["facts"] > 1000 and last["out_ent"].size > 1000
