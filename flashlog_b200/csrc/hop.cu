@@ -1480,16 +1480,23 @@ __device__ void bucket_hist(const ReduceArgs &a, ReduceSmem &sm, int64_t s0, int
     TileK &t = sm.t.k;
     for (int b = threadIdx.x; b <= nbins; b += kRThreads) t.off[b] = 0u;
     __syncthreads();
-    for (int64_t fb = 0; fb < ns; fb += kLoadStep) {
-        int32_t d[kLoadK];
+    int32_t d[kLoadK];
+    auto fetch = [&](int64_t fb) {
 #pragma unroll
         for (int k = 0; k < kLoadK; ++k) {
             const int64_t j = fb + k * kRThreads + threadIdx.x;
             d[k] = j < ns ? a.fact_dst[s0 + j] : -1;
         }
+    };
+    fetch(0);
+    for (int64_t fb = 0; fb < ns; fb += kLoadStep) {  // the next step's loads go out before this step's atomics
+        int32_t dc[kLoadK];
+#pragma unroll
+        for (int k = 0; k < kLoadK; ++k) dc[k] = d[k];
+        if (fb + kLoadStep < ns) fetch(fb + kLoadStep);
 #pragma unroll
         for (int k = 0; k < kLoadK; ++k)
-            if (d[k] >= 0 && static_cast<int64_t>(d[k]) < a.E) atomicAdd(&t.off[d[k] >> shift], 1u);
+            if (dc[k] >= 0 && static_cast<int64_t>(dc[k]) < a.E) atomicAdd(&t.off[dc[k] >> shift], 1u);
     }
     __syncthreads();
     const int per = (nbins + kRThreads - 1) / kRThreads;  // <= 8
@@ -1559,23 +1566,36 @@ __device__ float bucket_row(const ReduceArgs &a, ReduceSmem &sm, int64_t s0, int
         const int C = static_cast<int>(t.off[bh] - base);  // off[bh] is not advanced by this chunk
         const int64_t cbase = static_cast<int64_t>(bl) << shift;
         __syncthreads();  // every thread has read off[bl], off[bh] before the scatter advances them
-        // scatter the chunk's facts into their bins
-        for (int64_t fb = 0; fb < ns; fb += kLoadStep) {
+        // scatter the chunk's facts into their bins; each step's destinations
+        // and values are loaded together, one step ahead of their use
+        {
             int32_t d[kLoadK];
+            float fv[kLoadK];
+            auto fetch = [&](int64_t fb) {
 #pragma unroll
-            for (int k = 0; k < kLoadK; ++k) {
-                const int64_t j = fb + k * kRThreads + threadIdx.x;
-                d[k] = j < ns ? a.fact_dst[s0 + j] : -1;
-            }
+                for (int k = 0; k < kLoadK; ++k) {
+                    const int64_t j = fb + k * kRThreads + threadIdx.x;
+                    d[k] = j < ns ? a.fact_dst[s0 + j] : -1;
+                    fv[k] = j < ns ? a.fact_val[s0 + j] : 0.0f;
+                }
+            };
+            fetch(0);
+            for (int64_t fb = 0; fb < ns; fb += kLoadStep) {
+                int32_t dc[kLoadK];
+                float vc[kLoadK];
 #pragma unroll
-            for (int k = 0; k < kLoadK; ++k) {
-                if (d[k] < 0 || static_cast<int64_t>(d[k]) >= a.E) continue;
-                const int b = d[k] >> shift;
-                if (b < bl || b >= bh) continue;
-                const int64_t j = fb + k * kRThreads + threadIdx.x;
-                const uint32_t pos = atomicAdd(&t.off[b], 1u) - base;
-                t.key[pos] = (static_cast<unsigned long long>(d[k] - cbase) << 32) | static_cast<uint32_t>(j);
-                t.val[pos] = a.fact_val[s0 + j];
+                for (int k = 0; k < kLoadK; ++k) { dc[k] = d[k]; vc[k] = fv[k]; }
+                if (fb + kLoadStep < ns) fetch(fb + kLoadStep);
+#pragma unroll
+                for (int k = 0; k < kLoadK; ++k) {
+                    if (dc[k] < 0 || static_cast<int64_t>(dc[k]) >= a.E) continue;
+                    const int b = dc[k] >> shift;
+                    if (b < bl || b >= bh) continue;
+                    const int64_t j = fb + k * kRThreads + threadIdx.x;
+                    const uint32_t pos = atomicAdd(&t.off[b], 1u) - base;
+                    t.key[pos] = (static_cast<unsigned long long>(dc[k] - cbase) << 32) | static_cast<uint32_t>(j);
+                    t.val[pos] = vc[k];
+                }
             }
         }
         __syncthreads();
