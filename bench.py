@@ -331,16 +331,11 @@ def run_graph_arm(args, cfg, train, csr, rank, world, device):
     comm = torch.cuda.Stream() if world > 1 else None
 
     def run_parts(parts):
-        for j, part in enumerate(parts):
-            part()
-            if world > 1 and j < T:
-                hop = T - 1 - j
-                comm.wait_stream(torch.cuda.current_stream())
-                with torch.cuda.stream(comm):
-                    dist.all_reduce(step.grad_hop[hop])
         if world > 1:
-            torch.cuda.current_stream().wait_stream(comm)
-            table.sub_(step.grad, alpha=lr / world)
+            MG.run_parts_with_overlapped_allreduce(parts, step.grad_hop, step.grad, table, lr, comm)
+        else:
+            for part in parts:
+                part()
 
     clocks = ClockSampler(torch.cuda.current_device())
     clocks.start()  # before the warm-up: nvidia-smi's start-up must not fall in the timed region

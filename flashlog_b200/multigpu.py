@@ -43,6 +43,32 @@ def allreduce_mean_(grad: torch.Tensor, group=None) -> torch.Tensor:
     return grad
 
 
+def run_parts_with_overlapped_allreduce(parts, grad_hop, table_grad, table, lr: float, comm_stream=None,
+                                        group=None):
+    """One training step given as parts (DrumTrainStep.parts(), or replays of
+    their CUDA graphs): after part j < T has been issued, hop T-1-j's table
+    gradient grad_hop[T-1-j] is complete and its all-reduce (sum) is issued
+    on comm_stream (a CUDA stream; None: in order, e.g. gloo on CPU), so it
+    overlaps the parts that follow.  Then the update waits for all of them:
+    table -= lr / world * table_grad (a view of the summed hop gradients)."""
+    world = dist.get_world_size(group)
+    T = len(grad_hop)
+    for j, part in enumerate(parts):
+        part()
+        if world > 1 and j < T:
+            hop = T - 1 - j
+            if comm_stream is not None:
+                comm_stream.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(comm_stream):
+                    dist.all_reduce(grad_hop[hop], group=group)
+            else:
+                dist.all_reduce(grad_hop[hop], group=group)
+    if world > 1:
+        if comm_stream is not None:
+            torch.cuda.current_stream().wait_stream(comm_stream)
+        table.sub_(table_grad, alpha=lr / world)
+
+
 def max_time_sum_work(ms: float, work: float, device, group=None):
     """(max over ranks of ms, sum over ranks of work)."""
     if dist.get_world_size(group) == 1:

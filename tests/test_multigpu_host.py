@@ -56,6 +56,52 @@ def test_collectives_on_two_gloo_ranks():
         assert ranks_all == [0.0, 10.0, 20.0, 30.0, 40.0]     # unsharded order
 
 
+def _parts_worker(rank, world, port, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from flashlog_b200 import multigpu as MG
+        T = 3
+        grad_hop = torch.zeros(T, 4, 2)           # [T, rows, cols], as DrumTrainStep.grad_hop
+        table = torch.ones(4, T, 2)                # [rows, T, cols]
+        order = []
+
+        def part(hop):
+            def run():
+                order.append(hop)
+                if hop >= 0:  # the part completes hop `hop`'s gradient
+                    grad_hop[hop].fill_(float((rank + 1) * (hop + 1)))
+            return run
+        parts = [part(2), part(1), part(0), part(-1)]  # forward + last hop, hops T-2..0, the update part
+        MG.run_parts_with_overlapped_allreduce(parts, grad_hop, grad_hop.permute(1, 0, 2), table, lr=0.5)
+        out.put((rank, order, table.tolist(), grad_hop.tolist()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_overlapped_allreduce_parts_on_two_gloo_ranks():
+    """Each hop's gradient is summed over the ranks once its part has run, and
+    the update applies lr / world times the sums: here table = 1 - 0.25 *
+    (1 + 2) * (hop + 1) on both ranks."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_parts_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, order, table, grad in res:
+        assert order == [2, 1, 0, -1]
+        for hop in range(3):
+            assert grad[hop] == [[3.0 * (hop + 1)] * 2] * 4
+            for row in range(4):
+                assert table[row][hop] == [1.0 - 0.25 * 3.0 * (hop + 1)] * 2
+
+
 def test_single_process_is_identity():
     from flashlog_b200 import multigpu as MG
     if dist.is_initialized():
