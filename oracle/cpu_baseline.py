@@ -121,14 +121,27 @@ def drum_step_trace(csr_np, heads, tails, w_hops, mask, r_size, E, c1, c2, eps=1
     output state (row, entity, normalized value), the gradient w.r.t. w and
     the gradient w.r.t. the hop's output values.  Forward and backward run in
     the reference's compiled CPU extension
-    (flashlog.cpp:1231-1933); c1 is the oracle's restatement of
-    flashlog_kernel.py:1092-1137, itself pinned to that function's outputs.
+    (flashlog.cpp:1231-1933), on one thread; c1 is the oracle's restatement
+    of flashlog_kernel.py:1092-1137, itself pinned to that function's outputs.
     """
     import torch
 
     if not R.available():
         raise FileNotFoundError("the reference CPU extension (oracle/_ref) is not built")
     M = R.module()
+    # one thread: the extension's parallel loops merge per-thread partial sums,
+    # so its summation order (and last bits) would depend on the core count
+    threads = torch.get_num_threads()
+    torch.set_num_threads(1)
+    try:
+        return _trace(M, csr_np, heads, tails, w_hops, mask, r_size, E, c1, c2, eps)
+    finally:
+        torch.set_num_threads(threads)
+
+
+def _trace(M, csr_np, heads, tails, w_hops, mask, r_size, E, c1, c2, eps):
+    import torch
+
     Q, N, n = w_hops[0].shape
     T = len(w_hops)
     topk = c2 // 2 if c2 > 0 else (1 << 60)
