@@ -145,10 +145,9 @@ def test_step_update_touches_only_the_batch_rows(setup):
 def test_shared_selections_change_nothing(setup, dropout):
     """Rows that use another row's relation ranks have the same weights, so an
     entity in both has the same c2 selection: the step copies it (values
-    rescaled) instead of selecting again.  Outputs, loss and the per-query
-    logits gradients equal the step that selects every entry, bit for bit
-    (the table gradient adds duplicate relations with float atomics, so it
-    is not compared bitwise), and some entries did share."""
+    rescaled) instead of selecting again.  Outputs, loss and gradients equal
+    the step that selects every entry, bit for bit, and some entries did
+    share."""
     from flashlog_b200.step import DrumTrainStep
     from flashlog_b200.synthetic import training_queries
     cfg, train, graph = setup
@@ -172,8 +171,7 @@ def test_shared_selections_change_nothing(setup, dropout):
         shared = int((step.share[:int(step.rp_sel[T - 1][24 * N])] >= 0).sum()) if share else 0
         out.append((loss, [step.out_rp[k].clone() for k in range(T)],
                     [step.out_ent[k][:int(step.out_rp[k][-1])].clone() for k in range(T)],
-                    [step.out_y[k][:int(step.out_rp[k][-1])].clone() for k in range(T)], step.grad_logits.clone(),
-                    shared))
+                    [step.out_y[k][:int(step.out_rp[k][-1])].clone() for k in range(T)], step.grad.clone(), shared))
     (la, rpa, ea, ya, ga, sha), (lb, rpb, eb, yb, gb, _) = out
     assert sha > 0
     assert la == lb
