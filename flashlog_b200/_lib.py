@@ -67,7 +67,7 @@ class fl_hop_params(ctypes.Structure):
                 ("slot_capacity", ctypes.c_int64), ("status", ctypes.c_void_p), ("entry_info", ctypes.c_void_p),
                 ("vis_ori", ctypes.c_void_p), ("vis_inv", ctypes.c_void_p), ("work", ctypes.c_void_p),
                 ("rel_rank", ctypes.c_void_p), ("rank_row", ctypes.c_void_p),
-                ("row_order", ctypes.c_void_p), ("fact_edge", ctypes.c_void_p), ("share", ctypes.c_void_p)]
+                ("row_order", ctypes.c_void_p), ("fact_edge", ctypes.c_void_p)]
 
 
 _P = ctypes.c_void_p
@@ -118,7 +118,7 @@ SIGNATURES = {
                                        _SZ, _P]),
     "fl_normalize_forward": (ctypes.c_int, [_P, _P, _I64, ctypes.c_float, _P, _P, _P]),
     "fl_normalize_backward": (ctypes.c_int, [_P, _P, _P, _P, _I64, ctypes.c_float, _P, _P]),
-    "fl_hop_stats": (ctypes.c_int, [_P, _I64, _P, _I64, _SIDE, _SIDE, _P, _P, ctypes.c_int, _P, _P, _P]),
+    "fl_hop_stats": (ctypes.c_int, [_P, _I64, _P, _I64, _SIDE, _SIDE, _P, _P, ctypes.c_int, _P, _P]),
     "fl_rule_max_reduce": (ctypes.c_int, [_P, _I64, _P, _P, _I64, _P, _I64, _I64, _I64, _P, _P]),
     "fl_scatter_grad": (ctypes.c_int, [_P, _P, _I64, _P, _P, _I64, _P, _DROP, _P]),
     "fl_edge_weight_grad": (ctypes.c_int, [_PARAMS, _P, _P, _I64, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,

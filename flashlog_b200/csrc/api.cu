@@ -271,11 +271,10 @@ int fl_normalize_backward(const int64_t *row_ptr, const float *x, const float *d
 }
 
 int fl_hop_stats(const int64_t *row_ptr, int64_t rows, const int32_t *ent, int64_t S, fl_csr_side ori,
-                 fl_csr_side inv, const int32_t *entry_count, const int64_t *out_row_ptr, int wot_i,
-                 const int32_t *share, int64_t *acc, fl_stream_t stream) {
+                 fl_csr_side inv, const int32_t *entry_count, const int64_t *out_row_ptr, int wot_i, int64_t *acc,
+                 fl_stream_t stream) {
     FL_REQUIRE(acc != nullptr && rows >= 0 && S >= 0, "fl_hop_stats: bad arguments");
-    return hop_stats(row_ptr, rows, ent, S, ori, inv, entry_count, out_row_ptr, wot_i, share, acc,
-                     as_stream(stream));
+    return hop_stats(row_ptr, rows, ent, S, ori, inv, entry_count, out_row_ptr, wot_i, acc, as_stream(stream));
 }
 
 int fl_edge_weight_grad(const fl_hop_params *p, const int64_t *row_ptr, const float *val, int64_t S, const float *w,

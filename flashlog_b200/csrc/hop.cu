@@ -60,27 +60,11 @@ struct EntryInfo {
 static_assert(sizeof(EntryInfo) == FL_ENTRY_INFO_INTS * sizeof(int32_t), "entry record size of the C ABI");
 
 __global__ void hop_capacity_kernel(const int32_t *ent, const int64_t *row_ptr, int64_t rows, int64_t S, Side ori,
-                                    Side inv, int64_t topk, int wot_i, int sides, int64_t *cap, EntryInfo *info,
-                                    const int32_t *rank_row, int32_t *share) {
+                                    Side inv, int64_t topk, int wot_i, int sides, int64_t *cap, EntryInfo *info) {
     int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
     if (i >= S) return;
     if (i >= row_ptr[rows]) { cap[i] = 0; return; }  // beyond the live entries
     int64_t src = ent[i];
-    if (share) {
-        // the same entity in the row whose ranks (and weights) this row uses
-        const int64_t row = find_row(row_ptr, rows, i);
-        const int64_t rep = rank_row[row];
-        int32_t k = -1;
-        if (rep != row && rep >= 0 && rep < rows) {
-            int64_t lo = row_ptr[rep], hi = row_ptr[rep + 1];
-            while (lo < hi) {
-                const int64_t mid = lo + ((hi - lo) >> 1);
-                if (ent[mid] < src) lo = mid + 1; else hi = mid;
-            }
-            if (lo < row_ptr[rep + 1] && ent[lo] == src) k = static_cast<int32_t>(lo);
-        }
-        share[i] = k;
-    }
     // sides: bit 0 forward, bit 1 inverse; a disabled side gets an empty group range
     const int64_t g0o = ori.gptr[src], g1o = (sides & 1) ? ori.gptr[src + 1] : g0o;
     const int64_t g0i = inv.gptr[src], g1i = (sides & 2) ? inv.gptr[src + 1] : g0i;
@@ -172,7 +156,6 @@ struct ExpandArgs {
     float *fact_m;
     int32_t *fact_edge;                // triple id per fact (0 for identity) or null: the MAX tie key
     int32_t *entry_count;
-    const int32_t *share;              // per entry: the entry whose facts it copies, or -1; or null
 };
 
 // Multiplier m and visibility of the fact at CSR position p.
@@ -932,7 +915,7 @@ __global__ void __launch_bounds__(kExpandWarps * 32, kRanked ? 4 : 3) hop_expand
     // whole-warp entries (kBigPass), the team entries (kSmallPass) or both.
     auto four = [&](int64_t base, int which) {
         const int64_t i = base + team;
-        const bool mine = i < S_live && !(a.share != nullptr && a.share[i] >= 0);  // shared: copied afterwards
+        const bool mine = i < S_live;
         bool small = false, over = false;
         int64_t src = 0, out = 0, end = 0;
         EntryInfo e{0, 0, 0, 0, 0};
@@ -1003,41 +986,6 @@ __global__ void __launch_bounds__(kExpandWarps * 32, kRanked ? 4 : 3) hop_expand
         for (int64_t base = (static_cast<int64_t>(blockIdx.x) * kExpandWarps + wib) * 4; base < S_live;
              base += nwarps * 4)
             four(base, kBothPasses);
-    }
-}
-
-// Entries that share their representative's selection: one warp per entry
-// copies the representative's slot range (destinations, -1 markers,
-// relation columns) and writes its own values v * w[relation column], the
-// product the expansion forms (unit masks).
-__global__ void share_copy_kernel(ExpandArgs a) {
-    const int lane = threadIdx.x & 31;
-    const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-    const int64_t S_live = a.row_ptr[a.rows] < a.S ? a.row_ptr[a.rows] : a.S;
-    for (int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; i < S_live; i += nw) {
-        const int32_t k = a.share[i];
-        if (k < 0) continue;
-        const int64_t out = a.slot_base[i], end = a.slot_base[i + 1];
-        if (a.capacity > 0 && end > a.capacity) {
-            if (lane == 0) { a.entry_count[i] = 0; if (a.status) atomicOr(a.status, FL_STATUS_SLOT_OVERFLOW); }
-            continue;
-        }
-        const int64_t src = a.slot_base[k];
-        const int32_t cnt = a.entry_count[k];
-        const int64_t row = a.info ? static_cast<int64_t>(a.info[i].row) : find_row(a.row_ptr, a.rows, i);
-        const float *wrow = a.w + row * a.n;
-        const float v = a.val[i];
-        for (int64_t f = lane; f < end - out; f += 32) {
-            const int32_t d = a.fact_dst[src + f];
-            a.fact_dst[out + f] = d;
-            if (f < cnt) {
-                const int16_t rel = a.fact_rel[src + f];
-                a.fact_rel[out + f] = rel;
-                a.fact_val[out + f] = v * wrow[rel];
-                if (a.fact_edge) a.fact_edge[out + f] = a.fact_edge[src + f];
-            }
-        }
-        if (lane == 0) a.entry_count[i] = cnt;
     }
 }
 
@@ -2101,15 +2049,14 @@ __global__ void __launch_bounds__(kBThreads, 5) hop_backward_kernel(BackwardArgs
 // identity terms), [3] live outputs U.
 __global__ void hop_stats_kernel(const int64_t *row_ptr, int64_t rows, const int32_t *ent, int64_t S, Side ori, Side inv,
                                  const int32_t *entry_count, const int64_t *out_row_ptr, int wot_i,
-                                 const int32_t *share, unsigned long long *acc) {
+                                 unsigned long long *acc) {
     __shared__ long long scratch[33];
     const int64_t live = row_ptr[rows] < S ? row_ptr[rows] : S;
     long long g = 0, f = 0;
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < live;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         const int64_t src = ent[i];
-        if (share == nullptr || share[i] < 0)
-            g += (ori.gptr[src + 1] - ori.gptr[src]) + (inv.gptr[src + 1] - inv.gptr[src]);
+        g += (ori.gptr[src + 1] - ori.gptr[src]) + (inv.gptr[src + 1] - inv.gptr[src]);
         f += entry_count[i] - (wot_i ? 0 : 1);
     }
     g = block_sum(g, scratch);
@@ -2437,8 +2384,7 @@ int hop_plan(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *ent,
         launch(hop_capacity_kernel, static_cast<unsigned>((S + 255) / 256), 256, 0, st, ent, row_ptr, p->rows, S,
                make_side(ori, nullptr), make_side(inv, nullptr), p->topk_edges, (p->flags & FL_WOT_I) ? 1 : 0,
                ((p->flags & FL_NO_ORI) ? 0 : 1) | ((p->flags & FL_NO_INV) ? 0 : 2), cap,
-               reinterpret_cast<EntryInfo *>(p->entry_info), p->rank_row,
-               (p->rank_row != nullptr && !(p->flags & FL_SAMPLED)) ? p->share : nullptr);
+               reinterpret_cast<EntryInfo *>(p->entry_info));
     }
     int rc = exclusive_scan<int64_t>(cap, S, slot_base, scan_ws, sws, st);
     if (rc) return rc;
@@ -2466,11 +2412,6 @@ int hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *en
     a.rank_bin = static_cast<int32_t>((p->r_size + kRankBins - 1) / kRankBins);
     if (a.rel_rank != nullptr && (a.rank_bin < 1 || a.rank_bin > 32)) a.rel_rank = nullptr;
     a.fact_dst = fact_dst; a.fact_val = fact_val; a.fact_rel = fact_rel; a.fact_m = fact_m; a.entry_count = entry_count;
-    // shared selections need the plan's share map and unit masks
-    const bool sharing = p->share != nullptr && a.rel_rank != nullptr && a.rank_row != nullptr &&
-                         !(p->flags & FL_SAMPLED) && mask_csr_ori == nullptr && mask_csr_inv == nullptr &&
-                         edge_weight == nullptr && fact_m == nullptr;
-    a.share = sharing ? p->share : nullptr;
     int sms = fl_device_sm_count();
     const int64_t per_sm = 3;  // resident CTAs per SM (registers and staging buffers)
     int64_t cap_blocks = static_cast<int64_t>(sms > 0 ? sms : 148) * per_sm * 8;
@@ -2500,11 +2441,6 @@ int hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *en
             launch(hop_expand_kernel<true>, static_cast<unsigned>(blocks), kExpandWarps * 32, smem_rank, st, a);
         else
             launch(hop_expand_kernel<false>, static_cast<unsigned>(blocks), kExpandWarps * 32, smem_radix, st, a);
-        if (a.share != nullptr) {
-            int64_t cb = (S + 7) / 8;
-            const int64_t cmax = static_cast<int64_t>(sms > 0 ? sms : 148) * 16;
-            launch(share_copy_kernel, static_cast<unsigned>(cb < cmax ? cb : cmax), 256, 0, st, a);
-        }
     }
     return check_launch("hop_expand");
 }
@@ -2637,16 +2573,15 @@ int normalize_backward(const int64_t *row_ptr, const float *x, const float *deno
 }
 
 int hop_stats(const int64_t *row_ptr, int64_t rows, const int32_t *ent, int64_t S, const fl_csr_side &ori,
-              const fl_csr_side &inv, const int32_t *entry_count, const int64_t *out_row_ptr, int wot_i,
-              const int32_t *share, int64_t *acc, cudaStream_t st) {
+              const fl_csr_side &inv, const int32_t *entry_count, const int64_t *out_row_ptr, int wot_i, int64_t *acc,
+              cudaStream_t st) {
     const int sms = fl_device_sm_count();
     int64_t blocks = (S + 255) / 256;
     const int64_t cap = static_cast<int64_t>(sms > 0 ? sms : 148) * 4;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
     launch(hop_stats_kernel, static_cast<unsigned>(blocks), 256, 0, st, row_ptr, rows, ent, S, make_side(ori, nullptr),
-           make_side(inv, nullptr), entry_count, out_row_ptr, wot_i, share,
-           reinterpret_cast<unsigned long long *>(acc));
+           make_side(inv, nullptr), entry_count, out_row_ptr, wot_i, reinterpret_cast<unsigned long long *>(acc));
     return check_launch("hop_stats");
 }
 

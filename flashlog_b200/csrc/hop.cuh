@@ -42,8 +42,8 @@ int edge_weight_grad(const fl_hop_params *p, const int64_t *row_ptr, const float
                      const int64_t *out_row_ptr, const float *g, const float *edge_weight, float *grad_edge,
                      cudaStream_t st);
 int hop_stats(const int64_t *row_ptr, int64_t rows, const int32_t *ent, int64_t S, const fl_csr_side &ori,
-              const fl_csr_side &inv, const int32_t *entry_count, const int64_t *out_row_ptr, int wot_i,
-              const int32_t *share, int64_t *acc, cudaStream_t st);
+              const fl_csr_side &inv, const int32_t *entry_count, const int64_t *out_row_ptr, int wot_i, int64_t *acc,
+              cudaStream_t st);
 int scatter_grad(const float *grad_sel, const int64_t *src, int64_t n_sel, const int64_t *n_live, float *grad_full,
                  int64_t n_full, const int64_t *full_live, const fl_dropout *drop, cudaStream_t st);
 int topc_select(const int64_t *row_ptr, const int32_t *ent, const float *val, int64_t rows, int64_t S, int64_t c1,

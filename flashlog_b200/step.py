@@ -93,7 +93,7 @@ class DrumTrainStep:
     def __init__(self, graph: Graph, r_size: int, Q: int, T: int, N: int, c1, c2: int, table: torch.Tensor,
                  n_hide: int, lr: float = 0.01, eps: float = 1e-7, thr: float = 1e-7, stats: bool = True,
                  apply_update: bool = True, dropout: float = 0.0, dropout_seed: int = 0, zero_slack=None,
-                 record_grad_w: bool = False, share_selections: bool = True):
+                 record_grad_w: bool = False):
         dev = table.device
         self.dev, self.graph, self.r_size, self.Q, self.T, self.N = dev, graph, r_size, Q, T, N
         self.n = 2 * r_size + 1
@@ -164,9 +164,6 @@ class DrumTrainStep:
         self.rel_rank = _buf(rows * 2 * r_size, i16, dev) if self.use_rank else None
         # rows of queries with one relation have one w: they share the first such row's ranks
         self.rank_row = _buf(rows, i32, dev) if self.use_rank else None
-        # entries of rows that use another row's ranks: the same entity's entry
-        # there, whose c2 selection they share (fl_hop_plan writes it)
-        self.share = _buf(Smax, i32, dev) if (self.use_rank and share_selections) else None
         self.chan = torch.arange(N, dtype=torch.int64, device=dev)
         # per hop: rows by descending slot count, the reduction's and the backward's block order
         self.row_order = [_buf(rows, i32, dev) for _ in range(T)]
@@ -222,8 +219,7 @@ class DrumTrainStep:
                                self.vis[0].data_ptr(), self.vis[1].data_ptr(), self.work.data_ptr(),
                                self.rel_rank.data_ptr() if self.use_rank else None,
                                self.rank_row.data_ptr() if self.use_rank else None,
-                               self.row_order[t].data_ptr(), None,
-                               self.share.data_ptr() if self.share is not None else None)
+                               self.row_order[t].data_ptr())
 
     # ------------------------------------------------------------------
     def run(self):
@@ -301,7 +297,7 @@ class DrumTrainStep:
                 self.timer[t][-1].record()
             if self.stats is not None:
                 check(lb.fl_hop_stats(_p(rp_s), rows, _p(ent_s), self.S[t], g.ori, g.inv, _p(self.entry_count[t]),
-                                      _p(self.out_rp[t]), 0, _p(self.share), _p(self.stats), st), "hop_stats")
+                                      _p(self.out_rp[t]), 0, _p(self.stats), st), "hop_stats")
             rp_in, ent_in, val_in = self.out_rp[t], self.out_ent[t], self.out_y[t]
         # the backward reads no visibility: restore what the batch hid
         for k in range(2):

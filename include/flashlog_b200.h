@@ -91,15 +91,6 @@ typedef struct {
     int32_t *fact_edge;             /* i32[slots] or NULL: fl_hop_expand writes each
                                        fact's triple id (order[p]; 0 for identity),
                                        the tie key of fl_row_reduce_max          */
-    int32_t *share;                 /* i32[S] or NULL: with rank_row, fl_hop_plan
-                                       writes per entry the entry of the same
-                                       entity in the row whose ranks it uses
-                                       (-1: none, or a row of its own); such an
-                                       entry has the same c2 selection, and
-                                       fl_hop_expand copies its facts with the
-                                       values rescaled instead of selecting again.
-                                       Deterministic c2 with unit masks only
-                                       (no FL_SAMPLED, edge weights or CSR masks). */
 } fl_hop_params;
 
 /* Dropout of hop values fused into the kernels that write them (the models'
@@ -286,14 +277,12 @@ int fl_normalize_backward(const int64_t *row_ptr, const float *x, const float *d
                           float eps, float *gx, fl_stream_t stream);
 
 /* Work counts of one hop, added to acc (device i64[4]): live entries S,
- * relation groups visited G (both sides of every entry that selected its
- * own edges: entries with share[i] >= 0 copied a selection and visit none;
- * share may be NULL), facts through graph edges F, live outputs U.  No
- * synchronization; the measurement of bench.py reads them after its timed
- * region. */
+ * relation groups of both sides G, facts through graph edges F, live
+ * outputs U.  No synchronization; the measurement of bench.py reads them
+ * after its timed region. */
 int fl_hop_stats(const int64_t *row_ptr, int64_t rows, const int32_t *ent, int64_t S, fl_csr_side ori,
-                 fl_csr_side inv, const int32_t *entry_count, const int64_t *out_row_ptr, int wot_i,
-                 const int32_t *share, int64_t *acc, fl_stream_t stream);
+                 fl_csr_side inv, const int32_t *entry_count, const int64_t *out_row_ptr, int wot_i, int64_t *acc,
+                 fl_stream_t stream);
 
 /* Gradient of learnable edge weights (the --use_soft path): replaces the
  * chunk loops of flashlog_kernel.py:1306-1336 (SUM) and 1590-1614 (MAX).

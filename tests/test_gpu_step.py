@@ -139,42 +139,3 @@ def test_step_update_touches_only_the_batch_rows(setup):
     untouched = torch.ones(2 * R, dtype=torch.bool, device=dev)
     untouched[d(r[:16])] = False
     assert torch.equal(upd.table[untouched], table[untouched])
-
-
-@pytest.mark.parametrize("dropout", [0.0, 0.1])
-def test_shared_selections_change_nothing(setup, dropout):
-    """Rows that use another row's relation ranks have the same weights, so an
-    entity in both has the same c2 selection: the step copies it (values
-    rescaled) instead of selecting again.  Outputs, loss and gradients equal
-    the step that selects every entry, bit for bit, and some entries did
-    share."""
-    from flashlog_b200.step import DrumTrainStep
-    from flashlog_b200.synthetic import training_queries
-    cfg, train, graph = setup
-    R, T, N = cfg.relations, 3, 3
-    n = 2 * R + 1
-    dev = torch.device("cuda")
-    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
-    ids, h, r, t = training_queries(train, cfg, step=17)
-    h, r, t, ids = h[:24].copy(), r[:24].copy(), t[:24], ids[:12]
-    r[12:] = r[:12]  # half the queries repeat a relation: their rows share ranks
-    gen = torch.Generator(device="cpu").manual_seed(13)
-    table = torch.randn(2 * R, T, N, n, generator=gen).cuda()
-    out = []
-    for share in (True, False):
-        step = DrumTrainStep(graph, R, 24, T, N, 40, 16, table.clone(), n_hide=ids.size, apply_update=False,
-                             dropout=dropout, dropout_seed=3, share_selections=share)
-        step.load(d(h), d(t), d(r), d(ids))
-        loss = float(step.run())
-        torch.cuda.synchronize()
-        step.check()
-        shared = int((step.share[:int(step.rp_sel[T - 1][24 * N])] >= 0).sum()) if share else 0
-        out.append((loss, [step.out_rp[k].clone() for k in range(T)],
-                    [step.out_ent[k][:int(step.out_rp[k][-1])].clone() for k in range(T)],
-                    [step.out_y[k][:int(step.out_rp[k][-1])].clone() for k in range(T)], step.grad.clone(), shared))
-    (la, rpa, ea, ya, ga, sha), (lb, rpb, eb, yb, gb, _) = out
-    assert sha > 0
-    assert la == lb
-    for k in range(T):
-        assert torch.equal(rpa[k], rpb[k]) and torch.equal(ea[k], eb[k]) and torch.equal(ya[k], yb[k])
-    assert torch.equal(ga, gb)
