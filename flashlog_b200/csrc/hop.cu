@@ -1855,28 +1855,62 @@ __global__ void __launch_bounds__(kRThreads, kRowCtasPerSm) row_reduce_kernel(Re
 
 // Compact per-row outputs (at the row's slot base) into a row layout and
 // write normalized values.
-__global__ void compact_kernel(const int64_t *row_ptr, const int64_t *slot_base, const int64_t *out_row_ptr,
-                               int64_t rows, const int32_t *tmp_ent, const float *tmp_x, const float *out_sum,
-                               float eps, int32_t *out_ent, float *out_x, float *out_y, float *out_denom,
-                               DropoutArgs drop) {
-    const int64_t r = blockIdx.x;
-    if (r >= rows) return;
-    const int64_t o0 = out_row_ptr[r], n = out_row_ptr[r + 1] - o0;
-    const float d = out_sum[r];
-    if (threadIdx.x == 0 && out_denom) out_denom[r] = d;
-    if (n == 0) return;
-    const int64_t src0 = slot_base[row_ptr[r]];
-    const float dd = d > eps ? d : eps;
+constexpr int kCompactThreads = 256;
+constexpr int kCompactTile = 4 * kCompactThreads;  // outputs per CTA step
+
+// Compact the per-row outputs (written at each row's slot base) into the
+// packed row layout and normalize them.  Persistent CTAs take tiles of
+// kCompactTile consecutive output positions: one thread finds the rows
+// holding the tile's first and last output, every thread finds its own row
+// inside that range, and the copies are coalesced.  The row denominators
+// (empty rows included) are written by a strided loop over the rows.
+__global__ void __launch_bounds__(kCompactThreads) compact_kernel(
+    const int64_t *row_ptr, const int64_t *slot_base, const int64_t *out_row_ptr, int64_t rows, const int32_t *tmp_ent,
+    const float *tmp_x, const float *out_sum, float eps, int32_t *out_ent, float *out_x, float *out_y,
+    float *out_denom, DropoutArgs drop) {
+    __shared__ int64_t span[2];
+    if (out_denom)
+        for (int64_t r = blockIdx.x * static_cast<int64_t>(kCompactThreads) + threadIdx.x; r < rows;
+             r += static_cast<int64_t>(gridDim.x) * kCompactThreads)
+            out_denom[r] = out_sum[r];
+    const int64_t U = out_row_ptr[rows];
     const uint64_t key = drop.on ? dropout_key(drop) : 0ull;
-    for (int64_t k = threadIdx.x; k < n; k += blockDim.x) {
-        float x = tmp_x[src0 + k];
-        out_ent[o0 + k] = tmp_ent[src0 + k];
-        if (out_x) out_x[o0 + k] = x;
-        if (out_y) {
-            float y = x / dd;
-            if (drop.on) y *= dropout_factor(drop, key, o0 + k);  // the values' training dropout, in place
-            out_y[o0 + k] = y;
+    for (int64_t t0 = static_cast<int64_t>(blockIdx.x) * kCompactTile; t0 < U;
+         t0 += static_cast<int64_t>(gridDim.x) * kCompactTile) {
+        const int64_t t1 = (t0 + kCompactTile) < U ? (t0 + kCompactTile) : U;
+        if (threadIdx.x < 2) {  // largest row r with out_row_ptr[r] <= output (the rows holding t0 and t1 - 1)
+            const int64_t o = threadIdx.x == 0 ? t0 : t1 - 1;
+            int64_t lo = 0, hi = rows - 1;
+            while (lo < hi) {
+                const int64_t mid = (lo + hi + 1) >> 1;
+                if (out_row_ptr[mid] <= o) lo = mid; else hi = mid - 1;
+            }
+            span[threadIdx.x] = lo;
         }
+        __syncthreads();
+        const int64_t ra = span[0], rb = span[1];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int64_t o = t0 + k * kCompactThreads + threadIdx.x;
+            if (o >= t1) break;
+            int64_t lo = ra, hi = rb;
+            while (lo < hi) {
+                const int64_t mid = (lo + hi + 1) >> 1;
+                if (out_row_ptr[mid] <= o) lo = mid; else hi = mid - 1;
+            }
+            const int64_t r = lo;
+            const int64_t src = slot_base[row_ptr[r]] + (o - out_row_ptr[r]);
+            const float d = out_sum[r];
+            const float x = tmp_x[src];
+            out_ent[o] = tmp_ent[src];
+            if (out_x) out_x[o] = x;
+            if (out_y) {
+                float y = x / (d > eps ? d : eps);
+                if (drop.on) y *= dropout_factor(drop, key, o);  // the values' training dropout, in place
+                out_y[o] = y;
+            }
+        }
+        __syncthreads();  // span[] is rewritten for the next tile
     }
 }
 
@@ -2445,6 +2479,16 @@ int hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *en
     return check_launch("hop_expand");
 }
 
+// Persistent compaction grid: enough CTAs for the output capacity, at most 8 per SM.
+static int64_t compact_grid(int64_t rows, int64_t capacity) {
+    const int sms = fl_device_sm_count();
+    const int64_t cap = static_cast<int64_t>(sms > 0 ? sms : 148) * 8;
+    int64_t need = (capacity + kCompactTile - 1) / kCompactTile;
+    const int64_t need_rows = (rows + kCompactThreads - 1) / kCompactThreads;
+    if (need < need_rows) need = need_rows;
+    return need < 1 ? 1 : (need > cap ? cap : need);
+}
+
 static int reduce_rows(const int64_t *row_ptr, int64_t rows, int64_t E, const int64_t *slot_base,
                        const int32_t *fact_dst, const float *fact_val, int64_t total_slots, int32_t *fact_pos,
                        float eps, int64_t *out_row_ptr, int32_t *out_ent, float *out_x, float *out_y,
@@ -2488,7 +2532,8 @@ static int reduce_rows(const int64_t *row_ptr, int64_t rows, int64_t E, const in
     int rc = exclusive_scan<int64_t>(out_count, rows, out_row_ptr, scan_ws, sws, st);
     if (rc) return rc;
     if (rows > 0)
-        launch(compact_kernel, static_cast<unsigned>(rows), 256, 0, st, row_ptr, slot_base, out_row_ptr, rows, tmp_ent, tmp_x,
+        launch(compact_kernel, static_cast<unsigned>(compact_grid(rows, total_slots)), kCompactThreads, 0, st, row_ptr,
+               slot_base, out_row_ptr, rows, tmp_ent, tmp_x,
                out_sum, eps, out_ent, out_x, out_y, out_denom, dargs);
     return check_launch("row_compact");
 }

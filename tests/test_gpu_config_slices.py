@@ -10,8 +10,12 @@ compared with the reference's compiled OpenMP extension
 the same fp32 attention weights:
 
 * the c1 selection of every hop and the output coordinates: bit-exact;
-* the normalized values: rel 1e-5 (they are in fact bit-identical: both sum
-  every destination left to right in canonical order);
+* the normalized values y = x / d: at least 99.99% within rel 1e-5 and all
+  within rel 3e-5.  The sums x are taken left to right in canonical order on
+  both sides; the row normalizer d sums up to ~20,000 fp32 outputs, in
+  sequence in the reference and by a fixed tree here, and the two roundings
+  differ by up to ~2e-5 on the largest rows (config 3, hop 3: 3 of 834,884
+  values between 1e-5 and 1.7e-5);
 * d loss / d w of every hop and d loss / d y of every hop's output:
   rel 1e-5, with an absolute floor of 5e-5 x the largest magnitude of the
   hop's reference gradient.  Both sides sum thousands of fp32 terms in
@@ -64,6 +68,13 @@ def _graph(index):
     return _cached[index]
 
 
+def _close_values(got, want, what):
+    scale = float(np.abs(want).max()) if want.size else 0.0
+    np.testing.assert_allclose(got, want, rtol=3e-5, atol=1e-6 * scale, err_msg=what)
+    tight = np.abs(got - want) <= RTOL * np.abs(want) + 1e-6 * scale
+    assert tight.mean() >= 0.9999, (what, int((~tight).sum()))
+
+
 def _close(got, want, what, floor=1e-6):
     scale = float(np.abs(want).max()) if want.size else 0.0
     np.testing.assert_allclose(got, want, rtol=RTOL, atol=floor * scale, err_msg=what)
@@ -112,7 +123,7 @@ def test_train_step_slice_matches_reference_cpu(index):
         assert np.array_equal(np.repeat(np.arange(rows), counts), hop["out_row"]), f"hop {k}: output rows"
         assert np.array_equal(step.out_ent[k][:u].cpu().numpy().astype(np.int64), hop["out_ent"]), \
             f"hop {k}: output entities"
-        _close(step.out_y[k][:u].cpu().numpy(), hop["y"], f"hop {k}: values")
+        _close_values(step.out_y[k][:u].cpu().numpy(), hop["y"], f"hop {k}: values")
         _close(step.g_y[k][:u].cpu().numpy(), hop["g_out"], f"hop {k}: d loss / d y", GRAD_FLOOR)
         _close(step.grad_w_of(k).cpu().numpy(), hop["gw"], f"hop {k}: d loss / d w", GRAD_FLOOR)
     # the slice is not trivial: the last hop expands hub frontiers under both budgets
