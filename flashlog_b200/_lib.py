@@ -103,6 +103,7 @@ SIGNATURES = {
     "fl_hop_plan": (ctypes.c_int, [_PARAMS, _P, _P, _I64, _SIDE, _SIDE, _P, ctypes.POINTER(ctypes.c_int64), _P,
                                    _SZ, _P]),
     "fl_csr_visibility": (ctypes.c_int, [_P, _I64, _P, _P, _P]),
+    "fl_row_order": (ctypes.c_int, [_P, _P, _I64, _P, _P]),
     "fl_csr_mask": (ctypes.c_int, [_P, ctypes.c_int, _P, _I64, _P, _P, _P]),
     "fl_align_rows": (ctypes.c_int, [_P, _P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P]),
     "fl_relation_rank": (ctypes.c_int, [_P, _I64, _I64, _P, _P, _P]),

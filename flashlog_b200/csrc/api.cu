@@ -198,6 +198,11 @@ int fl_relation_rank(const float *w, int64_t rows, int64_t r_size, const int32_t
     return relation_rank(w, rows, r_size, rank_row, rank, as_stream(stream));
 }
 
+int fl_row_order(const int64_t *row_ptr, const int64_t *slot_base, int64_t rows, int32_t *order, fl_stream_t stream) {
+    FL_REQUIRE(rows == 0 || (row_ptr && slot_base && order), "fl_row_order: null pointer");
+    return row_order(row_ptr, slot_base, rows, order, as_stream(stream));
+}
+
 int fl_csr_visibility(const int32_t *order, int64_t m, const uint8_t *mask_triple, uint8_t *vis, fl_stream_t stream) {
     FL_REQUIRE(m >= 0 && (m == 0 || (order && mask_triple && vis)), "fl_csr_visibility: bad arguments");
     return csr_visibility(order, m, mask_triple, vis, as_stream(stream));

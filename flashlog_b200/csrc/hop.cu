@@ -83,6 +83,40 @@ __global__ void hop_capacity_kernel(const int32_t *ent, const int64_t *row_ptr, 
     cap[i] = d0 + d1 + (wot_i ? 0 : 1);
 }
 
+// Rows by descending slot count, ties to the lower row (a stable descending
+// argsort of the per-row slot counts): one block sorts the keys
+// (~count << 32 | row) ascending in shared memory by a bitonic network.
+constexpr int kRowOrderMax = 16384;
+__global__ void __launch_bounds__(1024) row_order_kernel(const int64_t *row_ptr, const int64_t *slot_base, int64_t rows,
+                                                        int32_t *order) {
+    extern __shared__ unsigned long long okey[];
+    int m = 1;
+    while (m < rows) m <<= 1;
+    for (int i = threadIdx.x; i < m; i += blockDim.x) {
+        unsigned long long k = ~0ull;
+        if (i < rows) {
+            const int64_t cnt = slot_base[row_ptr[i + 1]] - slot_base[row_ptr[i]];
+            k = (static_cast<unsigned long long>(~static_cast<uint32_t>(cnt)) << 32) | static_cast<uint32_t>(i);
+        }
+        okey[i] = k;
+    }
+    __syncthreads();
+    for (int k = 2; k <= m; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < m; i += blockDim.x) {
+                const int l = i ^ j;
+                if (l > i) {
+                    const unsigned long long a = okey[i], b = okey[l];
+                    const bool up = (i & k) == 0;
+                    if ((a > b) == up) { okey[i] = b; okey[l] = a; }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    for (int i = threadIdx.x; i < rows; i += blockDim.x) order[i] = static_cast<int32_t>(okey[i] & 0xffffffffull);
+}
+
 // CSR-ordered visibility of one side: vis[p] = mask_triple[order[p]].
 __global__ void csr_visibility_kernel(const int32_t *order, int64_t m, const uint8_t *mask_triple, uint8_t *vis) {
     for (int64_t p = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; p < m;
@@ -2382,6 +2416,23 @@ int relation_rank(const float *w, int64_t rows, int64_t r_size, const int32_t *r
         launch(rel_rank_kernel, static_cast<unsigned>(rows * 2), 1024, smem, st, w, 2 * r_size + 1, r_size, P,
                rank_row, rank);
     return check_launch("relation_rank");
+}
+
+int row_order(const int64_t *row_ptr, const int64_t *slot_base, int64_t rows, int32_t *order, cudaStream_t st) {
+    FL_REQUIRE(rows >= 0 && rows <= kRowOrderMax, "fl_row_order handles at most %d rows (got %lld)", kRowOrderMax,
+               static_cast<long long>(rows));
+    if (rows == 0) return FL_OK;
+    int m = 1;
+    while (m < rows) m <<= 1;
+    const size_t smem = static_cast<size_t>(m) * sizeof(unsigned long long);
+    static bool attr_set = false;
+    if (!attr_set) {
+        FL_CUDA(cudaFuncSetAttribute(row_order_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(kRowOrderMax * sizeof(unsigned long long))));
+        attr_set = true;
+    }
+    launch(row_order_kernel, 1, 1024, smem, st, row_ptr, slot_base, rows, order);
+    return check_launch("row_order");
 }
 
 int csr_visibility(const int32_t *order, int64_t m, const uint8_t *mask_triple, uint8_t *vis, cudaStream_t st) {

@@ -13,6 +13,7 @@ int hop_plan(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *ent,
              cudaStream_t st);
 int relation_rank(const float *w, int64_t rows, int64_t r_size, const int32_t *rank_row, uint16_t *rank,
                   cudaStream_t st);
+int row_order(const int64_t *row_ptr, const int64_t *slot_base, int64_t rows, int32_t *order, cudaStream_t st);
 int csr_visibility(const int32_t *order, int64_t m, const uint8_t *mask_triple, uint8_t *vis, cudaStream_t st);
 int hop_expand(const fl_hop_params *p, const int64_t *row_ptr, const int32_t *ent, const float *val, int64_t S,
                const float *w, const fl_csr_side &ori, const fl_csr_side &inv, const float *mask_csr_ori,

@@ -278,8 +278,11 @@ class DrumTrainStep:
             check(lb.fl_hop_plan(ctypes.byref(params), _p(rp_s), _p(ent_s), self.S[t], g.ori, g.inv,
                                  _p(self.slot_base[t]), None, ws, wsn, st), "hop_plan")
             # rows by descending slot count: the reduction and the backward take the heaviest first
-            rows_facts = self.slot_base[t][rp_s[1:]] - self.slot_base[t][rp_s[:-1]]
-            self.row_order[t].copy_(torch.argsort(rows_facts, descending=True, stable=True))
+            if rows <= 16384:
+                check(lb.fl_row_order(_p(rp_s), _p(self.slot_base[t]), rows, _p(self.row_order[t]), st), "row_order")
+            else:
+                rows_facts = self.slot_base[t][rp_s[1:]] - self.slot_base[t][rp_s[:-1]]
+                self.row_order[t].copy_(torch.argsort(rows_facts, descending=True, stable=True))
             if self.timer is not None:
                 self.timer[t][0].record()
             check(lb.fl_hop_expand(ctypes.byref(params), _p(rp_s), _p(ent_s), _p(val_s), self.S[t], _p(self.w[t]),

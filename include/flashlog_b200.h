@@ -181,6 +181,12 @@ int fl_relation_rank(const float *w, int64_t rows, int64_t r_size, const int32_t
  * by the hops. */
 int fl_csr_visibility(const int32_t *order, int64_t m, const uint8_t *mask_triple, uint8_t *vis, fl_stream_t stream);
 
+/* The order in which the row reduction and the backward take the rows
+ * (fl_hop_params.row_order): rows by descending slot count
+ * slot_base[row_ptr[r + 1]] - slot_base[row_ptr[r]], ties to the lower row.
+ * One block; at most 16384 rows (FL_EINVAL above). */
+int fl_row_order(const int64_t *row_ptr, const int64_t *slot_base, int64_t rows, int32_t *order, fl_stream_t stream);
+
 /* Kinds of the triple-indexed mask of fl_csr_mask. */
 enum { FL_MASK_U8 = 0, FL_MASK_F32 = 1 };
 

@@ -849,3 +849,23 @@ def test_max_product_matches_reference_golden(fk, g1, golden, ci):
     oi = out.indices().cpu().numpy()
     assert np.array_equal(oi[0] * cfg.entities + oi[1], g[f"r{ci}_key"])
     np.testing.assert_allclose(out.values().cpu().numpy(), g[f"r{ci}_val"], rtol=RTOL, atol=1e-9)
+
+
+@pytest.mark.parametrize("rows", [1, 7, 1536, 5000, 16384])
+def test_row_order_is_a_stable_descending_argsort(fk, rows):
+    """fl_row_order: rows by descending slot count, ties to the lower row."""
+    import ctypes
+    from flashlog_b200 import _lib
+    rng = np.random.default_rng(rows)
+    entries = rng.integers(0, 4, rows)                      # entries per row
+    row_ptr = np.concatenate([[0], np.cumsum(entries)]).astype(np.int64)
+    slots = rng.integers(0, 6, row_ptr[-1])                 # few distinct counts: many ties
+    slot_base = np.concatenate([[0], np.cumsum(slots)]).astype(np.int64)
+    order = torch.empty(rows, dtype=torch.int32, device="cuda")
+    rp, sb = _cuda(row_ptr), _cuda(slot_base)
+    rc = _lib.lib().fl_row_order(rp.data_ptr(), sb.data_ptr(), rows, order.data_ptr(),
+                                 ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0
+    counts = slot_base[row_ptr[1:]] - slot_base[row_ptr[:-1]]
+    want = np.argsort(-counts, kind="stable")
+    assert np.array_equal(order.cpu().numpy(), want)
