@@ -66,6 +66,10 @@ def parse():
                     help="instead of the training step: max-product rule-bank evaluation of this many test "
                          "queries (sharded over the ranks), --rule-bank rules, queries/s")
     ap.add_argument("--rule-bank", type=int, default=50_000)
+    ap.add_argument("--rule-timing", action="store_true",
+                    help="synchronize between the evaluator's phases and report their host times")
+    ap.add_argument("--rule-ops", choices=("edge", "uniform"), default="edge",
+                    help="body operators drawn by edge frequency (default) or uniformly over the 2R operators")
     ap.add_argument("--rule-max", action="store_true", help="mmDRUM (max over ranks); default smDRUM (sum)")
     return ap.parse_args()
 
@@ -525,11 +529,11 @@ def run_rules(args, rank, world, device):
     torch.cuda.empty_cache()
     src, rel, dst = evaluation_queries(test, cfg.relations, (args.rules + 1) // 2)
     src, rel, dst = src[:args.rules], rel[:args.rules], dst[:args.rules]
-    rules = rule_bank(train, rel, cfg.relations, args.rule_bank)
+    rules = rule_bank(train, rel, cfg.relations, args.rule_bank, uniform_ops=args.rule_ops == "uniform")
     lo, hi = MG.shard_bounds(src.size, rank, world)
     d = lambda a: torch.from_numpy(np.ascontiguousarray(a[lo:hi])).to(device)
     s_d, r_d, t_d = d(src), d(rel), d(dst)
-    stats = {}
+    stats = {"timing": bool(args.rule_timing)}
     # warm-up: the first relation group (kernel attributes, allocator)
     w_n = min(64, hi - lo)
     RB.evaluate_rule_bank(s_d[:w_n], r_d[:w_n], t_d[:w_n], rules, csr, cfg.relations, cfg.entities,
@@ -559,11 +563,16 @@ def run_rules(args, rank, world, device):
                 "unit": "queries/s", "n_gpus": world, "ms_total": ms, "wall_s_rank0": wall,
                 "higher_is_better": True, "scaling": "strong", "dtype": "f32", "data": "synthetic",
                 "config": {"workload": f"config {cfg.index}: {cfg.entities} entities, {cfg.train_triples} triples; "
-                                       f"{args.rules} test queries, {args.rule_bank} rules, "
+                                       f"{args.rules} test queries, {args.rule_bank} rules "
+                                       f"(body operators by {'edge frequency' if args.rule_ops == 'edge' else 'uniform draw'}), "
                                        f"{'mmDRUM (max)' if args.rule_max else 'smDRUM (sum)'} over 3 ranks",
                            "parallelism": f"query-sharded dp{world}"},
                 "metrics": {"mrr": float((1.0 / r).mean()), "hits@10": float((r <= 10).mean())},
-                "rules_after_pruning_last_batch": stats.get("rules_after"),
+                "rule_instances_rank0": stats.get("instances"), "batches_rank0": stats.get("batches"),
+                "entries_rank0": stats.get("entries"), "bitmap_rows_rank0": stats.get("bitmap_rows"),
+                "dense_queries_rank0": stats.get("dense_queries"),
+                "phase_s_rank0": {k: stats[k] for k in ("ground_s", "score_s") if k in stats},
+                "compacted_rules": stats.get("rules_after"),
                 "gpu_launches": launches}
         print(json.dumps(line))
 

@@ -134,6 +134,13 @@ SIGNATURES = {
     "fl_fixed_relation_fill": (ctypes.c_int, [_P, _P, _P, _P, _I64, _P, _I64, _I64, _SIDE, _SIDE, _P, _P, _P, _P,
                                               _P]),
     "fl_rule_rank_facts": (ctypes.c_int, [_P, _P, _P, _I64, _I64, _P, _I64, _P, _P, _P, _P, _P, _P, _P]),
+    "fl_rule_instance_facts": (ctypes.c_int, [_P, _P, _P, _I64, _P, _I64, _P, _P, _P, _P]),
+    "fl_fixed_relation_bitmap": (ctypes.c_int, [_P, _I64, _P, _P, _P, _P, _I64, _SIDE, _SIDE, _P, _I64,
+                                                _P]),
+    "fl_rule_instance_max": (ctypes.c_int, [_P, _P, _P, _I64, _P, _I64, _I64, _P, _P]),
+    "fl_bitmap_rows_workspace": (_SZ, [_I64, _I64]),
+    "fl_bitmap_rows_count": (ctypes.c_int, [_P, _I64, _I64, _P, _P, _P, _SZ, _P]),
+    "fl_bitmap_rows_emit": (ctypes.c_int, [_P, _I64, _I64, _P, _P, _P]),
     "fl_filtered_ranks_workspace": (_SZ, [_I64]),
     "fl_filtered_ranks": (ctypes.c_int, [_P, _P, _P, _I64, _P, _P, _I64, _I64, _I64, ctypes.c_int, _P, _P, _SZ,
                                          _P]),

@@ -52,6 +52,19 @@ size_t filtered_ranks_workspace(int64_t B);
 int rule_rank_facts(const int64_t *st_rp, const int32_t *st_ent, const float *st_val, int64_t B, int64_t C,
                     const float *w, int64_t ranks, const int64_t *run_rp, const int32_t *run_ent, const float *run_val,
                     int64_t *slot_base, int32_t *fact_dst, float *fact_val, cudaStream_t st);
+int rule_instance_facts(const int64_t *st_rp, const int32_t *st_ent, const int64_t *q_inst, int64_t B,
+                        const float *w, int64_t ranks, int64_t *slot_base, int32_t *fact_dst, float *fact_val,
+                        cudaStream_t st);
+int rule_instance_max(const int64_t *st_rp, const int32_t *st_ent, const int64_t *q_inst, int64_t nq, const float *w,
+                      int64_t ranks, int64_t E, unsigned int *acc, cudaStream_t st);
+size_t bitmap_rows_workspace(int64_t nb, int64_t words);
+int fixed_relation_bitmap(const int64_t *entries, int64_t n, const int64_t *entry_row, const int32_t *row_slot,
+                          const int32_t *ent, const int64_t *ops, int64_t R, const fl_csr_side &ori,
+                          const fl_csr_side &inv, uint32_t *bitmap, int64_t words, cudaStream_t st);
+int bitmap_rows_count(const uint32_t *bitmap, int64_t nb, int64_t words, int64_t *chunk_off, int64_t *row_ptr,
+                      void *ws, size_t ws_bytes, cudaStream_t st);
+int bitmap_rows_emit(const uint32_t *bitmap, int64_t nb, int64_t words, const int64_t *chunk_off, int32_t *ent,
+                     cudaStream_t st);
 int rule_max_reduce(const int64_t *row_ptr, int64_t rows, const int32_t *ent, const float *val, int64_t C,
                     const float *weights, int64_t ranks, int64_t B, int64_t E, unsigned int *acc, cudaStream_t st);
 int filtered_ranks(const int64_t *ib, const int64_t *ie, const float *v, int64_t nnz, const int64_t *targets,
@@ -327,6 +340,36 @@ int fl_rule_rank_facts(const int64_t *st_rp, const int32_t *st_ent, const float 
                        fl_stream_t stream) {
     return rule_rank_facts(st_rp, st_ent, st_val, B, C, w, ranks, run_rp, run_ent, run_val, slot_base, fact_dst,
                            fact_val, as_stream(stream));
+}
+
+int fl_rule_instance_facts(const int64_t *st_rp, const int32_t *st_ent, const int64_t *q_inst, int64_t B,
+                           const float *w, int64_t ranks, int64_t *slot_base, int32_t *fact_dst, float *fact_val,
+                           fl_stream_t stream) {
+    return rule_instance_facts(st_rp, st_ent, q_inst, B, w, ranks, slot_base, fact_dst, fact_val, as_stream(stream));
+}
+
+int fl_fixed_relation_bitmap(const int64_t *entries, int64_t n, const int64_t *entry_row, const int32_t *row_slot,
+                             const int32_t *ent, const int64_t *ops, int64_t r_size, fl_csr_side ori,
+                             fl_csr_side inv, uint32_t *bitmap, int64_t words, fl_stream_t stream) {
+    return fixed_relation_bitmap(entries, n, entry_row, row_slot, ent, ops, r_size, ori, inv, bitmap, words,
+                                 as_stream(stream));
+}
+
+int fl_rule_instance_max(const int64_t *st_rp, const int32_t *st_ent, const int64_t *q_inst, int64_t nq,
+                         const float *w, int64_t ranks, int64_t E, uint32_t *acc, fl_stream_t stream) {
+    return rule_instance_max(st_rp, st_ent, q_inst, nq, w, ranks, E, acc, as_stream(stream));
+}
+
+size_t fl_bitmap_rows_workspace(int64_t nb, int64_t words) { return bitmap_rows_workspace(nb, words); }
+
+int fl_bitmap_rows_count(const uint32_t *bitmap, int64_t nb, int64_t words, int64_t *chunk_off, int64_t *row_ptr,
+                         void *ws, size_t ws_bytes, fl_stream_t stream) {
+    return bitmap_rows_count(bitmap, nb, words, chunk_off, row_ptr, ws, ws_bytes, as_stream(stream));
+}
+
+int fl_bitmap_rows_emit(const uint32_t *bitmap, int64_t nb, int64_t words, const int64_t *chunk_off, int32_t *ent,
+                        fl_stream_t stream) {
+    return bitmap_rows_emit(bitmap, nb, words, chunk_off, ent, as_stream(stream));
 }
 
 int fl_filtered_ranks(const int64_t *idx_b, const int64_t *idx_e, const float *values, int64_t nnz,

@@ -1893,9 +1893,10 @@ constexpr int kCompactThreads = 256;
 constexpr int kCompactTile = 4 * kCompactThreads;  // outputs per CTA step
 
 // Compact the per-row outputs (written at each row's slot base) into the
-// packed row layout and normalize them.  Persistent CTAs take tiles of
-// kCompactTile consecutive output positions: one thread finds the rows
-// holding the tile's first and last output, every thread finds its own row
+// packed row layout and normalize them.  Persistent CTAs each take a
+// contiguous run of tiles of kCompactTile consecutive output positions: one
+// thread finds the rows holding the tile's first and last output, galloping
+// forward from the previous tile's last row, every thread finds its own row
 // inside that range, and the copies are coalesced.  The row denominators
 // (empty rows included) are written by a strided loop over the rows.
 __global__ void __launch_bounds__(kCompactThreads) compact_kernel(
@@ -1909,17 +1910,41 @@ __global__ void __launch_bounds__(kCompactThreads) compact_kernel(
             out_denom[r] = out_sum[r];
     const int64_t U = out_row_ptr[rows];
     const uint64_t key = drop.on ? dropout_key(drop) : 0ull;
-    for (int64_t t0 = static_cast<int64_t>(blockIdx.x) * kCompactTile; t0 < U;
-         t0 += static_cast<int64_t>(gridDim.x) * kCompactTile) {
+    // a contiguous run of tiles per CTA: the row of each tile's last output
+    // is where the next tile starts looking
+    const int64_t tiles = (U + kCompactTile - 1) / kCompactTile;
+    const int64_t per = (tiles + gridDim.x - 1) / gridDim.x;
+    const int64_t tb = static_cast<int64_t>(blockIdx.x) * per;
+    const int64_t te = (tb + per) < tiles ? (tb + per) : tiles;
+    if (tb >= te) return;
+    auto row_of = [&](int64_t o, int64_t lo) {  // largest r >= lo with out_row_ptr[r] <= o (galloping, then halving)
+        int64_t step = 1, hi = lo;
+        while (hi + step < rows && out_row_ptr[hi + step] <= o) { hi += step; step <<= 1; }
+        lo = hi;
+        hi = (hi + step) < rows ? (hi + step) : rows - 1;
+        while (lo < hi) {
+            const int64_t mid = (lo + hi + 1) >> 1;
+            if (out_row_ptr[mid] <= o) lo = mid; else hi = mid - 1;
+        }
+        return lo;
+    };
+    if (threadIdx.x == 0) {
+        int64_t lo = 0, hi = rows - 1;
+        const int64_t o = tb * kCompactTile;
+        while (lo < hi) {
+            const int64_t mid = (lo + hi + 1) >> 1;
+            if (out_row_ptr[mid] <= o) lo = mid; else hi = mid - 1;
+        }
+        span[1] = lo;
+    }
+    __syncthreads();
+    for (int64_t tile = tb; tile < te; ++tile) {
+        const int64_t t0 = tile * kCompactTile;
         const int64_t t1 = (t0 + kCompactTile) < U ? (t0 + kCompactTile) : U;
-        if (threadIdx.x < 2) {  // largest row r with out_row_ptr[r] <= output (the rows holding t0 and t1 - 1)
-            const int64_t o = threadIdx.x == 0 ? t0 : t1 - 1;
-            int64_t lo = 0, hi = rows - 1;
-            while (lo < hi) {
-                const int64_t mid = (lo + hi + 1) >> 1;
-                if (out_row_ptr[mid] <= o) lo = mid; else hi = mid - 1;
-            }
-            span[threadIdx.x] = lo;
+        if (threadIdx.x == 0) {
+            const int64_t ra = row_of(t0, span[1]);
+            span[0] = ra;
+            span[1] = row_of(t1 - 1, ra);
         }
         __syncthreads();
         const int64_t ra = span[0], rb = span[1];

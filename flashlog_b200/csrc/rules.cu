@@ -35,7 +35,7 @@ __global__ void fixed_count_kernel(const int64_t *b, const int64_t *l, const int
                                    const int64_t *ops, int64_t Lr, int64_t R, SideR ori, SideR inv, int64_t *cnt) {
     int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
     if (i >= nnz) return;
-    const int64_t op = ops[b[i] * Lr + l[i]];
+    const int64_t op = ops[b[i] * Lr + (l != nullptr ? l[i] : 0)];
     if (op == 2 * R) { cnt[i] = 1; return; }
     const bool inv_dir = op >= R;
     const int rel = static_cast<int>(inv_dir ? op - R : op);
@@ -51,9 +51,9 @@ __global__ void fixed_fill_kernel(const int64_t *b, const int64_t *l, const int3
     const int lane = threadIdx.x & 31;
     const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); i < nnz; i += nw) {
-        const int64_t op = ops[b[i] * Lr + l[i]];
+        const int64_t op = ops[b[i] * Lr + (l != nullptr ? l[i] : 0)];
         const int64_t out = slot_base[i];
-        const float v = val[i];
+        const float v = val != nullptr ? val[i] : 1.0f;
         if (op == 2 * R) {
             if (lane == 0) { fact_dst[out] = ent[i]; fact_val[out] = v; entry_count[i] = 1; }
             continue;
@@ -149,7 +149,7 @@ __global__ void rule_max_kernel(const int64_t *row_ptr, int64_t rows, const int3
         const int64_t q = r / C, c = r % C;
         const int64_t a = row_ptr[r], b = row_ptr[r + 1];
         for (int64_t k = a + lane; k < b; k += 32) {
-            if (!(val[k] > 0.0f)) continue;
+            if (val != nullptr && !(val[k] > 0.0f)) continue;
             const int64_t e = ent[k];
             for (int64_t rk = 0; rk < ranks; ++rk) {
                 const unsigned int wbits = __float_as_uint(weights[c * ranks + rk]);
@@ -200,7 +200,204 @@ __global__ void rank_facts_kernel(const int64_t *st_rp, const int32_t *st_ent, c
     }
 }
 
+// Rank-row starts of an instance-grouped state: query q owns the instance
+// rows [q_inst[q], q_inst[q + 1]) and row (q, r) holds all their entries.
+// Slots count from the first query's first entry.
+__global__ void inst_slots_kernel(const int64_t *st_rp, const int64_t *q_inst, int64_t B, int64_t ranks,
+                                  int64_t *slot_base) {
+    const int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (row > B * ranks) return;
+    const int64_t q = row / ranks, r = row % ranks;
+    const int64_t base = st_rp[q_inst[q]];
+    const int64_t nq = q < B ? st_rp[q_inst[q + 1]] - base : 0;
+    slot_base[row] = ranks * (base - st_rp[q_inst[0]]) + r * nq;
+}
+
+// One block per rank row (q, r): the entries of the query's instance rows in
+// instance order, each with its instance's weight at rank r.
+__global__ void inst_facts_kernel(const int64_t *st_rp, const int32_t *st_ent, const int64_t *q_inst,
+                                  const float *w, int64_t ranks, const int64_t *slot_base, int32_t *fact_dst,
+                                  float *fact_val) {
+    const int64_t row = blockIdx.x;
+    const int64_t q = row / ranks, r = row % ranks;
+    const int64_t s = slot_base[row];  // relative to the first query's first entry
+    const int64_t c0 = q_inst[q], c1 = q_inst[q + 1];
+    const int64_t base = st_rp[c0];
+    for (int64_t c = c0; c < c1; ++c) {
+        const int64_t a = st_rp[c], b = st_rp[c + 1];
+        const float wv = w[c * ranks + r];
+        for (int64_t i = a + threadIdx.x; i < b; i += blockDim.x) {
+            fact_dst[s + (i - base)] = wv != 0.0f ? st_ent[i] : -1;
+            fact_val[s + (i - base)] = wv;
+        }
+    }
+}
+
+// Dense rank maxima of an instance-grouped Boolean state (query q owns the
+// instance rows [q_inst[q], q_inst[q + 1]), q < nq): one warp per instance
+// raises acc[(q * ranks + r) * E + entity] to the fp32 bits of the
+// instance's weight at rank r, for every entity the instance reaches.
+__global__ void inst_max_kernel(const int64_t *st_rp, const int32_t *st_ent, const int64_t *q_inst, int64_t nq,
+                                const float *w, int64_t ranks, int64_t E, unsigned int *acc) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    const int64_t c_end = q_inst[nq];
+    for (int64_t c = q_inst[0] + blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); c < c_end;
+         c += nw) {
+        int64_t lo = 0, hi = nq - 1;  // the last query whose first instance is at or before c
+        while (lo < hi) {
+            const int64_t mid = (lo + hi + 1) >> 1;
+            if (q_inst[mid] <= c) lo = mid; else hi = mid - 1;
+        }
+        unsigned int *aq = acc + lo * ranks * E;
+        const int64_t a = st_rp[c], b = st_rp[c + 1];
+        for (int64_t k = a + lane; k < b; k += 32) {
+            const int64_t e = st_ent[k];
+            for (int64_t r = 0; r < ranks; ++r) {
+                const unsigned int wb = __float_as_uint(w[c * ranks + r]);
+                if (wb != 0u) atomicMax(aq + r * E + e, wb);
+            }
+        }
+    }
+}
+
+// Boolean fixed-operator step into per-row bitmaps (the rows of a rule
+// state whose facts outnumber its bitmap's words): one warp per listed
+// entry sets the bit of every destination of its row's operator.
+__global__ void fixed_bitmap_kernel(const int64_t *entries, int64_t n, const int64_t *entry_row,
+                                    const int32_t *row_slot, const int32_t *ent, const int64_t *ops, int64_t R,
+                                    SideR ori, SideR inv, uint32_t *bitmap, int64_t words) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t k = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); k < n; k += nw) {
+        const int64_t i = entries[k];
+        const int64_t row = entry_row[i];
+        uint32_t *bm = bitmap + static_cast<int64_t>(row_slot[row]) * words;
+        const int64_t op = ops[row];
+        const int32_t src = ent[i];
+        if (op == 2 * R) {
+            if (lane == 0) atomicOr(bm + (src >> 5), 1u << (src & 31));
+            continue;
+        }
+        const bool inv_dir = op >= R;
+        const int rel = static_cast<int>(inv_dir ? op - R : op);
+        const SideR &sd = inv_dir ? inv : ori;
+        const int64_t g = find_group(sd, src, rel);
+        if (g < 0) continue;
+        const int64_t c = sd.gcount[g], p0 = sd.gstart[g];
+        for (int64_t t = lane; t < c; t += 32) {
+            const int32_t d = sd.col[p0 + t];
+            atomicOr(bm + (d >> 5), 1u << (d & 31));
+        }
+    }
+}
+
+// Set-bit counts of chunks of kBmChunk consecutive bitmap words, one block each.
+constexpr int kBmChunk = 256;
+__global__ void __launch_bounds__(kBmChunk) bitmap_count_kernel(const uint32_t *bm, int64_t *chunk_cnt) {
+    __shared__ int64_t scratch[kBmChunk / 32 + 1];
+    const int64_t c = blockIdx.x;
+    const uint32_t w = bm[c * kBmChunk + threadIdx.x];
+    int64_t tot;
+    block_exclusive_scan<int64_t>(__popc(w), scratch, &tot);
+    if (threadIdx.x == 0) chunk_cnt[c] = tot;
+}
+
+__global__ void bitmap_rowptr_kernel(const int64_t *chunk_off, int64_t nb, int64_t chunks_per_row, int64_t *row_ptr) {
+    const int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (r <= nb) row_ptr[r] = chunk_off[r * chunks_per_row];
+}
+
+// The set bits of every row in ascending order: entity = word-in-row * 32 + bit.
+__global__ void __launch_bounds__(kBmChunk) bitmap_emit_kernel(const uint32_t *bm, int64_t words,
+                                                               const int64_t *chunk_off, int32_t *ent) {
+    __shared__ int64_t scratch[kBmChunk / 32 + 1];
+    const int64_t c = blockIdx.x;
+    const int64_t wi = c * kBmChunk + threadIdx.x;
+    uint32_t x = bm[wi];
+    int64_t tot;
+    int64_t o = block_exclusive_scan<int64_t>(__popc(x), scratch, &tot) + chunk_off[c];
+    const int64_t base = (wi % words) * 32;
+    while (x) {
+        const int b = __ffs(x) - 1;
+        x &= x - 1;
+        ent[o++] = static_cast<int32_t>(base + b);
+    }
+}
+
 }  // namespace
+
+int rule_instance_max(const int64_t *st_rp, const int32_t *st_ent, const int64_t *q_inst, int64_t nq, const float *w,
+                      int64_t ranks, int64_t E, unsigned int *acc, cudaStream_t st) {
+    FL_REQUIRE(nq >= 0 && ranks > 0 && E > 0 && st_rp && q_inst && w && acc, "fl_rule_instance_max: bad arguments");
+    if (nq > 0) {
+        const int sms = fl_device_sm_count();
+        launch(inst_max_kernel, static_cast<unsigned>((sms > 0 ? sms : 148) * 8), 256, 0, st, st_rp, st_ent, q_inst,
+               nq, w, ranks, E, acc);
+    }
+    return check_launch("rule_instance_max");
+}
+
+size_t bitmap_rows_workspace(int64_t nb, int64_t words) {
+    const int64_t chunks = nb * (words / kBmChunk);
+    return carve_bytes<int64_t>(chunks + 1) + scan_workspace(chunks) + 1024;
+}
+
+int fixed_relation_bitmap(const int64_t *entries, int64_t n, const int64_t *entry_row, const int32_t *row_slot,
+                          const int32_t *ent, const int64_t *ops, int64_t R, const fl_csr_side &ori,
+                          const fl_csr_side &inv, uint32_t *bitmap, int64_t words, cudaStream_t st) {
+    FL_REQUIRE(n >= 0 && words > 0 && (n == 0 || (entries && entry_row && row_slot && ent && ops && bitmap)),
+               "fl_fixed_relation_bitmap: bad arguments");
+    if (n > 0) {
+        const int sms = fl_device_sm_count();
+        int64_t blocks = (n + 7) / 8;
+        const int64_t cap = static_cast<int64_t>(sms > 0 ? sms : 148) * 16;
+        if (blocks > cap) blocks = cap;
+        launch(fixed_bitmap_kernel, static_cast<unsigned>(blocks), 256, 0, st, entries, n, entry_row, row_slot, ent,
+               ops, R, make_side_r(ori), make_side_r(inv), bitmap, words);
+    }
+    return check_launch("fixed_relation_bitmap");
+}
+
+int bitmap_rows_count(const uint32_t *bitmap, int64_t nb, int64_t words, int64_t *chunk_off, int64_t *row_ptr,
+                      void *ws, size_t ws_bytes, cudaStream_t st) {
+    FL_REQUIRE(nb >= 0 && words > 0 && words % kBmChunk == 0 && chunk_off && row_ptr,
+               "fl_bitmap_rows_count: words must be a positive multiple of 256");
+    const int64_t chunks = nb * (words / kBmChunk);
+    FL_REQUIRE(chunks < (int64_t(1) << 31), "fl_bitmap_rows_count: too many bitmap words");
+    Carve c(ws, ws_bytes);
+    int64_t *cnt = c.take<int64_t>(chunks + 1);
+    const size_t sws = scan_workspace(chunks);
+    void *scan_ws = c.take<char>(sws);
+    FL_REQUIRE(cnt && scan_ws, "fl_bitmap_rows_count: workspace too small");
+    if (chunks > 0) launch(bitmap_count_kernel, static_cast<unsigned>(chunks), kBmChunk, 0, st, bitmap, cnt);
+    int rc = exclusive_scan<int64_t>(cnt, chunks, chunk_off, scan_ws, sws, st);
+    if (rc) return rc;
+    launch(bitmap_rowptr_kernel, static_cast<unsigned>((nb + 1 + 255) / 256), 256, 0, st, chunk_off, nb,
+           words / kBmChunk, row_ptr);
+    return check_launch("bitmap_rows_count");
+}
+
+int bitmap_rows_emit(const uint32_t *bitmap, int64_t nb, int64_t words, const int64_t *chunk_off, int32_t *ent,
+                     cudaStream_t st) {
+    FL_REQUIRE(nb >= 0 && words > 0 && words % kBmChunk == 0 && chunk_off, "fl_bitmap_rows_emit: bad arguments");
+    const int64_t chunks = nb * (words / kBmChunk);
+    if (chunks > 0) launch(bitmap_emit_kernel, static_cast<unsigned>(chunks), kBmChunk, 0, st, bitmap, words, chunk_off, ent);
+    return check_launch("bitmap_rows_emit");
+}
+
+int rule_instance_facts(const int64_t *st_rp, const int32_t *st_ent, const int64_t *q_inst, int64_t B,
+                        const float *w, int64_t ranks, int64_t *slot_base, int32_t *fact_dst, float *fact_val,
+                        cudaStream_t st) {
+    FL_REQUIRE(B >= 0 && ranks > 0 && st_rp && q_inst && slot_base && w, "fl_rule_instance_facts: bad arguments");
+    const int64_t rows = B * ranks;
+    launch(inst_slots_kernel, static_cast<unsigned>((rows + 1 + 255) / 256), 256, 0, st, st_rp, q_inst, B, ranks,
+           slot_base);
+    if (rows > 0)
+        launch(inst_facts_kernel, static_cast<unsigned>(rows), 256, 0, st, st_rp, st_ent, q_inst, w, ranks, slot_base,
+               fact_dst, fact_val);
+    return check_launch("rule_instance_facts");
+}
 
 int rule_rank_facts(const int64_t *st_rp, const int32_t *st_ent, const float *st_val, int64_t B, int64_t C,
                     const float *w, int64_t ranks, const int64_t *run_rp, const int32_t *run_ent, const float *run_val,

@@ -266,6 +266,28 @@ def _graph_topk(csr_args):
                      inv_order, ori_gp, ori_gr, ori_gs, ori_gc, inv_gp, inv_gr, inv_gs, inv_gc))
 
 
+_VISIBILITY = {}  # the last (graph, mask, mask version) -> CSR-ordered visibility bytes
+
+
+def _visibility(graph, mask_values):
+    """CSR-ordered visibility bytes (ops.csr_visibility) of a triple mask, for
+    the top-k hops without edge weights: a hop then reads one byte beside the
+    edge instead of mask[order[p]].  The model calls every hop of a step with
+    the same mask tensor, so the bytes are kept for the last (graph, mask) and
+    rebuilt when torch's version counter of the mask changes (an in-place
+    write such as mask[hide] = False).  Returns None for a mask that is not a
+    CUDA tensor with one entry per triple (the hop then reads the mask)."""
+    if (mask_values is None or not isinstance(mask_values, torch.Tensor) or not mask_values.is_cuda
+            or mask_values.numel() < graph.csr[1].numel()):
+        return None
+    hit = _VISIBILITY.get("last")
+    if (hit is not None and hit[0]() is graph and hit[1]() is mask_values and hit[2] == mask_values._version):
+        return hit[3]
+    vis = ops.csr_visibility(graph, mask_values)
+    _VISIBILITY["last"] = (weakref.ref(graph), weakref.ref(mask_values), mask_values._version, vis)
+    return vis
+
+
 def _graph_groups(ori_col, ori_gp, ori_gr, ori_gs, ori_gc, inv_col, inv_gp, inv_gr, inv_gs, inv_gc):
     """Graph view from group arrays only (the all-edges operator passes no row_ptr/order)."""
     dev = ori_col.device
@@ -356,9 +378,11 @@ class FlashLogFunctionSparse3DTopKSum(autograd.Function):
         _check_w(wf)
         seed = int(torch.randint(0, 2 ** 63 - 1, ()).item()) if sampling else -1
         learn_ew = weight is not None and bool(getattr(weight, "requires_grad", False))
+        vis = _visibility(graph, mask_values) if weight is None else None
         fw = ops.hop_forward(row_ptr, ent, val, wf, graph, r_size, int(topk_edges),
                              _topk_flags(weight, edge_weight_is_score, sampling, wot_i),
-                             mask_triple=mask_values, edge_weight=None if weight is None else weight.detach(),
+                             mask_triple=None if vis is not None else mask_values, vis=vis,
+                             edge_weight=None if weight is None else weight.detach(),
                              seed=seed, record_edge=learn_ew)
         _kernel_log("sparse3d_topk_sum.cuda_forward", t0)
         ctx.fw = fw
@@ -455,11 +479,13 @@ class _Sparse3DSumNormFused(autograd.Function):
                 _check_bad(bad)
             state = (row_ptr, ent, val)
             sel_status = torch.zeros(1, dtype=torch.int32, device=val.device)
+            vis = _visibility(graph, mask_values) if weight is None else None
             for full in (False, True):
                 row_ptr, ent, val = _select_sources_async(ctx, *state, topk_nodes, B * L_, sel_status, full)
                 try:
                     fw = ops.hop_forward(row_ptr, ent, val, wf, graph, r_size, int(topk_edges),
-                                         _topk_flags(weight, False, sampling, wot_i), mask_triple=mask_values,
+                                         _topk_flags(weight, False, sampling, wot_i),
+                                         mask_triple=None if vis is not None else mask_values, vis=vis,
                                          edge_weight=None if weight is None else weight.detach(), seed=-1,
                                          eps=eps, check_w=True, sel_status=None if full else sel_status)
                     break

@@ -349,7 +349,9 @@ int fl_value_dropout(const float *x, float *y, int64_t n, const int64_t *live, d
  * holds a forward relation, inverse relation + R, or identity 2R.  Replaces
  * flashlog_forward_sparse3d_fixed_relation_cuda (flashlog.cu:1677-1741); the
  * facts are then reduced by fl_row_reduce.  plan: *total (host) receives the
- * number of facts (syncs). */
+ * number of facts (syncs).  l may be NULL (every entry in column 0, as for a
+ * state whose rows are rule instances with ops i64[B, 1]); val may be NULL
+ * (every value 1, a Boolean state). */
 size_t fl_fixed_relation_workspace(int64_t nnz);
 int fl_fixed_relation_plan(const int64_t *b, const int64_t *l, const int32_t *ent, int64_t nnz, const int64_t *ops,
                            int64_t Lr, int64_t r_size, fl_csr_side ori, fl_csr_side inv, int64_t *slot_base,
@@ -367,7 +369,8 @@ int fl_fixed_relation_fill(const int64_t *b, const int64_t *l, const int32_t *en
  * positive value raises acc[rank * B * E + q * E + entity] to the fp32 bit
  * pattern of weights[c * ranks + rank].  acc (u32, caller zeroed) then holds,
  * as fp32, the largest rank weight of the rules reaching each entity.
- * weights must be finite and nonnegative.  Order-independent and exact. */
+ * weights must be finite and nonnegative.  Order-independent and exact.
+ * val may be NULL (a Boolean state: every entry counts). */
 int fl_rule_max_reduce(const int64_t *row_ptr, int64_t rows, const int32_t *ent, const float *val, int64_t C,
                        const float *weights, int64_t ranks, int64_t B, int64_t E, uint32_t *acc, fl_stream_t stream);
 
@@ -386,6 +389,50 @@ int fl_rule_rank_facts(const int64_t *st_rp, const int32_t *st_ent, const float 
                        const float *w, int64_t ranks, const int64_t *run_rp, const int32_t *run_ent,
                        const float *run_val, int64_t *slot_base, int32_t *fact_dst, float *fact_val,
                        fl_stream_t stream);
+
+/* The rank-row facts of a state whose rows are rule instances (one query's
+ * instances contiguous: query q owns rows [q_inst[q], q_inst[q + 1]),
+ * q_inst i64[B + 1]; rows st_rp[rows + 1], entities st_ent): row (q, r)
+ * holds every entry of the query's instance rows in instance order with the
+ * instance's weight w[instance * ranks + r] as value (destination -1 where
+ * the weight is 0).  slot_base i64[B*ranks+1] gets ranks * (st_rp[q_inst[q]]
+ * - st_rp[q_inst[0]]) + r * (entries of query q), so a range of queries
+ * (q_inst offset to its first query) has facts from slot 0; fact_dst /
+ * fact_val the facts, for
+ * fl_row_reduce_max (FL_MAX_VALUE_ONLY).  The routed evaluation of
+ * rules/evaluate.py:1015-1095, where every query has the rules of its own
+ * relation, as one state over many queries. */
+int fl_rule_instance_facts(const int64_t *st_rp, const int32_t *st_ent, const int64_t *q_inst, int64_t B,
+                           const float *w, int64_t ranks, int64_t *slot_base, int32_t *fact_dst, float *fact_val,
+                           fl_stream_t stream);
+
+/* The same rank maxima as fl_rule_instance_facts + fl_row_reduce_max, into a
+ * dense accumulator for queries that reach a large share of the entities:
+ * acc u32[nq * ranks * E] (caller zeroed) gets at (q * ranks + r) * E + e
+ * the largest fp32 bit pattern of w[instance * ranks + r] over the instances
+ * of query q (rows q_inst[q] .. q_inst[q + 1] - 1, q < nq) whose row holds e.
+ * Weights must be finite and nonnegative; order-independent and exact. */
+int fl_rule_instance_max(const int64_t *st_rp, const int32_t *st_ent, const int64_t *q_inst, int64_t nq,
+                         const float *w, int64_t ranks, int64_t E, uint32_t *acc, fl_stream_t stream);
+
+/* Boolean fixed-operator step into per-row bitmaps, for the rows of a rule
+ * state with more facts than their bitmap has words: every listed entry
+ * entries[k] (k < n) of row entry_row[entries[k]] sets, in the bitmap of slot
+ * row_slot[row] (words u32 words each, caller zeroed), the bit of every
+ * destination of the row's operator ops[row] (identity 2R: the entity
+ * itself).  The rows' next states are then read out in entity order by
+ * fl_bitmap_rows_count (row_ptr i64[nb+1]; chunk_off i64[nb*words/256+1]
+ * kept for the emit) and fl_bitmap_rows_emit (ent i32[row_ptr[nb]]).  words
+ * must be a multiple of 256.  The set semantics are the Boolean projection
+ * after every rule step of rules/shared_inference.py:123-126. */
+int fl_fixed_relation_bitmap(const int64_t *entries, int64_t n, const int64_t *entry_row, const int32_t *row_slot,
+                             const int32_t *ent, const int64_t *ops, int64_t r_size, fl_csr_side ori,
+                             fl_csr_side inv, uint32_t *bitmap, int64_t words, fl_stream_t stream);
+size_t fl_bitmap_rows_workspace(int64_t nb, int64_t words);
+int fl_bitmap_rows_count(const uint32_t *bitmap, int64_t nb, int64_t words, int64_t *chunk_off, int64_t *row_ptr,
+                         void *ws, size_t ws_bytes, fl_stream_t stream);
+int fl_bitmap_rows_emit(const uint32_t *bitmap, int64_t nb, int64_t words, const int64_t *chunk_off, int32_t *ent,
+                        fl_stream_t stream);
 
 size_t fl_filtered_ranks_workspace(int64_t B);
 int fl_filtered_ranks(const int64_t *idx_b, const int64_t *idx_e, const float *values, int64_t nnz,

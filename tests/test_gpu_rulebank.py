@@ -7,10 +7,12 @@
 * First-operator pruning (rules/shared_inference.py:34-47) drops rules that
   cannot ground and changes no score.
 * evaluate_rule_bank (queries routed to the rules of their relation,
-  compacted per (head, body), scored and ranked with filtered tie-averaged
-  ranks) against the oracle's restatement run query group by query group:
-  ranks equal, on a seeded 4,000-rule bank over config-2 test queries, for
-  smDRUM (sum over ranks) and mmDRUM (max over ranks).
+  compacted per (head, body), grounded as batches of (query, rule)
+  instances, scored and ranked with filtered tie-averaged ranks) against the
+  oracle's restatement run query group by query group: ranks equal, on a
+  seeded 4,000-rule bank over config-2 test queries, for smDRUM (sum over
+  ranks) and mmDRUM (max over ranks), with steps and scores in one range and
+  split into many.
 Values are compared at rel 1e-5, keys and ranks exactly.
 """
 import numpy as np
@@ -109,8 +111,15 @@ def oracle_routed_ranks(src, rel, dst, rules, csr_np, R, E, final_max, sparse=Fa
 
 
 @pytest.mark.parametrize("final_max", [False, True])
-@pytest.mark.parametrize("budget", [0, 4 << 30])
-def test_routed_evaluation_matches_oracle(final_max, budget):
+@pytest.mark.parametrize("mode", ["sorted", "split", "dense", "auto"])
+def test_routed_evaluation_matches_oracle(final_max, mode):
+    """mode: "sorted" reduces every step by the row reduction and every
+    query's maxima by rank facts; "split" does the same in budgets of 4000
+    facts (many ranges of instances and of queries); "dense" takes every
+    step through entity bitmaps and every query through the dense
+    accumulator; "auto" chooses per instance and per query."""
+    budget = 4000 if mode == "split" else 1 << 29
+    big = {"sorted": 1 << 62, "split": 1 << 62, "dense": 0, "auto": None}[mode]
     if not torch.cuda.is_available():
         pytest.skip("needs a CUDA device")
     import flashlog_b200.flashlog_kernel as fk
@@ -124,8 +133,17 @@ def test_routed_evaluation_matches_oracle(final_max, budget):
     csr_np = O.build_csr(train[:, 0], train[:, 2], train[:, 1], E)
     src, rel, dst = evaluation_queries(test, R, 150)
     rules = rule_bank(train, rel, R, 4000)
+    stats = {}
     got = RB.evaluate_rule_bank(_cuda(src), _cuda(rel), _cuda(dst), rules, csr, R, E, final_max=final_max,
-                                chunk_size=16, query_batch=32, accumulator_bytes=budget).cpu().numpy()
+                                query_batch=32, fact_budget=budget, stats=stats, bitmap_min_facts=big,
+                                dense_min_entries=big).cpu().numpy()
     want = oracle_routed_ranks(src, rel, dst, rules, csr_np, R, E, final_max)
     assert np.array_equal(got, want)
+    assert stats["batches"] >= src.size // 32
+    if mode == "split":
+        assert stats["step_ranges"] > stats["batches"] * 3 and stats["score_ranges"] > stats["batches"]
+    if mode in ("sorted", "split"):
+        assert stats.get("bitmap_rows", 0) == 0 and stats["dense_queries"] == 0
+    if mode == "dense":
+        assert stats["bitmap_rows"] > 0 and stats["dense_queries"] > 0
     assert (want < 0.5 * E).sum() > 10  # some targets are reached by rules

@@ -169,3 +169,27 @@ def test_default_zero_slack_covers_rows_kept_whole():
         assert kept.sum() <= rows * c1 * slack, p
     C, S, F, U = capacities(8, 2, 10, 3, 100, 50, zero_slack=math.inf)
     assert S == C
+
+
+def test_routed_instances_cover_every_query_with_its_relations_rules():
+    """Host side of evaluate_rule_bank: batches in relation order, within
+    both budgets, every query once, with exactly the rules of its relation."""
+    from flashlog_b200.rules import route_instances
+    rng = np.random.default_rng(3)
+    heads = np.sort(rng.integers(0, 12, 200))
+    rel = rng.integers(0, 14, 500)  # relations 12, 13 have no rules
+    seen = []
+    for budget, qb in ((1 << 20, 4096), (50, 7), (1, 3)):
+        seen = []
+        last_rel = -1
+        for bq, q_inst, inst_rule in route_instances(rel, heads, qb, budget):
+            assert 1 <= bq.size <= qb
+            assert q_inst[0] == 0 and q_inst[-1] == inst_rule.size
+            assert bq.size == 1 or q_inst[-1] <= budget
+            assert rel[bq[0]] >= last_rel and np.all(np.diff(rel[bq]) >= 0)
+            last_rel = rel[bq[-1]]
+            for k, q in enumerate(bq):
+                mine = inst_rule[q_inst[k]:q_inst[k + 1]]
+                assert np.array_equal(mine, np.flatnonzero(heads == rel[q]))
+            seen.extend(bq.tolist())
+        assert sorted(seen) == list(range(rel.size))
