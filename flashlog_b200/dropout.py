@@ -80,7 +80,6 @@ def sparse_dropout(s: torch.Tensor, p: float, training: bool = True, seed: int |
     if s.dim() != 3:
         raise ValueError("sparse_dropout takes a [B, L, E] state")
     seed = draw_seed() if seed is None else seed
-    out = SparseValueDropout.apply(s, p, seed, device_counter(counter, s.device), subseq)
-    if _fk._is_own_output(s):
-        _fk._mark_own_output(out)  # the same indices, written by the library: the next hop trusts them
-    return out
+    # the output shares the input's index tensor, so a hop that returned the
+    # input also recognizes the output as its own (flashlog_kernel._own_rows)
+    return SparseValueDropout.apply(s, p, seed, device_counter(counter, s.device), subseq)

@@ -315,26 +315,31 @@ def _check_w(w):
                            "aborting before edge count/fill to prevent uninitialized indices")
 
 
-# Sparse states returned by the fused operator, keyed by the address of
-# their index storage (with the object kept weakly): their indices were
-# written by the library, in range and coalesced, so the next hop skips the
-# host read of the index check.
-_OWN_OUTPUTS = {}
+# The row layouts of the last states the fused operator returned, keyed by
+# their index tensor: a state on one of these index tensors (the output
+# itself, or a state built on its indices, as the models' value dropout
+# does) skips the host read of the index check (its indices were written by
+# the library, in range and coalesced) and the COO -> row conversion.  Each
+# entry holds its index tensor, so the storage cannot be reused while it is
+# listed; torch's version counter catches an in-place write to the indices.
+_OWN_ROWS = []  # (indices, version, row_ptr, ent), newest last
+_OWN_ROWS_KEEP = 2
 
 
-def _mark_own_output(t):
+def _mark_own_output(t, row_ptr, ent):
     idx = t._indices()
-    key = (idx.data_ptr(), tuple(idx.shape))
-    _OWN_OUTPUTS[key] = weakref.ref(t)
-    if len(_OWN_OUTPUTS) > 64:  # drop entries whose tensor is gone
-        for k in [k for k, r in _OWN_OUTPUTS.items() if r() is None]:
-            del _OWN_OUTPUTS[k]
+    _OWN_ROWS.append((idx, idx._version, row_ptr, ent))
+    del _OWN_ROWS[:-_OWN_ROWS_KEEP]
 
 
-def _is_own_output(t):
+def _own_rows(t):
+    """(row_ptr, ent) of a state on the indices of a recent output, else None."""
     idx = t._indices()
-    r = _OWN_OUTPUTS.get((idx.data_ptr(), tuple(idx.shape)))
-    return r is not None and r() is t
+    for i, v, rp, e in reversed(_OWN_ROWS):
+        if (i.data_ptr() == idx.data_ptr() and i.shape == idx.shape and i.stride() == idx.stride()
+                and i._version == v):
+            return rp, e
+    return None
 
 
 def _check_bad_and_w(bad, w):
@@ -461,14 +466,21 @@ class _Sparse3DSumNormFused(autograd.Function):
 
     @staticmethod
     def forward(ctx, sp_value, w, sp_batch, sp_level, sp_entity, csr, mask_values, weight, B, L_, E, r_size, wot_i,
-                topk_edges, topk_nodes, sampling, all_edges, masks_csr, eps, trusted=False):
+                topk_edges, topk_nodes, sampling, all_edges, masks_csr, eps, own_rows=None):
         _cuda_or_raise(sp_value)
         val = sp_value.detach().to(torch.float32).contiguous()
         graph = Graph.of(csr)
-        row_ptr, ent, bad = _rows(sp_batch, sp_level, sp_entity, B, L_, E, graph)
+        trusted = own_rows is not None
+        if trusted:
+            if graph.E < E:
+                raise ValueError(f"the CSR covers {graph.E} entities but the state has {E}")
+            (row_ptr, ent), bad = own_rows, None
+        else:
+            row_ptr, ent, bad = _rows(sp_batch, sp_level, sp_entity, B, L_, E, graph)
         wf = w.detach().to(torch.float32).contiguous()
         if all_edges:
-            _check_bad(bad)
+            if not trusted:
+                _check_bad(bad)
             ctx.pruned = None
             fw = ops.hop_forward(row_ptr, ent, val, wf, graph, r_size, L.NO_BUDGET, L.FL_WOT_I if wot_i else 0,
                                  mask_csr=masks_csr, eps=eps)
@@ -492,7 +504,8 @@ class _Sparse3DSumNormFused(autograd.Function):
                 except ops.SelectionOverflow:
                     continue  # explicit zeros past rows * c1: select again at the input's size
         else:
-            _check_bad(bad)
+            if not trusted:
+                _check_bad(bad)
             row_ptr, ent, val = _select_sources(ctx, row_ptr, ent, val, topk_nodes, sampling)
             _check_w(wf)
             seed = int(torch.randint(0, 2 ** 63 - 1, ()).item()) if sampling else -1
@@ -504,6 +517,7 @@ class _Sparse3DSumNormFused(autograd.Function):
         ctx.B, ctx.L, ctx.E = B, L_, E
         out = _coo(fw.out_row_ptr, fw.out_ent, fw.out_y, B, L_, E)
         ctx.out_indices = out.indices()
+        _mark_own_output(out, fw.out_row_ptr, fw.out_ent)
         return out
 
     @staticmethod
@@ -608,12 +622,11 @@ def vectorized_operation_sparse3d_csr_sum_norm(sp_state, w, csr_struct, mask_val
     if all_edges:
         prepared = _prepared_mask_pair(prepared_masks) if prepared_masks is not None else _prepared_mask_pair(mask_values)
         masks_csr = prepared if prepared is not None else prepare_csr_masks(csr_struct, mask_values, weight)
-    # a state this operator returned has valid, coalesced indices by construction
-    trusted = _is_own_output(sp_state)
+    # a state on the indices this operator returned: valid, coalesced, and in the row layout already
+    own = _own_rows(sp_state)
     out = _Sparse3DSumNormFused.apply(sp_state.values(), w, idx[0], idx[1], idx[2], _csr_parts(csr_struct),
                                       mask_values, weight, B, L_, E, r_size, wot_i, eff, nodes, sampled,
-                                      all_edges, masks_csr, eps, trusted)
-    _mark_own_output(out)
+                                      all_edges, masks_csr, eps, own)
     return out
 
 

@@ -224,6 +224,12 @@ def _reduce_rows(row_ptr, rows: int, E: int, slot_base, entry_count, fact_dst, f
     return out_row_ptr, out_ent[:int(out_row_ptr[rows].item())]
 
 
+# Facts above which a row always goes through a bitmap: the row reduction
+# runs one CTA per row and re-reads a row once per 12,288-fact chunk, so rows
+# far above a chunk are cheaper as bitmaps even when E is large.
+_BITMAP_ROW_FACTS = 1 << 16
+
+
 def _bitmap_words(E: int) -> int:
     """u32 words of one entity bitmap, rounded up to the 256-word chunks of fl_bitmap_rows_*."""
     return ((E + 31) // 32 + 255) // 256 * 256
@@ -348,7 +354,8 @@ def _fixed_step_rows(row_ptr, ent, ops_col, graph, relations: int, E: int, fact_
     instances: row i moves along operator ops_col[i] (flashlog.cu:1561-1741),
     and every reached entity is kept once (the step's Boolean projection,
     rules/shared_inference.py:123-126).  A row with more facts than
-    bitmap_min_facts (default: twice its entity bitmap's words) is reduced
+    bitmap_min_facts (default: twice its entity bitmap's words, at most
+    65,536) is reduced
     through the bitmap (fl_fixed_relation_bitmap); the others through the row
     reduction, over ranges of rows of at most
     fact_budget facts (or a single row).  stats counts the ranges
@@ -364,7 +371,7 @@ def _fixed_step_rows(row_ptr, ent, ops_col, graph, relations: int, E: int, fact_
     ops_col = ops_col.to(torch.int64).contiguous()
     plan = _plan_step(ent, b, ops_col, graph, relations)
     row_facts = plan[0][row_ptr[1:]] - plan[0][row_ptr[:-1]]
-    limit = 2 * _bitmap_words(E) if bitmap_min_facts is None else bitmap_min_facts
+    limit = min(2 * _bitmap_words(E), _BITMAP_ROW_FACTS) if bitmap_min_facts is None else bitmap_min_facts
     big = torch.nonzero(row_facts > limit).flatten().cpu().numpy()
     if big.size == 0:
         return _sorted_step(row_ptr, ent, b, ops_col, graph, relations, E, fact_budget, stats, plan)
@@ -521,7 +528,8 @@ def evaluate_rule_bank(sources, query_relations, targets, rules, csr_struct, rel
     operator per step for all instances at once, so the number of launches
     and host reads grows with the batches, not with the rules or the
     relations.  Instances whose step has many facts are reduced through entity
-    bitmaps (more than bitmap_min_facts, default twice the bitmap's words),
+    bitmaps (more than bitmap_min_facts, default twice the bitmap's words or
+    65,536, whichever is smaller),
     the others through the row reduction; a step with more than fact_budget
     facts runs over ranges of instances, which is the reference's per-source split
     (rules/shared_inference.py:60-76); an instance whose first operator has no
