@@ -8,6 +8,7 @@ not a fallback).
 """
 from __future__ import annotations
 
+import dataclasses
 import os
 import time
 
@@ -456,6 +457,53 @@ class FlashLogFunctionSparse3DAllEdgesSum(autograd.Function):
         return grads[:len(ctx.needs_input_grad)]
 
 
+# Fact counts of recent hops, by (graph, rows, input size class, c2, c1,
+# flags): a hop like one seen before sizes its fact buffers from that count
+# (with headroom) and skips the host read of the exact count.
+_FACTS_SEEN = {}
+
+
+def _remember_facts(key, n):
+    if len(_FACTS_SEEN) > 256:
+        _FACTS_SEEN.clear()
+    _FACTS_SEEN[key] = max(int(n), 1)
+
+
+def _speculative_hop(ctx, key, state, wf, graph, r_size, topk_edges, flags, topk_nodes, rows, hop_args):
+    """The hop with fact buffers of 1.5x the count of the last hop with the
+    same key and no host read before the launches: the output count, the
+    buffers' overflow status, the c1 selection's status and the weights'
+    finiteness come back in one read after the reduction.  Returns
+    (fw, selected state), or None when there is no count to go by or a
+    buffer ran short (the caller then sizes the buffers exactly).  Non-finite
+    weights raise the top-k operators' RuntimeError."""
+    seen = _FACTS_SEEN.get(key)
+    if seen is None:
+        return None
+    dev = wf.device
+    sel_status = torch.zeros(1, dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    sel = _select_sources_async(ctx, *state, topk_nodes, rows, sel_status, False)
+    finite = torch.isfinite(wf)
+    nonfinite = (~finite).any()
+    # the kernels run before the finiteness is read, so they get the weights
+    # with non-finite entries zeroed; such a call raises below and its outputs are dropped
+    fw = ops.hop_forward(*sel, torch.where(finite, wf, torch.zeros_like(wf)), graph, r_size, topk_edges, flags,
+                         slot_capacity=seen * 3 // 2 + 1024, status=status, out_sync=False, **hop_args)
+    got = torch.stack([fw.out_row_ptr[rows], fw.slot_base[sel[1].numel()], status[0].to(torch.int64),
+                       sel_status[0].to(torch.int64), nonfinite.to(torch.int64)]).cpu().tolist()
+    if got[4]:
+        raise RuntimeError("FlashLog sparse top-k received non-finite attention weights; "
+                           "aborting before edge count/fill to prevent uninitialized indices")
+    if (got[2] | got[3]) & L.FL_STATUS_SLOT_OVERFLOW:
+        return None
+    _remember_facts(key, got[1])
+    u = got[0]
+    fw = dataclasses.replace(fw, out_ent=fw.out_ent[:u], out_x=fw.out_x[:u], out_y=fw.out_y[:u],
+                             n_facts_slots=got[1])
+    return fw, sel
+
+
 class _Sparse3DSumNormFused(autograd.Function):
     """c1 + expansion + coalesce-sum + row normalization as one node.
 
@@ -492,17 +540,24 @@ class _Sparse3DSumNormFused(autograd.Function):
             state = (row_ptr, ent, val)
             sel_status = torch.zeros(1, dtype=torch.int32, device=val.device)
             vis = _visibility(graph, mask_values) if weight is None else None
-            for full in (False, True):
-                row_ptr, ent, val = _select_sources_async(ctx, *state, topk_nodes, B * L_, sel_status, full)
-                try:
-                    fw = ops.hop_forward(row_ptr, ent, val, wf, graph, r_size, int(topk_edges),
-                                         _topk_flags(weight, False, sampling, wot_i),
-                                         mask_triple=None if vis is not None else mask_values, vis=vis,
-                                         edge_weight=None if weight is None else weight.detach(), seed=-1,
-                                         eps=eps, check_w=True, sel_status=None if full else sel_status)
-                    break
-                except ops.SelectionOverflow:
-                    continue  # explicit zeros past rows * c1: select again at the input's size
+            hop_args = dict(mask_triple=None if vis is not None else mask_values, vis=vis,
+                            edge_weight=None if weight is None else weight.detach(), seed=-1, eps=eps)
+            flags = _topk_flags(weight, False, sampling, wot_i)
+            key = (id(graph), B * L_, int(ent.numel()).bit_length(), int(topk_edges), topk_nodes, flags)
+            fw = _speculative_hop(ctx, key, state, wf, graph, r_size, int(topk_edges), flags, topk_nodes, B * L_,
+                                  hop_args)
+            if fw is not None:
+                fw, (row_ptr, ent, val) = fw
+            else:
+                for full in (False, True):
+                    row_ptr, ent, val = _select_sources_async(ctx, *state, topk_nodes, B * L_, sel_status, full)
+                    try:
+                        fw = ops.hop_forward(row_ptr, ent, val, wf, graph, r_size, int(topk_edges), flags,
+                                             check_w=True, sel_status=None if full else sel_status, **hop_args)
+                        break
+                    except ops.SelectionOverflow:
+                        continue  # explicit zeros past rows * c1: select again at the input's size
+                _remember_facts(key, fw.n_facts_slots)
         else:
             if not trusted:
                 _check_bad(bad)
