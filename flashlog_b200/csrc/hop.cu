@@ -1109,7 +1109,6 @@ struct ReduceSmem {
     uint16_t mb_n[kTileK / (kRankBinMax + 1) + 1];
     int32_t mb_pair[kTileK / (kRankBinMax + 1) + 2];
     int mb_count, mb_mmax;
-    int next_win;  // emission: the next window to hand out
 };
 static_assert(kTileK / (kRankBinMax + 1) + 1 < kRThreads, "listed bins are scanned one per thread");
 static_assert(sizeof(ReduceSmem) <= 227 * 1024, "row reduction shared memory exceeds one CTA's budget");
@@ -1758,7 +1757,6 @@ __device__ float bucket_row(const ReduceArgs &a, ReduceSmem &sm, int64_t s0, int
         const int64_t wbase = *written;
         const int nwin = (C + 31) >> 5;
         auto dst_at = [&](int i) { return static_cast<uint32_t>(t.key[t.inv[i]] >> 32); };
-        if (threadIdx.x == 0) sm.next_win = kRWarps;
         for (int w = warp; w < nwin; w += kRWarps) {
             const int i = w * 32 + lane;
             const uint32_t d = i < C ? dst_at(i) : 0xffffffffu;
@@ -1775,9 +1773,7 @@ __device__ float bucket_row(const ReduceArgs &a, ReduceSmem &sm, int64_t s0, int
             if (threadIdx.x < nwin) sm.win[threadIdx.x] = static_cast<int32_t>(wex);
             __syncthreads();
         }
-        // windows handed out one at a time: a warp held up by a long run
-        // (a hub destination summed by its head lane) leaves the rest to others
-        for (int w = warp; w < nwin;) {
+        for (int w = warp; w < nwin; w += kRWarps) {
             const int i = w * 32 + lane;
             const bool has = i < C;
             int p = 0;
@@ -1840,9 +1836,6 @@ __device__ float bucket_row(const ReduceArgs &a, ReduceSmem &sm, int64_t s0, int
                 local += x;
             }
             if (has && !a.max_mode && a.fact_pos) a.fact_pos[s0 + static_cast<uint32_t>(k)] = static_cast<int32_t>(o);
-            int nxt = 0;
-            if (lane == 0) nxt = atomicAdd(&sm.next_win, 1);
-            w = __shfl_sync(kFull, nxt, 0);
         }
         *written = wbase + tot;
         __syncthreads();
