@@ -224,6 +224,10 @@ def _reduce_rows(row_ptr, rows: int, E: int, slot_base, entry_count, fact_dst, f
     return out_row_ptr, out_ent[:int(out_row_ptr[rows].item())]
 
 
+# Entries above which a query's maxima always go through the dense
+# accumulator: the sparse path ends in one row-reduction CTA per query.
+_DENSE_QUERY_ENTRIES = 1 << 16
+
 # Facts above which a row always goes through a bitmap: the row reduction
 # runs one CTA per row and re-reads a row once per 12,288-fact chunk, so rows
 # far above a chunk are cheaper as bitmaps even when E is large.
@@ -406,18 +410,19 @@ def _instance_scores(row_ptr, ent, q_inst, w_inst, ranks: int, E: int, final_max
     owns the instance rows [q_inst[q], q_inst[q + 1])): per rank r the largest
     weight of the instances reaching each entity, then _combine_ranks.  A
     query whose instances hold more than dense_min_entries entries (default
-    E / 8) starts a run that accumulates, with the queries after it (as many
-    as dense_bytes holds), in dense [ranks, E] buffers
-    (fl_rule_instance_max); the other runs go through rank facts and the
-    exact MAX row reduction, with at most fact_budget facts each (a single
-    query above it runs alone).  Both give the same rank rows.  stats counts the runs
+    E / 8 or 65,536, whichever is smaller) starts a run that accumulates, with
+    the queries after it (as many as dense_bytes holds), in dense [ranks, E]
+    buffers (fl_rule_instance_max), normalized in the rank-row layout and
+    combined densely; the other runs go through rank facts and the exact MAX
+    row reduction, with at most fact_budget facts each (a single query above
+    it runs alone).  Both give the same scores, bit for bit.  stats counts the runs
     ("score_ranges", "dense_queries").  Returns the row layout over the
     queries."""
     dev = ent.device
     Bq = q_inst.numel() - 1
     before = row_ptr[q_inst].cpu().numpy().astype(np.int64)  # entries before each query
     entries = np.diff(before)
-    dense = entries > (E // 8 if dense_min_entries is None else dense_min_entries)
+    dense = entries > (min(E // 8, _DENSE_QUERY_ENTRIES) if dense_min_entries is None else dense_min_entries)
     per_dense = max(1, dense_bytes // (4 * ranks * E))
     runs, qa = [], 0
     while qa < Bq:
@@ -445,9 +450,31 @@ def _instance_scores(row_ptr, ent, q_inst, w_inst, ranks: int, E: int, final_max
             row, r_ent = nz[:, 0], nz[:, 1]
             rp = torch.zeros(nq * ranks + 1, dtype=torch.int64, device=dev)
             torch.cumsum(torch.bincount(row, minlength=nq * ranks), 0, out=rp[1:])
-            x = acc.view(torch.float32).view(nq * ranks, E)[row, r_ent].contiguous()
-            r_ent = r_ent.to(torch.int32)
-            del acc
+            dense = acc.view(torch.float32).view(nq * ranks, E)
+            x = dense[row, r_ent].contiguous()
+            # normalized in the rank-row layout (the same sums as the sparse
+            # path), then combined densely: absent entries are +0.0, which
+            # leaves the rank-order sum and the max of the present ones exact
+            y, _ = ops.normalize_forward(rp, x, eps=1e-30)
+            dense[row, r_ent] = y
+            dense = dense.view(nq, ranks, E)
+            if final_max:
+                comb = dense.amax(1)
+            else:
+                comb = dense[:, 0].clone()
+                for r in range(1, ranks):
+                    comb += dense[:, r]
+            del acc, dense
+            nz = torch.nonzero(comb)
+            s_rp = torch.zeros(nq + 1, dtype=torch.int64, device=dev)
+            torch.cumsum(torch.bincount(nz[:, 0], minlength=nq), 0, out=s_rp[1:])
+            s_ent, s_x = nz[:, 1].to(torch.int32), comb[nz[:, 0], nz[:, 1]].contiguous()
+            del comb, nz
+            out_rp.append(s_rp[:-1] + offset)
+            out_ent.append(s_ent)
+            out_x.append(s_x)
+            offset += s_ent.numel()
+            continue
         else:
             T = int(ranks * (before[qb] - before[qa]))
             slot_base = torch.empty(nq * ranks + 1, dtype=torch.int64, device=dev)
@@ -536,7 +563,8 @@ def evaluate_rule_bank(sources, query_relations, targets, rules, csr_struct, rel
     edge at its source ends empty in the first step, as the reference's
     first-operator pruning (rules/shared_inference.py:34-47) drops it.  A
     query's rank maxima accumulate in a dense [ranks, E] buffer when its
-    instances hold more than dense_min_entries entries (default E / 8), else
+    instances hold more than dense_min_entries entries (default E / 8 or
+    65,536, whichever is smaller), else
     sparsely through the MAX row reduction (no [ranks, queries, E] buffer);
     both give the same scores.  Ranks come
     from fl_filtered_ranks against filter_keys (sorted keys q * E + e of known
