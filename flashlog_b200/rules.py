@@ -416,8 +416,8 @@ def _instance_scores(row_ptr, ent, q_inst, w_inst, ranks: int, E: int, final_max
     combined densely; the other runs go through rank facts and the exact MAX
     row reduction, with at most fact_budget facts each (a single query above
     it runs alone).  Both give the same scores, bit for bit.  stats counts the runs
-    ("score_ranges", "dense_queries").  Returns the row layout over the
-    queries."""
+    ("score_ranges", "dense_queries").  Yields, run by run, (qa, qb, row
+    layout over the queries qa..qb-1 of the state)."""
     dev = ent.device
     Bq = q_inst.numel() - 1
     before = row_ptr[q_inst].cpu().numpy().astype(np.int64)  # entries before each query
@@ -439,7 +439,6 @@ def _instance_scores(row_ptr, ent, q_inst, w_inst, ranks: int, E: int, final_max
         qa = qb
     stats["score_ranges"] = stats.get("score_ranges", 0) + len(runs)
     stats["dense_queries"] = stats.get("dense_queries", 0) + sum(qb - qa for qa, qb, d in runs if d)
-    out_rp, out_ent, out_x, offset = [], [], [], 0
     for qa, qb, is_dense in runs:
         nq = qb - qa
         if is_dense:
@@ -470,10 +469,7 @@ def _instance_scores(row_ptr, ent, q_inst, w_inst, ranks: int, E: int, final_max
             torch.cumsum(torch.bincount(nz[:, 0], minlength=nq), 0, out=s_rp[1:])
             s_ent, s_x = nz[:, 1].to(torch.int32), comb[nz[:, 0], nz[:, 1]].contiguous()
             del comb, nz
-            out_rp.append(s_rp[:-1] + offset)
-            out_ent.append(s_ent)
-            out_x.append(s_x)
-            offset += s_ent.numel()
+            yield qa, qb, (s_rp, s_ent, s_x)
             continue
         else:
             T = int(ranks * (before[qb] - before[qa]))
@@ -484,13 +480,7 @@ def _instance_scores(row_ptr, ent, q_inst, w_inst, ranks: int, E: int, final_max
                                                _p(slot_base), _p(fact_dst), _p(fact_val), _stream()),
                   "rule_instance_facts")
             rp, r_ent, x = ops.row_max(slot_base, fact_dst, fact_val, nq * ranks, E)
-        s_rp, s_ent, s_x = _combine_ranks(rp, r_ent, x, nq, ranks, E, final_max)
-        out_rp.append(s_rp[:-1] + offset)
-        out_ent.append(s_ent)
-        out_x.append(s_x)
-        offset += s_ent.numel()
-    out_rp.append(torch.tensor([offset], dtype=torch.int64, device=dev))
-    return torch.cat(out_rp), torch.cat(out_ent), torch.cat(out_x)
+        yield qa, qb, _combine_ranks(rp, r_ent, x, nq, ranks, E, final_max)
 
 
 class _PhaseClock:
@@ -598,31 +588,40 @@ def evaluate_rule_bank(sources, query_relations, targets, rules, csr_struct, rel
         tgt = targets[idx]
         counts = np.diff(q_inst_h)
         I = int(q_inst_h[-1])
+        clock = _PhaseClock(stats)
         if I:
             inst_rule = torch.from_numpy(inst_rule_h).to(dev)
             row_ptr = torch.arange(I + 1, dtype=torch.int64, device=dev)
             ent = torch.from_numpy(np.repeat(src_h[bq], counts).astype(np.int32)).to(dev)
-            clock = _PhaseClock(stats)
             for step in range(ops_all.shape[1]):
                 row_ptr, ent = _fixed_step_rows(row_ptr, ent, ops_all[inst_rule, step], graph, relations, E,
                                                 fact_budget, stats, bitmap_min_facts)
             stats["entries"] = stats.get("entries", 0) + ent.numel()
             clock.tick("ground_s")
-            s_rp, s_ent, s_x = _instance_scores(row_ptr, ent, torch.from_numpy(q_inst_h).to(dev),
-                                                weights[inst_rule].contiguous(), ranks, E, final_max, fact_budget,
-                                                stats, dense_min_entries)
-            clock.tick("score_s")
-            si_b = torch.repeat_interleave(torch.arange(Bq, device=dev), s_rp[1:] - s_rp[:-1],
-                                           output_size=s_ent.numel())
-            si_e, sv = s_ent.to(torch.int64), s_x
+            scored = _instance_scores(row_ptr, ent, torch.from_numpy(q_inst_h).to(dev),
+                                      weights[inst_rule].contiguous(), ranks, E, final_max, fact_budget, stats,
+                                      dense_min_entries)
         else:
-            si_b = si_e = torch.empty(0, dtype=torch.int64, device=dev)
-            sv = torch.empty(0, dtype=torch.float32, device=dev)
+            scored = [(0, Bq, None)]
         fk = torch.arange(Bq, device=dev) * E + tgt
         if filter_keys is not None:
             fk = torch.cat([fk, filter_keys(idx) if callable(filter_keys) else filter_keys[idx]])
-        fk = torch.unique(fk)
-        ranks_out[idx] = ops.filtered_ranks(si_b, si_e, sv, tgt, fk, Bq, E, True)
+        fk = torch.unique(fk)  # sorted: each run's keys are a contiguous range
+        bounds = torch.searchsorted(fk, torch.arange(Bq + 1, device=dev) * E).cpu().tolist()
+        # each run's queries are ranked as soon as they are scored (their scores are then dropped)
+        for qa, qb, sc in scored:
+            n = qb - qa
+            if sc is None:
+                si_b = si_e = torch.empty(0, dtype=torch.int64, device=dev)
+                sv = torch.empty(0, dtype=torch.float32, device=dev)
+            else:
+                s_rp, s_ent, s_x = sc
+                si_b = torch.repeat_interleave(torch.arange(n, device=dev), s_rp[1:] - s_rp[:-1],
+                                               output_size=s_ent.numel())
+                si_e, sv = s_ent.to(torch.int64), s_x
+            fk_run = fk[bounds[qa]:bounds[qb]] - qa * E
+            ranks_out[idx[qa:qb]] = ops.filtered_ranks(si_b, si_e, sv, tgt[qa:qb], fk_run, n, E, True)
+        clock.tick("score_s")
         stats["batches"] += 1
     return ranks_out
 
