@@ -139,6 +139,7 @@ SIGNATURES = {
                                                 _P]),
     "fl_rule_instance_max": (ctypes.c_int, [_P, _P, _P, _I64, _P, _I64, _I64, _P, _P]),
     "fl_bitmap_rows_workspace": (_SZ, [_I64, _I64]),
+    "fl_rows_copy": (ctypes.c_int, [_P, _P, _I64, _P, _P, _P]),
     "fl_bitmap_rows_count": (ctypes.c_int, [_P, _I64, _I64, _P, _P, _P, _SZ, _P]),
     "fl_bitmap_rows_emit": (ctypes.c_int, [_P, _I64, _I64, _P, _P, _P]),
     "fl_filtered_ranks_workspace": (_SZ, [_I64]),

@@ -57,6 +57,8 @@ int rule_instance_facts(const int64_t *st_rp, const int32_t *st_ent, const int64
                         cudaStream_t st);
 int rule_instance_max(const int64_t *st_rp, const int32_t *st_ent, const int64_t *q_inst, int64_t nq, const float *w,
                       int64_t ranks, int64_t E, unsigned int *acc, cudaStream_t st);
+int rows_copy(const int64_t *src_rp, const int32_t *src_ent, int64_t rows, const int64_t *dst_rp, int32_t *dst_ent,
+              cudaStream_t st);
 size_t bitmap_rows_workspace(int64_t nb, int64_t words);
 int fixed_relation_bitmap(const int64_t *entries, int64_t n, const int64_t *entry_row, const int32_t *row_slot,
                           const int32_t *ent, const int64_t *ops, int64_t R, const fl_csr_side &ori,
@@ -358,6 +360,11 @@ int fl_fixed_relation_bitmap(const int64_t *entries, int64_t n, const int64_t *e
 int fl_rule_instance_max(const int64_t *st_rp, const int32_t *st_ent, const int64_t *q_inst, int64_t nq,
                          const float *w, int64_t ranks, int64_t E, uint32_t *acc, fl_stream_t stream) {
     return rule_instance_max(st_rp, st_ent, q_inst, nq, w, ranks, E, acc, as_stream(stream));
+}
+
+int fl_rows_copy(const int64_t *src_rp, const int32_t *src_ent, int64_t rows, const int64_t *dst_rp, int32_t *dst_ent,
+                 fl_stream_t stream) {
+    return rows_copy(src_rp, src_ent, rows, dst_rp, dst_ent, as_stream(stream));
 }
 
 size_t fl_bitmap_rows_workspace(int64_t nb, int64_t words) { return bitmap_rows_workspace(nb, words); }

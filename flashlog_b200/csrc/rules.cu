@@ -292,6 +292,18 @@ __global__ void fixed_bitmap_kernel(const int64_t *entries, int64_t n, const int
     }
 }
 
+// Row copy: one warp per row moves the row's entries to the row's start in
+// another row layout (rows with no entries copy nothing).
+__global__ void rows_copy_kernel(const int64_t *src_rp, const int32_t *src_ent, int64_t rows, const int64_t *dst_rp,
+                                 int32_t *dst_ent) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += nw) {
+        const int64_t a = src_rp[r], n = src_rp[r + 1] - a, d = dst_rp[r];
+        for (int64_t k = lane; k < n; k += 32) dst_ent[d + k] = src_ent[a + k];
+    }
+}
+
 // Set-bit counts of chunks of kBmChunk consecutive bitmap words, one block each.
 constexpr int kBmChunk = 256;
 __global__ void __launch_bounds__(kBmChunk) bitmap_count_kernel(const uint32_t *bm, int64_t *chunk_cnt) {
@@ -336,6 +348,19 @@ int rule_instance_max(const int64_t *st_rp, const int32_t *st_ent, const int64_t
                nq, w, ranks, E, acc);
     }
     return check_launch("rule_instance_max");
+}
+
+int rows_copy(const int64_t *src_rp, const int32_t *src_ent, int64_t rows, const int64_t *dst_rp, int32_t *dst_ent,
+              cudaStream_t st) {
+    FL_REQUIRE(rows >= 0 && (rows == 0 || (src_rp && dst_rp)), "fl_rows_copy: bad arguments");
+    if (rows > 0) {
+        const int sms = fl_device_sm_count();
+        int64_t blocks = (rows + 7) / 8;
+        const int64_t cap = static_cast<int64_t>(sms > 0 ? sms : 148) * 16;
+        if (blocks > cap) blocks = cap;
+        launch(rows_copy_kernel, static_cast<unsigned>(blocks), 256, 0, st, src_rp, src_ent, rows, dst_rp, dst_ent);
+    }
+    return check_launch("rows_copy");
 }
 
 size_t bitmap_rows_workspace(int64_t nb, int64_t words) {

@@ -247,14 +247,11 @@ def _merge_rows(rows: int, parts):
     out_rp = torch.zeros(rows + 1, dtype=torch.int64, device=dev)
     torch.cumsum(counts, 0, out=out_rp[1:])
     total = int(out_rp[rows].item())
-    out = torch.empty(total, dtype=torch.int32, device=dev)
+    out = torch.empty(max(total, 1), dtype=torch.int32, device=dev)
     for rp, e in parts:
-        n = e.numel()
-        if n == 0:
-            continue
-        row = torch.repeat_interleave(torch.arange(rows, device=dev), rp[1:] - rp[:-1], output_size=n)
-        out[out_rp[row] + torch.arange(n, device=dev) - rp[row]] = e
-    return out_rp, out
+        if e.numel():
+            check(lib().fl_rows_copy(_p(rp), _p(e), rows, _p(out_rp), _p(out), _stream()), "rows_copy")
+    return out_rp, out[:total]
 
 
 def _plan_step(ent, b, ops_col, graph, relations: int):
@@ -502,11 +499,12 @@ class _PhaseClock:
             self.t = now
 
 
-def route_instances(rel_h, heads, query_batch: int, instance_budget: int):
+def route_instances(rel_h, heads, query_batch: int, instance_budget):
     """Batches of the routed evaluation (host side): the queries in relation
     order (stable), cut into batches of consecutive queries with at most
     query_batch queries and instance_budget instances (a query whose rules
-    alone exceed the budget forms its own batch).  heads: the head relation
+    alone exceed the budget forms its own batch).  instance_budget may be a
+    callable, read before every batch.  heads: the head relation
     of every compacted rule, ascending.  Yields (queries i64[Bq] in batch
     order, q_inst i64[Bq + 1] (query q owns instances q_inst[q]..q_inst[q+1]),
     inst_rule i64[instances] (the rule of every instance, in the order of
@@ -518,8 +516,9 @@ def route_instances(rel_h, heads, query_batch: int, instance_budget: int):
     order = np.argsort(rel_h, kind="stable")
     q0 = 0
     while q0 < rel_h.size:
+        budget = instance_budget() if callable(instance_budget) else instance_budget
         cum = np.cumsum(n_inst[order[q0:q0 + query_batch]])
-        q1 = q0 + max(1, int(np.searchsorted(cum, instance_budget, side="right")))
+        q1 = q0 + max(1, int(np.searchsorted(cum, budget, side="right")))
         bq = order[q0:q1]
         counts = n_inst[bq]
         q_inst = np.concatenate([[0], np.cumsum(counts)]).astype(np.int64)
@@ -532,7 +531,7 @@ def evaluate_rule_bank(sources, query_relations, targets, rules, csr_struct, rel
                        final_max: bool = False, chunk_size: int = 16, query_batch: int = 4096,
                        accumulator_bytes: int = 4 << 30, filter_keys=None, stats=None,
                        instance_budget: int = 1 << 20, fact_budget: int = 1 << 29, bitmap_min_facts=None,
-                       dense_min_entries=None):
+                       dense_min_entries=None, entry_budget: int = 1 << 28):
     """Filtered, tie-averaged ranks of the targets under the rule bank's
     max-product scores (rules/evaluate.py:1015-1095 with --aggregations
     routed_normalized and reduction 'max': smDRUM sums the normalized ranks,
@@ -540,7 +539,11 @@ def evaluate_rule_bank(sources, query_relations, targets, rules, csr_struct, rel
     is its relation (compacted per (head, body), rules/evaluate.py:94-119).
 
     The queries, ordered by relation, run in batches of at most query_batch
-    queries and instance_budget rule instances (query, rule); one batch is
+    queries and instance_budget rule instances (query, rule), fewer when the
+    instances reach many entities: after each batch the instance budget is
+    set so that the largest state of a step (entities over all instances)
+    would stay near entry_budget, from the batch's entities per instance (the
+    first batch takes at most 2^14 instances); one batch is
     one Boolean state whose rows are its instances, advanced one body
     operator per step for all instances at once, so the number of launches
     and host reads grows with the batches, not with the rules or the
@@ -582,7 +585,8 @@ def evaluate_rule_bank(sources, query_relations, targets, rules, csr_struct, rel
         graph = _graph(csr_struct)
     src_h = sources.to(torch.int64).cpu().numpy()
     stats.update(instances=int(n_inst.sum()), batches=0, rules_after=len(compact))
-    for bq, q_inst_h, inst_rule_h in route_instances(rel_h, heads, query_batch, instance_budget):
+    budget = {"instances": min(instance_budget, 1 << 14)}
+    for bq, q_inst_h, inst_rule_h in route_instances(rel_h, heads, query_batch, lambda: budget["instances"]):
         Bq = bq.size
         idx = torch.from_numpy(bq).to(dev)
         tgt = targets[idx]
@@ -593,10 +597,13 @@ def evaluate_rule_bank(sources, query_relations, targets, rules, csr_struct, rel
             inst_rule = torch.from_numpy(inst_rule_h).to(dev)
             row_ptr = torch.arange(I + 1, dtype=torch.int64, device=dev)
             ent = torch.from_numpy(np.repeat(src_h[bq], counts).astype(np.int32)).to(dev)
+            peak = 1
             for step in range(ops_all.shape[1]):
                 row_ptr, ent = _fixed_step_rows(row_ptr, ent, ops_all[inst_rule, step], graph, relations, E,
                                                 fact_budget, stats, bitmap_min_facts)
+                peak = max(peak, ent.numel())
             stats["entries"] = stats.get("entries", 0) + ent.numel()
+            budget["instances"] = int(min(instance_budget, max(256, entry_budget * I // peak)))
             clock.tick("ground_s")
             scored = _instance_scores(row_ptr, ent, torch.from_numpy(q_inst_h).to(dev),
                                       weights[inst_rule].contiguous(), ranks, E, final_max, fact_budget, stats,

@@ -429,6 +429,11 @@ int fl_fixed_relation_bitmap(const int64_t *entries, int64_t n, const int64_t *e
                              const int32_t *ent, const int64_t *ops, int64_t r_size, fl_csr_side ori,
                              fl_csr_side inv, uint32_t *bitmap, int64_t words, fl_stream_t stream);
 size_t fl_bitmap_rows_workspace(int64_t nb, int64_t words);
+/* Copies every row of a row layout (src_rp i64[rows+1], src_ent) to the
+ * start of the same row in another layout (dst_rp i64[rows], dst_ent), for
+ * merging the results of disjoint row sets. */
+int fl_rows_copy(const int64_t *src_rp, const int32_t *src_ent, int64_t rows, const int64_t *dst_rp, int32_t *dst_ent,
+                 fl_stream_t stream);
 int fl_bitmap_rows_count(const uint32_t *bitmap, int64_t nb, int64_t words, int64_t *chunk_off, int64_t *row_ptr,
                          void *ws, size_t ws_bytes, fl_stream_t stream);
 int fl_bitmap_rows_emit(const uint32_t *bitmap, int64_t nb, int64_t words, const int64_t *chunk_off, int32_t *ent,
