@@ -401,6 +401,36 @@ def _combine_ranks(rp, r_ent, x, nq: int, ranks: int, E: int, final_max: bool):
     return out_rp, out_ent, out_x
 
 
+def _dense_scores(acc, nq: int, ranks: int, E: int, final_max: bool):
+    """Scores of nq queries from their dense rank maxima acc (u32 fp32 bits,
+    [nq, ranks, E], consumed): the rank rows read back sorted, normalized in
+    the row layout (the same sums as the sparse path), written back and
+    combined densely, where the absent entries are +0.0 and leave the
+    rank-order sum and the max of the present ones exact.  Returns the row
+    layout over the queries."""
+    dev = acc.device
+    nz = torch.nonzero(acc.view(nq * ranks, E))
+    row, r_ent = nz[:, 0], nz[:, 1]
+    rp = torch.zeros(nq * ranks + 1, dtype=torch.int64, device=dev)
+    torch.cumsum(torch.bincount(row, minlength=nq * ranks), 0, out=rp[1:])
+    dense = acc.view(torch.float32).view(nq * ranks, E)
+    y, _ = ops.normalize_forward(rp, dense[row, r_ent].contiguous(), eps=1e-30)
+    dense[row, r_ent] = y
+    del nz, row, r_ent, y
+    dense = dense.view(nq, ranks, E)
+    if final_max:
+        comb = dense.amax(1)
+    else:
+        comb = dense[:, 0].clone()
+        for r in range(1, ranks):
+            comb += dense[:, r]
+    del dense
+    nz = torch.nonzero(comb)
+    s_rp = torch.zeros(nq + 1, dtype=torch.int64, device=dev)
+    torch.cumsum(torch.bincount(nz[:, 0], minlength=nq), 0, out=s_rp[1:])
+    return s_rp, nz[:, 1].to(torch.int32), comb[nz[:, 0], nz[:, 1]].contiguous()
+
+
 def _instance_scores(row_ptr, ent, q_inst, w_inst, ranks: int, E: int, final_max: bool, fact_budget: int, stats,
                      dense_min_entries=None, dense_bytes: int = 4 << 30):
     """Scores of the queries of an instance-grouped Boolean state (query q
@@ -442,31 +472,7 @@ def _instance_scores(row_ptr, ent, q_inst, w_inst, ranks: int, E: int, final_max
             acc = torch.zeros(nq * ranks * E, dtype=torch.int32, device=dev)
             check(lib().fl_rule_instance_max(_p(row_ptr), _p(ent), _p(q_inst[qa:]), nq, _p(w_inst), ranks, E,
                                              _p(acc), _stream()), "rule_instance_max")
-            nz = torch.nonzero(acc.view(nq * ranks, E))
-            row, r_ent = nz[:, 0], nz[:, 1]
-            rp = torch.zeros(nq * ranks + 1, dtype=torch.int64, device=dev)
-            torch.cumsum(torch.bincount(row, minlength=nq * ranks), 0, out=rp[1:])
-            dense = acc.view(torch.float32).view(nq * ranks, E)
-            x = dense[row, r_ent].contiguous()
-            # normalized in the rank-row layout (the same sums as the sparse
-            # path), then combined densely: absent entries are +0.0, which
-            # leaves the rank-order sum and the max of the present ones exact
-            y, _ = ops.normalize_forward(rp, x, eps=1e-30)
-            dense[row, r_ent] = y
-            dense = dense.view(nq, ranks, E)
-            if final_max:
-                comb = dense.amax(1)
-            else:
-                comb = dense[:, 0].clone()
-                for r in range(1, ranks):
-                    comb += dense[:, r]
-            del acc, dense
-            nz = torch.nonzero(comb)
-            s_rp = torch.zeros(nq + 1, dtype=torch.int64, device=dev)
-            torch.cumsum(torch.bincount(nz[:, 0], minlength=nq), 0, out=s_rp[1:])
-            s_ent, s_x = nz[:, 1].to(torch.int32), comb[nz[:, 0], nz[:, 1]].contiguous()
-            del comb, nz
-            yield qa, qb, (s_rp, s_ent, s_x)
+            yield qa, qb, _dense_scores(acc, nq, ranks, E, final_max)
             continue
         else:
             T = int(ranks * (before[qb] - before[qa]))
@@ -531,7 +537,7 @@ def evaluate_rule_bank(sources, query_relations, targets, rules, csr_struct, rel
                        final_max: bool = False, chunk_size: int = 16, query_batch: int = 4096,
                        accumulator_bytes: int = 4 << 30, filter_keys=None, stats=None,
                        instance_budget: int = 1 << 20, fact_budget: int = 1 << 29, bitmap_min_facts=None,
-                       dense_min_entries=None, entry_budget: int = 1 << 28):
+                       dense_min_entries=None, entry_budget: int = 1 << 27):
     """Filtered, tie-averaged ranks of the targets under the rule bank's
     max-product scores (rules/evaluate.py:1015-1095 with --aggregations
     routed_normalized and reduction 'max': smDRUM sums the normalized ranks,
@@ -543,7 +549,9 @@ def evaluate_rule_bank(sources, query_relations, targets, rules, csr_struct, rel
     instances reach many entities: after each batch the instance budget is
     set so that the largest state of a step (entities over all instances)
     would stay near entry_budget, from the batch's entities per instance (the
-    first batch takes at most 2^14 instances); one batch is
+    first batch takes at most 2^12 instances); a single query with more
+    instances than that is grounded in parts whose maxima meet in the query's
+    dense accumulator.  One batch is
     one Boolean state whose rows are its instances, advanced one body
     operator per step for all instances at once, so the number of launches
     and host reads grows with the batches, not with the rules or the
@@ -585,7 +593,7 @@ def evaluate_rule_bank(sources, query_relations, targets, rules, csr_struct, rel
         graph = _graph(csr_struct)
     src_h = sources.to(torch.int64).cpu().numpy()
     stats.update(instances=int(n_inst.sum()), batches=0, rules_after=len(compact))
-    budget = {"instances": min(instance_budget, 1 << 14)}
+    budget = {"instances": min(instance_budget, 1 << 12)}
     for bq, q_inst_h, inst_rule_h in route_instances(rel_h, heads, query_batch, lambda: budget["instances"]):
         Bq = bq.size
         idx = torch.from_numpy(bq).to(dev)
@@ -593,7 +601,36 @@ def evaluate_rule_bank(sources, query_relations, targets, rules, csr_struct, rel
         counts = np.diff(q_inst_h)
         I = int(q_inst_h[-1])
         clock = _PhaseClock(stats)
-        if I:
+        if I > budget["instances"] and Bq == 1:
+            # one query with more instances than a batch holds: its instances
+            # are grounded in parts, each part's maxima raised into the
+            # query's dense accumulator (the same maxima, in any part order)
+            acc = torch.zeros(ranks * E, dtype=torch.int32, device=dev)
+            c0 = 0
+            while c0 < I:
+                c1 = min(I, c0 + budget["instances"])
+                part_rule = torch.from_numpy(inst_rule_h[c0:c1]).to(dev)
+                row_ptr = torch.arange(c1 - c0 + 1, dtype=torch.int64, device=dev)
+                ent = torch.full((c1 - c0,), int(src_h[bq[0]]), dtype=torch.int32, device=dev)
+                peak = 1
+                for step in range(ops_all.shape[1]):
+                    row_ptr, ent = _fixed_step_rows(row_ptr, ent, ops_all[part_rule, step], graph, relations, E,
+                                                    fact_budget, stats, bitmap_min_facts)
+                    peak = max(peak, ent.numel())
+                stats["entries"] = stats.get("entries", 0) + ent.numel()
+                q_part = torch.tensor([0, c1 - c0], dtype=torch.int64, device=dev)
+                check(lib().fl_rule_instance_max(_p(row_ptr), _p(ent), _p(q_part), 1,
+                                                 _p(weights[part_rule].contiguous()), ranks, E, _p(acc), _stream()),
+                      "rule_instance_max")
+                del row_ptr, ent
+                budget["instances"] = int(min(instance_budget, max(256, entry_budget * (c1 - c0) // peak)))
+                c0 = c1
+            stats["split_queries"] = stats.get("split_queries", 0) + 1
+            stats["dense_queries"] = stats.get("dense_queries", 0) + 1
+            clock.tick("ground_s")
+            scored = [(0, 1, _dense_scores(acc, 1, ranks, E, final_max))]
+            del acc
+        elif I:
             inst_rule = torch.from_numpy(inst_rule_h).to(dev)
             row_ptr = torch.arange(I + 1, dtype=torch.int64, device=dev)
             ent = torch.from_numpy(np.repeat(src_h[bq], counts).astype(np.int32)).to(dev)

@@ -111,15 +111,18 @@ def oracle_routed_ranks(src, rel, dst, rules, csr_np, R, E, final_max, sparse=Fa
 
 
 @pytest.mark.parametrize("final_max", [False, True])
-@pytest.mark.parametrize("mode", ["sorted", "split", "dense", "auto"])
+@pytest.mark.parametrize("mode", ["sorted", "split", "dense", "auto", "parts"])
 def test_routed_evaluation_matches_oracle(final_max, mode):
     """mode: "sorted" reduces every step by the row reduction and every
     query's maxima by rank facts; "split" does the same in budgets of 4000
     facts (many ranges of instances and of queries); "dense" takes every
     step through entity bitmaps and every query through the dense
-    accumulator; "auto" chooses per instance and per query."""
+    accumulator; "auto" chooses per instance and per query; "parts" caps a
+    batch at 64 instances, so every query with more rules is grounded in
+    parts that meet in its dense accumulator."""
     budget = 4000 if mode == "split" else 1 << 29
-    big = {"sorted": 1 << 62, "split": 1 << 62, "dense": 0, "auto": None}[mode]
+    big = {"sorted": 1 << 62, "split": 1 << 62, "dense": 0, "auto": None, "parts": None}[mode]
+    instances = 64 if mode == "parts" else 1 << 20
     if not torch.cuda.is_available():
         pytest.skip("needs a CUDA device")
     import flashlog_b200.flashlog_kernel as fk
@@ -136,7 +139,7 @@ def test_routed_evaluation_matches_oracle(final_max, mode):
     stats = {}
     got = RB.evaluate_rule_bank(_cuda(src), _cuda(rel), _cuda(dst), rules, csr, R, E, final_max=final_max,
                                 query_batch=32, fact_budget=budget, stats=stats, bitmap_min_facts=big,
-                                dense_min_entries=big).cpu().numpy()
+                                dense_min_entries=big, instance_budget=instances).cpu().numpy()
     want = oracle_routed_ranks(src, rel, dst, rules, csr_np, R, E, final_max)
     assert np.array_equal(got, want)
     assert stats["batches"] >= src.size // 32
@@ -146,4 +149,6 @@ def test_routed_evaluation_matches_oracle(final_max, mode):
         assert stats.get("bitmap_rows", 0) == 0 and stats["dense_queries"] == 0
     if mode == "dense":
         assert stats["bitmap_rows"] > 0 and stats["dense_queries"] > 0
+    if mode == "parts":
+        assert stats["split_queries"] > 0
     assert (want < 0.5 * E).sum() > 10  # some targets are reached by rules
