@@ -234,28 +234,42 @@ __global__ void inst_facts_kernel(const int64_t *st_rp, const int32_t *st_ent, c
 }
 
 // Dense rank maxima of an instance-grouped Boolean state (query q owns the
-// instance rows [q_inst[q], q_inst[q + 1]), q < nq): one warp per instance
-// raises acc[(q * ranks + r) * E + entity] to the fp32 bits of the
-// instance's weight at rank r, for every entity the instance reaches.
+// instance rows [q_inst[q], q_inst[q + 1]), q < nq): for every entry of
+// every instance, acc[(q * ranks + r) * E + entity] is raised to the fp32
+// bits of the instance's weight at rank r.  The work is split by entries,
+// not by instances (an instance can hold millions of entries): each warp
+// takes runs of kMaxChunk consecutive entries, finds the instance of the
+// first by binary search and walks forward from there.
+constexpr int kMaxChunk = 256;
 __global__ void inst_max_kernel(const int64_t *st_rp, const int32_t *st_ent, const int64_t *q_inst, int64_t nq,
                                 const float *w, int64_t ranks, int64_t E, unsigned int *acc) {
     const int lane = threadIdx.x & 31;
     const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-    const int64_t c_end = q_inst[nq];
-    for (int64_t c = q_inst[0] + blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); c < c_end;
-         c += nw) {
-        int64_t lo = 0, hi = nq - 1;  // the last query whose first instance is at or before c
-        while (lo < hi) {
-            const int64_t mid = (lo + hi + 1) >> 1;
-            if (q_inst[mid] <= c) lo = mid; else hi = mid - 1;
+    const int64_t c_lo = q_inst[0], c_hi = q_inst[nq];
+    const int64_t e0 = st_rp[c_lo], e1 = st_rp[c_hi];
+    for (int64_t k0 = e0 + (blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5)) * kMaxChunk;
+         k0 < e1; k0 += nw * kMaxChunk) {
+        int64_t c = 0;
+        if (lane == 0) {  // the instance holding entry k0: the last c with st_rp[c] <= k0
+            int64_t lo = c_lo, hi = c_hi - 1;
+            while (lo < hi) {
+                const int64_t mid = (lo + hi + 1) >> 1;
+                if (st_rp[mid] <= k0) lo = mid; else hi = mid - 1;
+            }
+            c = lo;
         }
-        unsigned int *aq = acc + lo * ranks * E;
-        const int64_t a = st_rp[c], b = st_rp[c + 1];
-        for (int64_t k = a + lane; k < b; k += 32) {
+        c = __shfl_sync(0xffffffffu, c, 0);
+        int64_t q = 0;
+        while (q_inst[q + 1] <= c) ++q;  // q < nq: q_inst[nq] = c_hi > c
+        const int64_t k1 = (k0 + kMaxChunk) < e1 ? (k0 + kMaxChunk) : e1;
+        for (int64_t k = k0 + lane; k < k1; k += 32) {
+            while (st_rp[c + 1] <= k) ++c;  // c + 1 <= c_hi: st_rp[c_hi] = e1 > k
+            while (q_inst[q + 1] <= c) ++q;
             const int64_t e = st_ent[k];
+            unsigned int *aq = acc + q * ranks * E + e;
             for (int64_t r = 0; r < ranks; ++r) {
                 const unsigned int wb = __float_as_uint(w[c * ranks + r]);
-                if (wb != 0u) atomicMax(aq + r * E + e, wb);
+                if (wb != 0u) atomicMax(aq + r * E, wb);
             }
         }
     }
