@@ -1063,7 +1063,7 @@ constexpr int kLoadStep = kRThreads * kLoadK;
 constexpr int kKBitsMax = kRThreads == 1024 ? 13 : 12;
 constexpr int kKBins = 1 << kKBitsMax;  // destination bins per row (at most)
 constexpr int kTileK = 12 * kRThreads;  // facts per chunk
-constexpr int kRankBinMax = 64;        // bins up to this size: each fact ranked within its bin
+constexpr int kRankBinMax = 512;       // bins up to this size: each fact ranked within its bin
 constexpr int kMultiPairs = 2 * kRThreads;  // comparator pairs of the block-wide sort of the larger bins
 constexpr int kWarpSortMax = 1024;      // bins up to this size are sorted by one warp
 constexpr int kBigBinsMax = kTileK / kWarpSortMax + 1;
