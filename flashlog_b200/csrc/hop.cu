@@ -1060,6 +1060,7 @@ constexpr int kTileD = 6 * kRThreads;   // dense-window sub-tile
 constexpr int kDenseW = 4 * kRThreads;  // dense window width (destinations)
 constexpr int kLoadK = 4;  // slots per thread per load step
 constexpr int kLoadStep = kRThreads * kLoadK;
+static_assert(kLoadStep <= 6 * kRThreads, "a load step must fit an empty dense-window sub-tile, or load_range stalls");
 constexpr int kKBitsMax = kRThreads == 1024 ? 13 : 12;
 constexpr int kKBins = 1 << kKBitsMax;  // destination bins per row (at most)
 constexpr int kTileK = 12 * kRThreads;  // facts per chunk
