@@ -334,9 +334,12 @@ def run_graph_arm(args, cfg, train, csr, rank, world, device):
     # parts; the update waits for all of them.
     comm = torch.cuda.Stream() if world > 1 else None
 
-    def run_parts(parts):
+    # N > 1: only the union of the ranks' batch relations (rows of the table)
+    # can hold gradient; those rows alone are all-reduced and updated
+    def run_parts(parts, rels):
         if world > 1:
-            MG.run_parts_with_overlapped_allreduce(parts, step.grad_hop, step.grad, table, lr, comm)
+            rows = MG.union_rows(rels, table.shape[0])
+            MG.run_parts_with_overlapped_allreduce(parts, step.grad_hop, step.grad, table, lr, comm, rows=rows)
         else:
             for part in parts:
                 part()
@@ -349,7 +352,7 @@ def run_graph_arm(args, cfg, train, csr, rank, world, device):
         for b in dev_data[:args.warmup]:
             ids, h, r, t = b
             step.load(h, t, r, hide_of(ids))
-            run_parts(step.parts())
+            run_parts(step.parts(), r)
     torch.cuda.current_stream().wait_stream(side)
     torch.cuda.synchronize()
     step.check()
@@ -389,7 +392,7 @@ def run_graph_arm(args, cfg, train, csr, rank, world, device):
         if world == 1:
             graphs[k][0].replay()
         else:
-            run_parts([g.replay for g in graphs[k]])
+            run_parts([g.replay for g in graphs[k]], r)
     t1.record()
     torch.cuda.synchronize()
     if world > 1:

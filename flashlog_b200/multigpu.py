@@ -43,16 +43,42 @@ def allreduce_mean_(grad: torch.Tensor, group=None) -> torch.Tensor:
     return grad
 
 
+def union_rows(rels: torch.Tensor, n_rows: int, group=None) -> torch.Tensor:
+    """The table rows any rank's step can write: the sorted distinct values of
+    every rank's `rels` (the batch's query relations; the ranks' batches may
+    differ in size), from an all-reduced row mask.  The step's gradient is
+    zero outside them on every rank (DrumTrainStep zeroes grad_hop and adds
+    only the batch's rows).  One host read (the count)."""
+    mask = torch.zeros(n_rows, dtype=torch.int32, device=rels.device)
+    mask[rels.to(torch.int64)] = 1
+    if dist.get_world_size(group) > 1:
+        dist.all_reduce(mask, group=group)
+    return torch.nonzero(mask).flatten()
+
+
 def run_parts_with_overlapped_allreduce(parts, grad_hop, table_grad, table, lr: float, comm_stream=None,
-                                        group=None):
+                                        group=None, rows=None):
     """One training step given as parts (DrumTrainStep.parts(), or replays of
     their CUDA graphs): after part j < T has been issued, hop T-1-j's table
     gradient grad_hop[T-1-j] is complete and its all-reduce (sum) is issued
     on comm_stream (a CUDA stream; None: in order, e.g. gloo on CPU), so it
     overlaps the parts that follow.  Then the update waits for all of them:
-    table -= lr / world * table_grad (a view of the summed hop gradients)."""
+    table -= lr / world * table_grad (a view of the summed hop gradients).
+    rows (union_rows of the step): only those rows of each hop's gradient are
+    all-reduced, gathered into a compact buffer and written back, and only
+    those rows of the table are updated; the other rows are zero on every
+    rank, so the result is the same."""
     world = dist.get_world_size(group)
     T = len(grad_hop)
+
+    def reduce(hop):
+        if rows is None:
+            dist.all_reduce(grad_hop[hop], group=group)
+            return
+        buf = grad_hop[hop].index_select(0, rows)
+        dist.all_reduce(buf, group=group)
+        grad_hop[hop].index_copy_(0, rows, buf)
+
     for j, part in enumerate(parts):
         part()
         if world > 1 and j < T:
@@ -60,13 +86,16 @@ def run_parts_with_overlapped_allreduce(parts, grad_hop, table_grad, table, lr: 
             if comm_stream is not None:
                 comm_stream.wait_stream(torch.cuda.current_stream())
                 with torch.cuda.stream(comm_stream):
-                    dist.all_reduce(grad_hop[hop], group=group)
+                    reduce(hop)
             else:
-                dist.all_reduce(grad_hop[hop], group=group)
+                reduce(hop)
     if world > 1:
         if comm_stream is not None:
             torch.cuda.current_stream().wait_stream(comm_stream)
-        table.sub_(table_grad, alpha=lr / world)
+        if rows is None:
+            table.sub_(table_grad, alpha=lr / world)
+        else:
+            table.index_add_(0, rows, table_grad.index_select(0, rows), alpha=-lr / world)
 
 
 def max_time_sum_work(ms: float, work: float, device, group=None):

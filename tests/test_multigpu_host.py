@@ -80,6 +80,55 @@ def _parts_worker(rank, world, port, out):
         dist.destroy_process_group()
 
 
+def _parts_rows_worker(rank, world, port, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from flashlog_b200 import multigpu as MG
+        T = 3
+        rels = torch.tensor([0, 2, 2] if rank == 0 else [3, 2])  # the batch's query relations
+        rows = MG.union_rows(rels, 4)
+        grad_hop = torch.zeros(T, 4, 2)
+        table = torch.ones(4, T, 2)
+
+        def part(hop):
+            def run():
+                if hop >= 0:  # only the batch's rows are written, as DrumTrainStep does
+                    grad_hop[hop].zero_()
+                    grad_hop[hop][rels.unique()] = float((rank + 1) * (hop + 1))
+            return run
+        parts = [part(2), part(1), part(0), part(-1)]
+        MG.run_parts_with_overlapped_allreduce(parts, grad_hop, grad_hop.permute(1, 0, 2), table, lr=0.5,
+                                               rows=rows)
+        out.put((rank, rows.tolist(), table.tolist(), grad_hop.tolist()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_compact_allreduce_of_the_union_rows_on_two_gloo_ranks():
+    """Rank 0's batch writes rows {0, 2}, rank 1's rows {2, 3}: the union
+    [0, 2, 3] is all-reduced and updated; row 1 stays untouched, and every
+    row gets what the dense all-reduce would give."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_parts_rows_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    per_row = {0: 1.0, 1: 0.0, 2: 3.0, 3: 2.0}  # sum over ranks of (rank + 1) for the rows each rank writes
+    for rank, rows, table, grad in res:
+        assert rows == [0, 2, 3]
+        for hop in range(3):
+            for row in range(4):
+                assert grad[hop][row] == [per_row[row] * (hop + 1)] * 2
+                assert table[row][hop] == [1.0 - 0.25 * per_row[row] * (hop + 1)] * 2
+
+
 def test_overlapped_allreduce_parts_on_two_gloo_ranks():
     """Each hop's gradient is summed over the ranks once its part has run, and
     the update applies lr / world times the sums: here table = 1 - 0.25 *
