@@ -66,6 +66,9 @@ def parse():
                     help="instead of the training step: max-product rule-bank evaluation of this many test "
                          "queries (sharded over the ranks), --rule-bank rules, queries/s")
     ap.add_argument("--rule-bank", type=int, default=50_000)
+    ap.add_argument("--union-rows", action="store_true",
+                    help="N > 1: all-reduce only the table rows of the ranks' batch relations (one host read "
+                         "per step to find them) instead of the whole hop gradient")
     ap.add_argument("--rule-timing", action="store_true",
                     help="synchronize between the evaluator's phases and report their host times")
     ap.add_argument("--rule-ops", choices=("edge", "uniform"), default="edge",
@@ -334,11 +337,12 @@ def run_graph_arm(args, cfg, train, csr, rank, world, device):
     # parts; the update waits for all of them.
     comm = torch.cuda.Stream() if world > 1 else None
 
-    # N > 1: only the union of the ranks' batch relations (rows of the table)
-    # can hold gradient; those rows alone are all-reduced and updated
+    # N > 1 with --union-rows: only the union of the ranks' batch relations
+    # (rows of the table) can hold gradient, so those rows alone are
+    # all-reduced and updated; finding the union costs a host read per step
     def run_parts(parts, rels):
         if world > 1:
-            rows = MG.union_rows(rels, table.shape[0])
+            rows = MG.union_rows(rels, table.shape[0]) if args.union_rows else None
             MG.run_parts_with_overlapped_allreduce(parts, step.grad_hop, step.grad, table, lr, comm, rows=rows)
         else:
             for part in parts:
