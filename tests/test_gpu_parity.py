@@ -507,6 +507,39 @@ def test_sampled_c2_matches_oracle(fk, g1):
         assert np.array_equal(fw.out_x.cpu().numpy(), ref["out_val"]), topk
 
 
+def test_topk_rows_with_equal_weights_share_ranks(fk, g1):
+    """Rows whose weights are equal bit for bit (queries of one relation)
+    share one relation-rank computation (ops.identical_rows); the selections
+    equal the oracle's, and rows that only collide in hash keep their own."""
+    from flashlog_b200 import ops, _lib as Lb
+    from flashlog_b200.ops import Graph
+    cfg, train, csr_np, csr = g1
+    E, R = cfg.entities, cfg.relations
+    rng = np.random.default_rng(23)
+    B, L = 6, 3
+    row, ent, val = _state(rng, B, L, E, 30, zero_frac=0.0)
+    w = _w(rng, B, L, 2 * R + 1, False)
+    w[2] = w[0]
+    w[4] = w[0]
+    w[5, 1] = w[3, 1]  # one channel row equal across queries
+    rank_row = ops.identical_rows(_cuda(w).reshape(B * L, 2 * R + 1)).cpu().numpy()
+    want = np.arange(B * L)
+    want[[6, 7, 8]] = [0, 1, 2]
+    want[[12, 13, 14]] = [0, 1, 2]
+    want[16] = 10
+    assert np.array_equal(rank_row, want)
+    mask = (rng.random(train.shape[0]) > 0.1).astype(np.uint8)
+    rp, en, _ = ops.coo_to_rows(_cuda(row // L), _cuda(row % L), _cuda(ent), B, L, E)
+    for topk in (2, 5, 40):
+        fw = ops.hop_forward(rp, en, _cuda(val), _cuda(w), Graph.of(csr), R, topk,
+                             Lb.FL_SKIP_NONPOS_W | Lb.FL_DROP_MASKED, mask_triple=_cuda(mask))
+        ref = O.hop_forward(row, ent, val, w, csr_np, R, E, topk_edges=topk, mode=O.MODE_TOPK, mask=mask)
+        counts = (fw.out_row_ptr[1:] - fw.out_row_ptr[:-1]).cpu().numpy()
+        keys = np.repeat(np.arange(B * L), counts) * E + fw.out_ent.cpu().numpy()
+        assert np.array_equal(keys, ref["out_key"]), topk
+        assert np.array_equal(fw.out_x.cpu().numpy(), ref["out_val"]), topk
+
+
 def test_normalize_matches_reference_golden(fk, golden):
     d = golden("normalize.npz")
     row, ent, val = d["row"], d["ent"], d["val"]
