@@ -253,9 +253,10 @@ def identical_rows(w2d):
     hs = h[order]
     head = torch.ones(rows, dtype=torch.bool, device=dev)
     head[1:] = hs[1:] != hs[:-1]
-    first = order[torch.nonzero(head).flatten()]  # lowest row index of each hash (stable order)
+    # sorted position of each run's head (no host read): the lowest row index of each hash
+    at = torch.where(head, torch.arange(rows, device=dev), torch.zeros(rows, dtype=torch.int64, device=dev))
     rep = torch.empty(rows, dtype=torch.int64, device=dev)
-    rep[order] = first[torch.cumsum(head.to(torch.int64), 0) - 1]
+    rep[order] = order[torch.cummax(at, 0).values]
     same = (w2d == w2d[rep]).all(1)
     return torch.where(same, rep, torch.arange(rows, device=dev)).to(torch.int32)
 
