@@ -209,14 +209,13 @@ class HopForward:
 
 
 def hop_params(rows, Lch, n, r_size, E, topk_edges, flags, seed=-1, eps=EPS, slot_capacity=0, status=None,
-               entry_info=None, vis=None, work=None, rel_rank=None, rank_row=None):
+               entry_info=None, vis=None, work=None, rel_rank=None):
     return L.fl_hop_params(rows, Lch, n, r_size, E, int(min(topk_edges, L.NO_BUDGET)), int(flags), int(seed),
                            float(eps), int(slot_capacity), None if status is None else status.data_ptr(),
                            None if entry_info is None else entry_info.data_ptr(),
                            None if vis is None else vis[0].data_ptr(), None if vis is None else vis[1].data_ptr(),
                            None if work is None else work.data_ptr(),
-                           None if rel_rank is None else rel_rank.data_ptr(),
-                           None if rank_row is None else rank_row.data_ptr())
+                           None if rel_rank is None else rel_rank.data_ptr(), None)
 
 
 def relation_rank(w, r_size: int):
@@ -230,48 +229,6 @@ def relation_rank(w, r_size: int):
     rank = torch.empty(max(rows * 2 * r_size, 1), dtype=torch.int16, device=w.device)
     check(lib().fl_relation_rank(_p(w), rows, r_size, None, _p(rank), _stream()), "relation_rank")
     return rank
-
-
-_HASH_COEF = {}
-
-
-def identical_rows(w2d):
-    """rank_row for rows of equal weights: row r gets the first row (lowest
-    index) whose weights equal its own bit for bit, found by a hash of the
-    rows' fp32 bits and then checked element by element (a row whose check
-    fails keeps itself).  In a batch, queries with the same relation have the
-    same attention, so their rows share one rank computation."""
-    rows, n = w2d.shape
-    dev = w2d.device
-    coef = _HASH_COEF.get((n, dev))
-    if coef is None:
-        g = torch.Generator(device="cpu").manual_seed(0x5eed)
-        coef = (torch.randint(0, 1 << 62, (n,), generator=g, dtype=torch.int64) | 1).to(dev)
-        _HASH_COEF[(n, dev)] = coef
-    h = (w2d.view(torch.int32).to(torch.int64) * coef).sum(1)
-    order = torch.argsort(h, stable=True)
-    hs = h[order]
-    head = torch.ones(rows, dtype=torch.bool, device=dev)
-    head[1:] = hs[1:] != hs[:-1]
-    # sorted position of each run's head (no host read): the lowest row index of each hash
-    at = torch.where(head, torch.arange(rows, device=dev), torch.zeros(rows, dtype=torch.int64, device=dev))
-    rep = torch.empty(rows, dtype=torch.int64, device=dev)
-    rep[order] = order[torch.cummax(at, 0).values]
-    same = (w2d == w2d[rep]).all(1)
-    return torch.where(same, rep, torch.arange(rows, device=dev)).to(torch.int32)
-
-
-def relation_rank_shared(w, r_size: int):
-    """relation_rank for rows of distinct weights only: returns (rank,
-    rank_row), where rank_row (identical_rows) points every row to the row
-    whose ranks it uses; the ranks of the other rows are not written."""
-    if not (0 < r_size <= 16384):
-        return None, None
-    rows = w.numel() // (2 * r_size + 1)
-    rank_row = identical_rows(w.reshape(rows, 2 * r_size + 1))
-    rank = torch.empty(max(rows * 2 * r_size, 1), dtype=torch.int16, device=w.device)
-    check(lib().fl_relation_rank(_p(w), rows, r_size, _p(rank_row), _p(rank), _stream()), "relation_rank")
-    return rank, rank_row
 
 
 def csr_mask(mask, order, weight=None):
@@ -376,10 +333,10 @@ def hop_forward(row_ptr, ent, val, w, graph: Graph, r_size: int, topk_edges: int
                                                  for v in vis)):
         raise ValueError("vis must be the two u8 CSR-ordered visibility arrays of csr_visibility")
     work = torch.empty(2, dtype=torch.int32, device=dev)  # the expansion's two work queues
-    rel_rank, rank_row = (relation_rank_shared(w, r_size) if rank_select and (flags & L.FL_SKIP_NONPOS_W)
-                          and topk_edges < L.NO_BUDGET and not (flags & L.FL_SAMPLED) else (None, None))
+    rel_rank = (relation_rank(w, r_size) if rank_select and (flags & L.FL_SKIP_NONPOS_W)
+                and topk_edges < L.NO_BUDGET and not (flags & L.FL_SAMPLED) else None)
     params = hop_params(rows, Lch, n, r_size, graph.E, topk_edges, flags, seed, eps, slot_capacity or 0, status,
-                        entry_info, vis, work, rel_rank, rank_row)
+                        entry_info, vis, work, rel_rank)
     nonfinite = (~torch.isfinite(w)).any() if check_w else None
     check(lib().fl_hop_plan(ctypes.byref(params), _p(row_ptr), _p(ent), S, graph.ori, graph.inv, _p(slot_base),
                             ctypes.byref(total) if (sync and not check_w) else None, _p(ws), ws.numel(), _stream()),

@@ -194,18 +194,3 @@ def test_routed_instances_cover_every_query_with_its_relations_rules():
             seen.extend(bq.tolist())
         assert sorted(seen) == list(range(rel.size))
 
-
-def test_identical_rows_points_each_row_to_its_first_equal_row():
-    """ops.identical_rows (plain torch, here on the CPU): a row equal bit for
-    bit to an earlier row points to the first such row; the others to
-    themselves."""
-    torch = pytest.importorskip("torch")
-    from flashlog_b200 import ops
-    g = torch.Generator().manual_seed(3)
-    w = torch.rand(18, 25, generator=g)
-    w[6:9] = w[0:3]
-    w[12:15] = w[0:3]
-    w[16] = w[10]
-    w[17] = w[10]
-    w[17, 4] = torch.nextafter(w[17, 4], torch.tensor(2.0))  # one ulp apart: its own row
-    assert ops.identical_rows(w).tolist() == [0, 1, 2, 3, 4, 5, 0, 1, 2, 9, 10, 11, 0, 1, 2, 15, 10, 17]
