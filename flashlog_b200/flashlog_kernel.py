@@ -268,6 +268,7 @@ def _graph_topk(csr_args):
 
 
 _VISIBILITY = {}  # the last (graph, mask, mask version) -> CSR-ordered visibility bytes
+_VISIBILITY_MAX_EDGES = 1 << 26
 
 
 def _visibility(graph, mask_values):
@@ -277,9 +278,12 @@ def _visibility(graph, mask_values):
     the same mask tensor, so the bytes are kept for the last (graph, mask) and
     rebuilt when torch's version counter of the mask changes (an in-place
     write such as mask[hide] = False).  Returns None for a mask that is not a
-    CUDA tensor with one entry per triple (the hop then reads the mask)."""
+    CUDA tensor with one entry per triple, and for graphs of more than 2^26
+    edges per side: the bytes are rebuilt for every mask version (every
+    training step), and on such graphs the rebuild costs more than the per-fact
+    mask reads it saves (the hop then reads the mask)."""
     if (mask_values is None or not isinstance(mask_values, torch.Tensor) or not mask_values.is_cuda
-            or mask_values.numel() < graph.csr[1].numel()):
+            or mask_values.numel() < graph.csr[1].numel() or graph.csr[1].numel() > _VISIBILITY_MAX_EDGES):
         return None
     hit = _VISIBILITY.get("last")
     if (hit is not None and hit[0]() is graph and hit[1]() is mask_values and hit[2] == mask_values._version):
