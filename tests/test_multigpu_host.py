@@ -165,6 +165,7 @@ def test_single_process_is_identity():
         g = torch.ones(2)
         assert MG.allreduce_mean_(g) is g and g.tolist() == [1.0, 1.0]
         assert MG.max_time_sum_work(3.0, 4, torch.device("cpu")) == (3.0, 4)
+        assert MG.union_rows(torch.tensor([3, 1, 3]), 5).tolist() == [1, 3]
     finally:
         dist.destroy_process_group()
 
