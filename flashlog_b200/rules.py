@@ -13,13 +13,14 @@ reduction 'max' (Boolean paths):
   rules/evaluate.py:366-378, clamped at 1e-30), and the ranks are combined by
   sum (smDRUM) or by max (mmDRUM, final_max).
 
-The grounding runs in the library's fixed-relation kernels and the reduction
-in fl_rule_max_reduce (an exact, order-independent atomic max of the weights'
-fp32 bit patterns) or, sparsely, in the MAX row reduction.  max_product_scores
-(one rule list for all queries) processes rules in chunks of chunk_size and
-queries in batches whose [ranks, batch, E] accumulator fits
-`accumulator_bytes`; evaluate_rule_bank (each query with the rules of its own
-relation) grounds whole batches of (query, rule) instances at once.
+Both entry points ground whole batches of (query, rule) instances at once,
+one state row per instance, in the library's fixed-relation kernels (or
+entity bitmaps for instances with many facts).  The maxima go through dense
+per-query accumulators (fl_rule_instance_max: an exact, order-independent
+atomic max of the weights' fp32 bit patterns) or through rank facts and the
+MAX row reduction; both give the same scores.  max_product_scores gives
+every query the same rule list; evaluate_rule_bank gives each query the rules
+of its own relation.
 """
 from __future__ import annotations
 
@@ -44,27 +45,6 @@ def _graph(csr_struct):
 def _empty(B, E, device):
     return torch.sparse_coo_tensor(torch.empty((2, 0), dtype=torch.long, device=device),
                                    torch.empty(0, device=device), (B, E), is_coalesced=True)
-
-
-def _ground(sources, ops_chunk, graph, relations, E):
-    """Boolean end states of C rules for every query: rows q * C + c."""
-    B = sources.numel()
-    C, steps = ops_chunk.shape
-    dev = sources.device
-    b = torch.arange(B, device=dev).repeat_interleave(C)
-    l = torch.arange(C, device=dev).repeat(B)
-    e = sources.to(torch.int64).repeat_interleave(C)
-    v = torch.ones(B * C, dtype=torch.float32, device=dev)
-    for step in range(steps):
-        if v.numel() == 0:
-            break
-        step_ops = ops_chunk[:, step].unsqueeze(0).expand(B, C).contiguous()
-        row_ptr, ent, val = ops.fixed_relation(b, l, e, v, step_ops, graph, relations, B, C)
-        v = (val > 0).to(torch.float32)  # several paths are one Boolean proof
-        idx = ops.rows_to_coo(row_ptr, ent, C)
-        b, l, e = idx[0], idx[1], idx[2]
-    row_ptr, ent, _ = ops.coo_to_rows(b, l, e, B, C, E)
-    return row_ptr, ent, v
 
 
 def available_first_operators(sources, csr_struct, relations: int):
@@ -96,25 +76,6 @@ def _weights_and_ops(rules, relations, dev):
     return ranks, weights, ops_all
 
 
-def _sparse_scores(src, ops_all, weights, ranks, graph, relations, E, chunk_size, final_max):
-    """Rank rows of maxima accumulated chunk by chunk, normalized per (query,
-    rank) row (clamped at 1e-30, rules/evaluate.py:366-378) and combined by
-    sum (in rank order) or max; returns the row layout over the queries."""
-    Bq = src.numel()
-    running = None
-    for off in range(0, ops_all.shape[0], chunk_size):
-        ops_chunk = ops_all[off:off + chunk_size]
-        C = ops_chunk.shape[0]
-        row_ptr, ent, val = _ground(src, ops_chunk, graph, relations, E)
-        running = ops.rule_rank_maxima(row_ptr, ent, val, Bq, C, weights[off:off + C], ranks, E, running)
-    rp, ent, x = running
-    y, _ = ops.normalize_forward(rp, x, eps=1e-30)
-    if final_max:
-        return ops.row_max(rp[::ranks].contiguous(), ent, y, Bq, E)
-    out_rp, out_ent, out_x, _ = ops.channel_merge(rp, ent, y, Bq, ranks, E)
-    return out_rp, out_ent, out_x
-
-
 def max_product_scores(sources, rules, csr_struct, relations: int, entities: int, chunk_size: int = 16,
                        final_max: bool = False, accumulator_bytes: int = 4 << 30, query_batch: int = 256,
                        stats=None):
@@ -123,11 +84,14 @@ def max_product_scores(sources, rules, csr_struct, relations: int, entities: int
     rules: sequence of {'body': tuple of operators, 'rank_weights': list}
     (rules/evaluate.py:94-119), all with the same number of ranks.  Rules whose
     first operator has no edge at any source are dropped first
-    (rules/shared_inference.py:34-47).  When the [ranks, queries, E]
-    accumulator of a query batch fits accumulator_bytes, the maxima go
-    through the dense exact atomic max (fl_rule_max_reduce); otherwise (86M
-    entities) through sparse rank rows reduced by the MAX row reduction, in
-    batches of query_batch queries, with no dense buffer.
+    (rules/shared_inference.py:34-47).  Every query gets every remaining
+    rule: batches of at most query_batch queries (and 2^20 (query, rule)
+    instances) are grounded as one instance state each (_ground_instances).
+    When one query's [ranks, E] accumulator fits accumulator_bytes, the
+    maxima go through dense per-query accumulators (fl_rule_instance_max);
+    otherwise (86M entities) through rank facts and the MAX row reduction,
+    with no dense buffer.  chunk_size is the reference's knob, kept for the
+    signature: the scores do not depend on it.
     """
     if chunk_size < 1:
         raise ValueError("chunk_size must be positive")
@@ -156,38 +120,28 @@ def max_product_scores(sources, rules, csr_struct, relations: int, entities: int
         return _empty(B, E, dev)
     ranks, weights, ops_all = _weights_and_ops(rules, relations, dev)
     graph = _graph(csr_struct)
-    dense_qb = accumulator_bytes // max(1, ranks * E * 4)
-    stats["dense_accumulation"] = dense_qb >= min(B, 1)
-    qb = max(1, min(B, dense_qb)) if dense_qb >= 1 else max(1, min(B, query_batch))
+    K = len(rules)
+    dense = accumulator_bytes >= ranks * E * 4  # one query's [ranks, E] accumulator fits
+    stats["dense_accumulation"] = dense
+    qb = max(1, min(B, query_batch, (1 << 20) // K))  # at most 2^20 (query, rule) instances per batch
     keys_out, vals_out = [], []
     for q0 in range(0, B, qb):
-        src = sources[q0:q0 + qb]
+        src = sources[q0:q0 + qb].to(torch.int64)
         Bq = src.numel()
-        if dense_qb >= 1:
-            acc = torch.zeros(ranks * Bq * E, dtype=torch.int32, device=dev)
-            for off in range(0, len(rules), chunk_size):
-                ops_chunk = ops_all[off:off + chunk_size]
-                C = ops_chunk.shape[0]
-                row_ptr, ent, val = _ground(src, ops_chunk, graph, relations, E)
-                w = weights[off:off + C].contiguous()
-                check(lib().fl_rule_max_reduce(_p(row_ptr), Bq * C, _p(ent), _p(val), C, _p(w), ranks, Bq, E,
-                                               _p(acc), _stream()), "rule_max_reduce")
-            scores = acc.view(torch.float32).view(ranks, Bq, E)
-            totals = scores.sum(-1, keepdim=True)
-            norm = scores / totals.clamp_min(1e-30)
-            combined = (norm.amax(0) if final_max else norm.sum(0)).reshape(-1)
-            keys = combined.nonzero().flatten()
-            keys_out.append(keys + q0 * E)
-            vals_out.append(combined[keys])
-        else:
-            rp, ent, x = _sparse_scores(src, ops_all, weights, ranks, graph, relations, E, chunk_size, final_max)
-            counts = rp[1:] - rp[:-1]
-            q = torch.repeat_interleave(torch.arange(Bq, device=dev), counts, output_size=ent.numel())
-            keys_out.append((q + q0) * E + ent.to(torch.int64))
-            vals_out.append(x)
-    keys = torch.cat(keys_out)
-    return torch.sparse_coo_tensor(torch.stack((keys // E, keys % E)), torch.cat(vals_out), (B, E),
-                                   is_coalesced=True)
+        inst_rule = torch.arange(K, device=dev).repeat(Bq)
+        row_ptr, ent, _ = _ground_instances(src.repeat_interleave(K), inst_rule, ops_all, graph, relations, E,
+                                            1 << 29, stats, None)
+        q_inst = torch.arange(Bq + 1, dtype=torch.int64, device=dev) * K
+        for qa, qz, (s_rp, s_ent, s_x) in _instance_scores(
+                row_ptr, ent, q_inst, weights[inst_rule].contiguous(), ranks, E, final_max, 1 << 29, stats,
+                0 if dense else 1 << 62, accumulator_bytes if dense else 4 << 30):
+            q = torch.repeat_interleave(torch.arange(qz - qa, device=dev), s_rp[1:] - s_rp[:-1],
+                                        output_size=s_ent.numel())
+            keys_out.append((q + q0 + qa) * E + s_ent.to(torch.int64))
+            vals_out.append(s_x)
+    keys = torch.cat(keys_out) if keys_out else torch.empty(0, dtype=torch.int64, device=dev)
+    vals = torch.cat(vals_out) if vals_out else torch.empty(0, dtype=torch.float32, device=dev)
+    return torch.sparse_coo_tensor(torch.stack((keys // E, keys % E)), vals, (B, E), is_coalesced=True)
 
 
 def compact_routed_rules(rules):
@@ -486,6 +440,23 @@ def _instance_scores(row_ptr, ent, q_inst, w_inst, ranks: int, E: int, final_max
         yield qa, qb, _combine_ranks(rp, r_ent, x, nq, ranks, E, final_max)
 
 
+def _ground_instances(inst_src, inst_rule, ops_all, graph, relations: int, E: int, fact_budget: int, stats,
+                      bitmap_min_facts=None):
+    """Boolean end states of rule instances: row i starts at entity
+    inst_src[i] and follows the body of rule inst_rule[i] (ops_all, padded
+    with the identity) one fixed step at a time (_fixed_step_rows).  Returns
+    (row_ptr, ent, the largest state of a step in entries)."""
+    dev = inst_src.device
+    row_ptr = torch.arange(inst_src.numel() + 1, dtype=torch.int64, device=dev)
+    ent = inst_src.to(torch.int32)
+    peak = 1
+    for step in range(ops_all.shape[1]):
+        row_ptr, ent = _fixed_step_rows(row_ptr, ent, ops_all[inst_rule, step], graph, relations, E, fact_budget,
+                                        stats, bitmap_min_facts)
+        peak = max(peak, ent.numel())
+    return row_ptr, ent, peak
+
+
 class _PhaseClock:
     """Host time per phase of evaluate_rule_bank, accumulated in stats[name]
     when stats["timing"] is set (the device is synchronized at each tick);
@@ -610,13 +581,9 @@ def evaluate_rule_bank(sources, query_relations, targets, rules, csr_struct, rel
             while c0 < I:
                 c1 = min(I, c0 + budget["instances"])
                 part_rule = torch.from_numpy(inst_rule_h[c0:c1]).to(dev)
-                row_ptr = torch.arange(c1 - c0 + 1, dtype=torch.int64, device=dev)
-                ent = torch.full((c1 - c0,), int(src_h[bq[0]]), dtype=torch.int32, device=dev)
-                peak = 1
-                for step in range(ops_all.shape[1]):
-                    row_ptr, ent = _fixed_step_rows(row_ptr, ent, ops_all[part_rule, step], graph, relations, E,
-                                                    fact_budget, stats, bitmap_min_facts)
-                    peak = max(peak, ent.numel())
+                part_src = torch.full((c1 - c0,), int(src_h[bq[0]]), dtype=torch.int32, device=dev)
+                row_ptr, ent, peak = _ground_instances(part_src, part_rule, ops_all, graph, relations, E,
+                                                       fact_budget, stats, bitmap_min_facts)
                 stats["entries"] = stats.get("entries", 0) + ent.numel()
                 q_part = torch.tensor([0, c1 - c0], dtype=torch.int64, device=dev)
                 check(lib().fl_rule_instance_max(_p(row_ptr), _p(ent), _p(q_part), 1,
@@ -632,13 +599,9 @@ def evaluate_rule_bank(sources, query_relations, targets, rules, csr_struct, rel
             del acc
         elif I:
             inst_rule = torch.from_numpy(inst_rule_h).to(dev)
-            row_ptr = torch.arange(I + 1, dtype=torch.int64, device=dev)
-            ent = torch.from_numpy(np.repeat(src_h[bq], counts).astype(np.int32)).to(dev)
-            peak = 1
-            for step in range(ops_all.shape[1]):
-                row_ptr, ent = _fixed_step_rows(row_ptr, ent, ops_all[inst_rule, step], graph, relations, E,
-                                                fact_budget, stats, bitmap_min_facts)
-                peak = max(peak, ent.numel())
+            inst_src = torch.from_numpy(np.repeat(src_h[bq], counts).astype(np.int32)).to(dev)
+            row_ptr, ent, peak = _ground_instances(inst_src, inst_rule, ops_all, graph, relations, E, fact_budget,
+                                                   stats, bitmap_min_facts)
             stats["entries"] = stats.get("entries", 0) + ent.numel()
             budget["instances"] = int(min(instance_budget, max(256, entry_budget * I // peak)))
             clock.tick("ground_s")
